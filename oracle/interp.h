@@ -1,0 +1,24 @@
+// TEST INFRASTRUCTURE — the parity oracle and the timed CPU baseline, never a product path.
+//
+// A CPU restatement of rg's plan interpreter (src/plan.rs:657-1642 and the portable kernels of
+// src/tensor.rs:200-251): the same block/task chunking, thresholds, per-element arithmetic order,
+// naive GEMM loop order and glibc libm calls that rg uses on Linux. Only tests/, the smoke check
+// and bench.py's CPU-baseline leg load it.
+#pragma once
+#include "../rustautograd_b200/csrc/host/exec.h"
+
+namespace rg::oracle {
+
+// Worker threads for the parallel kernels (rayon's pool in rg). Results never depend on it.
+void set_threads(int n);
+int threads();
+
+// Executes every step of `plan` over `slots`.
+void exec_plan(const Plan& plan, std::vector<Buf>& slots);
+// Fresh frame with constants loaded (plan.rs:641-647).
+std::vector<Buf> frame(const Plan& plan);
+
+// The CPU device: plans run in this interpreter.
+std::shared_ptr<Device> cpu_device();
+
+}  // namespace rg::oracle

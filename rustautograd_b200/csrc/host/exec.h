@@ -1,0 +1,75 @@
+// The device contract a plan executes through (restates plan.rs:29-41 `Exec` and the program /
+// exec split of metal.rs:362-571). A `Device` turns a plan into a `Program` once, at compile
+// time; a `Program` hands out `Exec` frames, one per call or run.
+#pragma once
+#include <memory>
+#include <optional>
+#include <string>
+#include <vector>
+
+#include "plan.h"
+
+namespace rg {
+
+// validate.rs:248-268
+struct RunSpec {
+  std::vector<std::pair<size_t, size_t>> state;  // (input index, output index) fed back each step
+  std::vector<size_t> data;
+  std::vector<size_t> history;  // scalar outputs recorded per step
+};
+
+struct RunOut {
+  std::vector<Tensor> state;
+  std::vector<Tensor> outputs;
+  std::vector<std::vector<double>> history;
+  size_t steps = 0;
+  std::optional<size_t> nonfinite_step;
+  double seconds = 0;
+  std::optional<std::string> device_error;
+};
+
+struct Exec {
+  virtual ~Exec() = default;
+  virtual void load(size_t input, const Tensor& t) = 0;
+  virtual void step() = 0;
+  // Executes only step `k` of the plan: the instrumented (diagnostic) runs go one step at a time.
+  virtual void step_at(size_t k) = 0;
+  virtual void swap(size_t a, size_t b) = 0;
+  virtual Buf prefix(size_t slot, size_t n) = 0;
+  virtual void write_prefix(size_t slot, const Buf& b) = 0;
+  virtual double scalar(size_t slot) = 0;
+  virtual std::optional<std::string> failure() { return std::nullopt; }
+  // A device-resident implementation of the whole multi-step loop. Returns false when the
+  // device has none, and the host loop (run_loop) drives load/step/swap instead.
+  virtual bool run(const RunSpec&, const std::vector<Tensor>&, const std::vector<std::vector<Tensor>>&, size_t, RunOut*) { return false; }
+};
+
+struct Program {
+  virtual ~Program() = default;
+  virtual std::unique_ptr<Exec> exec() = 0;
+  virtual size_t allocated_bytes() const { return 0; }
+  virtual void inject_failure_for_test() {}
+  // Per-step timing and a launch breakdown for `profile` (metal.rs:692-712).
+  virtual bool step_timed(Exec&, std::vector<double>&) { return false; }
+  virtual Json breakdown(Exec&, size_t) { return Json(); }
+};
+
+struct Device {
+  virtual ~Device() = default;
+  virtual std::string name() const = 0;
+  virtual bool available() const = 0;
+  // The fusion configuration plans for this device are built with.
+  virtual Fuse fuse() const = 0;
+  // Compile-time failures (kernel build, memory) throw std::runtime_error.
+  virtual std::shared_ptr<Program> compile(const Plan& plan) = 0;
+};
+
+// Runs a plan once on a device with fresh buffers: the evaluator behind constant folding and
+// eager operations.
+std::vector<Tensor> run_once(Device& d, const Plan& plan, const std::vector<const Tensor*>& inputs);
+
+// validate.rs:290-363, generic over the device.
+RunOut run_loop(const Plan& p, Exec& e, const RunSpec& spec, const std::vector<Tensor>& state,
+                const std::vector<std::vector<Tensor>>& batches, size_t steps);
+
+}  // namespace rg

@@ -1,0 +1,372 @@
+// Restates src/optimize.rs (line references below are to that file).
+#include "optimize.h"
+
+#include <algorithm>
+#include <map>
+#include <unordered_map>
+
+#include "plan.h"
+
+namespace rg {
+
+namespace {
+
+constexpr size_t FOLD_LIMIT = 4096;
+constexpr size_t CSE_CONST_LIMIT = 16;
+constexpr size_t REMAT_MIN = size_t(1) << 14;
+constexpr double SEARCH_MIN_GAIN = 0.9;
+constexpr size_t COSTLY_REMAT_ABOVE_BYTES = size_t(2) << 30;
+
+// The value of a constant whose elements are all equal (optimize.rs:45-53).
+std::optional<double> splat(const Graph& g, uint32_t id) {
+  const Node& n = g.nodes[id];
+  if (n.op.kind != OpKind::Const) return std::nullopt;
+  const Tensor& t = *n.op.value;
+  if (t.n() == 0 || t.n() > FOLD_LIMIT) return std::nullopt;
+  double v0 = t.data.get(0);
+  for (size_t i = 1; i < t.n(); ++i)
+    if (!(t.data.get(i) == v0)) return std::nullopt;
+  if (!(v0 == v0)) return std::nullopt;  // NaN never equals itself
+  return v0;
+}
+
+// optimize.rs:55-77. Never rewrites `x * 0`: that would hide NaN/Inf in `x`.
+std::optional<uint32_t> identity(const Graph& g, const Op& op, const std::vector<uint32_t>& ins, const std::vector<size_t>& shape) {
+  auto same = [&](uint32_t id) { return g.shape(id) == shape; };
+  auto is = [&](uint32_t id, double c) {
+    auto s = splat(g, id);
+    return s && *s == c;
+  };
+  switch (op.kind) {
+    case OpKind::StopGradient: case OpKind::Custom: return ins[0];
+    case OpKind::Add:
+      if (is(ins[1], 0.0) && same(ins[0])) return ins[0];
+      if (is(ins[0], 0.0) && same(ins[1])) return ins[1];
+      return std::nullopt;
+    case OpKind::Sub:
+      if (is(ins[1], 0.0) && same(ins[0])) return ins[0];
+      return std::nullopt;
+    case OpKind::Mul:
+      if (is(ins[1], 1.0) && same(ins[0])) return ins[0];
+      if (is(ins[0], 1.0) && same(ins[1])) return ins[1];
+      return std::nullopt;
+    case OpKind::Div:
+    case OpKind::Pow:
+      if (is(ins[1], 1.0) && same(ins[0])) return ins[0];
+      return std::nullopt;
+    case OpKind::Neg:
+      if (g.nodes[ins[0]].op.kind == OpKind::Neg) return g.nodes[ins[0]].inputs[0];
+      return std::nullopt;
+    case OpKind::Reshape: case OpKind::BroadcastTo:
+      if (same(ins[0])) return ins[0];
+      return std::nullopt;
+    case OpKind::Cast:
+      if (op.dtype == g.dtype(ins[0])) return ins[0];
+      return std::nullopt;
+    case OpKind::Transpose: {
+      for (size_t i = 0; i < op.shape.size(); ++i)
+        if (op.shape[i] != i) return std::nullopt;
+      return ins[0];
+    }
+    default: return std::nullopt;
+  }
+}
+
+// optimize.rs:85-93
+bool recomputable(const Op& op, bool costly_too) {
+  bool elementwise = op.is_unary_elementwise() || op.is_binary_elementwise() || op.kind == OpKind::Where;
+  bool costly = op.kind == OpKind::Exp || op.kind == OpKind::Log || op.kind == OpKind::Sin || op.kind == OpKind::Cos ||
+                op.kind == OpKind::Tanh || op.kind == OpKind::Sqrt;
+  return elementwise && op.kind != OpKind::Pow && (costly_too || !costly);
+}
+
+bool is_leaf(const Node& n) { return n.op.kind == OpKind::Input || n.op.kind == OpKind::Const; }
+
+size_t count_kept(const Graph& g, const std::vector<uint32_t>& outputs) {
+  auto keep = g.reachable(outputs);
+  return (size_t)std::count(keep.begin(), keep.end(), true);
+}
+
+// optimize.rs:95-166
+std::pair<Graph, std::vector<uint32_t>> rematerialize(const Graph& g, const std::vector<uint32_t>& outputs, const std::vector<bool>& backward,
+                                                      size_t min_n, bool costly_too, OptStats& st) {
+  auto keep = g.reachable(outputs);
+  size_t N = g.nodes.size();
+  auto large = [&](uint32_t id) { return g.nodes[id].n() >= min_n; };
+  std::vector<bool> retained(N, false);
+  for (size_t i = 0; i < N; ++i)
+    if (keep[i] && backward[i])
+      for (auto x : g.nodes[i].inputs) retained[x] = retained[x] || !backward[x];
+  std::vector<bool> remat(N, false);
+  for (size_t i = N; i-- > 0;) {
+    const Node& n = g.nodes[i];
+    if (!retained[i] || backward[i] || !recomputable(n.op, costly_too) || !large((uint32_t)i)) continue;
+    std::vector<uint32_t> fresh;
+    for (auto x : n.inputs)
+      if (large(x) && !retained[x] && !is_leaf(g.nodes[x])) fresh.push_back(x);
+    fresh.erase(std::unique(fresh.begin(), fresh.end()), fresh.end());  // Vec::dedup
+    if (fresh.size() <= 1) {
+      remat[i] = true;
+      retained[i] = false;
+      for (auto x : n.inputs) retained[x] = true;
+    }
+  }
+  Graph h;
+  std::vector<uint32_t> map(N, UINT32_MAX);
+  std::vector<int64_t> clone(N, -1);
+  std::function<uint32_t(uint32_t)> value = [&](uint32_t i) -> uint32_t {
+    if (!remat[i]) return map[i];
+    if (clone[i] >= 0) return (uint32_t)clone[i];
+    const Node& n = g.nodes[i];
+    std::vector<uint32_t> ins;
+    for (auto x : n.inputs) ins.push_back(value(x));
+    h.cur_source = n.source;
+    uint32_t id = h.add(n.op, ins);
+    clone[i] = id;
+    st.rematerialized += 1;
+    return id;
+  };
+  for (size_t i = 0; i < N; ++i) {
+    const Node& n = g.nodes[i];
+    if (n.op.kind == OpKind::Input) {
+      h.cur_source = n.source;
+      map[i] = h.input(n.shape, n.dtype);
+      h.nodes[map[i]].op = n.op;
+      continue;
+    }
+    if (!keep[i]) continue;
+    std::vector<uint32_t> ins;
+    for (auto x : n.inputs) ins.push_back(backward[i] ? value(x) : map[x]);
+    h.cur_source = n.source;
+    map[i] = n.op.kind == OpKind::Const ? h.constant(n.op.value) : h.add(n.op, ins);
+  }
+  std::vector<uint32_t> out;
+  for (auto o : outputs) out.push_back(map[o]);
+  return {std::move(h), std::move(out)};
+}
+
+struct Simplified {
+  Graph g;
+  std::vector<uint32_t> out;
+  OptStats st;
+  std::vector<bool> backward;
+};
+
+// optimize.rs:286-403. Single forward rewrite: SSA order lets folds and identities cascade.
+Simplified simplify(const Graph& g, const std::vector<uint32_t>& outputs, bool flip_transposes) {
+  auto keep = g.reachable(outputs);
+  Simplified r;
+  r.st.nodes_before = (size_t)std::count(keep.begin(), keep.end(), true);
+  Graph& ng = r.g;
+  std::vector<uint32_t> map(g.nodes.size(), UINT32_MAX);
+  std::unordered_map<std::string, uint32_t> seen;
+  std::vector<bool>& backward = r.backward;
+
+  for (size_t i = 0; i < g.nodes.size(); ++i) {
+    const Node& node = g.nodes[i];
+    ng.cur_source = node.source;
+    ng.cur_origin.reset();
+    if (node.op.kind == OpKind::Input) {
+      map[i] = ng.input(node.shape, node.dtype);
+      ng.nodes[map[i]].op = node.op;  // reverse scans renumber their inputs
+      backward.resize(ng.nodes.size(), false);
+      continue;
+    }
+    if (!keep[i]) continue;
+    std::vector<uint32_t> ins;
+    for (auto x : node.inputs) ins.push_back(map[x]);
+
+    if (auto existing = identity(ng, node.op, ins, node.shape)) {
+      map[i] = *existing;
+      r.st.simplified += 1;
+      continue;
+    }
+    Op op = node.op;
+    if (op.kind == OpKind::Pow) {
+      auto s = splat(ng, ins[1]);
+      if (s && *s == 2.0 && ng.shape(ins[0]) == node.shape) {
+        op = Op::make(OpKind::Mul);
+        ins = {ins[0], ins[0]};
+        r.st.simplified += 1;
+      }
+    }
+    // Binary kernels broadcast by themselves, so a materialised broadcast is a wasted copy.
+    if (op.is_binary_elementwise()) {
+      for (int k = 0; k < 2; ++k) {
+        const Node& n = ng.nodes[ins[k]];
+        if (n.op.kind == OpKind::BroadcastTo) {
+          uint32_t source = n.inputs[0];
+          uint32_t other = ins[1 - k];
+          std::vector<size_t> joint;
+          if (broadcast_shapes(ng.shape(source), ng.shape(other), &joint) && joint == node.shape) {
+            ins[k] = source;
+            r.st.simplified += 1;
+          }
+        }
+      }
+    }
+    // A transposed operand is read through a flag; the copy then goes away with DCE.
+    if (flip_transposes && op.kind == OpKind::MatMul) {
+      auto flipped = [&](uint32_t id) -> std::optional<uint32_t> {
+        const Node& n = ng.nodes[id];
+        if (n.op.kind != OpKind::Transpose) return std::nullopt;
+        const auto& p = n.op.shape;
+        if (p.size() < 2) return std::nullopt;
+        for (size_t a = 0; a < p.size(); ++a) {
+          bool ok = a + 2 < p.size() ? a == p[a] : a + p[a] == 2 * p.size() - 3;
+          if (!ok) return std::nullopt;
+        }
+        return n.inputs[0];
+      };
+      auto fa = flipped(ins[0]);
+      auto fb = flipped(ins[1]);
+      if (fa || fb) {
+        op = Op::make(OpKind::MatMulT);
+        op.flag_a = (bool)fa;
+        op.flag_b = (bool)fb;
+        ins = {fa ? *fa : ins[0], fb ? *fb : ins[1]};
+        r.st.simplified += 1;
+      }
+    }
+    bool foldable = !op.is_control_flow() && op.kind != OpKind::Output && !ins.empty() && node.n() <= FOLD_LIMIT;
+    for (auto x : ins) foldable = foldable && ng.nodes[x].op.kind == OpKind::Const;
+    if (foldable) {
+      Graph tmp;
+      std::vector<uint32_t> ids;
+      for (auto x : ins) ids.push_back(tmp.constant(ng.nodes[x].op.value));
+      uint32_t id = tmp.add(op, ids);
+      auto value = eval(tmp, {id}, {});
+      Op c = Op::make(OpKind::Const);
+      c.value = std::make_shared<const Tensor>(std::move(value[0]));
+      op = std::move(c);
+      ins.clear();
+      r.st.folded += 1;
+    }
+    bool big_const = op.kind == OpKind::Const && op.value->n() > CSE_CONST_LIMIT;
+    std::string key;
+    if (!big_const) {
+      key = op.key();
+      key += '|';
+      for (auto x : ins) key += std::to_string(x) + ",";
+      auto it = seen.find(key);
+      if (it != seen.end()) {
+        map[i] = it->second;
+        r.st.cse += 1;
+        continue;
+      }
+    }
+    uint32_t id = op.kind == OpKind::Const ? ng.constant(op.value) : ng.add(op, ins);
+    ng.nodes[id].origin = node.origin;  // only presence is read after this point
+    backward.resize(ng.nodes.size(), false);
+    backward[id] = node.origin.has_value();
+    if (!big_const) seen[key] = id;
+    map[i] = id;
+  }
+  for (auto o : outputs) r.out.push_back(map[o]);
+  backward.resize(ng.nodes.size(), false);
+  return r;
+}
+
+OptResult finish(const Graph& ng, const std::vector<uint32_t>& out, const std::vector<bool>& backward, OptStats st) {
+  auto hr = rematerialize(ng, out, backward, REMAT_MIN, false, st);
+  if (Plan::build(hr.first, hr.second, true).peak_live_bytes > COSTLY_REMAT_ABOVE_BYTES) {
+    st.rematerialized = 0;
+    hr = rematerialize(ng, out, backward, REMAT_MIN, true, st);
+  }
+  st.nodes_after = count_kept(hr.first, hr.second);
+  return OptResult{std::move(hr.first), std::move(hr.second), st};
+}
+
+}  // namespace
+
+bool parse_opt_mode(const std::string& s, OptMode* m) {
+  if (s == "none") *m = OptMode::None;
+  else if (s == "standard") *m = OptMode::Standard;
+  else if (s == "search-exact") *m = OptMode::SearchExact;
+  else if (s == "search-linear") *m = OptMode::SearchLinear;
+  else if (s == "search") *m = OptMode::Search;
+  else if (s == "auto") *m = OptMode::Auto;
+  else return false;
+  return true;
+}
+
+Json OptStats::json() const {
+  Json j = Json::object();
+  j["nodes_before"] = nodes_before;
+  j["nodes_after"] = nodes_after;
+  j["constants_folded"] = folded;
+  j["algebraic_simplified"] = simplified;
+  j["cse_merged"] = cse;
+  j["rematerialized"] = rematerialized;
+  if (search) {
+    Json s = Json::object();
+    s["accepted"] = search->accepted;
+    s["iterations"] = search->iterations;
+    s["egraph_nodes"] = search->egraph_nodes;
+    s["cost_before"] = search->cost_before;
+    s["cost_after"] = search->cost_after;
+    j["search"] = s;
+  } else {
+    j["search"] = nullptr;
+  }
+  return j;
+}
+
+OptResult optimize(const Graph& g, const std::vector<uint32_t>& outputs) { return optimize_mode(g, outputs, OptMode::Standard); }
+
+// optimize.rs:210-246
+OptResult optimize_mode(const Graph& g, const std::vector<uint32_t>& outputs, OptMode mode) {
+  if (mode == OptMode::Auto) mode = OptMode::Standard;  // compile() resolves Auto before this point
+  if (mode == OptMode::None) {
+    size_t k = count_kept(g, outputs);
+    OptStats st;
+    st.nodes_before = st.nodes_after = k;
+    return OptResult{g, outputs, st};
+  }
+  if (mode == OptMode::Standard) {
+    Simplified s = simplify(g, outputs, true);
+    return finish(s.g, s.out, s.backward, s.st);
+  }
+  Simplified baseline = simplify(g, outputs, true);
+  Simplified first = simplify(g, outputs, false);
+  size_t before = count_kept(g, outputs);
+  if (mode == OptMode::SearchLinear && !has_matrix_structure(first.g, first.out)) {
+    baseline.st.nodes_before = before;
+    return finish(baseline.g, baseline.out, baseline.backward, baseline.st);
+  }
+  SearchStats ss;
+  std::optional<Simplified> candidate;
+  if (mode != OptMode::SearchExact) {
+    if (auto found = reassociate_products(first.g, first.out, &ss)) candidate = simplify(found->first, found->second, true);
+  }
+  ss.accepted = candidate.has_value() && ss.cost_after < ss.cost_before * SEARCH_MIN_GAIN;
+  Simplified& chosen = ss.accepted ? *candidate : baseline;
+  chosen.st.nodes_before = before;
+  chosen.st.search = ss;
+  return finish(chosen.g, chosen.out, chosen.backward, chosen.st);
+}
+
+// optimize.rs:260-277
+bool has_matrix_structure(const Graph& g, const std::vector<uint32_t>& outputs) {
+  auto keep = g.reachable(outputs);
+  auto is_product = [&](uint32_t id) {
+    const Node* n = &g.nodes[id];
+    if (n->op.kind == OpKind::Transpose && n->op.shape == std::vector<size_t>{1, 0}) n = &g.nodes[n->inputs[0]];
+    return n->op.kind == OpKind::MatMul;
+  };
+  for (size_t i = 0; i < g.nodes.size(); ++i) {
+    if (!keep[i]) continue;
+    const Node& n = g.nodes[i];
+    if (n.op.kind == OpKind::MatMul) {
+      for (auto x : n.inputs)
+        if (is_product(x)) return true;
+    } else if (n.op.kind == OpKind::Add) {
+      bool all = true;
+      for (auto x : n.inputs) all = all && is_product(x);
+      if (all) return true;
+    }
+  }
+  return false;
+}
+
+}  // namespace rg

@@ -1,0 +1,81 @@
+// The generic multi-step loop and one-off execution over the Exec contract.
+#include <chrono>
+#include <cmath>
+#include <stdexcept>
+#include <tuple>
+
+#include "exec.h"
+
+namespace rg {
+
+std::vector<Tensor> run_once(Device& d, const Plan& plan, const std::vector<const Tensor*>& inputs) {
+  auto prog = d.compile(plan);
+  auto e = prog->exec();
+  for (size_t k = 0; k < inputs.size(); ++k) e->load(k, *inputs[k]);
+  e->step();
+  if (auto f = e->failure()) throw std::runtime_error("device execution failed: " + *f);
+  std::vector<Tensor> out;
+  for (auto& o : plan.outputs) out.emplace_back(o.shape, e->prefix(o.slot, o.n));
+  return out;
+}
+
+// validate.rs:290-363. State moves by swapping buffers when the output's slot is private and of
+// the same capacity, by copying otherwise; the run stops after the first step whose history
+// scalars are not finite, with that step's state committed.
+RunOut run_loop(const Plan& p, Exec& e, const RunSpec& spec, const std::vector<Tensor>& state,
+                const std::vector<std::vector<Tensor>>& batches, size_t steps) {
+  for (size_t k = 0; k < spec.state.size() && k < state.size(); ++k) e.load(spec.state[k].first, state[k]);
+  auto load_batch = [&](const std::vector<Tensor>& b) {
+    for (size_t k = 0; k < spec.data.size() && k < b.size(); ++k) e.load(spec.data[k], b[k]);
+  };
+  if (batches.size() == 1) load_batch(batches[0]);
+
+  std::vector<size_t> out_slots;
+  for (auto& io : spec.state) out_slots.push_back(p.outputs[io.second].slot);
+  std::vector<std::pair<size_t, size_t>> swaps;
+  std::vector<std::tuple<size_t, size_t, size_t>> copies;
+  for (auto& io : spec.state) {
+    size_t is = p.input_slots[io.first], os = p.outputs[io.second].slot;
+    if (is == os) continue;
+    size_t users = 0;
+    for (size_t s : out_slots) users += s == os;
+    if (!p.pinned[os] && users == 1 && p.slots[os].second == p.slots[is].second) swaps.emplace_back(is, os);
+    else copies.emplace_back(is, os, p.outputs[io.second].n);
+  }
+  std::vector<size_t> hist_slots;
+  for (size_t o : spec.history) hist_slots.push_back(p.outputs[o].slot);
+
+  RunOut r;
+  r.history.assign(hist_slots.size(), {});
+  for (auto& h : r.history) h.reserve(steps);
+  auto started = std::chrono::steady_clock::now();
+  for (size_t k = 0; k < steps; ++k) {
+    if (batches.size() > 1) load_batch(batches[k % batches.size()]);
+    e.step();
+    r.device_error = e.failure();
+    if (r.device_error) break;
+    r.steps = k + 1;
+    bool bad = false;
+    for (size_t h = 0; h < hist_slots.size(); ++h) {
+      double v = e.scalar(hist_slots[h]);
+      bad = bad || !std::isfinite(v);
+      r.history[h].push_back(v);
+    }
+    if (bad) r.nonfinite_step = k;
+    if (k + 1 == steps || bad) {
+      r.outputs.clear();
+      for (auto& o : p.outputs) r.outputs.emplace_back(o.shape, e.prefix(o.slot, o.n));
+    }
+    std::vector<std::pair<size_t, Buf>> temp;
+    for (auto& c : copies) temp.emplace_back(std::get<0>(c), e.prefix(std::get<1>(c), std::get<2>(c)));
+    for (auto& sw : swaps) e.swap(sw.first, sw.second);
+    for (auto& t : temp) e.write_prefix(t.first, t.second);
+    if (bad) break;
+  }
+  r.seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - started).count();
+  for (auto& io : spec.state)
+    r.state.emplace_back(p.outputs[io.second].shape, e.prefix(p.input_slots[io.first], p.input_ns[io.first]));
+  return r;
+}
+
+}  // namespace rg
