@@ -764,6 +764,13 @@ void cast(const Instr& i, std::vector<Buf>& s) {
   else throw std::logic_error("same-dtype casts are aliases");
 }
 
+std::function<void(void*, size_t, DType)> g_all_reduce;
+
+void all_reduce(const Instr& i, std::vector<Buf>& s) {
+  std::memcpy(s[i.dst].data(), s[i.args[0]].data(), i.n * dtype_size(i.dtype));
+  if (g_all_reduce) g_all_reduce(s[i.dst].data(), i.n, i.dtype);
+}
+
 void key_split(const Instr& i, std::vector<Buf>& s) {
   uint64_t key = read_key(s[i.args[0]]);
   int32_t* d = S<int32_t>(s[i.dst]);
@@ -814,6 +821,7 @@ void exec_instr(const Instr& i, std::vector<Buf>& s) {
       if (s[i.args[0]].dtype == DType::F32) return arg_top_k<float>(i, s);
       return arg_top_k<double>(i, s);
     case OpKind::KeySplit: return key_split(i, s);
+    case OpKind::AllReduce: return all_reduce(i, s);
     case OpKind::Argmax:
       if (s[i.args[0]].dtype == DType::F32) return argmax<float>(i, s);
       return argmax<double>(i, s);
@@ -960,6 +968,7 @@ class CpuDevice : public Device {
 }  // namespace
 
 void set_threads(int n) { pool().resize(n); }
+void set_all_reduce(std::function<void(void*, size_t, DType)> hook) { g_all_reduce = std::move(hook); }
 int threads() { return pool().size(); }
 
 std::vector<Buf> frame(const Plan& plan) {

@@ -5,9 +5,15 @@
 // naive GEMM loop order and glibc libm calls that rg uses on Linux. Only tests/, the smoke check
 // and bench.py's CPU-baseline leg load it.
 #pragma once
+#include <functional>
+
 #include "../rustautograd_b200/csrc/host/exec.h"
 
 namespace rg::oracle {
+
+// The cross-rank sum behind the `all_reduce` op (data parallelism). Without a hook the op is the
+// identity, which is what a single rank computes.
+void set_all_reduce(std::function<void(void* data, size_t n, DType dtype)> hook);
 
 // Worker threads for the parallel kernels (rayon's pool in rg). Results never depend on it.
 void set_threads(int n);

@@ -26,6 +26,30 @@ void module_extra(py::module_& m) {
   set_evaluator([](const Plan& p, const std::vector<const Tensor*>& in) { return run_once(*oracle::cpu_device(), p, in); });
   m.def("set_threads", [](int n) { oracle::set_threads(n); });
   m.def("threads", [] { return oracle::threads(); });
+  // Installs the cross-rank sum of the `all_reduce` op: fn(bytes, dtype) -> bytes of the sum.
+  // Multi-process tests pass a torch.distributed (gloo) all-reduce here; None removes it.
+  m.def("set_all_reduce", [](py::object fn) {
+    if (fn.is_none()) {
+      oracle::set_all_reduce(nullptr);
+      return;
+    }
+    // The callable outlives this call; if it is still installed when the interpreter has shut
+    // down, it is left alone rather than released without a live interpreter.
+    auto keep = std::shared_ptr<py::object>(new py::object(fn), [](py::object* o) {
+      if (Py_IsInitialized()) {
+        py::gil_scoped_acquire gil;
+        delete o;
+      }
+    });
+    oracle::set_all_reduce([keep](void* data, size_t n, DType d) {
+      py::gil_scoped_acquire gil;
+      size_t bytes = n * dtype_size(d);
+      py::bytes out = (*keep)(py::bytes((const char*)data, bytes), std::string(dtype_name(d)));
+      std::string_view v = out;
+      if (v.size() != bytes) throw std::runtime_error("all_reduce hook returned the wrong number of bytes");
+      std::memcpy(data, v.data(), bytes);
+    });
+  });
   // Executes a plan blob (the C-ABI wire format) once on the CPU: inputs and outputs are
   // (bytes, shape, dtype) triples, so results cross between modules as plain data.
   m.def("run_plan_blob", [](py::bytes blob, std::vector<std::tuple<py::bytes, std::vector<size_t>, std::string>> inputs) {

@@ -1,0 +1,341 @@
+// NVRTC code generation for fused elementwise groups.
+#include "jit.h"
+
+#include <nvrtc.h>
+
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <functional>
+#include <sstream>
+#include <stdexcept>
+#include <sys/stat.h>
+#include <unistd.h>
+
+namespace rgc {
+
+using rg::ArgKind;
+using rg::DType;
+using rg::OpKind;
+
+const Driver& Driver::get() {
+  static Driver d = [] {
+    Driver x;
+    auto load = [](const char* name, void** fn) {
+      cudaDriverEntryPointQueryResult q;
+#pragma GCC diagnostic push
+#pragma GCC diagnostic ignored "-Wdeprecated-declarations"
+      cudaError_t e = cudaGetDriverEntryPoint(name, fn, cudaEnableDefault, &q);
+#pragma GCC diagnostic pop
+      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !*fn) throw std::runtime_error(std::string("CUDA driver entry point missing: ") + name);
+    };
+    load("cuModuleLoadData", (void**)&x.ModuleLoadData);
+    load("cuModuleGetFunction", (void**)&x.ModuleGetFunction);
+    load("cuModuleUnload", (void**)&x.ModuleUnload);
+    load("cuLaunchKernel", (void**)&x.LaunchKernel);
+    return x;
+  }();
+  return d;
+}
+
+namespace {
+
+const char* PRELUDE = R"(
+struct Dims { int rank; long long d[8]; long long st[8]; };
+struct ElemArgs { long long n; int vec; int pad; void* out[64]; const void* in[64]; long long row[64]; const Dims* bc; };
+__device__ __forceinline__ long long bc_off(const Dims& b, long long e) {
+  long long off = 0;
+  for (int d = b.rank - 1; d >= 0; --d) { long long c = e % b.d[d]; e /= b.d[d]; off += c * b.st[d]; }
+  return off;
+}
+__device__ __forceinline__ float rg_nan(float) { return __int_as_float(0x7fc00000); }
+__device__ __forceinline__ double rg_nan(double) { return __longlong_as_double(0x7ff8000000000000LL); }
+template <typename T> __device__ __forceinline__ T rg_max(T a, T b) { return a > b ? a : (b >= a ? b : rg_nan(a)); }
+template <typename T> __device__ __forceinline__ T rg_min(T a, T b) { return a < b ? a : (b <= a ? b : rg_nan(a)); }
+template <typename T> __device__ __forceinline__ T rg_sign(T x) { return x > (T)0 ? (T)1 : (x < (T)0 ? (T)-1 : x); }
+__device__ __forceinline__ int rg_iadd(int a, int b) { return (int)((unsigned)a + (unsigned)b); }
+__device__ __forceinline__ int rg_isub(int a, int b) { return (int)((unsigned)a - (unsigned)b); }
+__device__ __forceinline__ int rg_imul(int a, int b) { return (int)((unsigned)a * (unsigned)b); }
+)";
+
+std::string ctype(DType d) { return d == DType::F32 ? "float" : d == DType::F64 ? "double" : "int"; }
+std::string vtype(DType d) { return d == DType::F32 ? "float4" : d == DType::F64 ? "double2" : "int4"; }
+int vwidth(DType d) { return d == DType::F64 ? 2 : 4; }
+const char* lane(int j) {
+  static const char* n[] = {"x", "y", "z", "w"};
+  return n[j];
+}
+
+std::string fn1(DType d, const char* f32, const char* f64, const std::string& x) {
+  return std::string(d == DType::F64 ? f64 : f32) + "(" + x + ")";
+}
+
+// One micro-op as a C expression over operand expressions (plan.rs:935-963 semantics).
+std::string expr(DType d, const rg::Op& op, const std::vector<std::string>& a) {
+  bool I = d == DType::I32;
+  std::string T = ctype(d);
+  switch (op.kind) {
+    case OpKind::Neg: return "(-" + a[0] + ")";
+    case OpKind::Exp: return fn1(d, "expf", "exp", a[0]);
+    case OpKind::Log: return fn1(d, "logf", "log", a[0]);
+    case OpKind::Sqrt: return fn1(d, "sqrtf", "sqrt", a[0]);
+    case OpKind::Sin: return fn1(d, "sinf", "sin", a[0]);
+    case OpKind::Cos: return fn1(d, "cosf", "cos", a[0]);
+    case OpKind::Tanh: return fn1(d, "tanhf", "tanh", a[0]);
+    case OpKind::Abs: return fn1(d, "fabsf", "fabs", a[0]);
+    case OpKind::Sign: return "rg_sign<" + T + ">(" + a[0] + ")";
+    case OpKind::Floor: return fn1(d, "floorf", "floor", a[0]);
+    case OpKind::Add: return I ? "rg_iadd(" + a[0] + "," + a[1] + ")" : "(" + a[0] + " + " + a[1] + ")";
+    case OpKind::Sub: return I ? "rg_isub(" + a[0] + "," + a[1] + ")" : "(" + a[0] + " - " + a[1] + ")";
+    case OpKind::Mul: return I ? "rg_imul(" + a[0] + "," + a[1] + ")" : "(" + a[0] + " * " + a[1] + ")";
+    case OpKind::Div: return "(" + a[0] + " / " + a[1] + ")";
+    case OpKind::Pow: return (d == DType::F64 ? "pow(" : "powf(") + a[0] + "," + a[1] + ")";
+    case OpKind::Max: return "rg_max<" + T + ">(" + a[0] + "," + a[1] + ")";
+    case OpKind::Min: return "rg_min<" + T + ">(" + a[0] + "," + a[1] + ")";
+    case OpKind::Gt: return "((" + a[0] + " > " + a[1] + ") ? (" + T + ")1 : (" + T + ")0)";
+    case OpKind::Ge: return "((" + a[0] + " >= " + a[1] + ") ? (" + T + ")1 : (" + T + ")0)";
+    case OpKind::Where: return "((" + a[0] + " != (" + T + ")0) ? " + a[1] + " : " + a[2] + ")";
+    default: throw std::runtime_error(std::string("op is not elementwise: ") + op.name());
+  }
+}
+
+}  // namespace
+
+std::string ElemSpec::source_key() const {
+  std::string k = "d" + std::to_string((int)dtype) + "|";
+  for (auto& in : inputs) k += std::to_string((int)in.kind) + ",";
+  k += "|";
+  for (auto& m : ops) {
+    k += std::to_string((int)m.op.kind) + ":" + std::to_string(m.reg) + "(";
+    for (auto& a : m.args) k += (a.reg ? "r" : "i") + std::to_string(a.idx) + ",";
+    k += ")";
+  }
+  k += "|";
+  for (auto r : out_regs) k += std::to_string(r) + ",";
+  return k;
+}
+
+ElemSpec spec_from_group(const rg::Fused& f) {
+  ElemSpec s;
+  s.dtype = f.dtype;
+  s.shape = f.shape;
+  s.n = f.n;
+  int nbc = 0;
+  for (size_t k = 0; k < f.inputs.size(); ++k) {
+    ElemSpec::In in;
+    in.kind = f.inputs[k].kind;
+    in.row = f.inputs[k].row;
+    in.shape = f.input_shapes[k];
+    if (in.kind == ArgKind::Broadcast) in.bc = nbc++;
+    s.inputs.push_back(in);
+  }
+  s.ops = f.ops;
+  for (auto& o : f.outputs) s.out_regs.push_back(o.first);
+  return s;
+}
+
+ElemSpec spec_from_instr(const rg::Instr& i) {
+  ElemSpec s;
+  s.dtype = i.dtype;
+  s.shape = i.shape;
+  s.n = i.n;
+  size_t reg = 0;
+  rg::MicroOp m;
+  m.op = i.op;
+  int nbc = 0;
+  for (size_t k = 0; k < i.args.size(); ++k) {
+    const auto& as = i.arg_shapes[k];
+    ElemSpec::In in;
+    in.shape = as;
+    size_t n = rg::product(as);
+    if (as == i.shape) in.kind = ArgKind::Full;
+    else if (n == 1) in.kind = ArgKind::Splat;
+    else if (!as.empty() && !i.shape.empty() && as.back() == i.shape.back() && n == as.back()) {
+      in.kind = ArgKind::Row;
+      in.row = n;
+    } else {
+      in.kind = ArgKind::Broadcast;
+      in.bc = nbc++;
+    }
+    if (in.kind == ArgKind::Full) {
+      m.args.push_back(rg::Operand{false, k});
+    } else {
+      m.args.push_back(rg::Operand{true, reg});
+      ++reg;
+    }
+    s.inputs.push_back(in);
+  }
+  // Registers of non-full inputs come first, in input order, as in compile_group.
+  m.reg = reg;
+  s.ops.push_back(m);
+  s.out_regs.push_back(reg);
+  return s;
+}
+
+static std::string kernel_source(const ElemSpec& s, const std::string& name) {
+  std::ostringstream o;
+  std::string T = ctype(s.dtype), VT = vtype(s.dtype);
+  int VW = vwidth(s.dtype);
+  // Map: non-full input k -> register; compile_group assigns registers in input order.
+  std::vector<long> in_reg(s.inputs.size(), -1);
+  {
+    size_t r = 0;
+    for (size_t k = 0; k < s.inputs.size(); ++k)
+      if (s.inputs[k].kind != ArgKind::Full) in_reg[k] = (long)r++;
+  }
+  o << "extern \"C\" __global__ void __launch_bounds__(256) " << name << "(const ElemArgs a) {\n";
+  o << "  const long long n = a.n;\n";
+  o << "  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x, stride = (long long)gridDim.x * blockDim.x;\n";
+  for (size_t k = 0; k < s.inputs.size(); ++k)
+    if (s.inputs[k].kind == ArgKind::Splat) o << "  const " << T << " sp" << k << " = ((const " << T << "*)a.in[" << k << "])[0];\n";
+  auto emit = [&](int V, bool vec) {
+    const char* e0 = "e0";
+    for (size_t k = 0; k < s.inputs.size(); ++k) {
+      const auto& in = s.inputs[k];
+      if (in.kind == ArgKind::Full) {
+        o << "    " << T << " i" << k << "[" << V << "];\n";
+        if (!vec) {
+          o << "    i" << k << "[0] = ((const " << T << "*)a.in[" << k << "])[" << e0 << "];\n";
+        } else {
+          o << "    { " << VT << " v = ((const " << VT << "*)a.in[" << k << "])[" << e0 << " / " << V << "];";
+          for (int j = 0; j < V; ++j) o << " i" << k << "[" << j << "] = v." << lane(j) << ";";
+          o << " }\n";
+        }
+      } else {
+        long r = in_reg[k];
+        o << "    " << T << " r" << r << "[" << V << "];\n";
+        o << "    #pragma unroll\n    for (int j = 0; j < " << V << "; ++j) ";
+        if (in.kind == ArgKind::Splat) o << "r" << r << "[j] = sp" << k << ";\n";
+        else if (in.kind == ArgKind::Row) o << "r" << r << "[j] = ((const " << T << "*)a.in[" << k << "])[(" << e0 << " + j) % a.row[" << k << "]];\n";
+        else o << "r" << r << "[j] = ((const " << T << "*)a.in[" << k << "])[bc_off(a.bc[" << in.bc << "], " << e0 << " + j)];\n";
+      }
+    }
+    for (auto& m : s.ops) {
+      o << "    " << T << " r" << m.reg << "[" << V << "];\n";
+      o << "    #pragma unroll\n    for (int j = 0; j < " << V << "; ++j) r" << m.reg << "[j] = ";
+      std::vector<std::string> args;
+      for (auto& a : m.args) args.push_back((a.reg ? "r" : "i") + std::to_string(a.idx) + "[j]");
+      o << expr(s.dtype, m.op, args) << ";\n";
+    }
+    for (size_t q = 0; q < s.out_regs.size(); ++q) {
+      size_t r = s.out_regs[q];
+      if (!vec) {
+        o << "    ((" << T << "*)a.out[" << q << "])[" << e0 << "] = r" << r << "[0];\n";
+      } else {
+        o << "    { " << VT << " v;";
+        for (int j = 0; j < V; ++j) o << " v." << lane(j) << " = r" << r << "[" << j << "];";
+        o << " ((" << VT << "*)a.out[" << q << "])[" << e0 << " / " << V << "] = v; }\n";
+      }
+    }
+  };
+  o << "  if (a.vec) {\n";
+  o << "    const long long nv = n / " << VW << ";\n";
+  o << "    for (long long q = tid; q < nv; q += stride) {\n    const long long e0 = q * " << VW << ";\n";
+  emit(VW, true);
+  o << "    }\n  } else {\n";
+  o << "    for (long long e0 = tid; e0 < n; e0 += stride) {\n";
+  emit(1, false);
+  o << "    }\n  }\n}\n";
+  return o.str();
+}
+
+static uint64_t fnv1a(const std::string& s) {
+  uint64_t h = 1469598103934665603ull;
+  for (unsigned char c : s) {
+    h ^= c;
+    h *= 1099511628211ull;
+  }
+  return h;
+}
+
+std::string Jit::add(const ElemSpec& s) {
+  std::string key = s.source_key();
+  char name[64];
+  snprintf(name, sizeof name, "rg_elem_%016llx", (unsigned long long)fnv1a(key));
+  if (!built_.count(name) && !pending_.count(name)) pending_[name] = kernel_source(s, name);
+  return name;
+}
+
+static std::string cache_dir() {
+  const char* env = getenv("RGC_JIT_CACHE");
+  std::string d = env ? env : ("/tmp/rgc-jit-" + std::to_string(getuid()));
+  mkdir(d.c_str(), 0700);
+  return d;
+}
+
+void Jit::build() {
+  if (pending_.empty()) return;
+  std::string src = PRELUDE;
+  std::vector<std::string> names;
+  for (auto& [name, s] : pending_) {
+    src += s;
+    names.push_back(name);
+  }
+  const char* opts[] = {"--gpu-architecture=sm_100a", "--fmad=false", "--prec-div=true", "--prec-sqrt=true", "--ftz=false", "-default-device",
+                        "--std=c++17"};
+  std::string path = cache_dir() + "/" + std::to_string(fnv1a(src + "v1")) + ".cubin";
+  std::vector<char> cubin;
+  {
+    std::ifstream f(path, std::ios::binary);
+    if (f) cubin.assign(std::istreambuf_iterator<char>(f), std::istreambuf_iterator<char>());
+  }
+  if (cubin.empty()) {
+    nvrtcProgram prog;
+    if (nvrtcCreateProgram(&prog, src.c_str(), "rg_fused.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS) throw std::runtime_error("nvrtcCreateProgram failed");
+    nvrtcResult r = nvrtcCompileProgram(prog, (int)(sizeof opts / sizeof opts[0]), opts);
+    if (r != NVRTC_SUCCESS) {
+      size_t n = 0;
+      nvrtcGetProgramLogSize(prog, &n);
+      std::string log(n, '\0');
+      nvrtcGetProgramLog(prog, log.data());
+      nvrtcDestroyProgram(&prog);
+      throw std::runtime_error("NVRTC compilation of fused kernels failed: " + log.substr(0, 4000));
+    }
+    size_t n = 0;
+    nvrtcGetCUBINSize(prog, &n);
+    cubin.resize(n);
+    nvrtcGetCUBIN(prog, cubin.data());
+    nvrtcDestroyProgram(&prog);
+    std::string tmp = path + ".tmp" + std::to_string(getpid());
+    std::ofstream f(tmp, std::ios::binary);
+    f.write(cubin.data(), (std::streamsize)cubin.size());
+    f.close();
+    rename(tmp.c_str(), path.c_str());
+  }
+  const Driver& d = Driver::get();
+  CUmodule mod;
+  CUresult lr = d.ModuleLoadData(&mod, cubin.data());
+  if (lr != CUDA_SUCCESS) throw std::runtime_error("loading the fused-kernel module failed (CUresult " + std::to_string((int)lr) + ")");
+  modules_.push_back(mod);
+  for (auto& name : names) {
+    CUfunction fn;
+    if (d.ModuleGetFunction(&fn, mod, name.c_str()) != CUDA_SUCCESS) throw std::runtime_error("missing fused kernel " + name);
+    built_[name] = fn;
+  }
+  pending_.clear();
+}
+
+CUfunction Jit::function(const std::string& name) const {
+  auto it = built_.find(name);
+  if (it == built_.end()) throw std::runtime_error("fused kernel not built: " + name);
+  return it->second;
+}
+
+void Jit::launch(CUfunction f, const ElemArgs& a, long long n, int vec_width, cudaStream_t s) {
+  static int sms = [] {
+    int dev = 0, v = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    return v;
+  }();
+  long long work = a.vec ? n / vec_width : n;
+  long long blocks = (work + 255) / 256;
+  long long cap = (long long)sms * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  void* params[] = {(void*)&a};
+  CUresult r = Driver::get().LaunchKernel(f, (unsigned)blocks, 1, 1, 256, 1, 1, 0, (CUstream)s, params, nullptr);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("fused kernel launch failed (CUresult " + std::to_string((int)r) + ")");
+}
+
+}  // namespace rgc

@@ -1,0 +1,82 @@
+// NVRTC code generation for fused elementwise groups (plan.rs:86-111 `Fused`).
+//
+// A group's kernel is generated from its structure alone: dtype, the kind of each input
+// (full, splat, row, broadcast), the micro-op list and the outputs. Sizes, row lengths and
+// broadcast strides are runtime parameters, so the layers of a model share kernels and a
+// whole plan's kernels compile in one NVRTC call for sm_100a.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "kernels.cuh"
+#include "plan.h"
+
+namespace rgc {
+
+constexpr int JIT_MAX_IN = 64;
+constexpr int JIT_MAX_OUT = 64;
+
+// Must match the struct emitted into every generated kernel.
+struct ElemArgs {
+  long long n;
+  int vec;  // 1: full operands are 16-byte aligned and n is a multiple of the vector width
+  int pad;
+  void* out[JIT_MAX_OUT];
+  const void* in[JIT_MAX_IN];
+  long long row[JIT_MAX_IN];
+  const Dims* bc;  // device array: one descriptor per broadcast input
+};
+
+// A generated elementwise kernel: the structure (which decides the source) plus which argument
+// slot each group input and output binds to at launch.
+struct ElemSpec {
+  rg::DType dtype = rg::DType::F32;
+  struct In {
+    rg::ArgKind kind;
+    size_t row = 0;
+    int bc = -1;  // broadcast descriptor index
+    std::vector<size_t> shape;
+  };
+  std::vector<In> inputs;
+  std::vector<rg::MicroOp> ops;
+  std::vector<size_t> out_regs;
+  std::vector<size_t> shape;  // output shape
+  size_t n = 0;
+  std::string source_key() const;
+};
+
+// Builds an ElemSpec from a fused group or from a single elementwise instruction.
+ElemSpec spec_from_group(const rg::Fused& f);
+ElemSpec spec_from_instr(const rg::Instr& i);
+
+class Jit {
+ public:
+  // Registers a kernel; returns its name. Nothing compiles until `build`.
+  std::string add(const ElemSpec& s);
+  // Compiles every registered kernel not yet built (one NVRTC program) and loads it.
+  void build();
+  CUfunction function(const std::string& name) const;
+  static void launch(CUfunction f, const ElemArgs& a, long long n, int vec_width, cudaStream_t s);
+
+ private:
+  std::unordered_map<std::string, std::string> pending_;  // name -> source
+  std::unordered_map<std::string, CUfunction> built_;
+  std::vector<CUmodule> modules_;
+};
+
+// Driver entry points, resolved through the runtime so that nothing links libcuda directly.
+struct Driver {
+  CUresult (*ModuleLoadData)(CUmodule*, const void*) = nullptr;
+  CUresult (*ModuleGetFunction)(CUfunction*, CUmodule, const char*) = nullptr;
+  CUresult (*ModuleUnload)(CUmodule) = nullptr;
+  CUresult (*LaunchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, CUstream, void**, void**) = nullptr;
+  static const Driver& get();
+};
+
+}  // namespace rgc

@@ -1,0 +1,799 @@
+// Hand-written sm_100a kernels of the rg CUDA device (built with -fmad=false, IEEE division and
+// square root, so single operations round exactly as rg's CPU interpreter does).
+#include <cfloat>
+#include <cmath>
+#include <cstdio>
+
+#include "kernels.cuh"
+
+namespace rgc {
+
+namespace {
+
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  }
+  return n;
+}
+
+// Grid-stride launches use a multiple of the SM count: a few resident blocks per SM.
+unsigned grid_for(long long n, int threads = 256) {
+  long long b = (n + threads - 1) / threads;
+  long long cap = (long long)sm_count() * 8;
+  if (b > cap) b = cap;
+  if (b < 1) b = 1;
+  return (unsigned)b;
+}
+
+template <typename T> __device__ __forceinline__ T qnan();
+template <> __device__ __forceinline__ float qnan<float>() { return __int_as_float(0x7fc00000); }
+template <> __device__ __forceinline__ double qnan<double>() { return __longlong_as_double(0x7ff8000000000000LL); }
+
+template <typename T> __device__ __forceinline__ T rg_max(T a, T b) { return a > b ? a : (b >= a ? b : qnan<T>()); }
+template <typename T> __device__ __forceinline__ T rg_min(T a, T b) { return a < b ? a : (b <= a ? b : qnan<T>()); }
+
+template <typename T> __device__ __forceinline__ T combine(Red op, T acc, T x) {
+  return op == Red::Sum ? acc + x : op == Red::Max ? rg_max(acc, x) : rg_min(acc, x);
+}
+template <typename T> __device__ __forceinline__ T red_init(Red op) {
+  return op == Red::Sum ? (T)0 : op == Red::Max ? -(T)INFINITY : (T)INFINITY;
+}
+
+__device__ __forceinline__ long long clamp_index(int ix, long long dim) {
+  long long v = ix < 0 ? 0 : (long long)ix;
+  return v < dim - 1 ? v : dim - 1;
+}
+
+__device__ __forceinline__ unsigned long long mix(unsigned long long z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ unsigned long long read_key(const int32_t* k) {
+  return ((unsigned long long)(uint32_t)k[0] << 32) | (unsigned long long)(uint32_t)k[1];
+}
+
+#define GRID_STRIDE(e, n) for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < (n); e += (long long)gridDim.x * blockDim.x)
+
+// ---------------- memory movement ----------------
+
+template <typename T> __global__ void k_gather(T* __restrict__ dst, const T* __restrict__ src, Dims out, long long base, long long n) {
+  GRID_STRIDE(e, n) {
+    long long r = e, off = base;
+    for (int d = out.rank - 1; d >= 0; --d) {
+      long long c = r % out.d[d];
+      r /= out.d[d];
+      off += c * out.st[d];
+    }
+    dst[e] = src[off];
+  }
+}
+
+template <typename T> __global__ void k_scatter(T* __restrict__ dst, const T* __restrict__ src, Dims in, long long base, long long n) {
+  GRID_STRIDE(e, n) {
+    long long r = e, off = base;
+    for (int d = in.rank - 1; d >= 0; --d) {
+      long long c = r % in.d[d];
+      r /= in.d[d];
+      off += c * in.st[d];
+    }
+    dst[off] = src[e];
+  }
+}
+
+// 32x32 tiles through shared memory; the +1 column avoids bank conflicts.
+template <typename T> __global__ void k_transpose2(T* __restrict__ dst, const T* __restrict__ src, long long rows, long long cols) {
+  __shared__ T tile[32][33];
+  long long b = blockIdx.z;
+  const T* s = src + b * rows * cols;
+  T* d = dst + b * rows * cols;
+  long long c0 = (long long)blockIdx.x * 32, r0 = (long long)blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    long long r = r0 + i, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) tile[i][threadIdx.x] = s[r * cols + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    long long c = c0 + i, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) d[c * rows + r] = tile[threadIdx.x][i];
+  }
+}
+
+// ---------------- indexing ----------------
+
+template <typename T>
+__global__ void k_take_rows(T* __restrict__ dst, const T* __restrict__ src, const int32_t* __restrict__ idx, long long dim, long long n_idx,
+                            long long block, long long n) {
+  GRID_STRIDE(e, n) {
+    long long row = e / block, col = e - row * block;
+    long long j = row % n_idx, o = row / n_idx;
+    dst[e] = src[(o * dim + clamp_index(idx[j], dim)) * block + col];
+  }
+}
+
+template <typename T>
+__global__ void k_take_along(T* __restrict__ dst, const T* __restrict__ src, const int32_t* __restrict__ idx, long long n, long long v, long long k) {
+  GRID_STRIDE(j, n) { dst[j] = src[(j / k) * v + clamp_index(idx[j], v)]; }
+}
+
+// One block per destination row (o, r): the block scans the indices in chunks, compacts the
+// matching positions in ascending order, and every thread adds those rows for its columns in
+// that order, from zero: the same sequence of additions as plan.rs:1502-1519.
+template <typename T>
+__global__ void k_take_grad(T* __restrict__ dst, const T* __restrict__ ct, const int32_t* __restrict__ idx, long long dim, long long n_idx,
+                            long long block) {
+  __shared__ int hits[256];
+  __shared__ int warp_count[8];
+  __shared__ int total;
+  const long long r = blockIdx.x, o = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // Each thread owns columns threadIdx.x, +256, ...; block is usually <= 4 * 256.
+  constexpr int MAXC = 8;
+  T acc[MAXC];
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) acc[c] = (T)0;
+  T* out = dst + (o * dim + r) * block;
+  const T* base = ct + o * n_idx * block;
+  bool wide = block > 256 * MAXC;
+  if (wide) {
+    for (long long c = threadIdx.x; c < block; c += 256) out[c] = (T)0;
+  }
+  for (long long j0 = 0; j0 < n_idx; j0 += 256) {
+    long long j = j0 + threadIdx.x;
+    bool match = j < n_idx && clamp_index(idx[j], dim) == r;
+    unsigned ballot = __ballot_sync(0xffffffffu, match);
+    if (lane == 0) warp_count[warp] = __popc(ballot);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int t = 0;
+      for (int w = 0; w < 8; ++w) {
+        int c = warp_count[w];
+        warp_count[w] = t;
+        t += c;
+      }
+      total = t;
+    }
+    __syncthreads();
+    if (match) hits[warp_count[warp] + __popc(ballot & ((1u << lane) - 1u))] = (int)(j - j0);
+    __syncthreads();
+    int m = total;
+    for (int q = 0; q < m; ++q) {
+      const T* row = base + (j0 + hits[q]) * block;
+      if (!wide) {
+#pragma unroll
+        for (int c = 0; c < MAXC; ++c) {
+          long long col = threadIdx.x + 256LL * c;
+          if (col < block) acc[c] = acc[c] + row[col];
+        }
+      } else {
+        for (long long col = threadIdx.x; col < block; col += 256) out[col] = out[col] + row[col];
+      }
+    }
+    __syncthreads();
+  }
+  if (!wide) {
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c) {
+      long long col = threadIdx.x + 256LL * c;
+      if (col < block) out[col] = acc[c];
+    }
+  }
+}
+
+template <typename T>
+__global__ void k_take_along_grad(T* __restrict__ dst, const T* __restrict__ ct, const int32_t* __restrict__ idx, long long rows, long long v,
+                                  long long k) {
+  GRID_STRIDE(e, rows * v) {
+    long long row = e / v, c = e - row * v;
+    T acc = (T)0;
+    for (long long q = 0; q < k; ++q)
+      if (clamp_index(idx[row * k + q], v) == c) acc = acc + ct[row * k + q];
+    dst[e] = acc;
+  }
+}
+
+// ---------------- reductions ----------------
+
+// rg's fast_sum (plan.rs:1213-1230) for n small enough to do in one warp: lanes 0..7 each add
+// every eighth element in order, then lane 0 adds the eight lanes and the tail.
+template <typename T> __global__ void k_sum_exact(T* dst, const T* __restrict__ a, long long n) {
+  __shared__ T lanes[8];
+  int l = threadIdx.x;
+  long long full = n / 8 * 8;
+  if (l < 8) {
+    T acc = (T)0;
+    long long c = 0;
+    // Loads run ahead of the dependent additions.
+    for (; c + 8 * 16 <= full; c += 8 * 16) {
+      T v[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) v[u] = a[c + 8 * u + l];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) acc = acc + v[u];
+    }
+    for (; c < full; c += 8) acc = acc + a[c + l];
+    lanes[l] = acc;
+  }
+  __syncthreads();
+  if (l == 0) {
+    T out = (T)0;
+    for (int k = 0; k < 8; ++k) out = out + lanes[k];
+    for (long long i = full; i < n; ++i) out = out + a[i];
+    dst[0] = out;
+  }
+}
+
+// Fixed-order block sums: block b sums [b*chunk, (b+1)*chunk) with a fixed tree.
+template <typename T> __device__ T block_sum(T v) {
+  __shared__ T sh[32];
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+  int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  int nw = (blockDim.x + 31) >> 5;
+  v = threadIdx.x < nw ? sh[threadIdx.x] : (T)0;
+  if (warp == 0)
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+  __syncthreads();
+  return v;
+}
+
+template <typename T> __global__ void k_sum_chunks(T* __restrict__ part, const T* __restrict__ a, long long n, long long chunk) {
+  long long s = (long long)blockIdx.x * chunk, e = s + chunk < n ? s + chunk : n;
+  T v = (T)0;
+  for (long long i = s + threadIdx.x; i < e; i += blockDim.x) v += a[i];
+  v = block_sum(v);
+  if (threadIdx.x == 0) part[blockIdx.x] = v;
+}
+
+template <typename T> __global__ void k_sum_final(T* dst, const T* __restrict__ part, long long m) {
+  T v = (T)0;
+  for (long long i = threadIdx.x; i < m; i += blockDim.x) v += part[i];
+  v = block_sum(v);
+  if (threadIdx.x == 0) dst[0] = v;
+}
+
+// Warp per row for short rows, block per row for long ones.
+template <typename T> __global__ void k_reduce_rows_warp(T* __restrict__ dst, const T* __restrict__ a, Red op, long long rows, long long len) {
+  long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  for (long long r = warp; r < rows; r += nwarps) {
+    const T* row = a + r * len;
+    T acc = red_init<T>(op);
+    for (long long j = lane; j < len; j += 32) acc = combine(op, acc, row[j]);
+    for (int o = 16; o > 0; o >>= 1) acc = combine(op, acc, __shfl_down_sync(0xffffffffu, acc, o));
+    if (lane == 0) dst[r] = acc;
+  }
+}
+
+template <typename T> __global__ void k_reduce_rows_block(T* __restrict__ dst, const T* __restrict__ a, Red op, long long len) {
+  __shared__ T sh[32];
+  const T* row = a + (long long)blockIdx.x * len;
+  T acc = red_init<T>(op);
+  for (long long j = threadIdx.x; j < len; j += blockDim.x) acc = combine(op, acc, row[j]);
+  for (int o = 16; o > 0; o >>= 1) acc = combine(op, acc, __shfl_down_sync(0xffffffffu, acc, o));
+  int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) sh[warp] = acc;
+  __syncthreads();
+  if (warp == 0) {
+    int nw = blockDim.x >> 5;
+    acc = lane < nw ? sh[lane] : red_init<T>(op);
+    for (int o = 16; o > 0; o >>= 1) acc = combine(op, acc, __shfl_down_sync(0xffffffffu, acc, o));
+    if (lane == 0) dst[blockIdx.x] = acc;
+  }
+}
+
+constexpr long long REDUCE_ROWS = 64;
+
+template <typename T>
+__global__ void k_cols_partial(T* __restrict__ part, const T* __restrict__ a, Red op, long long rows, long long cols) {
+  long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  long long q = blockIdx.y;
+  long long r0 = q * REDUCE_ROWS, r1 = r0 + REDUCE_ROWS < rows ? r0 + REDUCE_ROWS : rows;
+  T acc = red_init<T>(op);
+  for (long long r = r0; r < r1; ++r) acc = combine(op, acc, a[r * cols + c]);
+  part[q * cols + c] = acc;
+}
+
+template <typename T> __global__ void k_cols_final(T* __restrict__ dst, const T* __restrict__ part, Red op, long long nparts, long long cols) {
+  GRID_STRIDE(c, cols) {
+    T acc = red_init<T>(op);
+    for (long long q = 0; q < nparts; ++q) acc = combine(op, acc, part[q * cols + c]);
+    dst[c] = acc;
+  }
+}
+
+template <typename T>
+__global__ void k_reduce_generic(T* __restrict__ dst, const T* __restrict__ a, Red op, Dims kept, Dims red, long long n_out, long long n_red) {
+  GRID_STRIDE(o, n_out) {
+    long long r = o, base = 0;
+    for (int d = kept.rank - 1; d >= 0; --d) {
+      long long c = r % kept.d[d];
+      r /= kept.d[d];
+      base += c * kept.st[d];
+    }
+    T acc = red_init<T>(op);
+    for (long long q = 0; q < n_red; ++q) {
+      long long rr = q, off = base;
+      for (int d = red.rank - 1; d >= 0; --d) {
+        long long c = rr % red.d[d];
+        rr /= red.d[d];
+        off += c * red.st[d];
+      }
+      acc = combine(op, acc, a[off]);
+    }
+    dst[o] = acc;
+  }
+}
+
+// ---------------- matrix products ----------------
+
+template <typename T, bool EXACT> __device__ __forceinline__ T mac(T acc, T a, T b);
+template <> __device__ __forceinline__ float mac<float, true>(float acc, float a, float b) { return __fadd_rn(acc, __fmul_rn(a, b)); }
+template <> __device__ __forceinline__ float mac<float, false>(float acc, float a, float b) { return fmaf(a, b, acc); }
+template <> __device__ __forceinline__ double mac<double, true>(double acc, double a, double b) { return __dadd_rn(acc, __dmul_rn(a, b)); }
+template <> __device__ __forceinline__ double mac<double, false>(double acc, double a, double b) { return fma(a, b, acc); }
+
+// 64x64 output tile per block, 16-deep k slices through shared memory, 4x4 outputs per thread.
+// Each output has one accumulator and k is visited in ascending order, so the EXACT variant
+// performs rg's additions in rg's order.
+template <typename T, bool EXACT>
+__global__ void __launch_bounds__(256) k_gemm(T* __restrict__ C, const T* __restrict__ A, const T* __restrict__ B, long long m, long long n,
+                                              long long k, bool ta, bool tb, GemmBatch bt) {
+  constexpr int BM = 64, BN = 64, BK = 16;
+  __shared__ T As[BK][BM + 4];
+  __shared__ T Bs[BK][BN + 4];
+  long long z = blockIdx.z, oa = 0, ob = 0;
+  {
+    long long r = z;
+    for (int d = bt.rank - 1; d >= 0; --d) {
+      long long c = r % bt.d[d];
+      r /= bt.d[d];
+      oa += c * bt.sa[d];
+      ob += c * bt.sb[d];
+    }
+  }
+  const T* Ab = A + oa;
+  const T* Bb = B + ob;
+  T* Cb = C + z * m * n;
+  long long row0 = (long long)blockIdx.y * BM, col0 = (long long)blockIdx.x * BN;
+  int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  T acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = (T)0;
+  for (long long k0 = 0; k0 < k; k0 += BK) {
+    // A tile: BM x BK, element (i, p) = op(A)[row0+i][k0+p]
+    for (int t = threadIdx.x; t < BM * BK; t += 256) {
+      int i, p;
+      if (ta) { p = t / BM; i = t % BM; } else { i = t / BK; p = t % BK; }
+      long long gr = row0 + i, gk = k0 + p;
+      T v = (T)0;
+      if (gr < m && gk < k) v = ta ? Ab[gk * m + gr] : Ab[gr * k + gk];
+      As[p][i] = v;
+    }
+    for (int t = threadIdx.x; t < BK * BN; t += 256) {
+      int p, j;
+      if (tb) { j = t / BK; p = t % BK; } else { p = t / BN; j = t % BN; }
+      long long gk = k0 + p, gc = col0 + j;
+      T v = (T)0;
+      if (gk < k && gc < n) v = tb ? Bb[gc * k + gk] : Bb[gk * n + gc];
+      Bs[p][j] = v;
+    }
+    __syncthreads();
+    long long kmax = k - k0 < BK ? k - k0 : BK;
+    for (int p = 0; p < kmax; ++p) {
+      T av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) av[i] = As[p][ty + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) bv[j] = Bs[p][tx + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = mac<T, EXACT>(acc[i][j], av[i], bv[j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    long long r = row0 + ty + 16 * i;
+    if (r >= m) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      long long c = col0 + tx + 16 * j;
+      if (c < n) Cb[r * n + c] = acc[i][j];
+    }
+  }
+}
+
+// ---------------- random numbers ----------------
+
+constexpr unsigned long long GAMMA = 0x9E3779B97F4A7C15ULL;
+constexpr unsigned long long GAMMA_SPLIT = 0xD1B54A32D192ED03ULL;
+
+__global__ void k_key_split(int32_t* dst, const int32_t* key, long long pairs) {
+  unsigned long long kk = read_key(key);
+  GRID_STRIDE(j, pairs) {
+    unsigned long long bits = mix(kk + (unsigned long long)(j + 1) * GAMMA_SPLIT);
+    dst[2 * j] = (int32_t)(uint32_t)(bits >> 32);
+    dst[2 * j + 1] = (int32_t)(uint32_t)bits;
+  }
+}
+
+template <typename T> __global__ void k_rand_uniform(T* dst, const int32_t* key, long long n) {
+  unsigned long long kk = read_key(key);
+  const int mant = sizeof(T) == 4 ? 24 : 53;
+  const double scale = sizeof(T) == 4 ? 5.9604644775390625e-08 : 1.1102230246251565e-16;
+  GRID_STRIDE(j, n) {
+    unsigned long long bits = mix(kk + (unsigned long long)(j + 1) * GAMMA) >> (64 - mant);
+    dst[j] = (T)((double)bits * scale);
+  }
+}
+
+template <typename T> __global__ void k_rand_normal(T* dst, const int32_t* key, long long n) {
+  unsigned long long kk = read_key(key);
+  const double two53 = 1.1102230246251565e-16;
+  const double TAU = 6.283185307179586;
+  GRID_STRIDE(j, n) {
+    double u1 = 1.0 - (double)(mix(kk + (unsigned long long)(2 * j + 1) * GAMMA) >> 11) * two53;
+    double u2 = (double)(mix(kk + (unsigned long long)(2 * j + 2) * GAMMA) >> 11) * two53;
+    dst[j] = (T)(sqrt(-2.0 * log(u1)) * cos(TAU * u2));
+  }
+}
+
+// ---------------- conversions and selection ----------------
+
+// Rust `as` from float to i32: truncate, saturate, NaN -> 0 (plan.rs:1624-1642).
+__device__ __forceinline__ int32_t to_i32(double x) {
+  if (x != x) return 0;
+  if (x >= 2147483647.0) return 2147483647;
+  if (x <= -2147483648.0) return (int32_t)(-2147483647 - 1);
+  return (int32_t)x;
+}
+
+template <typename D, typename S> __global__ void k_cast(D* dst, const S* src, long long n) {
+  GRID_STRIDE(j, n) { dst[j] = (D)src[j]; }
+}
+template <typename S> __global__ void k_cast_i32(int32_t* dst, const S* src, long long n) {
+  GRID_STRIDE(j, n) { dst[j] = to_i32((double)src[j]); }
+}
+
+// First index of the maximum, scanning with `x > best` (plan.rs:1437-1451): NaN never wins,
+// and a NaN at index 0 wins the whole row.
+template <typename T> __global__ void k_argmax(int32_t* dst, const T* __restrict__ a, long long rows, long long v) {
+  long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  for (long long r = warp; r < rows; r += nwarps) {
+    const T* row = a + r * v;
+    bool valid = false;
+    T bv = (T)0;
+    long long bi = 0;
+    for (long long j = lane; j < v; j += 32) {
+      T x = row[j];
+      if (x != x) continue;
+      if (!valid || x > bv) {
+        valid = true;
+        bv = x;
+        bi = j;
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      bool ov = __shfl_down_sync(0xffffffffu, (int)valid, o);
+      T ovv = __shfl_down_sync(0xffffffffu, bv, o);
+      long long oi = __shfl_down_sync(0xffffffffu, bi, o);
+      if (ov && (!valid || ovv > bv || (ovv == bv && oi < bi))) {
+        valid = true;
+        bv = ovv;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      T x0 = row[0];
+      dst[r] = (x0 != x0 || !valid) ? 0 : (int32_t)bi;
+    }
+  }
+}
+
+// Rank of each element under rg's total order (larger first, ties by index, NaN last); the
+// element of rank p < k is output p (plan.rs:833-866).
+template <typename T> __global__ void k_arg_top_k(int32_t* dst, const T* __restrict__ a, long long v, long long k) {
+  const T* row = a + (long long)blockIdx.x * v;
+  for (long long i = threadIdx.x; i < v; i += blockDim.x) {
+    T p = row[i];
+    bool pn = p != p;
+    long long rank = 0;
+    for (long long j = 0; j < v; ++j) {
+      T q = row[j];
+      bool qn = q != q;
+      bool before;
+      if (pn || qn) before = (pn != qn) ? pn : (j < i);
+      else before = q > p || (q == p && j < i);
+      rank += before;
+    }
+    if (rank < k) dst[(long long)blockIdx.x * k + rank] = (int32_t)i;
+  }
+}
+
+template <typename T> __global__ void k_cumsum(T* dst, const T* __restrict__ a, long long rows, long long v, bool reverse) {
+  GRID_STRIDE(r, rows) {
+    T acc = (T)0;
+    if (reverse) {
+      for (long long j = v - 1; j >= 0; --j) {
+        acc = acc + a[r * v + j];
+        dst[r * v + j] = acc;
+      }
+    } else {
+      for (long long j = 0; j < v; ++j) {
+        acc = acc + a[r * v + j];
+        dst[r * v + j] = acc;
+      }
+    }
+  }
+}
+
+__global__ void k_cumsum_i32(int32_t* dst, const int32_t* __restrict__ a, long long rows, long long v, bool reverse) {
+  GRID_STRIDE(r, rows) {
+    uint32_t acc = 0;
+    if (reverse) {
+      for (long long j = v - 1; j >= 0; --j) dst[r * v + j] = (int32_t)(acc += (uint32_t)a[r * v + j]);
+    } else {
+      for (long long j = 0; j < v; ++j) dst[r * v + j] = (int32_t)(acc += (uint32_t)a[r * v + j]);
+    }
+  }
+}
+
+// ---------------- run loop support ----------------
+
+__global__ void k_record_history(double* history, const void* const* slots, const int* types, int n, const long long* step, long long* bad) {
+  long long k = *step;
+  bool bad_now = false;
+  for (int h = 0; h < n; ++h) {
+    double v;
+    if (types[h] == 0) v = (double)*(const float*)slots[h];
+    else if (types[h] == 1) v = *(const double*)slots[h];
+    else v = (double)*(const int32_t*)slots[h];
+    history[k * n + h] = v;
+    bad_now = bad_now || !isfinite(v);
+  }
+  if (bad_now && *bad < 0) *bad = k;
+}
+
+__global__ void k_bump(long long* c) { *c += 1; }
+
+__global__ void k_load_batch(char* dst, const char* batches, size_t bytes, long long nb, const long long* counter) {
+  const char* src = batches + (size_t)(*counter % nb) * bytes;
+  GRID_STRIDE(i, (long long)bytes) { dst[i] = src[i]; }
+}
+
+template <typename T> __global__ void k_nonfinite(const T* a, long long n, int* flag) {
+  GRID_STRIDE(i, n) {
+    if (!isfinite(a[i])) *flag = 1;
+  }
+}
+
+}  // namespace
+
+size_t esize(EType t) { return t == EType::F64 ? 8 : 4; }
+
+void fill_zero(void* dst, size_t bytes, cudaStream_t s) { cudaMemsetAsync(dst, 0, bytes, s); }
+
+#define DISPATCH(t, F, ...)                 \
+  switch (t) {                              \
+    case EType::F32: F<float>(__VA_ARGS__); break;  \
+    case EType::F64: F<double>(__VA_ARGS__); break; \
+    default: F<int32_t>(__VA_ARGS__); break;        \
+  }
+
+template <typename T> static void gather_t(void* dst, const void* src, const Dims& out, long long base, long long n, cudaStream_t s) {
+  k_gather<T><<<grid_for(n), 256, 0, s>>>((T*)dst, (const T*)src, out, base, n);
+}
+void strided_gather(void* dst, const void* src, EType t, const Dims& out, long long base, long long n, cudaStream_t s) {
+  if (n <= 0) return;
+  DISPATCH(t, gather_t, dst, src, out, base, n, s);
+}
+
+template <typename T> static void scatter_t(void* dst, const void* src, const Dims& in, long long base, long long n, cudaStream_t s) {
+  k_scatter<T><<<grid_for(n), 256, 0, s>>>((T*)dst, (const T*)src, in, base, n);
+}
+void strided_scatter(void* dst, const void* src, EType t, const Dims& in, long long base, long long n, cudaStream_t s) {
+  if (n <= 0) return;
+  DISPATCH(t, scatter_t, dst, src, in, base, n, s);
+}
+
+template <typename T> static void transpose_t(void* dst, const void* src, long long batch, long long rows, long long cols, cudaStream_t s) {
+  dim3 grid((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32), (unsigned)batch);
+  k_transpose2<T><<<grid, dim3(32, 8), 0, s>>>((T*)dst, (const T*)src, rows, cols);
+}
+void transpose_last2(void* dst, const void* src, EType t, long long batch, long long rows, long long cols, cudaStream_t s) {
+  if (batch * rows * cols <= 0) return;
+  DISPATCH(t, transpose_t, dst, src, batch, rows, cols, s);
+}
+
+template <typename T>
+static void take_rows_t(void* dst, const void* src, const int32_t* idx, long long outer, long long dim, long long n_idx, long long block, cudaStream_t s) {
+  long long n = outer * n_idx * block;
+  k_take_rows<T><<<grid_for(n), 256, 0, s>>>((T*)dst, (const T*)src, idx, dim, n_idx, block, n);
+}
+void take_rows(void* dst, const void* src, const int32_t* idx, EType t, long long outer, long long dim, long long n_idx, long long block,
+               cudaStream_t s) {
+  if (outer * n_idx * block <= 0) return;
+  DISPATCH(t, take_rows_t, dst, src, idx, outer, dim, n_idx, block, s);
+}
+
+template <typename T> static void take_along_t(void* dst, const void* src, const int32_t* idx, long long n, long long v, long long k, cudaStream_t s) {
+  k_take_along<T><<<grid_for(n), 256, 0, s>>>((T*)dst, (const T*)src, idx, n, v, k);
+}
+void take_along(void* dst, const void* src, const int32_t* idx, EType t, long long n, long long v, long long k, cudaStream_t s) {
+  if (n <= 0) return;
+  DISPATCH(t, take_along_t, dst, src, idx, n, v, k, s);
+}
+
+void take_grad(void* dst, const void* ct, const int32_t* idx, EType t, long long outer, long long dim, long long n_idx, long long block,
+               cudaStream_t s) {
+  if (outer * dim * block <= 0) return;
+  dim3 grid((unsigned)dim, (unsigned)outer);
+  if (t == EType::F64) k_take_grad<double><<<grid, 256, 0, s>>>((double*)dst, (const double*)ct, idx, dim, n_idx, block);
+  else k_take_grad<float><<<grid, 256, 0, s>>>((float*)dst, (const float*)ct, idx, dim, n_idx, block);
+}
+
+void take_along_grad(void* dst, const void* ct, const int32_t* idx, EType t, long long rows, long long v, long long k, cudaStream_t s) {
+  if (rows * v <= 0) return;
+  if (t == EType::F64) k_take_along_grad<double><<<grid_for(rows * v), 256, 0, s>>>((double*)dst, (const double*)ct, idx, rows, v, k);
+  else k_take_along_grad<float><<<grid_for(rows * v), 256, 0, s>>>((float*)dst, (const float*)ct, idx, rows, v, k);
+}
+
+constexpr long long EXACT_SUM_MAX = 32768;
+constexpr long long SUM_CHUNK = 8192;
+
+size_t full_sum_scratch_bytes(long long n, EType t) {
+  if (n <= EXACT_SUM_MAX) return 0;
+  return (size_t)((n + SUM_CHUNK - 1) / SUM_CHUNK) * esize(t);
+}
+
+void reduce_full_sum(void* dst, const void* src, EType t, long long n, void* scratch, cudaStream_t s) {
+  if (n <= EXACT_SUM_MAX) {
+    if (t == EType::F64) k_sum_exact<double><<<1, 32, 0, s>>>((double*)dst, (const double*)src, n);
+    else k_sum_exact<float><<<1, 32, 0, s>>>((float*)dst, (const float*)src, n);
+    return;
+  }
+  long long parts = (n + SUM_CHUNK - 1) / SUM_CHUNK;
+  if (t == EType::F64) {
+    k_sum_chunks<double><<<(unsigned)parts, 256, 0, s>>>((double*)scratch, (const double*)src, n, SUM_CHUNK);
+    k_sum_final<double><<<1, 1024, 0, s>>>((double*)dst, (const double*)scratch, parts);
+  } else {
+    k_sum_chunks<float><<<(unsigned)parts, 256, 0, s>>>((float*)scratch, (const float*)src, n, SUM_CHUNK);
+    k_sum_final<float><<<1, 1024, 0, s>>>((float*)dst, (const float*)scratch, parts);
+  }
+}
+
+template <typename T> static void rows_t(void* dst, const void* src, Red op, long long rows, long long len, cudaStream_t s) {
+  if (len > 2048) {
+    k_reduce_rows_block<T><<<(unsigned)rows, 1024, 0, s>>>((T*)dst, (const T*)src, op, len);
+  } else {
+    long long threads = rows * 32;
+    k_reduce_rows_warp<T><<<grid_for(threads), 256, 0, s>>>((T*)dst, (const T*)src, op, rows, len);
+  }
+}
+void reduce_rows(void* dst, const void* src, EType t, Red op, long long rows, long long len, cudaStream_t s) {
+  if (rows <= 0) return;
+  if (t == EType::F64) rows_t<double>(dst, src, op, rows, len, s);
+  else rows_t<float>(dst, src, op, rows, len, s);
+}
+
+size_t cols_scratch_bytes(long long rows, long long cols, EType t) {
+  return (size_t)((rows + REDUCE_ROWS - 1) / REDUCE_ROWS) * (size_t)cols * esize(t);
+}
+
+template <typename T> static void cols_t(void* dst, const void* src, Red op, long long rows, long long cols, void* scratch, cudaStream_t s) {
+  long long parts = (rows + REDUCE_ROWS - 1) / REDUCE_ROWS;
+  dim3 grid((unsigned)((cols + 255) / 256), (unsigned)parts);
+  k_cols_partial<T><<<grid, 256, 0, s>>>((T*)scratch, (const T*)src, op, rows, cols);
+  k_cols_final<T><<<grid_for(cols), 256, 0, s>>>((T*)dst, (const T*)scratch, op, parts, cols);
+}
+void reduce_cols(void* dst, const void* src, EType t, Red op, long long rows, long long cols, void* scratch, cudaStream_t s) {
+  if (cols <= 0) return;
+  if (t == EType::F64) cols_t<double>(dst, src, op, rows, cols, scratch, s);
+  else cols_t<float>(dst, src, op, rows, cols, scratch, s);
+}
+
+void reduce_generic(void* dst, const void* src, EType t, Red op, const Dims& kept, const Dims& reduced, long long n_out, cudaStream_t s) {
+  if (n_out <= 0) return;
+  long long n_red = 1;
+  for (int d = 0; d < reduced.rank; ++d) n_red *= reduced.d[d];
+  if (t == EType::F64) k_reduce_generic<double><<<grid_for(n_out), 256, 0, s>>>((double*)dst, (const double*)src, op, kept, reduced, n_out, n_red);
+  else k_reduce_generic<float><<<grid_for(n_out), 256, 0, s>>>((float*)dst, (const float*)src, op, kept, reduced, n_out, n_red);
+}
+
+void gemm(void* c, const void* a, const void* b, EType t, long long m, long long n, long long k, bool ta, bool tb, const GemmBatch& batch,
+          long long count, bool exact, cudaStream_t s) {
+  if (m * n * count <= 0) return;
+  if (k == 0) {
+    cudaMemsetAsync(c, 0, (size_t)(m * n * count) * esize(t), s);
+    return;
+  }
+  dim3 grid((unsigned)((n + 63) / 64), (unsigned)((m + 63) / 64), (unsigned)count);
+  if (t == EType::F64) {
+    if (exact) k_gemm<double, true><<<grid, 256, 0, s>>>((double*)c, (const double*)a, (const double*)b, m, n, k, ta, tb, batch);
+    else k_gemm<double, false><<<grid, 256, 0, s>>>((double*)c, (const double*)a, (const double*)b, m, n, k, ta, tb, batch);
+  } else {
+    if (exact) k_gemm<float, true><<<grid, 256, 0, s>>>((float*)c, (const float*)a, (const float*)b, m, n, k, ta, tb, batch);
+    else k_gemm<float, false><<<grid, 256, 0, s>>>((float*)c, (const float*)a, (const float*)b, m, n, k, ta, tb, batch);
+  }
+}
+
+void key_split(int32_t* dst, const int32_t* key, long long pairs, cudaStream_t s) {
+  if (pairs <= 0) return;
+  k_key_split<<<grid_for(pairs), 256, 0, s>>>(dst, key, pairs);
+}
+
+void rand_uniform(void* dst, const int32_t* key, EType t, long long n, cudaStream_t s) {
+  if (n <= 0) return;
+  if (t == EType::F64) k_rand_uniform<double><<<grid_for(n), 256, 0, s>>>((double*)dst, key, n);
+  else k_rand_uniform<float><<<grid_for(n), 256, 0, s>>>((float*)dst, key, n);
+}
+
+void rand_normal(void* dst, const int32_t* key, EType t, long long n, cudaStream_t s) {
+  if (n <= 0) return;
+  if (t == EType::F64) k_rand_normal<double><<<grid_for(n), 256, 0, s>>>((double*)dst, key, n);
+  else k_rand_normal<float><<<grid_for(n), 256, 0, s>>>((float*)dst, key, n);
+}
+
+void cast(void* dst, EType dt, const void* src, EType st, long long n, cudaStream_t s) {
+  if (n <= 0) return;
+  unsigned g = grid_for(n);
+  if (dt == EType::F32 && st == EType::F64) k_cast<float, double><<<g, 256, 0, s>>>((float*)dst, (const double*)src, n);
+  else if (dt == EType::F64 && st == EType::F32) k_cast<double, float><<<g, 256, 0, s>>>((double*)dst, (const float*)src, n);
+  else if (dt == EType::F32 && st == EType::I32) k_cast<float, int32_t><<<g, 256, 0, s>>>((float*)dst, (const int32_t*)src, n);
+  else if (dt == EType::F64 && st == EType::I32) k_cast<double, int32_t><<<g, 256, 0, s>>>((double*)dst, (const int32_t*)src, n);
+  else if (dt == EType::I32 && st == EType::F32) k_cast_i32<float><<<g, 256, 0, s>>>((int32_t*)dst, (const float*)src, n);
+  else if (dt == EType::I32 && st == EType::F64) k_cast_i32<double><<<g, 256, 0, s>>>((int32_t*)dst, (const double*)src, n);
+}
+
+void argmax(int32_t* dst, const void* src, EType t, long long rows, long long v, cudaStream_t s) {
+  if (rows <= 0) return;
+  if (t == EType::F64) k_argmax<double><<<grid_for(rows * 32), 256, 0, s>>>(dst, (const double*)src, rows, v);
+  else k_argmax<float><<<grid_for(rows * 32), 256, 0, s>>>(dst, (const float*)src, rows, v);
+}
+
+void arg_top_k(int32_t* dst, const void* src, EType t, long long rows, long long v, long long k, cudaStream_t s) {
+  if (rows <= 0) return;
+  if (t == EType::F64) k_arg_top_k<double><<<(unsigned)rows, 256, 0, s>>>(dst, (const double*)src, v, k);
+  else k_arg_top_k<float><<<(unsigned)rows, 256, 0, s>>>(dst, (const float*)src, v, k);
+}
+
+void cumsum(void* dst, const void* src, EType t, long long rows, long long v, bool reverse, cudaStream_t s) {
+  if (rows <= 0 || v <= 0) return;
+  unsigned g = grid_for(rows, 128);
+  if (t == EType::F64) k_cumsum<double><<<g, 128, 0, s>>>((double*)dst, (const double*)src, rows, v, reverse);
+  else if (t == EType::F32) k_cumsum<float><<<g, 128, 0, s>>>((float*)dst, (const float*)src, rows, v, reverse);
+  else k_cumsum_i32<<<g, 128, 0, s>>>((int32_t*)dst, (const int32_t*)src, rows, v, reverse);
+}
+
+void record_history(double* history, const void* const* slots, const int* types, int n, const long long* step, long long* bad_step,
+                    cudaStream_t s) {
+  k_record_history<<<1, 1, 0, s>>>(history, slots, types, n, step, bad_step);
+}
+
+void bump_counter(long long* counter, cudaStream_t s) { k_bump<<<1, 1, 0, s>>>(counter); }
+
+void load_batch(void* dst, const void* batches, size_t bytes, long long n_batches, const long long* counter, cudaStream_t s) {
+  k_load_batch<<<grid_for((long long)bytes), 256, 0, s>>>((char*)dst, (const char*)batches, bytes, n_batches, counter);
+}
+
+void any_nonfinite(const void* src, EType t, long long n, int* flag, cudaStream_t s) {
+  if (n <= 0) return;
+  if (t == EType::F64) k_nonfinite<double><<<grid_for(n), 256, 0, s>>>((const double*)src, n, flag);
+  else if (t == EType::F32) k_nonfinite<float><<<grid_for(n), 256, 0, s>>>((const float*)src, n, flag);
+}
+
+}  // namespace rgc

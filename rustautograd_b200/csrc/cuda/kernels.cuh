@@ -1,0 +1,91 @@
+// Host-side launchers for the hand-written sm_100a kernels of the rg CUDA device.
+// Every kernel is deterministic: the same inputs give the same bits on every run, which the
+// device-resident run loop relies on to replay a chunk of steps exactly.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace rgc {
+
+constexpr int MAXR = 8;  // largest tensor rank the index kernels handle
+
+struct Dims {
+  int rank = 0;
+  long long d[MAXR] = {};   // extents
+  long long st[MAXR] = {};  // strides (elements) paired with the extents
+};
+
+enum class EType : int { F32 = 0, F64 = 1, I32 = 2 };
+
+size_t esize(EType t);
+
+// ---- memory movement ----
+void fill_zero(void* dst, size_t bytes, cudaStream_t s);
+// dst[e] = src[base + sum_d coord_d(e) * src.st[d]] over the output extents `out.d`.
+void strided_gather(void* dst, const void* src, EType t, const Dims& out, long long base, long long n, cudaStream_t s);
+// dst[base + sum_d coord_d(e) * dst.st[d]] = src[e] over the input extents `in.d`.
+void strided_scatter(void* dst, const void* src, EType t, const Dims& in, long long base, long long n, cudaStream_t s);
+// Tiled transpose of the last two axes of a [batch, rows, cols] view: dst[b][c][r] = src[b][r][c].
+void transpose_last2(void* dst, const void* src, EType t, long long batch, long long rows, long long cols, cudaStream_t s);
+
+// ---- indexing (plan.rs:1365-1389, 1502-1531) ----
+void take_rows(void* dst, const void* src, const int32_t* idx, EType t, long long outer, long long dim, long long n_idx,
+               long long block, cudaStream_t s);
+void take_along(void* dst, const void* src, const int32_t* idx, EType t, long long n, long long v, long long k, cudaStream_t s);
+// Deterministic scatter-add: each destination row sums its contributions in ascending index
+// order starting from zero, the order rg's sequential loop adds them.
+void take_grad(void* dst, const void* ct, const int32_t* idx, EType t, long long outer, long long dim, long long n_idx,
+               long long block, cudaStream_t s);
+void take_along_grad(void* dst, const void* ct, const int32_t* idx, EType t, long long rows, long long v, long long k,
+                     cudaStream_t s);
+
+// ---- reductions (plan.rs:1549-1622) ----
+enum class Red : int { Sum = 0, Max = 1, Min = 2 };
+// Full sum in rg's eight-lane order (bit-exact) for small n; a fixed-order tree otherwise.
+// `scratch` needs full_sum_scratch_bytes(n) bytes.
+size_t full_sum_scratch_bytes(long long n, EType t);
+void reduce_full_sum(void* dst, const void* src, EType t, long long n, void* scratch, cudaStream_t s);
+// Rows of length `len` reduced to one value each.
+void reduce_rows(void* dst, const void* src, EType t, Red op, long long rows, long long len, cudaStream_t s);
+// [rows, cols] reduced over rows; two passes over fixed 64-row chunks (the chunking of
+// plan.rs:1593-1612), partials in `scratch` (cols_scratch_bytes bytes).
+size_t cols_scratch_bytes(long long rows, long long cols, EType t);
+void reduce_cols(void* dst, const void* src, EType t, Red op, long long rows, long long cols, void* scratch, cudaStream_t s);
+// Anything else: one output per thread, reduced coordinates walked in row-major order.
+void reduce_generic(void* dst, const void* src, EType t, Red op, const Dims& kept, const Dims& reduced, long long n_out,
+                    cudaStream_t s);
+
+// ---- matrix products (tensor.rs:238-251, plan.rs:1453-1493) ----
+struct GemmBatch {
+  int rank = 0;
+  long long d[MAXR] = {};
+  long long sa[MAXR] = {}, sb[MAXR] = {};  // per-batch-dim element strides of A and B (0 = broadcast)
+};
+// C[b] (m x n) = op(A[b]) @ op(B[b]); `exact` keeps rg's loop arithmetic (k ascending, separate
+// multiply and add roundings), so results are bit-identical to the CPU interpreter.
+void gemm(void* c, const void* a, const void* b, EType t, long long m, long long n, long long k, bool ta, bool tb,
+          const GemmBatch& batch, long long count, bool exact, cudaStream_t s);
+
+// ---- random numbers (plan.rs:1403-1435, 1532-1544) ----
+void key_split(int32_t* dst, const int32_t* key, long long pairs, cudaStream_t s);
+void rand_uniform(void* dst, const int32_t* key, EType t, long long n, cudaStream_t s);
+void rand_normal(void* dst, const int32_t* key, EType t, long long n, cudaStream_t s);
+
+// ---- conversions and per-row selection ----
+void cast(void* dst, EType dt, const void* src, EType st, long long n, cudaStream_t s);
+void argmax(int32_t* dst, const void* src, EType t, long long rows, long long v, cudaStream_t s);
+void arg_top_k(int32_t* dst, const void* src, EType t, long long rows, long long v, long long k, cudaStream_t s);
+void cumsum(void* dst, const void* src, EType t, long long rows, long long v, bool reverse, cudaStream_t s);
+
+// ---- run loop support ----
+// history[step * n + h] = (double) slot_h[0]; sets *bad_step (if still -1) when not finite.
+void record_history(double* history, const void* const* slots, const int* types, int n, const long long* step,
+                    long long* bad_step, cudaStream_t s);
+void bump_counter(long long* counter, cudaStream_t s);
+// Loads batch (*counter % n_batches) of a data input from the device-resident batch array.
+void load_batch(void* dst, const void* batches, size_t bytes, long long n_batches, const long long* counter, cudaStream_t s);
+// Any non-finite value in a float buffer -> *flag = 1.
+void any_nonfinite(const void* src, EType t, long long n, int* flag, cudaStream_t s);
+
+}  // namespace rgc

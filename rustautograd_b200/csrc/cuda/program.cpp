@@ -1,0 +1,1340 @@
+// The rg CUDA device: plan lowering, device frames, the Exec contract, the device-resident run
+// loop, and the C ABI of include/rgc.h.
+//
+// Lowering turns each plan step into a launch closure over slot indices; a frame maps slot
+// indices to device pointers (one arena allocation per frame, 256-byte aligned slots), so a
+// buffer swap between steps is a pointer swap. The run loop captures one CUDA graph per buffer
+// layout (the state swaps are involutions, so two layouts alternate) and launches them back to
+// back with no host synchronisation inside a chunk of steps.
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <functional>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "blob.h"
+#include "dist.h"
+#include "jit.h"
+#include "kernels.cuh"
+#include "rgc.h"
+
+using rg::DType;
+using rg::Instr;
+using rg::OpKind;
+using rg::Plan;
+
+namespace rgc {
+
+namespace {
+
+thread_local std::string g_last_error;
+
+struct CudaError : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+void ck(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw CudaError(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+EType et(DType d) { return d == DType::F32 ? EType::F32 : d == DType::F64 ? EType::F64 : EType::I32; }
+
+constexpr size_t ALIGN = 256;
+size_t align_up(size_t x) { return (x + ALIGN - 1) / ALIGN * ALIGN; }
+
+// GEMMs up to this many multiply-adds keep rg's exact loop arithmetic (bit-identical results);
+// larger ones use fused multiply-add, within the 1e-4 parity tolerance.
+long long exact_gemm_limit() {
+  static long long v = [] {
+    const char* e = getenv("RGC_EXACT_GEMM");
+    if (e && std::string(e) == "1") return (long long)1 << 62;
+    return (long long)1 << 24;
+  }();
+  return v;
+}
+
+Jit& jit() {
+  static Jit j;
+  return j;
+}
+std::mutex& jit_mu() {
+  static std::mutex m;
+  return m;
+}
+
+struct Frame;
+struct Program;
+
+struct Ctx {
+  cudaStream_t s;
+  Frame* f;
+};
+
+using StepFn = std::function<void(Ctx&)>;
+
+struct Lowered {
+  StepFn run;
+  // Allocates what the step needs in a frame (nested body frames, staging) before any launch,
+  // so that launches can be captured into CUDA graphs.
+  std::function<void(Frame*, cudaStream_t)> prepare;
+  int kernels = 1;
+  bool capturable = true;
+};
+
+struct Frame {
+  Program* prog = nullptr;
+  char* arena = nullptr;
+  char* scratch = nullptr;
+  std::vector<char*> ptr;
+  cudaStream_t stream = nullptr;
+  bool failed = false;
+  std::string error;
+  // Control-flow bodies: one nested frame per body program, created on first use.
+  std::unordered_map<const Program*, std::unique_ptr<Frame>> bodies;
+  char* staging = nullptr;  // carry copies of a scan body
+  size_t staging_bytes = 0;
+  ~Frame();
+};
+
+struct Program {
+  int device = 0;
+  Plan plan;
+  std::vector<Lowered> steps;
+  std::vector<size_t> offsets;
+  size_t arena_bytes = 0;
+  size_t scratch_bytes = 0;
+  bool capturable = true;
+  std::vector<std::unique_ptr<Program>> subs;
+  Dims* bc_dev = nullptr;  // broadcast descriptors of the fused kernels
+  std::mutex mu;
+  std::vector<std::unique_ptr<Frame>> pool;
+  std::atomic<bool> inject{false};
+  std::atomic<uint64_t> launches{0};
+  std::atomic<size_t> frames_allocated{0};
+  int kernels_per_step = 0;
+  ~Program() {
+    pool.clear();
+    if (bc_dev) cudaFree(bc_dev);
+  }
+};
+
+Frame::~Frame() {
+  bodies.clear();
+  if (stream) cudaStreamDestroy(stream);
+  if (arena) cudaFree(arena);
+  if (scratch) cudaFree(scratch);
+  if (staging) cudaFree(staging);
+}
+
+std::unique_ptr<Program> make_program(const Plan& plan, int device);
+
+std::unique_ptr<Frame> make_frame(Program* p, cudaStream_t stream) {
+  auto f = std::make_unique<Frame>();
+  f->prog = p;
+  if (stream) {
+    f->stream = nullptr;  // borrowed
+  } else {
+    ck(cudaStreamCreateWithFlags(&f->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  }
+  if (p->arena_bytes) ck(cudaMalloc(&f->arena, p->arena_bytes), "cudaMalloc(frame)");
+  if (p->scratch_bytes) ck(cudaMalloc(&f->scratch, p->scratch_bytes), "cudaMalloc(scratch)");
+  f->ptr.resize(p->plan.slots.size());
+  for (size_t s = 0; s < f->ptr.size(); ++s) f->ptr[s] = f->arena + p->offsets[s];
+  cudaStream_t s = stream ? stream : f->stream;
+  // Constants stay resident for the frame's life: they are never overwritten.
+  for (auto& [slot, t] : p->plan.consts)
+    if (t->data.bytes()) ck(cudaMemcpyAsync(f->ptr[slot], t->data.data(), t->data.bytes(), cudaMemcpyHostToDevice, s), "upload constants");
+  ck(cudaStreamSynchronize(s), "upload constants");
+  p->frames_allocated += 1;
+  return f;
+}
+
+void prepare_frame(Program* p, Frame* f, cudaStream_t s) {
+  for (auto& st : p->steps)
+    if (st.prepare) st.prepare(f, s);
+}
+
+// The nested frame of a control-flow body, with `staging` bytes for carry copies.
+Frame* body_frame(Frame* parent, Program* body, cudaStream_t s, size_t staging = 0) {
+  auto& slot = parent->bodies[body];
+  if (!slot) {
+    slot = make_frame(body, s);
+    prepare_frame(body, slot.get(), s);
+  }
+  if (slot->staging_bytes < staging) {
+    if (slot->staging) cudaFree(slot->staging);
+    ck(cudaMalloc(&slot->staging, staging), "cudaMalloc(carry staging)");
+    slot->staging_bytes = staging;
+  }
+  return slot.get();
+}
+
+void run_steps(Program* p, Ctx& c) {
+  for (auto& st : p->steps) st.run(c);
+}
+
+Dims dims_of(const std::vector<size_t>& shape, const std::vector<size_t>& st) {
+  Dims d;
+  if (shape.size() > (size_t)MAXR) throw std::runtime_error("tensor rank above 8 is not supported by the CUDA device");
+  d.rank = (int)shape.size();
+  for (size_t k = 0; k < shape.size(); ++k) {
+    d.d[k] = (long long)shape[k];
+    d.st[k] = (long long)st[k];
+  }
+  return d;
+}
+
+// ---- lowering of one instruction ----
+
+struct Builder {
+  Program* p;
+  std::vector<Dims> bcs;  // broadcast descriptors, uploaded once per program
+  size_t scratch = 0;
+
+  Lowered elementwise(const ElemSpec& spec, std::vector<size_t> in_slots, std::vector<size_t> out_slots) {
+    std::string name;
+    {
+      std::lock_guard<std::mutex> lk(jit_mu());
+      name = jit().add(spec);
+    }
+    size_t bc0 = bcs.size();
+    for (auto& in : spec.inputs)
+      if (in.kind == rg::ArgKind::Broadcast) bcs.push_back(dims_of(spec.shape, rg::bstrides(in.shape, spec.shape.size())));
+    int vw = spec.dtype == DType::F64 ? 2 : 4;
+    bool vec_ok = spec.n % (size_t)vw == 0;
+    std::vector<long long> rows;
+    for (auto& in : spec.inputs) rows.push_back((long long)in.row);
+    long long n = (long long)spec.n;
+    Program* prog = p;
+    auto fn = std::make_shared<CUfunction>(nullptr);
+    Lowered l;
+    l.run = [=](Ctx& c) {
+      if (!*fn) {
+        std::lock_guard<std::mutex> lk(jit_mu());
+        *fn = jit().function(name);
+      }
+      ElemArgs a;
+      std::memset(&a, 0, sizeof a);
+      a.n = n;
+      a.vec = vec_ok ? 1 : 0;
+      for (size_t k = 0; k < in_slots.size(); ++k) {
+        a.in[k] = c.f->ptr[in_slots[k]];
+        a.row[k] = rows[k];
+      }
+      for (size_t q = 0; q < out_slots.size(); ++q) a.out[q] = c.f->ptr[out_slots[q]];
+      a.bc = prog->bc_dev + bc0;
+      if (n > 0) Jit::launch(*fn, a, n, vw, c.s);
+    };
+    if (in_slots.size() > (size_t)JIT_MAX_IN || out_slots.size() > (size_t)JIT_MAX_OUT)
+      throw std::runtime_error("fused group has too many operands for one kernel");
+    return l;
+  }
+
+  Lowered lower(const Instr& i) {
+    Lowered l;
+    const auto& a = i.args;
+    size_t dst = i.dst;
+    EType t = et(i.dtype);
+    long long n = (long long)i.n;
+    OpKind k = i.op.kind;
+    if (i.op.is_unary_elementwise() || i.op.is_binary_elementwise() || k == OpKind::Where) {
+      return elementwise(spec_from_instr(i), a, {dst});
+    }
+    switch (k) {
+      case OpKind::Cast: {
+        EType st = et(p->plan.slots[a[0]].first);
+        l.run = [=](Ctx& c) { cast(c.f->ptr[dst], t, c.f->ptr[a[0]], st, n, c.s); };
+        return l;
+      }
+      case OpKind::Transpose: {
+        const auto& perm = i.op.shape;
+        size_t r = perm.size();
+        bool last2 = r >= 2 && perm[r - 1] == r - 2 && perm[r - 2] == r - 1;
+        for (size_t d = 0; last2 && d + 2 < r; ++d) last2 = perm[d] == d;
+        if (last2) {
+          long long rows = (long long)i.arg_shapes[0][r - 2], cols = (long long)i.arg_shapes[0][r - 1];
+          long long batch = rows * cols ? n / (rows * cols) : 0;
+          l.run = [=](Ctx& c) { transpose_last2(c.f->ptr[dst], c.f->ptr[a[0]], t, batch, rows, cols, c.s); };
+          return l;
+        }
+        auto src = rg::strides(i.arg_shapes[0]);
+        std::vector<size_t> mapped;
+        for (size_t q : perm) mapped.push_back(src[q]);
+        Dims d = dims_of(i.shape, mapped);
+        l.run = [=](Ctx& c) { strided_gather(c.f->ptr[dst], c.f->ptr[a[0]], t, d, 0, n, c.s); };
+        return l;
+      }
+      case OpKind::BroadcastTo: {
+        Dims d = dims_of(i.shape, rg::bstrides(i.arg_shapes[0], i.shape.size()));
+        l.run = [=](Ctx& c) { strided_gather(c.f->ptr[dst], c.f->ptr[a[0]], t, d, 0, n, c.s); };
+        return l;
+      }
+      case OpKind::Slice: {
+        auto src = rg::strides(i.arg_shapes[0]);
+        long long base = 0;
+        for (size_t q = 0; q < src.size(); ++q) base += (long long)(i.op.starts[q] * src[q]);
+        Dims d = dims_of(i.shape, src);
+        l.run = [=](Ctx& c) { strided_gather(c.f->ptr[dst], c.f->ptr[a[0]], t, d, base, n, c.s); };
+        return l;
+      }
+      case OpKind::Pad: {
+        auto ds = rg::strides(i.shape);
+        long long base = 0;
+        for (size_t q = 0; q < ds.size(); ++q) base += (long long)(i.op.starts[q] * ds[q]);
+        Dims d = dims_of(i.arg_shapes[0], ds);
+        long long nin = (long long)rg::product(i.arg_shapes[0]);
+        size_t bytes = (size_t)n * esize(t);
+        l.kernels = 2;
+        l.run = [=](Ctx& c) {
+          fill_zero(c.f->ptr[dst], bytes, c.s);
+          strided_scatter(c.f->ptr[dst], c.f->ptr[a[0]], t, d, base, nin, c.s);
+        };
+        return l;
+      }
+      case OpKind::Concat: {
+        auto ds = rg::strides(i.shape);
+        size_t axis = i.op.index;
+        std::vector<std::pair<Dims, long long>> parts;
+        std::vector<long long> counts;
+        size_t at = 0;
+        for (size_t q = 0; q < a.size(); ++q) {
+          parts.emplace_back(dims_of(i.arg_shapes[q], ds), (long long)(at * ds[axis]));
+          counts.push_back((long long)rg::product(i.arg_shapes[q]));
+          at += i.arg_shapes[q][axis];
+        }
+        l.kernels = (int)a.size();
+        l.run = [=](Ctx& c) {
+          for (size_t q = 0; q < a.size(); ++q) strided_scatter(c.f->ptr[dst], c.f->ptr[a[q]], t, parts[q].first, parts[q].second, counts[q], c.s);
+        };
+        return l;
+      }
+      case OpKind::Take: {
+        const auto& xs = i.arg_shapes[0];
+        size_t axis = i.op.index;
+        long long block = 1, outer = 1;
+        for (size_t q = axis + 1; q < xs.size(); ++q) block *= (long long)xs[q];
+        for (size_t q = 0; q < axis; ++q) outer *= (long long)xs[q];
+        long long dim = (long long)xs[axis], n_idx = (long long)rg::product(i.arg_shapes[1]);
+        l.run = [=](Ctx& c) { take_rows(c.f->ptr[dst], c.f->ptr[a[0]], (const int32_t*)c.f->ptr[a[1]], t, outer, dim, n_idx, block, c.s); };
+        return l;
+      }
+      case OpKind::TakeAlong: {
+        long long v = (long long)i.arg_shapes[0].back(), kk = (long long)i.arg_shapes[1].back();
+        l.run = [=](Ctx& c) { take_along(c.f->ptr[dst], c.f->ptr[a[0]], (const int32_t*)c.f->ptr[a[1]], t, n, v, kk, c.s); };
+        return l;
+      }
+      case OpKind::TakeGrad: {
+        const auto& shape = i.op.shape;
+        size_t axis = i.op.index;
+        long long block = 1, outer = 1;
+        for (size_t q = axis + 1; q < shape.size(); ++q) block *= (long long)shape[q];
+        for (size_t q = 0; q < axis; ++q) outer *= (long long)shape[q];
+        long long dim = (long long)shape[axis], n_idx = (long long)rg::product(i.arg_shapes[1]);
+        l.run = [=](Ctx& c) { take_grad(c.f->ptr[dst], c.f->ptr[a[0]], (const int32_t*)c.f->ptr[a[1]], t, outer, dim, n_idx, block, c.s); };
+        return l;
+      }
+      case OpKind::TakeAlongGrad: {
+        long long v = (long long)i.op.shape.back(), kk = (long long)i.arg_shapes[1].back();
+        long long rows = v ? n / v : 0;
+        l.run = [=](Ctx& c) { take_along_grad(c.f->ptr[dst], c.f->ptr[a[0]], (const int32_t*)c.f->ptr[a[1]], t, rows, v, kk, c.s); };
+        return l;
+      }
+      case OpKind::MatMul:
+      case OpKind::MatMulT:
+        return matmul(i, k == OpKind::MatMulT && i.op.flag_a, k == OpKind::MatMulT && i.op.flag_b);
+      case OpKind::Reduce:
+        return reduce(i);
+      case OpKind::Cumsum: {
+        long long v = (long long)i.shape.back();
+        long long rows = v ? n / v : 0;
+        bool rev = i.op.flag_a;
+        l.run = [=](Ctx& c) { cumsum(c.f->ptr[dst], c.f->ptr[a[0]], t, rows, v, rev, c.s); };
+        return l;
+      }
+      case OpKind::Argmax: {
+        EType st = et(p->plan.slots[a[0]].first);
+        long long v = (long long)i.arg_shapes[0].back();
+        l.run = [=](Ctx& c) { argmax((int32_t*)c.f->ptr[dst], c.f->ptr[a[0]], st, n, v, c.s); };
+        return l;
+      }
+      case OpKind::ArgTopK: {
+        EType st = et(p->plan.slots[a[0]].first);
+        long long v = (long long)i.arg_shapes[0].back(), kk = (long long)i.op.index;
+        long long rows = kk ? n / kk : 0;
+        l.run = [=](Ctx& c) { arg_top_k((int32_t*)c.f->ptr[dst], c.f->ptr[a[0]], st, rows, v, kk, c.s); };
+        return l;
+      }
+      case OpKind::RandUniform:
+        l.run = [=](Ctx& c) { rand_uniform(c.f->ptr[dst], (const int32_t*)c.f->ptr[a[0]], t, n, c.s); };
+        return l;
+      case OpKind::RandNormal:
+        l.run = [=](Ctx& c) { rand_normal(c.f->ptr[dst], (const int32_t*)c.f->ptr[a[0]], t, n, c.s); };
+        return l;
+      case OpKind::KeySplit:
+        l.run = [=](Ctx& c) { key_split((int32_t*)c.f->ptr[dst], (const int32_t*)c.f->ptr[a[0]], n / 2, c.s); };
+        return l;
+      case OpKind::Scan:
+      case OpKind::While:
+      case OpKind::Cond:
+        return control(i);
+      default:
+        throw std::runtime_error(std::string("the CUDA device has no kernel for ") + i.op.name());
+    }
+  }
+
+  // plan.rs:1453-1493
+  Lowered matmul(const Instr& i, bool ta, bool tb) {
+    Lowered l;
+    const auto &sa = i.arg_shapes[0], &sb = i.arg_shapes[1];
+    size_t ar = sa.size(), br = sb.size();
+    long long m, kk, n;
+    if (ar >= 2) {
+      m = (long long)(ta ? sa[ar - 1] : sa[ar - 2]);
+      kk = (long long)(ta ? sa[ar - 2] : sa[ar - 1]);
+    } else {
+      m = 1;
+      kk = (long long)sa[0];
+    }
+    n = br >= 2 ? (long long)(tb ? sb[br - 2] : sb[br - 1]) : 1;
+    std::vector<size_t> ba(sa.begin(), sa.end() - std::min<size_t>(2, ar));
+    std::vector<size_t> bb(sb.begin(), sb.end() - std::min<size_t>(2, br));
+    GemmBatch bt;
+    long long count = 1;
+    if (bb.empty() && !ta) {
+      m *= (long long)rg::product(ba);  // row-major batches of A form one matrix
+    } else {
+      std::vector<size_t> batch;
+      rg::broadcast_shapes(ba, bb, &batch);
+      if (batch.size() > (size_t)MAXR) throw std::runtime_error("matmul batch rank above 8");
+      auto st_a = rg::bstrides(ba, batch.size()), st_b = rg::bstrides(bb, batch.size());
+      bt.rank = (int)batch.size();
+      for (size_t d = 0; d < batch.size(); ++d) {
+        bt.d[d] = (long long)batch[d];
+        bt.sa[d] = (long long)st_a[d] * m * kk;
+        bt.sb[d] = (long long)st_b[d] * kk * n;
+      }
+      count = (long long)rg::product(batch);
+    }
+    EType t = et(i.dtype);
+    bool exact = m * n * kk * count <= exact_gemm_limit();
+    size_t dst = i.dst, A = i.args[0], B = i.args[1];
+    l.run = [=](Ctx& c) { gemm(c.f->ptr[dst], c.f->ptr[A], c.f->ptr[B], t, m, n, kk, ta, tb, bt, count, exact, c.s); };
+    return l;
+  }
+
+  // plan.rs:1549-1622, routed by the shape of the reduced axis set.
+  Lowered reduce(const Instr& i) {
+    Lowered l;
+    const auto& in_shape = i.arg_shapes[0];
+    std::vector<size_t> axes = i.op.shape;
+    std::sort(axes.begin(), axes.end());
+    size_t r = in_shape.size();
+    EType t = et(i.dtype);
+    Red op = i.op.reduce == rg::ReduceKind::Sum ? Red::Sum : i.op.reduce == rg::ReduceKind::Max ? Red::Max : Red::Min;
+    size_t dst = i.dst, src = i.args[0];
+    long long n_in = (long long)rg::product(in_shape);
+    if (op == Red::Sum && axes.size() == r) {
+      scratch = std::max(scratch, full_sum_scratch_bytes(n_in, t));
+      l.kernels = n_in > 32768 ? 2 : 1;
+      l.run = [=](Ctx& c) { reduce_full_sum(c.f->ptr[dst], c.f->ptr[src], t, n_in, c.f->scratch, c.s); };
+      return l;
+    }
+    // Dims of extent 1 do not change the memory order; drop them before matching patterns.
+    std::vector<bool> red(r, false);
+    for (size_t ax : axes) red[ax] = true;
+    std::vector<size_t> keep_idx, red_idx;
+    for (size_t d = 0; d < r; ++d)
+      if (in_shape[d] != 1) (red[d] ? red_idx : keep_idx).push_back(d);
+    long long n_out = (long long)i.n;
+    auto contiguous = [](const std::vector<size_t>& v) {
+      for (size_t q = 1; q < v.size(); ++q)
+        if (v[q] < v[q - 1]) return false;
+      return true;
+    };
+    bool trailing = !red_idx.empty() && (keep_idx.empty() || keep_idx.back() < red_idx.front()) && contiguous(red_idx);
+    bool leading = !red_idx.empty() && !keep_idx.empty() && red_idx.back() < keep_idx.front();
+    long long n_red = 1;
+    for (size_t d : red_idx) n_red *= (long long)in_shape[d];
+    if (red_idx.empty()) {
+      // Reducing only extent-1 axes: an elementwise combine with the identity.
+      long long nn = n_out;
+      l.run = [=](Ctx& c) { reduce_rows(c.f->ptr[dst], c.f->ptr[src], t, op, nn, 1, c.s); };
+      return l;
+    }
+    if (trailing) {
+      long long rows = n_out, len = n_red;
+      l.run = [=](Ctx& c) { reduce_rows(c.f->ptr[dst], c.f->ptr[src], t, op, rows, len, c.s); };
+      return l;
+    }
+    if (leading) {
+      long long rows = n_red, cols = n_out;
+      scratch = std::max(scratch, cols_scratch_bytes(rows, cols, t));
+      l.kernels = 2;
+      l.run = [=](Ctx& c) { reduce_cols(c.f->ptr[dst], c.f->ptr[src], t, op, rows, cols, c.f->scratch, c.s); };
+      return l;
+    }
+    auto st = rg::strides(in_shape);
+    std::vector<size_t> kd, ks, rd, rs;
+    for (size_t d : keep_idx) {
+      kd.push_back(in_shape[d]);
+      ks.push_back(st[d]);
+    }
+    for (size_t d : red_idx) {
+      rd.push_back(in_shape[d]);
+      rs.push_back(st[d]);
+    }
+    Dims kept = dims_of(kd, ks), reduced = dims_of(rd, rs);
+    l.run = [=](Ctx& c) { reduce_generic(c.f->ptr[dst], c.f->ptr[src], t, op, kept, reduced, n_out, c.s); };
+    return l;
+  }
+
+  // plan.rs:737-831 on device buffers; the host only sequences the iterations.
+  Lowered control(const Instr& i) {
+    Lowered l;
+    Program* parent = p;
+    if (i.op.kind == OpKind::Scan) {
+      p->subs.push_back(make_program(*i.body_plan, p->device));
+      Program* body = p->subs.back().get();
+      size_t c = i.op.n_carry, x = i.op.n_x, length = i.op.length;
+      bool reverse = i.op.flag_a;
+      auto args = i.args;
+      auto outs = i.outs;
+      size_t n_y = body->plan.outputs.size() - c;
+      std::vector<size_t> es;
+      for (size_t q = 0; q < body->plan.input_slots.size(); ++q) es.push_back(rg::dtype_size(body->plan.slots[body->plan.input_slots[q]].first));
+      l.capturable = body->capturable;
+      l.kernels = 0;
+      size_t carry_bytes = 0;
+      for (size_t k = 0; k < c; ++k) carry_bytes += align_up(body->plan.outputs[k].n * es[k]);
+      l.prepare = [=](Frame* f, cudaStream_t st) { body_frame(f, body, st, carry_bytes); };
+      l.run = [=](Ctx& cx) {
+        Frame* bf = body_frame(cx.f, body, cx.s, carry_bytes);
+        const Plan& bp = body->plan;
+        auto cp = [&](void* d, const void* s, size_t bytes) {
+          if (bytes) ck(cudaMemcpyAsync(d, s, bytes, cudaMemcpyDeviceToDevice, cx.s), "scan copy");
+        };
+        for (size_t k = 0; k < args.size(); ++k)
+          if (k < c || k >= c + x) cp(bf->ptr[bp.input_slots[k]], cx.f->ptr[args[k]], bp.input_ns[k] * es[k]);
+        Ctx inner{cx.s, bf};
+        for (size_t st = 0; st < length; ++st) {
+          size_t at = reverse ? length - 1 - st : st;
+          for (size_t k = c; k < c + x; ++k) {
+            size_t m = bp.input_ns[k] * es[k];
+            cp(bf->ptr[bp.input_slots[k]], cx.f->ptr[args[k]] + at * m, m);
+          }
+          for (auto& [index, slot] : outs) {
+            if (index >= c + n_y) {
+              size_t k = index - c - n_y;
+              size_t m = bp.input_ns[k] * es[k];
+              cp(cx.f->ptr[slot] + at * m, bf->ptr[bp.input_slots[k]], m);
+            }
+          }
+          run_steps(body, inner);
+          for (auto& [index, slot] : outs) {
+            if (index >= c && index < c + n_y) {
+              const auto& o = bp.outputs[index];
+              size_t eb = rg::dtype_size(bp.slots[o.slot].first);
+              cp(cx.f->ptr[slot] + at * o.n * eb, bf->ptr[o.slot], o.n * eb);
+            }
+          }
+          // Body outputs feed the carries through staging: an output may be another carry's input.
+          size_t off = 0;
+          for (size_t k = 0; k < c; ++k) {
+            cp(bf->staging + off, bf->ptr[bp.outputs[k].slot], bp.outputs[k].n * es[k]);
+            off += align_up(bp.outputs[k].n * es[k]);
+          }
+          off = 0;
+          for (size_t k = 0; k < c; ++k) {
+            cp(bf->ptr[bp.input_slots[k]], bf->staging + off, bp.outputs[k].n * es[k]);
+            off += align_up(bp.outputs[k].n * es[k]);
+          }
+        }
+        for (auto& [index, slot] : outs)
+          if (index < c) cp(cx.f->ptr[slot], bf->ptr[bp.input_slots[index]], bp.input_ns[index] * es[index]);
+      };
+      (void)parent;
+      return l;
+    }
+    if (i.op.kind == OpKind::While) {
+      p->subs.push_back(make_program(*i.body_plan, p->device));
+      Program* cond = p->subs.back().get();
+      p->subs.push_back(make_program(*i.body2_plan, p->device));
+      Program* body = p->subs.back().get();
+      auto args = i.args;
+      auto outs = i.outs;
+      size_t n_carry = i.op.n_carry, max_it = i.op.max_iterations;
+      l.capturable = false;  // the host reads the condition each iteration
+      l.kernels = 0;
+      auto bytes_of = [](const Plan& pl, size_t k) { return pl.input_ns[k] * rg::dtype_size(pl.slots[pl.input_slots[k]].first); };
+      size_t carry_bytes = 0;
+      for (size_t k = 0; k < n_carry; ++k) carry_bytes += align_up(bytes_of(body->plan, k));
+      l.prepare = [=](Frame* f, cudaStream_t st) {
+        body_frame(f, cond, st);
+        body_frame(f, body, st, carry_bytes);
+      };
+      l.run = [=](Ctx& cx) {
+        Frame* cf = body_frame(cx.f, cond, cx.s);
+        Frame* bf = body_frame(cx.f, body, cx.s, carry_bytes);
+        const Plan& cp_ = cond->plan;
+        const Plan& bp = body->plan;
+        auto cp = [&](void* d, const void* s, size_t bytes) {
+          if (bytes) ck(cudaMemcpyAsync(d, s, bytes, cudaMemcpyDeviceToDevice, cx.s), "while copy");
+        };
+        for (size_t k = 0; k < args.size(); ++k) {
+          cp(cf->ptr[cp_.input_slots[k]], cx.f->ptr[args[k]], bytes_of(cp_, k));
+          cp(bf->ptr[bp.input_slots[k]], cx.f->ptr[args[k]], bytes_of(bp, k));
+        }
+        Ctx ci{cx.s, cf}, bi{cx.s, bf};
+        size_t count = 0;
+        for (;;) {
+          run_steps(cond, ci);
+          const auto& o = cp_.outputs[0];
+          double v = 0;
+          DType d = cp_.slots[o.slot].first;
+          char buf[8];
+          ck(cudaMemcpyAsync(buf, cf->ptr[o.slot], rg::dtype_size(d), cudaMemcpyDeviceToHost, cx.s), "while condition");
+          ck(cudaStreamSynchronize(cx.s), "while condition");
+          v = d == DType::F32 ? (double)*(float*)buf : d == DType::F64 ? *(double*)buf : (double)*(int32_t*)buf;
+          if (v == 0.0) break;
+          if (count == max_it) break;
+          run_steps(body, bi);
+          size_t off = 0;
+          for (size_t k = 0; k < n_carry; ++k) {
+            cp(bf->staging + off, bf->ptr[bp.outputs[k].slot], bytes_of(bp, k));
+            off += align_up(bytes_of(bp, k));
+          }
+          off = 0;
+          for (size_t k = 0; k < n_carry; ++k) {
+            cp(bf->ptr[bp.input_slots[k]], bf->staging + off, bytes_of(bp, k));
+            cp(cf->ptr[cp_.input_slots[k]], bf->staging + off, bytes_of(bp, k));
+            off += align_up(bytes_of(bp, k));
+          }
+          count += 1;
+        }
+        for (auto& [index, slot] : outs) {
+          if (index < n_carry) {
+            cp(cx.f->ptr[slot], bf->ptr[bp.input_slots[index]], bytes_of(bp, index));
+          } else {
+            int32_t cnt = (int32_t)count;
+            ck(cudaMemcpyAsync(cx.f->ptr[slot], &cnt, 4, cudaMemcpyHostToDevice, cx.s), "while count");
+            ck(cudaStreamSynchronize(cx.s), "while count");
+          }
+        }
+      };
+      return l;
+    }
+    // Cond
+    p->subs.push_back(make_program(*i.body_plan, p->device));
+    Program* then_p = p->subs.back().get();
+    p->subs.push_back(make_program(*i.body2_plan, p->device));
+    Program* else_p = p->subs.back().get();
+    auto args = i.args;
+    auto outs = i.outs;
+    DType pd = p->plan.slots[args[0]].first;
+    l.capturable = false;
+    l.kernels = 0;
+    l.prepare = [=](Frame* f, cudaStream_t st) {
+      body_frame(f, then_p, st);
+      body_frame(f, else_p, st);
+    };
+    l.run = [=](Ctx& cx) {
+      char buf[8];
+      ck(cudaMemcpyAsync(buf, cx.f->ptr[args[0]], rg::dtype_size(pd), cudaMemcpyDeviceToHost, cx.s), "cond predicate");
+      ck(cudaStreamSynchronize(cx.s), "cond predicate");
+      double v = pd == DType::F32 ? (double)*(float*)buf : pd == DType::F64 ? *(double*)buf : (double)*(int32_t*)buf;
+      Program* body = v != 0.0 ? then_p : else_p;
+      Frame* bf = body_frame(cx.f, body, cx.s);
+      const Plan& bp = body->plan;
+      for (size_t k = 0; k + 1 < args.size(); ++k) {
+        size_t bytes = bp.input_ns[k] * rg::dtype_size(bp.slots[bp.input_slots[k]].first);
+        if (bytes) ck(cudaMemcpyAsync(bf->ptr[bp.input_slots[k]], cx.f->ptr[args[k + 1]], bytes, cudaMemcpyDeviceToDevice, cx.s), "cond copy");
+      }
+      Ctx inner{cx.s, bf};
+      run_steps(body, inner);
+      for (auto& [index, slot] : outs) {
+        const auto& o = bp.outputs[index];
+        size_t bytes = o.n * rg::dtype_size(bp.slots[o.slot].first);
+        if (bytes) ck(cudaMemcpyAsync(cx.f->ptr[slot], bf->ptr[o.slot], bytes, cudaMemcpyDeviceToDevice, cx.s), "cond copy");
+      }
+    };
+    return l;
+  }
+};
+
+std::unique_ptr<Program> make_program(const Plan& plan, int device) {
+  auto p = std::make_unique<Program>();
+  p->device = device;
+  p->plan = plan;
+  p->offsets.resize(plan.slots.size());
+  size_t off = 0;
+  for (size_t s = 0; s < plan.slots.size(); ++s) {
+    p->offsets[s] = off;
+    off += align_up(std::max<size_t>(1, plan.slots[s].second) * rg::dtype_size(plan.slots[s].first));
+  }
+  p->arena_bytes = off;
+  Builder b{p.get()};
+  for (size_t k = 0; k < plan.steps.size(); ++k) {
+    const auto& st = plan.steps[k];
+    if (!st.fused && st.instr.op.kind == OpKind::AllReduce) {
+      // Consecutive all-reduces (a model's gradients) go to NCCL as one group.
+      std::vector<std::tuple<size_t, size_t, size_t, bool>> items;  // (src, dst, count, f64)
+      while (k < plan.steps.size() && !plan.steps[k].fused && plan.steps[k].instr.op.kind == OpKind::AllReduce) {
+        const Instr& i = plan.steps[k].instr;
+        items.emplace_back(i.args[0], i.dst, i.n, i.dtype == DType::F64);
+        ++k;
+      }
+      --k;
+      Lowered l;
+      l.kernels = (int)items.size();
+      l.run = [items](Ctx& c) {
+        if (!dist_active()) {
+          for (auto& [src, dst, n, f64] : items)
+            ck(cudaMemcpyAsync(c.f->ptr[dst], c.f->ptr[src], n * (f64 ? 8 : 4), cudaMemcpyDeviceToDevice, c.s), "all_reduce copy");
+          return;
+        }
+        dist_group_start();
+        for (auto& [src, dst, n, f64] : items) dist_all_reduce_into(c.f->ptr[dst], c.f->ptr[src], n, f64, c.s);
+        dist_group_end();
+      };
+      p->steps.push_back(std::move(l));
+      // The grouped step stands for several plan steps: keep step indices aligned.
+      for (size_t q = 1; q < items.size(); ++q) {
+        Lowered empty;
+        empty.kernels = 0;
+        empty.run = [](Ctx&) {};
+        p->steps.push_back(std::move(empty));
+      }
+      continue;
+    }
+    if (st.fused) {
+      std::vector<size_t> ins, outs;
+      for (auto& in : st.group.inputs) ins.push_back(in.slot);
+      for (auto& o : st.group.outputs) outs.push_back(o.second);
+      p->steps.push_back(b.elementwise(spec_from_group(st.group), ins, outs));
+    } else {
+      p->steps.push_back(b.lower(st.instr));
+    }
+  }
+  {
+    std::lock_guard<std::mutex> lk(jit_mu());
+    jit().build();
+  }
+  if (!b.bcs.empty()) {
+    ck(cudaMalloc(&p->bc_dev, b.bcs.size() * sizeof(Dims)), "cudaMalloc(broadcast descriptors)");
+    ck(cudaMemcpy(p->bc_dev, b.bcs.data(), b.bcs.size() * sizeof(Dims), cudaMemcpyHostToDevice), "upload broadcast descriptors");
+  }
+  p->scratch_bytes = b.scratch;
+  p->capturable = true;
+  p->kernels_per_step = 0;
+  for (auto& st : p->steps) {
+    p->capturable = p->capturable && st.capturable;
+    p->kernels_per_step += st.kernels;
+  }
+  return p;
+}
+
+bool graphs_enabled() {
+  static bool on = [] {
+    const char* e = getenv("RGC_NO_GRAPH");
+    return !(e && std::string(e) == "1");
+  }();
+  return on;
+}
+
+}  // namespace
+
+}  // namespace rgc
+
+// ---------------------------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------------------------
+
+using namespace rgc;
+
+struct rgc_program {
+  std::unique_ptr<Program> p;
+};
+
+struct rgc_exec {
+  rgc_program* owner = nullptr;
+  std::unique_ptr<Frame> f;
+};
+
+namespace {
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+template <typename F> int guard(F f) {
+  try {
+    g_last_error.clear();
+    return f();
+  } catch (const CudaError& e) {
+    return fail(RGC_ERR_CUDA, e.what());
+  } catch (const std::exception& e) {
+    return fail(RGC_ERR_INVALID, e.what());
+  }
+}
+
+void mark_failed(rgc_exec* e, const std::string& why) {
+  if (!e->f->failed) {
+    e->f->failed = true;
+    e->f->error = why;
+  }
+}
+
+// Launches one plan step sequence on the frame's stream with the current layout.
+void launch_plan(rgc_exec* e) {
+  Program* p = e->owner->p.get();
+  Ctx c{e->f->stream, e->f.get()};
+  run_steps(p, c);
+  p->launches += (uint64_t)p->kernels_per_step;
+}
+
+void check_async(rgc_exec* e) {
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) mark_failed(e, std::string("kernel launch failed: ") + cudaGetErrorString(err));
+}
+
+cudaGraphExec_t capture(cudaStream_t s, const std::function<void(cudaStream_t)>& body) {
+  cudaGraph_t graph;
+  ck(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+  try {
+    body(s);
+  } catch (...) {
+    cudaGraph_t g2;
+    cudaStreamEndCapture(s, &g2);
+    if (g2) cudaGraphDestroy(g2);
+    throw;
+  }
+  ck(cudaStreamEndCapture(s, &graph), "cudaStreamEndCapture");
+  cudaGraphExec_t exec;
+  ck(cudaGraphInstantiate(&exec, graph, 0), "cudaGraphInstantiate");
+  cudaGraphDestroy(graph);
+  return exec;
+}
+
+}  // namespace
+
+extern "C" {
+
+__attribute__((visibility("default"))) int rgc_available(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return 0;
+  }
+  int dev = 0, major = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  return major == 10 ? 1 : 0;
+}
+
+__attribute__((visibility("default"))) const char* rgc_last_error(void) { return g_last_error.c_str(); }
+
+__attribute__((visibility("default"))) int rgc_program_create(const uint8_t* blob, size_t len, int device, rgc_program** out) {
+  return guard([&] {
+    if (!blob || !out) return fail(RGC_ERR_INVALID, "null argument");
+    if (!rgc_available()) return fail(RGC_ERR_UNAVAILABLE, "no sm_100 CUDA device is available");
+    int dev = device;
+    if (dev < 0) ck(cudaGetDevice(&dev), "cudaGetDevice");
+    // Makes the device's primary context current: the JIT loads modules through the driver API.
+    ck(cudaSetDevice(dev), "cudaSetDevice");
+    ck(cudaFree(nullptr), "CUDA context initialisation");
+    Plan plan = rg::decode_plan(blob, len);
+    auto p = make_program(plan, dev);
+    *out = new rgc_program{std::move(p)};
+    return RGC_OK;
+  });
+}
+
+__attribute__((visibility("default"))) void rgc_program_destroy(rgc_program* p) {
+  if (!p) return;
+  cudaDeviceSynchronize();
+  delete p;
+}
+
+__attribute__((visibility("default"))) size_t rgc_program_allocated_bytes(const rgc_program* p) {
+  if (!p) return 0;
+  return (p->p->arena_bytes + p->p->scratch_bytes) * p->p->frames_allocated.load();
+}
+
+__attribute__((visibility("default"))) uint64_t rgc_program_launches(const rgc_program* p) { return p ? p->p->launches.load() : 0; }
+
+__attribute__((visibility("default"))) void rgc_program_inject_failure(rgc_program* p) {
+  if (p) p->p->inject = true;
+}
+
+__attribute__((visibility("default"))) int rgc_exec_acquire(rgc_program* p, rgc_exec** out) {
+  return guard([&] {
+    if (!p || !out) return fail(RGC_ERR_INVALID, "null argument");
+    ck(cudaSetDevice(p->p->device), "cudaSetDevice");
+    std::unique_ptr<Frame> f;
+    {
+      std::lock_guard<std::mutex> lk(p->p->mu);
+      if (!p->p->pool.empty()) {
+        f = std::move(p->p->pool.back());
+        p->p->pool.pop_back();
+      }
+    }
+    if (!f) {
+      f = make_frame(p->p.get(), nullptr);
+      prepare_frame(p->p.get(), f.get(), f->stream);
+      ck(cudaStreamSynchronize(f->stream), "prepare frame");
+    }
+    f->failed = false;
+    f->error.clear();
+    auto e = new rgc_exec;
+    e->owner = p;
+    e->f = std::move(f);
+    *out = e;
+    return RGC_OK;
+  });
+}
+
+__attribute__((visibility("default"))) void rgc_exec_release(rgc_exec* e) {
+  if (!e) return;
+  if (e->f) {
+    cudaStreamSynchronize(e->f->stream);
+    cudaError_t err = cudaGetLastError();
+    // A frame that saw a device error is not reused.
+    if (!e->f->failed && err == cudaSuccess) {
+      std::lock_guard<std::mutex> lk(e->owner->p->mu);
+      e->owner->p->pool.push_back(std::move(e->f));
+    }
+  }
+  delete e;
+}
+
+__attribute__((visibility("default"))) int rgc_exec_load(rgc_exec* e, size_t input, const void* host, size_t bytes) {
+  return guard([&] {
+    const Plan& plan = e->owner->p->plan;
+    if (input >= plan.input_slots.size()) return fail(RGC_ERR_INVALID, "input index out of range");
+    size_t slot = plan.input_slots[input];
+    size_t cap = plan.slots[slot].second * rg::dtype_size(plan.slots[slot].first);
+    if (bytes > cap) return fail(RGC_ERR_INVALID, "input larger than its slot");
+    if (bytes) {
+      ck(cudaMemcpyAsync(e->f->ptr[slot], host, bytes, cudaMemcpyHostToDevice, e->f->stream), "load input");
+      ck(cudaStreamSynchronize(e->f->stream), "load input");
+    }
+    return RGC_OK;
+  });
+}
+
+__attribute__((visibility("default"))) int rgc_exec_step(rgc_exec* e) {
+  return guard([&] {
+    if (e->f->failed) return fail(RGC_ERR_DEVICE, e->f->error);
+    if (e->owner->p->inject.exchange(false)) {
+      mark_failed(e, "injected failure for test");
+      return fail(RGC_ERR_DEVICE, e->f->error);
+    }
+    launch_plan(e);
+    check_async(e);
+    return e->f->failed ? fail(RGC_ERR_DEVICE, e->f->error) : RGC_OK;
+  });
+}
+
+__attribute__((visibility("default"))) int rgc_exec_step_at(rgc_exec* e, size_t k) {
+  return guard([&] {
+    Program* p = e->owner->p.get();
+    if (k >= p->steps.size()) return fail(RGC_ERR_INVALID, "step index out of range");
+    if (e->f->failed) return fail(RGC_ERR_DEVICE, e->f->error);
+    Ctx c{e->f->stream, e->f.get()};
+    p->steps[k].run(c);
+    p->launches += (uint64_t)p->steps[k].kernels;
+    check_async(e);
+    return e->f->failed ? fail(RGC_ERR_DEVICE, e->f->error) : RGC_OK;
+  });
+}
+
+__attribute__((visibility("default"))) int rgc_exec_swap(rgc_exec* e, size_t a, size_t b) {
+  return guard([&] {
+    if (a >= e->f->ptr.size() || b >= e->f->ptr.size()) return fail(RGC_ERR_INVALID, "slot out of range");
+    std::swap(e->f->ptr[a], e->f->ptr[b]);
+    return RGC_OK;
+  });
+}
+
+__attribute__((visibility("default"))) int rgc_exec_prefix(rgc_exec* e, size_t slot, void* host, size_t bytes) {
+  return guard([&] {
+    const Plan& plan = e->owner->p->plan;
+    if (slot >= plan.slots.size()) return fail(RGC_ERR_INVALID, "slot out of range");
+    if (bytes > plan.slots[slot].second * rg::dtype_size(plan.slots[slot].first)) return fail(RGC_ERR_INVALID, "read beyond the slot");
+    if (bytes) ck(cudaMemcpyAsync(host, e->f->ptr[slot], bytes, cudaMemcpyDeviceToHost, e->f->stream), "read slot");
+    cudaError_t err = cudaStreamSynchronize(e->f->stream);
+    if (err != cudaSuccess) {
+      mark_failed(e, cudaGetErrorString(err));
+      return fail(RGC_ERR_DEVICE, e->f->error);
+    }
+    return RGC_OK;
+  });
+}
+
+__attribute__((visibility("default"))) int rgc_exec_write_prefix(rgc_exec* e, size_t slot, const void* host, size_t bytes) {
+  return guard([&] {
+    const Plan& plan = e->owner->p->plan;
+    if (slot >= plan.slots.size()) return fail(RGC_ERR_INVALID, "slot out of range");
+    if (bytes > plan.slots[slot].second * rg::dtype_size(plan.slots[slot].first)) return fail(RGC_ERR_INVALID, "write beyond the slot");
+    if (bytes) {
+      ck(cudaMemcpyAsync(e->f->ptr[slot], host, bytes, cudaMemcpyHostToDevice, e->f->stream), "write slot");
+      ck(cudaStreamSynchronize(e->f->stream), "write slot");
+    }
+    return RGC_OK;
+  });
+}
+
+__attribute__((visibility("default"))) int rgc_exec_scalar(rgc_exec* e, size_t slot, double* out) {
+  return guard([&] {
+    const Plan& plan = e->owner->p->plan;
+    if (slot >= plan.slots.size()) return fail(RGC_ERR_INVALID, "slot out of range");
+    DType d = plan.slots[slot].first;
+    char buf[8] = {0};
+    int rc = rgc_exec_prefix(e, slot, buf, rg::dtype_size(d));
+    if (rc) return rc;
+    *out = d == DType::F32 ? (double)*(float*)buf : d == DType::F64 ? *(double*)buf : (double)*(int32_t*)buf;
+    return RGC_OK;
+  });
+}
+
+__attribute__((visibility("default"))) int rgc_exec_failure(rgc_exec* e, char* buf, size_t cap) {
+  if (!e || !e->f) return 0;
+  if (!e->f->failed) {
+    cudaError_t err = cudaStreamSynchronize(e->f->stream);
+    if (err == cudaSuccess) err = cudaGetLastError();
+    if (err != cudaSuccess) mark_failed(e, std::string("device error: ") + cudaGetErrorString(err));
+  }
+  if (!e->f->failed) return 0;
+  if (buf && cap) {
+    std::strncpy(buf, e->f->error.c_str(), cap - 1);
+    buf[cap - 1] = 0;
+  }
+  return 1;
+}
+
+__attribute__((visibility("default"))) int rgc_exec_slot_pointer(rgc_exec* e, size_t slot, void** out) {
+  if (!e || slot >= e->f->ptr.size()) return fail(RGC_ERR_INVALID, "slot out of range");
+  *out = e->f->ptr[slot];
+  return RGC_OK;
+}
+
+// validate.rs:290-363 on the device. Steps run in chunks without host synchronisation; every
+// step's history scalars go to a device array and the first non-finite step is recorded on the
+// device. State is snapshotted at each chunk start, so a chunk that went past a non-finite step
+// is restored and replayed (every kernel is deterministic) up to that step, which is where rg's
+// loop stops.
+__attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_run_spec* spec, const void* const* state, const void* const* batches,
+                                                        size_t n_batches, size_t steps, double* history, void* const* outputs, const size_t* output_bytes,
+                                                        size_t* steps_done, int64_t* nonfinite_step, double* seconds) {
+  return guard([&] {
+    Program* p = e->owner->p.get();
+    const Plan& plan = p->plan;
+    Frame* f = e->f.get();
+    cudaStream_t s = f->stream;
+    *steps_done = 0;
+    *nonfinite_step = -1;
+    *seconds = 0;
+    if (f->failed) return fail(RGC_ERR_DEVICE, f->error);
+    auto slot_bytes = [&](size_t slot) { return plan.slots[slot].second * rg::dtype_size(plan.slots[slot].first); };
+    auto in_bytes = [&](size_t input) { return plan.input_ns[input] * rg::dtype_size(plan.slots[plan.input_slots[input]].first); };
+    for (size_t k = 0; k < spec->n_state; ++k) {
+      if (spec->state_inputs[k] >= plan.input_slots.size() || spec->state_outputs[k] >= plan.outputs.size()) return fail(RGC_ERR_INVALID, "run spec index out of range");
+      size_t b = in_bytes(spec->state_inputs[k]);
+      if (b) ck(cudaMemcpyAsync(f->ptr[plan.input_slots[spec->state_inputs[k]]], state[k], b, cudaMemcpyHostToDevice, s), "load state");
+    }
+    for (size_t d = 0; d < spec->n_data; ++d)
+      if (spec->data_inputs[d] >= plan.input_slots.size()) return fail(RGC_ERR_INVALID, "run spec index out of range");
+    for (size_t h = 0; h < spec->n_history; ++h)
+      if (spec->history_outputs[h] >= plan.outputs.size()) return fail(RGC_ERR_INVALID, "run spec index out of range");
+    // Batches: one batch is loaded once; several live on the device and a kernel picks one per step.
+    std::vector<char*> batch_dev(spec->n_data, nullptr);
+    struct Cleanup {
+      std::vector<void*> ptrs;
+      ~Cleanup() {
+        for (void* q : ptrs) cudaFree(q);
+      }
+    } cleanup;
+    if (n_batches == 1) {
+      for (size_t d = 0; d < spec->n_data; ++d) {
+        size_t b = in_bytes(spec->data_inputs[d]);
+        if (b) ck(cudaMemcpyAsync(f->ptr[plan.input_slots[spec->data_inputs[d]]], batches[d], b, cudaMemcpyHostToDevice, s), "load batch");
+      }
+    } else if (n_batches > 1) {
+      for (size_t d = 0; d < spec->n_data; ++d) {
+        size_t b = in_bytes(spec->data_inputs[d]);
+        ck(cudaMalloc((void**)&batch_dev[d], std::max<size_t>(1, b * n_batches)), "cudaMalloc(batches)");
+        cleanup.ptrs.push_back(batch_dev[d]);
+        for (size_t q = 0; q < n_batches; ++q)
+          if (b) ck(cudaMemcpyAsync(batch_dev[d] + q * b, batches[q * spec->n_data + d], b, cudaMemcpyHostToDevice, s), "upload batches");
+      }
+    }
+    // Swaps and copies exactly as rg decides them (validate.rs:303-318).
+    std::vector<size_t> out_slots;
+    for (size_t k = 0; k < spec->n_state; ++k) out_slots.push_back(plan.outputs[spec->state_outputs[k]].slot);
+    std::vector<std::pair<size_t, size_t>> swaps;
+    std::vector<std::tuple<size_t, size_t, size_t>> copies;  // (input slot, output slot, bytes)
+    for (size_t k = 0; k < spec->n_state; ++k) {
+      size_t is = plan.input_slots[spec->state_inputs[k]], os = out_slots[k];
+      if (is == os) continue;
+      size_t users = std::count(out_slots.begin(), out_slots.end(), os);
+      if (!plan.pinned[os] && users == 1 && plan.slots[os].second == plan.slots[is].second) swaps.emplace_back(is, os);
+      else copies.emplace_back(is, os, plan.outputs[spec->state_outputs[k]].n * rg::dtype_size(plan.slots[os].first));
+    }
+    size_t nh = spec->n_history;
+    double* hist_dev = nullptr;
+    long long* ctr = nullptr;  // [0] = step counter, [1] = first non-finite step
+    char* staging = nullptr;
+    size_t staging_bytes = 0;
+    for (auto& c : copies) staging_bytes += align_up(std::get<2>(c));
+    ck(cudaMalloc((void**)&hist_dev, std::max<size_t>(1, nh * steps) * sizeof(double)), "cudaMalloc(history)");
+    cleanup.ptrs.push_back(hist_dev);
+    ck(cudaMalloc((void**)&ctr, 2 * sizeof(long long)), "cudaMalloc(counters)");
+    cleanup.ptrs.push_back(ctr);
+    if (staging_bytes) {
+      ck(cudaMalloc((void**)&staging, staging_bytes), "cudaMalloc(copy staging)");
+      cleanup.ptrs.push_back(staging);
+    }
+    // History slot pointers per layout, and types.
+    std::vector<int> types(nh);
+    for (size_t h = 0; h < nh; ++h) {
+      DType d = plan.slots[plan.outputs[spec->history_outputs[h]].slot].first;
+      types[h] = d == DType::F32 ? 0 : d == DType::F64 ? 1 : 2;
+    }
+    int* types_dev = nullptr;
+    void** hptr_dev = nullptr;  // [2][nh]
+    if (nh) {
+      ck(cudaMalloc((void**)&types_dev, nh * sizeof(int)), "cudaMalloc(types)");
+      cleanup.ptrs.push_back(types_dev);
+      ck(cudaMemcpyAsync(types_dev, types.data(), nh * sizeof(int), cudaMemcpyHostToDevice, s), "upload types");
+      ck(cudaMalloc((void**)&hptr_dev, 2 * nh * sizeof(void*)), "cudaMalloc(history pointers)");
+      cleanup.ptrs.push_back(hptr_dev);
+    }
+    // The two layouts: the current one, and the one after applying every swap.
+    std::vector<char*> layout[2];
+    layout[0] = f->ptr;
+    layout[1] = f->ptr;
+    for (auto& sw : swaps) std::swap(layout[1][sw.first], layout[1][sw.second]);
+    bool alternating = !swaps.empty();
+    if (nh) {
+      std::vector<void*> hp(2 * nh);
+      for (int L = 0; L < 2; ++L)
+        for (size_t h = 0; h < nh; ++h) hp[L * nh + h] = layout[L][plan.outputs[spec->history_outputs[h]].slot];
+      ck(cudaMemcpyAsync(hptr_dev, hp.data(), hp.size() * sizeof(void*), cudaMemcpyHostToDevice, s), "upload history pointers");
+    }
+    long long init[2] = {0, -1};
+    ck(cudaMemcpyAsync(ctr, init, sizeof init, cudaMemcpyHostToDevice, s), "reset counters");
+
+    // One step with layout L: batch load, the plan, history, copies (through staging), counter.
+    auto one_step = [&](int L, cudaStream_t st) {
+      f->ptr = layout[L];
+      if (n_batches > 1)
+        for (size_t d = 0; d < spec->n_data; ++d)
+          load_batch(f->ptr[plan.input_slots[spec->data_inputs[d]]], batch_dev[d], in_bytes(spec->data_inputs[d]), (long long)n_batches, ctr, st);
+      Ctx c{st, f};
+      run_steps(p, c);
+      if (nh) record_history(hist_dev, (const void* const*)(hptr_dev + L * nh), types_dev, (int)nh, ctr, ctr + 1, st);
+      size_t off = 0;
+      for (auto& cp : copies) {
+        ck(cudaMemcpyAsync(staging + off, layout[L][std::get<1>(cp)], std::get<2>(cp), cudaMemcpyDeviceToDevice, st), "state copy");
+        off += align_up(std::get<2>(cp));
+      }
+      off = 0;
+      for (auto& cp : copies) {
+        ck(cudaMemcpyAsync(layout[alternating ? 1 - L : L][std::get<0>(cp)], staging + off, std::get<2>(cp), cudaMemcpyDeviceToDevice, st), "state copy");
+        off += align_up(std::get<2>(cp));
+      }
+      bump_counter(ctr, st);
+    };
+    bool use_graphs = graphs_enabled() && p->capturable;
+    cudaGraphExec_t g[2] = {nullptr, nullptr};
+    struct GraphCleanup {
+      cudaGraphExec_t* g;
+      bool two;
+      ~GraphCleanup() {
+        if (g[0]) cudaGraphExecDestroy(g[0]);
+        if (two && g[1]) cudaGraphExecDestroy(g[1]);
+      }
+    } graph_cleanup{g, alternating};
+    if (use_graphs) {
+      for (int LL = 0; LL < (alternating ? 2 : 1); ++LL) g[LL] = capture(s, [&](cudaStream_t st) { one_step(LL, st); });
+      if (!alternating) g[1] = g[0];
+    }
+    uint64_t per_step = (uint64_t)p->kernels_per_step + (nh ? 1 : 0) + 1 + (n_batches > 1 ? spec->n_data : 0);
+    // State snapshot buffers (chunk starts), sized by the state inputs.
+    std::vector<std::pair<size_t, size_t>> snap_items;  // (input slot, bytes)
+    size_t snap_bytes = 0;
+    for (size_t k = 0; k < spec->n_state; ++k) {
+      size_t is = plan.input_slots[spec->state_inputs[k]];
+      snap_items.emplace_back(is, in_bytes(spec->state_inputs[k]));
+      snap_bytes += align_up(in_bytes(spec->state_inputs[k]));
+    }
+    char* snap = nullptr;
+    if (snap_bytes) {
+      ck(cudaMalloc((void**)&snap, snap_bytes), "cudaMalloc(snapshot)");
+      cleanup.ptrs.push_back(snap);
+    }
+    const char* env_chunk = getenv("RGC_RUN_CHUNK");
+    size_t chunk = env_chunk ? (size_t)std::max(1, atoi(env_chunk)) : 64;
+    int L = 0;
+    size_t done = 0;
+    long long bad = -1;
+    ck(cudaStreamSynchronize(s), "run setup");
+    // Device time of the loop, from events on the stream every step runs on.
+    cudaEvent_t ev0, ev1;
+    ck(cudaEventCreate(&ev0), "cudaEventCreate");
+    ck(cudaEventCreate(&ev1), "cudaEventCreate");
+    struct EventCleanup {
+      cudaEvent_t a, b;
+      ~EventCleanup() {
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+      }
+    } event_cleanup{ev0, ev1};
+    ck(cudaEventRecord(ev0, s), "cudaEventRecord");
+    auto snapshot = [&](int LL, bool restore) {
+      size_t off = 0;
+      for (auto& [slot, bytes] : snap_items) {
+        if (bytes) {
+          if (restore) ck(cudaMemcpyAsync(layout[LL][slot], snap + off, bytes, cudaMemcpyDeviceToDevice, s), "restore state");
+          else ck(cudaMemcpyAsync(snap + off, layout[LL][slot], bytes, cudaMemcpyDeviceToDevice, s), "snapshot state");
+        }
+        off += align_up(bytes);
+      }
+    };
+    auto launch = [&](int LL) {
+      if (use_graphs) ck(cudaGraphLaunch(g[LL], s), "cudaGraphLaunch");
+      else one_step(LL, s);
+      p->launches += per_step;
+    };
+    while (done < steps) {
+      if (p->inject.exchange(false)) {
+        mark_failed(e, "injected failure for test");
+        break;
+      }
+      size_t n = std::min(chunk, steps - done);
+      if (snap) snapshot(L, false);
+      int L0 = L;
+      for (size_t q = 0; q < n; ++q) {
+        launch(L);
+        if (alternating) L = 1 - L;
+      }
+      long long host_ctr[2];
+      ck(cudaMemcpyAsync(host_ctr, ctr, sizeof host_ctr, cudaMemcpyDeviceToHost, s), "read counters");
+      cudaError_t err = cudaStreamSynchronize(s);
+      if (err != cudaSuccess) {
+        mark_failed(e, std::string("device error: ") + cudaGetErrorString(err));
+        break;
+      }
+      if (host_ctr[1] >= 0) {
+        bad = host_ctr[1];
+        // Replay the chunk up to and including the bad step from the snapshot.
+        if (snap) snapshot(L0, true);
+        L = L0;
+        long long rewind[1] = {(long long)done};
+        ck(cudaMemcpyAsync(ctr, rewind, sizeof(long long), cudaMemcpyHostToDevice, s), "rewind counter");
+        for (long long q = (long long)done; q <= bad; ++q) {
+          launch(L);
+          if (alternating) L = 1 - L;
+        }
+        ck(cudaStreamSynchronize(s), "replay");
+        done = (size_t)bad + 1;
+        break;
+      }
+      done += n;
+    }
+    ck(cudaEventRecord(ev1, s), "cudaEventRecord");
+    ck(cudaStreamSynchronize(s), "run");
+    float ms = 0;
+    ck(cudaEventElapsedTime(&ms, ev0, ev1), "cudaEventElapsedTime");
+    *seconds = ms * 1e-3;
+    *steps_done = done;
+    *nonfinite_step = bad;
+    if (history && nh && done) {
+      std::vector<double> hv(nh * done);
+      ck(cudaMemcpy(hv.data(), hist_dev, hv.size() * sizeof(double), cudaMemcpyDeviceToHost), "read history");
+      for (size_t h = 0; h < nh; ++h)
+        for (size_t k = 0; k < done; ++k) history[h * steps + k] = hv[k * nh + h];
+    }
+    // Outputs of the last completed step live in the layout that step ran with.
+    int last_L = alternating && done ? 1 - L : L;
+    if (outputs && done) {
+      for (size_t o = 0; o < plan.outputs.size(); ++o) {
+        size_t b = std::min(output_bytes[o], slot_bytes(plan.outputs[o].slot));
+        if (b && outputs[o]) ck(cudaMemcpy(outputs[o], layout[last_L][plan.outputs[o].slot], b, cudaMemcpyDeviceToHost), "read outputs");
+      }
+    }
+    // The frame keeps the layout after the last step's swaps: the state is in the input slots.
+    f->ptr = layout[L];
+    if (f->failed) return fail(RGC_ERR_DEVICE, f->error);
+    return RGC_OK;
+  });
+}
+
+__attribute__((visibility("default"))) int rgc_exec_step_timed(rgc_exec* e, double* seconds, size_t n_steps) {
+  return guard([&] {
+    Program* p = e->owner->p.get();
+    if (n_steps < p->steps.size()) return fail(RGC_ERR_INVALID, "seconds array too short");
+    cudaStream_t s = e->f->stream;
+    std::vector<cudaEvent_t> ev(p->steps.size() + 1);
+    for (auto& x : ev) ck(cudaEventCreate(&x), "cudaEventCreate");
+    ck(cudaEventRecord(ev[0], s), "cudaEventRecord");
+    Ctx c{s, e->f.get()};
+    for (size_t k = 0; k < p->steps.size(); ++k) {
+      p->steps[k].run(c);
+      ck(cudaEventRecord(ev[k + 1], s), "cudaEventRecord");
+    }
+    ck(cudaStreamSynchronize(s), "step_timed");
+    for (size_t k = 0; k < p->steps.size(); ++k) {
+      float ms = 0;
+      cudaEventElapsedTime(&ms, ev[k], ev[k + 1]);
+      seconds[k] += ms * 1e-3;
+    }
+    for (auto& x : ev) cudaEventDestroy(x);
+    p->launches += (uint64_t)p->kernels_per_step;
+    return RGC_OK;
+  });
+}
+
+__attribute__((visibility("default"))) int rgc_exec_breakdown_json(rgc_exec* e, size_t repeats, char* buf, size_t cap) {
+  return guard([&] {
+    Program* p = e->owner->p.get();
+    cudaStream_t s = e->f->stream;
+    repeats = std::max<size_t>(1, repeats);
+    cudaEvent_t a, b;
+    ck(cudaEventCreate(&a), "cudaEventCreate");
+    ck(cudaEventCreate(&b), "cudaEventCreate");
+    auto t0 = std::chrono::steady_clock::now();
+    ck(cudaEventRecord(a, s), "cudaEventRecord");
+    for (size_t r = 0; r < repeats; ++r) launch_plan(e);
+    ck(cudaEventRecord(b, s), "cudaEventRecord");
+    auto t1 = std::chrono::steady_clock::now();
+    ck(cudaStreamSynchronize(s), "breakdown");
+    auto t2 = std::chrono::steady_clock::now();
+    float ms = 0;
+    cudaEventElapsedTime(&ms, a, b);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    char tmp[512];
+    snprintf(tmp, sizeof tmp,
+             "{\"repeats\":%zu,\"plan_steps\":%zu,\"kernels_per_step\":%d,\"gpu_seconds_per_step\":%.9g,\"launch_seconds_per_step\":%.9g,"
+             "\"wall_seconds_per_step\":%.9g,\"graph_capturable\":%s}",
+             repeats, p->steps.size(), p->kernels_per_step, ms * 1e-3 / repeats,
+             std::chrono::duration<double>(t1 - t0).count() / repeats, std::chrono::duration<double>(t2 - t0).count() / repeats,
+             p->capturable ? "true" : "false");
+    if (buf && cap) {
+      std::strncpy(buf, tmp, cap - 1);
+      buf[cap - 1] = 0;
+    }
+    return RGC_OK;
+  });
+}
+
+}  // extern "C"

@@ -461,6 +461,7 @@ Pairs vjp(Graph& g, size_t i, uint32_t ct, const std::vector<bool>& rel) {
     case OpKind::Floor: case OpKind::Argmax: case OpKind::RandUniform: case OpKind::RandNormal:
     case OpKind::KeySplit: case OpKind::Placeholder: case OpKind::ArgTopK: case OpKind::Output:
       break;
+    case OpKind::AllReduce: out.emplace_back(x, g.add(Op::make(OpKind::AllReduce), {ct})); break;
     case OpKind::Cumsum: {
       Op o = Op::make(OpKind::Cumsum);
       o.flag_a = !node.op.flag_a;

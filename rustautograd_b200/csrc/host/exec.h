@@ -52,7 +52,17 @@ struct Program {
   // Per-step timing and a launch breakdown for `profile` (metal.rs:692-712).
   virtual bool step_timed(Exec&, std::vector<double>&) { return false; }
   virtual Json breakdown(Exec&, size_t) { return Json(); }
+  // Device kernels launched on behalf of this program so far (0 where not counted).
+  virtual uint64_t launches() const { return 0; }
 };
+
+// Algorithmic work of each plan step: floating-point operations (2 per multiply-add) and the
+// bytes a step must read and write at least once. The roofline of a kernel is judged on these.
+struct StepCost {
+  std::string kind;  // "fused", "matmul", "reduce", ... (the op name for single instructions)
+  double flops = 0, bytes = 0;
+};
+std::vector<StepCost> step_costs(const Plan& p);
 
 struct Device {
   virtual ~Device() = default;

@@ -63,6 +63,7 @@ const char* Op::name() const {
     case OpKind::Output: return "output";
     case OpKind::Placeholder: return "placeholder";
     case OpKind::Custom: return "custom_vjp";
+    case OpKind::AllReduce: return "all_reduce";
   }
   return "?";
 }
@@ -499,7 +500,7 @@ std::vector<size_t> Graph::infer(const Op& op, const std::vector<std::vector<siz
     }
     case OpKind::RandUniform: case OpKind::RandNormal: return op.shape;
     case OpKind::KeySplit: return {op.index, 2};
-    case OpKind::Custom: return s[0];
+    case OpKind::Custom: case OpKind::AllReduce: return s[0];
     case OpKind::Reduce: {
       size_t r = s[0].size();
       std::vector<bool> seen(r, false);

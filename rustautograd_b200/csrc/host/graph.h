@@ -31,6 +31,8 @@ enum class OpKind : uint8_t {
   StopGradient, Floor, Take, TakeAlong, TakeGrad, TakeAlongGrad, Concat, Argmax,
   RandUniform, RandNormal, KeySplit, ArgTopK, Cumsum, Scan, While, Cond, Output,
   Placeholder, Custom,
+  // Data parallelism (no counterpart in rg): the sum of a value over all ranks.
+  AllReduce,
 };
 
 struct Op {

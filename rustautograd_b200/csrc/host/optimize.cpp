@@ -228,7 +228,7 @@ Simplified simplify(const Graph& g, const std::vector<uint32_t>& outputs, bool f
         r.st.simplified += 1;
       }
     }
-    bool foldable = !op.is_control_flow() && op.kind != OpKind::Output && !ins.empty() && node.n() <= FOLD_LIMIT;
+    bool foldable = !op.is_control_flow() && op.kind != OpKind::Output && op.kind != OpKind::AllReduce && !ins.empty() && node.n() <= FOLD_LIMIT;
     for (auto x : ins) foldable = foldable && ng.nodes[x].op.kind == OpKind::Const;
     if (foldable) {
       Graph tmp;

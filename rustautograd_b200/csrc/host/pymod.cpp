@@ -93,7 +93,7 @@ Op parse_op(const std::string& name, const py::dict* a) {
       {"cos", OpKind::Cos}, {"tanh", OpKind::Tanh}, {"abs", OpKind::Abs}, {"sign", OpKind::Sign}, {"add", OpKind::Add},
       {"sub", OpKind::Sub}, {"mul", OpKind::Mul}, {"div", OpKind::Div}, {"pow", OpKind::Pow}, {"maximum", OpKind::Max},
       {"minimum", OpKind::Min}, {"gt", OpKind::Gt}, {"ge", OpKind::Ge}, {"where", OpKind::Where}, {"matmul", OpKind::MatMul},
-      {"stop_gradient", OpKind::StopGradient}, {"floor", OpKind::Floor}, {"take_along", OpKind::TakeAlong}, {"argmax", OpKind::Argmax},
+      {"stop_gradient", OpKind::StopGradient}, {"floor", OpKind::Floor}, {"take_along", OpKind::TakeAlong}, {"argmax", OpKind::Argmax}, {"all_reduce", OpKind::AllReduce},
   };
   for (auto& [n, k] : simple)
     if (name == n) return Op::make(k);
@@ -356,6 +356,28 @@ PYBIND11_MODULE(RG_MODULE_NAME, m) {
       .def("plan_blob", [](const PyCompiled& self) {
         auto b = encode_plan(self.c->plan);
         return py::bytes((const char*)b.data(), b.size());
+      })
+      // Not in rg's module: device kernel launches so far, per-step device seconds (averaged over
+      // `repeats` runs timed with events between steps), and each step's algorithmic cost.
+      .def("launches", [](const PyCompiled& self) { return self.c->program->launches(); })
+      .def("step_seconds", [](const PyCompiled& self, std::vector<PyTensor> inputs, size_t repeats) {
+        auto in = tensors(inputs);
+        std::vector<double> secs(self.c->plan.steps.size(), 0.0);
+        {
+          py::gil_scoped_release nogil;
+          auto e = self.c->program->exec();
+          for (size_t k = 0; k < in.size(); ++k) e->load(k, in[k]);
+          repeats = std::max<size_t>(1, repeats);
+          for (size_t r = 0; r < repeats; ++r)
+            if (!self.c->program->step_timed(*e, secs)) throw std::runtime_error("this device does not time steps");
+        }
+        for (auto& s : secs) s /= (double)repeats;
+        return secs;
+      })
+      .def("step_costs", [](const PyCompiled& self) {
+        std::vector<std::tuple<std::string, double, double>> out;
+        for (auto& c : step_costs(self.c->plan)) out.emplace_back(c.kind, c.flops, c.bytes);
+        return out;
       })
       .def("plan_summary", [](const PyCompiled& self) {
         Json a = Json::array();

@@ -78,4 +78,45 @@ RunOut run_loop(const Plan& p, Exec& e, const RunSpec& spec, const std::vector<T
   return r;
 }
 
+std::vector<StepCost> step_costs(const Plan& p) {
+  std::vector<StepCost> out;
+  for (auto& st : p.steps) {
+    StepCost c;
+    if (st.fused) {
+      const Fused& f = st.group;
+      c.kind = "fused";
+      double es = (double)dtype_size(f.dtype);
+      // Full inputs and outputs stream once; splats, rows and broadcasts are reused from cache.
+      double full = 0;
+      for (auto& in : f.inputs) full += in.kind == ArgKind::Full ? 1.0 : 0.0;
+      c.bytes = (double)f.n * es * (full + (double)f.outputs.size());
+      c.flops = (double)f.n * (double)f.ops.size();
+      out.push_back(c);
+      continue;
+    }
+    const Instr& i = st.instr;
+    c.kind = i.op.name();
+    double es = (double)dtype_size(i.dtype);
+    double in_bytes = 0;
+    for (size_t k = 0; k < i.arg_shapes.size(); ++k) in_bytes += (double)product(i.arg_shapes[k]) * es;
+    if (i.op.kind == OpKind::MatMul || i.op.kind == OpKind::MatMulT) {
+      c.kind = "matmul";
+      const auto &sa = i.arg_shapes[0], &sb = i.arg_shapes[1];
+      bool ta = i.op.kind == OpKind::MatMulT && i.op.flag_a;
+      double k = sa.size() >= 2 ? (double)(ta ? sa[sa.size() - 2] : sa.back()) : (double)sa[0];
+      (void)sb;
+      c.flops = 2.0 * (double)i.n * k;
+      c.bytes = in_bytes + (double)i.n * es;
+    } else if (i.op.kind == OpKind::Reduce) {
+      c.flops = in_bytes / es;
+      c.bytes = in_bytes + (double)i.n * es;
+    } else {
+      c.bytes = in_bytes + (double)i.n * es;
+      c.flops = 0;
+    }
+    out.push_back(c);
+  }
+  return out;
+}
+
 }  // namespace rg

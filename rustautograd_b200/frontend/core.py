@@ -1,0 +1,543 @@
+"""Tracing front end for the rg engine interface (`_rg` modules).
+
+Python operations on `Tensor`s run eagerly (one-node graphs evaluated by the engine's device);
+inside `compile`, `value_and_grad` and friends they record nodes on a `Tracer`. The op sequence
+a program emits is the one rg's own front end emits (python/rg/_core.py), so the same program
+yields the same graph and therefore the same compiled plan: scalars become constants of the
+dtype of the first tensor operand, reductions over axes, `mean` as sum then divide, slicing as
+`slice` plus `reshape`, and so on. This front end works over any module with rg's `_rg`
+interface: the CUDA device module of this package (the default) or a CPU one.
+"""
+import array
+import json
+import os
+import sys
+
+_TYPECODES = {"float32": "f", "float64": "d", "int32": "i"}
+_state = {"native": None, "device": None}
+_trace_stack = []
+_PKG = os.path.dirname(os.path.abspath(__file__)) + os.sep
+
+
+def use(native, device=None):
+    """Selects the engine module (rg's `_rg` interface) and the default compile device."""
+    _state["native"] = native
+    _state["device"] = device
+
+
+def native():
+    if _state["native"] is None:
+        from .. import _rg
+        _state["native"] = _rg
+    return _state["native"]
+
+
+def default_device():
+    if _state["device"] is not None:
+        return _state["device"]
+    devs = native().available_devices()
+    return devs[0] if devs else "cuda"
+
+
+def _where_from():
+    f = sys._getframe(1)
+    while f is not None and f.f_code.co_filename.startswith(_PKG):
+        f = f.f_back
+    return f"{f.f_code.co_filename}:{f.f_lineno}" if f else None
+
+
+class DiagnosticError(Exception):
+    """A front-end diagnostic with the same JSON shape as the engine's."""
+
+
+def _error(code, observation, cause):
+    d = {"status": "validation_failed", "severity": "error", "code": code,
+         "node": {"id": None, "operation": None, "source": _where_from(), "role": "forward"},
+         "observation": observation, "diagnosis": {"cause": cause, "certainty": "verified"}}
+    e = DiagnosticError(json.dumps(d))
+    e.diagnostic = d
+    return e
+
+
+def _axis(x, axis):
+    return axis + x.ndim if axis < 0 else axis
+
+
+class _Math:
+    """Operators shared by concrete tensors and tracers."""
+    __array_ufunc__ = None
+
+    def __add__(self, o): return op("add", self, o)
+    def __radd__(self, o): return op("add", o, self)
+    def __sub__(self, o): return op("sub", self, o)
+    def __rsub__(self, o): return op("sub", o, self)
+    def __mul__(self, o): return op("mul", self, o)
+    def __rmul__(self, o): return op("mul", o, self)
+    def __truediv__(self, o): return op("div", self, o)
+    def __rtruediv__(self, o): return op("div", o, self)
+    def __pow__(self, o): return op("pow", self, o)
+    def __rpow__(self, o): return op("pow", o, self)
+    def __matmul__(self, o): return op("matmul", self, o)
+    def __rmatmul__(self, o): return op("matmul", o, self)
+    def __neg__(self): return op("neg", self)
+    def __abs__(self): return op("abs", self)
+    def __gt__(self, o): return op("gt", self, o)
+    def __ge__(self, o): return op("ge", self, o)
+    def __lt__(self, o): return op("gt", o, self)
+    def __le__(self, o): return op("ge", o, self)
+
+    @property
+    def ndim(self): return len(self.shape)
+
+    @property
+    def size(self):
+        n = 1
+        for d in self.shape:
+            n *= d
+        return n
+
+    def _axes(self, axis):
+        if axis is None:
+            return list(range(self.ndim))
+        axes = axis if isinstance(axis, (tuple, list)) else [axis]
+        return [a + self.ndim if a < 0 else a for a in axes]
+
+    def sum(self, axis=None, keepdims=False): return op("sum", self, axes=self._axes(axis), keepdims=keepdims)
+    def max(self, axis=None, keepdims=False): return op("max", self, axes=self._axes(axis), keepdims=keepdims)
+    def min(self, axis=None, keepdims=False): return op("min", self, axes=self._axes(axis), keepdims=keepdims)
+
+    def mean(self, axis=None, keepdims=False):
+        axes = self._axes(axis)
+        count = 1
+        for a in axes:
+            count *= self.shape[a] if 0 <= a < self.ndim else 1
+        return self.sum(axis=axes, keepdims=keepdims) / count
+
+    def reshape(self, *shape):
+        target = list(shape[0]) if len(shape) == 1 and isinstance(shape[0], (tuple, list)) else list(shape)
+        if target.count(-1) == 1:
+            known = 1
+            for d in target:
+                known *= d if d != -1 else 1
+            target[target.index(-1)] = self.size // known if known else 0
+        return op("reshape", self, shape=target)
+
+    def transpose(self, *perm):
+        p = list(perm[0]) if len(perm) == 1 and isinstance(perm[0], (tuple, list)) else list(perm)
+        return op("transpose", self, perm=p or list(reversed(range(self.ndim))))
+
+    @property
+    def T(self): return self.transpose()
+
+    def cast(self, dtype): return op("cast", self, dtype=dtype)
+    def astype(self, dtype): return self if self.dtype == dtype else self.cast(dtype)
+    def exp(self): return op("exp", self)
+    def log(self): return op("log", self)
+    def sqrt(self): return op("sqrt", self)
+    def tanh(self): return op("tanh", self)
+    def floor(self): return op("floor", self)
+
+    def squeeze(self, axis=None): return squeeze(self, axis)
+
+    def __iter__(self):
+        return (self[i] for i in range(self.shape[0]))
+
+    def __getitem__(self, key):
+        if isinstance(key, (Tensor, Tracer, list)):
+            return take(self, tensor(key, "int32") if isinstance(key, list) else key, 0)
+        key = key if isinstance(key, tuple) else (key,)
+        if any(k is Ellipsis for k in key):
+            at = next(i for i, k in enumerate(key) if k is Ellipsis)
+            used = sum(1 for k in key if k is not None and k is not Ellipsis)
+            key = key[:at] + (slice(None),) * (self.ndim - used) + key[at + 1:]
+        if sum(1 for k in key if k is not None) > self.ndim:
+            raise _error("INVALID_SLICE", {"shape": self.shape, "index_rank": len(key)}, "too_many_indices")
+        # A step other than 1 selects positions with `take`.
+        stepped, plain, position = self, [], 0
+        for k in key:
+            if isinstance(k, slice) and k.step not in (None, 1):
+                idx = list(range(*k.indices(self.shape[position])))
+                stepped = take(stepped, tensor(idx, "int32"), position)
+                k = slice(None)
+            plain.append(k)
+            position += 0 if k is None else 1
+        if stepped is not self:
+            return stepped[tuple(plain)]
+        starts, stops, keep, axis = [], [], [], 0
+        for k in key + (slice(None),) * (self.ndim - sum(1 for k in key if k is not None)):
+            if k is None:
+                keep.append(1)
+                continue
+            dim = self.shape[axis]
+            if isinstance(k, slice):
+                start, stop, _ = k.indices(dim)
+                starts.append(start)
+                stops.append(max(start, stop))
+                keep.append(max(0, stop - start))
+            else:
+                i = k + dim if k < 0 else k
+                if not 0 <= i < dim:
+                    raise _error("INVALID_SLICE", {"shape": self.shape, "axis": axis, "index": k}, "index_out_of_bounds")
+                starts.append(i)
+                stops.append(i + 1)
+            axis += 1
+        out = op("slice", self, starts=starts, stops=stops)
+        return out.reshape(keep) if tuple(keep) != out.shape else out
+
+
+class Tensor(_Math):
+    """A concrete value held by the engine module."""
+
+    def __init__(self, handle):
+        self._t = handle
+
+    @property
+    def shape(self): return tuple(self._t.shape)
+
+    @property
+    def dtype(self): return self._t.dtype
+
+    def numpy(self):
+        import numpy as np
+        return np.frombuffer(self._t.tobytes(), dtype=self.dtype).reshape(self.shape).copy()
+
+    def __array__(self, dtype=None, copy=None):
+        a = self.numpy()
+        return a if dtype is None else a.astype(dtype)
+
+    def tolist(self): return self.numpy().tolist()
+
+    def __float__(self):
+        flat = array.array(_TYPECODES[self.dtype])
+        flat.frombytes(self._t.tobytes())
+        return float(flat[0])
+
+    def __int__(self): return int(float(self))
+
+    def __index__(self): return int(float(self))
+
+    def item(self): return int(self) if self.dtype == "int32" else float(self)
+
+    def __repr__(self): return f"Tensor({self.tolist()}, dtype={self.dtype})"
+
+
+class Tracer(_Math):
+    """A node of the graph being traced."""
+
+    def __init__(self, graph, node):
+        self._g = graph
+        self._id = node
+
+    @property
+    def shape(self): return tuple(self._g.shape(self._id))
+
+    @property
+    def dtype(self): return self._g.dtype(self._id)
+
+    def __bool__(self):
+        raise _error("CONTROL_FLOW_ON_TRACER", {"node": self._id}, "python_value_depends_on_traced_tensor_use_rg_where")
+
+    def __repr__(self): return f"Tracer(node={self._id}, shape={self.shape}, dtype={self.dtype})"
+
+
+def _ints_only(x):
+    if isinstance(x, (list, tuple)):
+        return all(_ints_only(i) for i in x)
+    return isinstance(x, int)
+
+
+def tensor(data, dtype=None):
+    """A Tensor from a Tensor, numpy array, number or nested list (ints -> int32, floats -> float32)."""
+    if isinstance(data, Tensor):
+        return data if dtype in (None, data.dtype) else data.cast(dtype)
+    if hasattr(data, "tobytes") and hasattr(data, "dtype"):
+        name = str(data.dtype)
+        dt = dtype or (name if name in _TYPECODES else ("int32" if data.dtype.kind in "iub" else "float32"))
+        arr = data if name == dt else data.astype(dt)
+        return Tensor(native().Tensor(arr.tobytes(order="C"), list(arr.shape), dt))
+    dt = dtype or ("int32" if _ints_only(data) else "float32")
+    flat = array.array(_TYPECODES[dt])
+    conv = int if dt == "int32" else float
+    shape = []
+
+    def fill(x, depth):
+        if isinstance(x, (list, tuple)):
+            if depth == len(shape):
+                shape.append(len(x))
+            for v in x:
+                fill(v, depth + 1)
+        else:
+            flat.append(conv(x))
+    fill(data, 0)
+    return Tensor(native().Tensor(flat.tobytes(), shape, dt))
+
+
+def _filled(shape, value, dtype):
+    shape = [shape] if isinstance(shape, int) else list(shape)
+    n = 1
+    for d in shape:
+        n *= d
+    return Tensor(native().Tensor((array.array(_TYPECODES[dtype], [value]) * n).tobytes(), shape, dtype))
+
+
+def zeros(shape, dtype="float32"): return _filled(shape, 0, dtype)
+def ones(shape, dtype="float32"): return _filled(shape, 1, dtype)
+def full(shape, value, dtype="float32"): return _filled(shape, value, dtype)
+def zeros_like(x): return _filled(x.shape, 0, x.dtype)
+
+
+def arange(n, dtype="int32"):
+    return Tensor(native().Tensor(array.array(_TYPECODES[dtype], range(n)).tobytes(), [n], dtype))
+
+
+def tril(n, dtype="float32"):
+    """Lower-triangular ones: the causal mask."""
+    vals = array.array(_TYPECODES[dtype], [1 if j <= i else 0 for i in range(n) for j in range(n)])
+    return Tensor(native().Tensor(vals.tobytes(), [n, n], dtype))
+
+
+def _first_dtype(args):
+    for a in args:
+        if isinstance(a, (Tensor, Tracer)):
+            return a.dtype
+    return None
+
+
+def _as_node(g, a, dtype):
+    if isinstance(a, Tracer):
+        if a._g is g:
+            return a._id
+        raise _error("TRACER_LEAK", {"node": a._id}, "tracer_from_a_finished_trace")
+    if isinstance(a, float) and dtype == "int32" and not a.is_integer():
+        raise _error("DTYPE_MISMATCH", {"scalar": a, "tensor_dtype": dtype}, "fractional_scalar_with_int32_tensor_cast_first")
+    t = a if isinstance(a, Tensor) else tensor(a, dtype if isinstance(a, (int, float)) else None)
+    return g.constant(t._t, _where_from())
+
+
+def op(name, *args, **attrs):
+    """Records `name` on the current trace, or evaluates it at once outside one."""
+    dtype = _first_dtype(args)
+    src = _where_from()
+    if _trace_stack:
+        g = _trace_stack[-1]
+        ids = [_as_node(g, a, dtype) for a in args]
+        return Tracer(g, g.op(name, ids, attrs or None, src))
+    g = native().Graph()
+    ids = [_as_node(g, a, dtype) for a in args]
+    return Tensor(g.eval([g.op(name, ids, attrs or None, src)])[0])
+
+
+# ---- functions ----
+
+def stop_gradient(x): return op("stop_gradient", x)
+
+
+def where(c, a, b):
+    dt = _first_dtype((a, b))
+    if dt is not None and isinstance(c, (Tensor, Tracer)) and c.dtype != dt:
+        c = c.cast(dt)
+    return op("where", c, a, b)
+
+
+def maximum(a, b): return op("maximum", a, b)
+def minimum(a, b): return op("minimum", a, b)
+def exp(x): return op("exp", x)
+def log(x): return op("log", x)
+def sqrt(x): return op("sqrt", x)
+def tanh(x): return op("tanh", x)
+def floor(x): return op("floor", x)
+
+
+def all_reduce(x):
+    """Sum of `x` over every data-parallel rank (the identity on a single rank)."""
+    return op("all_reduce", x)
+
+
+def take(x, idx, axis=0):
+    return op("take", x, tensor(idx) if not isinstance(idx, (Tensor, Tracer)) else idx, axis=_axis(x, axis))
+
+
+def swapaxes(x, a, b):
+    p = list(range(x.ndim))
+    a, b = _axis(x, a), _axis(x, b)
+    p[a], p[b] = p[b], p[a]
+    return x.transpose(p)
+
+
+def take_along_axis(x, idx, axis=-1):
+    axis = _axis(x, axis)
+    idx = tensor(idx) if not isinstance(idx, (Tensor, Tracer)) else idx
+    if axis == x.ndim - 1:
+        return op("take_along", x, idx)
+    return swapaxes(op("take_along", swapaxes(x, axis, -1), swapaxes(idx, axis, -1)), axis, -1)
+
+
+def concatenate(xs, axis=0):
+    xs = list(xs)
+    return op("concat", *xs, axis=_axis(xs[0], axis))
+
+
+def squeeze(x, axis=None):
+    if axis is None:
+        drop = [i for i, d in enumerate(x.shape) if d == 1]
+    else:
+        drop = [_axis(x, a) for a in (axis if isinstance(axis, (tuple, list)) else [axis])]
+    return x.reshape([d for i, d in enumerate(x.shape) if i not in drop])
+
+
+# ---- pytrees (dict keys sorted, as rg's _flatten) ----
+
+def flatten(tree):
+    if tree is None:
+        return [], ("none",)
+    if isinstance(tree, (tuple, list)):
+        parts = [flatten(x) for x in tree]
+        return [l for p in parts for l in p[0]], (type(tree).__name__, tuple(p[1] for p in parts))
+    if isinstance(tree, dict):
+        keys = sorted(tree)
+        parts = [flatten(tree[k]) for k in keys]
+        return [l for p in parts for l in p[0]], ("dict", tuple(keys), tuple(p[1] for p in parts))
+    return [tree], None
+
+
+def unflatten(tdef, leaves):
+    it = iter(leaves)
+
+    def build(d):
+        if d is None:
+            return next(it)
+        if d[0] == "none":
+            return None
+        if d[0] == "dict":
+            return {k: build(s) for k, s in zip(d[1], d[2])}
+        items = [build(s) for s in d[1]]
+        return tuple(items) if d[0] == "tuple" else items
+    return build(tdef)
+
+
+def _paths(tdef, prefix):
+    if tdef is None:
+        return [prefix]
+    if tdef[0] == "none":
+        return []
+    if tdef[0] == "dict":
+        return [p for k, s in zip(tdef[1], tdef[2]) for p in _paths(s, f"{prefix}.{k}")]
+    return [p for i, s in enumerate(tdef[1]) for p in _paths(s, f"{prefix}.{i}")]
+
+
+def tree_map(f, t, *rest):
+    ls, d = flatten(t)
+    others = [flatten(r)[0] for r in rest]
+    return unflatten(d, [f(*vals) for vals in zip(ls, *others)])
+
+
+def tree_leaves(t): return flatten(t)[0]
+
+
+# ---- transformations ----
+
+def value_and_grad(f, argnums=0):
+    """`(*args) -> (value, grads of args[argnums])`, recorded as gradient nodes on the trace."""
+    many = isinstance(argnums, tuple)
+    nums = argnums if many else (argnums,)
+
+    def transformed(*args):
+        if not _trace_stack:
+            return compile(transformed, args, validate="none")(*args)
+        g = _trace_stack[-1]
+        src = _where_from()
+        call_args = list(args)
+        groups = []
+        for n in nums:
+            leaves, tdef = flatten(args[n])
+            dtype = _first_dtype(leaves)
+            lifted = [Tracer(g, _as_node(g, l, dtype or "float32")) for l in leaves]
+            call_args[n] = unflatten(tdef, lifted)
+            groups.append((lifted, tdef))
+        y = f(*call_args)
+        yid = _as_node(g, y, _first_dtype([t for lifted, _ in groups for t in lifted]) or "float32")
+        grads = []
+        for lifted, tdef in groups:
+            ids = g.grad(yid, [t._id for t in lifted], src)
+            grads.append(unflatten(tdef, [Tracer(g, i) for i in ids]))
+        return Tracer(g, yid), (tuple(grads) if many else grads[0])
+
+    return transformed
+
+
+class Compiled:
+    """An executable plan plus its compile report."""
+
+    def __init__(self, handle, in_def, in_sig, out_def, n_out):
+        self._n = handle
+        self._in_def = in_def
+        self._in_sig = in_sig
+        self._out_def = out_def
+        self._n_out = n_out
+        self.report = json.loads(handle.report_json)
+
+    def _inputs(self, args):
+        leaves, tdef = flatten(args)
+        ts = [tensor(l) for l in leaves]
+        if tdef != self._in_def or [(t.shape, t.dtype) for t in ts] != self._in_sig:
+            raise _error("INPUT_SIGNATURE_MISMATCH", {"expected": repr(self._in_sig), "recompile_required": True}, "input_signature_changed")
+        return [t._t for t in ts]
+
+    def __call__(self, *args):
+        out = self._n.call(self._inputs(args))
+        return unflatten(self._out_def, [Tensor(t) for t in out[:self._n_out]])
+
+    def plan_blob(self):
+        return self._n.plan_blob()
+
+
+def compile(fn, example_inputs, validate="standard", device=None, optimize="search-linear"):
+    """Traces `fn(*example_inputs)` and compiles it for `device` (default: the module's first)."""
+    if not isinstance(example_inputs, tuple):
+        example_inputs = (example_inputs,)
+    leaves, in_def = flatten(example_inputs)
+    leaves = [tensor(l) for l in leaves]
+    g = native().Graph()
+    src = _where_from()
+    tracers = [Tracer(g, g.input(list(t.shape), t.dtype, src)) for t in leaves]
+    _trace_stack.append(g)
+    try:
+        out = fn(*unflatten(in_def, tracers))
+        out_leaves, out_def = flatten(out)
+        dtype = _first_dtype(leaves) or "float32"
+        out_ids = [_as_node(g, l, dtype) for l in out_leaves]
+    finally:
+        _trace_stack.pop()
+    handle = native().compile(g, out_ids, [t._t for t in leaves], validate, device or default_device(), optimize)
+    return Compiled(handle, in_def, [(t.shape, t.dtype) for t in leaves], out_def, len(out_ids))
+
+
+class RunResult:
+    def __init__(self, **kw):
+        self.__dict__.update(kw)
+
+
+def run(compiled, state, data=None, steps=1):
+    """Iterates `state = step(state[, data])` in the engine: one native call, no Python per step."""
+    arity = len(compiled._in_def[1])
+    leaves, state_def = flatten(state)
+    leaves = [tensor(l) for l in leaves]
+    d = compiled._out_def
+    has_aux = not (d == state_def)
+    aux_def = d[1][1] if has_aux else None
+    n_state = len(leaves)
+    batches = []
+    if arity == 2:
+        batches = [[tensor(l)._t for l in flatten(data)[0]]]
+    aux_names = _paths(aux_def, "aux") if has_aux else []
+    shapes = compiled._n.output_shapes
+    scalar = [k for k in range(n_state, n_state + len(aux_names)) if all(x == 1 for x in shapes[k])]
+    names = {k: aux_names[k - n_state] for k in scalar}
+    state_map = [(k, k) for k in range(n_state)]
+    data_inputs = list(range(n_state, len(compiled._in_sig)))
+    new_state, outputs, hist, ran, bad, seconds = compiled._n.run(state_map, data_inputs, scalar, [t._t for t in leaves], batches, steps)
+    history = {names[k]: h for k, h in zip(scalar, hist)}
+    aux = unflatten(aux_def, [Tensor(t) for t in outputs[n_state:compiled._n_out]]) if has_aux and outputs else None
+    return RunResult(status="stopped_nonfinite" if bad is not None else "completed",
+                     state=unflatten(state_def, [Tensor(t) for t in new_state]), aux=aux, history=history, steps=ran,
+                     nonfinite_step=bad, elapsed=seconds)

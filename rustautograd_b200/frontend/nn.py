@@ -1,0 +1,142 @@
+"""Model building blocks traced onto rg's primitive ops (the compositions of python/rg/nn.py).
+
+Each function emits the same primitive ops in the same order as rg's version, so the CUDA
+device sees the plan rg would build: softmax and layer norm as reductions plus elementwise
+chains, cross-entropy as log-softmax then take-along then mean, attention with a materialised
+masked score matrix.
+"""
+import math
+
+from . import random
+from .core import exp, maximum, stop_gradient, swapaxes, take, take_along_axis, tanh, where, zeros, ones
+
+
+def gelu(x):
+    """Tanh approximation of the Gaussian error linear unit (nn.py:25-27)."""
+    return 0.5 * x * (1.0 + tanh(math.sqrt(2.0 / math.pi) * (x + 0.044715 * x * x * x)))
+
+
+def relu(x): return maximum(x, 0.0)
+
+
+def logsumexp(x, axis=-1, keepdims=False):
+    top = stop_gradient(x.max(axis=axis, keepdims=True))
+    out = exp(x - top).sum(axis=axis, keepdims=True).log() + top
+    return out if keepdims else out.squeeze(axis)
+
+
+def log_softmax(x, axis=-1):
+    return x - logsumexp(x, axis=axis, keepdims=True)
+
+
+def softmax(x, axis=-1):
+    e = exp(x - stop_gradient(x.max(axis=axis, keepdims=True)))
+    return e / e.sum(axis=axis, keepdims=True)
+
+
+def cross_entropy(logits, labels, axis=-1):
+    """Mean negative log-likelihood of int32 labels (nn.py:78-84)."""
+    lp = log_softmax(logits, axis)
+    idx = labels.reshape(tuple(labels.shape) + (1,))
+    return -take_along_axis(lp, idx).mean()
+
+
+def mse_loss(pred, target):
+    d = pred - target
+    return (d * d).mean()
+
+
+def normal_init(std=0.02):
+    return lambda key, shape, dtype="float32": random.normal(key, shape, dtype) * std
+
+
+class Linear:
+    """`x @ w + b`, w of shape (in, out)."""
+
+    def __init__(self, d_in, d_out, bias=True, init=None, dtype="float32"):
+        self.d_in, self.d_out, self.bias, self.dtype = d_in, d_out, bias, dtype
+        self.w_init = init or normal_init(0.02)
+
+    def init(self, key):
+        p = {"w": self.w_init(key, (self.d_in, self.d_out), self.dtype)}
+        if self.bias:
+            p["b"] = zeros(self.d_out, self.dtype)
+        return p
+
+    def __call__(self, p, x):
+        y = x @ p["w"]
+        return y + p["b"] if self.bias else y
+
+
+class Embedding:
+    def __init__(self, n, d, init=None, dtype="float32"):
+        self.n, self.d, self.dtype = n, d, dtype
+        self.w_init = init or normal_init(0.02)
+
+    def init(self, key):
+        return {"table": self.w_init(key, (self.n, self.d), self.dtype)}
+
+    def __call__(self, p, idx):
+        return take(p["table"], idx, 0)
+
+
+class LayerNorm:
+    def __init__(self, d, eps=1e-5, dtype="float32"):
+        self.d, self.eps, self.dtype = d, eps, dtype
+
+    def init(self, key=None):
+        return {"scale": ones(self.d, self.dtype), "shift": zeros(self.d, self.dtype)}
+
+    def __call__(self, p, x):
+        d = x - x.mean(axis=-1, keepdims=True)
+        v = (d * d).mean(axis=-1, keepdims=True)
+        return d / (v + self.eps).sqrt() * p["scale"] + p["shift"]
+
+
+class MultiHeadAttention:
+    """Self-attention with a full (T, T) score matrix and an optional visibility mask."""
+
+    def __init__(self, d, heads, bias=True, init=None, dtype="float32"):
+        if d % heads:
+            raise ValueError(f"model dimension {d} is not divisible by {heads} heads")
+        self.d, self.heads = d, heads
+        self.qkv = Linear(d, 3 * d, bias, init, dtype)
+        self.out = Linear(d, d, bias, init, dtype)
+
+    def init(self, key):
+        k1, k2 = random.split(key)
+        return {"qkv": self.qkv.init(k1), "out": self.out.init(k2)}
+
+    def __call__(self, p, x, mask=None, key=None):
+        b, t, d = x.shape
+        hd = d // self.heads
+        qkv = self.qkv(p["qkv"], x).reshape(b, t, 3, self.heads, hd).transpose(2, 0, 3, 1, 4)
+        q, k, v = qkv[0], qkv[1], qkv[2]
+        scores = q @ swapaxes(k, -1, -2) / math.sqrt(hd)
+        if mask is not None:
+            scores = where(mask, scores, -1e9)
+        weights = softmax(scores)
+        h = (weights @ v).transpose(0, 2, 1, 3).reshape(b, t, d)
+        return self.out(p["out"], h)
+
+
+class TransformerBlock:
+    """Pre-norm block: attention, then a GELU MLP, each with a residual connection."""
+
+    def __init__(self, d, heads, mlp_ratio=4, init=None, dtype="float32"):
+        self.norm1, self.norm2 = LayerNorm(d, dtype=dtype), LayerNorm(d, dtype=dtype)
+        self.attn = MultiHeadAttention(d, heads, True, init, dtype)
+        self.fc1 = Linear(d, mlp_ratio * d, True, init, dtype)
+        self.fc2 = Linear(mlp_ratio * d, d, True, init, dtype)
+
+    def init(self, key):
+        k1, k2, k3 = random.split(key, 3)
+        return {"norm1": self.norm1.init(), "attn": self.attn.init(k1), "norm2": self.norm2.init(), "fc1": self.fc1.init(k2), "fc2": self.fc2.init(k3)}
+
+    def __call__(self, p, x, mask=None, key=None):
+        # rg splits the block key even without dropout; the split is dead code the planner drops.
+        if key is not None:
+            k1, k2 = random.split(key)
+        x = x + self.attn(p["attn"], self.norm1(p["norm1"], x), mask)
+        h = self.fc2(p["fc2"], gelu(self.fc1(p["fc1"], self.norm2(p["norm2"], x))))
+        return x + h

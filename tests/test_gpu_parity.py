@@ -1,0 +1,281 @@
+"""CUDA device vs the CPU oracle on the same compiled plan (the plan blob crosses the C ABI).
+
+Tolerances: integer, index and RNG-bit outputs and every plan made of IEEE +,-,*,/ on small
+shapes are bit-exact; transcendental functions differ from glibc by a few ulp (CUDA's expf,
+tanhf...), so those outputs are compared at 1e-5 relative (max-norm); training-step losses and
+gradients at rg's north-star bound of 1e-4 relative (max-norm, rg's device-check metric).
+"""
+import numpy as np
+import pytest
+
+from rustautograd_b200 import frontend as F
+from helpers import assert_bits_equal, assert_parity, compile_and_compare, max_rel, np_of, triple
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _frontend(cuda):
+    F.use(cuda, "cuda")
+    yield
+
+
+def rnd(*shape, seed=0, dtype="float32", scale=1.0):
+    return F.tensor((np.random.default_rng(seed).normal(size=shape) * scale).astype(dtype))
+
+
+UNARY = [
+    ("neg", lambda x: -x, True),
+    ("abs", lambda x: abs(x), True),
+    ("sign", lambda x: F.op("sign", x), True),
+    ("floor", lambda x: F.floor(x * 3.0), True),
+    ("sqrt", lambda x: F.sqrt(abs(x)), True),
+    ("exp", lambda x: F.exp(x), False),
+    ("log", lambda x: F.log(abs(x) + 0.5), False),
+    ("sin", lambda x: F.op("sin", x), False),
+    ("cos", lambda x: F.op("cos", x), False),
+    ("tanh", lambda x: F.tanh(x), False),
+]
+
+
+@pytest.mark.parametrize("name,fn,exact", UNARY, ids=[u[0] for u in UNARY])
+@pytest.mark.parametrize("dtype", ["float32", "float64"])
+def test_unary(oracle, name, fn, exact, dtype):
+    x = rnd(1000, 37, seed=1, dtype=dtype)
+    assert_parity(oracle, fn, (x,), tol=1e-5 if dtype == "float32" else 1e-12, exact=exact)
+
+
+BINARY = [("add", lambda a, b: a + b), ("sub", lambda a, b: a - b), ("mul", lambda a, b: a * b), ("div", lambda a, b: a / b),
+          ("max", F.maximum), ("min", F.minimum), ("gt", lambda a, b: a > b), ("ge", lambda a, b: a >= b)]
+SHAPES = [((64, 33), (64, 33)), ((), (64, 33)), ((64, 33), ()), ((64, 33), (33,)), ((64, 1), (64, 33)), ((5, 1, 7), (1, 9, 7)), ((2, 3, 4, 5), (3, 1, 5))]
+
+
+@pytest.mark.parametrize("name,fn", BINARY, ids=[b[0] for b in BINARY])
+@pytest.mark.parametrize("sa,sb", SHAPES)
+def test_binary_broadcast_is_bit_exact(oracle, name, fn, sa, sb):
+    a, b = rnd(*sa, seed=2), rnd(*sb, seed=3)
+    assert_parity(oracle, fn, (a, b), exact=True)
+
+
+def test_pow_and_ieee_specials(oracle):
+    v = np.array([0.0, -0.0, 1.0, -1.0, 2.5, -2.0, np.inf, -np.inf, np.nan, 1e-30, 3e38, -7.0], dtype="float32")
+    x = F.tensor(v)
+    e = F.tensor(np.array([2.0, 3.0, 0.5, -1.0, 2.0, 3.0, 2.0, 3.0, 1.0, -2.0, 2.0, 2.0], dtype="float32"))
+    fns = lambda a, b: (a ** b, F.maximum(a, b), F.minimum(a, b), F.op("sign", a), a / b, F.exp(a), F.tanh(a), F.sqrt(a), F.floor(a))
+    gpu, cpu, _ = compile_and_compare(oracle, fns, (x, e))
+    for k, (g, w) in enumerate(zip(gpu, cpu)):
+        np.testing.assert_array_equal(np.isnan(g), np.isnan(w), err_msg=f"NaN pattern of output {k}")
+        m = ~np.isnan(w)
+        np.testing.assert_allclose(g[m], w[m], rtol=2e-6, err_msg=f"output {k}")
+
+
+def test_fused_chain_matches_and_forms_groups(oracle):
+    x, y = rnd(3, 4096, seed=4), rnd(4096, seed=5)
+    fn = lambda a, b: F.tanh(a * 0.7978845608 * (a + 0.044715 * a * a * a)) * b + F.exp(-abs(a)) / (1.0 + b * b)
+    gpu, cpu, c = assert_parity(oracle, fn, (x, y), tol=1e-5)
+    assert c.report["graph"]["fused_groups"] >= 1
+
+
+def test_where_and_int_arithmetic_wrap(oracle):
+    c = F.tensor((np.arange(24).reshape(4, 6) % 3 == 0).astype("float32"))
+    a, b = rnd(4, 6, seed=6), rnd(4, 6, seed=7)
+    assert_parity(oracle, lambda c, a, b: F.where(c, a, b), (c, a, b), exact=True)
+    i = F.tensor(np.array([2147483647, -2147483648, 5, -7, 123456789], dtype="int32"))
+    j = F.tensor(np.array([1, -1, 3, 9, 1000], dtype="int32"))
+    assert_parity(oracle, lambda p, q: (p + q, p - q, p * q, p > q, p >= q), (i, j), exact=True)
+
+
+@pytest.mark.parametrize("axes", [None, 0, 1, 2, (0, 1), (1, 2), (0, 2)])
+@pytest.mark.parametrize("kind", ["sum", "max", "min"])
+def test_reductions(oracle, axes, kind):
+    x = rnd(9, 130, 67, seed=8)
+    fn = lambda a: getattr(a, kind)(axis=axes, keepdims=False)
+    assert_parity(oracle, fn, (x,), tol=1e-5, exact=kind != "sum")
+
+
+def test_small_full_sum_is_bit_exact(oracle):
+    # rg's eight-lane fast_sum order, reproduced on the device for small tensors.
+    for n in [1, 7, 8, 9, 256, 1000, 4099]:
+        x = rnd(n, seed=n)
+        assert_parity(oracle, lambda a: a.sum(), (x,), exact=True)
+
+
+@pytest.mark.parametrize("perm", [(1, 0), (0, 2, 1), (2, 0, 1), (1, 0, 2), (2, 0, 3, 1)])
+def test_transpose(oracle, perm):
+    shape = (5, 7, 9, 11)[: len(perm)]
+    assert_parity(oracle, lambda a: a.transpose(perm) * 1.0, (rnd(*shape, seed=9),), exact=True)
+
+
+def test_structural_copies(oracle):
+    x = rnd(6, 10, 12, seed=10)
+    fn = lambda a: (a[1:5, ::2, 3:], F.op("broadcast_to", a[:, :1, :], shape=[6, 4, 12]), F.concatenate([a, a * 2.0], 1), a[2], a[:, 3, None])
+    assert_parity(oracle, fn, (x,), exact=True)
+
+
+def test_take_and_take_along_with_clamping(oracle):
+    table = rnd(11, 8, seed=11)
+    idx = F.tensor(np.array([[3, 0, 10], [12, -1, 5]], dtype="int32"))  # out of range clamps
+    along = F.tensor(np.array([[1], [0], [7], [2], [9], [3], [5], [4], [6], [0], [1]], dtype="int32"))
+    fn = lambda t, i, j: (F.take(t, i, 0), F.take(t, F.tensor(np.array([1, 7], dtype="int32")), 1), F.take_along_axis(t, j))
+    assert_parity(oracle, fn, (table, idx, along), exact=True)
+
+
+def test_scatter_add_gradients_are_bit_exact(oracle):
+    # TakeGrad / TakeAlongGrad: every destination adds its contributions in index order from zero.
+    table = rnd(17, 64, seed=12)
+    idx = F.tensor(np.random.default_rng(13).integers(0, 17, size=(300,), dtype="int32"))
+    lab = F.tensor(np.random.default_rng(14).integers(0, 64, size=(17, 3), dtype="int32"))
+
+    def loss(t, i, l):
+        e = F.take(t, i, 0)
+        return (e * e * F.tensor(np.linspace(0.5, 2.0, 64).astype("float32"))).sum() + F.take_along_axis(t, l).sum()
+    fn = lambda t, i, l: F.value_and_grad(loss)(t, i, l)
+    assert_parity(oracle, fn, (table, idx, lab), tol=1e-6)
+    # The gradient alone (no full-sum of the loss in the way) must be bit-identical.
+    g = lambda t, i, l: F.value_and_grad(loss)(t, i, l)[1]
+    assert_parity(oracle, g, (table, idx, lab), exact=True)
+
+
+@pytest.mark.parametrize("sa,sb,kw", [
+    ((37, 19), (19, 23), {}),
+    ((4, 37, 19), (19, 23), {}),
+    ((4, 37, 19), (4, 19, 23), {}),
+    ((3, 1, 7, 5), (1, 2, 5, 6), {}),
+    ((19,), (19, 23), {}),
+    ((37, 19), (19,), {}),
+    ((19, 37), (19, 23), {"ta": True}),
+    ((37, 19), (23, 19), {"tb": True}),
+])
+def test_matmul_small_is_bit_exact(oracle, sa, sb, kw):
+    a, b = rnd(*sa, seed=15), rnd(*sb, seed=16)
+
+    def fn(x, y):
+        if kw.get("ta"):
+            x = F.swapaxes(x, -1, -2)
+        if kw.get("tb"):
+            y = F.swapaxes(y, -1, -2)
+        return x @ y
+    assert_parity(oracle, fn, (a, b), exact=True)
+
+
+def test_matmul_large_within_tolerance(oracle):
+    a, b = rnd(512, 384, seed=17), rnd(384, 640, seed=18)
+    assert_parity(oracle, lambda x, y: (x @ y, F.swapaxes(x, 0, 1) @ (x @ y)), (a, b), tol=1e-5)
+
+
+def test_random_streams_are_bit_exact(oracle):
+    key = F.tensor(np.array([7, 11], dtype="int32"))
+    fn = lambda k: (F.op("key_split", k, n=5), F.op("random_uniform", k, shape=[1000, 3], dtype="float32"),
+                    F.op("random_uniform", k, shape=[999], dtype="float64"), F.random.randint(k, (513,), 0, 97))
+    assert_parity(oracle, fn, (key,), exact=True)
+    gpu, cpu, _ = compile_and_compare(oracle, lambda k: (F.op("random_normal", k, shape=[4096], dtype="float64"),
+                                                          F.op("random_normal", k, shape=[4096], dtype="float32")), (key,))
+    assert max_rel(gpu[0], cpu[0]) < 1e-14
+    assert max_rel(gpu[1], cpu[1]) < 1e-6
+
+
+def test_casts_saturate_like_rust(oracle):
+    v = np.array([0.5, -0.5, 2.9, -2.9, 3e9, -3e9, np.nan, np.inf, -np.inf, 1e20], dtype="float64")
+    x = F.tensor(v)
+    fn = lambda a: (a.cast("int32"), a.cast("float32"), a.cast("float32").cast("int32"), a.cast("int32").cast("float64"))
+    assert_parity(oracle, fn, (x,), exact=True)
+
+
+def test_selection_ops(oracle):
+    x = F.tensor(np.array([[1.0, 3.0, 3.0, -1.0, np.nan, 2.0], [np.nan, 5.0, 1.0, 5.0, 0.0, -2.0], [0.0, -0.0, 0.0, 1.0, 1.0, 1.0]], dtype="float32"))
+    fn = lambda a: (F.op("argmax", a), F.op("arg_top_k", a, k=4), F.op("cumsum", a * 1.0, reverse=False), F.op("cumsum", a * 1.0, reverse=True))
+    gpu, cpu, _ = compile_and_compare(oracle, fn, (x,))
+    for k in range(2):
+        assert_bits_equal(gpu[k], cpu[k], f"output {k}")
+    for k in range(2, 4):
+        np.testing.assert_array_equal(np.isnan(gpu[k]), np.isnan(cpu[k]))
+
+
+def linear_regression():
+    x = np.random.default_rng(0).normal(size=(256, 8)).astype("float32")
+    y = x @ np.arange(8, dtype="float32")
+
+    def loss(w, batch):
+        return (((batch[0] @ w) - batch[1]) ** 2).mean()
+
+    def step(w, batch):
+        value, g = F.value_and_grad(loss)(w, batch)
+        return w - 0.05 * g, value
+    return step, x, y
+
+
+def test_linear_regression_run_is_bit_identical_to_the_oracle(oracle):
+    """500 steps, history and final weights bit-for-bit equal to rg's CPU."""
+    step, x, y = linear_regression()
+    w0 = F.zeros(8)
+    c = F.compile(step, (w0, (F.tensor(x), F.tensor(y))), validate="basic", device="cuda")
+    r = F.run(c, w0, (F.tensor(x), F.tensor(y)), steps=500)
+    assert r.status == "completed" and r.steps == 500
+    assert r.history["aux"][-1] < 1e-3
+    blob = c.plan_blob()
+    ins = [triple(F.zeros(8)), triple(F.tensor(x)), triple(F.tensor(y))]
+    st, hist, steps, _ = oracle.run_plan_blob_steps(blob, [(0, 0)], [1, 2], [1], ins, 500)
+    assert steps == 500
+    np.testing.assert_array_equal(np.array(r.history["aux"]), np.array(hist[0]))
+    assert_bits_equal(r.state.numpy(), np_of(st[0]), "final weights")
+
+
+def test_run_stops_at_the_first_nonfinite_step_like_rg(oracle):
+    step, x, y = linear_regression()
+
+    def divergent(w, batch):
+        value, g = F.value_and_grad(lambda w, b: (((b[0] @ w) - b[1]) ** 2).mean())(w, batch)
+        return w - 40.0 * g, value
+    w0 = F.zeros(8)
+    c = F.compile(divergent, (w0, (F.tensor(x), F.tensor(y))), validate="none", device="cuda")
+    r = F.run(c, w0, (F.tensor(x), F.tensor(y)), steps=1000)
+    ins = [triple(F.zeros(8)), triple(F.tensor(x)), triple(F.tensor(y))]
+    st, hist, steps, _ = oracle.run_plan_blob_steps(c.plan_blob(), [(0, 0)], [1, 2], [1], ins, 1000)
+    assert r.status == "stopped_nonfinite"
+    assert r.steps == steps and r.nonfinite_step == steps - 1
+    np.testing.assert_array_equal(np.array(r.history["aux"]), np.array(hist[0]))
+    assert_bits_equal(r.state.numpy(), np_of(st[0]), "state at the stop")
+
+
+def small_gpt(batch=8, block=16, d=32, heads=4, layers=2, vocab=40, dtype="float32"):
+    model = F.gpt.GPT(vocab=vocab, block=block, d=d, heads=heads, layers=layers)
+    params = model.init(F.random.key(0))
+    if dtype != "float32":
+        params = F.tree_map(lambda v: v.cast(dtype), params)
+    opt = F.optim.adamw(1e-3, weight_decay=0.01)
+    state = {"params": params, "opt": opt.init(params), "key": F.random.key(1)}
+    tokens = F.tensor(np.random.default_rng(0).integers(0, vocab, size=4000, dtype="int32"))
+    return model, opt, state, tokens
+
+
+def test_gpt_train_step_matches_the_oracle(oracle):
+    model, opt, state, tokens = small_gpt()
+    step = F.gpt.make_train_step(model, opt, 8)
+    gpu, cpu, c = assert_parity(oracle, step, (state, tokens), tol=1e-4)
+    assert c.report["graph"]["fused_groups"] > 10
+
+
+def test_gpt_loss_and_gradients_in_float64(oracle):
+    model, opt, state, tokens = small_gpt(dtype="float64")
+    x = F.tensor(np.random.default_rng(1).integers(0, 40, size=(4, 16), dtype="int32"))
+
+    def fn(p, x):
+        return F.value_and_grad(lambda p, x: F.nn.cross_entropy(model(p, x), x))(p, x)
+    assert_parity(oracle, fn, (state["params"], x), tol=1e-10)
+
+
+def test_gpt_training_run_tracks_the_oracle(oracle):
+    model, opt, state, tokens = small_gpt()
+    step = F.gpt.make_train_step(model, opt, 8)
+    c = F.compile(step, (state, tokens), validate="none", device="cuda")
+    r = F.run(c, state, tokens, steps=30)
+    assert r.status == "completed"
+    leaves = F.flatten((state, tokens))[0]
+    n_state = len(leaves) - 1
+    st, hist, steps, _ = oracle.run_plan_blob_steps(c.plan_blob(), [(k, k) for k in range(n_state)], [n_state], [n_state],
+                                                     [triple(F.tensor(l)) for l in leaves], 30)
+    assert steps == 30
+    # AdamW amplifies ulp differences over many steps; the loss trajectory stays within 1e-4.
+    h_gpu, h_cpu = np.array(r.history["aux"]), np.array(hist[0])
+    assert np.max(np.abs(h_gpu - h_cpu) / np.abs(h_cpu)) < 1e-4
+    assert h_gpu[-1] < h_gpu[0]
