@@ -21,6 +21,7 @@
 
 #include "blob.h"
 #include "dist.h"
+#include "gemm_tc.cuh"
 #include "jit.h"
 #include "kernels.cuh"
 #include "rgc.h"
@@ -58,6 +59,14 @@ long long exact_gemm_limit() {
     return (long long)1 << 24;
   }();
   return v;
+}
+
+bool tc_disabled() {
+  static bool off = [] {
+    const char* e = getenv("RGC_NO_TC");
+    return e && std::string(e) == "1";
+  }();
+  return off;
 }
 
 Jit& jit() {
@@ -113,6 +122,7 @@ struct Program {
   bool capturable = true;
   std::vector<std::unique_ptr<Program>> subs;
   Dims* bc_dev = nullptr;  // broadcast descriptors of the fused kernels
+  int* tc_error = nullptr;  // set by a tensor-core GEMM whose pipeline wait gave up
   std::mutex mu;
   std::vector<std::unique_ptr<Frame>> pool;
   std::atomic<bool> inject{false};
@@ -122,6 +132,7 @@ struct Program {
   ~Program() {
     pool.clear();
     if (bc_dev) cudaFree(bc_dev);
+    if (tc_error) cudaFree(tc_error);
   }
 };
 
@@ -425,6 +436,44 @@ struct Builder {
     EType t = et(i.dtype);
     bool exact = m * n * kk * count <= exact_gemm_limit();
     size_t dst = i.dst, A = i.args[0], B = i.args[1];
+    // Large fp32 products run on the tensor cores (3xTF32) when their batch folds into one
+    // strided dimension; small ones keep rg's exact loop arithmetic on the SIMT cores.
+    TcGemm tg;
+    tg.m = m;
+    tg.n = n;
+    tg.k = kk;
+    tg.ta = ta;
+    tg.tb = tb;
+    bool foldable = true;
+    if (bt.rank == 0) {
+      tg.batch = 1;
+    } else {
+      // Fold adjacent batch dims whose strides chain for both operands.
+      long long d = bt.d[bt.rank - 1], sa_ = bt.sa[bt.rank - 1], sb_ = bt.sb[bt.rank - 1];
+      for (int q = bt.rank - 2; q >= 0 && foldable; --q) {
+        bool chain_a = bt.sa[q] == sa_ * d || (bt.sa[q] == 0 && sa_ == 0);
+        bool chain_b = bt.sb[q] == sb_ * d || (bt.sb[q] == 0 && sb_ == 0);
+        foldable = chain_a && chain_b;
+        d *= bt.d[q];
+      }
+      tg.batch = count;
+      tg.batch_a = sa_;
+      tg.batch_b = sb_;
+    }
+    bool use_tc = !tc_disabled() && t == EType::F32 && !exact && foldable && tc_gemm_supported(tg);
+    if (use_tc) {
+      tc_gemm_init();
+      scratch = std::max(scratch, tc_gemm_scratch_bytes(tg));
+      l.kernels = 3;  // two operand splits and the product
+      l.run = [=](Ctx& c) {
+        TcGemm g = tg;
+        g.a = (const float*)c.f->ptr[A];
+        g.b = (const float*)c.f->ptr[B];
+        g.c = (float*)c.f->ptr[dst];
+        tc_gemm(g, c.f->scratch, c.f->prog->tc_error, c.s);
+      };
+      return l;
+    }
     l.run = [=](Ctx& c) { gemm(c.f->ptr[dst], c.f->ptr[A], c.f->ptr[B], t, m, n, kk, ta, tb, bt, count, exact, c.s); };
     return l;
   }
@@ -672,6 +721,8 @@ std::unique_ptr<Program> make_program(const Plan& plan, int device) {
   auto p = std::make_unique<Program>();
   p->device = device;
   p->plan = plan;
+  ck(cudaMalloc((void**)&p->tc_error, sizeof(int)), "cudaMalloc(error flag)");
+  ck(cudaMemset(p->tc_error, 0, sizeof(int)), "cudaMemset(error flag)");
   p->offsets.resize(plan.slots.size());
   size_t off = 0;
   for (size_t s = 0; s < plan.slots.size(); ++s) {
@@ -798,6 +849,13 @@ void launch_plan(rgc_exec* e) {
   Ctx c{e->f->stream, e->f.get()};
   run_steps(p, c);
   p->launches += (uint64_t)p->kernels_per_step;
+}
+
+// A tensor-core GEMM whose pipeline wait gave up leaves a code in the program's error flag.
+void check_tc_error(rgc_exec* e) {
+  int code = 0;
+  if (cudaMemcpy(&code, e->owner->p->tc_error, sizeof code, cudaMemcpyDeviceToHost) == cudaSuccess && code)
+    mark_failed(e, "tensor-core GEMM pipeline wait timed out (stage " + std::to_string(code) + ")");
 }
 
 void check_async(rgc_exec* e) {
@@ -1012,6 +1070,7 @@ __attribute__((visibility("default"))) int rgc_exec_failure(rgc_exec* e, char* b
     if (err == cudaSuccess) err = cudaGetLastError();
     if (err != cudaSuccess) mark_failed(e, std::string("device error: ") + cudaGetErrorString(err));
   }
+  if (!e->f->failed) check_tc_error(e);
   if (!e->f->failed) return 0;
   if (buf && cap) {
     std::strncpy(buf, e->f->error.c_str(), cap - 1);
@@ -1273,6 +1332,7 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
     }
     // The frame keeps the layout after the last step's swaps: the state is in the input slots.
     f->ptr = layout[L];
+    if (!f->failed) check_tc_error(e);
     if (f->failed) return fail(RGC_ERR_DEVICE, f->error);
     return RGC_OK;
   });
