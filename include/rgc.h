@@ -110,6 +110,20 @@ int rgc_exec_breakdown_json(rgc_exec* e, size_t repeats, char* buf, size_t cap);
 /* Kernel launches issued since the program was created (all execs), for accounting. */
 uint64_t rgc_program_launches(const rgc_program* p);
 
+/* Sum of the `n` elements of the device array `src` (dtype 0 = float32, 1 = float64) into the
+ * one-element device array `dst`, enqueued on `stream` (a cudaStream_t; NULL = the legacy default
+ * stream). Same kernels and summation order as a plan's full-tensor Sum, so the result is
+ * bit-identical to it. No counterpart in the reference: it exists for callers that may not
+ * allocate device memory when they need the sum (an allocator's own callbacks or out-of-memory
+ * handler, a host whose memory pool owns the whole device heap, a loop where cudaMalloc's
+ * implicit synchronisation is not allowed). It allocates nothing: the partial sums go to a fixed
+ * 256 KiB array in the library (held on every GPU that loads it until exit), which limits n to
+ * 2^29 float32 or 2^28 float64 elements; larger n fails with RGC_ERR_INVALID before any launch.
+ * The array needs no clearing between calls, but all calls on a device share it, so calls that
+ * may overlap on the GPU race. The first call on a device does set-up (looks up the array's
+ * address, loads the kernels): make it before beginning any stream capture. */
+int rgc_sum_noalloc(const void* src, int64_t n, int dtype, void* dst, void* stream);
+
 /* Data parallelism: one process per GPU; rank 0 creates the id, every rank joins. */
 int rgc_dist_unique_id(uint8_t id[128]);
 int rgc_dist_init(int rank, int world, const uint8_t id[128]);

@@ -883,6 +883,15 @@ cudaGraphExec_t capture(cudaStream_t s, const std::function<void(cudaStream_t)>&
 
 }  // namespace
 
+// For entry points defined in other files of this library: sets (or, with an empty message,
+// clears) what rgc_last_error reports on this thread, and returns `code`.
+namespace rgc {
+int set_last_error(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+}  // namespace rgc
+
 extern "C" {
 
 __attribute__((visibility("default"))) int rgc_available(void) {
