@@ -219,15 +219,15 @@ def main():
     state_bytes = sum(len(x.tobytes()) for x in state_leaves)
     data_bytes = len(tokens._t.tobytes())
 
+    # Roofline of the dominant kernel class: per-step device times (CUDA events between plan
+    # steps on the device's stream) over the same compiled plan and inputs. Every rank runs it:
+    # the plan's all-reduce steps are collectives.
+    secs = compiled._n.step_seconds(state_leaves + data, 2)
     out = None
     if rank == 0:
         value = done / device_s
         flops = train_flops(cfg, cfg["batch"]) / world
         pk = peaks()
-        # Roofline of the dominant kernel class: per-step device times (CUDA events between
-        # plan steps on the device's stream) over the same compiled plan and inputs.
-        inputs = state_leaves + data
-        secs = compiled._n.step_seconds(inputs, 2)
         costs = compiled._n.step_costs()
         by_kind = {}
         for (kind, fl, by), s in zip(costs, secs):

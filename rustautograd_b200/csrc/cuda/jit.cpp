@@ -42,11 +42,58 @@ namespace {
 
 const char* PRELUDE = R"(
 struct Dims { int rank; long long d[8]; long long st[8]; };
-struct ElemArgs { long long n; int vec; int pad; void* out[64]; const void* in[64]; long long row[64]; const Dims* bc; };
+struct FDiv { unsigned d, m, s; };
+struct FDims { int rank; FDiv d[8]; long long st[8]; };
+struct ElemArgs { long long n; int vec; int small; void* out[64]; const void* in[64]; FDiv row[64]; const FDims* bc; const Dims* bc64; };
+__device__ __forceinline__ unsigned rg_fdiv(unsigned n, const FDiv& f) { return (__umulhi(n, f.m) + n) >> f.s; }
 __device__ __forceinline__ long long bc_off(const Dims& b, long long e) {
   long long off = 0;
   for (int d = b.rank - 1; d >= 0; --d) { long long c = e % b.d[d]; e /= b.d[d]; off += c * b.st[d]; }
   return off;
+}
+// Offset of element e under a merged broadcast descriptor; *inner receives e's innermost coordinate.
+__device__ __forceinline__ long long rg_bc_off(const FDims& b, unsigned e, unsigned* inner) {
+  long long off = 0;
+  *inner = 0;
+  for (int d = b.rank - 1; d >= 0; --d) {
+    unsigned q = rg_fdiv(e, b.d[d]);
+    unsigned c = e - q * b.d[d].d;
+    if (d == b.rank - 1) *inner = c;
+    off += (long long)c * b.st[d];
+    e = q;
+  }
+  return off;
+}
+// V consecutive elements of a broadcast input: one offset computation when they share the
+// innermost run, else one per element.
+template <typename T, int V> __device__ __forceinline__ void rg_bc_fill(T* r, const T* p, const FDims& b, unsigned e) {
+  unsigned c;
+  long long off = rg_bc_off(b, e, &c);
+  if (b.rank == 0) {
+    #pragma unroll
+    for (int j = 0; j < V; ++j) r[j] = p[0];
+    return;
+  }
+  const unsigned inner = b.d[b.rank - 1].d;
+  const long long st = b.st[b.rank - 1];
+  if (c + V <= inner) {
+    #pragma unroll
+    for (int j = 0; j < V; ++j) r[j] = p[off + j * st];
+  } else {
+    #pragma unroll
+    for (int j = 0; j < V; ++j) { unsigned cj; r[j] = p[rg_bc_off(b, e + j, &cj)]; }
+  }
+}
+// V consecutive elements of a row input (the input repeats every f.d elements).
+template <typename T, int V> __device__ __forceinline__ void rg_row_fill(T* r, const T* p, unsigned e, const FDiv& f) {
+  if (f.d >= V) {
+    unsigned c = e - rg_fdiv(e, f) * f.d;
+    #pragma unroll
+    for (int j = 0; j < V; ++j) { unsigned i = c + j; i = i >= f.d ? i - f.d : i; r[j] = p[i]; }
+  } else {
+    #pragma unroll
+    for (int j = 0; j < V; ++j) { unsigned ej = e + j; r[j] = p[ej - rg_fdiv(ej, f) * f.d]; }
+  }
 }
 __device__ __forceinline__ float rg_nan(float) { return __int_as_float(0x7fc00000); }
 __device__ __forceinline__ double rg_nan(double) { return __longlong_as_double(0x7ff8000000000000LL); }
@@ -175,7 +222,7 @@ ElemSpec spec_from_instr(const rg::Instr& i) {
 static std::string kernel_source(const ElemSpec& s, const std::string& name) {
   std::ostringstream o;
   std::string T = ctype(s.dtype), VT = vtype(s.dtype);
-  int VW = vwidth(s.dtype);
+  const int VW = vwidth(s.dtype);
   // Map: non-full input k -> register; compile_group assigns registers in input order.
   std::vector<long> in_reg(s.inputs.size(), -1);
   {
@@ -183,58 +230,97 @@ static std::string kernel_source(const ElemSpec& s, const std::string& name) {
     for (size_t k = 0; k < s.inputs.size(); ++k)
       if (s.inputs[k].kind != ArgKind::Full) in_reg[k] = (long)r++;
   }
-  o << "extern \"C\" __global__ void __launch_bounds__(256) " << name << "(const ElemArgs a) {\n";
-  o << "  const long long n = a.n;\n";
-  o << "  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x, stride = (long long)gridDim.x * blockDim.x;\n";
-  for (size_t k = 0; k < s.inputs.size(); ++k)
-    if (s.inputs[k].kind == ArgKind::Splat) o << "  const " << T << " sp" << k << " = ((const " << T << "*)a.in[" << k << "])[0];\n";
-  auto emit = [&](int V, bool vec) {
-    const char* e0 = "e0";
-    for (size_t k = 0; k < s.inputs.size(); ++k) {
-      const auto& in = s.inputs[k];
-      if (in.kind == ArgKind::Full) {
-        o << "    " << T << " i" << k << "[" << V << "];\n";
-        if (!vec) {
-          o << "    i" << k << "[0] = ((const " << T << "*)a.in[" << k << "])[" << e0 << "];\n";
-        } else {
-          o << "    { " << VT << " v = ((const " << VT << "*)a.in[" << k << "])[" << e0 << " / " << V << "];";
-          for (int j = 0; j < V; ++j) o << " i" << k << "[" << j << "] = v." << lane(j) << ";";
-          o << " }\n";
-        }
-      } else {
-        long r = in_reg[k];
-        o << "    " << T << " r" << r << "[" << V << "];\n";
-        o << "    #pragma unroll\n    for (int j = 0; j < " << V << "; ++j) ";
-        if (in.kind == ArgKind::Splat) o << "r" << r << "[j] = sp" << k << ";\n";
-        else if (in.kind == ArgKind::Row) o << "r" << r << "[j] = ((const " << T << "*)a.in[" << k << "])[(" << e0 << " + j) % a.row[" << k << "]];\n";
-        else o << "r" << r << "[j] = ((const " << T << "*)a.in[" << k << "])[bc_off(a.bc[" << in.bc << "], " << e0 << " + j)];\n";
-      }
-    }
+  auto in_ptr = [&](size_t k) { return "((const " + T + "*)a.in[" + std::to_string(k) + "])"; };
+  // The micro-ops over G lanes, then the outputs.
+  auto ops = [&](int G) {
     for (auto& m : s.ops) {
-      o << "    " << T << " r" << m.reg << "[" << V << "];\n";
-      o << "    #pragma unroll\n    for (int j = 0; j < " << V << "; ++j) r" << m.reg << "[j] = ";
+      o << "      " << T << " r" << m.reg << "[" << G << "];\n";
+      o << "      #pragma unroll\n      for (int j = 0; j < " << G << "; ++j) r" << m.reg << "[j] = ";
       std::vector<std::string> args;
-      for (auto& a : m.args) args.push_back((a.reg ? "r" : "i") + std::to_string(a.idx) + "[j]");
+      for (auto& x : m.args) args.push_back((x.reg ? "r" : "i") + std::to_string(x.idx) + "[j]");
       o << expr(s.dtype, m.op, args) << ";\n";
     }
-    for (size_t q = 0; q < s.out_regs.size(); ++q) {
-      size_t r = s.out_regs[q];
-      if (!vec) {
-        o << "    ((" << T << "*)a.out[" << q << "])[" << e0 << "] = r" << r << "[0];\n";
+  };
+  o << "extern \"C\" __global__ void __launch_bounds__(256) " << name << "(const ElemArgs a) {\n";
+  for (size_t k = 0; k < s.inputs.size(); ++k)
+    if (s.inputs[k].kind == ArgKind::Splat) o << "  const " << T << " sp" << k << " = " << in_ptr(k) << "[0];\n";
+  o << "  if (a.small) {\n";
+  o << "    const unsigned n = (unsigned)a.n, tid = blockIdx.x * blockDim.x + threadIdx.x, stride = gridDim.x * blockDim.x;\n";
+  // Vector path: two 16-byte vectors per thread per iteration (all loads before any store).
+  o << "    if (a.vec) {\n";
+  o << "     const unsigned nv = n / " << VW << ";\n";
+  o << "     for (unsigned q = tid; q < nv; q += 2u * stride) {\n";
+  o << "      const unsigned q1 = q + stride;\n      const bool h1 = q1 < nv;\n";
+  o << "      const unsigned ea = q * " << VW << ", eb = (h1 ? q1 : q) * " << VW << ";\n";
+  const int G = 2 * VW;
+  for (size_t k = 0; k < s.inputs.size(); ++k) {
+    const auto& in = s.inputs[k];
+    if (in.kind == ArgKind::Full) {
+      o << "      " << T << " i" << k << "[" << G << "];\n";
+      o << "      { const " << VT << " va = ((const " << VT << "*)a.in[" << k << "])[q], vb = ((const " << VT << "*)a.in[" << k
+        << "])[h1 ? q1 : q];";
+      for (int j = 0; j < VW; ++j) o << " i" << k << "[" << j << "] = va." << lane(j) << ";";
+      for (int j = 0; j < VW; ++j) o << " i" << k << "[" << VW + j << "] = vb." << lane(j) << ";";
+      o << " }\n";
+    } else {
+      long r = in_reg[k];
+      o << "      " << T << " r" << r << "[" << G << "];\n";
+      if (in.kind == ArgKind::Splat) {
+        o << "      #pragma unroll\n      for (int j = 0; j < " << G << "; ++j) r" << r << "[j] = sp" << k << ";\n";
+      } else if (in.kind == ArgKind::Row) {
+        o << "      rg_row_fill<" << T << ", " << VW << ">(r" << r << ", " << in_ptr(k) << ", ea, a.row[" << k << "]);\n";
+        o << "      rg_row_fill<" << T << ", " << VW << ">(r" << r << " + " << VW << ", " << in_ptr(k) << ", eb, a.row[" << k << "]);\n";
       } else {
-        o << "    { " << VT << " v;";
-        for (int j = 0; j < V; ++j) o << " v." << lane(j) << " = r" << r << "[" << j << "];";
-        o << " ((" << VT << "*)a.out[" << q << "])[" << e0 << " / " << V << "] = v; }\n";
+        o << "      rg_bc_fill<" << T << ", " << VW << ">(r" << r << ", " << in_ptr(k) << ", a.bc[" << in.bc << "], ea);\n";
+        o << "      rg_bc_fill<" << T << ", " << VW << ">(r" << r << " + " << VW << ", " << in_ptr(k) << ", a.bc[" << in.bc << "], eb);\n";
       }
     }
-  };
-  o << "  if (a.vec) {\n";
-  o << "    const long long nv = n / " << VW << ";\n";
-  o << "    for (long long q = tid; q < nv; q += stride) {\n    const long long e0 = q * " << VW << ";\n";
-  emit(VW, true);
-  o << "    }\n  } else {\n";
-  o << "    for (long long e0 = tid; e0 < n; e0 += stride) {\n";
-  emit(1, false);
+  }
+  ops(G);
+  for (size_t q = 0; q < s.out_regs.size(); ++q) {
+    size_t r = s.out_regs[q];
+    o << "      { " << VT << " va, vb;";
+    for (int j = 0; j < VW; ++j) o << " va." << lane(j) << " = r" << r << "[" << j << "];";
+    for (int j = 0; j < VW; ++j) o << " vb." << lane(j) << " = r" << r << "[" << VW + j << "];";
+    o << " ((" << VT << "*)a.out[" << q << "])[q] = va; if (h1) ((" << VT << "*)a.out[" << q << "])[q1] = vb; }\n";
+  }
+  o << "     }\n";
+  o << "    } else {\n";
+  // Scalar path with 32-bit index math.
+  o << "     for (unsigned e = tid; e < n; e += stride) {\n";
+  for (size_t k = 0; k < s.inputs.size(); ++k) {
+    const auto& in = s.inputs[k];
+    if (in.kind == ArgKind::Full) {
+      o << "      " << T << " i" << k << "[1] = {" << in_ptr(k) << "[e]};\n";
+    } else {
+      long r = in_reg[k];
+      o << "      " << T << " r" << r << "[1];\n";
+      if (in.kind == ArgKind::Splat) o << "      r" << r << "[0] = sp" << k << ";\n";
+      else if (in.kind == ArgKind::Row) o << "      r" << r << "[0] = " << in_ptr(k) << "[e - rg_fdiv(e, a.row[" << k << "]) * a.row[" << k << "].d];\n";
+      else o << "      { unsigned c; r" << r << "[0] = " << in_ptr(k) << "[rg_bc_off(a.bc[" << in.bc << "], e, &c)]; }\n";
+    }
+  }
+  ops(1);
+  for (size_t q = 0; q < s.out_regs.size(); ++q) o << "      ((" << T << "*)a.out[" << q << "])[e] = r" << s.out_regs[q] << "[0];\n";
+  o << "     }\n    }\n";
+  // 64-bit path for 2^31 elements or more.
+  o << "  } else {\n";
+  o << "    const long long n = a.n, tid = (long long)blockIdx.x * blockDim.x + threadIdx.x, stride = (long long)gridDim.x * blockDim.x;\n";
+  o << "    for (long long e = tid; e < n; e += stride) {\n";
+  for (size_t k = 0; k < s.inputs.size(); ++k) {
+    const auto& in = s.inputs[k];
+    if (in.kind == ArgKind::Full) {
+      o << "      " << T << " i" << k << "[1] = {" << in_ptr(k) << "[e]};\n";
+    } else {
+      long r = in_reg[k];
+      o << "      " << T << " r" << r << "[1];\n";
+      if (in.kind == ArgKind::Splat) o << "      r" << r << "[0] = sp" << k << ";\n";
+      else if (in.kind == ArgKind::Row) o << "      r" << r << "[0] = " << in_ptr(k) << "[e % (long long)a.row[" << k << "].d];\n";
+      else o << "      r" << r << "[0] = " << in_ptr(k) << "[bc_off(a.bc64[" << in.bc << "], e)];\n";
+    }
+  }
+  ops(1);
+  for (size_t q = 0; q < s.out_regs.size(); ++q) o << "      ((" << T << "*)a.out[" << q << "])[e] = r" << s.out_regs[q] << "[0];\n";
   o << "    }\n  }\n}\n";
   return o.str();
 }
@@ -273,7 +359,7 @@ void Jit::build() {
   }
   const char* opts[] = {"--gpu-architecture=sm_100a", "--fmad=false", "--prec-div=true", "--prec-sqrt=true", "--ftz=false", "-default-device",
                         "--std=c++17"};
-  std::string path = cache_dir() + "/" + std::to_string(fnv1a(src + "v1")) + ".cubin";
+  std::string path = cache_dir() + "/" + std::to_string(fnv1a(src + "v2")) + ".cubin";
   std::vector<char> cubin;
   {
     std::ifstream f(path, std::ios::binary);
@@ -328,7 +414,7 @@ void Jit::launch(CUfunction f, const ElemArgs& a, long long n, int vec_width, cu
     cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
     return v;
   }();
-  long long work = a.vec ? n / vec_width : n;
+  long long work = a.vec ? (n / vec_width + 1) / 2 : n;
   long long blocks = (work + 255) / 256;
   long long cap = (long long)sms * 8;
   if (blocks > cap) blocks = cap;

@@ -25,12 +25,13 @@ constexpr int JIT_MAX_OUT = 64;
 // Must match the struct emitted into every generated kernel.
 struct ElemArgs {
   long long n;
-  int vec;  // 1: full operands are 16-byte aligned and n is a multiple of the vector width
-  int pad;
+  int vec;    // 1: full operands are 16-byte aligned and n is a multiple of the vector width
+  int small;  // 1: n < 2^31 and every merged broadcast extent fits, so index math is 32-bit
   void* out[JIT_MAX_OUT];
   const void* in[JIT_MAX_IN];
-  long long row[JIT_MAX_IN];
-  const Dims* bc;  // device array: one descriptor per broadcast input
+  FDiv row[JIT_MAX_IN];  // row length of each row input
+  const FDims* bc;       // device array: one merged descriptor per broadcast input
+  const Dims* bc64;      // device array: the same descriptors unmerged, for the 64-bit path
 };
 
 // A generated elementwise kernel: the structure (which decides the source) plus which argument

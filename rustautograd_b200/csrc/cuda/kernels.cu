@@ -86,6 +86,41 @@ template <typename T> __global__ void k_scatter(T* __restrict__ dst, const T* __
   }
 }
 
+__device__ __forceinline__ unsigned fdiv(unsigned n, const FDiv& f) { return (__umulhi(n, f.m) + n) >> f.s; }
+
+// Offset of element e (row-major over the extents of `s`) under the strides of `s`.
+__device__ __forceinline__ long long fd_off(const FDims& s, unsigned e) {
+  long long off = 0;
+  for (int d = s.rank - 1; d >= 0; --d) {
+    unsigned q = fdiv(e, s.d[d]);
+    off += (long long)(e - q * s.d[d].d) * s.st[d];
+    e = q;
+  }
+  return off;
+}
+
+template <typename T> __global__ void k_gather32(T* __restrict__ dst, const T* __restrict__ src, FDims s, long long base, unsigned n) {
+  for (unsigned e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) dst[e] = src[base + fd_off(s, e)];
+}
+
+template <typename T> __global__ void k_scatter32(T* __restrict__ dst, const T* __restrict__ src, FDims s, long long base, unsigned n) {
+  for (unsigned e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) dst[base + fd_off(s, e)] = src[e];
+}
+
+// 16-byte vectors: the innermost extent is contiguous on both sides and every offset is a
+// multiple of the vector width V, so V consecutive elements move as one load and one store.
+template <typename VT, int V>
+__global__ void k_gather_vec(VT* __restrict__ dst, const VT* __restrict__ src, FDims s, long long base, unsigned nv) {
+  for (unsigned q = blockIdx.x * blockDim.x + threadIdx.x; q < nv; q += gridDim.x * blockDim.x)
+    dst[q] = src[(base + fd_off(s, q * V)) / V];
+}
+
+template <typename VT, int V>
+__global__ void k_scatter_vec(VT* __restrict__ dst, const VT* __restrict__ src, FDims s, long long base, unsigned nv) {
+  for (unsigned q = blockIdx.x * blockDim.x + threadIdx.x; q < nv; q += gridDim.x * blockDim.x)
+    dst[(base + fd_off(s, q * V)) / V] = src[q];
+}
+
 // 32x32 tiles through shared memory; the +1 column avoids bank conflicts.
 template <typename T> __global__ void k_transpose2(T* __restrict__ dst, const T* __restrict__ src, long long rows, long long cols) {
   __shared__ T tile[32][33];
@@ -183,6 +218,137 @@ __global__ void k_take_grad(T* __restrict__ dst, const T* __restrict__ ct, const
       if (col < block) out[col] = acc[c];
     }
   }
+}
+
+// ---- take_grad through per-row hit lists (a stable counting sort of the positions by row) ----
+// Positions are cut into chunks of TG_CHUNK; cnt[r * chunks + c] counts chunk c's positions that
+// land in row r. An exclusive scan of that matrix in row-major order gives where each (row,
+// chunk) run starts in the list, so placing every chunk's positions in order sorts them by row
+// and keeps ascending position order within a row.
+constexpr int TG_CHUNK = 1024;
+
+__global__ void k_tg_count(int* __restrict__ cnt, const int32_t* __restrict__ idx, long long dim, long long n_idx, long long chunks) {
+  GRID_STRIDE(j, n_idx) {
+    long long r = clamp_index(idx[j], dim);
+    atomicAdd(&cnt[r * chunks + j / TG_CHUNK], 1);
+  }
+}
+
+// Exclusive scan of m values in place, one block of 1024 threads: each thread owns a contiguous run.
+__global__ void k_tg_scan(int* __restrict__ v, long long m) {
+  __shared__ int part[1024];
+  const long long per = (m + 1023) / 1024;
+  const long long s = threadIdx.x * per, e = s + per < m ? s + per : m;
+  int sum = 0;
+  for (long long i = s; i < e; ++i) sum += v[i];
+  part[threadIdx.x] = sum;
+  __syncthreads();
+  for (int o = 1; o < 1024; o <<= 1) {
+    int x = threadIdx.x >= o ? part[threadIdx.x - o] : 0;
+    __syncthreads();
+    part[threadIdx.x] += x;
+    __syncthreads();
+  }
+  int run = part[threadIdx.x] - sum;
+  for (long long i = s; i < e; ++i) {
+    int c = v[i];
+    v[i] = run;
+    run += c;
+  }
+}
+
+// One warp per chunk, positions in ascending order 32 at a time: lanes with the same row take
+// consecutive slots after that row's running offset.
+__global__ void k_tg_place(int* __restrict__ list, int* __restrict__ off, const int32_t* __restrict__ idx, long long dim, long long n_idx,
+                           long long chunks) {
+  const long long c = blockIdx.x;
+  const int lane = threadIdx.x;
+  const long long j_end = (c + 1) * TG_CHUNK < n_idx ? (c + 1) * TG_CHUNK : n_idx;
+  for (long long j0 = c * TG_CHUNK; j0 < j_end; j0 += 32) {
+    const long long j = j0 + lane;
+    const bool live = j < j_end;
+    const int r = live ? (int)clamp_index(idx[j], dim) : -1 - lane;
+    const unsigned peers = __match_any_sync(0xffffffffu, r);
+    const int leader = __ffs(peers) - 1;
+    int base = 0;
+    if (live && lane == leader) {
+      base = off[(long long)r * chunks + c];
+      off[(long long)r * chunks + c] = base + __popc(peers);
+    }
+    base = __shfl_sync(0xffffffffu, base, leader);
+    if (live) list[base + __popc(peers & ((1u << lane) - 1u))] = (int)j;
+    __syncwarp();
+  }
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+template <int N> __device__ __forceinline__ void cp_async_n(void* smem, const void* gmem) {
+  unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], %2;\n" ::"r"(s), "l"(gmem), "n"(N));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N> __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+// Block (row r, 32-column slice, outer o): every thread stages slices of the row's hit rows into
+// shared memory, TG_STAGES stages in flight; warp 0 adds them in list order (ascending
+// positions), one column per lane, starting from zero.
+constexpr int TG_HITS = 32;    // hit rows per stage
+constexpr int TG_STAGES = 8;   // stages in flight
+constexpr int TG_COLS = 32;    // columns per block
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256) k_tg_accumulate(T* __restrict__ dst, const T* __restrict__ ct, const int* __restrict__ list,
+                                                     const int* __restrict__ off, long long dim, long long n_idx, long long block,
+                                                     long long chunks) {
+  extern __shared__ __align__(16) unsigned char tg_smem[];
+  T* buf = (T*)tg_smem;  // [TG_STAGES][TG_HITS][TG_COLS]
+  const long long r = blockIdx.x, o = blockIdx.z;
+  const long long col0 = (long long)blockIdx.y * TG_COLS;
+  const int width = (int)(block - col0 < TG_COLS ? block - col0 : TG_COLS);
+  // After placement each counter holds the start of the next (row, chunk) run, so row r ends
+  // at its last chunk's counter and starts where row r - 1 ends.
+  const long long lo = r > 0 ? off[r * chunks - 1] : 0;
+  const long long hi = off[r * chunks + chunks - 1];
+  const long long m = hi - lo;
+  const T* base = ct + o * n_idx * block + col0;
+  const int* hits = list + lo;
+  constexpr int PER = VEC ? (int)(16 / sizeof(T)) : 1;  // elements per copy
+  const int copies_per_hit = (width + PER - 1) / PER;
+  const long long stages = (m + TG_HITS - 1) / TG_HITS;
+  auto issue = [&](long long s) {
+    if (s < stages) {
+      T* b = buf + (s % TG_STAGES) * TG_HITS * TG_COLS;
+      const long long h0 = s * TG_HITS;
+      const int nh = (int)(m - h0 < TG_HITS ? m - h0 : TG_HITS);
+      for (int q = threadIdx.x; q < nh * copies_per_hit; q += blockDim.x) {
+        const int h = q / copies_per_hit, k = (q - h * copies_per_hit) * PER;
+        const T* src = base + (long long)hits[h0 + h] * block + k;
+        if (VEC) cp_async16(b + h * TG_COLS + k, src);
+        else cp_async_n<(int)sizeof(T)>(b + h * TG_COLS + k, src);
+      }
+    }
+    cp_async_commit();
+  };
+  for (int s = 0; s < TG_STAGES - 1; ++s) issue(s);
+  T acc = (T)0;
+  const int lane = threadIdx.x;
+  for (long long s = 0; s < stages; ++s) {
+    issue(s + TG_STAGES - 1);
+    cp_async_wait<TG_STAGES - 1>();
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const T* b = buf + (s % TG_STAGES) * TG_HITS * TG_COLS;
+      const int nh = (int)(m - s * TG_HITS < TG_HITS ? m - s * TG_HITS : TG_HITS);
+      if (lane < width)
+        for (int h = 0; h < nh; ++h) acc = acc + b[h * TG_COLS + lane];
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+  if (threadIdx.x < width) dst[(o * dim + r) * block + col0 + threadIdx.x] = acc;
 }
 
 template <typename T>
@@ -594,17 +760,95 @@ void fill_zero(void* dst, size_t bytes, cudaStream_t s) { cudaMemsetAsync(dst, 0
     default: F<int32_t>(__VA_ARGS__); break;        \
   }
 
-template <typename T> static void gather_t(void* dst, const void* src, const Dims& out, long long base, long long n, cudaStream_t s) {
-  k_gather<T><<<grid_for(n), 256, 0, s>>>((T*)dst, (const T*)src, out, base, n);
+FDims fast_dims(const Dims& in, bool* ok) {
+  // Outer to inner; a dimension folds into the next inner one when stepping it equals stepping
+  // the inner one through its whole extent.
+  long long d[MAXR], st[MAXR];
+  int r = 0;
+  *ok = true;
+  for (int k = 0; k < in.rank; ++k) {
+    if (in.d[k] == 1) continue;
+    d[r] = in.d[k];
+    st[r] = in.st[k];
+    ++r;
+  }
+  long long md[MAXR], mst[MAXR];
+  int m = 0;
+  for (int k = 0; k < r; ++k) {
+    if (m > 0 && mst[m - 1] == st[k] * d[k]) {
+      md[m - 1] *= d[k];
+      mst[m - 1] = st[k];
+    } else {
+      md[m] = d[k];
+      mst[m] = st[k];
+      ++m;
+    }
+  }
+  FDims f;
+  f.rank = m;
+  for (int k = 0; k < m; ++k) {
+    if (md[k] >= (1ll << 31)) *ok = false;
+    f.d[k] = make_fdiv(*ok ? (unsigned long long)md[k] : 1ull);
+    f.st[k] = mst[k];
+  }
+  return f;
 }
+
+namespace {
+
+// Vector width (elements per 16 bytes) usable for a strided copy: the merged innermost extent
+// is contiguous and every stride, the base offset and the count are multiples of it.
+template <typename T> int vec_width(const FDims& f, long long base, long long n) {
+  constexpr int V = (int)(16 / sizeof(T));
+  if (f.rank == 0 || n % V || base % V) return 1;
+  if (f.st[f.rank - 1] != 1 || f.d[f.rank - 1].d % V) return 1;
+  for (int k = 0; k + 1 < f.rank; ++k)
+    if (f.st[k] % V) return 1;
+  return V;
+}
+
+template <typename T> struct Vec16;
+template <> struct Vec16<float> { using type = float4; };
+template <> struct Vec16<double> { using type = double2; };
+template <> struct Vec16<int32_t> { using type = int4; };
+
+template <typename T> void gather_t(void* dst, const void* src, const Dims& out, long long base, long long n, cudaStream_t s) {
+  bool ok = false;
+  FDims f = fast_dims(out, &ok);
+  if (!ok || n >= (1ll << 31)) {
+    k_gather<T><<<grid_for(n), 256, 0, s>>>((T*)dst, (const T*)src, out, base, n);
+    return;
+  }
+  constexpr int V = (int)(16 / sizeof(T));
+  using VT = typename Vec16<T>::type;
+  if (vec_width<T>(f, base, n) == V)
+    k_gather_vec<VT, V><<<grid_for(n / V), 256, 0, s>>>((VT*)dst, (const VT*)src, f, base, (unsigned)(n / V));
+  else
+    k_gather32<T><<<grid_for(n), 256, 0, s>>>((T*)dst, (const T*)src, f, base, (unsigned)n);
+}
+
+template <typename T> void scatter_t(void* dst, const void* src, const Dims& in, long long base, long long n, cudaStream_t s) {
+  bool ok = false;
+  FDims f = fast_dims(in, &ok);
+  if (!ok || n >= (1ll << 31)) {
+    k_scatter<T><<<grid_for(n), 256, 0, s>>>((T*)dst, (const T*)src, in, base, n);
+    return;
+  }
+  constexpr int V = (int)(16 / sizeof(T));
+  using VT = typename Vec16<T>::type;
+  if (vec_width<T>(f, base, n) == V)
+    k_scatter_vec<VT, V><<<grid_for(n / V), 256, 0, s>>>((VT*)dst, (const VT*)src, f, base, (unsigned)(n / V));
+  else
+    k_scatter32<T><<<grid_for(n), 256, 0, s>>>((T*)dst, (const T*)src, f, base, (unsigned)n);
+}
+
+}  // namespace
+
 void strided_gather(void* dst, const void* src, EType t, const Dims& out, long long base, long long n, cudaStream_t s) {
   if (n <= 0) return;
   DISPATCH(t, gather_t, dst, src, out, base, n, s);
 }
 
-template <typename T> static void scatter_t(void* dst, const void* src, const Dims& in, long long base, long long n, cudaStream_t s) {
-  k_scatter<T><<<grid_for(n), 256, 0, s>>>((T*)dst, (const T*)src, in, base, n);
-}
 void strided_scatter(void* dst, const void* src, EType t, const Dims& in, long long base, long long n, cudaStream_t s) {
   if (n <= 0) return;
   DISPATCH(t, scatter_t, dst, src, in, base, n, s);
@@ -638,12 +882,50 @@ void take_along(void* dst, const void* src, const int32_t* idx, EType t, long lo
   DISPATCH(t, take_along_t, dst, src, idx, n, v, k, s);
 }
 
+size_t take_grad_scratch_bytes(long long dim, long long n_idx) {
+  long long chunks = (n_idx + TG_CHUNK - 1) / TG_CHUNK;
+  auto a256 = [](long long b) { return (size_t)((b + 255) / 256 * 256); };
+  return a256(dim * chunks * 4) + a256(n_idx * 4);
+}
+
+template <typename T, bool VEC> static void tg_accumulate(void* dst, const void* ct, const int* list, const int* off, long long outer, long long dim,
+                                                           long long n_idx, long long block, long long chunks, cudaStream_t s) {
+  constexpr int smem = TG_STAGES * TG_HITS * TG_COLS * (int)sizeof(T);
+  static bool attr = [] {
+    cudaFuncSetAttribute(k_tg_accumulate<T, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    return true;
+  }();
+  (void)attr;
+  dim3 grid((unsigned)dim, (unsigned)((block + TG_COLS - 1) / TG_COLS), (unsigned)outer);
+  k_tg_accumulate<T, VEC><<<grid, 256, smem, s>>>((T*)dst, (const T*)ct, list, off, dim, n_idx, block, chunks);
+}
+
 void take_grad(void* dst, const void* ct, const int32_t* idx, EType t, long long outer, long long dim, long long n_idx, long long block,
-               cudaStream_t s) {
+               void* scratch, cudaStream_t s) {
   if (outer * dim * block <= 0) return;
-  dim3 grid((unsigned)dim, (unsigned)outer);
-  if (t == EType::F64) k_take_grad<double><<<grid, 256, 0, s>>>((double*)dst, (const double*)ct, idx, dim, n_idx, block);
-  else k_take_grad<float><<<grid, 256, 0, s>>>((float*)dst, (const float*)ct, idx, dim, n_idx, block);
+  const long long chunks = (n_idx + TG_CHUNK - 1) / TG_CHUNK;
+  const bool listed = scratch && n_idx > 0 && n_idx < (1ll << 31) && dim * chunks <= (1ll << 22) && dim < (1ll << 31) &&
+                      outer <= 65535 && (block + TG_COLS - 1) / TG_COLS <= 65535;
+  if (!listed) {
+    dim3 grid((unsigned)dim, (unsigned)outer);
+    if (t == EType::F64) k_take_grad<double><<<grid, 256, 0, s>>>((double*)dst, (const double*)ct, idx, dim, n_idx, block);
+    else k_take_grad<float><<<grid, 256, 0, s>>>((float*)dst, (const float*)ct, idx, dim, n_idx, block);
+    return;
+  }
+  int* cnt = (int*)scratch;
+  int* list = (int*)((char*)scratch + (dim * chunks * 4 + 255) / 256 * 256);
+  cudaMemsetAsync(cnt, 0, (size_t)(dim * chunks) * 4, s);
+  k_tg_count<<<grid_for(n_idx), 256, 0, s>>>(cnt, idx, dim, n_idx, chunks);
+  k_tg_scan<<<1, 1024, 0, s>>>(cnt, dim * chunks);
+  k_tg_place<<<(unsigned)chunks, 32, 0, s>>>(list, cnt, idx, dim, n_idx, chunks);
+  const bool vec = (block * (long long)esize(t)) % 16 == 0;
+  if (t == EType::F64) {
+    if (vec) tg_accumulate<double, true>(dst, ct, list, cnt, outer, dim, n_idx, block, chunks, s);
+    else tg_accumulate<double, false>(dst, ct, list, cnt, outer, dim, n_idx, block, chunks, s);
+  } else {
+    if (vec) tg_accumulate<float, true>(dst, ct, list, cnt, outer, dim, n_idx, block, chunks, s);
+    else tg_accumulate<float, false>(dst, ct, list, cnt, outer, dim, n_idx, block, chunks, s);
+  }
 }
 
 void take_along_grad(void* dst, const void* ct, const int32_t* idx, EType t, long long rows, long long v, long long k, cudaStream_t s) {

@@ -16,6 +16,34 @@ struct Dims {
   long long st[MAXR] = {};  // strides (elements) paired with the extents
 };
 
+// Division by a runtime-invariant divisor d in [1, 2^31] for dividends below 2^31, as a multiply
+// and shift (the round-up method of Granlund and Montgomery, "Division by invariant integers
+// using multiplication", PLDI 1994): with s = ceil(log2 d) and m = floor(2^32 (2^s - d) / d) + 1,
+// n / d = (umulhi(n, m) + n) >> s. Index kernels use it instead of 64-bit division.
+struct FDiv {
+  unsigned d = 1, m = 1, s = 0;
+};
+inline FDiv make_fdiv(unsigned long long d) {
+  FDiv f;
+  f.d = (unsigned)d;
+  unsigned s = 0;
+  while ((1ull << s) < d) ++s;
+  f.s = s;
+  f.m = (unsigned)(((1ull << 32) * ((1ull << s) - d)) / d + 1);
+  return f;
+}
+
+// Dims with extents as fast divisors, adjacent dimensions merged where the memory order allows
+// and extents of 1 dropped (rank 0 = a single element). Valid when every extent and the element
+// count are below 2^31.
+struct FDims {
+  int rank = 0;
+  FDiv d[MAXR];
+  long long st[MAXR] = {};
+};
+// Merges and converts; `ok` is false when some extent is 2^31 or more.
+FDims fast_dims(const Dims& in, bool* ok);
+
 enum class EType : int { F32 = 0, F64 = 1, I32 = 2 };
 
 size_t esize(EType t);
@@ -34,9 +62,11 @@ void take_rows(void* dst, const void* src, const int32_t* idx, EType t, long lon
                long long block, cudaStream_t s);
 void take_along(void* dst, const void* src, const int32_t* idx, EType t, long long n, long long v, long long k, cudaStream_t s);
 // Deterministic scatter-add: each destination row sums its contributions in ascending index
-// order starting from zero, the order rg's sequential loop adds them.
+// order starting from zero, the order rg's sequential loop adds them. The positions are first
+// sorted by row into per-row hit lists in `scratch` (take_grad_scratch_bytes bytes).
+size_t take_grad_scratch_bytes(long long dim, long long n_idx);
 void take_grad(void* dst, const void* ct, const int32_t* idx, EType t, long long outer, long long dim, long long n_idx,
-               long long block, cudaStream_t s);
+               long long block, void* scratch, cudaStream_t s);
 void take_along_grad(void* dst, const void* ct, const int32_t* idx, EType t, long long rows, long long v, long long k,
                      cudaStream_t s);
 

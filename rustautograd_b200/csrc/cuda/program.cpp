@@ -121,7 +121,8 @@ struct Program {
   size_t scratch_bytes = 0;
   bool capturable = true;
   std::vector<std::unique_ptr<Program>> subs;
-  Dims* bc_dev = nullptr;  // broadcast descriptors of the fused kernels
+  FDims* bc_dev = nullptr;  // broadcast descriptors of the fused kernels
+  Dims* bc64_dev = nullptr;
   int* tc_error = nullptr;  // set by a tensor-core GEMM whose pipeline wait gave up
   std::mutex mu;
   std::vector<std::unique_ptr<Frame>> pool;
@@ -132,6 +133,7 @@ struct Program {
   ~Program() {
     pool.clear();
     if (bc_dev) cudaFree(bc_dev);
+    if (bc64_dev) cudaFree(bc64_dev);
     if (tc_error) cudaFree(tc_error);
   }
 };
@@ -206,7 +208,8 @@ Dims dims_of(const std::vector<size_t>& shape, const std::vector<size_t>& st) {
 
 struct Builder {
   Program* p;
-  std::vector<Dims> bcs;  // broadcast descriptors, uploaded once per program
+  std::vector<FDims> bcs;  // broadcast descriptors, uploaded once per program
+  std::vector<Dims> bcs64;
   size_t scratch = 0;
 
   Lowered elementwise(const ElemSpec& spec, std::vector<size_t> in_slots, std::vector<size_t> out_slots) {
@@ -216,12 +219,19 @@ struct Builder {
       name = jit().add(spec);
     }
     size_t bc0 = bcs.size();
+    bool small = spec.n < (1ull << 31);
     for (auto& in : spec.inputs)
-      if (in.kind == rg::ArgKind::Broadcast) bcs.push_back(dims_of(spec.shape, rg::bstrides(in.shape, spec.shape.size())));
+      if (in.kind == rg::ArgKind::Broadcast) {
+        Dims d = dims_of(spec.shape, rg::bstrides(in.shape, spec.shape.size()));
+        bool ok = false;
+        bcs.push_back(fast_dims(d, &ok));
+        bcs64.push_back(d);
+        small = small && ok;
+      }
     int vw = spec.dtype == DType::F64 ? 2 : 4;
     bool vec_ok = spec.n % (size_t)vw == 0;
-    std::vector<long long> rows;
-    for (auto& in : spec.inputs) rows.push_back((long long)in.row);
+    std::vector<FDiv> rows;
+    for (auto& in : spec.inputs) rows.push_back(in.kind == rg::ArgKind::Row && in.row > 0 ? make_fdiv(in.row) : FDiv{});
     long long n = (long long)spec.n;
     Program* prog = p;
     auto fn = std::make_shared<CUfunction>(nullptr);
@@ -235,12 +245,14 @@ struct Builder {
       std::memset(&a, 0, sizeof a);
       a.n = n;
       a.vec = vec_ok ? 1 : 0;
+      a.small = small ? 1 : 0;
       for (size_t k = 0; k < in_slots.size(); ++k) {
         a.in[k] = c.f->ptr[in_slots[k]];
         a.row[k] = rows[k];
       }
       for (size_t q = 0; q < out_slots.size(); ++q) a.out[q] = c.f->ptr[out_slots[q]];
       a.bc = prog->bc_dev + bc0;
+      a.bc64 = prog->bc64_dev + bc0;
       if (n > 0) Jit::launch(*fn, a, n, vw, c.s);
     };
     if (in_slots.size() > (size_t)JIT_MAX_IN || out_slots.size() > (size_t)JIT_MAX_OUT)
@@ -348,7 +360,11 @@ struct Builder {
         for (size_t q = axis + 1; q < shape.size(); ++q) block *= (long long)shape[q];
         for (size_t q = 0; q < axis; ++q) outer *= (long long)shape[q];
         long long dim = (long long)shape[axis], n_idx = (long long)rg::product(i.arg_shapes[1]);
-        l.run = [=](Ctx& c) { take_grad(c.f->ptr[dst], c.f->ptr[a[0]], (const int32_t*)c.f->ptr[a[1]], t, outer, dim, n_idx, block, c.s); };
+        scratch = std::max(scratch, take_grad_scratch_bytes(dim, n_idx));
+        l.kernels = 5;
+        l.run = [=](Ctx& c) {
+          take_grad(c.f->ptr[dst], c.f->ptr[a[0]], (const int32_t*)c.f->ptr[a[1]], t, outer, dim, n_idx, block, c.f->scratch, c.s);
+        };
         return l;
       }
       case OpKind::TakeAlongGrad: {
@@ -778,8 +794,10 @@ std::unique_ptr<Program> make_program(const Plan& plan, int device) {
     jit().build();
   }
   if (!b.bcs.empty()) {
-    ck(cudaMalloc(&p->bc_dev, b.bcs.size() * sizeof(Dims)), "cudaMalloc(broadcast descriptors)");
-    ck(cudaMemcpy(p->bc_dev, b.bcs.data(), b.bcs.size() * sizeof(Dims), cudaMemcpyHostToDevice), "upload broadcast descriptors");
+    ck(cudaMalloc(&p->bc_dev, b.bcs.size() * sizeof(FDims)), "cudaMalloc(broadcast descriptors)");
+    ck(cudaMemcpy(p->bc_dev, b.bcs.data(), b.bcs.size() * sizeof(FDims), cudaMemcpyHostToDevice), "upload broadcast descriptors");
+    ck(cudaMalloc(&p->bc64_dev, b.bcs64.size() * sizeof(Dims)), "cudaMalloc(broadcast descriptors)");
+    ck(cudaMemcpy(p->bc64_dev, b.bcs64.data(), b.bcs64.size() * sizeof(Dims), cudaMemcpyHostToDevice), "upload broadcast descriptors");
   }
   p->scratch_bytes = b.scratch;
   p->capturable = true;

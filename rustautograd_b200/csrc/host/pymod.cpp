@@ -391,6 +391,11 @@ PYBIND11_MODULE(RG_MODULE_NAME, m) {
           } else {
             j["op"] = st.instr.op.name();
             j["shape"] = Json(st.instr.shape);
+            Json args = Json::array();
+            for (auto& s : st.instr.arg_shapes) args.push(Json(s));
+            j["args"] = args;
+            j["attr"] = Json(st.instr.op.shape);
+            j["flags"] = Json(std::vector<size_t>{(size_t)st.instr.op.flag_a, (size_t)st.instr.op.flag_b});
           }
           a.push(j);
         }

@@ -57,6 +57,21 @@ def test_binary_broadcast_is_bit_exact(oracle, name, fn, sa, sb):
     assert_parity(oracle, fn, (a, b), exact=True)
 
 
+@pytest.mark.parametrize("sa,sb", [
+    ((8, 4, 64, 64), (8, 4, 64, 1)),    # softmax normalisation: column broadcast
+    ((8, 4, 64, 64), (64, 64)),         # mask: row input
+    ((16, 6, 10), (16, 1, 10)),         # middle broadcast, inner run 10 (vectors straddle rows)
+    ((9, 6), (9, 1)),                   # inner extent 6: vectors cross the broadcast run
+    ((3, 5, 2, 4), (5, 1, 1)),          # extents of 1 merged away
+    ((2, 3, 4, 5), (3, 1, 5)),
+])
+@pytest.mark.parametrize("dtype", ["float32", "float64"])
+def test_broadcast_index_paths_are_bit_exact(oracle, sa, sb, dtype):
+    a, b = rnd(*sa, seed=31, dtype=dtype), rnd(*sb, seed=32, dtype=dtype)
+    fn = lambda a, b: (a / b, (a * b + 1.0) * a, F.maximum(a, b) - b)
+    assert_parity(oracle, fn, (a, b), exact=True)
+
+
 def test_pow_and_ieee_specials(oracle):
     v = np.array([0.0, -0.0, 1.0, -1.0, 2.5, -2.0, np.inf, -np.inf, np.nan, 1e-30, 3e38, -7.0], dtype="float32")
     x = F.tensor(v)
@@ -134,6 +149,32 @@ def test_scatter_add_gradients_are_bit_exact(oracle):
     # The gradient alone (no full-sum of the loss in the way) must be bit-identical.
     g = lambda t, i, l: F.value_and_grad(loss)(t, i, l)[1]
     assert_parity(oracle, g, (table, idx, lab), exact=True)
+
+
+@pytest.mark.parametrize("table,n_idx,axis,dtype,skew", [
+    ((96, 512), (8, 256), 0, "float32", "zipf"),      # many position chunks, 16-byte staging
+    ((40, 37), (3000,), 0, "float32", "uniform"),     # row width not a multiple of 4: element staging
+    ((50, 70), (5000,), 0, "float64", "zipf"),
+    ((7, 33), (2500,), 0, "float64", "uniform"),
+    ((3, 20, 48), (1500,), 1, "float32", "zipf"),     # outer extent 3
+    ((30, 64), (4000,), 0, "float32", "clamp"),       # out-of-range indices clamp to the ends
+])
+def test_scatter_add_hit_lists_are_bit_exact(oracle, table, n_idx, axis, dtype, skew):
+    rng = np.random.default_rng(21)
+    dim = table[axis]
+    if skew == "zipf":
+        p = (np.arange(dim) + 1.0) ** -1.1
+        idx = rng.choice(dim, size=n_idx, p=p / p.sum())
+    elif skew == "clamp":
+        idx = rng.integers(-5, dim + 5, size=n_idx)
+    else:
+        idx = rng.integers(0, dim, size=n_idx)
+    t = rnd(*table, seed=22, dtype=dtype)
+    i = F.tensor(idx.astype("int32"))
+    out_shape = table[:axis] + n_idx + table[axis + 1:]
+    w = rnd(*out_shape, seed=23, dtype=dtype)
+    g = lambda t, i, w: F.value_and_grad(lambda t, i, w: (F.take(t, i, axis) * w).sum())(t, i, w)[1]
+    assert_parity(oracle, g, (t, i, w), exact=True)
 
 
 @pytest.mark.parametrize("sa,sb,kw", [
