@@ -1,18 +1,27 @@
 // fp32-accurate GEMM on sm_100a tensor cores: 3xTF32 with tcgen05.mma, TMEM accumulators and a
 // TMA-fed, mbarrier-synchronised shared-memory pipeline (no cluster multicast).
 //
-// Each fp32 operand x is split once, before the product, into hi = tf32(x) (rounded, low 13 bits
-// zero) and lo = x - hi; C = A_hi B_hi + A_hi B_lo + A_lo B_hi, accumulated in fp32 in TMEM. The
-// dropped A_lo B_lo term and the truncation of lo to TF32 leave a relative error near 1e-6,
+// Each fp32 operand x is split, inside the kernel, into hi = tf32(x) (rounded to nearest, low 13
+// bits zero) and lo = x - hi; C = A_hi B_hi + A_hi B_lo + A_lo B_hi, accumulated in fp32 in TMEM.
+// The dropped A_lo B_lo term and the TF32 truncation of lo leave a relative error near 1e-6,
 // well inside the 1e-4 parity bound.
 //
-// Tile: 128 (M) x BN (N) x 32 (K) per stage, 3 stages. The split pre-pass writes both operands
-// K-major whatever their layout in memory (ta/tb), so TMA always fills 128-byte-swizzled K-major
-// tiles and the MMA always runs in its K-major x K-major form. Warp 0 lane 0 issues TMA, warp 1 lane 0 issues MMAs, all four warps
-// drain the accumulator (each warp owns 32 TMEM lanes = 32 rows). Every wait is bounded by a
-// wall-clock limit; on expiry the kernel records an error code and exits cleanly.
+// Persistent kernel, one CTA per SM, 10 warps:
+//   warp 0      TMA producer: raw fp32 tiles of A (128 x 32) and B (BN x 32) per stage, in the
+//               operands' own memory order (K-major, or MN-major for transposed storage).
+//   warp 1      MMA issuer: three tcgen05.mma per 8-deep K step, into one of two TMEM
+//               accumulators (128 lanes x BN fp32 columns each), so that a tile's epilogue
+//               overlaps the next tile's main loop.
+//   warps 2-5   converters: raw tile -> hi in place, lo beside it; a proxy fence makes the
+//               generic-proxy stores visible to the tensor cores.
+//   warps 6-9   epilogue: tcgen05.ld of the accumulator, 16-byte stores to C (or to a split-K
+//               partial, summed afterwards in split order, so results stay deterministic).
+// Work units are (output tile, K split) pairs handed out round-robin over the persistent CTAs.
+// Every wait is bounded by a wall-clock limit; on expiry the kernel records an error code, lets
+// its copies and products in flight finish, frees its TMEM and exits.
 #include <cuda.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <stdexcept>
 #include <string>
@@ -23,9 +32,18 @@ namespace rgc {
 
 namespace {
 
-constexpr int BM = 128, BK = 32, STAGES = 3;
-constexpr uint32_t A_TILE = BM * BK * 4;  // 16 KB
+constexpr int BM = 128, BK = 32;
+constexpr int THREADS = 320;
+constexpr uint32_t A_BYTES = BM * BK * 4;  // 16 KB
 constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;
+
+template <int BN> struct Shape {
+  static constexpr uint32_t B_BYTES = BN * BK * 4;
+  static constexpr uint32_t RAW = A_BYTES + B_BYTES;  // raw tiles, converted to hi in place
+  static constexpr uint32_t STAGE = 2 * RAW;          // + lo tiles
+  static constexpr int STAGES = (200 * 1024) / STAGE > 4 ? 4 : (200 * 1024) / STAGE;
+  static constexpr uint32_t SMEM = 1024 + STAGES * STAGE + 256;
+};
 
 __device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -43,6 +61,10 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(bar)), "r"(bytes) : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(bar)) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t phase) {
   uint32_t ok;
   asm volatile(
@@ -55,11 +77,12 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t phase) {
 
 // Waits for `phase` of `bar`; gives up after WAIT_LIMIT_NS or when another role aborted.
 __device__ bool mbar_wait(uint64_t* bar, uint32_t phase, volatile int* abort, int* err, int code) {
-  unsigned long long t0 = now_ns();
-  for (;;) {
+  unsigned long long t0 = 0;
+  for (int spin = 0;; ++spin) {
     if (mbar_try(bar, phase)) return true;
     if (*abort) return false;
-    if (now_ns() - t0 > WAIT_LIMIT_NS) {
+    if (spin == 64) t0 = now_ns();
+    if (spin > 64 && now_ns() - t0 > WAIT_LIMIT_NS) {
       *abort = 1;
       atomicExch(err, code);
       return false;
@@ -67,21 +90,34 @@ __device__ bool mbar_wait(uint64_t* bar, uint32_t phase, volatile int* abort, in
   }
 }
 
-__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+__device__ __forceinline__ void tma_load(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(saddr(dst)),
-      "l"(map), "r"(saddr(bar)), "r"(c0), "r"(c1), "r"(c2)
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst), "l"(map),
+      "r"(saddr(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
 
 // Shared-memory matrix descriptors (tcgen05 "matrix descriptor", version 1, 128-byte swizzle).
-// K-major: rows of 32 fp32 (128 B), 8-row groups 1024 B apart.
+// K-major tile: rows of 32 fp32 (128 B) along K, 8-row groups 1024 B apart.
 __device__ __forceinline__ uint64_t desc_k(uint32_t addr) {
   uint64_t d = (uint64_t)((addr >> 4) & 0x3FFF);
-  d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset: next 8-row group
-  d |= (uint64_t)1 << 46;             // descriptor version
-  d |= (uint64_t)2 << 61;             // 128-byte swizzle
+  d |= (uint64_t)1 << 16;            // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset: next 8-row group
+  d |= (uint64_t)1 << 46;            // descriptor version
+  d |= (uint64_t)2 << 61;            // 128-byte swizzle
+  return d;
+}
+// MN-major tile: 32-element (128 B) runs along M or N, one per K row; a TMA box of 32 K rows
+// (4 KB) per 32 MN elements. For 32-bit operands the tensor cores read MN-major tiles only in
+// the "128-byte swizzle with 32-byte atoms" layout (layout type 1; TMA's SWIZZLE_128B_ATOM_32B):
+// 4-row atoms of 512 B. Leading byte offset = next 32 MN elements (4 KB), stride byte offset =
+// next 4 K rows (512 B).
+__device__ __forceinline__ uint64_t desc_mn(uint32_t addr) {
+  uint64_t d = (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)(4096 >> 4) << 16;
+  d |= (uint64_t)(512 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)1 << 61;
   return d;
 }
 
@@ -112,35 +148,55 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-template <int BN>
-__global__ void __launch_bounds__(128, 1)
-    k_tc_gemm(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl, const __grid_constant__ CUtensorMap mBh,
-              const __grid_constant__ CUtensorMap mBl, float* __restrict__ C, long long M, long long N, int num_kb, int za, int zb, int* err) {
-  constexpr uint32_t B_TILE = BN * BK * 4;
-  constexpr uint32_t STAGE = 2 * A_TILE + 2 * B_TILE;
+__device__ __forceinline__ float tf32_rna(float v) {
+  uint32_t h;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
+  return __uint_as_float(h);
+}
+
+struct Work {
+  long long M, N;
+  int mt, nt, batch, splits;
+  int num_kb, kb_per_split;
+  int za, zb;         // 1 when the operand has its own matrix per batch entry, else 0
+  float* C;           // output (splits == 1) or partials [splits][batch][M][N]
+};
+
+template <int BN, bool AMN, bool BMN>
+__global__ void __launch_bounds__(THREADS, 1)
+    k_tc3(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mB, const Work w, int* err) {
+  using S = Shape<BN>;
+  constexpr int STAGES = S::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* full = (uint64_t*)(smem + STAGES * STAGE);
-  uint64_t* empty = full + STAGES;
-  uint64_t* accum = empty + STAGES;
-  uint32_t* tmem_slot = (uint32_t*)(accum + 1);
+  uint64_t* full = (uint64_t*)(smem + STAGES * S::STAGE);
+  uint64_t* conv = full + STAGES;
+  uint64_t* empty = conv + STAGES;
+  uint64_t* acc_full = empty + STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint64_t* done = acc_empty + 2;
+  uint32_t* tmem_slot = (uint32_t*)(done + 1);
   volatile int* abort = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int z = blockIdx.z;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const long long units = (long long)w.mt * w.nt * w.batch * w.splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
+      mbar_init(&conv[s], 4);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(done, 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)), "r"((uint32_t)BN) : "memory");
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)), "r"((uint32_t)(2 * BN)) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   fence_before();
@@ -148,126 +204,195 @@ __global__ void __launch_bounds__(128, 1)
   fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Instruction descriptor: M = 128, N = BN, TF32 x TF32 -> F32, both operands K-major.
-  const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+  auto decode = [&](long long u, int& m_t, int& n_t, int& z, int& sp) {
+    n_t = (int)(u % w.nt);
+    u /= w.nt;
+    m_t = (int)(u % w.mt);
+    u /= w.mt;
+    z = (int)(u % w.batch);
+    sp = (int)(u / w.batch);
+  };
+  auto kb_range = [&](int sp, int& kb0, int& kb1) {
+    kb0 = sp * w.kb_per_split;
+    kb1 = kb0 + w.kb_per_split < w.num_kb ? kb0 + w.kb_per_split : w.num_kb;
+  };
 
-  if (threadIdx.x == 0) {
-    // Producer: one stage = A hi, A lo, B hi, B lo for one 32-wide slice of K.
-    int issued = 0;
-    for (int kb = 0; kb < num_kb; ++kb) {
-      const int s = kb % STAGES;
-      if (kb >= STAGES && !mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1, abort, err, 1)) break;
-      mbar_expect_tx(&full[s], STAGE);
-      uint8_t* st = smem + s * STAGE;
-      const int k0 = kb * BK;
-      tma_load(st, &mAh, &full[s], k0, m0, z * za);
-      tma_load(st + A_TILE, &mAl, &full[s], k0, m0, z * za);
-      uint8_t* sb = st + 2 * A_TILE;
-      tma_load(sb, &mBh, &full[s], k0, n0, z * zb);
-      tma_load(sb + B_TILE, &mBl, &full[s], k0, n0, z * zb);
-      issued = kb + 1;
-    }
-    if (*abort) {
-      // Let the copies already in flight land before the block's shared memory goes away.
-      for (int kb = (issued > STAGES ? issued - STAGES : 0); kb < issued; ++kb) {
+  if (warp == 0) {
+    if (lane == 0) {
+      // Producer.
+      long long it = 0;
+      for (long long u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
+        int m_t, n_t, z, sp, kb0, kb1;
+        decode(u, m_t, n_t, z, sp);
+        kb_range(sp, kb0, kb1);
+        const int m0 = m_t * BM, n0 = n_t * BN;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = (int)(it % STAGES);
+          if (it >= STAGES && !mbar_wait(&empty[s], (uint32_t)(((it / STAGES) - 1) & 1), abort, err, 1)) break;
+          mbar_expect_tx(&full[s], S::RAW);
+          const uint32_t sa = saddr(smem + s * S::STAGE), sb = sa + A_BYTES;
+          const int k0 = kb * BK;
+          if (AMN) {
+#pragma unroll
+            for (int i = 0; i < BM / 32; ++i) tma_load(sa + i * 4096, &mA, &full[s], m0 + 32 * i, k0, z * w.za);
+          } else {
+            tma_load(sa, &mA, &full[s], k0, m0, z * w.za);
+          }
+          if (BMN) {
+#pragma unroll
+            for (int i = 0; i < BN / 32; ++i) tma_load(sb + i * 4096, &mB, &full[s], n0 + 32 * i, k0, z * w.zb);
+          } else {
+            tma_load(sb, &mB, &full[s], k0, n0, z * w.zb);
+          }
+        }
+        if (*abort) break;
+      }
+      // Copies in flight land before the block's shared memory goes away.
+      for (long long j = (it > STAGES ? it - STAGES : 0); j < it; ++j) {
         unsigned long long t0 = now_ns();
-        while (!mbar_try(&full[kb % STAGES], (kb / STAGES) & 1) && now_ns() - t0 < WAIT_LIMIT_NS) {
+        while (!mbar_try(&full[j % STAGES], (uint32_t)((j / STAGES) & 1)) && now_ns() - t0 < WAIT_LIMIT_NS) {
         }
       }
     }
-  } else if (threadIdx.x == 32) {
-    // MMA issuer: three TF32 products per 8-deep K step into the TMEM accumulator.
-    for (int kb = 0; kb < num_kb; ++kb) {
-      const int s = kb % STAGES;
-      if (!mbar_wait(&full[s], (kb / STAGES) & 1, abort, err, 2)) break;
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // MMA issuer. Instruction descriptor: M = 128, N = BN, TF32 x TF32 -> F32.
+      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((AMN ? 1u : 0u) << 15) | ((BMN ? 1u : 0u) << 16) |
+                             ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+      long long it = 0, t = 0;
+      for (long long u = blockIdx.x; u < units && !*abort; u += gridDim.x, ++t) {
+        int m_t, n_t, z, sp, kb0, kb1;
+        decode(u, m_t, n_t, z, sp);
+        kb_range(sp, kb0, kb1);
+        const int b = (int)(t & 1);
+        if (t >= 2 && !mbar_wait(&acc_empty[b], (uint32_t)(((t >> 1) - 1) & 1), abort, err, 4)) break;
+        fence_after();
+        const uint32_t acc = tmem + (uint32_t)(b * BN);
+        bool first = true;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = (int)(it % STAGES);
+          if (!mbar_wait(&conv[s], (uint32_t)((it / STAGES) & 1), abort, err, 2)) break;
+          fence_after();
+          const uint32_t ah = saddr(smem + s * S::STAGE), bh = ah + A_BYTES;
+          const uint32_t al = ah + S::RAW, bl = bh + S::RAW;
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; ++kk) {
+            const uint32_t ka = AMN ? kk * 1024 : kk * 32, kb_ = BMN ? kk * 1024 : kk * 32;
+            const uint64_t dah = AMN ? desc_mn(ah + ka) : desc_k(ah + ka), dal = AMN ? desc_mn(al + ka) : desc_k(al + ka);
+            const uint64_t dbh = BMN ? desc_mn(bh + kb_) : desc_k(bh + kb_), dbl = BMN ? desc_mn(bl + kb_) : desc_k(bl + kb_);
+            mma_tf32(acc, dah, dbh, idesc, first ? 0u : 1u);
+            mma_tf32(acc, dah, dbl, idesc, 1);
+            mma_tf32(acc, dal, dbh, idesc, 1);
+            first = false;
+          }
+          mma_commit(&empty[s]);
+        }
+        mma_commit(&acc_full[b]);
+      }
+      mma_commit(done);
+    }
+  } else if (warp < 6) {
+    // Converters: 128 threads split each stage's raw tiles into hi (in place) and lo.
+    const int ct = threadIdx.x - 64;
+    long long it = 0;
+    for (long long u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
+      int m_t, n_t, z, sp, kb0, kb1;
+      decode(u, m_t, n_t, z, sp);
+      kb_range(sp, kb0, kb1);
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        const int s = (int)(it % STAGES);
+        if (!mbar_wait(&full[s], (uint32_t)((it / STAGES) & 1), abort, err, 5)) {
+          ok = false;
+          break;
+        }
+        float4* raw = (float4*)(smem + s * S::STAGE);
+        float4* lo = (float4*)(smem + s * S::STAGE + S::RAW);
+#pragma unroll 4
+        for (int i = ct; i < (int)(S::RAW / 16); i += 128) {
+          float4 v = raw[i], h;
+          h.x = tf32_rna(v.x);
+          h.y = tf32_rna(v.y);
+          h.z = tf32_rna(v.z);
+          h.w = tf32_rna(v.w);
+          raw[i] = h;
+          lo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[s]);
+      }
+      if (!ok) break;
+    }
+  } else {
+    // Epilogue: warp w drains TMEM lanes [32 (w % 4), +32) = rows of the tile.
+    const int lg = warp & 3;
+    long long t = 0;
+    for (long long u = blockIdx.x; u < units && !*abort; u += gridDim.x, ++t) {
+      int m_t, n_t, z, sp;
+      decode(u, m_t, n_t, z, sp);
+      const int b = (int)(t & 1);
+      if (!mbar_wait(&acc_full[b], (uint32_t)((t >> 1) & 1), abort, err, 3)) break;
       fence_after();
-      const uint32_t sa = saddr(smem + s * STAGE);
-      const uint32_t sb = sa + 2 * A_TILE;
-#pragma unroll
-      for (int kk = 0; kk < BK / 8; ++kk) {
-        // K advances 8 fp32 = 32 bytes within the 128-byte swizzle row.
-        const uint64_t ah = desc_k(sa + kk * 32), al = desc_k(sa + A_TILE + kk * 32);
-        const uint64_t bh = desc_k(sb + kk * 32), bl = desc_k(sb + B_TILE + kk * 32);
-        mma_tf32(tmem, ah, bh, idesc, (kb | kk) != 0);
-        mma_tf32(tmem, ah, bl, idesc, 1);
-        mma_tf32(tmem, al, bh, idesc, 1);
-      }
-      mma_commit(&empty[s]);
-    }
-    mma_commit(accum);  // also after an abort: the epilogue waits for the products in flight
-  }
-  __syncwarp();
-
-  // Epilogue: warp w drains TMEM lanes [32w, 32w + 32) = rows m0 + 32w + lane.
-  bool ok = mbar_wait(accum, 0, abort, err, 3);
-  fence_after();
-  const long long row = m0 + warp * 32 + lane;
-  if (ok && !*abort) {
+      const long long row = (long long)m_t * BM + lg * 32 + lane;
+      const long long n0 = (long long)n_t * BN;
+      float* out = w.C + (((long long)sp * w.batch + z) * w.M + row) * w.N;
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      uint32_t v[32];
-      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, v);
-      if (row < M) {
-        float* out = C + (long long)z * M * N + row * N + n0 + c;
-        const long long lim = N - (n0 + c);
-        if (lim >= 32 && (((uintptr_t)out & 15) == 0)) {
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)(b * BN + c), v);
+        if (row < w.M) {
+          float* o = out + n0 + c;
+          const long long lim = w.N - (n0 + c);
+          if (lim >= 32 && (((uintptr_t)o & 15) == 0)) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) *(float4*)(out + j) = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
-        } else {
+            for (int j = 0; j < 32; j += 4)
+              *(float4*)(o + j) = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+          } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (j < lim) out[j] = __uint_as_float(v[j]);
+            for (int j = 0; j < 32; ++j)
+              if (j < lim) o[j] = __uint_as_float(v[j]);
+          }
         }
       }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
   }
-  fence_before();
+
   __syncthreads();
   if (warp == 0) {
+    // Every product issued has completed before the accumulator is freed.
+    if (lane == 0) {
+      unsigned long long t0 = now_ns();
+      while (!mbar_try(done, 0) && now_ns() - t0 < WAIT_LIMIT_NS) {
+      }
+    }
+    __syncwarp();
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * BN)) : "memory");
   }
 }
 
-__device__ __forceinline__ void split1(float v, float* hi, float* lo) {
-  uint32_t h;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
-  *hi = __uint_as_float(h);
-  *lo = v - *hi;
+// Split-K partials [splits][count] summed in split order.
+__global__ void k_sum_splits(float* __restrict__ c, const float* __restrict__ part, long long count, int splits) {
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < count; e += (long long)gridDim.x * blockDim.x) {
+    float acc = part[e];
+    for (int s = 1; s < splits; ++s) acc = acc + part[(long long)s * count + e];
+    c[e] = acc;
+  }
 }
 
-// Operand preparation, K-major: out[z][r][k] for r < R, k < Kp (zero for k >= K), with
-// hi = round-to-nearest TF32 of the value (low 13 bits zero) and lo = value - hi.
-// Source element (z, r, k) is src[z * sz + r * K + k].
-__global__ void k_split_rows(float* __restrict__ hi, float* __restrict__ lo, const float* __restrict__ src, long long nmat, long long R,
-                             long long K, long long Kp, long long sz) {
+// Copies rows x K operand matrices into K-major order with K padded to Kp (zeros), for operands
+// whose own layout cannot be read by TMA (a row pitch that is not a multiple of 16 bytes).
+// Element (z, r, k) is src[z * sz + r * K + k] (trans = false) or src[z * sz + k * R + r].
+__global__ void k_pack(float* __restrict__ dst, const float* __restrict__ src, long long nmat, long long R, long long K, long long Kp, long long sz,
+                       bool trans) {
   const long long n = nmat * R * Kp;
   for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
     long long k = e % Kp, rz = e / Kp, r = rz % R, z = rz / R;
-    float v = k < K ? src[z * sz + r * K + k] : 0.f;
-    split1(v, hi + e, lo + e);
-  }
-}
-
-// The same from a source stored transposed: element (z, r, k) is src[z * sz + k * R + r].
-// 32 x 32 tiles through shared memory keep both the reads and the writes coalesced.
-__global__ void k_split_cols(float* __restrict__ hi, float* __restrict__ lo, const float* __restrict__ src, long long R, long long K, long long Kp,
-                             long long sz) {
-  __shared__ float tile[32][33];
-  const long long z = blockIdx.z;
-  const long long r0 = (long long)blockIdx.x * 32, k0 = (long long)blockIdx.y * 32;
-  const float* s = src + z * sz;
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    long long k = k0 + i, r = r0 + threadIdx.x;
-    tile[i][threadIdx.x] = (k < K && r < R) ? s[k * R + r] : 0.f;
-  }
-  __syncthreads();
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    long long r = r0 + i, k = k0 + threadIdx.x;
-    if (r < R && k < Kp) {
-      long long o = (z * R + r) * Kp + k;
-      split1(tile[threadIdx.x][i], hi + o, lo + o);
-    }
+    dst[e] = k < K ? src[z * sz + (trans ? k * R + r : r * K + k)] : 0.f;
   }
 }
 
@@ -290,33 +415,109 @@ EncodeTiled encoder() {
 
 // A 3-D fp32 tensor map: dims {inner, outer, batch}, row stride and batch stride in elements.
 CUtensorMap make_map(const float* base, long long inner, long long outer, long long batch, long long row_stride, long long batch_stride,
-                     uint32_t box_inner, uint32_t box_outer) {
+                     uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
   CUtensorMap m;
   cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)batch};
-  cuuint64_t strides[2] = {(cuuint64_t)(row_stride * 4), (cuuint64_t)(batch_stride * 4)};
+  cuuint64_t strides[2] = {(cuuint64_t)(row_stride * 4), (cuuint64_t)(std::max<long long>(batch_stride, row_stride * outer) * 4)};
   cuuint32_t box[3] = {box_inner, box_outer, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed (CUresult " + std::to_string((int)r) + ")");
   return m;
 }
 
-int pick_bn(long long n) { return n >= 96 ? 128 : n > 32 ? 64 : 32; }
+int pick_bn(long long n) { return n > 128 ? 256 : n > 64 ? 128 : 64; }
 
 size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+int sm_count() {
+  static int sms = [] {
+    int d = 0, v = 148;
+    cudaGetDevice(&d);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, d);
+    return v;
+  }();
+  return sms;
+}
+
+// The launch decided for one product: operand layouts, packing, tile width, K splits.
+struct Plan3 {
+  bool a_mn, b_mn;      // operand read MN-major
+  bool pack_a, pack_b;  // operand first packed K-major (row pitch not 16-byte aligned)
+  long long kp;         // K of packed operands (multiple of 4)
+  int bn, splits, num_kb, kb_per_split;
+  long long mt, nt;
+  size_t pack_a_bytes, pack_b_bytes, part_bytes;
+};
+
+Plan3 plan3(const TcGemm& g) {
+  Plan3 p;
+  // A is [m, k] (K-major) unless ta: [k, m] (MN-major). B is [k, n] (MN-major) unless tb: [n, k].
+  p.a_mn = g.ta;
+  p.b_mn = !g.tb;
+  const long long pitch_a = p.a_mn ? g.m : g.k, pitch_b = p.b_mn ? g.n : g.k;
+  p.pack_a = pitch_a % 4 != 0 || (g.batch_a % 4) != 0;
+  p.pack_b = pitch_b % 4 != 0 || (g.batch_b % 4) != 0;
+  p.kp = (g.k + 3) / 4 * 4;
+  const long long nma = g.batch_a ? g.batch : 1, nmb = g.batch_b ? g.batch : 1;
+  p.pack_a_bytes = p.pack_a ? align256((size_t)(nma * g.m * p.kp) * 4) : 0;
+  p.pack_b_bytes = p.pack_b ? align256((size_t)(nmb * g.n * p.kp) * 4) : 0;
+  if (p.pack_a) p.a_mn = false;
+  if (p.pack_b) p.b_mn = false;
+  p.bn = pick_bn(g.n);
+  p.mt = (g.m + BM - 1) / BM;
+  p.nt = (g.n + p.bn - 1) / p.bn;
+  p.num_kb = (int)((g.k + BK - 1) / BK);
+  // Split K when the output tiles alone leave SMs idle: pick the split count (at least 8 K
+  // blocks per split) that fills the most of whole waves, less a small charge per split for the
+  // partial sums it writes and reads back.
+  const long long tiles = p.mt * p.nt * g.batch, sms = sm_count();
+  p.splits = 1;
+  if (tiles < sms && p.num_kb >= 16) {
+    double best = -1;
+    for (int s = 1; s <= 32 && s * 8 <= p.num_kb; ++s) {
+      long long units = tiles * s, waves = (units + sms - 1) / sms;
+      double score = (double)units / (double)(waves * sms) - 0.003 * s;
+      if (score > best + 1e-9) {
+        best = score;
+        p.splits = s;
+      }
+    }
+  }
+  p.kb_per_split = (p.num_kb + p.splits - 1) / p.splits;
+  p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
+  p.part_bytes = p.splits > 1 ? align256((size_t)p.splits * (size_t)(g.batch * g.m * g.n) * 4) : 0;
+  return p;
+}
+
+template <int BN, bool AMN, bool BMN> void set_smem() {
+  cudaError_t e = cudaFuncSetAttribute(k_tc3<BN, AMN, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Shape<BN>::SMEM);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("tensor-core GEMM setup failed: ") + cudaGetErrorString(e));
+}
+template <int BN> void set_smem_all() {
+  set_smem<BN, false, false>();
+  set_smem<BN, false, true>();
+  set_smem<BN, true, false>();
+  set_smem<BN, true, true>();
+}
+
+template <int BN>
+void launch3(bool amn, bool bmn, unsigned grid, const CUtensorMap& ma, const CUtensorMap& mb, const Work& w, int* err, cudaStream_t s) {
+  const size_t smem = Shape<BN>::SMEM;
+  if (!amn && !bmn) k_tc3<BN, false, false><<<grid, THREADS, smem, s>>>(ma, mb, w, err);
+  else if (!amn && bmn) k_tc3<BN, false, true><<<grid, THREADS, smem, s>>>(ma, mb, w, err);
+  else if (amn && !bmn) k_tc3<BN, true, false><<<grid, THREADS, smem, s>>>(ma, mb, w, err);
+  else k_tc3<BN, true, true><<<grid, THREADS, smem, s>>>(ma, mb, w, err);
+}
 
 }  // namespace
 
 void tc_gemm_init() {
   static bool done = [] {
-    for (int bn : {32, 64, 128}) {
-      size_t smem = 1024 + STAGES * (2 * A_TILE + 2 * (size_t)bn * BK * 4) + 256;
-      cudaError_t e = bn == 128 ? cudaFuncSetAttribute(k_tc_gemm<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-                      : bn == 64 ? cudaFuncSetAttribute(k_tc_gemm<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-                                 : cudaFuncSetAttribute(k_tc_gemm<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) throw std::runtime_error(std::string("tensor-core GEMM setup failed: ") + cudaGetErrorString(e));
-    }
+    set_smem_all<64>();
+    set_smem_all<128>();
+    set_smem_all<256>();
     encoder();
     return true;
   }();
@@ -324,66 +525,73 @@ void tc_gemm_init() {
 }
 
 bool tc_gemm_supported(const TcGemm& g) {
-  if (g.m <= 0 || g.n <= 0 || g.k <= 0 || g.batch <= 0 || g.batch > 65535) return false;
+  if (g.m <= 0 || g.n <= 0 || g.k <= 0 || g.batch <= 0 || g.batch > (1LL << 30)) return false;
   if (g.m > (1LL << 31) || g.n > (1LL << 31) || g.k > (1LL << 31)) return false;
   return true;
 }
 
-namespace {
-long long kpad(long long k) { return (k + 3) / 4 * 4; }  // a K-major row of Kp floats is 16-byte aligned
-}  // namespace
-
 size_t tc_gemm_scratch_bytes(const TcGemm& g) {
-  long long nma = g.batch_a ? g.batch : 1, nmb = g.batch_b ? g.batch : 1, kp = kpad(g.k);
-  return 2 * (align256((size_t)(nma * g.m * kp) * 4) + align256((size_t)(nmb * g.n * kp) * 4));
+  Plan3 p = plan3(g);
+  return p.pack_a_bytes + p.pack_b_bytes + p.part_bytes;
 }
 
 void tc_gemm(const TcGemm& g, void* scratch, int* error, cudaStream_t s) {
-  // Both operands are first written K-major (hi and lo halves, K padded to a multiple of 4 with
-  // zeros): the product then always runs in the K-major x K-major MMA form.
-  const int za = g.batch_a ? 1 : 0, zb = g.batch_b ? 1 : 0;
-  const long long nma = za ? g.batch : 1, nmb = zb ? g.batch : 1, kp = kpad(g.k);
-  char* p = (char*)scratch;
-  float* ah = (float*)p;
-  p += align256((size_t)(nma * g.m * kp) * 4);
-  float* al = (float*)p;
-  p += align256((size_t)(nma * g.m * kp) * 4);
-  float* bh = (float*)p;
-  p += align256((size_t)(nmb * g.n * kp) * 4);
-  float* bl = (float*)p;
-  static int sms = [] {
-    int d = 0, v = 148;
-    cudaGetDevice(&d);
-    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, d);
-    return v;
-  }();
-  // rows x K matrices, `trans`: stored [K, rows] instead of [rows, K].
-  auto prepare = [&](float* hi, float* lo, const float* x, long long nmat, long long rows, long long sz, bool trans) {
-    if (trans) {
-      dim3 grid((unsigned)((rows + 31) / 32), (unsigned)((kp + 31) / 32), (unsigned)nmat);
-      k_split_cols<<<grid, dim3(32, 8), 0, s>>>(hi, lo, x, rows, g.k, kp, sz);
-    } else {
-      long long n = nmat * rows * kp;
-      long long blocks = std::min<long long>((n + 255) / 256, (long long)sms * 8);
-      k_split_rows<<<(unsigned)std::max<long long>(blocks, 1), 256, 0, s>>>(hi, lo, x, nmat, rows, g.k, kp, sz);
-    }
-  };
-  prepare(ah, al, g.a, nma, g.m, g.batch_a, g.ta);
-  prepare(bh, bl, g.b, nmb, g.n, g.batch_b, !g.tb);
+  Plan3 p = plan3(g);
+  char* sp = (char*)scratch;
+  const long long nma = g.batch_a ? g.batch : 1, nmb = g.batch_b ? g.batch : 1;
+  const float* a = g.a;
+  const float* b = g.b;
+  long long ka = g.k, kb = g.k;  // row pitch (in K) of K-major operands
+  if (p.pack_a) {
+    float* d = (float*)sp;
+    sp += p.pack_a_bytes;
+    long long n = nma * g.m * p.kp;
+    k_pack<<<(unsigned)std::max<long long>(1, std::min<long long>((n + 255) / 256, sm_count() * 8LL)), 256, 0, s>>>(d, g.a, nma, g.m, g.k, p.kp, g.batch_a, g.ta);
+    a = d;
+    ka = p.kp;
+  }
+  if (p.pack_b) {
+    float* d = (float*)sp;
+    sp += p.pack_b_bytes;
+    long long n = nmb * g.n * p.kp;
+    k_pack<<<(unsigned)std::max<long long>(1, std::min<long long>((n + 255) / 256, sm_count() * 8LL)), 256, 0, s>>>(d, g.b, nmb, g.n, g.k, p.kp, g.batch_b, !g.tb);
+    b = d;
+    kb = p.kp;
+  }
+  float* part = p.splits > 1 ? (float*)sp : nullptr;
 
-  const int bn = pick_bn(g.n);
-  CUtensorMap mah = make_map(ah, kp, g.m, nma, kp, g.m * kp, 32, BM);
-  CUtensorMap mal = make_map(al, kp, g.m, nma, kp, g.m * kp, 32, BM);
-  CUtensorMap mbh = make_map(bh, kp, g.n, nmb, kp, g.n * kp, 32, (uint32_t)bn);
-  CUtensorMap mbl = make_map(bl, kp, g.n, nmb, kp, g.n * kp, 32, (uint32_t)bn);
-  const int num_kb = (int)((kp + BK - 1) / BK);
-  dim3 grid((unsigned)((g.n + bn - 1) / bn), (unsigned)((g.m + BM - 1) / BM), (unsigned)g.batch);
-  const size_t stage = 2 * A_TILE + 2 * (size_t)bn * BK * 4;
-  const size_t smem = 1024 + STAGES * stage + 256;
-  auto launch = [&](auto kernel) { kernel<<<grid, 128, smem, s>>>(mah, mal, mbh, mbl, g.c, g.m, g.n, num_kb, za, zb, error); };
-  if (bn == 128) launch(k_tc_gemm<128>);
-  else if (bn == 64) launch(k_tc_gemm<64>);
-  else launch(k_tc_gemm<32>);
+  // Tensor maps over the operands as stored. Batch strides: packed operands are dense.
+  const long long sa = p.pack_a ? g.m * p.kp : g.batch_a, sb = p.pack_b ? g.n * p.kp : g.batch_b;
+  const CUtensorMapSwizzle kmaj = CU_TENSOR_MAP_SWIZZLE_128B, mnmaj = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+  CUtensorMap ma = p.a_mn ? make_map(a, g.m, g.k, nma, g.m, sa, 32, 32, mnmaj) : make_map(a, ka, g.m, nma, ka, sa, 32, BM, kmaj);
+  CUtensorMap mb = p.b_mn ? make_map(b, g.n, g.k, nmb, g.n, sb, 32, 32, mnmaj) : make_map(b, kb, g.n, nmb, kb, sb, 32, (uint32_t)p.bn, kmaj);
+
+  Work w;
+  w.M = g.m;
+  w.N = g.n;
+  w.mt = (int)p.mt;
+  w.nt = (int)p.nt;
+  w.batch = (int)g.batch;
+  w.splits = p.splits;
+  w.num_kb = p.num_kb;
+  w.kb_per_split = p.kb_per_split;
+  w.za = g.batch_a ? 1 : 0;
+  w.zb = g.batch_b ? 1 : 0;
+  w.C = part ? part : g.c;
+  const long long units = p.mt * p.nt * g.batch * p.splits;
+  const unsigned grid = (unsigned)std::min<long long>(units, sm_count());
+  if (p.bn == 256) launch3<256>(p.a_mn, p.b_mn, grid, ma, mb, w, error, s);
+  else if (p.bn == 128) launch3<128>(p.a_mn, p.b_mn, grid, ma, mb, w, error, s);
+  else launch3<64>(p.a_mn, p.b_mn, grid, ma, mb, w, error, s);
+  if (part) {
+    const long long count = g.batch * g.m * g.n;
+    k_sum_splits<<<(unsigned)std::max<long long>(1, std::min<long long>((count + 255) / 256, sm_count() * 8LL)), 256, 0, s>>>(g.c, part, count, p.splits);
+  }
+}
+
+int tc_gemm_launches(const TcGemm& g) {
+  Plan3 p = plan3(g);
+  return 1 + (p.pack_a ? 1 : 0) + (p.pack_b ? 1 : 0) + (p.splits > 1 ? 1 : 0);
 }
 
 }  // namespace rgc

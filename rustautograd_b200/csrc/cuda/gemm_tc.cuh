@@ -25,8 +25,11 @@ struct TcGemm {
 void tc_gemm_init();
 // Whether the tensor-core path takes this product (fp32 only; alignment and shape limits).
 bool tc_gemm_supported(const TcGemm& g);
-// Scratch bytes the product needs for the low TF32 halves of its operands.
+// Scratch bytes the product needs: packed copies of operands whose row pitch TMA cannot read
+// (not a multiple of 16 bytes) and split-K partial sums.
 size_t tc_gemm_scratch_bytes(const TcGemm& g);
+// Kernel launches one product takes.
+int tc_gemm_launches(const TcGemm& g);
 // Launches the product; `scratch` holds tc_gemm_scratch_bytes bytes; `error` is a device int set
 // non-zero if a pipeline wait in the kernel gave up (it then exits without hanging).
 void tc_gemm(const TcGemm& g, void* scratch, int* error, cudaStream_t s);

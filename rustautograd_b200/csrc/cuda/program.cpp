@@ -480,7 +480,7 @@ struct Builder {
     if (use_tc) {
       tc_gemm_init();
       scratch = std::max(scratch, tc_gemm_scratch_bytes(tg));
-      l.kernels = 3;  // two operand splits and the product
+      l.kernels = tc_gemm_launches(tg);
       l.run = [=](Ctx& c) {
         TcGemm g = tg;
         g.a = (const float*)c.f->ptr[A];

@@ -213,6 +213,10 @@ TC_CASES = [
     ((16, 2, 130, 101), (16, 2, 101, 36), False, False),  # ragged, K not a multiple of 4
     ((515, 301), (301, 259), False, False),         # odd sizes everywhere
     ((301, 515), (259, 301), True, True),
+    ((6000, 160), (6000, 260), True, False),        # weight-gradient shape: split K, both operands MN-major
+    ((40, 8000), (8000, 72), False, False),         # one output tile, split K
+    ((4000, 96), (50, 96), False, True),            # narrow N (64-wide tiles), B K-major
+    ((300, 200), (200, 150), False, False),         # B row pitch not a multiple of 4: packed K-major
 ]
 
 
