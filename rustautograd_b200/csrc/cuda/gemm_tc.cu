@@ -1,10 +1,11 @@
 // fp32-accurate GEMM on sm_100a tensor cores: 3xTF32 with tcgen05.mma, TMEM accumulators and a
 // TMA-fed, mbarrier-synchronised shared-memory pipeline (no cluster multicast).
 //
-// Each fp32 operand x is split, inside the kernel, into hi = tf32(x) (rounded to nearest, low 13
-// bits zero) and lo = x - hi; C = A_hi B_hi + A_hi B_lo + A_lo B_hi, accumulated in fp32 in TMEM.
-// The dropped A_lo B_lo term and the TF32 truncation of lo leave a relative error near 1e-6,
-// well inside the 1e-4 parity bound.
+// Each fp32 operand x is split, inside the kernel, into hi = x with its low 13 mantissa bits
+// dropped (the TF32 value the tensor cores read from the raw fp32 tile, so hi needs no copy) and
+// lo = x - hi (exact); C = A_hi B_hi + A_hi B_lo + A_lo B_hi, accumulated in fp32 in TMEM. The
+// dropped A_lo B_lo term and the TF32 truncation of lo leave a relative error near 1e-6, well
+// inside the 1e-4 parity bound.
 //
 // Persistent kernel, one CTA per SM, 10 warps:
 //   warp 0      TMA producer: raw fp32 tiles of A (128 x 32) and B (BN x 32) per stage, in the
@@ -12,7 +13,7 @@
 //   warp 1      MMA issuer: three tcgen05.mma per 8-deep K step, into one of two TMEM
 //               accumulators (128 lanes x BN fp32 columns each), so that a tile's epilogue
 //               overlaps the next tile's main loop.
-//   warps 2-5   converters: raw tile -> hi in place, lo beside it; a proxy fence makes the
+//   warps 2-5   converters: lo tiles beside the raw tiles; a proxy fence makes the
 //               generic-proxy stores visible to the tensor cores.
 //   warps 6-9   epilogue: tcgen05.ld of the accumulator, 16-byte stores to C (or to a split-K
 //               partial, summed afterwards in split order, so results stay deterministic).
@@ -39,7 +40,7 @@ constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;
 
 template <int BN> struct Shape {
   static constexpr uint32_t B_BYTES = BN * BK * 4;
-  static constexpr uint32_t RAW = A_BYTES + B_BYTES;  // raw tiles, converted to hi in place
+  static constexpr uint32_t RAW = A_BYTES + B_BYTES;  // raw tiles (read by the MMA as hi)
   static constexpr uint32_t STAGE = 2 * RAW;          // + lo tiles
   static constexpr int STAGES = (200 * 1024) / STAGE > 4 ? 4 : (200 * 1024) / STAGE;
   static constexpr uint32_t SMEM = 1024 + STAGES * STAGE + 256;
@@ -148,11 +149,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ float tf32_rna(float v) {
-  uint32_t h;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
-  return __uint_as_float(h);
-}
+// The TF32 value the tensor cores take from an fp32 operand: its low 13 mantissa bits dropped.
+__device__ __forceinline__ float tf32_trunc(float v) { return __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); }
 
 struct Work {
   long long M, N;
@@ -292,7 +290,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mma_commit(done);
     }
   } else if (warp < 6) {
-    // Converters: 128 threads split each stage's raw tiles into hi (in place) and lo.
+    // Converters: 128 threads write each stage's lo tiles (the raw tiles serve as hi).
     const int ct = threadIdx.x - 64;
     long long it = 0;
     for (long long u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
@@ -310,13 +308,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         float4* lo = (float4*)(smem + s * S::STAGE + S::RAW);
 #pragma unroll 4
         for (int i = ct; i < (int)(S::RAW / 16); i += 128) {
-          float4 v = raw[i], h;
-          h.x = tf32_rna(v.x);
-          h.y = tf32_rna(v.y);
-          h.z = tf32_rna(v.z);
-          h.w = tf32_rna(v.w);
-          raw[i] = h;
-          lo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+          const float4 v = raw[i];
+          lo[i] = make_float4(v.x - tf32_trunc(v.x), v.y - tf32_trunc(v.y), v.z - tf32_trunc(v.z), v.w - tf32_trunc(v.w));
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
