@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""GPT training steps/s on the rg CUDA device (B200), 1 to 8 GPUs, against rg's CPU interpreter.
+"""Steps/s of rg plans on the CUDA device (B200), 1 to 8 GPUs, against rg's CPU interpreter.
 
 Default workload: BASELINE config 5, the char-level GPT with vocab 96, context 256, d_model 512,
 12 layers, 8 heads, GELU MLP 4x, pre-LayerNorm, AdamW(1e-3), global batch 512 split by batch over
@@ -9,10 +9,15 @@ all-reduce when N > 1, and the AdamW update.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|reference]
 
+Other workloads (--config): gpt-d256-l6 (the 1-GPU companion of config 5), gpt-d128-l4
+(config 4), adamw-c2 (config 2: the AdamW update of four large tensors, HBM-bound),
+linreg-c1 (config 1), gemm-mlp (one 131072 x 512 x 2048 product of config 5, for profiling).
+
 `value` is device time (CUDA events inside the run loop, state already in HBM); `e2e` is the
-same run through the C-ABI run call from host buffers (state and data copied in, state and loss
-history copied out, inside the timed region). `--impl reference` times rg's CPU interpreter (the
-restatement under oracle/, rg itself cannot be built here) on a bounded sample of the workload.
+same run through the C-ABI run call from host buffers (state and data copied in, state and the
+per-step history scalar copied out, inside the timed region). `--impl reference` times rg's CPU
+interpreter (the restatement under oracle/; rg itself cannot be built here) on a bounded sample
+of the workload.
 """
 import argparse
 import json
@@ -28,29 +33,181 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-CONFIGS = {
-    # BASELINE config 5 (scaling config) and its one-GPU companion; config 4.
-    "gpt-d512-l12": dict(vocab=96, block=256, d=512, heads=8, layers=12, batch=512, tokens="zipf"),
-    "gpt-d256-l6": dict(vocab=96, block=256, d=256, heads=8, layers=6, batch=64, tokens="zipf"),
-    "gpt-d128-l4": dict(vocab=96, block=128, d=128, heads=4, layers=4, batch=64, tokens="uniform"),
-}
 N_TOKENS = 200_000
 
 
-def tokens_for(cfg):
-    rng = np.random.default_rng(0)
-    if cfg["tokens"] == "uniform":
-        return rng.integers(0, cfg["vocab"], size=N_TOKENS, dtype="int32")
-    p = (np.arange(cfg["vocab"]) + 1.0) ** -1.1
-    return rng.choice(cfg["vocab"], size=N_TOKENS, p=p / p.sum()).astype("int32")
+# ---------------------------------------------------------------------------------------------
+# Workloads. Each builds (step function, state, data leaves) with the front end `F`, states the
+# algorithmic work of one step, and times a bounded sample of itself on the CPU oracle.
+# ---------------------------------------------------------------------------------------------
+
+class Gpt:
+    metric = "GPT train steps/sec"
+    bound = "tensor"
+    scalar_output = True
+
+    def __init__(self, name, vocab, block, d, heads, layers, batch, tokens):
+        self.name, self.vocab, self.block, self.d, self.heads, self.layers, self.batch, self.tokens = name, vocab, block, d, heads, layers, batch, tokens
+
+    def tokens_array(self):
+        rng = np.random.default_rng(0)
+        if self.tokens == "uniform":
+            return rng.integers(0, self.vocab, size=N_TOKENS, dtype="int32")
+        p = (np.arange(self.vocab) + 1.0) ** -1.1
+        return rng.choice(self.vocab, size=N_TOKENS, p=p / p.sum()).astype("int32")
+
+    def build(self, F, world=1, rank=0, batch=None):
+        batch = batch or self.batch
+        model = F.gpt.GPT(vocab=self.vocab, block=self.block, d=self.d, heads=self.heads, layers=self.layers)
+        params = model.init(F.random.key(0))
+        opt = F.optim.adamw(1e-3, weight_decay=0.01)
+        state = {"params": params, "opt": opt.init(params), "key": F.random.key(1)}
+        return F.gpt.make_train_step(model, opt, batch, world, rank), state, [F.tensor(self.tokens_array())]
+
+    def flops(self, batch=None):
+        """Matmul FLOPs of one training step (forward x3), full T x T attention, as the plan runs it."""
+        batch = batch or self.batch
+        d, t, L, v = self.d, self.block, self.layers, self.vocab
+        tokens = batch * t
+        per_layer = 2 * tokens * d * (3 * d + d + 4 * d + 4 * d) + 2 * 2 * batch * t * t * d
+        return 3 * (L * per_layer + 2 * tokens * d * v)
+
+    def config(self, world):
+        return {"workload": f"{self.name} global_batch={self.batch} T={self.block}", "global_batch": self.batch,
+                "per_rank_batch": self.batch // world, "seq_len": self.block, "d_model": self.d, "layers": self.layers,
+                "heads": self.heads, "vocab": self.vocab, "parallelism": f"dp{world}",
+                "l2": "state (params + AdamW moments) larger than L2 is streamed every step"}
+
+    def cpu_sample(self, F, oracle, budget=15.0):
+        """Batch-1 steps of the same model, scaled by the batch (every op of the step but the
+        optimizer update scales linearly in the batch)."""
+        step, state, data = self.build(F, batch=1)
+        c = F.compile(step, (state, data[0]), validate="none", device="cpu")
+        t, n = 0.0, 0
+        while n < 3 and t < budget:
+            t += F.run(c, state, data[0], steps=1).elapsed
+            n += 1
+        return t / n * self.batch, f"{n} steps of batch 1 (T={self.block}), scaled x{self.batch} to the global batch"
 
 
-def train_flops(cfg, batch):
-    """Matmul FLOPs of one training step (forward x3), full T x T attention, as the plan runs it."""
-    d, t, L, v = cfg["d"], cfg["block"], cfg["layers"], cfg["vocab"]
-    tokens = batch * t
-    per_layer = 2 * tokens * d * (3 * d + d + 4 * d + 4 * d) + 2 * 2 * batch * t * t * d
-    return 3 * (L * per_layer + 2 * tokens * d * v)
+class AdamW:
+    """AdamW over four f32 tensors (25.17 M elements), grads as the data batch.
+    Algorithmic traffic: read w, g, m, v and write w, m, v = 28 bytes per element per step."""
+    metric = "AdamW steps/sec"
+    bound = "hbm"
+    scalar_output = True
+    SHAPES = [(4096, 4096), (4096,), (1024, 4096), (4096, 1024)]
+
+    def __init__(self, name):
+        self.name = name
+        self.n = sum(int(np.prod(s)) for s in self.SHAPES)
+
+    def build(self, F, world=1, rank=0, scale=1):
+        rng = np.random.default_rng(0)
+        shapes = [tuple(max(1, x // scale) for x in s) for s in self.SHAPES]
+        mk = lambda s: F.tensor((rng.normal(size=s) * 0.02).astype("float32"))
+        params = [mk(s) for s in shapes]
+        grads = [mk(s) for s in shapes]
+        mu = [mk(s) for s in shapes]
+        nu = [F.tensor(np.abs(mk(s).numpy())) for s in shapes]
+        opt = F.optim.adamw(1e-3, 0.9, 0.999, 1e-8, 0.01)
+        state = {"params": params, "opt": {"count": F.full((), 0, "float32"), "mu": mu, "nu": nu}}
+
+        def step(state, g):
+            p, o = opt.update(g, state["opt"], state["params"])
+            return {"params": p, "opt": o}, o["count"]
+        return step, state, grads
+
+    def flops(self, batch=None):
+        return 0.0
+
+    def algorithmic_bytes(self):
+        return 28.0 * self.n
+
+    def config(self, world):
+        return {"workload": f"{self.name} 4 tensors {self.n} elements", "elements": self.n, "parallelism": "replicas",
+                "l2": "704 MB of state and gradients streamed every step (larger than L2)"}
+
+    def cpu_sample(self, F, oracle, budget=15.0):
+        step, state, grads = self.build(F)
+        c = F.compile(step, (state, grads), validate="none", device="cpu")
+        t, n = 0.0, 0
+        while n < 5 and t < budget:
+            t += F.run(c, state, grads, steps=1).elapsed
+            n += 1
+        return t / n, f"{n} full steps"
+
+
+class LinReg:
+    """the README linear regression, 500 gradient steps per run."""
+    metric = "linear-regression steps/sec"
+    bound = "latency"
+    scalar_output = True
+
+    def __init__(self, name):
+        self.name = name
+
+    def build(self, F, world=1, rank=0):
+        x = np.random.default_rng(0).normal(size=(256, 8)).astype("float32")
+        y = x @ np.arange(8, dtype="float32")
+
+        def step(w, batch):
+            value, g = F.value_and_grad(lambda w, b: (((b[0] @ w) - b[1]) ** 2).mean())(w, batch)
+            return w - 0.05 * g, value
+        return step, F.zeros(8), [F.tensor(x), F.tensor(y)]
+
+    def flops(self, batch=None):
+        return 4.0 * 256 * 8
+
+    def config(self, world):
+        return {"workload": f"{self.name} x (256, 8) f32, lr 0.05", "parallelism": "replicas", "l2": "8 KB of data, L2-resident by design"}
+
+    def cpu_sample(self, F, oracle, budget=15.0):
+        step, state, data = self.build(F)
+        c = F.compile(step, (state, list(data)), validate="none", device="cpu")
+        r = F.run(c, state, list(data), steps=500)
+        return r.elapsed / 500, "500 steps in one run"
+
+
+class Gemm:
+    """One product of config 5's MLP (131072 tokens x 512 -> 2048), C as the state."""
+    metric = "GEMM steps/sec"
+    bound = "tensor"
+    scalar_output = False
+
+    def __init__(self, name, m, k, n):
+        self.name, self.m, self.k, self.n = name, m, k, n
+
+    def build(self, F, world=1, rank=0, m=None):
+        m = m or self.m
+        rng = np.random.default_rng(0)
+        a = F.tensor(rng.normal(size=(m, self.k)).astype("float32"))
+        b = F.tensor((rng.normal(size=(self.k, self.n)) * 0.05).astype("float32"))
+        return (lambda c, ab: ab[0] @ ab[1]), F.zeros((m, self.n)), [a, b]
+
+    def flops(self, batch=None):
+        return 2.0 * self.m * self.k * self.n
+
+    def config(self, world):
+        return {"workload": f"{self.name} {self.m}x{self.k} @ {self.k}x{self.n} f32", "parallelism": "replicas",
+                "l2": "operands and result (1.3 GB) larger than L2"}
+
+    def cpu_sample(self, F, oracle, budget=15.0):
+        m = 1024
+        step, state, data = self.build(F, m=m)
+        c = F.compile(step, (state, list(data)), validate="none", device="cpu")
+        t = F.run(c, state, list(data), steps=1).elapsed
+        return t * self.m / m, f"one product with {m} of {self.m} rows, scaled x{self.m // m}"
+
+
+WORKLOADS = {
+    "gpt-d512-l12": Gpt("gpt-d512-l12", vocab=96, block=256, d=512, heads=8, layers=12, batch=512, tokens="zipf"),
+    "gpt-d256-l6": Gpt("gpt-d256-l6", vocab=96, block=256, d=256, heads=8, layers=6, batch=64, tokens="zipf"),
+    "gpt-d128-l4": Gpt("gpt-d128-l4", vocab=96, block=128, d=128, heads=4, layers=4, batch=64, tokens="uniform"),
+    "adamw-c2": AdamW("adamw-c2"),
+    "linreg-c1": LinReg("linreg-c1"),
+    "gemm-mlp": Gemm("gemm-mlp", m=131072, k=512, n=2048),
+}
 
 
 class Clocks:
@@ -104,37 +261,50 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
-def build_model(F, cfg, world, rank):
-    model = F.gpt.GPT(vocab=cfg["vocab"], block=cfg["block"], d=cfg["d"], heads=cfg["heads"], layers=cfg["layers"])
-    params = model.init(F.random.key(0))
-    opt = F.optim.adamw(1e-3, weight_decay=0.01)
-    state = {"params": params, "opt": opt.init(params), "key": F.random.key(1)}
-    step = F.gpt.make_train_step(model, opt, cfg["batch"], world, rank)
-    return step, state
+def traffic_for(workload, kernel):
+    """DRAM bytes per launch of the dominant kernel class, from the committed ncu summary."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get(workload, {}).get(kernel)
+    except (OSError, ValueError):
+        return None
 
 
-def cpu_sample(cfg, seconds_budget=30.0):
-    """rg's CPU interpreter (restated) on one-sequence batches of the same model: seconds per
-    sequence, which scales linearly to the configured batch. Returns (seconds/step at the full
-    batch, sample description, threads)."""
+def cpu_baseline(w):
+    """The CPU oracle (restated rg interpreter) on all host threads, on a bounded sample."""
     sys.path.insert(0, os.path.join(ROOT, "oracle", "_build"))
     from rustautograd_b200 import build_ext
     build_ext.build_oracle()
     import _rg_oracle
     from rustautograd_b200 import frontend as F
     F.use(_rg_oracle, "cpu")
-    sample = dict(cfg, batch=1)
-    step, state = build_model(F, sample, 1, 0)
-    tokens = F.tensor(tokens_for(cfg))
-    c = F.compile(step, (state, tokens), validate="none", device="cpu")
-    F.run(c, state, tokens, steps=1)  # first touch of the frame's pages
-    t, n = 0.0, 0
-    while n < 3 and t < seconds_budget:
-        r = F.run(c, state, tokens, steps=1)
-        t += r.elapsed
-        n += 1
-    per_seq = t / n
-    return per_seq * cfg["batch"], f"{n} steps of batch 1 (T={cfg['block']}), scaled x{cfg['batch']} to the global batch", _rg_oracle.threads()
+    secs, sample = w.cpu_sample(F, _rg_oracle)
+    return secs, sample, _rg_oracle.threads()
+
+
+def roofline(w, compiled, secs, pk):
+    """The dominant kernel class of a step by device time (CUDA events between plan steps)."""
+    costs = compiled._n.step_costs()
+    by_kind = {}
+    for (kind, fl, by), s in zip(costs, secs):
+        e = by_kind.setdefault(kind, [0.0, 0.0, 0.0, 0])
+        e[0] += s
+        e[1] += fl
+        e[2] += by
+        e[3] += 1
+    total = sum(v[0] for v in by_kind.values()) or 1e-30
+    top = max(by_kind, key=lambda k: by_kind[k][0])
+    t_s, fl, by, n = by_kind[top]
+    if top == "matmul":
+        achieved, peak, unit, bound = fl / t_s / 1e12, pk["bf16_tflops_sustained"], "TFLOP/s", "tensor"
+    else:
+        achieved, peak, unit, bound = by / t_s / 1e9, pk["hbm_gbs"], "GB/s", "hbm"
+    fused = by_kind.get("fused", [1e-30, 0, 0, 0])
+    return {"bound": bound, "kernel": top, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
+            "peak_source": pk["source"], "traffic": traffic_for(w.name, top), "launches_per_step": n, "share_of_step": t_s / total,
+            "algorithmic_per_launch": (fl if top == "matmul" else by) / max(n, 1),
+            "fused_elementwise": {"achieved_gbs": fused[2] / fused[0] / 1e9, "frac_of_hbm": fused[2] / fused[0] / 1e9 / pk["hbm_gbs"],
+                                  "share_of_step": fused[0] / total}}
 
 
 def main():
@@ -142,26 +312,24 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="gpt-d512-l12", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="gpt-d512-l12", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
-    cfg = CONFIGS[args.config]
+    w = WORKLOADS[args.config]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    metric = "GPT train steps/sec"
-    workload = f"{args.config} global_batch={cfg['batch']} T={cfg['block']}"
 
     if args.impl == "reference":
         if rank != 0:
             return
-        secs, sample, threads = cpu_sample(cfg)
+        secs, sample, threads = cpu_baseline(w)
         value = 1.0 / secs
         print(json.dumps({
-            "impl": "reference", "metric": metric, "value": value, "unit": "steps/s", "n_gpus": args.gpus, "steps": args.steps,
+            "impl": "reference", "metric": w.metric, "value": value, "unit": "steps/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": secs * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic", "config": {"workload": workload},
+            "dtype": "f32", "data": "synthetic", "config": w.config(args.gpus),
             "cpu_baseline": {"value": value, "unit": "steps/s", "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }))
@@ -180,23 +348,26 @@ def main():
         raise SystemExit("no usable sm_100 GPU: the CUDA device is unavailable")
     F.use(_rg, "cuda")
     if world > 1:
+        if not isinstance(w, Gpt):
+            raise SystemExit(f"{args.config} runs on one GPU (replicas only); the data-parallel path is the GPT step")
         uid = [_rg.dist_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         _rg.dist_init(rank, world, uid[0])
 
-    step, state = build_model(F, cfg, world, rank)
-    tokens = F.tensor(tokens_for(cfg))
+    step, state, data = w.build(F, world, rank)
+    data_arg = data[0] if len(data) == 1 else list(data)
     t0 = time.perf_counter()
-    compiled = F.compile(step, (state, tokens), validate="none", device="cuda")
+    compiled = F.compile(step, (state, data_arg), validate="none", device="cuda")
     compile_s = time.perf_counter() - t0
     n_state = len(F.flatten(state)[0])
     state_leaves = [F.tensor(l)._t for l in F.flatten(state)[0]]
-    data = [tokens._t]
+    data_leaves = [F.tensor(l)._t for l in F.flatten(data_arg)[0]]
     state_map = [(k, k) for k in range(n_state)]
-    hist = [n_state]
+    data_inputs = list(range(n_state, n_state + len(data_leaves)))
+    hist = [n_state] if w.scalar_output else []  # the step's scalar output (loss, or the step count)
 
     def run(steps):
-        return compiled._n.run(state_map, [n_state], hist, state_leaves, [data], steps)
+        return compiled._n.run(state_map, data_inputs, hist, state_leaves, [data_leaves], steps)
 
     run(args.warmup)
     launches0 = compiled._n.launches()
@@ -218,58 +389,41 @@ def main():
         t = torch.tensor([device_s, wall], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         device_s, wall = t.tolist()
-    loss = history[0]
+    hist0 = history[0] if history else [None]
     state_bytes = sum(len(x.tobytes()) for x in state_leaves)
-    data_bytes = len(tokens._t.tobytes())
+    data_bytes = sum(len(x.tobytes()) for x in data_leaves)
 
-    # Roofline of the dominant kernel class: per-step device times (CUDA events between plan
-    # steps on the device's stream) over the same compiled plan and inputs. Every rank runs it:
-    # the plan's all-reduce steps are collectives.
-    secs = compiled._n.step_seconds(state_leaves + data, 2)
+    # Per-step device times for the roofline, on every rank: the plan's all-reduce steps are
+    # collectives.
+    secs = compiled._n.step_seconds(state_leaves + data_leaves, 2)
     out = None
     if rank == 0:
         value = done / device_s
-        flops = train_flops(cfg, cfg["batch"]) / world
         pk = peaks()
-        costs = compiled._n.step_costs()
-        by_kind = {}
-        for (kind, fl, by), s in zip(costs, secs):
-            e = by_kind.setdefault(kind, [0.0, 0.0, 0.0, 0])
-            e[0] += s
-            e[1] += fl
-            e[2] += by
-            e[3] += 1
-        total = sum(v[0] for v in by_kind.values())
-        top = max(by_kind, key=lambda k: by_kind[k][0])
-        t_s, fl, by, n = by_kind[top]
-        if top == "matmul":
-            achieved, peak, unit, bound = fl / t_s / 1e12, pk["bf16_tflops_sustained"], "TFLOP/s", "tensor"
-        else:
-            achieved, peak, unit, bound = by / t_s / 1e9, pk["hbm_gbs"], "GB/s", "hbm"
-        fused = by_kind.get("fused", [1e-30, 0, 0, 0])
-        roofline = {"bound": bound, "kernel": top, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
-                    "peak_source": pk["source"], "traffic": None, "launches_per_step": n, "share_of_step": t_s / total,
-                    "fused_elementwise": {"achieved_gbs": fused[2] / fused[0] / 1e9, "frac_of_hbm": fused[2] / fused[0] / 1e9 / pk["hbm_gbs"],
-                                          "share_of_step": fused[0] / total}}
+        rf = roofline(w, compiled, secs, pk)
+        if w.bound == "hbm":
+            # The whole step is one bandwidth-bound update: report it against HBM directly.
+            gbs = w.algorithmic_bytes() / (device_s / done) / 1e9
+            rf.update({"bound": "hbm", "kernel": "step", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"],
+                       "algorithmic_per_launch": w.algorithmic_bytes() / max(rf["launches_per_step"], 1)})
         cpu = None
         if not args.no_cpu_baseline:
-            secs_cpu, sample, threads = cpu_sample(cfg)
+            secs_cpu, sample, threads = cpu_baseline(w)
             cpu = {"value": 1.0 / secs_cpu, "unit": "steps/s", "cores": threads, "kind": "port", "sample": sample}
+        mem = compiled.report.get("memory", {})
+        cfg = dict(w.config(world), frame_bytes=mem.get("device_bytes_allocated"))
         out = {
-            "metric": metric, "value": value, "unit": "steps/s", "n_gpus": world, "steps": done, "warmup": args.warmup,
+            "metric": w.metric, "value": value, "unit": "steps/s", "n_gpus": world, "steps": done, "warmup": args.warmup,
             "ms_per_step": device_s / done * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic",
-            "config": {"workload": workload, "global_batch": cfg["batch"], "per_rank_batch": cfg["batch"] // world, "seq_len": cfg["block"],
-                       "d_model": cfg["d"], "layers": cfg["layers"], "heads": cfg["heads"], "vocab": cfg["vocab"],
-                       "parallelism": f"dp{world}", "l2": "state (params + AdamW moments) larger than L2 is streamed every step"},
+            "dtype": "f32", "data": "synthetic", "config": cfg,
             "e2e": {"value": done / wall, "unit": "steps/s", "h2d_bytes_per_step": (state_bytes + data_bytes) / done,
                     "d2h_bytes_per_step": (state_bytes + 8 * done) / done},
             "gpu_launches": launches,
-            "tflops_per_gpu": flops * done / device_s / 1e12,
-            "roofline": roofline,
+            "tflops_per_gpu": w.flops() / world * done / device_s / 1e12,
+            "roofline": rf,
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
-            "loss": {"first": loss[0], "last": loss[-1], "nonfinite_step": bad},
+            "history": {"first": hist0[0], "last": hist0[-1], "nonfinite_step": bad},
             "compile_seconds": compile_s,
         }
     if dist:
