@@ -262,12 +262,14 @@ def peaks():
 
 
 def traffic_for(workload, kernel):
-    """DRAM bytes per launch of the dominant kernel class, from the committed ncu summary."""
+    """DRAM bytes per launch of the dominant kernel class and what launch they were measured on,
+    from the committed ncu summaries (dram__bytes_read.sum + dram__bytes_write.sum)."""
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            return json.load(f).get(workload, {}).get(kernel)
-    except (OSError, ValueError):
-        return None
+            t = json.load(f).get(workload, {}).get(kernel)
+        return (t["bytes"], t["of"]) if t else (None, None)
+    except (OSError, ValueError, KeyError):
+        return None, None
 
 
 def cpu_baseline(w):
@@ -300,8 +302,9 @@ def roofline(w, compiled, secs, pk):
     else:
         achieved, peak, unit, bound = by / t_s / 1e9, pk["hbm_gbs"], "GB/s", "hbm"
     fused = by_kind.get("fused", [1e-30, 0, 0, 0])
+    traffic, traffic_of = traffic_for(w.name, top)
     return {"bound": bound, "kernel": top, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
-            "peak_source": pk["source"], "traffic": traffic_for(w.name, top), "launches_per_step": n, "share_of_step": t_s / total,
+            "peak_source": pk["source"], "traffic": traffic, "traffic_of": traffic_of, "launches_per_step": n, "share_of_step": t_s / total,
             "algorithmic_per_launch": (fl if top == "matmul" else by) / max(n, 1),
             "fused_elementwise": {"achieved_gbs": fused[2] / fused[0] / 1e9, "frac_of_hbm": fused[2] / fused[0] / 1e9 / pk["hbm_gbs"],
                                   "share_of_step": fused[0] / total}}
