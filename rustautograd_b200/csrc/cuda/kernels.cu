@@ -438,6 +438,86 @@ template <typename T> __global__ void k_reduce_rows_warp(T* __restrict__ dst, co
   }
 }
 
+// Rows of 16-byte-aligned length: each lane reads 16-byte vectors (the within-row combination
+// order is the vector-lane order, then the warp tree; only Sum depends on it).
+template <typename T, typename VT, int V>
+__global__ void k_reduce_rows_warp_vec(T* __restrict__ dst, const T* __restrict__ a, Red op, long long rows, long long len) {
+  long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  const long long nv = len / V;
+  for (long long r = warp; r < rows; r += nwarps) {
+    const VT* row = (const VT*)(a + r * len);
+    T acc = red_init<T>(op);
+    for (long long j = lane; j < nv; j += 32) {
+      const VT v = row[j];
+      const T* e = (const T*)&v;
+#pragma unroll
+      for (int q = 0; q < V; ++q) acc = combine(op, acc, e[q]);
+    }
+    for (int o = 16; o > 0; o >>= 1) acc = combine(op, acc, __shfl_down_sync(0xffffffffu, acc, o));
+    if (lane == 0) dst[r] = acc;
+  }
+}
+
+// Row sums in the order of rg's fast_sum (plan.rs:1213-1230): eight running sums, element j
+// going to sum j % 8, then 0 + s0 + ... + s7 and the n % 8 tail in order; bit-identical to the
+// CPU interpreter. Vector form: a lane owns E consecutive sums (E = elements per 16 bytes) and
+// L = 8 / E lanes share a row; scalar form: one sum per lane, eight lanes per row.
+template <typename T, typename VT, int E>
+__global__ void k_rows_fast_sum_vec(T* __restrict__ dst, const T* __restrict__ a, long long rows, long long len) {
+  constexpr int L = 8 / E, RPW = 32 / L;
+  const int lane = threadIdx.x & 31, sub = lane / L, q = lane % L;
+  const long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  const long long full = len / 8 * 8;
+  for (long long r0 = warp * RPW; r0 < rows; r0 += nwarps * RPW) {
+    const long long r = r0 + sub;
+    T acc[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[e] = (T)0;
+    const T* row = a + (r < rows ? r : 0) * len;
+    if (r < rows) {
+      for (long long c = 0; c < full; c += 8) {
+        const VT v = *(const VT*)(row + c + q * E);
+        const T* x = (const T*)&v;
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[e] = acc[e] + x[e];
+      }
+    }
+    T out = (T)0;
+#pragma unroll
+    for (int k = 0; k < L; ++k)
+#pragma unroll
+      for (int e = 0; e < E; ++e) out = out + __shfl_sync(0xffffffffu, acc[e], sub * L + k);
+    if (q == 0 && r < rows) {
+      for (long long i = full; i < len; ++i) out = out + row[i];
+      dst[r] = out;
+    }
+  }
+}
+
+template <typename T> __global__ void k_rows_fast_sum(T* __restrict__ dst, const T* __restrict__ a, long long rows, long long len) {
+  const int lane = threadIdx.x & 31, sub = lane >> 3, chain = lane & 7;
+  const long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  const long long full = len / 8 * 8;
+  for (long long r0 = warp * 4; r0 < rows; r0 += nwarps * 4) {
+    const long long r = r0 + sub;
+    T acc = (T)0;
+    const T* row = a + (r < rows ? r : 0) * len;
+    if (r < rows)
+      for (long long c = chain; c < full; c += 8) acc = acc + row[c];
+    T out = (T)0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) out = out + __shfl_sync(0xffffffffu, acc, sub * 8 + k);
+    if (chain == 0 && r < rows) {
+      for (long long i = full; i < len; ++i) out = out + row[i];
+      dst[r] = out;
+    }
+  }
+}
+
 template <typename T> __global__ void k_reduce_rows_block(T* __restrict__ dst, const T* __restrict__ a, Red op, long long len) {
   __shared__ T sh[32];
   const T* row = a + (long long)blockIdx.x * len;
@@ -468,13 +548,50 @@ __global__ void k_cols_partial(T* __restrict__ part, const T* __restrict__ a, Re
   part[q * cols + c] = acc;
 }
 
-template <typename T> __global__ void k_cols_final(T* __restrict__ dst, const T* __restrict__ part, Red op, long long nparts, long long cols) {
-  GRID_STRIDE(c, cols) {
-    T acc = red_init<T>(op);
-    for (long long q = 0; q < nparts; ++q) acc = combine(op, acc, part[q * cols + c]);
-    dst[c] = acc;
+// The final column pass with its loads staged: block = 32 columns; every thread copies slices of
+// the next partial rows into shared memory (TG_STAGES stages in flight), warp 0 combines them in
+// partial order, one column per lane: a sequential order per column with many loads in flight.
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256) k_cols_final_staged(T* __restrict__ dst, const T* __restrict__ part, Red op, long long nparts, long long cols) {
+  extern __shared__ __align__(16) unsigned char cf_smem[];
+  T* buf = (T*)cf_smem;  // [TG_STAGES][TG_HITS][TG_COLS]
+  const long long col0 = (long long)blockIdx.x * TG_COLS;
+  const int width = (int)(cols - col0 < TG_COLS ? cols - col0 : TG_COLS);
+  constexpr int PER = VEC ? (int)(16 / sizeof(T)) : 1;
+  const int copies_per_row = (width + PER - 1) / PER;
+  const long long stages = (nparts + TG_HITS - 1) / TG_HITS;
+  auto issue = [&](long long st) {
+    if (st < stages) {
+      T* b = buf + (st % TG_STAGES) * TG_HITS * TG_COLS;
+      const long long q0 = st * TG_HITS;
+      const int nq = (int)(nparts - q0 < TG_HITS ? nparts - q0 : TG_HITS);
+      for (int x = threadIdx.x; x < nq * copies_per_row; x += blockDim.x) {
+        const int h = x / copies_per_row, k = (x - h * copies_per_row) * PER;
+        const T* src = part + (q0 + h) * cols + col0 + k;
+        if (VEC) cp_async16(b + h * TG_COLS + k, src);
+        else cp_async_n<(int)sizeof(T)>(b + h * TG_COLS + k, src);
+      }
+    }
+    cp_async_commit();
+  };
+  for (int st = 0; st < TG_STAGES - 1; ++st) issue(st);
+  T acc = red_init<T>(op);
+  const int lane = threadIdx.x;
+  for (long long st = 0; st < stages; ++st) {
+    issue(st + TG_STAGES - 1);
+    cp_async_wait<TG_STAGES - 1>();
+    __syncthreads();
+    if (threadIdx.x < 32 && lane < width) {
+      const T* b = buf + (st % TG_STAGES) * TG_HITS * TG_COLS;
+      const int nq = (int)(nparts - st * TG_HITS < TG_HITS ? nparts - st * TG_HITS : TG_HITS);
+      for (int h = 0; h < nq; ++h) acc = combine(op, acc, b[h * TG_COLS + lane]);
+    }
+    __syncthreads();
   }
+  cp_async_wait<0>();
+  if (threadIdx.x < width) dst[col0 + threadIdx.x] = acc;
 }
+
 
 template <typename T>
 __global__ void k_reduce_generic(T* __restrict__ dst, const T* __restrict__ a, Red op, Dims kept, Dims red, long long n_out, long long n_red) {
@@ -959,11 +1076,25 @@ void reduce_full_sum(void* dst, const void* src, EType t, long long n, void* scr
 }
 
 template <typename T> static void rows_t(void* dst, const void* src, Red op, long long rows, long long len, cudaStream_t s) {
+  if (op == Red::Sum && len <= 65536) {
+    constexpr int E = (int)(16 / sizeof(T));
+    using VT = typename Vec16<T>::type;
+    if (len % E == 0 && ((uintptr_t)src & 15) == 0)
+      k_rows_fast_sum_vec<T, VT, E><<<grid_for(rows * (8 / E)), 256, 0, s>>>((T*)dst, (const T*)src, rows, len);
+    else
+      k_rows_fast_sum<T><<<grid_for(rows * 8), 256, 0, s>>>((T*)dst, (const T*)src, rows, len);
+    return;
+  }
   if (len > 2048) {
     k_reduce_rows_block<T><<<(unsigned)rows, 1024, 0, s>>>((T*)dst, (const T*)src, op, len);
   } else {
     long long threads = rows * 32;
-    k_reduce_rows_warp<T><<<grid_for(threads), 256, 0, s>>>((T*)dst, (const T*)src, op, rows, len);
+    constexpr int V = (int)(16 / sizeof(T));
+    using VT = typename Vec16<T>::type;
+    if (len % V == 0 && ((uintptr_t)src & 15) == 0)
+      k_reduce_rows_warp_vec<T, VT, V><<<grid_for(threads), 256, 0, s>>>((T*)dst, (const T*)src, op, rows, len);
+    else
+      k_reduce_rows_warp<T><<<grid_for(threads), 256, 0, s>>>((T*)dst, (const T*)src, op, rows, len);
   }
 }
 void reduce_rows(void* dst, const void* src, EType t, Red op, long long rows, long long len, cudaStream_t s) {
@@ -976,16 +1107,41 @@ size_t cols_scratch_bytes(long long rows, long long cols, EType t) {
   return (size_t)((rows + REDUCE_ROWS - 1) / REDUCE_ROWS) * (size_t)cols * esize(t);
 }
 
-template <typename T> static void cols_t(void* dst, const void* src, Red op, long long rows, long long cols, void* scratch, cudaStream_t s) {
+// Every output column sums `nparts` rows of `part` in row order, staged through shared memory.
+template <typename T> static void ordered_cols(void* dst, const T* part, Red op, long long nparts, long long cols, cudaStream_t s) {
+  constexpr int smem = TG_STAGES * TG_HITS * TG_COLS * (int)sizeof(T);
+  const unsigned blocks = (unsigned)((cols + TG_COLS - 1) / TG_COLS);
+  if ((cols * (long long)sizeof(T)) % 16 == 0 && ((uintptr_t)part & 15) == 0) {
+    static bool attr = (cudaFuncSetAttribute(k_cols_final_staged<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), true);
+    (void)attr;
+    k_cols_final_staged<T, true><<<blocks, 256, smem, s>>>((T*)dst, part, op, nparts, cols);
+  } else {
+    static bool attr = (cudaFuncSetAttribute(k_cols_final_staged<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), true);
+    (void)attr;
+    k_cols_final_staged<T, false><<<blocks, 256, smem, s>>>((T*)dst, part, op, nparts, cols);
+  }
+}
+
+// rg reduces a [rows, cols] view over its rows sequentially below its parallel threshold (2^20
+// elements for sums, 2^16 for max/min) and through fixed 64-row partials above it
+// (plan.rs:1549-1612); both orders are kept, so sums are bit-identical.
+template <typename T>
+static void cols_t(void* dst, const void* src, Red op, long long rows, long long cols, bool chunked, void* scratch, cudaStream_t s) {
+  // Max and min do not depend on the order: they always take the partials when large.
+  const bool partials = (chunked || op != Red::Sum) && rows * cols >= (op == Red::Sum ? (1ll << 20) : (1ll << 16));
+  if (!partials) {
+    ordered_cols<T>(dst, (const T*)src, op, rows, cols, s);
+    return;
+  }
   long long parts = (rows + REDUCE_ROWS - 1) / REDUCE_ROWS;
   dim3 grid((unsigned)((cols + 255) / 256), (unsigned)parts);
   k_cols_partial<T><<<grid, 256, 0, s>>>((T*)scratch, (const T*)src, op, rows, cols);
-  k_cols_final<T><<<grid_for(cols), 256, 0, s>>>((T*)dst, (const T*)scratch, op, parts, cols);
+  ordered_cols<T>(dst, (const T*)scratch, op, parts, cols, s);
 }
-void reduce_cols(void* dst, const void* src, EType t, Red op, long long rows, long long cols, void* scratch, cudaStream_t s) {
+void reduce_cols(void* dst, const void* src, EType t, Red op, long long rows, long long cols, bool chunked, void* scratch, cudaStream_t s) {
   if (cols <= 0) return;
-  if (t == EType::F64) cols_t<double>(dst, src, op, rows, cols, scratch, s);
-  else cols_t<float>(dst, src, op, rows, cols, scratch, s);
+  if (t == EType::F64) cols_t<double>(dst, src, op, rows, cols, chunked, scratch, s);
+  else cols_t<float>(dst, src, op, rows, cols, chunked, scratch, s);
 }
 
 void reduce_generic(void* dst, const void* src, EType t, Red op, const Dims& kept, const Dims& reduced, long long n_out, cudaStream_t s) {

@@ -78,10 +78,11 @@ size_t full_sum_scratch_bytes(long long n, EType t);
 void reduce_full_sum(void* dst, const void* src, EType t, long long n, void* scratch, cudaStream_t s);
 // Rows of length `len` reduced to one value each.
 void reduce_rows(void* dst, const void* src, EType t, Red op, long long rows, long long len, cudaStream_t s);
-// [rows, cols] reduced over rows; two passes over fixed 64-row chunks (the chunking of
-// plan.rs:1593-1612), partials in `scratch` (cols_scratch_bytes bytes).
+// [rows, cols] reduced over rows in rg's order: sequentially, or, when `chunked` (rg's own
+// pattern test for its parallel path) and the input reaches rg's parallel threshold, through
+// fixed 64-row partials (plan.rs:1593-1612) kept in `scratch` (cols_scratch_bytes bytes).
 size_t cols_scratch_bytes(long long rows, long long cols, EType t);
-void reduce_cols(void* dst, const void* src, EType t, Red op, long long rows, long long cols, void* scratch, cudaStream_t s);
+void reduce_cols(void* dst, const void* src, EType t, Red op, long long rows, long long cols, bool chunked, void* scratch, cudaStream_t s);
 // Anything else: one output per thread, reduced coordinates walked in row-major order.
 void reduce_generic(void* dst, const void* src, EType t, Red op, const Dims& kept, const Dims& reduced, long long n_out,
                     cudaStream_t s);

@@ -540,9 +540,11 @@ struct Builder {
     }
     if (leading) {
       long long rows = n_red, cols = n_out;
+      // rg's parallel path chunks only when every axis but the last is reduced (plan.rs:1593).
+      const bool chunked = axes.size() + 1 == r && !red[r - 1];
       scratch = std::max(scratch, cols_scratch_bytes(rows, cols, t));
       l.kernels = 2;
-      l.run = [=](Ctx& c) { reduce_cols(c.f->ptr[dst], c.f->ptr[src], t, op, rows, cols, c.f->scratch, c.s); };
+      l.run = [=](Ctx& c) { reduce_cols(c.f->ptr[dst], c.f->ptr[src], t, op, rows, cols, chunked, c.f->scratch, c.s); };
       return l;
     }
     auto st = rg::strides(in_shape);

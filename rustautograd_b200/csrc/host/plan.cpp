@@ -151,6 +151,61 @@ size_t external_inputs(const Graph& g, const std::vector<size_t>& members, const
 
 std::vector<Item> schedule_levels(const Graph& g, const std::vector<bool>& keep, const Fuse& cfg);
 
+// Fuse::hoist_small: tiny elementwise, cast and key-split nodes whose inputs are leaves or
+// themselves hoisted.
+std::vector<bool> hoisted_small(const Graph& g, const std::vector<bool>& keep) {
+  std::vector<bool> up(g.nodes.size(), false);
+  for (size_t i = 0; i < g.nodes.size(); ++i) {
+    const Node& n = g.nodes[i];
+    if (!keep[i] || is_leaf(n) || n.n() > 64) continue;
+    const OpKind k = n.op.kind;
+    bool kind_ok = n.op.is_unary_elementwise() || n.op.is_binary_elementwise() || k == OpKind::Where || k == OpKind::Cast || k == OpKind::KeySplit;
+    if (!kind_ok) continue;
+    bool ready = true;
+    for (auto x : n.inputs) ready = ready && (up[x] || is_leaf(g.nodes[x]));
+    up[i] = ready;
+  }
+  return up;
+}
+
+std::vector<bool> hoisted_for(const Graph& g, const std::vector<bool>& keep, const Fuse& cfg) {
+  if (cfg.gpu && cfg.hoist) return hoisted(g, keep);
+  if (cfg.hoist_small) return hoisted_small(g, keep);
+  return std::vector<bool>(g.nodes.size(), false);
+}
+
+// Emits the hoisted nodes first, in graph order. Under hoist_small, consecutive fusable nodes of
+// one shape and dtype become one group (a scalar chain runs as a single kernel).
+void emit_hoisted(const Graph& g, const std::vector<bool>& up, const Fuse& cfg, std::vector<Item>& items) {
+  std::vector<size_t> open;
+  auto close = [&]() {
+    if (open.size() >= 2) {
+      Item it;
+      it.group = true;
+      it.members = open;
+      items.push_back(std::move(it));
+    } else {
+      for (size_t m : open) items.push_back(Item{false, m, {}});
+    }
+    open.clear();
+  };
+  for (size_t i = 0; i < g.nodes.size(); ++i) {
+    if (!up[i]) continue;
+    const Node& n = g.nodes[i];
+    if (cfg.hoist_small && fusable(g, i, true)) {
+      bool same = open.empty() || (g.nodes[open[0]].shape == n.shape && g.nodes[open[0]].dtype == n.dtype);
+      if (!same || external_inputs(g, open, n) + open.size() + 1 > cfg.max_bindings) close();
+      open.push_back(i);
+    } else {
+      bool reads_open = false;
+      for (auto x : n.inputs) reads_open = reads_open || contains(open, x);
+      if (reads_open) close();
+      items.push_back(Item{false, i, {}});
+    }
+  }
+  close();
+}
+
 // plan.rs:297-350
 std::vector<Item> schedule(const Graph& g, const std::vector<bool>& keep, const Fuse& cfg) {
   if (cfg.gpu && cfg.levels) return schedule_levels(g, keep, cfg);
@@ -169,9 +224,8 @@ std::vector<Item> schedule(const Graph& g, const std::vector<bool>& keep, const 
     }
     open.clear();
   };
-  std::vector<bool> up = (cfg.gpu && cfg.hoist) ? hoisted(g, keep) : std::vector<bool>(g.nodes.size(), false);
-  for (size_t i = 0; i < g.nodes.size(); ++i)
-    if (up[i]) items.push_back(Item{false, i, {}});
+  std::vector<bool> up = hoisted_for(g, keep, cfg);
+  emit_hoisted(g, up, cfg, items);
   for (size_t i = 0; i < g.nodes.size(); ++i) {
     const Node& n = g.nodes[i];
     if (!keep[i] || up[i] || is_leaf(n)) continue;
@@ -193,10 +247,9 @@ std::vector<Item> schedule(const Graph& g, const std::vector<bool>& keep, const 
 
 // plan.rs:352-414: every node gets a dependency level; a level holds one group per shape.
 std::vector<Item> schedule_levels(const Graph& g, const std::vector<bool>& keep, const Fuse& cfg) {
-  std::vector<bool> up = cfg.hoist ? hoisted(g, keep) : std::vector<bool>(g.nodes.size(), false);
+  std::vector<bool> up = hoisted_for(g, keep, cfg);
   std::vector<Item> items;
-  for (size_t i = 0; i < g.nodes.size(); ++i)
-    if (up[i]) items.push_back(Item{false, i, {}});
+  emit_hoisted(g, up, cfg, items);
   auto gpu_fusable = [&](size_t i) { return fusable(g, i, true) && !(cfg.hoist && g.nodes[i].dtype == DType::F64); };
   std::vector<size_t> level(g.nodes.size(), 0);
   std::vector<std::vector<size_t>> by_level;

@@ -22,14 +22,19 @@ struct Fuse {
   bool levels = false;
   bool hoist = false;
   size_t max_bindings = 28;
+  // Schedule tiny (at most 64-element) elementwise chains that depend only on inputs first, so
+  // that a scalar chain (an optimizer's step count and bias corrections) does not push the
+  // tensor ops that read it into a later dependency level and split their fusion group.
+  bool hoist_small = false;
 
-  static Fuse DEFAULT() { return Fuse{200000.0, false, false, false, 28}; }
-  static Fuse METAL() { return Fuse{0.0, true, true, true, 28}; }
+  static Fuse DEFAULT() { return Fuse{200000.0, false, false, false, 28, false}; }
+  static Fuse METAL() { return Fuse{0.0, true, true, true, 28, false}; }
   // The CUDA device's configuration: groups of any cost, in dependency-level order when that
   // is cheaper, with up to 64 bindings per kernel (kernel parameters, not a binding table).
-  static Fuse CUDA() { return Fuse{0.0, true, true, false, 64}; }
+  static Fuse CUDA() { return Fuse{0.0, true, true, false, 64, true}; }
   std::string key() const {
-    return std::to_string(parallel_ns) + (gpu ? "g" : "c") + (levels ? "l" : "n") + (hoist ? "h" : "x") + std::to_string(max_bindings);
+    return std::to_string(parallel_ns) + (gpu ? "g" : "c") + (levels ? "l" : "n") + (hoist ? "h" : "x") + std::to_string(max_bindings) +
+           (hoist_small ? "s" : "");
   }
 };
 

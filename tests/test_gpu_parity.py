@@ -108,6 +108,25 @@ def test_reductions(oracle, axes, kind):
     assert_parity(oracle, fn, (x,), tol=1e-5, exact=kind != "sum")
 
 
+@pytest.mark.parametrize("shape,axis,dtype", [
+    ((8192, 37), 0, "float32"),    # 128 partial rows, element staging
+    ((5000, 64), 0, "float32"),    # 16-byte staging
+    ((4100, 10), 0, "float64"),
+    ((64, 70, 9), (0, 1), "float32"),
+])
+@pytest.mark.parametrize("kind", ["sum", "max", "min"])
+def test_leading_axis_reductions_keep_rgs_order(oracle, shape, axis, dtype, kind):
+    # 64-row partials, then the partials in order: the order of plan.rs:1593-1612, so bit-exact.
+    x = rnd(*shape, seed=41, dtype=dtype)
+    assert_parity(oracle, lambda a: getattr(a, kind)(axis=axis), (x,), exact=True)
+
+
+@pytest.mark.parametrize("shape", [(300, 256), (77, 68), (5, 3, 2048), (33, 4)])
+def test_row_reductions_vector_loads(oracle, shape):
+    x = rnd(*shape, seed=42)
+    assert_parity(oracle, lambda a: (a.sum(axis=-1), a.max(axis=-1), a.min(axis=-1)), (x,), tol=1e-5)
+
+
 def test_small_full_sum_is_bit_exact(oracle):
     # rg's eight-lane fast_sum order, reproduced on the device for small tensors.
     for n in [1, 7, 8, 9, 256, 1000, 4099]:
