@@ -4,9 +4,12 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <stdexcept>
+#include <thread>
 
 #include "rgc.h"
 
@@ -22,6 +25,7 @@ struct Nccl {
   ncclResult_t (*GroupStart)() = nullptr;
   ncclResult_t (*GroupEnd)() = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
 };
 
@@ -29,6 +33,7 @@ std::mutex g_mu;
 Nccl g_nccl;
 ncclComm_t g_comm = nullptr;
 int g_rank = 0, g_world = 1;
+bool g_aborted = false;
 
 void load() {
   if (g_nccl.lib) return;
@@ -48,6 +53,7 @@ void load() {
   g_nccl.GroupStart = (decltype(g_nccl.GroupStart))sym("ncclGroupStart");
   g_nccl.GroupEnd = (decltype(g_nccl.GroupEnd))sym("ncclGroupEnd");
   g_nccl.CommDestroy = (decltype(g_nccl.CommDestroy))sym("ncclCommDestroy");
+  g_nccl.CommAbort = (decltype(g_nccl.CommAbort))sym("ncclCommAbort");
   g_nccl.GetErrorString = (decltype(g_nccl.GetErrorString))sym("ncclGetErrorString");
   g_nccl.lib = lib;
 }
@@ -59,6 +65,7 @@ void nck(ncclResult_t r, const char* what) {
 }  // namespace
 
 bool dist_active() { return g_comm != nullptr && g_world > 1; }
+bool dist_aborted() { return g_aborted; }
 int dist_rank() { return g_rank; }
 int dist_world() { return g_world; }
 
@@ -69,6 +76,39 @@ void dist_all_reduce(void* buf, size_t count, bool is_f64, cudaStream_t stream) 
 
 void dist_all_reduce_into(void* dst, const void* src, size_t count, bool is_f64, cudaStream_t stream) {
   nck(g_nccl.AllReduce(src, dst, count, is_f64 ? ncclFloat64 : ncclFloat32, ncclSum, g_comm, stream), "ncclAllReduce");
+}
+
+cudaError_t dist_sync(cudaStream_t stream, std::string* why) {
+  if (!dist_active()) return cudaStreamSynchronize(stream);
+  double limit = 300.0;
+  if (const char* e = std::getenv("RGC_COLLECTIVE_TIMEOUT_S")) limit = std::atof(e) > 0 ? std::atof(e) : limit;
+  const auto t0 = std::chrono::steady_clock::now();
+  auto pause = std::chrono::microseconds(20);
+  for (;;) {
+    cudaError_t q = cudaStreamQuery(stream);
+    if (q != cudaErrorNotReady) return q;
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > limit) break;
+    std::this_thread::sleep_for(pause);
+    if (pause < std::chrono::milliseconds(2)) pause *= 2;
+  }
+  // A collective has waited past the limit (another rank stopped or diverged): abort the
+  // communicator so that its kernels return, then drain the stream.
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_comm) {
+      g_nccl.CommAbort(g_comm);
+      g_comm = nullptr;
+      g_aborted = true;
+    }
+  }
+  // The aborted collectives return; the drain is bounded as well.
+  const auto t1 = std::chrono::steady_clock::now();
+  while (cudaStreamQuery(stream) == cudaErrorNotReady &&
+         std::chrono::duration<double>(std::chrono::steady_clock::now() - t1).count() < 30.0)
+    std::this_thread::sleep_for(std::chrono::milliseconds(1));
+  cudaGetLastError();
+  if (why) *why = "a collective waited more than " + std::to_string((int)limit) + " s for another rank; the communicator was aborted";
+  return cudaErrorLaunchTimeout;
 }
 
 void dist_group_start() {
@@ -112,6 +152,7 @@ __attribute__((visibility("default"))) int rgc_dist_init(int rank, int world, co
     ncclComm_t comm;
     nck(g_nccl.CommInitRank(&comm, world, u, rank), "ncclCommInitRank");
     g_comm = comm;
+    g_aborted = false;
     g_rank = rank;
     g_world = world;
     return RGC_OK;

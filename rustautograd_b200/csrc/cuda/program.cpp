@@ -763,6 +763,7 @@ std::unique_ptr<Program> make_program(const Plan& plan, int device) {
       Lowered l;
       l.kernels = (int)items.size();
       l.run = [items](Ctx& c) {
+        if (dist_aborted()) throw std::runtime_error("the data-parallel communicator was aborted after a stalled collective");
         if (!dist_active()) {
           for (auto& [src, dst, n, f64] : items)
             ck(cudaMemcpyAsync(c.f->ptr[dst], c.f->ptr[src], n * (f64 ? 8 : 4), cudaMemcpyDeviceToDevice, c.s), "all_reduce copy");
@@ -1057,9 +1058,10 @@ __attribute__((visibility("default"))) int rgc_exec_prefix(rgc_exec* e, size_t s
     if (slot >= plan.slots.size()) return fail(RGC_ERR_INVALID, "slot out of range");
     if (bytes > plan.slots[slot].second * rg::dtype_size(plan.slots[slot].first)) return fail(RGC_ERR_INVALID, "read beyond the slot");
     if (bytes) ck(cudaMemcpyAsync(host, e->f->ptr[slot], bytes, cudaMemcpyDeviceToHost, e->f->stream), "read slot");
-    cudaError_t err = cudaStreamSynchronize(e->f->stream);
+    std::string why;
+    cudaError_t err = dist_sync(e->f->stream, &why);
     if (err != cudaSuccess) {
-      mark_failed(e, cudaGetErrorString(err));
+      mark_failed(e, why.empty() ? std::string(cudaGetErrorString(err)) : why);
       return fail(RGC_ERR_DEVICE, e->f->error);
     }
     return RGC_OK;
@@ -1095,9 +1097,10 @@ __attribute__((visibility("default"))) int rgc_exec_scalar(rgc_exec* e, size_t s
 __attribute__((visibility("default"))) int rgc_exec_failure(rgc_exec* e, char* buf, size_t cap) {
   if (!e || !e->f) return 0;
   if (!e->f->failed) {
-    cudaError_t err = cudaStreamSynchronize(e->f->stream);
+    std::string why;
+    cudaError_t err = dist_sync(e->f->stream, &why);
     if (err == cudaSuccess) err = cudaGetLastError();
-    if (err != cudaSuccess) mark_failed(e, std::string("device error: ") + cudaGetErrorString(err));
+    if (err != cudaSuccess) mark_failed(e, why.empty() ? std::string("device error: ") + cudaGetErrorString(err) : why);
   }
   if (!e->f->failed) check_tc_error(e);
   if (!e->f->failed) return 0;
@@ -1316,9 +1319,10 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
       }
       long long host_ctr[2];
       ck(cudaMemcpyAsync(host_ctr, ctr, sizeof host_ctr, cudaMemcpyDeviceToHost, s), "read counters");
-      cudaError_t err = cudaStreamSynchronize(s);
+      std::string why;
+      cudaError_t err = dist_sync(s, &why);
       if (err != cudaSuccess) {
-        mark_failed(e, std::string("device error: ") + cudaGetErrorString(err));
+        mark_failed(e, why.empty() ? std::string("device error: ") + cudaGetErrorString(err) : why);
         break;
       }
       if (host_ctr[1] >= 0) {

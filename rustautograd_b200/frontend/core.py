@@ -303,11 +303,29 @@ def _first_dtype(args):
     return None
 
 
+class _BodyScope:
+    """A control-flow body being traced: values of enclosing traces it reads become extra body
+    inputs, in first-use order (`captures`: enclosing node -> body input)."""
+
+    def __init__(self, parent, captures=None):
+        self.parent = parent
+        self.captures = dict(captures or {})
+
+
+_body_scopes = {}  # id(body graph) -> _BodyScope
+
+
 def _as_node(g, a, dtype):
     if isinstance(a, Tracer):
         if a._g is g:
             return a._id
-        raise _error("TRACER_LEAK", {"node": a._id}, "tracer_from_a_finished_trace")
+        scope = _body_scopes.get(id(g))
+        if scope is None:
+            raise _error("TRACER_LEAK", {"node": a._id}, "tracer_from_a_finished_trace")
+        outer = _as_node(scope.parent, a, dtype)
+        if outer not in scope.captures:
+            scope.captures[outer] = g.input(list(a.shape), a.dtype, _where_from())
+        return scope.captures[outer]
     if isinstance(a, float) and dtype == "int32" and not a.is_integer():
         raise _error("DTYPE_MISMATCH", {"scalar": a, "tensor_dtype": dtype}, "fractional_scalar_with_int32_tensor_cast_first")
     t = a if isinstance(a, Tensor) else tensor(a, dtype if isinstance(a, (int, float)) else None)
@@ -375,6 +393,184 @@ def take_along_axis(x, idx, axis=-1):
 def concatenate(xs, axis=0):
     xs = list(xs)
     return op("concat", *xs, axis=_axis(xs[0], axis))
+
+
+def _on_last(x, axis, fn):
+    axis = _axis(x, axis)
+    if axis == x.ndim - 1:
+        return fn(x)
+    return swapaxes(fn(swapaxes(x, axis, -1)), axis, -1)
+
+
+def top_k(x, k, axis=-1):
+    """The `k` largest values and their int32 indices, descending; ties keep index order, NaN last."""
+    idx = _on_last(x, axis, lambda v: op("arg_top_k", v, k=k))
+    return take_along_axis(x, idx, axis), idx
+
+
+def argsort(x, axis=-1, descending=False):
+    """Indices that sort `x`: stable, NaN last in both directions."""
+    n = x.shape[_axis(x, axis)]
+    return _on_last(x if descending else -x, axis, lambda v: op("arg_top_k", v, k=n))
+
+
+def sort(x, axis=-1, descending=False):
+    return take_along_axis(x, argsort(x, axis, descending), axis)
+
+
+def cumsum(x, axis=-1):
+    return _on_last(x, axis, lambda v: op("cumsum", v, reverse=False))
+
+
+def argmax(x, axis=-1):
+    """Index of the largest value on `axis` (int32, that axis removed); `axis=None` flattens first."""
+    if axis is None:
+        return op("argmax", x.reshape(-1))
+    axis = _axis(x, axis)
+    return op("argmax", x if axis == x.ndim - 1 else swapaxes(x, axis, -1))
+
+
+# ---- control flow (one graph node each; bodies are traced into their own graphs) ----
+
+def _lift(tree, g):
+    leaves, tdef = flatten(tree)
+    dtype = _first_dtype(leaves) or "float32"
+    return [Tracer(g, _as_node(g, l, dtype)) for l in leaves], tdef
+
+
+def _trace_body(fn, specs, make_args, seed=None):
+    """Traces `fn` into a new graph whose first inputs follow `specs` ((shape, dtype) pairs).
+    Returns (body graph, output ids, output tree, scope with the captured enclosing values)."""
+    body = native().Graph()
+    src = _where_from()
+    args = [Tracer(body, body.input(list(sh), dt, src)) for sh, dt in specs]
+    scope = _BodyScope(_trace_stack[-1])
+    for outer, (sh, dt) in (seed or {}).items():
+        scope.captures[outer] = body.input(list(sh), dt, src)
+    _body_scopes[id(body)] = scope
+    _trace_stack.append(body)
+    try:
+        out = fn(*make_args(args))
+        leaves, tdef = flatten(out)
+        ids = [_as_node(body, l, _first_dtype(leaves) or "float32") for l in leaves]
+    finally:
+        _trace_stack.pop()
+        del _body_scopes[id(body)]
+    return body, ids, tdef, scope
+
+
+def _signature(g, ids):
+    return [(tuple(g.shape(i)), g.dtype(i)) for i in ids]
+
+
+def _shape_mismatch(part, want, got):
+    return _error("CONTROL_FLOW_SHAPE_MISMATCH", {"part": part, "expected": repr(want), "got": repr(got)}, f"{part}_structure_or_shape_changed")
+
+
+def _eagerly(fn, *args):
+    """Control flow outside a trace: compile the call and run it once."""
+    return compile(fn, args, validate="none")(*args)
+
+
+def scan(f, init, xs=None, length=None):
+    """`carry, y = f(carry, x)` over the first axis of `xs` in one graph node (python/rg/_core.py
+    scan). Returns (final carry, stacked ys). `xs=None` needs `length`; `f` then gets None."""
+    if not _trace_stack:
+        if xs is None:
+            return _eagerly(lambda i: scan(f, i, None, length), init)
+        return _eagerly(lambda i, x: scan(f, i, x, length), init, xs)
+    g = _trace_stack[-1]
+    src = _where_from()
+    carry, c_def = _lift(init, g)
+    xl, x_def = _lift(xs, g) if xs is not None else ([], None)
+    lengths = {t.shape[0] if t.ndim else None for t in xl}
+    if length is not None:
+        lengths.add(length)
+    if len(lengths) != 1 or None in lengths:
+        raise _error("CONTROL_FLOW_SHAPE_MISMATCH", {"part": "xs", "lengths": repr(sorted(map(str, lengths)))},
+                     "xs_need_one_shared_first_axis_or_an_explicit_length")
+    n = lengths.pop()
+
+    def make_args(inputs):
+        c = unflatten(c_def, inputs[:len(carry)])
+        x = unflatten(x_def, inputs[len(carry):]) if xs is not None else None
+        return c, x
+
+    specs = [(t.shape, t.dtype) for t in carry] + [(t.shape[1:], t.dtype) for t in xl]
+
+    def body_fn(c, x):
+        out = f(c, x)
+        if not (isinstance(out, tuple) and len(out) == 2):
+            raise _error("CONTROL_FLOW_SHAPE_MISMATCH", {"part": "body", "returned": type(out).__name__}, "scan_body_must_return_carry_and_y")
+        return out[0], (() if out[1] is None else out[1])
+
+    body, ids, out_def, scope = _trace_body(body_fn, specs, make_args)
+    if out_def[1][0] != c_def:
+        raise _shape_mismatch("carry", c_def, out_def[1][0])
+    want = [(t.shape, t.dtype) for t in carry]
+    if _signature(body, ids[:len(carry)]) != want:
+        raise _shape_mismatch("carry", want, _signature(body, ids[:len(carry)]))
+    inputs = [t._id for t in carry] + [t._id for t in xl] + list(scope.captures)
+    node = g.scan(body, ids, len(carry), len(xl), n, inputs, src)
+    final = [Tracer(g, g.output(node, k, list(t.shape), t.dtype)) for k, t in enumerate(carry)]
+    ys = [Tracer(g, g.output(node, len(carry) + k, [n] + list(sh), dt)) for k, (sh, dt) in enumerate(_signature(body, ids[len(carry):]))]
+    return unflatten(c_def, final), (None if out_def[1][1] == ("tuple", ()) else unflatten(out_def[1][1], ys))
+
+
+def while_loop(cond_fn, body_fn, init, max_iterations=100000):
+    """`state = body_fn(state)` while `cond_fn(state)` is nonzero (python/rg/_core.py while_loop).
+    Not differentiable; stops at `max_iterations`."""
+    if not _trace_stack:
+        return _eagerly(lambda i: while_loop(cond_fn, body_fn, i, max_iterations), init)
+    g = _trace_stack[-1]
+    src = _where_from()
+    carry, c_def = _lift(init, g)
+    specs = [(t.shape, t.dtype) for t in carry]
+    make_args = lambda inputs: (unflatten(c_def, inputs[:len(carry)]),)
+    cond_g, cond_ids, _, c_scope = _trace_body(cond_fn, specs, make_args)
+    if len(cond_ids) != 1 or list(cond_g.shape(cond_ids[0])) not in ([], [1]):
+        raise _error("CONTROL_FLOW_SHAPE_MISMATCH", {"part": "condition", "outputs": [cond_g.shape(i) for i in cond_ids]},
+                     "condition_must_be_a_scalar")
+    seen = {o: (tuple(g.shape(o)), g.dtype(o)) for o in c_scope.captures}
+    body, ids, out_def, b_scope = _trace_body(body_fn, specs, make_args, seen)
+    if out_def != c_def:
+        raise _shape_mismatch("state", c_def, out_def)
+    if _signature(body, ids) != [(tuple(s), d) for s, d in specs]:
+        raise _shape_mismatch("state", specs, _signature(body, ids))
+    # The condition takes the same inputs as the body (extra ones unused).
+    for outer in b_scope.captures:
+        if outer not in c_scope.captures:
+            cond_g.input(list(g.shape(outer)), g.dtype(outer), src)
+    inputs = [t._id for t in carry] + list(b_scope.captures)
+    node = g.while_loop(cond_g, cond_ids[0], body, ids, len(carry), max_iterations, inputs, src)
+    return unflatten(c_def, [Tracer(g, g.output(node, k, list(t.shape), t.dtype)) for k, t in enumerate(carry)])
+
+
+def cond(pred, then_fn, else_fn, *args):
+    """Runs only the chosen branch (python/rg/_core.py cond). Differentiable; both branches take
+    `*args` and return the same structure, shapes and dtypes."""
+    if not _trace_stack:
+        return _eagerly(lambda p, *a: cond(p, then_fn, else_fn, *a), pred, *args)
+    g = _trace_stack[-1]
+    src = _where_from()
+    leaves, tdef = _lift(args, g)
+    pid = _as_node(g, pred, _first_dtype([pred]) or "float32")
+    specs = [(t.shape, t.dtype) for t in leaves]
+    make_args = lambda inputs: unflatten(tdef, inputs)
+    then_g, then_ids, then_def, t_scope = _trace_body(then_fn, specs, make_args)
+    seen = {o: (tuple(g.shape(o)), g.dtype(o)) for o in t_scope.captures}
+    else_g, else_ids, else_def, e_scope = _trace_body(else_fn, specs, make_args, seen)
+    if then_def != else_def:
+        raise _shape_mismatch("branches", then_def, else_def)
+    want, got = _signature(then_g, then_ids), _signature(else_g, else_ids)
+    if want != got:
+        raise _shape_mismatch("branches", want, got)
+    for outer in e_scope.captures:
+        if outer not in t_scope.captures:
+            then_g.input(list(g.shape(outer)), g.dtype(outer), src)
+    inputs = [pid] + [t._id for t in leaves] + list(e_scope.captures)
+    node = g.cond(then_g, then_ids, else_g, else_ids, inputs, src)
+    return unflatten(then_def, [Tracer(g, g.output(node, k, list(sh), dt)) for k, (sh, dt) in enumerate(want)])
 
 
 def squeeze(x, axis=None):

@@ -7,7 +7,7 @@ own rows, and scales its loss by the global token count, so that the all-reduced
 the full-batch gradients.
 """
 from . import nn, random
-from .core import all_reduce, arange, take, tree_map, tril, value_and_grad
+from .core import all_reduce, arange, compile, concatenate, run, take, tensor, tree_map, tril, value_and_grad, zeros
 
 
 class GPT:
@@ -74,3 +74,30 @@ def make_train_step(model, opt, batch, world=1, rank=0):
         params, opt_state = opt.update(grads, state["opt"], state["params"])
         return {"params": params, "opt": opt_state, "key": keys[0]}, value
     return step
+
+
+def compile_sampler(model, params, temperature=1.0, top_k=None, top_p=None, device=None):
+    """A compiled step that appends one sampled token to a fixed-length context (examples/gpt.py
+    compile_sampler): `run` then generates with no Python per token."""
+
+    def step(state):
+        k1, k2 = random.split(state["key"])
+        logits = model(params, state["ctx"])[:, -1, :] / temperature
+        if top_k:
+            logits = nn.top_k_logits(logits, top_k)
+        if top_p:
+            logits = nn.top_p_logits(logits, top_p)
+        token = random.categorical(k2, logits)
+        ctx = concatenate([state["ctx"][:, 1:], token[:, None]], axis=1)
+        return {"ctx": ctx, "key": k1}, token[0]
+
+    start = {"ctx": zeros((1, model.block), "int32"), "key": random.key(0)}
+    return compile(step, (start,), validate="basic", device=device)
+
+
+def generate(sampler, block, prompt_ids, n, seed=0):
+    """`n` tokens after `prompt_ids`, left-padded to the fixed context length."""
+    ids = ([prompt_ids[0]] * block + list(prompt_ids))[-block:]
+    state = {"ctx": tensor([ids], "int32"), "key": random.key(seed)}
+    out = run(sampler, state, steps=n)
+    return [int(t) for t in out.history["aux"]]

@@ -8,7 +8,7 @@ masked score matrix.
 import math
 
 from . import random
-from .core import exp, maximum, stop_gradient, swapaxes, take, take_along_axis, tanh, where, zeros, ones
+from .core import argsort, cumsum, exp, maximum, stop_gradient, swapaxes, take, take_along_axis, tanh, top_k, where, zeros, ones
 
 
 def gelu(x):
@@ -32,6 +32,21 @@ def log_softmax(x, axis=-1):
 def softmax(x, axis=-1):
     e = exp(x - stop_gradient(x.max(axis=axis, keepdims=True)))
     return e / e.sum(axis=axis, keepdims=True)
+
+
+def top_k_logits(logits, k):
+    """Keeps the `k` largest logits of the last axis; the rest drop to -1e9 (nn.py:60-63)."""
+    values, _ = top_k(logits, k)
+    return where(logits >= values[..., -1:], logits, -1e9)
+
+
+def top_p_logits(logits, p):
+    """Nucleus filter (nn.py:66-72): keeps the smallest set of top tokens whose probability
+    reaches `p`; a token stays while the probability mass ranked before it is below `p`."""
+    order = argsort(logits, descending=True)
+    probs = softmax(take_along_axis(logits, order))
+    keep_sorted = (cumsum(probs) - probs) < p
+    return where(take_along_axis(keep_sorted, argsort(order.cast(logits.dtype))), logits, -1e9)
 
 
 def cross_entropy(logits, labels, axis=-1):

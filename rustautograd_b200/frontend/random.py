@@ -1,6 +1,6 @@
 """Keyed random numbers (the op compositions of python/rg/random.py): every function is pure
 in its key, so a compiled step that carries its key in its state replays exactly."""
-from .core import floor, op, tensor
+from .core import argmax, floor, log, maximum, op, tensor
 
 
 def key(seed):
@@ -27,3 +27,19 @@ def randint(k, shape, low, high):
     """Uniform int32 in [low, high), drawn in float64 so every integer of the range is reachable."""
     u = op("random_uniform", k, shape=list(shape), dtype="float64")
     return floor(low + (high - low) * u).cast("int32")
+
+
+def bernoulli(k, p=0.5, shape=(), dtype="float32"):
+    """1 with probability `p`, else 0, as floats."""
+    return op("gt", tensor(float(p), dtype), op("random_uniform", k, shape=list(shape), dtype=dtype))
+
+
+def gumbel(k, shape=(), dtype="float32"):
+    u = op("random_uniform", k, shape=list(shape), dtype=dtype)
+    eps = 1e-7 if dtype == "float32" else 1e-15
+    return -log(-log(maximum(u, eps)))
+
+
+def categorical(k, logits, axis=-1):
+    """Indices drawn from unnormalised log-probabilities with the Gumbel-max trick."""
+    return argmax(logits + gumbel(k, logits.shape, logits.dtype), axis)
