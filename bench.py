@@ -11,7 +11,8 @@ all-reduce when N > 1, and the AdamW update.
 
 Other workloads (--config): gpt-d256-l6 (the 1-GPU companion of config 5), gpt-d128-l4
 (config 4), adamw-c2 (config 2: the AdamW update of four large tensors, HBM-bound),
-linreg-c1 (config 1), gemm-mlp (one 131072 x 512 x 2048 product of config 5, for profiling).
+linreg-c1 (config 1), chain-c3 (config 3: matrix chains reordered by the e-graph search),
+gemm-mlp (one 131072 x 512 x 2048 product of config 5, for profiling).
 
 `value` is device time (CUDA events inside the run loop, state already in HBM); `e2e` is the
 same run through the C-ABI run call from host buffers (state and data copied in, state and the
@@ -200,6 +201,57 @@ class Gemm:
         return t * self.m / m, f"one product with {m} of {self.m} rows, scaled x{self.m // m}"
 
 
+class Chain:
+    """value and gradients of sum(A@B@C@D) and sum(x@(U@V)@x^T), compiled with
+    optimize="search-linear" (the e-graph reorders both chains). A step recomputes both losses
+    and all seven gradients; the gradients are the state (replaced every step)."""
+    metric = "matrix-chain steps/sec"
+    bound = "tensor"
+    scalar_output = True
+
+    def __init__(self, name, scale=1):
+        self.name, self.scale = name, scale
+
+    def inputs(self, F, scale=None):
+        s = scale or self.scale
+        n = 4096 // s
+        rng = np.random.default_rng(0)
+        mk = lambda *shape: F.tensor(rng.normal(size=shape).astype("float32"))
+        return [mk(n, 16), mk(16, n), mk(n, 16), mk(16, n), mk(1024 // s, n), mk(n, 32), mk(32, n)]
+
+    @staticmethod
+    def losses(F):
+        f1 = lambda a, b, c, d: (a @ b @ c @ d).sum()
+        f2 = lambda x, u, v: (x @ (u @ v) @ F.swapaxes(x, 0, 1)).sum()
+
+        def step(grads, args):
+            a, b, c, d, x, u, v = args
+            l1, g1 = F.value_and_grad(f1, argnums=(0, 1, 2, 3))(a, b, c, d)
+            l2, g2 = F.value_and_grad(f2, argnums=(0, 1, 2))(x, u, v)
+            return list(g1) + list(g2), l1 + l2
+        return step
+
+    def build(self, F, world=1, rank=0, scale=None):
+        args = self.inputs(F, scale)
+        return self.losses(F), [F.zeros(a.shape) for a in args], args
+
+    def compile_options(self):
+        return {"optimize": "search-linear"}
+
+    def flops(self, batch=None):
+        return 0.0
+
+    def config(self, world):
+        return {"workload": f"{self.name} A(4096,16)@B@C@D and x(1024,4096)@(U@V)@x^T, values and gradients, search-linear",
+                "parallelism": "replicas", "l2": "operands and products larger than L2 (the 4096x4096 output of the first chain)"}
+
+    def cpu_sample(self, F, oracle, budget=15.0):
+        step, state, data = self.build(F, scale=4)
+        c = F.compile(step, (state, data), validate="none", device="cpu", optimize="search-linear")
+        t = F.run(c, state, data, steps=1).elapsed
+        return t * 16, "one step at a quarter of every large dimension (16x fewer multiplications), scaled x16"
+
+
 WORKLOADS = {
     "gpt-d512-l12": Gpt("gpt-d512-l12", vocab=96, block=256, d=512, heads=8, layers=12, batch=512, tokens="zipf"),
     "gpt-d256-l6": Gpt("gpt-d256-l6", vocab=96, block=256, d=256, heads=8, layers=6, batch=64, tokens="zipf"),
@@ -207,6 +259,7 @@ WORKLOADS = {
     "adamw-c2": AdamW("adamw-c2"),
     "linreg-c1": LinReg("linreg-c1"),
     "gemm-mlp": Gemm("gemm-mlp", m=131072, k=512, n=2048),
+    "chain-c3": Chain("chain-c3"),
 }
 
 
@@ -360,7 +413,8 @@ def main():
     step, state, data = w.build(F, world, rank)
     data_arg = data[0] if len(data) == 1 else list(data)
     t0 = time.perf_counter()
-    compiled = F.compile(step, (state, data_arg), validate="none", device="cuda")
+    options = w.compile_options() if hasattr(w, "compile_options") else {}
+    compiled = F.compile(step, (state, data_arg), validate="none", device="cuda", **options)
     compile_s = time.perf_counter() - t0
     n_state = len(F.flatten(state)[0])
     state_leaves = [F.tensor(l)._t for l in F.flatten(state)[0]]

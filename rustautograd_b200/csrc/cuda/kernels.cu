@@ -624,15 +624,17 @@ template <> __device__ __forceinline__ float mac<float, false>(float acc, float 
 template <> __device__ __forceinline__ double mac<double, true>(double acc, double a, double b) { return __dadd_rn(acc, __dmul_rn(a, b)); }
 template <> __device__ __forceinline__ double mac<double, false>(double acc, double a, double b) { return fma(a, b, acc); }
 
-// 64x64 output tile per block, 16-deep k slices through shared memory, 4x4 outputs per thread.
-// Each output has one accumulator and k is visited in ascending order, so the EXACT variant
-// performs rg's additions in rg's order.
+// 64x64 output tile per block, 4x4 outputs per thread, k in 32-deep (f64: 16-deep) slices through
+// two shared-memory buffers: the next slice's elements are loaded into registers while the current one is
+// multiplied, one barrier per slice. Each output has one accumulator and k is visited in
+// ascending order, so the EXACT variant performs rg's additions in rg's order.
 template <typename T, bool EXACT>
 __global__ void __launch_bounds__(256) k_gemm(T* __restrict__ C, const T* __restrict__ A, const T* __restrict__ B, long long m, long long n,
                                               long long k, bool ta, bool tb, GemmBatch bt) {
-  constexpr int BM = 64, BN = 64, BK = 16;
-  __shared__ T As[BK][BM + 4];
-  __shared__ T Bs[BK][BN + 4];
+  constexpr int BM = 64, BN = 64, BK = sizeof(T) == 8 ? 16 : 32;  // two buffers within 48 KB
+  constexpr int LA = BM * BK / 256, LB = BK * BN / 256;         // elements per thread per slice
+  __shared__ T As[2][BK][BM + 4];
+  __shared__ T Bs[2][BK][BN + 4];
   long long z = blockIdx.z, oa = 0, ob = 0;
   {
     long long r = z;
@@ -646,45 +648,68 @@ __global__ void __launch_bounds__(256) k_gemm(T* __restrict__ C, const T* __rest
   const T* Ab = A + oa;
   const T* Bb = B + ob;
   T* Cb = C + z * m * n;
-  long long row0 = (long long)blockIdx.y * BM, col0 = (long long)blockIdx.x * BN;
-  int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const long long row0 = (long long)blockIdx.y * BM, col0 = (long long)blockIdx.x * BN;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  T ra[LA], rb[LB];
+  // Element t of a slice: A tile (i, p) = op(A)[row0 + i][k0 + p], B tile (p, j) = op(B)[k0 + p][col0 + j],
+  // enumerated so that consecutive threads read consecutive addresses.
+  auto load = [&](long long k0) {
+#pragma unroll
+    for (int q = 0; q < LA; ++q) {
+      const int t = threadIdx.x + 256 * q;
+      const int i = ta ? t % BM : t / BK, p = ta ? t / BM : t % BK;
+      const long long gr = row0 + i, gk = k0 + p;
+      ra[q] = (gr < m && gk < k) ? (ta ? Ab[gk * m + gr] : Ab[gr * k + gk]) : (T)0;
+    }
+#pragma unroll
+    for (int q = 0; q < LB; ++q) {
+      const int t = threadIdx.x + 256 * q;
+      const int j = tb ? t / BK : t % BN, p = tb ? t % BK : t / BN;
+      const long long gk = k0 + p, gc = col0 + j;
+      rb[q] = (gk < k && gc < n) ? (tb ? Bb[gc * k + gk] : Bb[gk * n + gc]) : (T)0;
+    }
+  };
+  auto store = [&](int buf) {
+#pragma unroll
+    for (int q = 0; q < LA; ++q) {
+      const int t = threadIdx.x + 256 * q;
+      const int i = ta ? t % BM : t / BK, p = ta ? t / BM : t % BK;
+      As[buf][p][i] = ra[q];
+    }
+#pragma unroll
+    for (int q = 0; q < LB; ++q) {
+      const int t = threadIdx.x + 256 * q;
+      const int j = tb ? t / BK : t % BN, p = tb ? t % BK : t / BN;
+      Bs[buf][p][j] = rb[q];
+    }
+  };
   T acc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = (T)0;
+  load(0);
+  store(0);
+  __syncthreads();
+  int buf = 0;
   for (long long k0 = 0; k0 < k; k0 += BK) {
-    // A tile: BM x BK, element (i, p) = op(A)[row0+i][k0+p]
-    for (int t = threadIdx.x; t < BM * BK; t += 256) {
-      int i, p;
-      if (ta) { p = t / BM; i = t % BM; } else { i = t / BK; p = t % BK; }
-      long long gr = row0 + i, gk = k0 + p;
-      T v = (T)0;
-      if (gr < m && gk < k) v = ta ? Ab[gk * m + gr] : Ab[gr * k + gk];
-      As[p][i] = v;
-    }
-    for (int t = threadIdx.x; t < BK * BN; t += 256) {
-      int p, j;
-      if (tb) { j = t / BK; p = t % BK; } else { p = t / BN; j = t % BN; }
-      long long gk = k0 + p, gc = col0 + j;
-      T v = (T)0;
-      if (gk < k && gc < n) v = tb ? Bb[gc * k + gk] : Bb[gk * n + gc];
-      Bs[p][j] = v;
-    }
-    __syncthreads();
-    long long kmax = k - k0 < BK ? k - k0 : BK;
+    const bool more = k0 + BK < k;
+    if (more) load(k0 + BK);
+    const int kmax = (int)(k - k0 < BK ? k - k0 : BK);
     for (int p = 0; p < kmax; ++p) {
       T av[4], bv[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) av[i] = As[p][ty + 16 * i];
+      for (int i = 0; i < 4; ++i) av[i] = As[buf][p][ty + 16 * i];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) bv[j] = Bs[p][tx + 16 * j];
+      for (int j = 0; j < 4; ++j) bv[j] = Bs[buf][p][tx + 16 * j];
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = mac<T, EXACT>(acc[i][j], av[i], bv[j]);
     }
+    if (more) store(buf ^ 1);
     __syncthreads();
+    buf ^= 1;
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {

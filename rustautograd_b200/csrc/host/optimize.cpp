@@ -15,6 +15,8 @@ constexpr size_t FOLD_LIMIT = 4096;
 constexpr size_t CSE_CONST_LIMIT = 16;
 constexpr size_t REMAT_MIN = size_t(1) << 14;
 constexpr double SEARCH_MIN_GAIN = 0.9;
+// egraph.rs:363: iteration and e-node limits of the search (never a time limit).
+constexpr size_t SEARCH_ITERATIONS = 6, SEARCH_NODES = 20000;
 constexpr size_t COSTLY_REMAT_ABOVE_BYTES = size_t(2) << 30;
 
 // The value of a constant whose elements are all equal (optimize.rs:45-53).
@@ -315,7 +317,7 @@ Json OptStats::json() const {
 OptResult optimize(const Graph& g, const std::vector<uint32_t>& outputs) { return optimize_mode(g, outputs, OptMode::Standard); }
 
 // optimize.rs:210-246
-OptResult optimize_mode(const Graph& g, const std::vector<uint32_t>& outputs, OptMode mode) {
+OptResult optimize_mode(const Graph& g, const std::vector<uint32_t>& outputs, OptMode mode, bool gpu) {
   if (mode == OptMode::Auto) mode = OptMode::Standard;  // compile() resolves Auto before this point
   if (mode == OptMode::None) {
     size_t k = count_kept(g, outputs);
@@ -336,9 +338,12 @@ OptResult optimize_mode(const Graph& g, const std::vector<uint32_t>& outputs, Op
   }
   SearchStats ss;
   std::optional<Simplified> candidate;
-  if (mode != OptMode::SearchExact) {
-    if (auto found = reassociate_products(first.g, first.out, &ss)) candidate = simplify(found->first, found->second, true);
-  }
+  const CostModel& model = gpu ? CostModel::CUDA : CostModel::CPU;
+  const int set = mode == OptMode::Search ? 2 : mode == OptMode::SearchLinear ? 1 : 0;
+  if (auto found = search(first.g, first.out, model, set, SEARCH_ITERATIONS, SEARCH_NODES, &ss)) candidate = simplify(found->first, found->second, true);
+  // Compare final forms: both sides have folded constants and flagged transposes.
+  ss.cost_before = model.graph_cost(baseline.g, baseline.out);
+  ss.cost_after = candidate ? model.graph_cost(candidate->g, candidate->out) : ss.cost_before;
   ss.accepted = candidate.has_value() && ss.cost_after < ss.cost_before * SEARCH_MIN_GAIN;
   Simplified& chosen = ss.accepted ? *candidate : baseline;
   chosen.st.nodes_before = before;

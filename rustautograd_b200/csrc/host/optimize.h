@@ -31,11 +31,23 @@ struct OptResult {
 };
 
 OptResult optimize(const Graph& g, const std::vector<uint32_t>& outputs);
-OptResult optimize_mode(const Graph& g, const std::vector<uint32_t>& outputs, OptMode mode);
+// `gpu` selects the GPU cost model for the search modes (rg: the Metal model on its GPU).
+OptResult optimize_mode(const Graph& g, const std::vector<uint32_t>& outputs, OptMode mode, bool gpu = false);
 bool has_matrix_structure(const Graph& g, const std::vector<uint32_t>& outputs);
 
-// Matrix-product reassociation for `search-linear` (the Linear rule set of egraph.rs:148-157,
-// restricted to chains of plain products): returns a cheaper equivalent graph, if any.
-std::optional<std::pair<Graph, std::vector<uint32_t>>> reassociate_products(const Graph& g, const std::vector<uint32_t>& outputs, SearchStats* st);
+// Estimated nanoseconds per node (egraph.rs:170-233); only ratios matter.
+struct CostModel {
+  double per_op, per_element, per_flop, per_math_element, per_transpose_element;
+  static const CostModel CPU, METAL, CUDA;
+  double node(const Op& op, const std::vector<size_t>& shape, const std::vector<const std::vector<size_t>*>& args) const;
+  // Whole-graph cost, shared values counted once; nodes whose inputs are all constants are free.
+  double graph_cost(const Graph& g, const std::vector<uint32_t>& outputs) const;
+};
+
+// Equality saturation (egraph.rs:367-427): a cheaper graph computing the same outputs under the
+// rule set (0 exact, 1 linear: + matrix-product reassociation and factoring, 2 rounding: +
+// elementwise associativity and distribution), if the search finds one.
+std::optional<std::pair<Graph, std::vector<uint32_t>>> search(const Graph& g, const std::vector<uint32_t>& outputs, const CostModel& model,
+                                                              int rule_set, size_t iter_limit, size_t node_limit, SearchStats* st);
 
 }  // namespace rg

@@ -430,5 +430,22 @@ PYBIND11_MODULE(RG_MODULE_NAME, m) {
   }, py::arg("graph"), py::arg("outputs"), py::arg("examples"), py::arg("level"), py::arg("device"), py::arg("optimize"));
 
   m.def("available_devices", [] { return module_available_devices(); });
+  // Not in rg's module: the equality-saturation search on its own (the unit rg's engine tests
+  // exercise), returning (graph, outputs, stats) or None. model: "cpu" | "metal" | "cuda";
+  // rule_set: 0 exact, 1 linear, 2 rounding.
+  m.def("_egraph_search", [](const PyGraph& graph, std::vector<uint32_t> outputs, const std::string& model, int rule_set, size_t iterations,
+                             size_t nodes) -> py::object {
+    const CostModel& cm = model == "metal" ? CostModel::METAL : model == "cuda" ? CostModel::CUDA : CostModel::CPU;
+    SearchStats st;
+    auto found = search(graph.g, outputs, cm, rule_set, iterations, nodes, &st);
+    if (!found) return py::none();
+    py::dict stats;
+    stats["iterations"] = st.iterations;
+    stats["egraph_nodes"] = st.egraph_nodes;
+    stats["cost_before"] = cm.graph_cost(graph.g, outputs);
+    stats["cost_after"] = cm.graph_cost(found->first, found->second);
+    PyGraph out{std::move(found->first)};
+    return py::make_tuple(py::cast(std::move(out)), found->second, stats);
+  });
   module_extra(m);
 }

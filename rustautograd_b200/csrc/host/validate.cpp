@@ -418,7 +418,7 @@ Json Compiled::optimizer_check(const std::vector<Tensor>& examples) const {
   for (auto& t : examples) inputs.push_back(as_f64(t));
   std::vector<const Tensor*> ptrs;
   for (auto& t : inputs) ptrs.push_back(&t);
-  OptResult opt = optimize_mode(shadow, outputs, mode);
+  OptResult opt = optimize_mode(shadow, outputs, mode, device->fuse().gpu);
   auto fast = run_once(*device, Plan::build_fused(opt.graph, opt.outputs, device->fuse()), ptrs);
   auto reference = run_once(*device, Plan::build(shadow, outputs, false), ptrs);
   double max_rel = 0;
@@ -460,7 +460,7 @@ std::pair<Json, std::vector<Json>> Compiled::device_check(const std::vector<Tens
     s["skipped"] = "no_cpu_reference_in_this_process";
     return {s, diags};
   }
-  OptResult opt = optimize_mode(raw, outputs, mode);
+  OptResult opt = optimize_mode(raw, outputs, mode, device->fuse().gpu);
   Plan cpu_plan = Plan::build_fused(opt.graph, opt.outputs, Fuse::DEFAULT());
   std::vector<Tensor> cpu = g_reference(cpu_plan, examples);
   std::vector<Tensor> gpu;
@@ -844,7 +844,7 @@ namespace {
 std::unique_ptr<Compiled> build(const Graph& raw, const std::vector<uint32_t>& outputs, const std::vector<Tensor>& examples, Level level,
                                 std::shared_ptr<Device> device, OptMode mode) {
   auto c = std::make_unique<Compiled>();
-  OptResult opt = optimize_mode(raw, outputs, mode);
+  OptResult opt = optimize_mode(raw, outputs, mode, device->fuse().gpu);
   c->plan = Plan::build_fused(opt.graph, opt.outputs, device->fuse());
   try {
     c->program = device->compile(c->plan);

@@ -271,3 +271,116 @@ def test_device_switch_reports_unknown_devices(oracle):  # python.rs:268-277
         m.compile(g, [x], [T(m, [2], [1, 2], "float32")], "none", "metal", "standard")
     assert e.value.diagnostic["code"] == "DEVICE_UNAVAILABLE"
     assert e.value.diagnostic["observation"]["available"] == ["cpu"]
+
+
+# ---- equality saturation (tests/engine.rs:1357-1460) ----
+
+def _eval_graph(m, g, outs, inputs):
+    c = m.compile(g, list(outs), inputs, "none", "cpu", "none")
+    return [np.frombuffer(t.tobytes(), dtype=t.dtype) for t in c.call(inputs)]
+
+
+def _chain(m, sizes):
+    g = m.Graph()
+    ids, inputs = [], []
+    for a, b in zip(sizes[:-1], sizes[1:]):
+        ids.append(g.input([a, b], "float64"))
+        inputs.append(T(m, (a, b), np.sin(np.arange(a * b) * 0.31)))
+    v = ids[0]
+    for x in ids[1:]:
+        v = g.op("matmul", [v, x])
+    return g, v, inputs
+
+
+def _optimal_chain_flops(d):
+    n = len(d) - 1
+    best = [[0.0] * n for _ in range(n)]
+    for length in range(2, n + 1):
+        for i in range(n - length + 1):
+            j = i + length - 1
+            best[i][j] = min(best[i][k] + best[k + 1][j] + d[i] * d[k + 1] * d[j + 1] for k in range(i, j))
+    return best[0][n - 1]
+
+
+def _matmul_flops(g, out):
+    nodes = json.loads(g._describe())
+    keep, stack = set(), [out]
+    while stack:
+        i = stack.pop()
+        if i not in keep:
+            keep.add(i)
+            stack.extend(nodes[i]["inputs"])
+    total = 0
+    for i in keep:
+        n = nodes[i]
+        if n["op"] == "matmul":
+            a, b = nodes[n["inputs"][0]]["shape"], nodes[n["inputs"][1]]["shape"]
+            total += int(np.prod(a)) * b[1]
+    return total
+
+
+@pytest.mark.parametrize("sizes", [[30, 35, 15, 5, 10, 20, 25], [1024, 8, 1024, 8, 1024], [4, 300, 2, 500, 3, 200, 6], [10, 20, 30, 40, 30]])
+def test_saturation_finds_the_optimal_matrix_chain_order(oracle, sizes):  # engine.rs:1393-1412
+    g, out, inputs = _chain(oracle, sizes)
+    found = oracle._egraph_search(g, [out], "cpu", 2, 12, 50000)
+    h, ids, _ = found if found else (g, [out], None)
+    assert _matmul_flops(h, ids[0]) <= _optimal_chain_flops(sizes) * 1.01
+    a, b = _eval_graph(oracle, h, ids, inputs)[0], _eval_graph(oracle, g, [out], inputs)[0]
+    assert np.max(np.abs(a - b)) <= 1e-9 * max(1.0, np.abs(b).max())
+
+
+def test_saturation_factors_common_terms_and_rejects_shape_changes(oracle):  # engine.rs:1414-1438
+    g = oracle.Graph()
+    a, b, c = (g.input([64, 64], "float64") for _ in range(3))
+    s = g.op("add", [g.op("matmul", [a, b]), g.op("matmul", [a, c])])
+    h, ids, _ = oracle._egraph_search(g, [s], "cpu", 2, 6, 20000)
+    assert sum(1 for n in json.loads(h._describe()) if n["op"] == "matmul") == 1
+    v = lambda k: T(oracle, (64, 64), np.sin(np.arange(4096) * k * 0.01))
+    x, y, z = v(1), v(2), v(3)
+    np.testing.assert_allclose(_eval_graph(oracle, h, ids, [x, y, z])[0], _eval_graph(oracle, g, [s], [x, y, z])[0], atol=1e-9)
+    # a * (b + c) with broadcasting: factoring [3] and [2, 3] operands must keep the [2, 3] shape.
+    g = oracle.Graph()
+    a, b, c = g.input([3], "float64"), g.input([3], "float64"), g.input([2, 3], "float64")
+    s = g.op("add", [g.op("mul", [a, b]), g.op("mul", [a, c])])
+    found = oracle._egraph_search(g, [s], "cpu", 2, 6, 20000)
+    h, ids, _ = found if found else (g, [s], None)
+    assert json.loads(h._describe())[ids[0]]["shape"] == [2, 3]
+
+
+def test_exact_rules_never_change_a_bit_on_special_values(oracle):  # engine.rs:1440-1460
+    sp = [0.0, -0.0, 1.0, -1.5, 1e300, -1e300, np.inf, -np.inf, np.nan, 1e-300]
+    n = len(sp)
+    ta = T(oracle, (n * n,), np.repeat(sp, n))
+    tb = T(oracle, (n * n,), np.tile(sp, n))
+    g = oracle.Graph()
+    x, y = g.input([n * n], "float64"), g.input([n * n], "float64")
+    nx = g.op("neg", [x])
+    outs = [g.op("sub", [g.op("neg", [nx]), y]), g.op("mul", [nx, y]), g.op("div", [nx, y]), g.op("add", [y, x])]
+    h, ids, _ = oracle._egraph_search(g, outs, "cpu", 0, 6, 20000)
+    want, got = _eval_graph(oracle, g, outs, [ta, tb]), _eval_graph(oracle, h, ids, [ta, tb])
+    for u, v in zip(want, got):
+        same = (u.view(np.int64) == v.view(np.int64)) | (np.isnan(u) & np.isnan(v))
+        assert same.all()
+
+
+def test_search_linear_reorders_the_config3_chains(oracle):
+    """BASELINE config 3 at a quarter scale: `optimize="search-linear"` reorders A@B@C@D and
+    x@(U@V)@x^T (forward and gradients) to far fewer multiplications, and the values stay within
+    1e-4 of the plan as written."""
+    from rustautograd_b200 import frontend as F
+    F.use(oracle, "cpu")
+    rng = np.random.default_rng(0)
+    n = 1024
+    mk = lambda *s: F.tensor(rng.normal(size=s).astype("float32"))
+    A, B, C, D = mk(n, 16), mk(16, n), mk(n, 16), mk(16, n)
+    x, U, V = mk(256, n), mk(n, 32), mk(32, n)
+    cases = [(lambda a, b, c, d: (a @ b @ c @ d).sum(), (A, B, C, D)), (lambda x, u, v: (x @ (u @ v) @ F.swapaxes(x, 0, 1)).sum(), (x, U, V))]
+    for fn, args in cases:
+        g = lambda *a: F.value_and_grad(fn, argnums=tuple(range(len(a))))(*a)
+        opt = F.compile(g, args, validate="none", device="cpu", optimize="search-linear")
+        std = F.compile(g, args, validate="none", device="cpu", optimize="standard")
+        search = opt.report["graph"]["optimization"]["search"]
+        assert search["accepted"] and search["cost_after"] < 0.5 * search["cost_before"], search
+        for u, w in zip(F.tree_leaves(opt(*args)), F.tree_leaves(std(*args))):
+            u, w = np.asarray(u.numpy(), np.float64), np.asarray(w.numpy(), np.float64)
+            assert np.abs(u - w).max() <= 1e-4 * np.abs(w).max()
