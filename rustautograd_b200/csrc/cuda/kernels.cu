@@ -628,11 +628,13 @@ template <> __device__ __forceinline__ double mac<double, false>(double acc, dou
 // two shared-memory buffers: the next slice's elements are loaded into registers while the current one is
 // multiplied, one barrier per slice. Each output has one accumulator and k is visited in
 // ascending order, so the EXACT variant performs rg's additions in rg's order.
-template <typename T, bool EXACT>
+template <typename T, bool EXACT, int TILE>
 __global__ void __launch_bounds__(256) k_gemm(T* __restrict__ C, const T* __restrict__ A, const T* __restrict__ B, long long m, long long n,
                                               long long k, bool ta, bool tb, GemmBatch bt) {
-  constexpr int BM = 64, BN = 64, BK = sizeof(T) == 8 ? 16 : 32;  // two buffers within 48 KB
-  constexpr int LA = BM * BK / 256, LB = BK * BN / 256;         // elements per thread per slice
+  // TILE 64: 4x4 outputs per thread; TILE 16 (small outputs, usually long k): one per thread.
+  constexpr int BM = TILE, BN = TILE, R = TILE / 16;
+  constexpr int BK = TILE == 16 ? 64 : (sizeof(T) == 8 ? 16 : 32);  // two buffers within 48 KB
+  constexpr int LA = BM * BK / 256, LB = BK * BN / 256;             // elements per thread per slice
   __shared__ T As[2][BK][BM + 4];
   __shared__ T Bs[2][BK][BN + 4];
   long long z = blockIdx.z, oa = 0, ob = 0;
@@ -683,11 +685,11 @@ __global__ void __launch_bounds__(256) k_gemm(T* __restrict__ C, const T* __rest
       Bs[buf][p][j] = rb[q];
     }
   };
-  T acc[4][4];
+  T acc[R][R];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < R; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = (T)0;
+    for (int j = 0; j < R; ++j) acc[i][j] = (T)0;
   load(0);
   store(0);
   __syncthreads();
@@ -697,26 +699,26 @@ __global__ void __launch_bounds__(256) k_gemm(T* __restrict__ C, const T* __rest
     if (more) load(k0 + BK);
     const int kmax = (int)(k - k0 < BK ? k - k0 : BK);
     for (int p = 0; p < kmax; ++p) {
-      T av[4], bv[4];
+      T av[R], bv[R];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) av[i] = As[buf][p][ty + 16 * i];
+      for (int i = 0; i < R; ++i) av[i] = As[buf][p][ty + 16 * i];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) bv[j] = Bs[buf][p][tx + 16 * j];
+      for (int j = 0; j < R; ++j) bv[j] = Bs[buf][p][tx + 16 * j];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < R; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = mac<T, EXACT>(acc[i][j], av[i], bv[j]);
+        for (int j = 0; j < R; ++j) acc[i][j] = mac<T, EXACT>(acc[i][j], av[i], bv[j]);
     }
     if (more) store(buf ^ 1);
     __syncthreads();
     buf ^= 1;
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < R; ++i) {
     long long r = row0 + ty + 16 * i;
     if (r >= m) continue;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < R; ++j) {
       long long c = col0 + tx + 16 * j;
       if (c < n) Cb[r * n + c] = acc[i][j];
     }
@@ -1184,13 +1186,19 @@ void gemm(void* c, const void* a, const void* b, EType t, long long m, long long
     cudaMemsetAsync(c, 0, (size_t)(m * n * count) * esize(t), s);
     return;
   }
-  dim3 grid((unsigned)((n + 63) / 64), (unsigned)((m + 63) / 64), (unsigned)count);
+  // 16x16 tiles (one output per thread) when 64x64 tiles would not fill the GPU once.
+  const bool small = ((n + 63) / 64) * ((m + 63) / 64) * count < sm_count();
+  const long long tile = small ? 16 : 64;
+  dim3 grid((unsigned)((n + tile - 1) / tile), (unsigned)((m + tile - 1) / tile), (unsigned)count);
+  auto run = [&](auto kernel, auto* cc, auto* aa, auto* bb) { kernel<<<grid, 256, 0, s>>>(cc, aa, bb, m, n, k, ta, tb, batch); };
   if (t == EType::F64) {
-    if (exact) k_gemm<double, true><<<grid, 256, 0, s>>>((double*)c, (const double*)a, (const double*)b, m, n, k, ta, tb, batch);
-    else k_gemm<double, false><<<grid, 256, 0, s>>>((double*)c, (const double*)a, (const double*)b, m, n, k, ta, tb, batch);
+    auto *cc = (double*)c, *aa = (double*)a, *bb = (double*)b;
+    if (small) exact ? run(k_gemm<double, true, 16>, cc, aa, bb) : run(k_gemm<double, false, 16>, cc, aa, bb);
+    else exact ? run(k_gemm<double, true, 64>, cc, aa, bb) : run(k_gemm<double, false, 64>, cc, aa, bb);
   } else {
-    if (exact) k_gemm<float, true><<<grid, 256, 0, s>>>((float*)c, (const float*)a, (const float*)b, m, n, k, ta, tb, batch);
-    else k_gemm<float, false><<<grid, 256, 0, s>>>((float*)c, (const float*)a, (const float*)b, m, n, k, ta, tb, batch);
+    auto *cc = (float*)c, *aa = (float*)a, *bb = (float*)b;
+    if (small) exact ? run(k_gemm<float, true, 16>, cc, aa, bb) : run(k_gemm<float, false, 16>, cc, aa, bb);
+    else exact ? run(k_gemm<float, true, 64>, cc, aa, bb) : run(k_gemm<float, false, 64>, cc, aa, bb);
   }
 }
 

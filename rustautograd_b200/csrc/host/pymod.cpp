@@ -430,6 +430,35 @@ PYBIND11_MODULE(RG_MODULE_NAME, m) {
   }, py::arg("graph"), py::arg("outputs"), py::arg("examples"), py::arg("level"), py::arg("device"), py::arg("optimize"));
 
   m.def("available_devices", [] { return module_available_devices(); });
+  // Not in rg's module: the CPU interpreter validate's device check compares a GPU against
+  // (validate.rs:674-705). rg links its own; this module has none and takes one from the
+  // embedding process: fn(plan blob bytes, [(bytes, shape, dtype)]) -> [(bytes, shape, dtype)].
+  // None removes it (the check then reports itself skipped).
+  m.def("_set_reference_runner", [](py::object fn) {
+    if (fn.is_none()) {
+      set_reference_runner(nullptr);
+      return;
+    }
+    auto holder = std::shared_ptr<py::object>(new py::object(fn), [](py::object* o) {
+      if (Py_IsInitialized()) {
+        py::gil_scoped_acquire gil;
+        delete o;
+      }
+    });
+    set_reference_runner([holder](const Plan& plan, const std::vector<Tensor>& inputs) {
+      py::gil_scoped_acquire gil;
+      auto blob = encode_plan(plan);
+      py::list ins;
+      for (auto& t : inputs) ins.append(py::make_tuple(py::bytes((const char*)t.data.data(), t.data.bytes()), t.shape, std::string(dtype_name(t.dtype()))));
+      py::object res = (*holder)(py::bytes((const char*)blob.data(), blob.size()), ins);
+      std::vector<Tensor> out;
+      for (auto item : res) {
+        auto tup = item.cast<py::tuple>();
+        out.push_back(*make_tensor(tup[0].cast<py::bytes>(), tup[1].cast<std::vector<size_t>>(), tup[2].cast<std::string>()).t);
+      }
+      return out;
+    });
+  });
   // Not in rg's module: the equality-saturation search on its own (the unit rg's engine tests
   // exercise), returning (graph, outputs, stats) or None. model: "cpu" | "metal" | "cuda";
   // rule_set: 0 exact, 1 linear, 2 rounding.

@@ -664,12 +664,13 @@ def value_and_grad(f, argnums=0):
 class Compiled:
     """An executable plan plus its compile report."""
 
-    def __init__(self, handle, in_def, in_sig, out_def, n_out):
+    def __init__(self, handle, in_def, in_sig, out_def, n_out, extras=()):
         self._n = handle
         self._in_def = in_def
         self._in_sig = in_sig
         self._out_def = out_def
         self._n_out = n_out
+        self._extras = list(extras)  # names of the observe=True instrument outputs after the outputs
         self.report = json.loads(handle.report_json)
 
     def _inputs(self, args):
@@ -687,8 +688,48 @@ class Compiled:
         return self._n.plan_blob()
 
 
-def compile(fn, example_inputs, validate="standard", device=None, optimize="search-linear"):
-    """Traces `fn(*example_inputs)` and compiles it for `device` (default: the module's first)."""
+def _instruments(g, in_def, inputs, out_leaves, out_def):
+    """observe=True statistics as (name, node) pairs (python/rg/_core.py _instruments): per
+    differentiated input the gradient's norm, largest magnitude and zero fraction, the global
+    gradient norm, and, when the step returns its new state, each parameter's relative update."""
+    names = {t._id: n for t, n in zip(inputs, _paths(in_def, ""))}
+    latest = {}
+    for _, wrt, grad_id in g.grad_records():
+        if wrt in names:
+            latest[wrt] = grad_id
+    extras, total = [], 0.0
+    for wrt, grad_id in latest.items():
+        name = names[wrt].lstrip(".")
+        name = name[2:] if name.startswith("0.") else name
+        gr = Tracer(g, grad_id)
+        squared = (gr * gr).sum()
+        total = total + squared
+        extras.append((f"grad.{name}.norm", squared.sqrt()))
+        extras.append((f"grad.{name}.max", abs(gr).max()))
+        extras.append((f"grad.{name}.zero", (0.0 >= abs(gr)).sum() / max(1, gr.size)))
+    if latest:
+        extras.append(("grad.global_norm", total.sqrt()))
+    state_def = in_def[1][0] if in_def and in_def[0] == "tuple" and in_def[1] else None
+    n_state = len(_paths(state_def, "")) if state_def is not None else 0
+    returns_state = state_def is not None and (out_def == state_def or (out_def is not None and out_def[0] == "tuple" and len(out_def[1]) == 2
+                                                                          and out_def[1][0] == state_def))
+    if returns_state:
+        for old, new in zip(inputs[:n_state], out_leaves[:n_state]):
+            if old._id in latest and isinstance(new, Tracer):
+                name = names[old._id].lstrip(".")
+                name = name[2:] if name.startswith("0.") else name
+                d = new - old
+                size_now = (old * old).sum().sqrt()
+                # A parameter at exactly zero records 0, not a huge ratio (and not NaN, which
+                # would stop `run`).
+                extras.append((f"update.{name}", where(size_now > 0.0, (d * d).sum().sqrt() / where(size_now > 0.0, size_now, 1.0), 0.0)))
+    return [(n, _as_node(g, v, "float32")) for n, v in extras]
+
+
+def compile(fn, example_inputs, validate="standard", device=None, optimize="search-linear", observe=False):
+    """Traces `fn(*example_inputs)` and compiles it for `device` (default: the module's first).
+    `observe=True` adds per-parameter gradient and update statistics as extra outputs, computed
+    in the plan on the device; `run` records them in its history."""
     if not isinstance(example_inputs, tuple):
         example_inputs = (example_inputs,)
     leaves, in_def = flatten(example_inputs)
@@ -702,10 +743,11 @@ def compile(fn, example_inputs, validate="standard", device=None, optimize="sear
         out_leaves, out_def = flatten(out)
         dtype = _first_dtype(leaves) or "float32"
         out_ids = [_as_node(g, l, dtype) for l in out_leaves]
+        extras = _instruments(g, in_def, tracers, out_leaves, out_def) if observe else []
     finally:
         _trace_stack.pop()
-    handle = native().compile(g, out_ids, [t._t for t in leaves], validate, device or default_device(), optimize)
-    return Compiled(handle, in_def, [(t.shape, t.dtype) for t in leaves], out_def, len(out_ids))
+    handle = native().compile(g, out_ids + [i for _, i in extras], [t._t for t in leaves], validate, device or default_device(), optimize)
+    return Compiled(handle, in_def, [(t.shape, t.dtype) for t in leaves], out_def, len(out_ids), [n for n, _ in extras])
 
 
 class RunResult:
@@ -729,6 +771,9 @@ def run(compiled, state, data=None, steps=1):
     shapes = compiled._n.output_shapes
     scalar = [k for k in range(n_state, n_state + len(aux_names)) if all(x == 1 for x in shapes[k])]
     names = {k: aux_names[k - n_state] for k in scalar}
+    for j, name in enumerate(compiled._extras):
+        scalar.append(compiled._n_out + j)
+        names[compiled._n_out + j] = name
     state_map = [(k, k) for k in range(n_state)]
     data_inputs = list(range(n_state, len(compiled._in_sig)))
     new_state, outputs, hist, ran, bad, seconds = compiled._n.run(state_map, data_inputs, scalar, [t._t for t in leaves], batches, steps)
