@@ -20,6 +20,7 @@
  *   rgc_exec_scalar             plan.rs:36            `Exec::scalar`
  *   rgc_exec_failure            plan.rs:38-40         `Exec::failure`
  *   rgc_exec_run                validate.rs:290-363   `run_loop`, kept on the device (no host sync per step)
+ *   rgc_exec_step_checked       validate.rs:132-230   the non-finite observer's per-step scan, on the device
  *   rgc_exec_step_timed         metal.rs:692-700      `step_timed`
  *   rgc_exec_breakdown_json     metal.rs:701-712      `breakdown`
  *   rgc_dist_*                  (new) data-parallel communicator for the gradient all-reduce step
@@ -101,6 +102,13 @@ typedef struct {
 int rgc_exec_run(rgc_exec* e, const rgc_run_spec* spec, const void* const* state, const void* const* batches,
                  size_t n_batches, size_t steps, double* history, void* const* outputs, const size_t* output_bytes,
                  size_t* steps_done, int64_t* nonfinite_step, double* seconds);
+
+/* One step with a check after every plan step, for validate's non-finite observer
+ * (validate.rs:132-230) on large plans: flags[k] = 1 when plan step k produced a non-finite
+ * value (every float output of the step, fused groups included), flags[n + k] = 1 when an index
+ * read by step k (take, take_along) lay outside its axis; n = number of plan steps, the array
+ * holds 2n entries. */
+int rgc_exec_step_checked(rgc_exec* e, int32_t* flags, size_t n_flags);
 
 /* Per-step device seconds, accumulated into seconds[n_steps] (metal.rs:692-700). */
 int rgc_exec_step_timed(rgc_exec* e, double* seconds, size_t n_steps);

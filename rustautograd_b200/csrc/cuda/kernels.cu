@@ -885,6 +885,12 @@ __global__ void k_load_batch(char* dst, const char* batches, size_t bytes, long 
   GRID_STRIDE(i, (long long)bytes) { dst[i] = src[i]; }
 }
 
+__global__ void k_index_outside(const int32_t* idx, long long n, long long dim, int* flag) {
+  GRID_STRIDE(i, n) {
+    if (idx[i] < 0 || idx[i] >= dim) *flag = 1;
+  }
+}
+
 template <typename T> __global__ void k_nonfinite(const T* a, long long n, int* flag) {
   GRID_STRIDE(i, n) {
     if (!isfinite(a[i])) *flag = 1;
@@ -1259,6 +1265,11 @@ void bump_counter(long long* counter, cudaStream_t s) { k_bump<<<1, 1, 0, s>>>(c
 
 void load_batch(void* dst, const void* batches, size_t bytes, long long n_batches, const long long* counter, cudaStream_t s) {
   k_load_batch<<<grid_for((long long)bytes), 256, 0, s>>>((char*)dst, (const char*)batches, bytes, n_batches, counter);
+}
+
+void index_outside(const int32_t* idx, long long n, long long dim, int* flag, cudaStream_t s) {
+  if (n <= 0) return;
+  k_index_outside<<<grid_for(n), 256, 0, s>>>(idx, n, dim, flag);
 }
 
 void any_nonfinite(const void* src, EType t, long long n, int* flag, cudaStream_t s) {

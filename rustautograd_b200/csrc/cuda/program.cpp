@@ -1371,6 +1371,56 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
   });
 }
 
+__attribute__((visibility("default"))) int rgc_exec_step_checked(rgc_exec* e, int32_t* flags, size_t n_flags) {
+  return guard([&] {
+    if (e->f->failed) return fail(RGC_ERR_DEVICE, e->f->error);
+    Program* p = e->owner->p.get();
+    const Plan& plan = p->plan;
+    const size_t n = plan.steps.size();
+    if (!flags || n_flags < 2 * n) return fail(RGC_ERR_INVALID, "flags array shorter than twice the plan's steps");
+    cudaStream_t s = e->f->stream;
+    int* dflags = nullptr;
+    ck(cudaMallocAsync((void**)&dflags, std::max<size_t>(1, 2 * n) * sizeof(int), s), "cudaMallocAsync(check flags)");
+    ck(cudaMemsetAsync(dflags, 0, std::max<size_t>(1, 2 * n) * sizeof(int), s), "cudaMemsetAsync(check flags)");
+    Ctx c{s, e->f.get()};
+    auto check = [&](size_t slot, size_t count, int* flag) {
+      DType d = plan.slots[slot].first;
+      if (d != DType::I32 && count) any_nonfinite(e->f->ptr[slot], et(d), (long long)count, flag, s);
+    };
+    for (size_t k = 0; k < n; ++k) {
+      const rg::Step& st = plan.steps[k];
+      if (!st.fused && (st.instr.op.kind == OpKind::Take || st.instr.op.kind == OpKind::TakeAlong)) {
+        const Instr& i = st.instr;
+        const size_t dim = i.op.kind == OpKind::Take ? i.arg_shapes[0][i.op.index] : i.arg_shapes[0].back();
+        index_outside((const int32_t*)e->f->ptr[i.args[1]], (long long)rg::product(i.arg_shapes[1]), (long long)dim, dflags + n + k, s);
+      }
+      p->steps[k].run(c);
+      if (st.fused) {
+        for (auto& o : st.group.outputs) check(o.second, st.group.n, dflags + k);
+      } else if (st.instr.op.is_control_flow()) {
+        for (auto& [index, slot] : st.instr.outs) {
+          (void)index;
+          check(slot, plan.slots[slot].second, dflags + k);
+        }
+      } else if (st.instr.op.kind != OpKind::AllReduce || !st.instr.args.empty()) {
+        check(st.instr.dst, st.instr.n, dflags + k);
+      }
+    }
+    std::vector<int> host(2 * n);
+    if (n) ck(cudaMemcpyAsync(host.data(), dflags, 2 * n * sizeof(int), cudaMemcpyDeviceToHost, s), "read check flags");
+    ck(cudaFreeAsync(dflags, s), "cudaFreeAsync(check flags)");
+    std::string why;
+    cudaError_t err = dist_sync(s, &why);
+    if (err != cudaSuccess) {
+      mark_failed(e, why.empty() ? std::string("device error: ") + cudaGetErrorString(err) : why);
+      return fail(RGC_ERR_DEVICE, e->f->error);
+    }
+    for (size_t q = 0; q < 2 * n; ++q) flags[q] = host[q];
+    p->launches += (uint64_t)p->kernels_per_step;
+    return RGC_OK;
+  });
+}
+
 __attribute__((visibility("default"))) int rgc_exec_step_timed(rgc_exec* e, double* seconds, size_t n_steps) {
   return guard([&] {
     Program* p = e->owner->p.get();

@@ -118,6 +118,11 @@ class CudaProgram : public Program {
   std::unique_ptr<Exec> exec() override { return std::make_unique<CudaExec>(p_, plan_); }
   size_t allocated_bytes() const override { return rgc_program_allocated_bytes(p_); }
   void inject_failure_for_test() override { rgc_program_inject_failure(p_); }
+  bool step_checked(Exec& e, std::vector<int32_t>& flags) override {
+    int rc = rgc_exec_step_checked(static_cast<CudaExec&>(e).handle(), flags.data(), flags.size());
+    if (rc != RGC_OK) throw std::runtime_error(rgc_last_error());
+    return true;
+  }
   bool step_timed(Exec& e, std::vector<double>& seconds) override {
     return rgc_exec_step_timed(static_cast<CudaExec&>(e).handle(), seconds.data(), seconds.size()) == RGC_OK;
   }

@@ -51,6 +51,9 @@ struct Program {
   virtual void inject_failure_for_test() {}
   // Per-step timing and a launch breakdown for `profile` (metal.rs:692-712).
   virtual bool step_timed(Exec&, std::vector<double>&) { return false; }
+  // One step with non-finite and index-range flags per plan step (2 x steps entries), computed
+  // on the device; false where the device has no such scan.
+  virtual bool step_checked(Exec&, std::vector<int32_t>&) { return false; }
   virtual Json breakdown(Exec&, size_t) { return Json(); }
   // Device kernels launched on behalf of this program so far (0 where not counted).
   virtual uint64_t launches() const { return 0; }

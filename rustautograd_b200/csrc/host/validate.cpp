@@ -379,8 +379,39 @@ std::pair<Json, std::vector<Json>> Compiled::gradient_stats(const std::vector<Te
 }
 
 // validate.rs:604-632
+std::optional<std::vector<Tensor>> Compiled::scanned(const std::vector<Tensor>& inputs) const {
+  if (!device->fuse().gpu) return std::nullopt;
+  for (auto& t : inputs)
+    if (!t.is_finite()) return std::nullopt;
+  {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!scan_program_) {
+      std::vector<uint32_t> all = raw_outputs();
+      OptResult opt = optimize_mode(raw, all, mode, true);
+      scan_plan_ = Plan::build_fused(opt.graph, opt.outputs, device->fuse());
+      scan_program_ = device->compile(scan_plan_);
+    }
+  }
+  auto e = scan_program_->exec();
+  for (size_t k = 0; k < inputs.size(); ++k) e->load(k, inputs[k]);
+  std::vector<int32_t> flags(2 * scan_plan_.steps.size(), 0);
+  if (!scan_program_->step_checked(*e, flags)) return std::nullopt;
+  if (auto f = e->failure()) throw DiagError(device_failure(device->name(), *f));
+  for (int32_t f : flags)
+    if (f) return std::nullopt;
+  return read_outputs(scan_plan_, *e);
+}
+
 Json Compiled::check(const std::vector<Tensor>& inputs) const {
-  Observed o = observed(inputs);
+  Observed o;
+  bool on_device = false;
+  if (auto values = scanned(inputs)) {
+    // Nothing non-finite and every index in range: no roots to look for.
+    o.values = std::move(*values);
+    on_device = true;
+  } else {
+    o = observed(inputs);
+  }
   std::vector<size_t> bad_outputs;
   for (size_t k = 0; k < outputs.size(); ++k)
     if (!o.values[k].is_finite()) bad_outputs.push_back(k);
@@ -405,6 +436,7 @@ Json Compiled::check(const std::vector<Tensor>& inputs) const {
   nf["root_nodes"] = found;
   nf["propagated_nodes"] = o.propagated;
   nf["affected_outputs"] = Json(bad_outputs);
+  nf["scan"] = on_device ? "device" : "stepwise";
   out["nonfinite"] = nf;
   out["gradients"] = gs.first;
   out["diagnostics"] = d;

@@ -52,6 +52,10 @@ class Compiled {
     std::vector<Tensor> values;
   };
   Observed observed(const std::vector<Tensor>& inputs) const;
+  // The observer's common case on a device with a per-step scan: the optimised plan of all
+  // outputs and gradients run once with non-finite and index flags computed on the device.
+  // Returns the values when nothing was flagged (nothing to explain), else nothing.
+  std::optional<std::vector<Tensor>> scanned(const std::vector<Tensor>& inputs) const;
   std::vector<uint32_t> raw_outputs() const;
   std::pair<Json, std::vector<Json>> gradient_stats(const std::vector<Tensor>& vals) const;
   Json optimizer_check(const std::vector<Tensor>& examples) const;  // throws DiagError
@@ -59,6 +63,8 @@ class Compiled {
   std::pair<Json, std::vector<Json>> grad_check(const std::vector<Tensor>& examples) const;
   std::pair<Json, std::vector<Json>> perturbation_check(const std::vector<Tensor>& examples) const;
   mutable std::shared_ptr<Program> raw_program_;
+  mutable std::shared_ptr<Program> scan_program_;
+  mutable Plan scan_plan_;
   mutable std::mutex mu_;
 };
 

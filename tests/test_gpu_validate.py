@@ -92,3 +92,19 @@ def test_observe_statistics_are_computed_on_the_device(cuda, oracle):
     ro = F.run(co, state, tokens, steps=5)
     for name in ("grad.global_norm", "aux"):
         assert max_rel(np.array(r.history[name]), np.array(ro.history[name])) <= 1e-3, name
+
+
+def test_standard_validation_scans_for_nonfinite_values_on_the_device(cuda):
+    """The finite observer's common case runs as one device pass over the optimised plan with
+    per-step flags; a non-finite value falls back to the step-by-step observer, which names the
+    root node."""
+    F.use(cuda, "cuda")
+    model, opt, state, tokens = _small_gpt()
+    c = F.compile(F.gpt.make_train_step(model, opt, 8), (state, tokens), validate="standard", device="cuda")
+    finite = _check(c.report, "finite")
+    assert finite["nonfinite"]["scan"] == "device" and finite["status"] in ("pass", "warn"), finite
+    x = F.tensor(np.array([1.0, -1.0, 4.0], "float32"))
+    bad = F.compile(lambda a: F.log(a) * 2.0, (x,), validate="standard", device="cuda")
+    finite = _check(bad.report, "finite")
+    assert finite["nonfinite"]["scan"] == "stepwise" and finite["nonfinite"]["root_nodes"] >= 1, finite
+    assert any(d["code"].startswith("NONFINITE") or d["code"].startswith("LOG") or "DOMAIN" in d["code"] for d in bad.report["diagnostics"])
