@@ -885,6 +885,20 @@ __global__ void k_load_batch(char* dst, const char* batches, size_t bytes, long 
   GRID_STRIDE(i, (long long)bytes) { dst[i] = src[i]; }
 }
 
+// The condition of a conditional graph node: the scalar predicate is nonzero and, for a while
+// loop, its iteration count (bumped first inside the loop body) is below the limit.
+__global__ void k_set_conditional(cudaGraphConditionalHandle h, const void* pred, int dtype, long long* count, long long limit, int bump) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  if (count && bump) *count += 1;
+  const double v = dtype == 0 ? (double)*(const float*)pred : dtype == 1 ? *(const double*)pred : (double)*(const int32_t*)pred;
+  const bool go = v != 0.0 && (!count || *count < limit);
+  cudaGraphSetConditional(h, go ? 1u : 0u);
+}
+
+__global__ void k_write_count(int32_t* dst, const long long* count) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) *dst = (int32_t)*count;
+}
+
 __global__ void k_index_outside(const int32_t* idx, long long n, long long dim, int* flag) {
   GRID_STRIDE(i, n) {
     if (idx[i] < 0 || idx[i] >= dim) *flag = 1;
@@ -1266,6 +1280,12 @@ void bump_counter(long long* counter, cudaStream_t s) { k_bump<<<1, 1, 0, s>>>(c
 void load_batch(void* dst, const void* batches, size_t bytes, long long n_batches, const long long* counter, cudaStream_t s) {
   k_load_batch<<<grid_for((long long)bytes), 256, 0, s>>>((char*)dst, (const char*)batches, bytes, n_batches, counter);
 }
+
+void set_conditional(cudaGraphConditionalHandle h, const void* pred, EType t, long long* count, long long limit, bool bump, cudaStream_t s) {
+  k_set_conditional<<<1, 32, 0, s>>>(h, pred, (int)t, count, limit, bump ? 1 : 0);
+}
+
+void write_count(int32_t* dst, const long long* count, cudaStream_t s) { k_write_count<<<1, 32, 0, s>>>(dst, count); }
 
 void index_outside(const int32_t* idx, long long n, long long dim, int* flag, cudaStream_t s) {
   if (n <= 0) return;

@@ -118,6 +118,10 @@ void bump_counter(long long* counter, cudaStream_t s);
 void load_batch(void* dst, const void* batches, size_t bytes, long long n_batches, const long long* counter, cudaStream_t s);
 // Any non-finite value in a float buffer -> *flag = 1.
 void any_nonfinite(const void* src, EType t, long long n, int* flag, cudaStream_t s);
+// Control flow in CUDA graphs: sets conditional node `h` from a scalar predicate (and, with
+// `count`, the iteration count below `limit`; `bump` first adds one to it); the count as int32.
+void set_conditional(cudaGraphConditionalHandle h, const void* pred, EType t, long long* count, long long limit, bool bump, cudaStream_t s);
+void write_count(int32_t* dst, const long long* count, cudaStream_t s);
 // Any index outside [0, dim) -> *flag = 1.
 void index_outside(const int32_t* idx, long long n, long long dim, int* flag, cudaStream_t s);
 

@@ -109,6 +109,11 @@ struct Frame {
   std::unordered_map<const Program*, std::unique_ptr<Frame>> bodies;
   char* staging = nullptr;  // carry copies of a scan body
   size_t staging_bytes = 0;
+  // Control-flow bodies captured into conditional graph nodes: the stream their body graph is
+  // captured on and a device iteration counter.
+  cudaStream_t side = nullptr;
+  long long* counter = nullptr;
+  cudaGraphConditionalHandle ctl_handle = 0;
   ~Frame();
 };
 
@@ -140,6 +145,8 @@ struct Program {
 
 Frame::~Frame() {
   bodies.clear();
+  if (side) cudaStreamDestroy(side);
+  if (counter) cudaFree(counter);
   if (stream) cudaStreamDestroy(stream);
   if (arena) cudaFree(arena);
   if (scratch) cudaFree(scratch);
@@ -174,12 +181,17 @@ void prepare_frame(Program* p, Frame* f, cudaStream_t s) {
     if (st.prepare) st.prepare(f, s);
 }
 
-// The nested frame of a control-flow body, with `staging` bytes for carry copies.
-Frame* body_frame(Frame* parent, Program* body, cudaStream_t s, size_t staging = 0) {
+// The nested frame of a control-flow body, with `staging` bytes for carry copies and, for
+// bodies that may be captured into conditional graph nodes, a side stream and a counter.
+Frame* body_frame(Frame* parent, Program* body, cudaStream_t s, size_t staging = 0, bool control = false) {
   auto& slot = parent->bodies[body];
   if (!slot) {
     slot = make_frame(body, s);
     prepare_frame(body, slot.get(), s);
+  }
+  if (control && !slot->side) {
+    ck(cudaStreamCreateWithFlags(&slot->side, cudaStreamNonBlocking), "cudaStreamCreate(control flow)");
+    ck(cudaMalloc((void**)&slot->counter, sizeof(long long)), "cudaMalloc(iteration counter)");
   }
   if (slot->staging_bytes < staging) {
     if (slot->staging) cudaFree(slot->staging);
@@ -202,6 +214,54 @@ Dims dims_of(const std::vector<size_t>& shape, const std::vector<size_t>& st) {
     d.st[k] = (long long)st[k];
   }
   return d;
+}
+
+// ---- control flow inside CUDA graph capture ----
+
+bool capturing(cudaStream_t s) {
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  return cudaStreamIsCapturing(s, &st) == cudaSuccess && st == cudaStreamCaptureStatusActive;
+}
+
+// Adds a conditional node (type, `bodies` body graphs) after the work captured on `s` so far, makes
+// it the capture's only dependency, and returns its handle and body graphs. `prologue` runs on
+// `s` before the node is added and receives the handle (to set the condition on the device).
+std::vector<cudaGraph_t> add_conditional(cudaStream_t s, cudaGraphConditionalNodeType type, unsigned bodies,
+                                         const std::function<void(cudaGraphConditionalHandle)>& prologue) {
+  cudaStreamCaptureStatus cs;
+  cudaGraph_t graph = nullptr;
+  const cudaGraphNode_t* deps = nullptr;
+  size_t nd = 0;
+  ck(cudaStreamGetCaptureInfo(s, &cs, nullptr, &graph, &deps, &nd), "cudaStreamGetCaptureInfo");
+  cudaGraphConditionalHandle h;
+  ck(cudaGraphConditionalHandleCreate(&h, graph, 0, 0), "cudaGraphConditionalHandleCreate");
+  prologue(h);
+  ck(cudaStreamGetCaptureInfo(s, &cs, nullptr, &graph, &deps, &nd), "cudaStreamGetCaptureInfo");
+  // Zeroed storage: the parameter union has members with non-trivial constructors in C++.
+  alignas(cudaGraphNodeParams) unsigned char storage[sizeof(cudaGraphNodeParams)] = {};
+  cudaGraphNodeParams& params = *reinterpret_cast<cudaGraphNodeParams*>(storage);
+  params.type = cudaGraphNodeTypeConditional;
+  params.conditional.handle = h;
+  params.conditional.type = type;
+  params.conditional.size = bodies;
+  cudaGraphNode_t node;
+  ck(cudaGraphAddNode(&node, graph, deps, nd, &params), "cudaGraphAddNode(conditional)");
+  ck(cudaStreamUpdateCaptureDependencies(s, &node, 1, cudaStreamSetCaptureDependencies), "cudaStreamUpdateCaptureDependencies");
+  return std::vector<cudaGraph_t>(params.conditional.phGraph_out, params.conditional.phGraph_out + bodies);
+}
+
+// Captures `fill(side)` into `graph` on the stream `side`.
+void capture_into(cudaGraph_t graph, cudaStream_t side, const std::function<void(cudaStream_t)>& fill) {
+  ck(cudaStreamBeginCaptureToGraph(side, graph, nullptr, nullptr, 0, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCaptureToGraph");
+  try {
+    fill(side);
+  } catch (...) {
+    cudaGraph_t g;
+    cudaStreamEndCapture(side, &g);
+    throw;
+  }
+  cudaGraph_t g;
+  ck(cudaStreamEndCapture(side, &g), "cudaStreamEndCapture(conditional body)");
 }
 
 // ---- lowering of one instruction ----
@@ -637,26 +697,63 @@ struct Builder {
       auto args = i.args;
       auto outs = i.outs;
       size_t n_carry = i.op.n_carry, max_it = i.op.max_iterations;
-      l.capturable = false;  // the host reads the condition each iteration
+      // Inside graph capture the loop becomes a conditional WHILE node whose condition a kernel
+      // sets on the device; run directly, the host reads the condition each iteration.
+      l.capturable = cond->capturable && body->capturable;
       l.kernels = 0;
       auto bytes_of = [](const Plan& pl, size_t k) { return pl.input_ns[k] * rg::dtype_size(pl.slots[pl.input_slots[k]].first); };
       size_t carry_bytes = 0;
       for (size_t k = 0; k < n_carry; ++k) carry_bytes += align_up(bytes_of(body->plan, k));
       l.prepare = [=](Frame* f, cudaStream_t st) {
         body_frame(f, cond, st);
-        body_frame(f, body, st, carry_bytes);
+        body_frame(f, body, st, carry_bytes, true);
       };
       l.run = [=](Ctx& cx) {
         Frame* cf = body_frame(cx.f, cond, cx.s);
-        Frame* bf = body_frame(cx.f, body, cx.s, carry_bytes);
+        Frame* bf = body_frame(cx.f, body, cx.s, carry_bytes, true);
         const Plan& cp_ = cond->plan;
         const Plan& bp = body->plan;
-        auto cp = [&](void* d, const void* s, size_t bytes) {
-          if (bytes) ck(cudaMemcpyAsync(d, s, bytes, cudaMemcpyDeviceToDevice, cx.s), "while copy");
+        auto cp_on = [&](cudaStream_t st, void* d, const void* s, size_t bytes) {
+          if (bytes) ck(cudaMemcpyAsync(d, s, bytes, cudaMemcpyDeviceToDevice, st), "while copy");
         };
+        auto cp = [&](void* d, const void* s, size_t bytes) { cp_on(cx.s, d, s, bytes); };
         for (size_t k = 0; k < args.size(); ++k) {
           cp(cf->ptr[cp_.input_slots[k]], cx.f->ptr[args[k]], bytes_of(cp_, k));
           cp(bf->ptr[bp.input_slots[k]], cx.f->ptr[args[k]], bytes_of(bp, k));
+        }
+        const auto& co = cp_.outputs[0];
+        const EType ct = et(cp_.slots[co.slot].first);
+        if (capturing(cx.s)) {
+          auto graphs = add_conditional(cx.s, cudaGraphCondTypeWhile, 1, [&](cudaGraphConditionalHandle h) {
+            ck(cudaMemsetAsync(bf->counter, 0, sizeof(long long), cx.s), "while counter");
+            Ctx ci{cx.s, cf};
+            run_steps(cond, ci);
+            set_conditional(h, cf->ptr[co.slot], ct, bf->counter, (long long)max_it, false, cx.s);
+            bf->ctl_handle = h;
+          });
+          const cudaGraphConditionalHandle h = bf->ctl_handle;
+          capture_into(graphs[0], bf->side, [&](cudaStream_t st) {
+            Ctx bi{st, bf}, ci{st, cf};
+            run_steps(body, bi);
+            size_t off = 0;
+            for (size_t k = 0; k < n_carry; ++k) {
+              cp_on(st, bf->staging + off, bf->ptr[bp.outputs[k].slot], bytes_of(bp, k));
+              off += align_up(bytes_of(bp, k));
+            }
+            off = 0;
+            for (size_t k = 0; k < n_carry; ++k) {
+              cp_on(st, bf->ptr[bp.input_slots[k]], bf->staging + off, bytes_of(bp, k));
+              cp_on(st, cf->ptr[cp_.input_slots[k]], bf->staging + off, bytes_of(bp, k));
+              off += align_up(bytes_of(bp, k));
+            }
+            run_steps(cond, ci);
+            set_conditional(h, cf->ptr[co.slot], ct, bf->counter, (long long)max_it, true, st);
+          });
+          for (auto& [index, slot] : outs) {
+            if (index < n_carry) cp(cx.f->ptr[slot], bf->ptr[bp.input_slots[index]], bytes_of(bp, index));
+            else write_count((int32_t*)cx.f->ptr[slot], bf->counter, cx.s);
+          }
+          return;
         }
         Ctx ci{cx.s, cf}, bi{cx.s, bf};
         size_t count = 0;
@@ -705,13 +802,38 @@ struct Builder {
     auto args = i.args;
     auto outs = i.outs;
     DType pd = p->plan.slots[args[0]].first;
-    l.capturable = false;
+    // Inside graph capture: a conditional IF node with an else body; run directly, the host
+    // reads the predicate.
+    l.capturable = then_p->capturable && else_p->capturable;
     l.kernels = 0;
     l.prepare = [=](Frame* f, cudaStream_t st) {
-      body_frame(f, then_p, st);
-      body_frame(f, else_p, st);
+      body_frame(f, then_p, st, 0, true);
+      body_frame(f, else_p, st, 0, true);
     };
     l.run = [=](Ctx& cx) {
+      auto branch = [&](Program* body, cudaStream_t st) {
+        Frame* bf = body_frame(cx.f, body, cx.s, 0, true);
+        const Plan& bp = body->plan;
+        for (size_t k = 0; k + 1 < args.size(); ++k) {
+          size_t bytes = bp.input_ns[k] * rg::dtype_size(bp.slots[bp.input_slots[k]].first);
+          if (bytes) ck(cudaMemcpyAsync(bf->ptr[bp.input_slots[k]], cx.f->ptr[args[k + 1]], bytes, cudaMemcpyDeviceToDevice, st), "cond copy");
+        }
+        Ctx inner{st, bf};
+        run_steps(body, inner);
+        for (auto& [index, slot] : outs) {
+          const auto& o = bp.outputs[index];
+          size_t bytes = o.n * rg::dtype_size(bp.slots[o.slot].first);
+          if (bytes) ck(cudaMemcpyAsync(cx.f->ptr[slot], bf->ptr[o.slot], bytes, cudaMemcpyDeviceToDevice, st), "cond copy");
+        }
+      };
+      if (capturing(cx.s)) {
+        auto graphs = add_conditional(cx.s, cudaGraphCondTypeIf, 2, [&](cudaGraphConditionalHandle h) {
+          set_conditional(h, cx.f->ptr[args[0]], et(pd), nullptr, 0, false, cx.s);
+        });
+        capture_into(graphs[0], body_frame(cx.f, then_p, cx.s, 0, true)->side, [&](cudaStream_t st) { branch(then_p, st); });
+        capture_into(graphs[1], body_frame(cx.f, else_p, cx.s, 0, true)->side, [&](cudaStream_t st) { branch(else_p, st); });
+        return;
+      }
       char buf[8];
       ck(cudaMemcpyAsync(buf, cx.f->ptr[args[0]], rg::dtype_size(pd), cudaMemcpyDeviceToHost, cx.s), "cond predicate");
       ck(cudaStreamSynchronize(cx.s), "cond predicate");

@@ -122,3 +122,25 @@ def test_gpt_sampler_generates_the_oracles_tokens(oracle):
                                                      [triple(F.tensor(l)) for l in leaves], 24)
     assert steps == 24
     np.testing.assert_array_equal(np.array(r.history["aux"]), np.array(hist[0]))
+
+
+def test_device_side_control_flow_in_a_captured_run(oracle):
+    """A run's step graph holds while and cond as conditional graph nodes (the condition set by
+    a kernel, no host round trip): nested loops, a loop stopped by its iteration limit, and both
+    branches taken across steps, against the oracle step for step."""
+    data = rnd(16, seed=11)
+
+    def step(s, d):
+        def body(v):
+            inner = F.while_loop(lambda u: (u.sum() < 40.0).cast("float32"), lambda u: u + 1.0, v * 0.5, max_iterations=7)
+            return F.cond((inner.sum() > 30.0).cast("float32"), lambda w: w * 0.9, lambda w: w * 1.1 + 0.3, inner)
+        s2 = F.while_loop(lambda v: (v.max() < 25.0).cast("float32"), body, s, max_iterations=9)
+        s3 = F.cond((d.sum() > s2.sum() * 0.01).cast("float32"), lambda v: v * 0.25, lambda v: v * 0.75, s2)
+        return s3, s3.sum()
+    s0 = F.ones(16)
+    c = F.compile(step, (s0, data), validate="none", device="cuda")
+    r = F.run(c, s0, data, steps=25)
+    st, hist, steps, _ = oracle.run_plan_blob_steps(c.plan_blob(), [(0, 0)], [1], [1], [triple(s0), triple(data)], 25)
+    assert steps == 25 and r.steps == 25
+    np.testing.assert_array_equal(np.array(r.history["aux"]), np.array(hist[0]))
+    assert_bits_equal(r.state.numpy(), np_of(st[0]), "state")
