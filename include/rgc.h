@@ -21,6 +21,7 @@
  *   rgc_exec_failure            plan.rs:38-40         `Exec::failure`
  *   rgc_exec_run                validate.rs:290-363   `run_loop`, kept on the device (no host sync per step)
  *   rgc_exec_step_checked       validate.rs:132-230   the non-finite observer's per-step scan, on the device
+ *   rgc_exec_save_slots/_load_slots checkpoint.py:37-105 safetensors checkpoints, device <-> file
  *   rgc_exec_step_timed         metal.rs:692-700      `step_timed`
  *   rgc_exec_breakdown_json     metal.rs:701-712      `breakdown`
  *   rgc_dist_*                  (new) data-parallel communicator for the gradient all-reduce step
@@ -81,6 +82,8 @@ int rgc_exec_slot_pointer(rgc_exec* e, size_t slot, void** out);
 
 /* The multi-step run (validate.rs:290-363) on the device.
  * state_inputs/state_outputs: n_state (input index, output index) pairs fed back each step.
+ * `state` NULL: the state inputs already hold the state (left by an earlier run on this exec, or
+ * written by rgc_exec_load / rgc_exec_load_slots), so nothing is uploaded.
  * data_inputs: n_data input indices loaded from `batches`, cycled one batch per step.
  * history_outputs: n_history scalar outputs recorded per step into `history` (row-major
  * [n_history][steps], doubles). State and batch tensors are host memory: state[k] has the bytes
@@ -109,6 +112,15 @@ int rgc_exec_run(rgc_exec* e, const rgc_run_spec* spec, const void* const* state
  * read by step k (take, take_along) lay outside its axis; n = number of plan steps, the array
  * holds 2n entries. */
 int rgc_exec_step_checked(rgc_exec* e, int32_t* flags, size_t n_flags);
+
+/* Checkpoints straight between device slots and a file (checkpoint.py:37-105 writes and reads
+ * the same safetensors layout from host tensors). Save writes `path` through a temporary file
+ * renamed into place: the 8-byte little-endian header length, `header` (header_len bytes), then
+ * sizes[k] bytes of slots[k] in order, streamed through pinned host memory. Load reads sizes[k]
+ * bytes at file offsets[k] into slots[k]. */
+int rgc_exec_save_slots(rgc_exec* e, const char* path, const char* header, size_t header_len, const size_t* slots, const size_t* sizes,
+                        size_t n);
+int rgc_exec_load_slots(rgc_exec* e, const char* path, const uint64_t* offsets, const size_t* slots, const size_t* sizes, size_t n);
 
 /* Per-step device seconds, accumulated into seconds[n_steps] (metal.rs:692-700). */
 int rgc_exec_step_timed(rgc_exec* e, double* seconds, size_t n_steps);

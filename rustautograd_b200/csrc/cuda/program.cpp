@@ -16,6 +16,8 @@
 #include <mutex>
 #include <stdexcept>
 #include <string>
+#include <tuple>
+#include <unistd.h>
 #include <unordered_map>
 #include <vector>
 
@@ -1261,7 +1263,7 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
     for (size_t k = 0; k < spec->n_state; ++k) {
       if (spec->state_inputs[k] >= plan.input_slots.size() || spec->state_outputs[k] >= plan.outputs.size()) return fail(RGC_ERR_INVALID, "run spec index out of range");
       size_t b = in_bytes(spec->state_inputs[k]);
-      if (b) ck(cudaMemcpyAsync(f->ptr[plan.input_slots[spec->state_inputs[k]]], state[k], b, cudaMemcpyHostToDevice, s), "load state");
+      if (b && state) ck(cudaMemcpyAsync(f->ptr[plan.input_slots[spec->state_inputs[k]]], state[k], b, cudaMemcpyHostToDevice, s), "load state");
     }
     for (size_t d = 0; d < spec->n_data; ++d)
       if (spec->data_inputs[d] >= plan.input_slots.size()) return fail(RGC_ERR_INVALID, "run spec index out of range");
@@ -1539,6 +1541,116 @@ __attribute__((visibility("default"))) int rgc_exec_step_checked(rgc_exec* e, in
     }
     for (size_t q = 0; q < 2 * n; ++q) flags[q] = host[q];
     p->launches += (uint64_t)p->kernels_per_step;
+    return RGC_OK;
+  });
+}
+
+namespace {
+// Pinned staging for checkpoint streaming: two buffers, so that one chunk's device copy overlaps
+// the file I/O of the other.
+struct Pinned {
+  static constexpr size_t CHUNK = size_t(64) << 20;
+  void* buf[2] = {nullptr, nullptr};
+  cudaEvent_t done[2] = {nullptr, nullptr};
+  Pinned() {
+    for (int i = 0; i < 2; ++i) {
+      ck(cudaMallocHost(&buf[i], CHUNK), "cudaMallocHost(checkpoint staging)");
+      ck(cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming), "cudaEventCreate");
+    }
+  }
+  ~Pinned() {
+    for (int i = 0; i < 2; ++i) {
+      if (buf[i]) cudaFreeHost(buf[i]);
+      if (done[i]) cudaEventDestroy(done[i]);
+    }
+  }
+};
+}  // namespace
+
+__attribute__((visibility("default"))) int rgc_exec_save_slots(rgc_exec* e, const char* path, const char* header, size_t header_len,
+                                                             const size_t* slots, const size_t* sizes, size_t n) {
+  return guard([&] {
+    if (e->f->failed) return fail(RGC_ERR_DEVICE, e->f->error);
+    const Plan& plan = e->owner->p->plan;
+    if (!path || (header_len && !header) || (n && (!slots || !sizes))) return fail(RGC_ERR_INVALID, "null argument");
+    for (size_t k = 0; k < n; ++k) {
+      if (slots[k] >= plan.slots.size()) return fail(RGC_ERR_INVALID, "slot out of range");
+      if (sizes[k] > plan.slots[slots[k]].second * rg::dtype_size(plan.slots[slots[k]].first)) return fail(RGC_ERR_INVALID, "read beyond the slot");
+    }
+    cudaStream_t s = e->f->stream;
+    std::string tmp = std::string(path) + ".tmp." + std::to_string(getpid());
+    FILE* fp = std::fopen(tmp.c_str(), "wb");
+    if (!fp) return fail(RGC_ERR_INVALID, std::string("cannot open ") + tmp + " for writing");
+    bool ok = true;
+    try {
+      uint64_t len = header_len;
+      unsigned char le[8];
+      for (int i = 0; i < 8; ++i) le[i] = (unsigned char)(len >> (8 * i));
+      ok = std::fwrite(le, 1, 8, fp) == 8 && std::fwrite(header, 1, header_len, fp) == header_len;
+      Pinned pin;
+      // Chunks of every slot in order, double-buffered: copy chunk c + 1 while writing chunk c.
+      std::vector<std::tuple<size_t, size_t, size_t>> chunks;  // (slot, offset, bytes)
+      for (size_t k = 0; k < n; ++k)
+        for (size_t off = 0; off < sizes[k]; off += Pinned::CHUNK) chunks.emplace_back(slots[k], off, std::min(Pinned::CHUNK, sizes[k] - off));
+      auto issue = [&](size_t c) {
+        auto [slot, off, bytes] = chunks[c];
+        ck(cudaMemcpyAsync(pin.buf[c & 1], e->f->ptr[slot] + off, bytes, cudaMemcpyDeviceToHost, s), "checkpoint read");
+        ck(cudaEventRecord(pin.done[c & 1], s), "cudaEventRecord");
+      };
+      if (!chunks.empty()) issue(0);
+      for (size_t c = 0; c < chunks.size() && ok; ++c) {
+        if (c + 1 < chunks.size()) issue(c + 1);
+        ck(cudaEventSynchronize(pin.done[c & 1]), "checkpoint read");
+        size_t bytes = std::get<2>(chunks[c]);
+        ok = std::fwrite(pin.buf[c & 1], 1, bytes, fp) == bytes;
+      }
+      ck(cudaStreamSynchronize(s), "checkpoint read");
+      ok = ok && std::fflush(fp) == 0 && fsync(fileno(fp)) == 0;
+    } catch (...) {
+      std::fclose(fp);
+      std::remove(tmp.c_str());
+      throw;
+    }
+    ok = (std::fclose(fp) == 0) && ok;
+    if (!ok || std::rename(tmp.c_str(), path) != 0) {
+      std::remove(tmp.c_str());
+      return fail(RGC_ERR_INVALID, std::string("writing the checkpoint ") + path + " failed");
+    }
+    return RGC_OK;
+  });
+}
+
+__attribute__((visibility("default"))) int rgc_exec_load_slots(rgc_exec* e, const char* path, const uint64_t* offsets, const size_t* slots,
+                                                             const size_t* sizes, size_t n) {
+  return guard([&] {
+    if (e->f->failed) return fail(RGC_ERR_DEVICE, e->f->error);
+    const Plan& plan = e->owner->p->plan;
+    if (!path || (n && (!offsets || !slots || !sizes))) return fail(RGC_ERR_INVALID, "null argument");
+    for (size_t k = 0; k < n; ++k) {
+      if (slots[k] >= plan.slots.size()) return fail(RGC_ERR_INVALID, "slot out of range");
+      if (sizes[k] > plan.slots[slots[k]].second * rg::dtype_size(plan.slots[slots[k]].first)) return fail(RGC_ERR_INVALID, "write beyond the slot");
+    }
+    FILE* fp = std::fopen(path, "rb");
+    if (!fp) return fail(RGC_ERR_INVALID, std::string("cannot open ") + path);
+    struct Closer {
+      FILE* f;
+      ~Closer() { std::fclose(f); }
+    } closer{fp};
+    cudaStream_t s = e->f->stream;
+    Pinned pin;
+    size_t c = 0;
+    for (size_t k = 0; k < n; ++k) {
+      if (std::fseek(fp, (long)offsets[k], SEEK_SET) != 0) return fail(RGC_ERR_INVALID, std::string(path) + ": offset beyond the file");
+      for (size_t off = 0; off < sizes[k]; off += Pinned::CHUNK, ++c) {
+        const size_t bytes = std::min(Pinned::CHUNK, sizes[k] - off);
+        // The buffer's previous copy must be done before it is refilled.
+        ck(cudaEventSynchronize(pin.done[c & 1]), "checkpoint write");
+        if (std::fread(pin.buf[c & 1], 1, bytes, fp) != bytes) return fail(RGC_ERR_INVALID, std::string(path) + ": file shorter than its header says");
+        ck(cudaMemcpyAsync(e->f->ptr[slots[k]] + off, pin.buf[c & 1], bytes, cudaMemcpyHostToDevice, s), "checkpoint write");
+        ck(cudaEventRecord(pin.done[c & 1], s), "cudaEventRecord");
+      }
+    }
+    ck(cudaStreamSynchronize(s), "checkpoint write");
     return RGC_OK;
   });
 }

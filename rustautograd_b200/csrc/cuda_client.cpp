@@ -64,6 +64,7 @@ class CudaExec : public Exec {
     rgc_run_spec rs{si.data(), so.data(), si.size(), spec.data.data(), spec.data.size(), spec.history.data(), spec.history.size()};
     std::vector<const void*> st;
     for (auto& t : state) st.push_back(t.data.data());
+    const void* const* state_ptrs = spec.resident ? nullptr : st.data();
     std::vector<const void*> bt;
     for (auto& b : batches)
       for (size_t d = 0; d < spec.data.size(); ++d) bt.push_back(b[d].data.data());
@@ -81,22 +82,41 @@ class CudaExec : public Exec {
     size_t done = 0;
     int64_t bad = -1;
     double secs = 0;
-    int rc = rgc_exec_run(e_, &rs, st.data(), bt.data(), batches.size(), steps, hist.data(), optr.data(), obytes.data(), &done, &bad, &secs);
+    // State outputs come back through the state inputs (below), not a second copy.
+    for (auto& [i, o] : spec.state) {
+      (void)i;
+      optr[o] = nullptr;
+      obytes[o] = 0;
+    }
+    int rc = rgc_exec_run(e_, &rs, state_ptrs, bt.data(), batches.size(), steps, hist.data(), optr.data(), obytes.data(), &done, &bad, &secs);
     out->steps = done;
     out->seconds = secs;
     if (bad >= 0) out->nonfinite_step = (size_t)bad;
     if (rc != RGC_OK) out->device_error = std::string(rgc_last_error());
     out->history.assign(spec.history.size(), {});
     for (size_t h = 0; h < spec.history.size(); ++h) out->history[h].assign(hist.begin() + h * steps, hist.begin() + h * steps + done);
+    if (!spec.resident) {
+      for (auto& [i, o] : spec.state) {
+        size_t slot = plan_.input_slots[i];
+        Buf b(plan_.slots[slot].first, plan_.input_ns[i]);
+        rgc_exec_prefix(e_, slot, b.data(), b.bytes());
+        out->state.emplace_back(plan_.outputs[o].shape, std::move(b));
+        if (done) outs[o] = out->state.back().data;  // the last step's state output is the new state
+      }
+    }
     if (done) {
       for (size_t o = 0; o < plan_.outputs.size(); ++o) out->outputs.emplace_back(plan_.outputs[o].shape, std::move(outs[o]));
     }
-    for (auto& [i, o] : spec.state) {
-      size_t slot = plan_.input_slots[i];
-      Buf b(plan_.slots[slot].first, plan_.input_ns[i]);
-      rgc_exec_prefix(e_, slot, b.data(), b.bytes());
-      out->state.emplace_back(plan_.outputs[o].shape, std::move(b));
-    }
+    return true;
+  }
+  bool save_slots(const std::string& path, const std::string& header, const std::vector<size_t>& slots, const std::vector<size_t>& sizes) override {
+    if (rgc_exec_save_slots(e_, path.c_str(), header.data(), header.size(), slots.data(), sizes.data(), slots.size()) != RGC_OK)
+      throw std::runtime_error(rgc_last_error());
+    return true;
+  }
+  bool load_slots(const std::string& path, const std::vector<uint64_t>& offsets, const std::vector<size_t>& slots, const std::vector<size_t>& sizes) override {
+    if (rgc_exec_load_slots(e_, path.c_str(), offsets.data(), slots.data(), sizes.data(), slots.size()) != RGC_OK)
+      throw std::runtime_error(rgc_last_error());
     return true;
   }
   rgc_exec* handle() { return e_; }

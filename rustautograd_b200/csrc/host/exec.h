@@ -16,6 +16,9 @@ struct RunSpec {
   std::vector<std::pair<size_t, size_t>> state;  // (input index, output index) fed back each step
   std::vector<size_t> data;
   std::vector<size_t> history;  // scalar outputs recorded per step
+  // The state already lives in the exec's state inputs (an earlier run, a load or a checkpoint
+  // restore) and stays there afterwards: nothing is uploaded or read back.
+  bool resident = false;
 };
 
 struct RunOut {
@@ -39,6 +42,12 @@ struct Exec {
   virtual void write_prefix(size_t slot, const Buf& b) = 0;
   virtual double scalar(size_t slot) = 0;
   virtual std::optional<std::string> failure() { return std::nullopt; }
+  // Checkpoint streaming (checkpoint.py:37-105 layout) straight between slots and a file:
+  // `header` then sizes[k] bytes of each slot, or file bytes at offsets[k] into each slot.
+  // False where the device has no direct path (the caller then goes through prefix and
+  // write_prefix).
+  virtual bool save_slots(const std::string&, const std::string&, const std::vector<size_t>&, const std::vector<size_t>&) { return false; }
+  virtual bool load_slots(const std::string&, const std::vector<uint64_t>&, const std::vector<size_t>&, const std::vector<size_t>&) { return false; }
   // A device-resident implementation of the whole multi-step loop. Returns false when the
   // device has none, and the host loop (run_loop) drives load/step/swap instead.
   virtual bool run(const RunSpec&, const std::vector<Tensor>&, const std::vector<std::vector<Tensor>>&, size_t, RunOut*) { return false; }

@@ -148,6 +148,27 @@ struct PyCompiled {
   std::unique_ptr<Compiled> c;
 };
 
+// Not in rg's module: a run whose state stays in one exec's frame between calls (on the CUDA
+// device: in HBM), with checkpoints streamed between that frame and safetensors files.
+struct PySession {
+  py::object owner;  // the Compiled, kept alive
+  const Compiled* c = nullptr;
+  std::unique_ptr<Exec> e;
+  RunSpec spec;
+  bool resident = true;             // the device runs the loop itself
+  std::vector<Tensor> host_state;   // otherwise the state between runs
+  std::vector<size_t> state_slots() const {
+    std::vector<size_t> v;
+    for (auto& [i, o] : spec.state) v.push_back(c->plan.input_slots[i]);
+    return v;
+  }
+  std::vector<size_t> state_bytes() const {
+    std::vector<size_t> v;
+    for (auto& [i, o] : spec.state) v.push_back(c->plan.input_ns[i] * dtype_size(c->plan.slots[c->plan.input_slots[i]].first));
+    return v;
+  }
+};
+
 }  // namespace
 
 PYBIND11_MODULE(RG_MODULE_NAME, m) {
@@ -278,7 +299,108 @@ PYBIND11_MODULE(RG_MODULE_NAME, m) {
       })
       .def_property_readonly("n_nodes", [](const PyGraph& self) { return self.g.nodes.size(); });
 
+  py::class_<PySession>(m, "Session")
+      .def("run", [](PySession& self, std::vector<std::vector<PyTensor>> batches, size_t steps) {
+        std::vector<std::vector<Tensor>> bs;
+        for (auto& b : batches) bs.push_back(tensors(b));
+        RunOut out;
+        {
+          py::gil_scoped_release nogil;
+          if (self.resident) {
+            RunSpec spec = self.spec;
+            spec.resident = true;
+            self.resident = self.e->run(spec, {}, bs, steps, &out);
+          }
+          if (!self.resident) {
+            out = run_loop(self.c->plan, *self.e, self.spec, self.host_state, bs, steps);
+            self.host_state = out.state;
+          }
+        }
+        if (out.device_error) {
+          Json d = device_failure(self.c->device->name(), *out.device_error);
+          d["observation"]["completed_steps"] = out.steps;
+          raise_diag(d);
+        }
+        std::optional<size_t> bad = out.nonfinite_step;
+        return py::make_tuple(wrap(std::move(out.outputs)), out.history, out.steps, bad, out.seconds);
+      })
+      .def("state", [](PySession& self) {
+        if (!self.resident) return wrap(self.host_state);
+        std::vector<Tensor> out;
+        auto slots = self.state_slots();
+        for (size_t k = 0; k < slots.size(); ++k) {
+          auto [i, o] = self.spec.state[k];
+          out.emplace_back(self.c->plan.outputs[o].shape, self.e->prefix(slots[k], self.c->plan.input_ns[i]));
+        }
+        return wrap(std::move(out));
+      })
+      .def("save", [](PySession& self, const std::string& path, py::bytes header) {
+        std::string h = header;
+        py::gil_scoped_release nogil;
+        auto slots = self.state_slots();
+        auto sizes = self.state_bytes();
+        if (self.resident && self.e->save_slots(path, h, slots, sizes)) return;
+        // Generic path: the state as host tensors, written in the same layout.
+        std::string tmp = path + ".tmp";
+        FILE* fp = std::fopen(tmp.c_str(), "wb");
+        if (!fp) throw std::runtime_error("cannot open " + tmp + " for writing");
+        uint64_t len = h.size();
+        unsigned char le[8];
+        for (int i = 0; i < 8; ++i) le[i] = (unsigned char)(len >> (8 * i));
+        bool ok = std::fwrite(le, 1, 8, fp) == 8 && std::fwrite(h.data(), 1, h.size(), fp) == h.size();
+        for (size_t k = 0; k < slots.size() && ok; ++k) {
+          auto [i, o] = self.spec.state[k];
+          (void)o;
+          Buf b = self.resident ? self.e->prefix(slots[k], self.c->plan.input_ns[i]) : self.host_state[k].data;
+          ok = std::fwrite(b.data(), 1, b.bytes(), fp) == b.bytes();
+        }
+        ok = (std::fclose(fp) == 0) && ok;
+        if (!ok || std::rename(tmp.c_str(), path.c_str()) != 0) throw std::runtime_error("writing the checkpoint " + path + " failed");
+      })
+      .def("restore", [](PySession& self, const std::string& path, std::vector<uint64_t> offsets) {
+        py::gil_scoped_release nogil;
+        auto slots = self.state_slots();
+        auto sizes = self.state_bytes();
+        if (offsets.size() != slots.size()) throw std::runtime_error("one file offset per state tensor is needed");
+        if (self.resident && self.e->load_slots(path, offsets, slots, sizes)) return;
+        FILE* fp = std::fopen(path.c_str(), "rb");
+        if (!fp) throw std::runtime_error("cannot open " + path);
+        for (size_t k = 0; k < slots.size(); ++k) {
+          auto [i, o] = self.spec.state[k];
+          Buf b(self.c->plan.slots[slots[k]].first, self.c->plan.input_ns[i]);
+          bool ok = std::fseek(fp, (long)offsets[k], SEEK_SET) == 0 && std::fread(b.data(), 1, b.bytes(), fp) == b.bytes();
+          if (!ok) {
+            std::fclose(fp);
+            throw std::runtime_error(path + ": file shorter than its header says");
+          }
+          // Both copies: a device without a resident run loop uses the host copy.
+          self.e->write_prefix(slots[k], b);
+          self.host_state[k] = Tensor(self.c->plan.outputs[o].shape, std::move(b));
+        }
+        std::fclose(fp);
+      });
+
   py::class_<PyCompiled>(m, "Compiled")
+      .def("session", [](py::object owner, std::vector<std::pair<size_t, size_t>> state_map, std::vector<size_t> data_inputs,
+                         std::vector<size_t> history, std::vector<PyTensor> state) {
+        const PyCompiled& self = owner.cast<const PyCompiled&>();
+        RunSpec spec{state_map, data_inputs, history};
+        guarded([&] {
+          self.c->validate_spec(spec);
+          return 0;
+        });
+        PySession ses;
+        ses.owner = owner;
+        ses.c = self.c.get();
+        ses.spec = spec;
+        ses.host_state = tensors(state);
+        {
+          py::gil_scoped_release nogil;
+          ses.e = self.c->program->exec();
+          for (size_t k = 0; k < spec.state.size() && k < ses.host_state.size(); ++k) ses.e->load(spec.state[k].first, ses.host_state[k]);
+        }
+        return ses;
+      })
       .def_property_readonly("report_json", [](const PyCompiled& self) { return self.c->report.dump(); })
       .def_property_readonly("output_shapes", [](const PyCompiled& self) {
         std::vector<std::vector<size_t>> s;
