@@ -5,6 +5,7 @@
 #include <nccl.h>
 
 #include <chrono>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -93,6 +94,8 @@ cudaError_t dist_sync(cudaStream_t stream, std::string* why) {
   }
   // A collective has waited past the limit (another rank stopped or diverged): abort the
   // communicator so that its kernels return, then drain the stream.
+  const bool trace = std::getenv("RGC_TRACE_DIST") != nullptr;
+  if (trace) std::fprintf(stderr, "rgc dist: rank %d: stream still busy after %.1f s, aborting the communicator\n", g_rank, limit);
   {
     std::lock_guard<std::mutex> lk(g_mu);
     if (g_comm) {
@@ -101,11 +104,13 @@ cudaError_t dist_sync(cudaStream_t stream, std::string* why) {
       g_aborted = true;
     }
   }
+  if (trace) std::fprintf(stderr, "rgc dist: rank %d: communicator aborted\n", g_rank);
   // The aborted collectives return; the drain is bounded as well.
   const auto t1 = std::chrono::steady_clock::now();
   while (cudaStreamQuery(stream) == cudaErrorNotReady &&
          std::chrono::duration<double>(std::chrono::steady_clock::now() - t1).count() < 30.0)
     std::this_thread::sleep_for(std::chrono::milliseconds(1));
+  if (trace) std::fprintf(stderr, "rgc dist: rank %d: stream %s after the abort\n", g_rank, cudaStreamQuery(stream) == cudaErrorNotReady ? "still busy" : "drained");
   cudaGetLastError();
   if (why) *why = "a collective waited more than " + std::to_string((int)limit) + " s for another rank; the communicator was aborted";
   return cudaErrorLaunchTimeout;

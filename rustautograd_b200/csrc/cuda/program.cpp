@@ -97,6 +97,10 @@ struct Lowered {
   std::function<void(Frame*, cudaStream_t)> prepare;
   int kernels = 1;
   bool capturable = true;
+  // An NCCL collective: under data parallelism it is launched directly rather than from a CUDA
+  // graph, because aborting a communicator whose kernels run inside a graph launch does not
+  // return while they wait for a partner that has gone.
+  bool collective = false;
 };
 
 struct Frame {
@@ -116,6 +120,12 @@ struct Frame {
   cudaStream_t side = nullptr;
   long long* counter = nullptr;
   cudaGraphConditionalHandle ctl_handle = 0;
+  // Pinned host memory for reads that the host polls (step counters, check flags, slot reads
+  // under data parallelism): a device-to-host copy into pageable memory blocks the calling thread
+  // until the stream reaches it, which behind a stalled collective is never.
+  void* pinned = nullptr;
+  size_t pinned_bytes = 0;
+  void* host_buffer(size_t bytes);
   ~Frame();
 };
 
@@ -153,6 +163,30 @@ Frame::~Frame() {
   if (arena) cudaFree(arena);
   if (scratch) cudaFree(scratch);
   if (staging) cudaFree(staging);
+  if (pinned) cudaFreeHost(pinned);
+}
+
+void* Frame::host_buffer(size_t bytes) {
+  if (bytes > pinned_bytes) {
+    if (pinned) cudaFreeHost(pinned);
+    pinned = nullptr;
+    pinned_bytes = 0;
+    size_t want = std::max<size_t>(bytes, 4096);
+    ck(cudaMallocHost(&pinned, want), "cudaMallocHost(frame host buffer)");
+    pinned_bytes = want;
+  }
+  return pinned;
+}
+
+// A scalar read by the host between launches (host-driven while / cond), waited for with the
+// polled wait that gives up on a stalled collective.
+double read_scalar(Frame* f, const void* dev, DType d, cudaStream_t s, const char* what) {
+  char* buf = (char*)f->host_buffer(8);
+  ck(cudaMemcpyAsync(buf, dev, rg::dtype_size(d), cudaMemcpyDeviceToHost, s), what);
+  std::string why;
+  cudaError_t err = dist_sync(s, &why);
+  if (err != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + (why.empty() ? cudaGetErrorString(err) : why));
+  return d == DType::F32 ? (double)*(float*)buf : d == DType::F64 ? *(double*)buf : (double)*(int32_t*)buf;
 }
 
 std::unique_ptr<Program> make_program(const Plan& plan, int device);
@@ -764,10 +798,7 @@ struct Builder {
           const auto& o = cp_.outputs[0];
           double v = 0;
           DType d = cp_.slots[o.slot].first;
-          char buf[8];
-          ck(cudaMemcpyAsync(buf, cf->ptr[o.slot], rg::dtype_size(d), cudaMemcpyDeviceToHost, cx.s), "while condition");
-          ck(cudaStreamSynchronize(cx.s), "while condition");
-          v = d == DType::F32 ? (double)*(float*)buf : d == DType::F64 ? *(double*)buf : (double)*(int32_t*)buf;
+          v = read_scalar(cx.f, cf->ptr[o.slot], d, cx.s, "while condition");
           if (v == 0.0) break;
           if (count == max_it) break;
           run_steps(body, bi);
@@ -836,10 +867,7 @@ struct Builder {
         capture_into(graphs[1], body_frame(cx.f, else_p, cx.s, 0, true)->side, [&](cudaStream_t st) { branch(else_p, st); });
         return;
       }
-      char buf[8];
-      ck(cudaMemcpyAsync(buf, cx.f->ptr[args[0]], rg::dtype_size(pd), cudaMemcpyDeviceToHost, cx.s), "cond predicate");
-      ck(cudaStreamSynchronize(cx.s), "cond predicate");
-      double v = pd == DType::F32 ? (double)*(float*)buf : pd == DType::F64 ? *(double*)buf : (double)*(int32_t*)buf;
+      double v = read_scalar(cx.f, cx.f->ptr[args[0]], pd, cx.s, "cond predicate");
       Program* body = v != 0.0 ? then_p : else_p;
       Frame* bf = body_frame(cx.f, body, cx.s);
       const Plan& bp = body->plan;
@@ -886,6 +914,7 @@ std::unique_ptr<Program> make_program(const Plan& plan, int device) {
       --k;
       Lowered l;
       l.kernels = (int)items.size();
+      l.collective = true;
       l.run = [items](Ctx& c) {
         if (dist_aborted()) throw std::runtime_error("the data-parallel communicator was aborted after a stalled collective");
         if (!dist_active()) {
@@ -1181,9 +1210,26 @@ __attribute__((visibility("default"))) int rgc_exec_prefix(rgc_exec* e, size_t s
     const Plan& plan = e->owner->p->plan;
     if (slot >= plan.slots.size()) return fail(RGC_ERR_INVALID, "slot out of range");
     if (bytes > plan.slots[slot].second * rg::dtype_size(plan.slots[slot].first)) return fail(RGC_ERR_INVALID, "read beyond the slot");
-    if (bytes) ck(cudaMemcpyAsync(host, e->f->ptr[slot], bytes, cudaMemcpyDeviceToHost, e->f->stream), "read slot");
     std::string why;
-    cudaError_t err = dist_sync(e->f->stream, &why);
+    cudaError_t err = cudaSuccess;
+    if (!dist_active()) {
+      if (bytes) ck(cudaMemcpyAsync(host, e->f->ptr[slot], bytes, cudaMemcpyDeviceToHost, e->f->stream), "read slot");
+      err = cudaStreamSynchronize(e->f->stream);
+    } else {
+      // Through pinned memory in chunks, so that the wait is the polled one that can give up on
+      // a collective stalled earlier in the stream.
+      const size_t chunk = size_t(16) << 20;
+      size_t off = 0;
+      do {
+        const size_t b = std::min(chunk, bytes - off);
+        void* stage = e->f->host_buffer(std::max<size_t>(b, 1));
+        if (b) ck(cudaMemcpyAsync(stage, e->f->ptr[slot] + off, b, cudaMemcpyDeviceToHost, e->f->stream), "read slot");
+        err = dist_sync(e->f->stream, &why);
+        if (err != cudaSuccess) break;
+        std::memcpy((char*)host + off, stage, b);
+        off += b;
+      } while (off < bytes);
+    }
     if (err != cudaSuccess) {
       mark_failed(e, why.empty() ? std::string(cudaGetErrorString(err)) : why);
       return fail(RGC_ERR_DEVICE, e->f->error);
@@ -1347,14 +1393,17 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
     long long init[2] = {0, -1};
     ck(cudaMemcpyAsync(ctr, init, sizeof init, cudaMemcpyHostToDevice, s), "reset counters");
 
-    // One step with layout L: batch load, the plan, history, copies (through staging), counter.
-    auto one_step = [&](int L, cudaStream_t st) {
+    // One step with layout L: batch load, the plan's steps [first, last), history, copies
+    // (through staging), counter. The batch load belongs to the first piece of a step and the
+    // rest to the last.
+    auto step_part = [&](int L, cudaStream_t st, size_t first, size_t last) {
       f->ptr = layout[L];
-      if (n_batches > 1)
+      if (first == 0 && n_batches > 1)
         for (size_t d = 0; d < spec->n_data; ++d)
           load_batch(f->ptr[plan.input_slots[spec->data_inputs[d]]], batch_dev[d], in_bytes(spec->data_inputs[d]), (long long)n_batches, ctr, st);
       Ctx c{st, f};
-      run_steps(p, c);
+      for (size_t k = first; k < last; ++k) p->steps[k].run(c);
+      if (last < p->steps.size()) return;
       if (nh) record_history(hist_dev, (const void* const*)(hptr_dev + L * nh), types_dev, (int)nh, ctr, ctr + 1, st);
       size_t off = 0;
       for (auto& cp : copies) {
@@ -1369,18 +1418,55 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
       bump_counter(ctr, st);
     };
     bool use_graphs = graphs_enabled() && p->capturable;
-    cudaGraphExec_t g[2] = {nullptr, nullptr};
+    // A step replays as pieces: CUDA graphs for the runs of steps between collectives, and under
+    // data parallelism each collective launched directly (so that a stalled one can be aborted).
+    struct Piece {
+      cudaGraphExec_t g[2] = {nullptr, nullptr};
+      size_t first = 0, last = 0;  // plan steps; a direct piece has last == first + 1
+      bool direct = false;
+    };
+    std::vector<Piece> pieces;
     struct GraphCleanup {
-      cudaGraphExec_t* g;
+      std::vector<Piece>& pieces;
       bool two;
       ~GraphCleanup() {
-        if (g[0]) cudaGraphExecDestroy(g[0]);
-        if (two && g[1]) cudaGraphExecDestroy(g[1]);
+        for (auto& pc : pieces) {
+          if (pc.g[0]) cudaGraphExecDestroy(pc.g[0]);
+          if (two && pc.g[1]) cudaGraphExecDestroy(pc.g[1]);
+        }
       }
-    } graph_cleanup{g, alternating};
+    } graph_cleanup{pieces, alternating};
     if (use_graphs) {
-      for (int LL = 0; LL < (alternating ? 2 : 1); ++LL) g[LL] = capture(s, [&](cudaStream_t st) { one_step(LL, st); });
-      if (!alternating) g[1] = g[0];
+      const bool split = dist_active();
+      size_t start = 0;
+      for (size_t k = 0; k <= p->steps.size(); ++k) {
+        const bool cut = k == p->steps.size() || (split && p->steps[k].collective);
+        if (!cut) continue;
+        Piece pc;
+        pc.first = start;
+        pc.last = k;
+        pieces.push_back(pc);
+        if (k < p->steps.size()) {
+          Piece d;
+          d.first = k;
+          d.last = k + 1;
+          d.direct = true;
+          pieces.push_back(d);
+        }
+        start = k + 1;
+      }
+      // The last graph piece carries the step's epilogue, even when the plan ends in a collective.
+      if (pieces.back().direct) {
+        Piece tail;
+        tail.first = tail.last = p->steps.size();
+        pieces.push_back(tail);
+      }
+      for (auto& pc : pieces) {
+        if (pc.direct) continue;
+        for (int LL = 0; LL < (alternating ? 2 : 1); ++LL)
+          pc.g[LL] = capture(s, [&](cudaStream_t st) { step_part(LL, st, pc.first, pc.last); });
+        if (!alternating) pc.g[1] = pc.g[0];
+      }
     }
     uint64_t per_step = (uint64_t)p->kernels_per_step + (nh ? 1 : 0) + 1 + (n_batches > 1 ? spec->n_data : 0);
     // State snapshot buffers (chunk starts), sized by the state inputs.
@@ -1425,8 +1511,19 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
       }
     };
     auto launch = [&](int LL) {
-      if (use_graphs) ck(cudaGraphLaunch(g[LL], s), "cudaGraphLaunch");
-      else one_step(LL, s);
+      if (!use_graphs) {
+        step_part(LL, s, 0, p->steps.size());
+      } else {
+        for (auto& pc : pieces) {
+          if (!pc.direct) {
+            ck(cudaGraphLaunch(pc.g[LL], s), "cudaGraphLaunch");
+            continue;
+          }
+          f->ptr = layout[LL];
+          Ctx c{s, f};
+          p->steps[pc.first].run(c);
+        }
+      }
       p->launches += per_step;
     };
     while (done < steps) {
@@ -1441,8 +1538,8 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
         launch(L);
         if (alternating) L = 1 - L;
       }
-      long long host_ctr[2];
-      ck(cudaMemcpyAsync(host_ctr, ctr, sizeof host_ctr, cudaMemcpyDeviceToHost, s), "read counters");
+      long long* host_ctr = (long long*)f->host_buffer(2 * sizeof(long long));
+      ck(cudaMemcpyAsync(host_ctr, ctr, 2 * sizeof(long long), cudaMemcpyDeviceToHost, s), "read counters");
       std::string why;
       cudaError_t err = dist_sync(s, &why);
       if (err != cudaSuccess) {
@@ -1530,8 +1627,8 @@ __attribute__((visibility("default"))) int rgc_exec_step_checked(rgc_exec* e, in
         check(st.instr.dst, st.instr.n, dflags + k);
       }
     }
-    std::vector<int> host(2 * n);
-    if (n) ck(cudaMemcpyAsync(host.data(), dflags, 2 * n * sizeof(int), cudaMemcpyDeviceToHost, s), "read check flags");
+    int* host = (int*)e->f->host_buffer(std::max<size_t>(1, 2 * n) * sizeof(int));
+    if (n) ck(cudaMemcpyAsync(host, dflags, 2 * n * sizeof(int), cudaMemcpyDeviceToHost, s), "read check flags");
     ck(cudaFreeAsync(dflags, s), "cudaFreeAsync(check flags)");
     std::string why;
     cudaError_t err = dist_sync(s, &why);

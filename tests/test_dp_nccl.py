@@ -37,8 +37,19 @@ def _model(F, world, rank, batch=8):
 def _rank(rank, world, port, out_dir, mode):
     import sys
     sys.path.insert(0, ROOT)
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0", RGC_COLLECTIVE_TIMEOUT_S="5")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0", RGC_COLLECTIVE_TIMEOUT_S="5",
+                      RGC_TRACE_DIST="1")
+    err = os.open(os.path.join(out_dir, f"rank{rank}.stderr"), os.O_WRONLY | os.O_CREAT | os.O_APPEND)
+    os.dup2(err, 2)
     import datetime
+    import faulthandler
+    # Where each rank is blocked if it has not finished in time, for the failure message.
+    trace = open(os.path.join(out_dir, f"rank{rank}.trace"), "w")
+    faulthandler.dump_traceback_later(50, exit=False, file=trace)
+
+    def progress(what):
+        with open(os.path.join(out_dir, f"rank{rank}.progress"), "a") as f:
+            f.write(what + "\n")
     import torch
     import torch.distributed as dist
     torch.cuda.set_device(rank)
@@ -62,6 +73,7 @@ def _rank(rank, world, port, out_dir, mode):
         # steps with nothing in flight; rank 0's next all-reduce has no partner and must end with
         # an error once the collective timeout has passed.
         F.run(c, state, tokens, steps=1)
+        progress("first step done")
         dist.barrier()
         if rank == 1:
             np.save(os.path.join(out_dir, "rank1.npy"), np.array({}, dtype=object), allow_pickle=True)
@@ -71,8 +83,11 @@ def _rank(rank, world, port, out_dir, mode):
             result = {"error": ""}
         except Exception as e:  # DiagnosticError from the device failure
             result = {"error": str(getattr(e, "diagnostic", e))}
+        progress("second run returned: " + result["error"][:200])
     np.save(os.path.join(out_dir, f"rank{rank}.npy"), np.array(result, dtype=object), allow_pickle=True)
     _rg.dist_finalize()
+    progress("finalized")
+    faulthandler.cancel_dump_traceback_later()
     if mode != "stall":
         dist.destroy_process_group()
 
@@ -89,7 +104,12 @@ def _spawn(tmp_path, mode):
     for p in procs:
         if p.is_alive():
             p.kill()
-    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    def read(name):
+        path = os.path.join(tmp_path, name)
+        return open(path).read() if os.path.exists(path) else ""
+    if not all(p.exitcode == 0 for p in procs):
+        pytest.fail(f"exit codes {[p.exitcode for p in procs]}\n" + "\n".join(
+            f"--- rank{r}.{kind}\n{read(f'rank{r}.{kind}')[-4000:]}" for r in range(2) for kind in ("progress", "trace", "stderr")))
     return [np.load(os.path.join(tmp_path, f"rank{r}.npy"), allow_pickle=True).item() for r in range(2)]
 
 
