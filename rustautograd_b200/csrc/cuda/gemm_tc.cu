@@ -20,10 +20,19 @@
 // Work units are (output tile, K split) pairs handed out round-robin over the persistent CTAs.
 // Every wait is bounded by a wall-clock limit; on expiry the kernel records an error code, lets
 // its copies and products in flight finish, frees its TMEM and exits.
+//
+// Pair form (PAIR = true, clusters of two CTAs on two SMs): the pair computes a 256 x BN tile
+// with tcgen05.mma.cta_group::2 issued by the even CTA. Each CTA loads and converts its own 128
+// rows of A and its own BN/2 columns of B; the tensor cores of both SMs read both halves of B,
+// so each SM's shared memory carries half the B traffic and conversion work of the single-CTA
+// form, and each CTA's TMEM holds the accumulator of its 128 rows. The odd CTA's converters and
+// epilogue arrive on the even CTA's barriers through cluster addresses; the even CTA's commits
+// signal both CTAs' barriers (one commit per CTA; no multicast).
 #include <cuda.h>
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -38,8 +47,9 @@ constexpr int THREADS = 320;
 constexpr uint32_t A_BYTES = BM * BK * 4;  // 16 KB
 constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;
 
-template <int BN> struct Shape {
-  static constexpr uint32_t B_BYTES = BN * BK * 4;
+template <int BN, bool PAIR = false> struct Shape {
+  static constexpr int BROWS = PAIR ? BN / 2 : BN;  // B rows (N columns) this CTA loads
+  static constexpr uint32_t B_BYTES = BROWS * BK * 4;
   static constexpr uint32_t RAW = A_BYTES + B_BYTES;  // raw tiles (read by the MMA as hi)
   static constexpr uint32_t STAGE = 2 * RAW;          // + lo tiles
   static constexpr int STAGES = (200 * 1024) / STAGE > 4 ? 4 : (200 * 1024) / STAGE;
@@ -66,21 +76,29 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(bar)) : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t phase) {
+// CLUSTER: acquire at cluster scope, for barriers that the other CTA of a pair arrives on.
+template <bool CLUSTER = false> __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t phase) {
   uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(saddr(bar)), "r"(phase)
-      : "memory");
+  if (CLUSTER)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(saddr(bar)), "r"(phase)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(saddr(bar)), "r"(phase)
+        : "memory");
   return ok != 0;
 }
 
 // Waits for `phase` of `bar`; gives up after WAIT_LIMIT_NS or when another role aborted.
-__device__ bool mbar_wait(uint64_t* bar, uint32_t phase, volatile int* abort, int* err, int code) {
+template <bool CLUSTER = false> __device__ bool mbar_wait(uint64_t* bar, uint32_t phase, volatile int* abort, int* err, int code) {
   unsigned long long t0 = 0;
   for (int spin = 0;; ++spin) {
-    if (mbar_try(bar, phase)) return true;
+    if (mbar_try<CLUSTER>(bar, phase)) return true;
     if (*abort) return false;
     if (spin == 64) t0 = now_ns();
     if (spin > 64 && now_ns() - t0 > WAIT_LIMIT_NS) {
@@ -134,6 +152,47 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(bar)) : "memory");
 }
 
+// ---- CTA pairs (clusters of two) ----
+__device__ __forceinline__ uint32_t cta_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_index() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_total() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// The cluster address of the barrier at the same offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr(local)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mma_tf32_pair(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  const uint32_t no_mask = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\ttcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, "
+      "p;\n\t}" ::"r"(tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(no_mask)
+      : "memory");
+}
+// Completion of the pair's products so far, signalled on the barrier at cluster address `caddr`.
+__device__ __forceinline__ void mma_commit_pair(uint32_t caddr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(caddr) : "memory");
+}
+
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
@@ -160,11 +219,13 @@ struct Work {
   float* C;           // output (splits == 1) or partials [splits][batch][M][N]
 };
 
-template <int BN, bool AMN, bool BMN>
+template <int BN, bool AMN, bool BMN, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     k_tc3(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mB, const Work w, int* err) {
-  using S = Shape<BN>;
+  using S = Shape<BN, PAIR>;
   constexpr int STAGES = S::STAGES;
+  constexpr int TM = PAIR ? 2 * BM : BM;  // output rows per work unit
+  constexpr int PEERS = PAIR ? 2 : 1;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = (uint64_t*)(smem + STAGES * S::STAGE);
@@ -178,27 +239,38 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long units = (long long)w.mt * w.nt * w.batch * w.splits;
+  // This CTA's place: rank within its pair (0 issues the products), first unit and stride.
+  const uint32_t rank = PAIR ? cta_rank() : 0;
+  const long long first_unit = PAIR ? (long long)cluster_index() : (long long)blockIdx.x;
+  const long long unit_stride = PAIR ? (long long)cluster_total() : (long long)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&conv[s], 4);
+      mbar_init(&conv[s], 4 * PEERS);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], 4 * PEERS);
     }
     mbar_init(done, 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)), "r"((uint32_t)(2 * BN)) : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)), "r"((uint32_t)(2 * BN)) : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)), "r"((uint32_t)(2 * BN)) : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
   }
   fence_before();
   __syncthreads();
+  // Both CTAs' barriers exist before either arrives on the other's.
+  if (PAIR) cluster_sync();
   fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -217,13 +289,13 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // Producer.
+      // Producer: this CTA's rows of A and columns of B.
       long long it = 0;
-      for (long long u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
+      for (long long u = first_unit; u < units && !*abort; u += unit_stride) {
         int m_t, n_t, z, sp, kb0, kb1;
         decode(u, m_t, n_t, z, sp);
         kb_range(sp, kb0, kb1);
-        const int m0 = m_t * BM, n0 = n_t * BN;
+        const int m0 = m_t * TM + (int)rank * BM, n0 = n_t * BN + (int)rank * S::BROWS;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = (int)(it % STAGES);
           if (it >= STAGES && !mbar_wait(&empty[s], (uint32_t)(((it / STAGES) - 1) & 1), abort, err, 1)) break;
@@ -238,7 +310,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           if (BMN) {
 #pragma unroll
-            for (int i = 0; i < BN / 32; ++i) tma_load(sb + i * 4096, &mB, &full[s], n0 + 32 * i, k0, z * w.zb);
+            for (int i = 0; i < S::BROWS / 32; ++i) tma_load(sb + i * 4096, &mB, &full[s], n0 + 32 * i, k0, z * w.zb);
           } else {
             tma_load(sb, &mB, &full[s], k0, n0, z * w.zb);
           }
@@ -253,23 +325,23 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // MMA issuer. Instruction descriptor: M = 128, N = BN, TF32 x TF32 -> F32.
+    if (lane == 0 && rank == 0) {
+      // MMA issuer. Instruction descriptor: M = TM, N = BN, TF32 x TF32 -> F32.
       const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((AMN ? 1u : 0u) << 15) | ((BMN ? 1u : 0u) << 16) |
-                             ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+                             ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
       long long it = 0, t = 0;
-      for (long long u = blockIdx.x; u < units && !*abort; u += gridDim.x, ++t) {
+      for (long long u = first_unit; u < units && !*abort; u += unit_stride, ++t) {
         int m_t, n_t, z, sp, kb0, kb1;
         decode(u, m_t, n_t, z, sp);
         kb_range(sp, kb0, kb1);
         const int b = (int)(t & 1);
-        if (t >= 2 && !mbar_wait(&acc_empty[b], (uint32_t)(((t >> 1) - 1) & 1), abort, err, 4)) break;
+        if (t >= 2 && !mbar_wait<PAIR>(&acc_empty[b], (uint32_t)(((t >> 1) - 1) & 1), abort, err, 4)) break;
         fence_after();
         const uint32_t acc = tmem + (uint32_t)(b * BN);
         bool first = true;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = (int)(it % STAGES);
-          if (!mbar_wait(&conv[s], (uint32_t)((it / STAGES) & 1), abort, err, 2)) break;
+          if (!mbar_wait<PAIR>(&conv[s], (uint32_t)((it / STAGES) & 1), abort, err, 2)) break;
           fence_after();
           const uint32_t ah = saddr(smem + s * S::STAGE), bh = ah + A_BYTES;
           const uint32_t al = ah + S::RAW, bl = bh + S::RAW;
@@ -278,22 +350,43 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint32_t ka = AMN ? kk * 1024 : kk * 32, kb_ = BMN ? kk * 1024 : kk * 32;
             const uint64_t dah = AMN ? desc_mn(ah + ka) : desc_k(ah + ka), dal = AMN ? desc_mn(al + ka) : desc_k(al + ka);
             const uint64_t dbh = BMN ? desc_mn(bh + kb_) : desc_k(bh + kb_), dbl = BMN ? desc_mn(bl + kb_) : desc_k(bl + kb_);
-            mma_tf32(acc, dah, dbh, idesc, first ? 0u : 1u);
-            mma_tf32(acc, dah, dbl, idesc, 1);
-            mma_tf32(acc, dal, dbh, idesc, 1);
+            if (PAIR) {
+              mma_tf32_pair(acc, dah, dbh, idesc, first ? 0u : 1u);
+              mma_tf32_pair(acc, dah, dbl, idesc, 1);
+              mma_tf32_pair(acc, dal, dbh, idesc, 1);
+            } else {
+              mma_tf32(acc, dah, dbh, idesc, first ? 0u : 1u);
+              mma_tf32(acc, dah, dbl, idesc, 1);
+              mma_tf32(acc, dal, dbh, idesc, 1);
+            }
             first = false;
           }
-          mma_commit(&empty[s]);
+          if (PAIR) {
+            mma_commit_pair(cluster_addr(&empty[s], 0));
+            mma_commit_pair(cluster_addr(&empty[s], 1));
+          } else {
+            mma_commit(&empty[s]);
+          }
         }
-        mma_commit(&acc_full[b]);
+        if (PAIR) {
+          mma_commit_pair(cluster_addr(&acc_full[b], 0));
+          mma_commit_pair(cluster_addr(&acc_full[b], 1));
+        } else {
+          mma_commit(&acc_full[b]);
+        }
       }
-      mma_commit(done);
+      if (PAIR) {
+        mma_commit_pair(cluster_addr(done, 0));
+        mma_commit_pair(cluster_addr(done, 1));
+      } else {
+        mma_commit(done);
+      }
     }
   } else if (warp < 6) {
     // Converters: 128 threads write each stage's lo tiles (the raw tiles serve as hi).
     const int ct = threadIdx.x - 64;
     long long it = 0;
-    for (long long u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
+    for (long long u = first_unit; u < units && !*abort; u += unit_stride) {
       int m_t, n_t, z, sp, kb0, kb1;
       decode(u, m_t, n_t, z, sp);
       kb_range(sp, kb0, kb1);
@@ -313,21 +406,24 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
-        if (lane == 0) mbar_arrive(&conv[s]);
+        if (lane == 0) {
+          if (PAIR) mbar_arrive_remote(cluster_addr(&conv[s], 0));
+          else mbar_arrive(&conv[s]);
+        }
       }
       if (!ok) break;
     }
   } else {
-    // Epilogue: warp w drains TMEM lanes [32 (w % 4), +32) = rows of the tile.
+    // Epilogue: warp w drains TMEM lanes [32 (w % 4), +32) = rows of this CTA's part of the tile.
     const int lg = warp & 3;
     long long t = 0;
-    for (long long u = blockIdx.x; u < units && !*abort; u += gridDim.x, ++t) {
+    for (long long u = first_unit; u < units && !*abort; u += unit_stride, ++t) {
       int m_t, n_t, z, sp;
       decode(u, m_t, n_t, z, sp);
       const int b = (int)(t & 1);
       if (!mbar_wait(&acc_full[b], (uint32_t)((t >> 1) & 1), abort, err, 3)) break;
       fence_after();
-      const long long row = (long long)m_t * BM + lg * 32 + lane;
+      const long long row = (long long)m_t * TM + (long long)rank * BM + lg * 32 + lane;
       const long long n0 = (long long)n_t * BN;
       float* out = w.C + (((long long)sp * w.batch + z) * w.M + row) * w.N;
 #pragma unroll 1
@@ -350,21 +446,28 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (lane == 0) {
+        if (PAIR) mbar_arrive_remote(cluster_addr(&acc_empty[b], 0));
+        else mbar_arrive(&acc_empty[b]);
+      }
     }
   }
 
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 0 && lane == 0) {
     // Every product issued has completed before the accumulator is freed.
-    if (lane == 0) {
-      unsigned long long t0 = now_ns();
-      while (!mbar_try(done, 0) && now_ns() - t0 < WAIT_LIMIT_NS) {
-      }
+    unsigned long long t0 = now_ns();
+    while (!mbar_try(done, 0) && now_ns() - t0 < WAIT_LIMIT_NS) {
     }
-    __syncwarp();
+  }
+  __syncthreads();
+  // Neither CTA of a pair frees its TMEM or leaves (its shared memory holds operands and
+  // barriers the other uses) before both are done.
+  if (PAIR) cluster_sync();
+  if (warp == 0) {
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * BN)) : "memory");
+    if (PAIR) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * BN)) : "memory");
+    else asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * BN)) : "memory");
   }
 }
 
@@ -434,8 +537,12 @@ int sm_count() {
   return sms;
 }
 
+// Concurrently resident CTA pairs of the pair form (0 when pairs cannot be launched).
+int g_pairs = 0;
+
 // The launch decided for one product: operand layouts, packing, tile width, K splits.
 struct Plan3 {
+  bool pair;            // CTA-pair form (256-row tiles)
   bool a_mn, b_mn;      // operand read MN-major
   bool pack_a, pack_b;  // operand first packed K-major (row pitch not 16-byte aligned)
   long long kp;         // K of packed operands (multiple of 4)
@@ -459,13 +566,17 @@ Plan3 plan3(const TcGemm& g) {
   if (p.pack_a) p.a_mn = false;
   if (p.pack_b) p.b_mn = false;
   p.bn = pick_bn(g.n);
-  p.mt = (g.m + BM - 1) / BM;
+  // Pairs of CTAs take 256-row tiles when there are rows for both and B is wide enough that
+  // halving its per-SM traffic pays.
+  p.pair = g_pairs > 0 && p.bn >= 128 && g.m > BM;
+  const long long tm = p.pair ? 2 * BM : BM;
+  p.mt = (g.m + tm - 1) / tm;
   p.nt = (g.n + p.bn - 1) / p.bn;
   p.num_kb = (int)((g.k + BK - 1) / BK);
   // Split K when the output tiles alone leave SMs idle: pick the split count (at least 8 K
   // blocks per split) that fills the most of whole waves, less a small charge per split for the
   // partial sums it writes and reads back.
-  const long long tiles = p.mt * p.nt * g.batch, sms = sm_count();
+  const long long tiles = p.mt * p.nt * g.batch, sms = p.pair ? g_pairs : sm_count();
   p.splits = 1;
   if (tiles < sms && p.num_kb >= 16) {
     double best = -1;
@@ -484,34 +595,82 @@ Plan3 plan3(const TcGemm& g) {
   return p;
 }
 
-template <int BN, bool AMN, bool BMN> void set_smem() {
-  cudaError_t e = cudaFuncSetAttribute(k_tc3<BN, AMN, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Shape<BN>::SMEM);
+template <int BN, bool AMN, bool BMN, bool PAIR> void set_smem() {
+  cudaError_t e = cudaFuncSetAttribute(k_tc3<BN, AMN, BMN, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Shape<BN, PAIR>::SMEM);
   if (e != cudaSuccess) throw std::runtime_error(std::string("tensor-core GEMM setup failed: ") + cudaGetErrorString(e));
 }
-template <int BN> void set_smem_all() {
-  set_smem<BN, false, false>();
-  set_smem<BN, false, true>();
-  set_smem<BN, true, false>();
-  set_smem<BN, true, true>();
+template <int BN, bool PAIR> void set_smem_all() {
+  set_smem<BN, false, false, PAIR>();
+  set_smem<BN, false, true, PAIR>();
+  set_smem<BN, true, false, PAIR>();
+  set_smem<BN, true, true, PAIR>();
 }
 
-template <int BN>
+template <int BN, bool AMN, bool BMN, bool PAIR>
+void launch_one(unsigned grid, const CUtensorMap& ma, const CUtensorMap& mb, const Work& w, int* err, cudaStream_t s) {
+  const size_t smem = Shape<BN, PAIR>::SMEM;
+  if constexpr (!PAIR) {
+    k_tc3<BN, AMN, BMN, false><<<grid, THREADS, smem, s>>>(ma, mb, w, err);
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_tc3<BN, AMN, BMN, true>, ma, mb, w, err);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("tensor-core GEMM launch failed: ") + cudaGetErrorString(e));
+  }
+}
+
+template <int BN, bool PAIR>
 void launch3(bool amn, bool bmn, unsigned grid, const CUtensorMap& ma, const CUtensorMap& mb, const Work& w, int* err, cudaStream_t s) {
-  const size_t smem = Shape<BN>::SMEM;
-  if (!amn && !bmn) k_tc3<BN, false, false><<<grid, THREADS, smem, s>>>(ma, mb, w, err);
-  else if (!amn && bmn) k_tc3<BN, false, true><<<grid, THREADS, smem, s>>>(ma, mb, w, err);
-  else if (amn && !bmn) k_tc3<BN, true, false><<<grid, THREADS, smem, s>>>(ma, mb, w, err);
-  else k_tc3<BN, true, true><<<grid, THREADS, smem, s>>>(ma, mb, w, err);
+  if (!amn && !bmn) launch_one<BN, false, false, PAIR>(grid, ma, mb, w, err, s);
+  else if (!amn && bmn) launch_one<BN, false, true, PAIR>(grid, ma, mb, w, err, s);
+  else if (amn && !bmn) launch_one<BN, true, false, PAIR>(grid, ma, mb, w, err, s);
+  else launch_one<BN, true, true, PAIR>(grid, ma, mb, w, err, s);
+}
+
+// How many CTA pairs of the pair form can be resident at once (their shared memory puts one CTA
+// on an SM; pairs must sit on two SMs of one cluster group).
+template <int BN> int resident_pairs() {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * sm_count());
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = Shape<BN, true>::SMEM;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, k_tc3<BN, false, false, true>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
 }
 
 }  // namespace
 
 void tc_gemm_init() {
   static bool done = [] {
-    set_smem_all<64>();
-    set_smem_all<128>();
-    set_smem_all<256>();
+    set_smem_all<64, false>();
+    set_smem_all<128, false>();
+    set_smem_all<256, false>();
+    set_smem_all<128, true>();
+    set_smem_all<256, true>();
     encoder();
+    const char* off = getenv("RGC_TC_NO_PAIR");
+    g_pairs = off && std::string(off) == "1" ? 0 : std::min(resident_pairs<128>(), resident_pairs<256>());
     return true;
   }();
   (void)done;
@@ -557,7 +716,8 @@ void tc_gemm(const TcGemm& g, void* scratch, int* error, cudaStream_t s) {
   const long long sa = p.pack_a ? g.m * p.kp : g.batch_a, sb = p.pack_b ? g.n * p.kp : g.batch_b;
   const CUtensorMapSwizzle kmaj = CU_TENSOR_MAP_SWIZZLE_128B, mnmaj = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
   CUtensorMap ma = p.a_mn ? make_map(a, g.m, g.k, nma, g.m, sa, 32, 32, mnmaj) : make_map(a, ka, g.m, nma, ka, sa, 32, BM, kmaj);
-  CUtensorMap mb = p.b_mn ? make_map(b, g.n, g.k, nmb, g.n, sb, 32, 32, mnmaj) : make_map(b, kb, g.n, nmb, kb, sb, 32, (uint32_t)p.bn, kmaj);
+  const uint32_t b_rows = (uint32_t)(p.pair ? p.bn / 2 : p.bn);  // B rows one CTA loads
+  CUtensorMap mb = p.b_mn ? make_map(b, g.n, g.k, nmb, g.n, sb, 32, 32, mnmaj) : make_map(b, kb, g.n, nmb, kb, sb, 32, b_rows, kmaj);
 
   Work w;
   w.M = g.m;
@@ -572,10 +732,16 @@ void tc_gemm(const TcGemm& g, void* scratch, int* error, cudaStream_t s) {
   w.zb = g.batch_b ? 1 : 0;
   w.C = part ? part : g.c;
   const long long units = p.mt * p.nt * g.batch * p.splits;
-  const unsigned grid = (unsigned)std::min<long long>(units, sm_count());
-  if (p.bn == 256) launch3<256>(p.a_mn, p.b_mn, grid, ma, mb, w, error, s);
-  else if (p.bn == 128) launch3<128>(p.a_mn, p.b_mn, grid, ma, mb, w, error, s);
-  else launch3<64>(p.a_mn, p.b_mn, grid, ma, mb, w, error, s);
+  if (p.pair) {
+    const unsigned grid = (unsigned)(2 * std::min<long long>(units, g_pairs));
+    if (p.bn == 256) launch3<256, true>(p.a_mn, p.b_mn, grid, ma, mb, w, error, s);
+    else launch3<128, true>(p.a_mn, p.b_mn, grid, ma, mb, w, error, s);
+  } else {
+    const unsigned grid = (unsigned)std::min<long long>(units, sm_count());
+    if (p.bn == 256) launch3<256, false>(p.a_mn, p.b_mn, grid, ma, mb, w, error, s);
+    else if (p.bn == 128) launch3<128, false>(p.a_mn, p.b_mn, grid, ma, mb, w, error, s);
+    else launch3<64, false>(p.a_mn, p.b_mn, grid, ma, mb, w, error, s);
+  }
   if (part) {
     const long long count = g.batch * g.m * g.n;
     k_sum_splits<<<(unsigned)std::max<long long>(1, std::min<long long>((count + 255) / 256, sm_count() * 8LL)), 256, 0, s>>>(g.c, part, count, p.splits);

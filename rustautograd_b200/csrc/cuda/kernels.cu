@@ -1,8 +1,10 @@
 // Hand-written sm_100a kernels of the rg CUDA device (built with -fmad=false, IEEE division and
 // square root, so single operations round exactly as rg's CPU interpreter does).
+#include <algorithm>
 #include <cfloat>
 #include <cmath>
 #include <cstdio>
+#include <type_traits>
 
 #include "kernels.cuh"
 
@@ -548,50 +550,96 @@ __global__ void k_cols_partial(T* __restrict__ part, const T* __restrict__ a, Re
   part[q * cols + c] = acc;
 }
 
-// The final column pass with its loads staged: block = 32 columns; every thread copies slices of
-// the next partial rows into shared memory (TG_STAGES stages in flight), warp 0 combines them in
-// partial order, one column per lane: a sequential order per column with many loads in flight.
+// The 64-row partials with 16-byte loads: a thread folds PER adjacent columns (PER chains, each in
+// row order), a full 64-row block fully unrolled so its loads are all in flight at once.
+template <typename T, typename V, int PER>
+__global__ void k_cols_partial_vec(T* __restrict__ part, const T* __restrict__ a, Red op, long long rows, long long cols) {
+  const long long ncv = cols / PER;
+  const long long cv = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (cv >= ncv) return;
+  const long long q = blockIdx.y, r0 = q * REDUCE_ROWS;
+  const long long n = rows - r0 < REDUCE_ROWS ? rows - r0 : REDUCE_ROWS;
+  const V* src = (const V*)(a + r0 * cols) + cv;
+  T acc[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) acc[j] = red_init<T>(op);
+  if (n == REDUCE_ROWS) {
+#pragma unroll 16
+    for (int r = 0; r < (int)REDUCE_ROWS; ++r) {
+      const V v = src[r * ncv];
+      const T* e = (const T*)&v;
+#pragma unroll
+      for (int j = 0; j < PER; ++j) acc[j] = combine(op, acc[j], e[j]);
+    }
+  } else {
+    for (long long r = 0; r < n; ++r) {
+      const V v = src[r * ncv];
+      const T* e = (const T*)&v;
+#pragma unroll
+      for (int j = 0; j < PER; ++j) acc[j] = combine(op, acc[j], e[j]);
+    }
+  }
+  V out;
+  T* o = (T*)&out;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) o[j] = acc[j];
+  ((V*)(part + q * cols))[cv] = out;
+}
+
+// The final column fold: every output column folds its `nparts` rows in row order (the 64-row
+// partials, or the rows themselves), one thread per column. A block owns one 32-byte sector of
+// columns and stages CF_ROWS-row chunks of them in shared memory, double-buffered: the serial
+// folds read shared memory while the next chunk is in flight, and the grid has a block per
+// sector instead of per 32 columns.
+constexpr int CF_ROWS = 1024;
 template <typename T, bool VEC>
-__global__ void __launch_bounds__(256) k_cols_final_staged(T* __restrict__ dst, const T* __restrict__ part, Red op, long long nparts, long long cols) {
+__global__ void __launch_bounds__(256) k_cols_fold(T* __restrict__ dst, const T* __restrict__ part, Red op, long long nparts, long long cols) {
+  constexpr int C = 32 / (int)sizeof(T);  // columns per block
+  constexpr int PER = VEC ? 16 / (int)sizeof(T) : 1;
   extern __shared__ __align__(16) unsigned char cf_smem[];
-  T* buf = (T*)cf_smem;  // [TG_STAGES][TG_HITS][TG_COLS]
-  const long long col0 = (long long)blockIdx.x * TG_COLS;
-  const int width = (int)(cols - col0 < TG_COLS ? cols - col0 : TG_COLS);
-  constexpr int PER = VEC ? (int)(16 / sizeof(T)) : 1;
-  const int copies_per_row = (width + PER - 1) / PER;
-  const long long stages = (nparts + TG_HITS - 1) / TG_HITS;
-  auto issue = [&](long long st) {
-    if (st < stages) {
-      T* b = buf + (st % TG_STAGES) * TG_HITS * TG_COLS;
-      const long long q0 = st * TG_HITS;
-      const int nq = (int)(nparts - q0 < TG_HITS ? nparts - q0 : TG_HITS);
-      for (int x = threadIdx.x; x < nq * copies_per_row; x += blockDim.x) {
-        const int h = x / copies_per_row, k = (x - h * copies_per_row) * PER;
+  T* buf = (T*)cf_smem;  // [2][CF_ROWS][C]
+  const long long col0 = (long long)blockIdx.x * C;
+  const int width = (int)(cols - col0 < C ? cols - col0 : C);
+  const int copies = (width + PER - 1) / PER;  // per row (VEC: width is a multiple of PER)
+  const long long chunks = (nparts + CF_ROWS - 1) / CF_ROWS;
+  auto issue = [&](long long ch) {
+    if (ch < chunks) {
+      T* b = buf + (ch & 1) * CF_ROWS * C;
+      const long long q0 = ch * CF_ROWS;
+      const int nq = (int)(nparts - q0 < CF_ROWS ? nparts - q0 : CF_ROWS);
+      for (int x = threadIdx.x; x < nq * copies; x += blockDim.x) {
+        const int h = x / copies, k = (x - h * copies) * PER;
         const T* src = part + (q0 + h) * cols + col0 + k;
-        if (VEC) cp_async16(b + h * TG_COLS + k, src);
-        else cp_async_n<(int)sizeof(T)>(b + h * TG_COLS + k, src);
+        if (VEC) cp_async16(b + h * C + k, src);
+        else cp_async_n<(int)sizeof(T)>(b + h * C + k, src);
       }
     }
     cp_async_commit();
   };
-  for (int st = 0; st < TG_STAGES - 1; ++st) issue(st);
+  issue(0);
   T acc = red_init<T>(op);
-  const int lane = threadIdx.x;
-  for (long long st = 0; st < stages; ++st) {
-    issue(st + TG_STAGES - 1);
-    cp_async_wait<TG_STAGES - 1>();
+  for (long long ch = 0; ch < chunks; ++ch) {
+    issue(ch + 1);
+    cp_async_wait<1>();
     __syncthreads();
-    if (threadIdx.x < 32 && lane < width) {
-      const T* b = buf + (st % TG_STAGES) * TG_HITS * TG_COLS;
-      const int nq = (int)(nparts - st * TG_HITS < TG_HITS ? nparts - st * TG_HITS : TG_HITS);
-      for (int h = 0; h < nq; ++h) acc = combine(op, acc, b[h * TG_COLS + lane]);
+    if (threadIdx.x < width) {
+      const T* b = buf + (ch & 1) * CF_ROWS * C + threadIdx.x;
+      const int nq = (int)(nparts - ch * CF_ROWS < CF_ROWS ? nparts - ch * CF_ROWS : CF_ROWS);
+      int h = 0;
+      for (; h + 16 <= nq; h += 16) {
+        T v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = b[(h + j) * C];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc = combine(op, acc, v[j]);
+      }
+      for (; h < nq; ++h) acc = combine(op, acc, b[h * C]);
     }
     __syncthreads();
   }
   cp_async_wait<0>();
   if (threadIdx.x < width) dst[col0 + threadIdx.x] = acc;
 }
-
 
 template <typename T>
 __global__ void k_reduce_generic(T* __restrict__ dst, const T* __restrict__ a, Red op, Dims kept, Dims red, long long n_out, long long n_red) {
@@ -1156,16 +1204,17 @@ size_t cols_scratch_bytes(long long rows, long long cols, EType t) {
 
 // Every output column sums `nparts` rows of `part` in row order, staged through shared memory.
 template <typename T> static void ordered_cols(void* dst, const T* part, Red op, long long nparts, long long cols, cudaStream_t s) {
-  constexpr int smem = TG_STAGES * TG_HITS * TG_COLS * (int)sizeof(T);
-  const unsigned blocks = (unsigned)((cols + TG_COLS - 1) / TG_COLS);
+  constexpr int C = 32 / (int)sizeof(T);
+  constexpr int smem = 2 * CF_ROWS * 32;
+  const unsigned blocks = (unsigned)((cols + C - 1) / C);
   if ((cols * (long long)sizeof(T)) % 16 == 0 && ((uintptr_t)part & 15) == 0) {
-    static bool attr = (cudaFuncSetAttribute(k_cols_final_staged<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), true);
+    static bool attr = (cudaFuncSetAttribute(k_cols_fold<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), true);
     (void)attr;
-    k_cols_final_staged<T, true><<<blocks, 256, smem, s>>>((T*)dst, part, op, nparts, cols);
+    k_cols_fold<T, true><<<blocks, 256, smem, s>>>((T*)dst, part, op, nparts, cols);
   } else {
-    static bool attr = (cudaFuncSetAttribute(k_cols_final_staged<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), true);
+    static bool attr = (cudaFuncSetAttribute(k_cols_fold<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), true);
     (void)attr;
-    k_cols_final_staged<T, false><<<blocks, 256, smem, s>>>((T*)dst, part, op, nparts, cols);
+    k_cols_fold<T, false><<<blocks, 256, smem, s>>>((T*)dst, part, op, nparts, cols);
   }
 }
 
@@ -1181,8 +1230,17 @@ static void cols_t(void* dst, const void* src, Red op, long long rows, long long
     return;
   }
   long long parts = (rows + REDUCE_ROWS - 1) / REDUCE_ROWS;
-  dim3 grid((unsigned)((cols + 255) / 256), (unsigned)parts);
-  k_cols_partial<T><<<grid, 256, 0, s>>>((T*)scratch, (const T*)src, op, rows, cols);
+  constexpr int PER = 16 / (int)sizeof(T);
+  if (cols % PER == 0 && ((uintptr_t)src & 15) == 0 && ((uintptr_t)scratch & 15) == 0) {
+    using V = typename std::conditional<sizeof(T) == 4, float4, double2>::type;
+    const long long ncv = cols / PER;
+    const unsigned threads = (unsigned)std::min<long long>(256, (ncv + 31) / 32 * 32);
+    dim3 grid((unsigned)((ncv + threads - 1) / threads), (unsigned)parts);
+    k_cols_partial_vec<T, V, PER><<<grid, threads, 0, s>>>((T*)scratch, (const T*)src, op, rows, cols);
+  } else {
+    dim3 grid((unsigned)((cols + 255) / 256), (unsigned)parts);
+    k_cols_partial<T><<<grid, 256, 0, s>>>((T*)scratch, (const T*)src, op, rows, cols);
+  }
   ordered_cols<T>(dst, (const T*)scratch, op, parts, cols, s);
 }
 void reduce_cols(void* dst, const void* src, EType t, Red op, long long rows, long long cols, bool chunked, void* scratch, cudaStream_t s) {

@@ -113,6 +113,9 @@ def test_reductions(oracle, axes, kind):
     ((5000, 64), 0, "float32"),    # 16-byte staging
     ((4100, 10), 0, "float64"),
     ((64, 70, 9), (0, 1), "float32"),
+    ((140001, 8), 0, "float32"),   # 2188 partial rows: the fold stages three 1024-row chunks
+    ((70000, 17), 0, "float32"),   # unaligned columns, 4-byte staging, two chunks
+    ((140000, 6), 0, "float64"),   # below rg's parallel threshold: one sequential fold per column
 ])
 @pytest.mark.parametrize("kind", ["sum", "max", "min"])
 def test_leading_axis_reductions_keep_rgs_order(oracle, shape, axis, dtype, kind):
@@ -236,6 +239,10 @@ TC_CASES = [
     ((40, 8000), (8000, 72), False, False),         # one output tile, split K
     ((4000, 96), (50, 96), False, True),            # narrow N (64-wide tiles), B K-major
     ((300, 200), (200, 150), False, False),         # B row pitch not a multiple of 4: packed K-major
+    ((257, 64), (64, 129), False, False),           # CTA pairs: one row past a pair tile, the odd CTA's B half mostly past N
+    ((1000, 72), (72, 100), False, False),          # CTA pairs with 128-wide tiles
+    ((16, 256, 64), (16, 256, 64), False, True),    # batched CTA pairs, B K-major (q @ k^T at T = 256)
+    ((520, 4000), (4000, 300), False, False),       # CTA pairs with split K
 ]
 
 
