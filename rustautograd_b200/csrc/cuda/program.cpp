@@ -10,6 +10,8 @@
 #include <atomic>
 #include <chrono>
 #include <cmath>
+#include <cstdint>
+#include <cstdio>
 #include <cstring>
 #include <functional>
 #include <memory>
@@ -126,6 +128,50 @@ struct Frame {
   void* pinned = nullptr;
   size_t pinned_bytes = 0;
   void* host_buffer(size_t bytes);
+  // What rgc_exec_run sets up, kept between runs on this frame: grow-only device buffers and
+  // the step graphs captured for the last run, with the key they were captured for (run spec,
+  // buffer addresses) and the two pointer layouts they replay. A run with the same key and
+  // layouts (in either order) launches the cached graphs instead of capturing again.
+  struct RunPiece {
+    cudaGraphExec_t g[2] = {nullptr, nullptr};
+    size_t first = 0, last = 0;  // plan steps; a direct piece has last == first + 1
+    bool direct = false;
+  };
+  struct RunCache {
+    double* hist = nullptr;
+    size_t hist_cap = 0;  // doubles
+    long long* ctr = nullptr;
+    char* staging = nullptr;
+    size_t staging_cap = 0;
+    int* types = nullptr;
+    void** hptr = nullptr;
+    size_t nh_cap = 0;
+    char* snap = nullptr;
+    size_t snap_cap = 0;
+    std::vector<char*> batch;
+    std::vector<size_t> batch_cap;
+    std::vector<RunPiece> pieces;
+    bool alternating = false;
+    bool captured = false;
+    std::vector<uintptr_t> key;
+    std::vector<char*> layout[2];
+    void drop_graphs() {
+      for (auto& pc : pieces) {
+        if (pc.g[0]) cudaGraphExecDestroy(pc.g[0]);
+        if (pc.g[1] && pc.g[1] != pc.g[0]) cudaGraphExecDestroy(pc.g[1]);
+      }
+      pieces.clear();
+      captured = false;
+      key.clear();
+    }
+    ~RunCache() {
+      drop_graphs();
+      for (void* q : {(void*)hist, (void*)ctr, (void*)staging, (void*)types, (void*)hptr, (void*)snap})
+        if (q) cudaFree(q);
+      for (char* q : batch)
+        if (q) cudaFree(q);
+    }
+  } run;
   ~Frame();
 };
 
@@ -1304,6 +1350,13 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
     *nonfinite_step = -1;
     *seconds = 0;
     if (f->failed) return fail(RGC_ERR_DEVICE, f->error);
+    // RGC_TRACE_RUN=1 prints where a run's wall time goes (set-up, capture, loop, read-back).
+    using Clock = std::chrono::steady_clock;
+    static const bool trace = [] {
+      const char* v = getenv("RGC_TRACE_RUN");
+      return v && std::string(v) == "1";
+    }();
+    const auto t_start = Clock::now();
     auto slot_bytes = [&](size_t slot) { return plan.slots[slot].second * rg::dtype_size(plan.slots[slot].first); };
     auto in_bytes = [&](size_t input) { return plan.input_ns[input] * rg::dtype_size(plan.slots[plan.input_slots[input]].first); };
     for (size_t k = 0; k < spec->n_state; ++k) {
@@ -1316,23 +1369,33 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
     for (size_t h = 0; h < spec->n_history; ++h)
       if (spec->history_outputs[h] >= plan.outputs.size()) return fail(RGC_ERR_INVALID, "run spec index out of range");
     // Batches: one batch is loaded once; several live on the device and a kernel picks one per step.
+    // Device buffers of the run (batches, history, counters, copy staging, snapshot) are the
+    // frame's, grown when a run needs more and kept for the next run.
+    Frame::RunCache& rc = f->run;
+    auto grow = [](auto*& ptr, size_t& cap, size_t want, const char* what) {
+      using T = std::remove_reference_t<decltype(*ptr)>;
+      if (want <= cap) return;
+      if (ptr) cudaFree((void*)ptr);
+      ptr = nullptr;
+      cap = 0;
+      ck(cudaMalloc((void**)&ptr, want * sizeof(T)), what);
+      cap = want;
+    };
     std::vector<char*> batch_dev(spec->n_data, nullptr);
-    struct Cleanup {
-      std::vector<void*> ptrs;
-      ~Cleanup() {
-        for (void* q : ptrs) cudaFree(q);
-      }
-    } cleanup;
     if (n_batches == 1) {
       for (size_t d = 0; d < spec->n_data; ++d) {
         size_t b = in_bytes(spec->data_inputs[d]);
         if (b) ck(cudaMemcpyAsync(f->ptr[plan.input_slots[spec->data_inputs[d]]], batches[d], b, cudaMemcpyHostToDevice, s), "load batch");
       }
     } else if (n_batches > 1) {
+      if (rc.batch.size() < spec->n_data) {
+        rc.batch.resize(spec->n_data, nullptr);
+        rc.batch_cap.resize(spec->n_data, 0);
+      }
       for (size_t d = 0; d < spec->n_data; ++d) {
         size_t b = in_bytes(spec->data_inputs[d]);
-        ck(cudaMalloc((void**)&batch_dev[d], std::max<size_t>(1, b * n_batches)), "cudaMalloc(batches)");
-        cleanup.ptrs.push_back(batch_dev[d]);
+        grow(rc.batch[d], rc.batch_cap[d], std::max<size_t>(1, b * n_batches), "cudaMalloc(batches)");
+        batch_dev[d] = rc.batch[d];
         for (size_t q = 0; q < n_batches; ++q)
           if (b) ck(cudaMemcpyAsync(batch_dev[d] + q * b, batches[q * spec->n_data + d], b, cudaMemcpyHostToDevice, s), "upload batches");
       }
@@ -1350,19 +1413,16 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
       else copies.emplace_back(is, os, plan.outputs[spec->state_outputs[k]].n * rg::dtype_size(plan.slots[os].first));
     }
     size_t nh = spec->n_history;
-    double* hist_dev = nullptr;
-    long long* ctr = nullptr;  // [0] = step counter, [1] = first non-finite step
-    char* staging = nullptr;
     size_t staging_bytes = 0;
     for (auto& c : copies) staging_bytes += align_up(std::get<2>(c));
-    ck(cudaMalloc((void**)&hist_dev, std::max<size_t>(1, nh * steps) * sizeof(double)), "cudaMalloc(history)");
-    cleanup.ptrs.push_back(hist_dev);
-    ck(cudaMalloc((void**)&ctr, 2 * sizeof(long long)), "cudaMalloc(counters)");
-    cleanup.ptrs.push_back(ctr);
-    if (staging_bytes) {
-      ck(cudaMalloc((void**)&staging, staging_bytes), "cudaMalloc(copy staging)");
-      cleanup.ptrs.push_back(staging);
-    }
+    // History capacity: at least 2^16 steps, so that runs of different lengths share one capture.
+    grow(rc.hist, rc.hist_cap, std::max<size_t>(1, nh * std::max<size_t>(steps, size_t(1) << 16)), "cudaMalloc(history)");
+    size_t ctr_cap = rc.ctr ? 2 : 0;
+    grow(rc.ctr, ctr_cap, 2, "cudaMalloc(counters)");
+    if (staging_bytes) grow(rc.staging, rc.staging_cap, staging_bytes, "cudaMalloc(copy staging)");
+    double* hist_dev = rc.hist;
+    long long* ctr = rc.ctr;  // [0] = step counter, [1] = first non-finite step
+    char* staging = staging_bytes ? rc.staging : nullptr;
     // History slot pointers per layout, and types.
     std::vector<int> types(nh);
     for (size_t h = 0; h < nh; ++h) {
@@ -1372,11 +1432,15 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
     int* types_dev = nullptr;
     void** hptr_dev = nullptr;  // [2][nh]
     if (nh) {
-      ck(cudaMalloc((void**)&types_dev, nh * sizeof(int)), "cudaMalloc(types)");
-      cleanup.ptrs.push_back(types_dev);
+      if (nh > rc.nh_cap) {
+        size_t tcap = rc.nh_cap, pcap = 2 * rc.nh_cap;
+        grow(rc.types, tcap, nh, "cudaMalloc(types)");
+        grow(rc.hptr, pcap, 2 * nh, "cudaMalloc(history pointers)");
+        rc.nh_cap = nh;
+      }
+      types_dev = rc.types;
+      hptr_dev = rc.hptr;
       ck(cudaMemcpyAsync(types_dev, types.data(), nh * sizeof(int), cudaMemcpyHostToDevice, s), "upload types");
-      ck(cudaMalloc((void**)&hptr_dev, 2 * nh * sizeof(void*)), "cudaMalloc(history pointers)");
-      cleanup.ptrs.push_back(hptr_dev);
     }
     // The two layouts: the current one, and the one after applying every swap.
     std::vector<char*> layout[2];
@@ -1384,10 +1448,44 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
     layout[1] = f->ptr;
     for (auto& sw : swaps) std::swap(layout[1][sw.first], layout[1][sw.second]);
     bool alternating = !swaps.empty();
+    bool use_graphs = graphs_enabled() && p->capturable;
+    const bool split = dist_active();
+    // What a captured step depends on besides the layouts.
+    std::vector<uintptr_t> key;
+    auto put = [&](uintptr_t v) { key.push_back(v); };
+    put(spec->n_state);
+    for (size_t k = 0; k < spec->n_state; ++k) {
+      put(spec->state_inputs[k]);
+      put(spec->state_outputs[k]);
+    }
+    put(spec->n_data);
+    for (size_t d = 0; d < spec->n_data; ++d) {
+      put(spec->data_inputs[d]);
+      put((uintptr_t)batch_dev[d]);
+    }
+    put(nh);
+    for (size_t h = 0; h < nh; ++h) put(spec->history_outputs[h]);
+    put(n_batches);
+    for (const void* q : {(const void*)hist_dev, (const void*)ctr, (const void*)staging, (const void*)types_dev, (const void*)hptr_dev}) put((uintptr_t)q);
+    put(split);
+    // The loop starts in layout `L`; a cached capture whose layouts are this run's in the other
+    // order is replayed with the layouts renamed to its order.
+    int L = 0;
+    bool reuse = false;
+    if (use_graphs && rc.captured && rc.key == key && rc.alternating == alternating) {
+      if (rc.layout[0] == layout[0] && rc.layout[1] == layout[1]) {
+        reuse = true;
+      } else if (alternating && rc.layout[0] == layout[1] && rc.layout[1] == layout[0]) {
+        reuse = true;
+        std::swap(layout[0], layout[1]);
+        L = 1;
+      }
+    }
+    if (!reuse) rc.drop_graphs();
     if (nh) {
       std::vector<void*> hp(2 * nh);
-      for (int L = 0; L < 2; ++L)
-        for (size_t h = 0; h < nh; ++h) hp[L * nh + h] = layout[L][plan.outputs[spec->history_outputs[h]].slot];
+      for (int LL = 0; LL < 2; ++LL)
+        for (size_t h = 0; h < nh; ++h) hp[LL * nh + h] = layout[LL][plan.outputs[spec->history_outputs[h]].slot];
       ck(cudaMemcpyAsync(hptr_dev, hp.data(), hp.size() * sizeof(void*), cudaMemcpyHostToDevice, s), "upload history pointers");
     }
     long long init[2] = {0, -1};
@@ -1396,58 +1494,42 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
     // One step with layout L: batch load, the plan's steps [first, last), history, copies
     // (through staging), counter. The batch load belongs to the first piece of a step and the
     // rest to the last.
-    auto step_part = [&](int L, cudaStream_t st, size_t first, size_t last) {
-      f->ptr = layout[L];
+    auto step_part = [&](int LL, cudaStream_t st, size_t first, size_t last) {
+      f->ptr = layout[LL];
       if (first == 0 && n_batches > 1)
         for (size_t d = 0; d < spec->n_data; ++d)
           load_batch(f->ptr[plan.input_slots[spec->data_inputs[d]]], batch_dev[d], in_bytes(spec->data_inputs[d]), (long long)n_batches, ctr, st);
       Ctx c{st, f};
       for (size_t k = first; k < last; ++k) p->steps[k].run(c);
       if (last < p->steps.size()) return;
-      if (nh) record_history(hist_dev, (const void* const*)(hptr_dev + L * nh), types_dev, (int)nh, ctr, ctr + 1, st);
+      if (nh) record_history(hist_dev, (const void* const*)(hptr_dev + LL * nh), types_dev, (int)nh, ctr, ctr + 1, st);
       size_t off = 0;
       for (auto& cp : copies) {
-        ck(cudaMemcpyAsync(staging + off, layout[L][std::get<1>(cp)], std::get<2>(cp), cudaMemcpyDeviceToDevice, st), "state copy");
+        ck(cudaMemcpyAsync(staging + off, layout[LL][std::get<1>(cp)], std::get<2>(cp), cudaMemcpyDeviceToDevice, st), "state copy");
         off += align_up(std::get<2>(cp));
       }
       off = 0;
       for (auto& cp : copies) {
-        ck(cudaMemcpyAsync(layout[alternating ? 1 - L : L][std::get<0>(cp)], staging + off, std::get<2>(cp), cudaMemcpyDeviceToDevice, st), "state copy");
+        ck(cudaMemcpyAsync(layout[alternating ? 1 - LL : LL][std::get<0>(cp)], staging + off, std::get<2>(cp), cudaMemcpyDeviceToDevice, st), "state copy");
         off += align_up(std::get<2>(cp));
       }
       bump_counter(ctr, st);
     };
-    bool use_graphs = graphs_enabled() && p->capturable;
     // A step replays as pieces: CUDA graphs for the runs of steps between collectives, and under
     // data parallelism each collective launched directly (so that a stalled one can be aborted).
-    struct Piece {
-      cudaGraphExec_t g[2] = {nullptr, nullptr};
-      size_t first = 0, last = 0;  // plan steps; a direct piece has last == first + 1
-      bool direct = false;
-    };
-    std::vector<Piece> pieces;
-    struct GraphCleanup {
-      std::vector<Piece>& pieces;
-      bool two;
-      ~GraphCleanup() {
-        for (auto& pc : pieces) {
-          if (pc.g[0]) cudaGraphExecDestroy(pc.g[0]);
-          if (two && pc.g[1]) cudaGraphExecDestroy(pc.g[1]);
-        }
-      }
-    } graph_cleanup{pieces, alternating};
-    if (use_graphs) {
-      const bool split = dist_active();
+    std::vector<Frame::RunPiece>& pieces = rc.pieces;
+    const auto t_setup = Clock::now();
+    if (use_graphs && !reuse) {
       size_t start = 0;
       for (size_t k = 0; k <= p->steps.size(); ++k) {
         const bool cut = k == p->steps.size() || (split && p->steps[k].collective);
         if (!cut) continue;
-        Piece pc;
+        Frame::RunPiece pc;
         pc.first = start;
         pc.last = k;
         pieces.push_back(pc);
         if (k < p->steps.size()) {
-          Piece d;
+          Frame::RunPiece d;
           d.first = k;
           d.last = k + 1;
           d.direct = true;
@@ -1457,7 +1539,7 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
       }
       // The last graph piece carries the step's epilogue, even when the plan ends in a collective.
       if (pieces.back().direct) {
-        Piece tail;
+        Frame::RunPiece tail;
         tail.first = tail.last = p->steps.size();
         pieces.push_back(tail);
       }
@@ -1467,7 +1549,13 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
           pc.g[LL] = capture(s, [&](cudaStream_t st) { step_part(LL, st, pc.first, pc.last); });
         if (!alternating) pc.g[1] = pc.g[0];
       }
+      rc.key = key;
+      rc.alternating = alternating;
+      rc.layout[0] = layout[0];
+      rc.layout[1] = layout[1];
+      rc.captured = true;
     }
+    const auto t_capture = Clock::now();
     uint64_t per_step = (uint64_t)p->kernels_per_step + (nh ? 1 : 0) + 1 + (n_batches > 1 ? spec->n_data : 0);
     // State snapshot buffers (chunk starts), sized by the state inputs.
     std::vector<std::pair<size_t, size_t>> snap_items;  // (input slot, bytes)
@@ -1479,12 +1567,11 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
     }
     char* snap = nullptr;
     if (snap_bytes) {
-      ck(cudaMalloc((void**)&snap, snap_bytes), "cudaMalloc(snapshot)");
-      cleanup.ptrs.push_back(snap);
+      grow(rc.snap, rc.snap_cap, snap_bytes, "cudaMalloc(snapshot)");
+      snap = rc.snap;
     }
     const char* env_chunk = getenv("RGC_RUN_CHUNK");
     size_t chunk = env_chunk ? (size_t)std::max(1, atoi(env_chunk)) : 64;
-    int L = 0;
     size_t done = 0;
     long long bad = -1;
     ck(cudaStreamSynchronize(s), "run setup");
@@ -1565,6 +1652,7 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
     }
     ck(cudaEventRecord(ev1, s), "cudaEventRecord");
     ck(cudaStreamSynchronize(s), "run");
+    const auto t_loop = Clock::now();
     float ms = 0;
     ck(cudaEventElapsedTime(&ms, ev0, ev1), "cudaEventElapsedTime");
     *seconds = ms * 1e-3;
@@ -1586,6 +1674,12 @@ __attribute__((visibility("default"))) int rgc_exec_run(rgc_exec* e, const rgc_r
     }
     // The frame keeps the layout after the last step's swaps: the state is in the input slots.
     f->ptr = layout[L];
+    if (trace) {
+      auto ms_between = [](Clock::time_point a, Clock::time_point b) { return std::chrono::duration<double, std::milli>(b - a).count(); };
+      fprintf(stderr, "[rgc run] steps %zu: setup %.3f ms, capture %.3f ms (%s), loop %.3f ms (device %.3f ms), read-back %.3f ms\n", done,
+              ms_between(t_start, t_setup), ms_between(t_setup, t_capture), !use_graphs ? "no graphs" : reuse ? "cached" : "captured",
+              ms_between(t_capture, t_loop), (double)ms, ms_between(t_loop, Clock::now()));
+    }
     if (!f->failed) check_tc_error(e);
     if (f->failed) return fail(RGC_ERR_DEVICE, f->error);
     return RGC_OK;

@@ -54,8 +54,8 @@ class CudaExec : public Exec {
     if (!failed_read_.empty()) return failed_read_;
     return std::nullopt;
   }
-  bool run(const RunSpec& spec, const std::vector<Tensor>& state, const std::vector<std::vector<Tensor>>& batches, size_t steps,
-           RunOut* out) override {
+  bool run(const RunSpec& spec, const std::vector<const Tensor*>& state, const std::vector<std::vector<const Tensor*>>& batches,
+           size_t steps, RunOut* out) override {
     std::vector<size_t> si, so;
     for (auto& [i, o] : spec.state) {
       si.push_back(i);
@@ -63,18 +63,24 @@ class CudaExec : public Exec {
     }
     rgc_run_spec rs{si.data(), so.data(), si.size(), spec.data.data(), spec.data.size(), spec.history.data(), spec.history.size()};
     std::vector<const void*> st;
-    for (auto& t : state) st.push_back(t.data.data());
+    for (const Tensor* t : state) st.push_back(t->data.data());
     const void* const* state_ptrs = spec.resident ? nullptr : st.data();
     std::vector<const void*> bt;
     for (auto& b : batches)
-      for (size_t d = 0; d < spec.data.size(); ++d) bt.push_back(b[d].data.data());
+      for (size_t d = 0; d < spec.data.size(); ++d) bt.push_back(b[d]->data.data());
     std::vector<double> hist(spec.history.size() * steps);
     std::vector<Buf> outs;
     std::vector<void*> optr;
     std::vector<size_t> obytes;
-    for (auto& o : plan_.outputs) {
-      outs.emplace_back(plan_.slots[o.slot].first, o.n);
+    // State outputs get no host buffer here: they come back once, as the new state (below), and
+    // the outputs hold empty placeholders for them (`state_outputs_elided`); a resident run
+    // leaves the state on the device and its placeholders stay empty.
+    std::vector<bool> is_state(plan_.outputs.size(), false);
+    for (auto& [i, o] : spec.state) {
+      (void)i;
+      is_state[o] = true;
     }
+    for (size_t o = 0; o < plan_.outputs.size(); ++o) outs.emplace_back(plan_.slots[plan_.outputs[o].slot].first, is_state[o] ? 0 : plan_.outputs[o].n);
     for (auto& b : outs) {
       optr.push_back(b.data());
       obytes.push_back(b.bytes());
@@ -101,11 +107,14 @@ class CudaExec : public Exec {
         Buf b(plan_.slots[slot].first, plan_.input_ns[i]);
         rgc_exec_prefix(e_, slot, b.data(), b.bytes());
         out->state.emplace_back(plan_.outputs[o].shape, std::move(b));
-        if (done) outs[o] = out->state.back().data;  // the last step's state output is the new state
       }
+      out->state_outputs_elided = done > 0;
     }
     if (done) {
-      for (size_t o = 0; o < plan_.outputs.size(); ++o) out->outputs.emplace_back(plan_.outputs[o].shape, std::move(outs[o]));
+      for (size_t o = 0; o < plan_.outputs.size(); ++o) {
+        std::vector<size_t> shape = outs[o].n == 0 && is_state[o] ? std::vector<size_t>{0} : plan_.outputs[o].shape;
+        out->outputs.emplace_back(shape, std::move(outs[o]));
+      }
     }
     return true;
   }

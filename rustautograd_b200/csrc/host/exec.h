@@ -29,6 +29,9 @@ struct RunOut {
   std::optional<size_t> nonfinite_step;
   double seconds = 0;
   std::optional<std::string> device_error;
+  // Set by a device run that returns state outputs only once, as `state`: outputs[o] of every
+  // state pair (i, o) is then an empty placeholder whose value is the matching state tensor.
+  bool state_outputs_elided = false;
 };
 
 struct Exec {
@@ -50,7 +53,10 @@ struct Exec {
   virtual bool load_slots(const std::string&, const std::vector<uint64_t>&, const std::vector<size_t>&, const std::vector<size_t>&) { return false; }
   // A device-resident implementation of the whole multi-step loop. Returns false when the
   // device has none, and the host loop (run_loop) drives load/step/swap instead.
-  virtual bool run(const RunSpec&, const std::vector<Tensor>&, const std::vector<std::vector<Tensor>>&, size_t, RunOut*) { return false; }
+  // State and batch tensors are borrowed for the call (no host copies of them are made).
+  virtual bool run(const RunSpec&, const std::vector<const Tensor*>&, const std::vector<std::vector<const Tensor*>>&, size_t, RunOut*) {
+    return false;
+  }
 };
 
 struct Program {

@@ -64,6 +64,14 @@ std::vector<Tensor> tensors(const std::vector<PyTensor>& v) {
   return out;
 }
 
+// Borrowed views of Python-held tensors (immutable, kept alive by the caller's list).
+std::vector<const Tensor*> refs(const std::vector<PyTensor>& v) {
+  std::vector<const Tensor*> out;
+  out.reserve(v.size());
+  for (auto& p : v) out.push_back(p.t.get());
+  return out;
+}
+
 std::vector<PyTensor> wrap(std::vector<Tensor> v) {
   std::vector<PyTensor> out;
   for (auto& t : v) out.push_back(PyTensor{std::make_shared<const Tensor>(std::move(t))});
@@ -301,8 +309,8 @@ PYBIND11_MODULE(RG_MODULE_NAME, m) {
 
   py::class_<PySession>(m, "Session")
       .def("run", [](PySession& self, std::vector<std::vector<PyTensor>> batches, size_t steps) {
-        std::vector<std::vector<Tensor>> bs;
-        for (auto& b : batches) bs.push_back(tensors(b));
+        std::vector<std::vector<const Tensor*>> bs;
+        for (auto& b : batches) bs.push_back(refs(b));
         RunOut out;
         {
           py::gil_scoped_release nogil;
@@ -312,7 +320,9 @@ PYBIND11_MODULE(RG_MODULE_NAME, m) {
             self.resident = self.e->run(spec, {}, bs, steps, &out);
           }
           if (!self.resident) {
-            out = run_loop(self.c->plan, *self.e, self.spec, self.host_state, bs, steps);
+            std::vector<std::vector<Tensor>> owned;
+            for (auto& b : batches) owned.push_back(tensors(b));
+            out = run_loop(self.c->plan, *self.e, self.spec, self.host_state, owned, steps);
             self.host_state = out.state;
           }
         }
@@ -442,13 +452,13 @@ PYBIND11_MODULE(RG_MODULE_NAME, m) {
           self.c->validate_spec(spec);
           return 0;
         });
-        auto st = tensors(state);
-        std::vector<std::vector<Tensor>> bs;
-        for (auto& b : batches) bs.push_back(tensors(b));
+        auto st = refs(state);
+        std::vector<std::vector<const Tensor*>> bs;
+        for (auto& b : batches) bs.push_back(refs(b));
         RunOut out;
         {
           py::gil_scoped_release nogil;
-          out = self.c->run(spec, st, bs, steps);
+          out = self.c->run_refs(spec, st, bs, steps);
         }
         if (out.device_error) {
           Json d = device_failure(self.c->device->name(), *out.device_error);
@@ -456,7 +466,13 @@ PYBIND11_MODULE(RG_MODULE_NAME, m) {
           raise_diag(d);
         }
         std::optional<size_t> bad = out.nonfinite_step;
-        return py::make_tuple(wrap(std::move(out.state)), wrap(std::move(out.outputs)), out.history, out.steps, bad, out.seconds);
+        auto new_state = wrap(std::move(out.state));
+        auto outputs = wrap(std::move(out.outputs));
+        // A state output's value is the new state tensor: share it rather than copy it.
+        if (out.state_outputs_elided)
+          for (size_t k = 0; k < state_map.size() && k < new_state.size(); ++k)
+            if (state_map[k].second < outputs.size()) outputs[state_map[k].second] = new_state[k];
+        return py::make_tuple(new_state, outputs, out.history, out.steps, bad, out.seconds);
       })
       .def("replay", [](const PyCompiled& self, std::vector<std::pair<size_t, size_t>> state_map, std::vector<size_t> data_inputs,
                         std::vector<size_t> history, std::vector<PyTensor> state, std::vector<std::vector<PyTensor>> batches, size_t steps) -> py::object {

@@ -831,20 +831,46 @@ void Compiled::validate_spec(const RunSpec& spec) const {
 }
 
 // validate.rs:937-951
-RunOut Compiled::run(const RunSpec& spec, const std::vector<Tensor>& state, const std::vector<std::vector<Tensor>>& batches, size_t steps) const {
+RunOut Compiled::run_refs(const RunSpec& spec, const std::vector<const Tensor*>& state, const std::vector<std::vector<const Tensor*>>& batches,
+                          size_t steps) const {
+  auto owned = [](const std::vector<const Tensor*>& v) {
+    std::vector<Tensor> out;
+    out.reserve(v.size());
+    for (const Tensor* t : v) out.push_back(*t);
+    return out;
+  };
   std::unique_ptr<Exec> e;
   try {
     e = program->exec();
   } catch (const std::exception& ex) {
     RunOut r;
-    r.state = state;
+    r.state = owned(state);
     r.history.assign(spec.history.size(), {});
     r.device_error = ex.what();
     return r;
   }
   RunOut r;
   if (e->run(spec, state, batches, steps, &r)) return r;
-  return run_loop(plan, *e, spec, state, batches, steps);
+  std::vector<std::vector<Tensor>> bs;
+  for (auto& b : batches) bs.push_back(owned(b));
+  return run_loop(plan, *e, spec, owned(state), bs, steps);
+}
+
+RunOut Compiled::run(const RunSpec& spec, const std::vector<Tensor>& state, const std::vector<std::vector<Tensor>>& batches, size_t steps) const {
+  std::vector<const Tensor*> sp;
+  for (auto& t : state) sp.push_back(&t);
+  std::vector<std::vector<const Tensor*>> bp;
+  for (auto& b : batches) {
+    bp.emplace_back();
+    for (auto& t : b) bp.back().push_back(&t);
+  }
+  RunOut r = run_refs(spec, sp, bp, steps);
+  if (r.state_outputs_elided) {
+    for (size_t k = 0; k < spec.state.size() && k < r.state.size(); ++k)
+      if (spec.state[k].second < r.outputs.size()) r.outputs[spec.state[k].second] = r.state[k];
+    r.state_outputs_elided = false;
+  }
+  return r;
 }
 
 // validate.rs:955-970

@@ -38,6 +38,9 @@ class Compiled {
   Json profile(const std::vector<Tensor>& inputs, size_t repeats) const;
   void validate_spec(const RunSpec& spec) const;
   RunOut run(const RunSpec& spec, const std::vector<Tensor>& state, const std::vector<std::vector<Tensor>>& batches, size_t steps) const;
+  // The same run over borrowed tensors; the result may have `state_outputs_elided` set.
+  RunOut run_refs(const RunSpec& spec, const std::vector<const Tensor*>& state, const std::vector<std::vector<const Tensor*>>& batches,
+                  size_t steps) const;
   // (step, batch index, state before it) of the first non-finite step, if any.
   bool replay(const RunSpec& spec, const std::vector<Tensor>& state, const std::vector<std::vector<Tensor>>& batches, size_t steps,
               size_t* step, size_t* batch, std::vector<Tensor>* before) const;
