@@ -33,6 +33,7 @@ const Driver& Driver::get() {
     load("cuModuleGetFunction", (void**)&x.ModuleGetFunction);
     load("cuModuleUnload", (void**)&x.ModuleUnload);
     load("cuLaunchKernel", (void**)&x.LaunchKernel);
+    load("cuOccupancyMaxActiveBlocksPerMultiprocessor", (void**)&x.OccupancyMaxActiveBlocksPerMultiprocessor);
     return x;
   }();
   return d;
@@ -95,6 +96,32 @@ template <typename T, int V> __device__ __forceinline__ void rg_row_fill(T* r, c
     for (int j = 0; j < V; ++j) { unsigned ej = e + j; r[j] = p[ej - rg_fdiv(ej, f) * f.d]; }
   }
 }
+// V consecutive elements of a column input (value e / f.d for element e).
+template <typename T, int V> __device__ __forceinline__ void rg_col_fill(T* r, const T* p, unsigned e, const FDiv& f) {
+  const unsigned q = rg_fdiv(e, f);
+  if (e - q * f.d + V <= f.d) {
+    const T v = p[q];
+    #pragma unroll
+    for (int j = 0; j < V; ++j) r[j] = v;
+  } else {
+    #pragma unroll
+    for (int j = 0; j < V; ++j) r[j] = p[rg_fdiv(e + j, f)];
+  }
+}
+// IEEE x / y. A zero numerator would send the division down its slow path (taken when the
+// quotient may underflow), which costs several times the fast one; causal masks make half of a
+// softmax's numerators zero. For y neither zero nor NaN the quotient is a zero with the sign of
+// x * y, so zero numerators are answered directly and never enter the division.
+__device__ __forceinline__ float rg_div(float x, float y) {
+  const bool z = x == 0.0f && y == y && y != 0.0f;
+  const float q = (z ? 1.0f : x) / y;
+  return z ? __int_as_float((__float_as_int(x) ^ __float_as_int(y)) & (int)0x80000000u) : q;
+}
+__device__ __forceinline__ double rg_div(double x, double y) {
+  const bool z = x == 0.0 && y == y && y != 0.0;
+  const double q = (z ? 1.0 : x) / y;
+  return z ? __longlong_as_double((__double_as_longlong(x) ^ __double_as_longlong(y)) & (long long)0x8000000000000000ull) : q;
+}
 __device__ __forceinline__ float rg_nan(float) { return __int_as_float(0x7fc00000); }
 __device__ __forceinline__ double rg_nan(double) { return __longlong_as_double(0x7ff8000000000000LL); }
 template <typename T> __device__ __forceinline__ T rg_max(T a, T b) { return a > b ? a : (b >= a ? b : rg_nan(a)); }
@@ -135,7 +162,7 @@ std::string expr(DType d, const rg::Op& op, const std::vector<std::string>& a) {
     case OpKind::Add: return I ? "rg_iadd(" + a[0] + "," + a[1] + ")" : "(" + a[0] + " + " + a[1] + ")";
     case OpKind::Sub: return I ? "rg_isub(" + a[0] + "," + a[1] + ")" : "(" + a[0] + " - " + a[1] + ")";
     case OpKind::Mul: return I ? "rg_imul(" + a[0] + "," + a[1] + ")" : "(" + a[0] + " * " + a[1] + ")";
-    case OpKind::Div: return "(" + a[0] + " / " + a[1] + ")";
+    case OpKind::Div: return I ? "(" + a[0] + " / " + a[1] + ")" : "rg_div(" + a[0] + "," + a[1] + ")";
     case OpKind::Pow: return (d == DType::F64 ? "pow(" : "powf(") + a[0] + "," + a[1] + ")";
     case OpKind::Max: return "rg_max<" + T + ">(" + a[0] + "," + a[1] + ")";
     case OpKind::Min: return "rg_min<" + T + ">(" + a[0] + "," + a[1] + ")";
@@ -150,7 +177,7 @@ std::string expr(DType d, const rg::Op& op, const std::vector<std::string>& a) {
 
 std::string ElemSpec::source_key() const {
   std::string k = "d" + std::to_string((int)dtype) + "|";
-  for (auto& in : inputs) k += std::to_string((int)in.kind) + ",";
+  for (auto& in : inputs) k += std::to_string((int)in.kind) + (in.col ? "c," : ",");
   k += "|";
   for (auto& m : ops) {
     k += std::to_string((int)m.op.kind) + ":" + std::to_string(m.reg) + "(";
@@ -160,6 +187,14 @@ std::string ElemSpec::source_key() const {
   k += "|";
   for (auto r : out_regs) k += std::to_string(r) + ",";
   return k;
+}
+
+// The column length when a broadcast input has the output's shape with a last extent of 1.
+static size_t column_of(const std::vector<size_t>& in, const std::vector<size_t>& out) {
+  if (in.size() != out.size() || out.empty() || in.back() != 1 || out.back() <= 1) return 0;
+  for (size_t d = 0; d + 1 < out.size(); ++d)
+    if (in[d] != out[d]) return 0;
+  return out.back();
 }
 
 ElemSpec spec_from_group(const rg::Fused& f) {
@@ -173,7 +208,10 @@ ElemSpec spec_from_group(const rg::Fused& f) {
     in.kind = f.inputs[k].kind;
     in.row = f.inputs[k].row;
     in.shape = f.input_shapes[k];
-    if (in.kind == ArgKind::Broadcast) in.bc = nbc++;
+    if (in.kind == ArgKind::Broadcast) {
+      in.bc = nbc++;
+      in.col = column_of(in.shape, f.shape);
+    }
     s.inputs.push_back(in);
   }
   s.ops = f.ops;
@@ -203,6 +241,7 @@ ElemSpec spec_from_instr(const rg::Instr& i) {
     } else {
       in.kind = ArgKind::Broadcast;
       in.bc = nbc++;
+      in.col = column_of(as, i.shape);
     }
     if (in.kind == ArgKind::Full) {
       m.args.push_back(rg::Operand{false, k});
@@ -241,10 +280,15 @@ static std::string kernel_source(const ElemSpec& s, const std::string& name) {
       o << expr(s.dtype, m.op, args) << ";\n";
     }
   };
-  o << "extern \"C\" __global__ void __launch_bounds__(256) " << name << "(const ElemArgs a) {\n";
-  for (size_t k = 0; k < s.inputs.size(); ++k)
-    if (s.inputs[k].kind == ArgKind::Splat) o << "  const " << T << " sp" << k << " = " << in_ptr(k) << "[0];\n";
-  o << "  if (a.small) {\n";
+  // Two kernels: `name` for n < 2^31 with 32-bit index math, `name_w` with 64-bit index math.
+  // Separate kernels keep the 64-bit path's registers out of the common one's occupancy.
+  auto header = [&](const std::string& fn) {
+    o << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const ElemArgs a) {\n";
+    for (size_t k = 0; k < s.inputs.size(); ++k)
+      if (s.inputs[k].kind == ArgKind::Splat) o << "  const " << T << " sp" << k << " = " << in_ptr(k) << "[0];\n";
+  };
+  header(name);
+  o << "  {\n";
   o << "    const unsigned n = (unsigned)a.n, tid = blockIdx.x * blockDim.x + threadIdx.x, stride = gridDim.x * blockDim.x;\n";
   // Vector path: two 16-byte vectors per thread per iteration (all loads before any store).
   o << "    if (a.vec) {\n";
@@ -270,6 +314,9 @@ static std::string kernel_source(const ElemSpec& s, const std::string& name) {
       } else if (in.kind == ArgKind::Row) {
         o << "      rg_row_fill<" << T << ", " << VW << ">(r" << r << ", " << in_ptr(k) << ", ea, a.row[" << k << "]);\n";
         o << "      rg_row_fill<" << T << ", " << VW << ">(r" << r << " + " << VW << ", " << in_ptr(k) << ", eb, a.row[" << k << "]);\n";
+      } else if (in.col) {
+        o << "      rg_col_fill<" << T << ", " << VW << ">(r" << r << ", " << in_ptr(k) << ", ea, a.row[" << k << "]);\n";
+        o << "      rg_col_fill<" << T << ", " << VW << ">(r" << r << " + " << VW << ", " << in_ptr(k) << ", eb, a.row[" << k << "]);\n";
       } else {
         o << "      rg_bc_fill<" << T << ", " << VW << ">(r" << r << ", " << in_ptr(k) << ", a.bc[" << in.bc << "], ea);\n";
         o << "      rg_bc_fill<" << T << ", " << VW << ">(r" << r << " + " << VW << ", " << in_ptr(k) << ", a.bc[" << in.bc << "], eb);\n";
@@ -297,6 +344,7 @@ static std::string kernel_source(const ElemSpec& s, const std::string& name) {
       o << "      " << T << " r" << r << "[1];\n";
       if (in.kind == ArgKind::Splat) o << "      r" << r << "[0] = sp" << k << ";\n";
       else if (in.kind == ArgKind::Row) o << "      r" << r << "[0] = " << in_ptr(k) << "[e - rg_fdiv(e, a.row[" << k << "]) * a.row[" << k << "].d];\n";
+      else if (in.col) o << "      r" << r << "[0] = " << in_ptr(k) << "[rg_fdiv(e, a.row[" << k << "])];\n";
       else o << "      { unsigned c; r" << r << "[0] = " << in_ptr(k) << "[rg_bc_off(a.bc[" << in.bc << "], e, &c)]; }\n";
     }
   }
@@ -304,7 +352,9 @@ static std::string kernel_source(const ElemSpec& s, const std::string& name) {
   for (size_t q = 0; q < s.out_regs.size(); ++q) o << "      ((" << T << "*)a.out[" << q << "])[e] = r" << s.out_regs[q] << "[0];\n";
   o << "     }\n    }\n";
   // 64-bit path for 2^31 elements or more.
-  o << "  } else {\n";
+  o << "  }\n}\n";
+  header(name + "_w");
+  o << "  {\n";
   o << "    const long long n = a.n, tid = (long long)blockIdx.x * blockDim.x + threadIdx.x, stride = (long long)gridDim.x * blockDim.x;\n";
   o << "    for (long long e = tid; e < n; e += stride) {\n";
   for (size_t k = 0; k < s.inputs.size(); ++k) {
@@ -359,7 +409,7 @@ void Jit::build() {
   }
   const char* opts[] = {"--gpu-architecture=sm_100a", "--fmad=false", "--prec-div=true", "--prec-sqrt=true", "--ftz=false", "-default-device",
                         "--std=c++17"};
-  std::string path = cache_dir() + "/" + std::to_string(fnv1a(src + "v2")) + ".cubin";
+  std::string path = cache_dir() + "/" + std::to_string(fnv1a(src + "v3")) + ".cubin";
   std::vector<char> cubin;
   {
     std::ifstream f(path, std::ios::binary);
@@ -393,11 +443,12 @@ void Jit::build() {
   CUresult lr = d.ModuleLoadData(&mod, cubin.data());
   if (lr != CUDA_SUCCESS) throw std::runtime_error("loading the fused-kernel module failed (CUresult " + std::to_string((int)lr) + ")");
   modules_.push_back(mod);
-  for (auto& name : names) {
-    CUfunction fn;
-    if (d.ModuleGetFunction(&fn, mod, name.c_str()) != CUDA_SUCCESS) throw std::runtime_error("missing fused kernel " + name);
-    built_[name] = fn;
-  }
+  for (auto& name : names)
+    for (const std::string& fname : {name, name + "_w"}) {
+      CUfunction fn;
+      if (d.ModuleGetFunction(&fn, mod, fname.c_str()) != CUDA_SUCCESS) throw std::runtime_error("missing fused kernel " + fname);
+      built_[fname] = fn;
+    }
   pending_.clear();
 }
 
@@ -414,9 +465,24 @@ void Jit::launch(CUfunction f, const ElemArgs& a, long long n, int vec_width, cu
     cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
     return v;
   }();
+  // One wave of resident blocks: how many fit per SM depends on the generated kernel's
+  // registers (a fixed 8 per SM would leave a partial second wave above 32 registers).
+  static std::mutex mu;
+  static std::unordered_map<CUfunction, int> resident;
+  int per_sm = 0;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = resident.find(f);
+    if (it != resident.end()) {
+      per_sm = it->second;
+    } else {
+      if (Driver::get().OccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, f, 256, 0) != CUDA_SUCCESS || per_sm <= 0) per_sm = 1;
+      resident[f] = per_sm;
+    }
+  }
   long long work = a.vec ? (n / vec_width + 1) / 2 : n;
   long long blocks = (work + 255) / 256;
-  long long cap = (long long)sms * 8;
+  long long cap = (long long)sms * per_sm;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   void* params[] = {(void*)&a};

@@ -29,7 +29,7 @@ struct ElemArgs {
   int small;  // 1: n < 2^31 and every merged broadcast extent fits, so index math is 32-bit
   void* out[JIT_MAX_OUT];
   const void* in[JIT_MAX_IN];
-  FDiv row[JIT_MAX_IN];  // row length of each row input
+  FDiv row[JIT_MAX_IN];  // row length of each row input, output last extent of each column input
   const FDims* bc;       // device array: one merged descriptor per broadcast input
   const Dims* bc64;      // device array: the same descriptors unmerged, for the 64-bit path
 };
@@ -42,6 +42,9 @@ struct ElemSpec {
     rg::ArgKind kind;
     size_t row = 0;
     int bc = -1;  // broadcast descriptor index
+    // A broadcast input of the output's shape with a last extent of 1 (a softmax or LayerNorm
+    // statistic): element e reads value e / col, with col the output's last extent.
+    size_t col = 0;
     std::vector<size_t> shape;
   };
   std::vector<In> inputs;
@@ -77,6 +80,7 @@ struct Driver {
   CUresult (*ModuleGetFunction)(CUfunction*, CUmodule, const char*) = nullptr;
   CUresult (*ModuleUnload)(CUmodule) = nullptr;
   CUresult (*LaunchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, CUstream, void**, void**) = nullptr;
+  CUresult (*OccupancyMaxActiveBlocksPerMultiprocessor)(int*, CUfunction, int, size_t) = nullptr;
   static const Driver& get();
 };
 

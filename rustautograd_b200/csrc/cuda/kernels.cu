@@ -4,6 +4,9 @@
 #include <cfloat>
 #include <cmath>
 #include <cstdio>
+#include <map>
+#include <mutex>
+#include <tuple>
 #include <type_traits>
 
 #include "kernels.cuh"
@@ -26,6 +29,35 @@ int sm_count() {
 unsigned grid_for(long long n, int threads = 256) {
   long long b = (n + threads - 1) / threads;
   long long cap = (long long)sm_count() * 8;
+  if (b > cap) b = cap;
+  if (b < 1) b = 1;
+  return (unsigned)b;
+}
+
+// Blocks of `kernel` resident on one SM at `threads` threads per block (its registers and shared
+// memory decide it), looked up once per kernel and block size.
+int resident_blocks(const void* kernel, int threads, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, size_t>, int> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  auto key = std::make_tuple(kernel, threads, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int nb = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kernel, threads, smem) != cudaSuccess || nb <= 0) {
+    cudaGetLastError();
+    nb = 1;
+  }
+  cache[key] = nb;
+  return nb;
+}
+
+// A grid-stride launch of `kernel` over n work items, covering the GPU in exactly one wave: as
+// many blocks as are resident at once (fewer when n is small). A fixed 8 blocks per SM would
+// leave a partial second wave for kernels that need more than 32 registers per thread.
+template <typename K> unsigned grid_k(K* kernel, long long n, int threads = 256, size_t smem = 0) {
+  long long b = (n + threads - 1) / threads;
+  long long cap = (long long)sm_count() * resident_blocks((const void*)kernel, threads, smem);
   if (b > cap) b = cap;
   if (b < 1) b = 1;
   return (unsigned)b;
@@ -451,6 +483,7 @@ __global__ void k_reduce_rows_warp_vec(T* __restrict__ dst, const T* __restrict_
   for (long long r = warp; r < rows; r += nwarps) {
     const VT* row = (const VT*)(a + r * len);
     T acc = red_init<T>(op);
+#pragma unroll 4
     for (long long j = lane; j < nv; j += 32) {
       const VT v = row[j];
       const T* e = (const T*)&v;
@@ -480,6 +513,9 @@ __global__ void k_rows_fast_sum_vec(T* __restrict__ dst, const T* __restrict__ a
     for (int e = 0; e < E; ++e) acc[e] = (T)0;
     const T* row = a + (r < rows ? r : 0) * len;
     if (r < rows) {
+      // Unrolled so that several 16-byte loads are in flight per lane; the additions into each
+      // running sum stay in element order.
+#pragma unroll 4
       for (long long c = 0; c < full; c += 8) {
         const VT v = *(const VT*)(row + c + q * E);
         const T* x = (const T*)&v;
@@ -1028,30 +1064,30 @@ template <typename T> void gather_t(void* dst, const void* src, const Dims& out,
   bool ok = false;
   FDims f = fast_dims(out, &ok);
   if (!ok || n >= (1ll << 31)) {
-    k_gather<T><<<grid_for(n), 256, 0, s>>>((T*)dst, (const T*)src, out, base, n);
+    k_gather<T><<<grid_k(k_gather<T>, n), 256, 0, s>>>((T*)dst, (const T*)src, out, base, n);
     return;
   }
   constexpr int V = (int)(16 / sizeof(T));
   using VT = typename Vec16<T>::type;
   if (vec_width<T>(f, base, n) == V)
-    k_gather_vec<VT, V><<<grid_for(n / V), 256, 0, s>>>((VT*)dst, (const VT*)src, f, base, (unsigned)(n / V));
+    k_gather_vec<VT, V><<<grid_k(k_gather_vec<VT, V>, n / V), 256, 0, s>>>((VT*)dst, (const VT*)src, f, base, (unsigned)(n / V));
   else
-    k_gather32<T><<<grid_for(n), 256, 0, s>>>((T*)dst, (const T*)src, f, base, (unsigned)n);
+    k_gather32<T><<<grid_k(k_gather32<T>, n), 256, 0, s>>>((T*)dst, (const T*)src, f, base, (unsigned)n);
 }
 
 template <typename T> void scatter_t(void* dst, const void* src, const Dims& in, long long base, long long n, cudaStream_t s) {
   bool ok = false;
   FDims f = fast_dims(in, &ok);
   if (!ok || n >= (1ll << 31)) {
-    k_scatter<T><<<grid_for(n), 256, 0, s>>>((T*)dst, (const T*)src, in, base, n);
+    k_scatter<T><<<grid_k(k_scatter<T>, n), 256, 0, s>>>((T*)dst, (const T*)src, in, base, n);
     return;
   }
   constexpr int V = (int)(16 / sizeof(T));
   using VT = typename Vec16<T>::type;
   if (vec_width<T>(f, base, n) == V)
-    k_scatter_vec<VT, V><<<grid_for(n / V), 256, 0, s>>>((VT*)dst, (const VT*)src, f, base, (unsigned)(n / V));
+    k_scatter_vec<VT, V><<<grid_k(k_scatter_vec<VT, V>, n / V), 256, 0, s>>>((VT*)dst, (const VT*)src, f, base, (unsigned)(n / V));
   else
-    k_scatter32<T><<<grid_for(n), 256, 0, s>>>((T*)dst, (const T*)src, f, base, (unsigned)n);
+    k_scatter32<T><<<grid_k(k_scatter32<T>, n), 256, 0, s>>>((T*)dst, (const T*)src, f, base, (unsigned)n);
 }
 
 }  // namespace
@@ -1078,7 +1114,7 @@ void transpose_last2(void* dst, const void* src, EType t, long long batch, long 
 template <typename T>
 static void take_rows_t(void* dst, const void* src, const int32_t* idx, long long outer, long long dim, long long n_idx, long long block, cudaStream_t s) {
   long long n = outer * n_idx * block;
-  k_take_rows<T><<<grid_for(n), 256, 0, s>>>((T*)dst, (const T*)src, idx, dim, n_idx, block, n);
+  k_take_rows<T><<<grid_k(k_take_rows<T>, n), 256, 0, s>>>((T*)dst, (const T*)src, idx, dim, n_idx, block, n);
 }
 void take_rows(void* dst, const void* src, const int32_t* idx, EType t, long long outer, long long dim, long long n_idx, long long block,
                cudaStream_t s) {
@@ -1087,7 +1123,7 @@ void take_rows(void* dst, const void* src, const int32_t* idx, EType t, long lon
 }
 
 template <typename T> static void take_along_t(void* dst, const void* src, const int32_t* idx, long long n, long long v, long long k, cudaStream_t s) {
-  k_take_along<T><<<grid_for(n), 256, 0, s>>>((T*)dst, (const T*)src, idx, n, v, k);
+  k_take_along<T><<<grid_k(k_take_along<T>, n), 256, 0, s>>>((T*)dst, (const T*)src, idx, n, v, k);
 }
 void take_along(void* dst, const void* src, const int32_t* idx, EType t, long long n, long long v, long long k, cudaStream_t s) {
   if (n <= 0) return;
@@ -1127,7 +1163,7 @@ void take_grad(void* dst, const void* ct, const int32_t* idx, EType t, long long
   int* cnt = (int*)scratch;
   int* list = (int*)((char*)scratch + (dim * chunks * 4 + 255) / 256 * 256);
   cudaMemsetAsync(cnt, 0, (size_t)(dim * chunks) * 4, s);
-  k_tg_count<<<grid_for(n_idx), 256, 0, s>>>(cnt, idx, dim, n_idx, chunks);
+  k_tg_count<<<grid_k(k_tg_count, n_idx), 256, 0, s>>>(cnt, idx, dim, n_idx, chunks);
   k_tg_scan<<<1, 1024, 0, s>>>(cnt, dim * chunks);
   k_tg_place<<<(unsigned)chunks, 32, 0, s>>>(list, cnt, idx, dim, n_idx, chunks);
   const bool vec = (block * (long long)esize(t)) % 16 == 0;
@@ -1142,8 +1178,8 @@ void take_grad(void* dst, const void* ct, const int32_t* idx, EType t, long long
 
 void take_along_grad(void* dst, const void* ct, const int32_t* idx, EType t, long long rows, long long v, long long k, cudaStream_t s) {
   if (rows * v <= 0) return;
-  if (t == EType::F64) k_take_along_grad<double><<<grid_for(rows * v), 256, 0, s>>>((double*)dst, (const double*)ct, idx, rows, v, k);
-  else k_take_along_grad<float><<<grid_for(rows * v), 256, 0, s>>>((float*)dst, (const float*)ct, idx, rows, v, k);
+  if (t == EType::F64) k_take_along_grad<double><<<grid_k(k_take_along_grad<double>, rows * v), 256, 0, s>>>((double*)dst, (const double*)ct, idx, rows, v, k);
+  else k_take_along_grad<float><<<grid_k(k_take_along_grad<float>, rows * v), 256, 0, s>>>((float*)dst, (const float*)ct, idx, rows, v, k);
 }
 
 constexpr long long EXACT_SUM_MAX = 32768;
@@ -1175,9 +1211,9 @@ template <typename T> static void rows_t(void* dst, const void* src, Red op, lon
     constexpr int E = (int)(16 / sizeof(T));
     using VT = typename Vec16<T>::type;
     if (len % E == 0 && ((uintptr_t)src & 15) == 0)
-      k_rows_fast_sum_vec<T, VT, E><<<grid_for(rows * (8 / E)), 256, 0, s>>>((T*)dst, (const T*)src, rows, len);
+      k_rows_fast_sum_vec<T, VT, E><<<grid_k(k_rows_fast_sum_vec<T, VT, E>, rows * (8 / E)), 256, 0, s>>>((T*)dst, (const T*)src, rows, len);
     else
-      k_rows_fast_sum<T><<<grid_for(rows * 8), 256, 0, s>>>((T*)dst, (const T*)src, rows, len);
+      k_rows_fast_sum<T><<<grid_k(k_rows_fast_sum<T>, rows * 8), 256, 0, s>>>((T*)dst, (const T*)src, rows, len);
     return;
   }
   if (len > 2048) {
@@ -1187,9 +1223,9 @@ template <typename T> static void rows_t(void* dst, const void* src, Red op, lon
     constexpr int V = (int)(16 / sizeof(T));
     using VT = typename Vec16<T>::type;
     if (len % V == 0 && ((uintptr_t)src & 15) == 0)
-      k_reduce_rows_warp_vec<T, VT, V><<<grid_for(threads), 256, 0, s>>>((T*)dst, (const T*)src, op, rows, len);
+      k_reduce_rows_warp_vec<T, VT, V><<<grid_k(k_reduce_rows_warp_vec<T, VT, V>, threads), 256, 0, s>>>((T*)dst, (const T*)src, op, rows, len);
     else
-      k_reduce_rows_warp<T><<<grid_for(threads), 256, 0, s>>>((T*)dst, (const T*)src, op, rows, len);
+      k_reduce_rows_warp<T><<<grid_k(k_reduce_rows_warp<T>, threads), 256, 0, s>>>((T*)dst, (const T*)src, op, rows, len);
   }
 }
 void reduce_rows(void* dst, const void* src, EType t, Red op, long long rows, long long len, cudaStream_t s) {
@@ -1253,8 +1289,8 @@ void reduce_generic(void* dst, const void* src, EType t, Red op, const Dims& kep
   if (n_out <= 0) return;
   long long n_red = 1;
   for (int d = 0; d < reduced.rank; ++d) n_red *= reduced.d[d];
-  if (t == EType::F64) k_reduce_generic<double><<<grid_for(n_out), 256, 0, s>>>((double*)dst, (const double*)src, op, kept, reduced, n_out, n_red);
-  else k_reduce_generic<float><<<grid_for(n_out), 256, 0, s>>>((float*)dst, (const float*)src, op, kept, reduced, n_out, n_red);
+  if (t == EType::F64) k_reduce_generic<double><<<grid_k(k_reduce_generic<double>, n_out), 256, 0, s>>>((double*)dst, (const double*)src, op, kept, reduced, n_out, n_red);
+  else k_reduce_generic<float><<<grid_k(k_reduce_generic<float>, n_out), 256, 0, s>>>((float*)dst, (const float*)src, op, kept, reduced, n_out, n_red);
 }
 
 void gemm(void* c, const void* a, const void* b, EType t, long long m, long long n, long long k, bool ta, bool tb, const GemmBatch& batch,
@@ -1282,19 +1318,19 @@ void gemm(void* c, const void* a, const void* b, EType t, long long m, long long
 
 void key_split(int32_t* dst, const int32_t* key, long long pairs, cudaStream_t s) {
   if (pairs <= 0) return;
-  k_key_split<<<grid_for(pairs), 256, 0, s>>>(dst, key, pairs);
+  k_key_split<<<grid_k(k_key_split, pairs), 256, 0, s>>>(dst, key, pairs);
 }
 
 void rand_uniform(void* dst, const int32_t* key, EType t, long long n, cudaStream_t s) {
   if (n <= 0) return;
-  if (t == EType::F64) k_rand_uniform<double><<<grid_for(n), 256, 0, s>>>((double*)dst, key, n);
-  else k_rand_uniform<float><<<grid_for(n), 256, 0, s>>>((float*)dst, key, n);
+  if (t == EType::F64) k_rand_uniform<double><<<grid_k(k_rand_uniform<double>, n), 256, 0, s>>>((double*)dst, key, n);
+  else k_rand_uniform<float><<<grid_k(k_rand_uniform<float>, n), 256, 0, s>>>((float*)dst, key, n);
 }
 
 void rand_normal(void* dst, const int32_t* key, EType t, long long n, cudaStream_t s) {
   if (n <= 0) return;
-  if (t == EType::F64) k_rand_normal<double><<<grid_for(n), 256, 0, s>>>((double*)dst, key, n);
-  else k_rand_normal<float><<<grid_for(n), 256, 0, s>>>((float*)dst, key, n);
+  if (t == EType::F64) k_rand_normal<double><<<grid_k(k_rand_normal<double>, n), 256, 0, s>>>((double*)dst, key, n);
+  else k_rand_normal<float><<<grid_k(k_rand_normal<float>, n), 256, 0, s>>>((float*)dst, key, n);
 }
 
 void cast(void* dst, EType dt, const void* src, EType st, long long n, cudaStream_t s) {
@@ -1310,8 +1346,8 @@ void cast(void* dst, EType dt, const void* src, EType st, long long n, cudaStrea
 
 void argmax(int32_t* dst, const void* src, EType t, long long rows, long long v, cudaStream_t s) {
   if (rows <= 0) return;
-  if (t == EType::F64) k_argmax<double><<<grid_for(rows * 32), 256, 0, s>>>(dst, (const double*)src, rows, v);
-  else k_argmax<float><<<grid_for(rows * 32), 256, 0, s>>>(dst, (const float*)src, rows, v);
+  if (t == EType::F64) k_argmax<double><<<grid_k(k_argmax<double>, rows * 32), 256, 0, s>>>(dst, (const double*)src, rows, v);
+  else k_argmax<float><<<grid_k(k_argmax<float>, rows * 32), 256, 0, s>>>(dst, (const float*)src, rows, v);
 }
 
 void arg_top_k(int32_t* dst, const void* src, EType t, long long rows, long long v, long long k, cudaStream_t s) {
@@ -1336,7 +1372,7 @@ void record_history(double* history, const void* const* slots, const int* types,
 void bump_counter(long long* counter, cudaStream_t s) { k_bump<<<1, 1, 0, s>>>(counter); }
 
 void load_batch(void* dst, const void* batches, size_t bytes, long long n_batches, const long long* counter, cudaStream_t s) {
-  k_load_batch<<<grid_for((long long)bytes), 256, 0, s>>>((char*)dst, (const char*)batches, bytes, n_batches, counter);
+  k_load_batch<<<grid_k(k_load_batch, (long long)bytes), 256, 0, s>>>((char*)dst, (const char*)batches, bytes, n_batches, counter);
 }
 
 void set_conditional(cudaGraphConditionalHandle h, const void* pred, EType t, long long* count, long long limit, bool bump, cudaStream_t s) {
@@ -1347,13 +1383,13 @@ void write_count(int32_t* dst, const long long* count, cudaStream_t s) { k_write
 
 void index_outside(const int32_t* idx, long long n, long long dim, int* flag, cudaStream_t s) {
   if (n <= 0) return;
-  k_index_outside<<<grid_for(n), 256, 0, s>>>(idx, n, dim, flag);
+  k_index_outside<<<grid_k(k_index_outside, n), 256, 0, s>>>(idx, n, dim, flag);
 }
 
 void any_nonfinite(const void* src, EType t, long long n, int* flag, cudaStream_t s) {
   if (n <= 0) return;
-  if (t == EType::F64) k_nonfinite<double><<<grid_for(n), 256, 0, s>>>((const double*)src, n, flag);
-  else if (t == EType::F32) k_nonfinite<float><<<grid_for(n), 256, 0, s>>>((const float*)src, n, flag);
+  if (t == EType::F64) k_nonfinite<double><<<grid_k(k_nonfinite<double>, n), 256, 0, s>>>((const double*)src, n, flag);
+  else if (t == EType::F32) k_nonfinite<float><<<grid_k(k_nonfinite<float>, n), 256, 0, s>>>((const float*)src, n, flag);
 }
 
 }  // namespace rgc

@@ -373,15 +373,17 @@ struct Builder {
     int vw = spec.dtype == DType::F64 ? 2 : 4;
     bool vec_ok = spec.n % (size_t)vw == 0;
     std::vector<FDiv> rows;
-    for (auto& in : spec.inputs) rows.push_back(in.kind == rg::ArgKind::Row && in.row > 0 ? make_fdiv(in.row) : FDiv{});
+    for (auto& in : spec.inputs)
+      rows.push_back(in.kind == rg::ArgKind::Row && in.row > 0 ? make_fdiv(in.row) : in.col ? make_fdiv(in.col) : FDiv{});
     long long n = (long long)spec.n;
     Program* prog = p;
+    // The 32-bit-index kernel, or its 64-bit twin (`name_w`) when some index may not fit.
     auto fn = std::make_shared<CUfunction>(nullptr);
     Lowered l;
     l.run = [=](Ctx& c) {
       if (!*fn) {
         std::lock_guard<std::mutex> lk(jit_mu());
-        *fn = jit().function(name);
+        *fn = jit().function(small ? name : name + "_w");
       }
       ElemArgs a;
       std::memset(&a, 0, sizeof a);

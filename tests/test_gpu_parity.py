@@ -84,6 +84,28 @@ def test_pow_and_ieee_specials(oracle):
         np.testing.assert_allclose(g[m], w[m], rtol=2e-6, err_msg=f"output {k}")
 
 
+@pytest.mark.parametrize("dtype", ["float32", "float64"])
+def test_division_of_every_special_pair_is_bit_exact(oracle, dtype):
+    """x / y over all pairs of signed zeros, denormals, infinities, NaN and ordinary values (zero
+    numerators take their own path on the device), alone and inside a fused group."""
+    tiny = np.finfo(dtype).smallest_subnormal
+    v = np.array([0.0, -0.0, 1.0, -1.5, tiny, -tiny, 1e-30, 3e38, np.inf, -np.inf, np.nan, 7.0], dtype=dtype)
+    x = F.tensor(np.repeat(v, v.size))
+    y = F.tensor(np.tile(v, v.size))
+    assert_parity(oracle, lambda a, b: (a / b, (a * 2.0) / (b + 0.0)), (x, y), exact=True)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "float64"])
+def test_causal_softmax_division_with_zero_numerators_is_bit_exact(oracle, dtype):
+    """The column-broadcast division of a causal softmax, whose upper triangle is zero."""
+    t = 64
+    e = np.random.default_rng(41).random((4, 3, t, t)).astype(dtype)
+    e[..., np.triu_indices(t, 1)[0], np.triu_indices(t, 1)[1]] = 0.0
+    e[0, 0, 0, 0] = -0.0
+    s = F.tensor(e.sum(-1, keepdims=True))
+    assert_parity(oracle, lambda a, b: a / b, (F.tensor(e), s), exact=True)
+
+
 def test_fused_chain_matches_and_forms_groups(oracle):
     x, y = rnd(3, 4096, seed=4), rnd(4096, seed=5)
     fn = lambda a, b: F.tanh(a * 0.7978845608 * (a + 0.044715 * a * a * a)) * b + F.exp(-abs(a)) / (1.0 + b * b)
