@@ -513,10 +513,21 @@ __global__ void k_rows_fast_sum_vec(T* __restrict__ dst, const T* __restrict__ a
     for (int e = 0; e < E; ++e) acc[e] = (T)0;
     const T* row = a + (r < rows ? r : 0) * len;
     if (r < rows) {
-      // Unrolled so that several 16-byte loads are in flight per lane; the additions into each
-      // running sum stay in element order.
-#pragma unroll 4
-      for (long long c = 0; c < full; c += 8) {
+      // Batches of 8 vectors loaded before they are added, so that several 16-byte loads are in
+      // flight per lane; the additions into each running sum stay in element order.
+      long long c = 0;
+      for (; c + 64 <= full; c += 64) {
+        VT v[8];
+#pragma unroll
+        for (int h = 0; h < 8; ++h) v[h] = *(const VT*)(row + c + 8 * h + q * E);
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          const T* x = (const T*)&v[h];
+#pragma unroll
+          for (int e = 0; e < E; ++e) acc[e] = acc[e] + x[e];
+        }
+      }
+      for (; c < full; c += 8) {
         const VT v = *(const VT*)(row + c + q * E);
         const T* x = (const T*)&v;
 #pragma unroll
@@ -600,12 +611,17 @@ __global__ void k_cols_partial_vec(T* __restrict__ part, const T* __restrict__ a
 #pragma unroll
   for (int j = 0; j < PER; ++j) acc[j] = red_init<T>(op);
   if (n == REDUCE_ROWS) {
-#pragma unroll 16
-    for (int r = 0; r < (int)REDUCE_ROWS; ++r) {
-      const V v = src[r * ncv];
-      const T* e = (const T*)&v;
+    // 16 rows' loads issued before their additions, four batches per partial.
+    for (int r = 0; r < (int)REDUCE_ROWS; r += 16) {
+      V v[16];
 #pragma unroll
-      for (int j = 0; j < PER; ++j) acc[j] = combine(op, acc[j], e[j]);
+      for (int h = 0; h < 16; ++h) v[h] = src[(r + h) * ncv];
+#pragma unroll
+      for (int h = 0; h < 16; ++h) {
+        const T* e = (const T*)&v[h];
+#pragma unroll
+        for (int j = 0; j < PER; ++j) acc[j] = combine(op, acc[j], e[j]);
+      }
     }
   } else {
     for (long long r = 0; r < n; ++r) {
