@@ -53,7 +53,9 @@ template <int BN, bool PAIR = false> struct Shape {
   static constexpr uint32_t RAW = A_BYTES + B_BYTES;  // raw tiles (read by the MMA as hi)
   static constexpr uint32_t STAGE = 2 * RAW;          // + lo tiles
   static constexpr int STAGES = (200 * 1024) / STAGE > 4 ? 4 : (200 * 1024) / STAGE;
-  static constexpr uint32_t SMEM = 1024 + STAGES * STAGE + 256;
+  // Epilogue staging: one 32 x 33-word block per epilogue warp, after the barriers.
+  static constexpr uint32_t EPI = 4 * 32 * 33 * 4;
+  static constexpr uint32_t SMEM = 1024 + STAGES * STAGE + 256 + EPI;
 };
 
 __device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -415,7 +417,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // Epilogue: warp w drains TMEM lanes [32 (w % 4), +32) = rows of this CTA's part of the tile.
+    // For short K (at most 4 K blocks) the output dominates, and each 32 x 32 block goes through
+    // shared memory (row pitch 33 words, conflict-free both ways) so that one warp store writes
+    // four whole 128-byte row segments instead of 16 bytes in each of 32 rows. Longer K keeps the
+    // direct stores: there the main loop is bound by shared-memory bandwidth.
     const int lg = warp & 3;
+    const bool staged = w.num_kb <= 4;
+    float* ep = (float*)(smem + STAGES * S::STAGE + 256) + lg * (32 * 33);
+    const bool vec_out = (w.N % 4) == 0 && (((uintptr_t)w.C & 15) == 0);
     long long t = 0;
     for (long long u = first_unit; u < units && !*abort; u += unit_stride, ++t) {
       int m_t, n_t, z, sp;
@@ -426,6 +435,36 @@ __global__ void __launch_bounds__(THREADS, 1)
       const long long row = (long long)m_t * TM + (long long)rank * BM + lg * 32 + lane;
       const long long n0 = (long long)n_t * BN;
       float* out = w.C + (((long long)sp * w.batch + z) * w.M + row) * w.N;
+      if (staged) {
+        const long long row0 = row - lane;
+        float* mat = w.C + ((long long)sp * w.batch + z) * w.M * w.N;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v[32];
+          tmem_ld32(tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)(b * BN + c), v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) ep[lane * 33 + j] = __uint_as_float(v[j]);
+          __syncwarp();
+          // Lane l stores columns 4 (l % 8) .. +3 of block row 4 i + l / 8.
+          const long long col = n0 + c + (lane & 7) * 4;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int rr = i * 4 + (lane >> 3);
+            const float* src = ep + rr * 33 + (lane & 7) * 4;
+            if (row0 + rr < w.M) {
+              float* o = mat + (row0 + rr) * w.N + col;
+              if (vec_out && col + 4 <= w.N) {
+                *(float4*)o = make_float4(src[0], src[1], src[2], src[3]);
+              } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                  if (col + k < w.N) o[k] = src[k];
+              }
+            }
+          }
+          __syncwarp();
+        }
+      } else {
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t v[32];
@@ -443,6 +482,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               if (j < lim) o[j] = __uint_as_float(v[j]);
           }
         }
+      }
       }
       fence_before();
       __syncwarp();

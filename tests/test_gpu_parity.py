@@ -152,6 +152,15 @@ def test_row_reductions_vector_loads(oracle, shape):
     assert_parity(oracle, lambda a: (a.sum(axis=-1), a.max(axis=-1), a.min(axis=-1)), (x,), tol=1e-5)
 
 
+@pytest.mark.parametrize("length", [4, 8, 63, 64, 65, 127, 128, 200, 256, 1000])
+@pytest.mark.parametrize("dtype", ["float32", "float64"])
+def test_row_sums_keep_rgs_eight_lane_order(oracle, length, dtype):
+    # Row sums in fast_sum order (plan.rs:1213-1230): lengths around the kernel's 64-element load
+    # batches and its 8-element tail.
+    x = rnd(300, length, seed=43, dtype=dtype)
+    assert_parity(oracle, lambda a: a.sum(axis=-1), (x,), exact=True)
+
+
 def test_small_full_sum_is_bit_exact(oracle):
     # rg's eight-lane fast_sum order, reproduced on the device for small tensors.
     for n in [1, 7, 8, 9, 256, 1000, 4099]:
@@ -261,8 +270,11 @@ TC_CASES = [
     ((40, 8000), (8000, 72), False, False),         # one output tile, split K
     ((4000, 96), (50, 96), False, True),            # narrow N (64-wide tiles), B K-major
     ((300, 200), (200, 150), False, False),         # B row pitch not a multiple of 4: packed K-major
-    ((257, 64), (64, 129), False, False),           # CTA pairs: one row past a pair tile, the odd CTA's B half mostly past N
-    ((1000, 72), (72, 100), False, False),          # CTA pairs with 128-wide tiles
+    ((8, 257, 64), (8, 64, 129), False, False),     # CTA pairs: one row past a pair tile, the odd CTA's B half mostly past N
+    ((3, 1000, 72), (3, 72, 100), False, False),    # CTA pairs with 128-wide tiles
+    ((8, 257, 96), (8, 96, 259), False, False),     # short K (staged epilogue): ragged rows, N not a multiple of 4
+    ((16, 256, 32), (16, 256, 32), False, True),    # short K, q @ k^T at head size 32
+    ((9, 128, 130), (9, 128, 120), True, False),    # four K blocks (the staged epilogue's limit), A MN-major
     ((16, 256, 64), (16, 256, 64), False, True),    # batched CTA pairs, B K-major (q @ k^T at T = 256)
     ((520, 4000), (4000, 300), False, False),       # CTA pairs with split K
 ]
