@@ -34,6 +34,7 @@ const Driver& Driver::get() {
     load("cuModuleUnload", (void**)&x.ModuleUnload);
     load("cuLaunchKernel", (void**)&x.LaunchKernel);
     load("cuOccupancyMaxActiveBlocksPerMultiprocessor", (void**)&x.OccupancyMaxActiveBlocksPerMultiprocessor);
+    load("cuLaunchKernelEx", (void**)&x.LaunchKernelEx);
     return x;
   }();
   return d;
@@ -282,8 +283,13 @@ static std::string kernel_source(const ElemSpec& s, const std::string& name) {
   };
   // Two kernels: `name` for n < 2^31 with 32-bit index math, `name_w` with 64-bit index math.
   // Separate kernels keep the 64-bit path's registers out of the common one's occupancy.
+  // Each kernel first waits for the grids it depends on (programmatic dependent launch: it may be
+  // scheduled while the previous kernel drains) and lets its own dependents launch, then reads its
+  // operands.
   auto header = [&](const std::string& fn) {
     o << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const ElemArgs a) {\n";
+    o << "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n";
+    o << "  asm volatile(\"griddepcontrol.launch_dependents;\" ::: \"memory\");\n";
     for (size_t k = 0; k < s.inputs.size(); ++k)
       if (s.inputs[k].kind == ArgKind::Splat) o << "  const " << T << " sp" << k << " = " << in_ptr(k) << "[0];\n";
   };
@@ -409,7 +415,7 @@ void Jit::build() {
   }
   const char* opts[] = {"--gpu-architecture=sm_100a", "--fmad=false", "--prec-div=true", "--prec-sqrt=true", "--ftz=false", "-default-device",
                         "--std=c++17"};
-  std::string path = cache_dir() + "/" + std::to_string(fnv1a(src + "v3")) + ".cubin";
+  std::string path = cache_dir() + "/" + std::to_string(fnv1a(src + "v5")) + ".cubin";
   std::vector<char> cubin;
   {
     std::ifstream f(path, std::ios::binary);
@@ -486,7 +492,19 @@ void Jit::launch(CUfunction f, const ElemArgs& a, long long n, int vec_width, cu
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   void* params[] = {(void*)&a};
-  CUresult r = Driver::get().LaunchKernel(f, (unsigned)blocks, 1, 1, 256, 1, 1, 0, (CUstream)s, params, nullptr);
+  CUlaunchConfig cfg = {};
+  cfg.gridDimX = (unsigned)blocks;
+  cfg.gridDimY = cfg.gridDimZ = 1;
+  cfg.blockDimX = 256;
+  cfg.blockDimY = cfg.blockDimZ = 1;
+  cfg.sharedMemBytes = 0;
+  cfg.hStream = (CUstream)s;
+  CUlaunchAttribute attr[1];
+  attr[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+  attr[0].value.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  CUresult r = Driver::get().LaunchKernelEx(&cfg, f, params, nullptr);
   if (r != CUDA_SUCCESS) throw std::runtime_error("fused kernel launch failed (CUresult " + std::to_string((int)r) + ")");
 }
 

@@ -4,7 +4,10 @@
 #include <cfloat>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <map>
+#include <string>
+#include <utility>
 #include <mutex>
 #include <tuple>
 #include <type_traits>
@@ -12,6 +15,14 @@
 #include "kernels.cuh"
 
 namespace rgc {
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("RGC_NO_PDL");
+    return !(e && std::string(e) == "1");
+  }();
+  return on;
+}
 
 namespace {
 
@@ -50,6 +61,35 @@ int resident_blocks(const void* kernel, int threads, size_t smem) {
   }
   cache[key] = nb;
   return nb;
+}
+
+// Programmatic dependent launch. Every kernel in this file begins with griddepcontrol.wait, which
+// returns once the grids it depends on have completed and their memory is visible, so its
+// launches carry the programmatic-serialization attribute. It then allows its own dependents to
+// launch (griddepcontrol.launch_dependents): once all of its blocks are running, the next
+// kernel's blocks are scheduled onto the SMs its finishing blocks free, and park in their own
+// wait, instead of being launched after it has ended. RGC_NO_PDL=1 launches without the attribute.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... P, typename... A>
+void launch_with(bool pdl, void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
+}
+template <typename... P, typename... A> void launch(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A&&... args) {
+  launch_with(true, kernel, grid, block, smem, s, std::forward<A>(args)...);
 }
 
 // A grid-stride launch of `kernel` over n work items, covering the GPU in exactly one wave: as
@@ -97,6 +137,7 @@ __device__ __forceinline__ unsigned long long read_key(const int32_t* k) {
 // ---------------- memory movement ----------------
 
 template <typename T> __global__ void k_gather(T* __restrict__ dst, const T* __restrict__ src, Dims out, long long base, long long n) {
+  pdl_wait();
   GRID_STRIDE(e, n) {
     long long r = e, off = base;
     for (int d = out.rank - 1; d >= 0; --d) {
@@ -109,6 +150,7 @@ template <typename T> __global__ void k_gather(T* __restrict__ dst, const T* __r
 }
 
 template <typename T> __global__ void k_scatter(T* __restrict__ dst, const T* __restrict__ src, Dims in, long long base, long long n) {
+  pdl_wait();
   GRID_STRIDE(e, n) {
     long long r = e, off = base;
     for (int d = in.rank - 1; d >= 0; --d) {
@@ -134,10 +176,12 @@ __device__ __forceinline__ long long fd_off(const FDims& s, unsigned e) {
 }
 
 template <typename T> __global__ void k_gather32(T* __restrict__ dst, const T* __restrict__ src, FDims s, long long base, unsigned n) {
+  pdl_wait();
   for (unsigned e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) dst[e] = src[base + fd_off(s, e)];
 }
 
 template <typename T> __global__ void k_scatter32(T* __restrict__ dst, const T* __restrict__ src, FDims s, long long base, unsigned n) {
+  pdl_wait();
   for (unsigned e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) dst[base + fd_off(s, e)] = src[e];
 }
 
@@ -145,18 +189,21 @@ template <typename T> __global__ void k_scatter32(T* __restrict__ dst, const T* 
 // multiple of the vector width V, so V consecutive elements move as one load and one store.
 template <typename VT, int V>
 __global__ void k_gather_vec(VT* __restrict__ dst, const VT* __restrict__ src, FDims s, long long base, unsigned nv) {
+  pdl_wait();
   for (unsigned q = blockIdx.x * blockDim.x + threadIdx.x; q < nv; q += gridDim.x * blockDim.x)
     dst[q] = src[(base + fd_off(s, q * V)) / V];
 }
 
 template <typename VT, int V>
 __global__ void k_scatter_vec(VT* __restrict__ dst, const VT* __restrict__ src, FDims s, long long base, unsigned nv) {
+  pdl_wait();
   for (unsigned q = blockIdx.x * blockDim.x + threadIdx.x; q < nv; q += gridDim.x * blockDim.x)
     dst[(base + fd_off(s, q * V)) / V] = src[q];
 }
 
 // 32x32 tiles through shared memory; the +1 column avoids bank conflicts.
 template <typename T> __global__ void k_transpose2(T* __restrict__ dst, const T* __restrict__ src, long long rows, long long cols) {
+  pdl_wait();
   __shared__ T tile[32][33];
   long long b = blockIdx.z;
   const T* s = src + b * rows * cols;
@@ -178,6 +225,7 @@ template <typename T> __global__ void k_transpose2(T* __restrict__ dst, const T*
 template <typename T>
 __global__ void k_take_rows(T* __restrict__ dst, const T* __restrict__ src, const int32_t* __restrict__ idx, long long dim, long long n_idx,
                             long long block, long long n) {
+  pdl_wait();
   GRID_STRIDE(e, n) {
     long long row = e / block, col = e - row * block;
     long long j = row % n_idx, o = row / n_idx;
@@ -187,6 +235,7 @@ __global__ void k_take_rows(T* __restrict__ dst, const T* __restrict__ src, cons
 
 template <typename T>
 __global__ void k_take_along(T* __restrict__ dst, const T* __restrict__ src, const int32_t* __restrict__ idx, long long n, long long v, long long k) {
+  pdl_wait();
   GRID_STRIDE(j, n) { dst[j] = src[(j / k) * v + clamp_index(idx[j], v)]; }
 }
 
@@ -196,6 +245,7 @@ __global__ void k_take_along(T* __restrict__ dst, const T* __restrict__ src, con
 template <typename T>
 __global__ void k_take_grad(T* __restrict__ dst, const T* __restrict__ ct, const int32_t* __restrict__ idx, long long dim, long long n_idx,
                             long long block) {
+  pdl_wait();
   __shared__ int hits[256];
   __shared__ int warp_count[8];
   __shared__ int total;
@@ -262,6 +312,7 @@ __global__ void k_take_grad(T* __restrict__ dst, const T* __restrict__ ct, const
 constexpr int TG_CHUNK = 1024;
 
 __global__ void k_tg_count(int* __restrict__ cnt, const int32_t* __restrict__ idx, long long dim, long long n_idx, long long chunks) {
+  pdl_wait();
   GRID_STRIDE(j, n_idx) {
     long long r = clamp_index(idx[j], dim);
     atomicAdd(&cnt[r * chunks + j / TG_CHUNK], 1);
@@ -270,6 +321,7 @@ __global__ void k_tg_count(int* __restrict__ cnt, const int32_t* __restrict__ id
 
 // Exclusive scan of m values in place, one block of 1024 threads: each thread owns a contiguous run.
 __global__ void k_tg_scan(int* __restrict__ v, long long m) {
+  pdl_wait();
   __shared__ int part[1024];
   const long long per = (m + 1023) / 1024;
   const long long s = threadIdx.x * per, e = s + per < m ? s + per : m;
@@ -295,6 +347,7 @@ __global__ void k_tg_scan(int* __restrict__ v, long long m) {
 // consecutive slots after that row's running offset.
 __global__ void k_tg_place(int* __restrict__ list, int* __restrict__ off, const int32_t* __restrict__ idx, long long dim, long long n_idx,
                            long long chunks) {
+  pdl_wait();
   const long long c = blockIdx.x;
   const int lane = threadIdx.x;
   const long long j_end = (c + 1) * TG_CHUNK < n_idx ? (c + 1) * TG_CHUNK : n_idx;
@@ -337,6 +390,7 @@ template <typename T, bool VEC>
 __global__ void __launch_bounds__(256) k_tg_accumulate(T* __restrict__ dst, const T* __restrict__ ct, const int* __restrict__ list,
                                                      const int* __restrict__ off, long long dim, long long n_idx, long long block,
                                                      long long chunks) {
+  pdl_wait();
   extern __shared__ __align__(16) unsigned char tg_smem[];
   T* buf = (T*)tg_smem;  // [TG_STAGES][TG_HITS][TG_COLS]
   const long long r = blockIdx.x, o = blockIdx.z;
@@ -388,6 +442,7 @@ __global__ void __launch_bounds__(256) k_tg_accumulate(T* __restrict__ dst, cons
 template <typename T>
 __global__ void k_take_along_grad(T* __restrict__ dst, const T* __restrict__ ct, const int32_t* __restrict__ idx, long long rows, long long v,
                                   long long k) {
+  pdl_wait();
   GRID_STRIDE(e, rows * v) {
     long long row = e / v, c = e - row * v;
     T acc = (T)0;
@@ -402,6 +457,7 @@ __global__ void k_take_along_grad(T* __restrict__ dst, const T* __restrict__ ct,
 // rg's fast_sum (plan.rs:1213-1230) for n small enough to do in one warp: lanes 0..7 each add
 // every eighth element in order, then lane 0 adds the eight lanes and the tail.
 template <typename T> __global__ void k_sum_exact(T* dst, const T* __restrict__ a, long long n) {
+  pdl_wait();
   __shared__ T lanes[8];
   int l = threadIdx.x;
   long long full = n / 8 * 8;
@@ -444,6 +500,7 @@ template <typename T> __device__ T block_sum(T v) {
 }
 
 template <typename T> __global__ void k_sum_chunks(T* __restrict__ part, const T* __restrict__ a, long long n, long long chunk) {
+  pdl_wait();
   long long s = (long long)blockIdx.x * chunk, e = s + chunk < n ? s + chunk : n;
   T v = (T)0;
   for (long long i = s + threadIdx.x; i < e; i += blockDim.x) v += a[i];
@@ -452,6 +509,7 @@ template <typename T> __global__ void k_sum_chunks(T* __restrict__ part, const T
 }
 
 template <typename T> __global__ void k_sum_final(T* dst, const T* __restrict__ part, long long m) {
+  pdl_wait();
   T v = (T)0;
   for (long long i = threadIdx.x; i < m; i += blockDim.x) v += part[i];
   v = block_sum(v);
@@ -460,6 +518,7 @@ template <typename T> __global__ void k_sum_final(T* dst, const T* __restrict__ 
 
 // Warp per row for short rows, block per row for long ones.
 template <typename T> __global__ void k_reduce_rows_warp(T* __restrict__ dst, const T* __restrict__ a, Red op, long long rows, long long len) {
+  pdl_wait();
   long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
   long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
@@ -476,6 +535,7 @@ template <typename T> __global__ void k_reduce_rows_warp(T* __restrict__ dst, co
 // order is the vector-lane order, then the warp tree; only Sum depends on it).
 template <typename T, typename VT, int V>
 __global__ void k_reduce_rows_warp_vec(T* __restrict__ dst, const T* __restrict__ a, Red op, long long rows, long long len) {
+  pdl_wait();
   long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
   long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
@@ -501,6 +561,7 @@ __global__ void k_reduce_rows_warp_vec(T* __restrict__ dst, const T* __restrict_
 // L = 8 / E lanes share a row; scalar form: one sum per lane, eight lanes per row.
 template <typename T, typename VT, int E>
 __global__ void k_rows_fast_sum_vec(T* __restrict__ dst, const T* __restrict__ a, long long rows, long long len) {
+  pdl_wait();
   constexpr int L = 8 / E, RPW = 32 / L;
   const int lane = threadIdx.x & 31, sub = lane / L, q = lane % L;
   const long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -547,6 +608,7 @@ __global__ void k_rows_fast_sum_vec(T* __restrict__ dst, const T* __restrict__ a
 }
 
 template <typename T> __global__ void k_rows_fast_sum(T* __restrict__ dst, const T* __restrict__ a, long long rows, long long len) {
+  pdl_wait();
   const int lane = threadIdx.x & 31, sub = lane >> 3, chain = lane & 7;
   const long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
@@ -568,6 +630,7 @@ template <typename T> __global__ void k_rows_fast_sum(T* __restrict__ dst, const
 }
 
 template <typename T> __global__ void k_reduce_rows_block(T* __restrict__ dst, const T* __restrict__ a, Red op, long long len) {
+  pdl_wait();
   __shared__ T sh[32];
   const T* row = a + (long long)blockIdx.x * len;
   T acc = red_init<T>(op);
@@ -588,6 +651,7 @@ constexpr long long REDUCE_ROWS = 64;
 
 template <typename T>
 __global__ void k_cols_partial(T* __restrict__ part, const T* __restrict__ a, Red op, long long rows, long long cols) {
+  pdl_wait();
   long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= cols) return;
   long long q = blockIdx.y;
@@ -601,6 +665,7 @@ __global__ void k_cols_partial(T* __restrict__ part, const T* __restrict__ a, Re
 // row order), a full 64-row block fully unrolled so its loads are all in flight at once.
 template <typename T, typename V, int PER>
 __global__ void k_cols_partial_vec(T* __restrict__ part, const T* __restrict__ a, Red op, long long rows, long long cols) {
+  pdl_wait();
   const long long ncv = cols / PER;
   const long long cv = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (cv >= ncv) return;
@@ -646,6 +711,7 @@ __global__ void k_cols_partial_vec(T* __restrict__ part, const T* __restrict__ a
 constexpr int CF_ROWS = 1024;
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(256) k_cols_fold(T* __restrict__ dst, const T* __restrict__ part, Red op, long long nparts, long long cols) {
+  pdl_wait();
   constexpr int C = 32 / (int)sizeof(T);  // columns per block
   constexpr int PER = VEC ? 16 / (int)sizeof(T) : 1;
   extern __shared__ __align__(16) unsigned char cf_smem[];
@@ -695,6 +761,7 @@ __global__ void __launch_bounds__(256) k_cols_fold(T* __restrict__ dst, const T*
 
 template <typename T>
 __global__ void k_reduce_generic(T* __restrict__ dst, const T* __restrict__ a, Red op, Dims kept, Dims red, long long n_out, long long n_red) {
+  pdl_wait();
   GRID_STRIDE(o, n_out) {
     long long r = o, base = 0;
     for (int d = kept.rank - 1; d >= 0; --d) {
@@ -731,6 +798,7 @@ template <> __device__ __forceinline__ double mac<double, false>(double acc, dou
 template <typename T, bool EXACT, int TILE>
 __global__ void __launch_bounds__(256) k_gemm(T* __restrict__ C, const T* __restrict__ A, const T* __restrict__ B, long long m, long long n,
                                               long long k, bool ta, bool tb, GemmBatch bt) {
+  pdl_wait();
   // TILE 64: 4x4 outputs per thread; TILE 16 (small outputs, usually long k): one per thread.
   constexpr int BM = TILE, BN = TILE, R = TILE / 16;
   constexpr int BK = TILE == 16 ? 64 : (sizeof(T) == 8 ? 16 : 32);  // two buffers within 48 KB
@@ -831,6 +899,7 @@ constexpr unsigned long long GAMMA = 0x9E3779B97F4A7C15ULL;
 constexpr unsigned long long GAMMA_SPLIT = 0xD1B54A32D192ED03ULL;
 
 __global__ void k_key_split(int32_t* dst, const int32_t* key, long long pairs) {
+  pdl_wait();
   unsigned long long kk = read_key(key);
   GRID_STRIDE(j, pairs) {
     unsigned long long bits = mix(kk + (unsigned long long)(j + 1) * GAMMA_SPLIT);
@@ -840,6 +909,7 @@ __global__ void k_key_split(int32_t* dst, const int32_t* key, long long pairs) {
 }
 
 template <typename T> __global__ void k_rand_uniform(T* dst, const int32_t* key, long long n) {
+  pdl_wait();
   unsigned long long kk = read_key(key);
   const int mant = sizeof(T) == 4 ? 24 : 53;
   const double scale = sizeof(T) == 4 ? 5.9604644775390625e-08 : 1.1102230246251565e-16;
@@ -850,6 +920,7 @@ template <typename T> __global__ void k_rand_uniform(T* dst, const int32_t* key,
 }
 
 template <typename T> __global__ void k_rand_normal(T* dst, const int32_t* key, long long n) {
+  pdl_wait();
   unsigned long long kk = read_key(key);
   const double two53 = 1.1102230246251565e-16;
   const double TAU = 6.283185307179586;
@@ -871,15 +942,18 @@ __device__ __forceinline__ int32_t to_i32(double x) {
 }
 
 template <typename D, typename S> __global__ void k_cast(D* dst, const S* src, long long n) {
+  pdl_wait();
   GRID_STRIDE(j, n) { dst[j] = (D)src[j]; }
 }
 template <typename S> __global__ void k_cast_i32(int32_t* dst, const S* src, long long n) {
+  pdl_wait();
   GRID_STRIDE(j, n) { dst[j] = to_i32((double)src[j]); }
 }
 
 // First index of the maximum, scanning with `x > best` (plan.rs:1437-1451): NaN never wins,
 // and a NaN at index 0 wins the whole row.
 template <typename T> __global__ void k_argmax(int32_t* dst, const T* __restrict__ a, long long rows, long long v) {
+  pdl_wait();
   long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
   long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
@@ -917,6 +991,7 @@ template <typename T> __global__ void k_argmax(int32_t* dst, const T* __restrict
 // Rank of each element under rg's total order (larger first, ties by index, NaN last); the
 // element of rank p < k is output p (plan.rs:833-866).
 template <typename T> __global__ void k_arg_top_k(int32_t* dst, const T* __restrict__ a, long long v, long long k) {
+  pdl_wait();
   const T* row = a + (long long)blockIdx.x * v;
   for (long long i = threadIdx.x; i < v; i += blockDim.x) {
     T p = row[i];
@@ -935,6 +1010,7 @@ template <typename T> __global__ void k_arg_top_k(int32_t* dst, const T* __restr
 }
 
 template <typename T> __global__ void k_cumsum(T* dst, const T* __restrict__ a, long long rows, long long v, bool reverse) {
+  pdl_wait();
   GRID_STRIDE(r, rows) {
     T acc = (T)0;
     if (reverse) {
@@ -952,6 +1028,7 @@ template <typename T> __global__ void k_cumsum(T* dst, const T* __restrict__ a, 
 }
 
 __global__ void k_cumsum_i32(int32_t* dst, const int32_t* __restrict__ a, long long rows, long long v, bool reverse) {
+  pdl_wait();
   GRID_STRIDE(r, rows) {
     uint32_t acc = 0;
     if (reverse) {
@@ -965,6 +1042,7 @@ __global__ void k_cumsum_i32(int32_t* dst, const int32_t* __restrict__ a, long l
 // ---------------- run loop support ----------------
 
 __global__ void k_record_history(double* history, const void* const* slots, const int* types, int n, const long long* step, long long* bad) {
+  pdl_wait();
   long long k = *step;
   bool bad_now = false;
   for (int h = 0; h < n; ++h) {
@@ -978,9 +1056,11 @@ __global__ void k_record_history(double* history, const void* const* slots, cons
   if (bad_now && *bad < 0) *bad = k;
 }
 
-__global__ void k_bump(long long* c) { *c += 1; }
+__global__ void k_bump(long long* c) {
+  pdl_wait(); *c += 1; }
 
 __global__ void k_load_batch(char* dst, const char* batches, size_t bytes, long long nb, const long long* counter) {
+  pdl_wait();
   const char* src = batches + (size_t)(*counter % nb) * bytes;
   GRID_STRIDE(i, (long long)bytes) { dst[i] = src[i]; }
 }
@@ -988,6 +1068,7 @@ __global__ void k_load_batch(char* dst, const char* batches, size_t bytes, long 
 // The condition of a conditional graph node: the scalar predicate is nonzero and, for a while
 // loop, its iteration count (bumped first inside the loop body) is below the limit.
 __global__ void k_set_conditional(cudaGraphConditionalHandle h, const void* pred, int dtype, long long* count, long long limit, int bump) {
+  pdl_wait();
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   if (count && bump) *count += 1;
   const double v = dtype == 0 ? (double)*(const float*)pred : dtype == 1 ? *(const double*)pred : (double)*(const int32_t*)pred;
@@ -996,16 +1077,19 @@ __global__ void k_set_conditional(cudaGraphConditionalHandle h, const void* pred
 }
 
 __global__ void k_write_count(int32_t* dst, const long long* count) {
+  pdl_wait();
   if (threadIdx.x == 0 && blockIdx.x == 0) *dst = (int32_t)*count;
 }
 
 __global__ void k_index_outside(const int32_t* idx, long long n, long long dim, int* flag) {
+  pdl_wait();
   GRID_STRIDE(i, n) {
     if (idx[i] < 0 || idx[i] >= dim) *flag = 1;
   }
 }
 
 template <typename T> __global__ void k_nonfinite(const T* a, long long n, int* flag) {
+  pdl_wait();
   GRID_STRIDE(i, n) {
     if (!isfinite(a[i])) *flag = 1;
   }
@@ -1080,30 +1164,30 @@ template <typename T> void gather_t(void* dst, const void* src, const Dims& out,
   bool ok = false;
   FDims f = fast_dims(out, &ok);
   if (!ok || n >= (1ll << 31)) {
-    k_gather<T><<<grid_k(k_gather<T>, n), 256, 0, s>>>((T*)dst, (const T*)src, out, base, n);
+    launch(k_gather<T>, grid_k(k_gather<T>, n), 256, 0, s, (T*)dst, (const T*)src, out, base, n);
     return;
   }
   constexpr int V = (int)(16 / sizeof(T));
   using VT = typename Vec16<T>::type;
   if (vec_width<T>(f, base, n) == V)
-    k_gather_vec<VT, V><<<grid_k(k_gather_vec<VT, V>, n / V), 256, 0, s>>>((VT*)dst, (const VT*)src, f, base, (unsigned)(n / V));
+    launch(k_gather_vec<VT, V>, grid_k(k_gather_vec<VT, V>, n / V), 256, 0, s, (VT*)dst, (const VT*)src, f, base, (unsigned)(n / V));
   else
-    k_gather32<T><<<grid_k(k_gather32<T>, n), 256, 0, s>>>((T*)dst, (const T*)src, f, base, (unsigned)n);
+    launch(k_gather32<T>, grid_k(k_gather32<T>, n), 256, 0, s, (T*)dst, (const T*)src, f, base, (unsigned)n);
 }
 
 template <typename T> void scatter_t(void* dst, const void* src, const Dims& in, long long base, long long n, cudaStream_t s) {
   bool ok = false;
   FDims f = fast_dims(in, &ok);
   if (!ok || n >= (1ll << 31)) {
-    k_scatter<T><<<grid_k(k_scatter<T>, n), 256, 0, s>>>((T*)dst, (const T*)src, in, base, n);
+    launch(k_scatter<T>, grid_k(k_scatter<T>, n), 256, 0, s, (T*)dst, (const T*)src, in, base, n);
     return;
   }
   constexpr int V = (int)(16 / sizeof(T));
   using VT = typename Vec16<T>::type;
   if (vec_width<T>(f, base, n) == V)
-    k_scatter_vec<VT, V><<<grid_k(k_scatter_vec<VT, V>, n / V), 256, 0, s>>>((VT*)dst, (const VT*)src, f, base, (unsigned)(n / V));
+    launch(k_scatter_vec<VT, V>, grid_k(k_scatter_vec<VT, V>, n / V), 256, 0, s, (VT*)dst, (const VT*)src, f, base, (unsigned)(n / V));
   else
-    k_scatter32<T><<<grid_k(k_scatter32<T>, n), 256, 0, s>>>((T*)dst, (const T*)src, f, base, (unsigned)n);
+    launch(k_scatter32<T>, grid_k(k_scatter32<T>, n), 256, 0, s, (T*)dst, (const T*)src, f, base, (unsigned)n);
 }
 
 }  // namespace
@@ -1120,7 +1204,7 @@ void strided_scatter(void* dst, const void* src, EType t, const Dims& in, long l
 
 template <typename T> static void transpose_t(void* dst, const void* src, long long batch, long long rows, long long cols, cudaStream_t s) {
   dim3 grid((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32), (unsigned)batch);
-  k_transpose2<T><<<grid, dim3(32, 8), 0, s>>>((T*)dst, (const T*)src, rows, cols);
+  launch(k_transpose2<T>, grid, dim3(32, 8), 0, s, (T*)dst, (const T*)src, rows, cols);
 }
 void transpose_last2(void* dst, const void* src, EType t, long long batch, long long rows, long long cols, cudaStream_t s) {
   if (batch * rows * cols <= 0) return;
@@ -1130,7 +1214,7 @@ void transpose_last2(void* dst, const void* src, EType t, long long batch, long 
 template <typename T>
 static void take_rows_t(void* dst, const void* src, const int32_t* idx, long long outer, long long dim, long long n_idx, long long block, cudaStream_t s) {
   long long n = outer * n_idx * block;
-  k_take_rows<T><<<grid_k(k_take_rows<T>, n), 256, 0, s>>>((T*)dst, (const T*)src, idx, dim, n_idx, block, n);
+  launch(k_take_rows<T>, grid_k(k_take_rows<T>, n), 256, 0, s, (T*)dst, (const T*)src, idx, dim, n_idx, block, n);
 }
 void take_rows(void* dst, const void* src, const int32_t* idx, EType t, long long outer, long long dim, long long n_idx, long long block,
                cudaStream_t s) {
@@ -1139,7 +1223,7 @@ void take_rows(void* dst, const void* src, const int32_t* idx, EType t, long lon
 }
 
 template <typename T> static void take_along_t(void* dst, const void* src, const int32_t* idx, long long n, long long v, long long k, cudaStream_t s) {
-  k_take_along<T><<<grid_k(k_take_along<T>, n), 256, 0, s>>>((T*)dst, (const T*)src, idx, n, v, k);
+  launch(k_take_along<T>, grid_k(k_take_along<T>, n), 256, 0, s, (T*)dst, (const T*)src, idx, n, v, k);
 }
 void take_along(void* dst, const void* src, const int32_t* idx, EType t, long long n, long long v, long long k, cudaStream_t s) {
   if (n <= 0) return;
@@ -1161,7 +1245,7 @@ template <typename T, bool VEC> static void tg_accumulate(void* dst, const void*
   }();
   (void)attr;
   dim3 grid((unsigned)dim, (unsigned)((block + TG_COLS - 1) / TG_COLS), (unsigned)outer);
-  k_tg_accumulate<T, VEC><<<grid, 256, smem, s>>>((T*)dst, (const T*)ct, list, off, dim, n_idx, block, chunks);
+  launch(k_tg_accumulate<T, VEC>, grid, 256, smem, s, (T*)dst, (const T*)ct, list, off, dim, n_idx, block, chunks);
 }
 
 void take_grad(void* dst, const void* ct, const int32_t* idx, EType t, long long outer, long long dim, long long n_idx, long long block,
@@ -1172,16 +1256,16 @@ void take_grad(void* dst, const void* ct, const int32_t* idx, EType t, long long
                       outer <= 65535 && (block + TG_COLS - 1) / TG_COLS <= 65535;
   if (!listed) {
     dim3 grid((unsigned)dim, (unsigned)outer);
-    if (t == EType::F64) k_take_grad<double><<<grid, 256, 0, s>>>((double*)dst, (const double*)ct, idx, dim, n_idx, block);
-    else k_take_grad<float><<<grid, 256, 0, s>>>((float*)dst, (const float*)ct, idx, dim, n_idx, block);
+    if (t == EType::F64) launch(k_take_grad<double>, grid, 256, 0, s, (double*)dst, (const double*)ct, idx, dim, n_idx, block);
+    else launch(k_take_grad<float>, grid, 256, 0, s, (float*)dst, (const float*)ct, idx, dim, n_idx, block);
     return;
   }
   int* cnt = (int*)scratch;
   int* list = (int*)((char*)scratch + (dim * chunks * 4 + 255) / 256 * 256);
   cudaMemsetAsync(cnt, 0, (size_t)(dim * chunks) * 4, s);
-  k_tg_count<<<grid_k(k_tg_count, n_idx), 256, 0, s>>>(cnt, idx, dim, n_idx, chunks);
-  k_tg_scan<<<1, 1024, 0, s>>>(cnt, dim * chunks);
-  k_tg_place<<<(unsigned)chunks, 32, 0, s>>>(list, cnt, idx, dim, n_idx, chunks);
+  launch(k_tg_count, grid_k(k_tg_count, n_idx), 256, 0, s, cnt, idx, dim, n_idx, chunks);
+  launch(k_tg_scan, 1, 1024, 0, s, cnt, dim * chunks);
+  launch(k_tg_place, (unsigned)chunks, 32, 0, s, list, cnt, idx, dim, n_idx, chunks);
   const bool vec = (block * (long long)esize(t)) % 16 == 0;
   if (t == EType::F64) {
     if (vec) tg_accumulate<double, true>(dst, ct, list, cnt, outer, dim, n_idx, block, chunks, s);
@@ -1194,8 +1278,8 @@ void take_grad(void* dst, const void* ct, const int32_t* idx, EType t, long long
 
 void take_along_grad(void* dst, const void* ct, const int32_t* idx, EType t, long long rows, long long v, long long k, cudaStream_t s) {
   if (rows * v <= 0) return;
-  if (t == EType::F64) k_take_along_grad<double><<<grid_k(k_take_along_grad<double>, rows * v), 256, 0, s>>>((double*)dst, (const double*)ct, idx, rows, v, k);
-  else k_take_along_grad<float><<<grid_k(k_take_along_grad<float>, rows * v), 256, 0, s>>>((float*)dst, (const float*)ct, idx, rows, v, k);
+  if (t == EType::F64) launch(k_take_along_grad<double>, grid_k(k_take_along_grad<double>, rows * v), 256, 0, s, (double*)dst, (const double*)ct, idx, rows, v, k);
+  else launch(k_take_along_grad<float>, grid_k(k_take_along_grad<float>, rows * v), 256, 0, s, (float*)dst, (const float*)ct, idx, rows, v, k);
 }
 
 constexpr long long EXACT_SUM_MAX = 32768;
@@ -1208,17 +1292,17 @@ size_t full_sum_scratch_bytes(long long n, EType t) {
 
 void reduce_full_sum(void* dst, const void* src, EType t, long long n, void* scratch, cudaStream_t s) {
   if (n <= EXACT_SUM_MAX) {
-    if (t == EType::F64) k_sum_exact<double><<<1, 32, 0, s>>>((double*)dst, (const double*)src, n);
-    else k_sum_exact<float><<<1, 32, 0, s>>>((float*)dst, (const float*)src, n);
+    if (t == EType::F64) launch(k_sum_exact<double>, 1, 32, 0, s, (double*)dst, (const double*)src, n);
+    else launch(k_sum_exact<float>, 1, 32, 0, s, (float*)dst, (const float*)src, n);
     return;
   }
   long long parts = (n + SUM_CHUNK - 1) / SUM_CHUNK;
   if (t == EType::F64) {
-    k_sum_chunks<double><<<(unsigned)parts, 256, 0, s>>>((double*)scratch, (const double*)src, n, SUM_CHUNK);
-    k_sum_final<double><<<1, 1024, 0, s>>>((double*)dst, (const double*)scratch, parts);
+    launch(k_sum_chunks<double>, (unsigned)parts, 256, 0, s, (double*)scratch, (const double*)src, n, SUM_CHUNK);
+    launch(k_sum_final<double>, 1, 1024, 0, s, (double*)dst, (const double*)scratch, parts);
   } else {
-    k_sum_chunks<float><<<(unsigned)parts, 256, 0, s>>>((float*)scratch, (const float*)src, n, SUM_CHUNK);
-    k_sum_final<float><<<1, 1024, 0, s>>>((float*)dst, (const float*)scratch, parts);
+    launch(k_sum_chunks<float>, (unsigned)parts, 256, 0, s, (float*)scratch, (const float*)src, n, SUM_CHUNK);
+    launch(k_sum_final<float>, 1, 1024, 0, s, (float*)dst, (const float*)scratch, parts);
   }
 }
 
@@ -1227,21 +1311,21 @@ template <typename T> static void rows_t(void* dst, const void* src, Red op, lon
     constexpr int E = (int)(16 / sizeof(T));
     using VT = typename Vec16<T>::type;
     if (len % E == 0 && ((uintptr_t)src & 15) == 0)
-      k_rows_fast_sum_vec<T, VT, E><<<grid_k(k_rows_fast_sum_vec<T, VT, E>, rows * (8 / E)), 256, 0, s>>>((T*)dst, (const T*)src, rows, len);
+      launch(k_rows_fast_sum_vec<T, VT, E>, grid_k(k_rows_fast_sum_vec<T, VT, E>, rows * (8 / E)), 256, 0, s, (T*)dst, (const T*)src, rows, len);
     else
-      k_rows_fast_sum<T><<<grid_k(k_rows_fast_sum<T>, rows * 8), 256, 0, s>>>((T*)dst, (const T*)src, rows, len);
+      launch(k_rows_fast_sum<T>, grid_k(k_rows_fast_sum<T>, rows * 8), 256, 0, s, (T*)dst, (const T*)src, rows, len);
     return;
   }
   if (len > 2048) {
-    k_reduce_rows_block<T><<<(unsigned)rows, 1024, 0, s>>>((T*)dst, (const T*)src, op, len);
+    launch(k_reduce_rows_block<T>, (unsigned)rows, 1024, 0, s, (T*)dst, (const T*)src, op, len);
   } else {
     long long threads = rows * 32;
     constexpr int V = (int)(16 / sizeof(T));
     using VT = typename Vec16<T>::type;
     if (len % V == 0 && ((uintptr_t)src & 15) == 0)
-      k_reduce_rows_warp_vec<T, VT, V><<<grid_k(k_reduce_rows_warp_vec<T, VT, V>, threads), 256, 0, s>>>((T*)dst, (const T*)src, op, rows, len);
+      launch(k_reduce_rows_warp_vec<T, VT, V>, grid_k(k_reduce_rows_warp_vec<T, VT, V>, threads), 256, 0, s, (T*)dst, (const T*)src, op, rows, len);
     else
-      k_reduce_rows_warp<T><<<grid_k(k_reduce_rows_warp<T>, threads), 256, 0, s>>>((T*)dst, (const T*)src, op, rows, len);
+      launch(k_reduce_rows_warp<T>, grid_k(k_reduce_rows_warp<T>, threads), 256, 0, s, (T*)dst, (const T*)src, op, rows, len);
   }
 }
 void reduce_rows(void* dst, const void* src, EType t, Red op, long long rows, long long len, cudaStream_t s) {
@@ -1262,11 +1346,11 @@ template <typename T> static void ordered_cols(void* dst, const T* part, Red op,
   if ((cols * (long long)sizeof(T)) % 16 == 0 && ((uintptr_t)part & 15) == 0) {
     static bool attr = (cudaFuncSetAttribute(k_cols_fold<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), true);
     (void)attr;
-    k_cols_fold<T, true><<<blocks, 256, smem, s>>>((T*)dst, part, op, nparts, cols);
+    launch(k_cols_fold<T, true>, blocks, 256, smem, s, (T*)dst, part, op, nparts, cols);
   } else {
     static bool attr = (cudaFuncSetAttribute(k_cols_fold<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), true);
     (void)attr;
-    k_cols_fold<T, false><<<blocks, 256, smem, s>>>((T*)dst, part, op, nparts, cols);
+    launch(k_cols_fold<T, false>, blocks, 256, smem, s, (T*)dst, part, op, nparts, cols);
   }
 }
 
@@ -1288,10 +1372,10 @@ static void cols_t(void* dst, const void* src, Red op, long long rows, long long
     const long long ncv = cols / PER;
     const unsigned threads = (unsigned)std::min<long long>(256, (ncv + 31) / 32 * 32);
     dim3 grid((unsigned)((ncv + threads - 1) / threads), (unsigned)parts);
-    k_cols_partial_vec<T, V, PER><<<grid, threads, 0, s>>>((T*)scratch, (const T*)src, op, rows, cols);
+    launch(k_cols_partial_vec<T, V, PER>, grid, threads, 0, s, (T*)scratch, (const T*)src, op, rows, cols);
   } else {
     dim3 grid((unsigned)((cols + 255) / 256), (unsigned)parts);
-    k_cols_partial<T><<<grid, 256, 0, s>>>((T*)scratch, (const T*)src, op, rows, cols);
+    launch(k_cols_partial<T>, grid, 256, 0, s, (T*)scratch, (const T*)src, op, rows, cols);
   }
   ordered_cols<T>(dst, (const T*)scratch, op, parts, cols, s);
 }
@@ -1305,8 +1389,8 @@ void reduce_generic(void* dst, const void* src, EType t, Red op, const Dims& kep
   if (n_out <= 0) return;
   long long n_red = 1;
   for (int d = 0; d < reduced.rank; ++d) n_red *= reduced.d[d];
-  if (t == EType::F64) k_reduce_generic<double><<<grid_k(k_reduce_generic<double>, n_out), 256, 0, s>>>((double*)dst, (const double*)src, op, kept, reduced, n_out, n_red);
-  else k_reduce_generic<float><<<grid_k(k_reduce_generic<float>, n_out), 256, 0, s>>>((float*)dst, (const float*)src, op, kept, reduced, n_out, n_red);
+  if (t == EType::F64) launch(k_reduce_generic<double>, grid_k(k_reduce_generic<double>, n_out), 256, 0, s, (double*)dst, (const double*)src, op, kept, reduced, n_out, n_red);
+  else launch(k_reduce_generic<float>, grid_k(k_reduce_generic<float>, n_out), 256, 0, s, (float*)dst, (const float*)src, op, kept, reduced, n_out, n_red);
 }
 
 void gemm(void* c, const void* a, const void* b, EType t, long long m, long long n, long long k, bool ta, bool tb, const GemmBatch& batch,
@@ -1320,7 +1404,7 @@ void gemm(void* c, const void* a, const void* b, EType t, long long m, long long
   const bool small = ((n + 63) / 64) * ((m + 63) / 64) * count < sm_count();
   const long long tile = small ? 16 : 64;
   dim3 grid((unsigned)((n + tile - 1) / tile), (unsigned)((m + tile - 1) / tile), (unsigned)count);
-  auto run = [&](auto kernel, auto* cc, auto* aa, auto* bb) { kernel<<<grid, 256, 0, s>>>(cc, aa, bb, m, n, k, ta, tb, batch); };
+  auto run = [&](auto kernel, auto* cc, auto* aa, auto* bb) { launch(kernel, grid, 256, 0, s, cc, aa, bb, m, n, k, ta, tb, batch); };
   if (t == EType::F64) {
     auto *cc = (double*)c, *aa = (double*)a, *bb = (double*)b;
     if (small) exact ? run(k_gemm<double, true, 16>, cc, aa, bb) : run(k_gemm<double, false, 16>, cc, aa, bb);
@@ -1334,78 +1418,79 @@ void gemm(void* c, const void* a, const void* b, EType t, long long m, long long
 
 void key_split(int32_t* dst, const int32_t* key, long long pairs, cudaStream_t s) {
   if (pairs <= 0) return;
-  k_key_split<<<grid_k(k_key_split, pairs), 256, 0, s>>>(dst, key, pairs);
+  launch(k_key_split, grid_k(k_key_split, pairs), 256, 0, s, dst, key, pairs);
 }
 
 void rand_uniform(void* dst, const int32_t* key, EType t, long long n, cudaStream_t s) {
   if (n <= 0) return;
-  if (t == EType::F64) k_rand_uniform<double><<<grid_k(k_rand_uniform<double>, n), 256, 0, s>>>((double*)dst, key, n);
-  else k_rand_uniform<float><<<grid_k(k_rand_uniform<float>, n), 256, 0, s>>>((float*)dst, key, n);
+  if (t == EType::F64) launch(k_rand_uniform<double>, grid_k(k_rand_uniform<double>, n), 256, 0, s, (double*)dst, key, n);
+  else launch(k_rand_uniform<float>, grid_k(k_rand_uniform<float>, n), 256, 0, s, (float*)dst, key, n);
 }
 
 void rand_normal(void* dst, const int32_t* key, EType t, long long n, cudaStream_t s) {
   if (n <= 0) return;
-  if (t == EType::F64) k_rand_normal<double><<<grid_k(k_rand_normal<double>, n), 256, 0, s>>>((double*)dst, key, n);
-  else k_rand_normal<float><<<grid_k(k_rand_normal<float>, n), 256, 0, s>>>((float*)dst, key, n);
+  if (t == EType::F64) launch(k_rand_normal<double>, grid_k(k_rand_normal<double>, n), 256, 0, s, (double*)dst, key, n);
+  else launch(k_rand_normal<float>, grid_k(k_rand_normal<float>, n), 256, 0, s, (float*)dst, key, n);
 }
 
 void cast(void* dst, EType dt, const void* src, EType st, long long n, cudaStream_t s) {
   if (n <= 0) return;
   unsigned g = grid_for(n);
-  if (dt == EType::F32 && st == EType::F64) k_cast<float, double><<<g, 256, 0, s>>>((float*)dst, (const double*)src, n);
-  else if (dt == EType::F64 && st == EType::F32) k_cast<double, float><<<g, 256, 0, s>>>((double*)dst, (const float*)src, n);
-  else if (dt == EType::F32 && st == EType::I32) k_cast<float, int32_t><<<g, 256, 0, s>>>((float*)dst, (const int32_t*)src, n);
-  else if (dt == EType::F64 && st == EType::I32) k_cast<double, int32_t><<<g, 256, 0, s>>>((double*)dst, (const int32_t*)src, n);
-  else if (dt == EType::I32 && st == EType::F32) k_cast_i32<float><<<g, 256, 0, s>>>((int32_t*)dst, (const float*)src, n);
-  else if (dt == EType::I32 && st == EType::F64) k_cast_i32<double><<<g, 256, 0, s>>>((int32_t*)dst, (const double*)src, n);
+  if (dt == EType::F32 && st == EType::F64) launch(k_cast<float, double>, g, 256, 0, s, (float*)dst, (const double*)src, n);
+  else if (dt == EType::F64 && st == EType::F32) launch(k_cast<double, float>, g, 256, 0, s, (double*)dst, (const float*)src, n);
+  else if (dt == EType::F32 && st == EType::I32) launch(k_cast<float, int32_t>, g, 256, 0, s, (float*)dst, (const int32_t*)src, n);
+  else if (dt == EType::F64 && st == EType::I32) launch(k_cast<double, int32_t>, g, 256, 0, s, (double*)dst, (const int32_t*)src, n);
+  else if (dt == EType::I32 && st == EType::F32) launch(k_cast_i32<float>, g, 256, 0, s, (int32_t*)dst, (const float*)src, n);
+  else if (dt == EType::I32 && st == EType::F64) launch(k_cast_i32<double>, g, 256, 0, s, (int32_t*)dst, (const double*)src, n);
 }
 
 void argmax(int32_t* dst, const void* src, EType t, long long rows, long long v, cudaStream_t s) {
   if (rows <= 0) return;
-  if (t == EType::F64) k_argmax<double><<<grid_k(k_argmax<double>, rows * 32), 256, 0, s>>>(dst, (const double*)src, rows, v);
-  else k_argmax<float><<<grid_k(k_argmax<float>, rows * 32), 256, 0, s>>>(dst, (const float*)src, rows, v);
+  if (t == EType::F64) launch(k_argmax<double>, grid_k(k_argmax<double>, rows * 32), 256, 0, s, dst, (const double*)src, rows, v);
+  else launch(k_argmax<float>, grid_k(k_argmax<float>, rows * 32), 256, 0, s, dst, (const float*)src, rows, v);
 }
 
 void arg_top_k(int32_t* dst, const void* src, EType t, long long rows, long long v, long long k, cudaStream_t s) {
   if (rows <= 0) return;
-  if (t == EType::F64) k_arg_top_k<double><<<(unsigned)rows, 256, 0, s>>>(dst, (const double*)src, v, k);
-  else k_arg_top_k<float><<<(unsigned)rows, 256, 0, s>>>(dst, (const float*)src, v, k);
+  if (t == EType::F64) launch(k_arg_top_k<double>, (unsigned)rows, 256, 0, s, dst, (const double*)src, v, k);
+  else launch(k_arg_top_k<float>, (unsigned)rows, 256, 0, s, dst, (const float*)src, v, k);
 }
 
 void cumsum(void* dst, const void* src, EType t, long long rows, long long v, bool reverse, cudaStream_t s) {
   if (rows <= 0 || v <= 0) return;
   unsigned g = grid_for(rows, 128);
-  if (t == EType::F64) k_cumsum<double><<<g, 128, 0, s>>>((double*)dst, (const double*)src, rows, v, reverse);
-  else if (t == EType::F32) k_cumsum<float><<<g, 128, 0, s>>>((float*)dst, (const float*)src, rows, v, reverse);
-  else k_cumsum_i32<<<g, 128, 0, s>>>((int32_t*)dst, (const int32_t*)src, rows, v, reverse);
+  if (t == EType::F64) launch(k_cumsum<double>, g, 128, 0, s, (double*)dst, (const double*)src, rows, v, reverse);
+  else if (t == EType::F32) launch(k_cumsum<float>, g, 128, 0, s, (float*)dst, (const float*)src, rows, v, reverse);
+  else launch(k_cumsum_i32, g, 128, 0, s, (int32_t*)dst, (const int32_t*)src, rows, v, reverse);
 }
 
 void record_history(double* history, const void* const* slots, const int* types, int n, const long long* step, long long* bad_step,
                     cudaStream_t s) {
-  k_record_history<<<1, 1, 0, s>>>(history, slots, types, n, step, bad_step);
+  launch(k_record_history, 1, 1, 0, s, history, slots, types, n, step, bad_step);
 }
 
-void bump_counter(long long* counter, cudaStream_t s) { k_bump<<<1, 1, 0, s>>>(counter); }
+void bump_counter(long long* counter, cudaStream_t s) { launch(k_bump, 1, 1, 0, s, counter); }
 
 void load_batch(void* dst, const void* batches, size_t bytes, long long n_batches, const long long* counter, cudaStream_t s) {
-  k_load_batch<<<grid_k(k_load_batch, (long long)bytes), 256, 0, s>>>((char*)dst, (const char*)batches, bytes, n_batches, counter);
+  launch(k_load_batch, grid_k(k_load_batch, (long long)bytes), 256, 0, s, (char*)dst, (const char*)batches, bytes, n_batches, counter);
 }
 
 void set_conditional(cudaGraphConditionalHandle h, const void* pred, EType t, long long* count, long long limit, bool bump, cudaStream_t s) {
-  k_set_conditional<<<1, 32, 0, s>>>(h, pred, (int)t, count, limit, bump ? 1 : 0);
+  // The kernel that sets a conditional graph node's condition keeps a plain launch.
+  launch_with(false, k_set_conditional, 1, 32, 0, s, h, pred, (int)t, count, limit, bump ? 1 : 0);
 }
 
-void write_count(int32_t* dst, const long long* count, cudaStream_t s) { k_write_count<<<1, 32, 0, s>>>(dst, count); }
+void write_count(int32_t* dst, const long long* count, cudaStream_t s) { launch(k_write_count, 1, 32, 0, s, dst, count); }
 
 void index_outside(const int32_t* idx, long long n, long long dim, int* flag, cudaStream_t s) {
   if (n <= 0) return;
-  k_index_outside<<<grid_k(k_index_outside, n), 256, 0, s>>>(idx, n, dim, flag);
+  launch(k_index_outside, grid_k(k_index_outside, n), 256, 0, s, idx, n, dim, flag);
 }
 
 void any_nonfinite(const void* src, EType t, long long n, int* flag, cudaStream_t s) {
   if (n <= 0) return;
-  if (t == EType::F64) k_nonfinite<double><<<grid_k(k_nonfinite<double>, n), 256, 0, s>>>((const double*)src, n, flag);
-  else if (t == EType::F32) k_nonfinite<float><<<grid_k(k_nonfinite<float>, n), 256, 0, s>>>((const float*)src, n, flag);
+  if (t == EType::F64) launch(k_nonfinite<double>, grid_k(k_nonfinite<double>, n), 256, 0, s, (const double*)src, n, flag);
+  else if (t == EType::F32) launch(k_nonfinite<float>, grid_k(k_nonfinite<float>, n), 256, 0, s, (const float*)src, n, flag);
 }
 
 }  // namespace rgc

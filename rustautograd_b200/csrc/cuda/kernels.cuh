@@ -49,6 +49,8 @@ enum class EType : int { F32 = 0, F64 = 1, I32 = 2 };
 size_t esize(EType t);
 
 // ---- memory movement ----
+// Whether launches carry the programmatic-dependent-launch attribute (off with RGC_NO_PDL=1).
+bool pdl_enabled();
 void fill_zero(void* dst, size_t bytes, cudaStream_t s);
 // dst[e] = src[base + sum_d coord_d(e) * src.st[d]] over the output extents `out.d`.
 void strided_gather(void* dst, const void* src, EType t, const Dims& out, long long base, long long n, cudaStream_t s);
