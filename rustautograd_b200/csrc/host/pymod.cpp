@@ -498,6 +498,8 @@ PYBIND11_MODULE(RG_MODULE_NAME, m) {
       // Not in rg's module: device kernel launches so far, per-step device seconds (averaged over
       // `repeats` runs timed with events between steps), and each step's algorithmic cost.
       .def("launches", [](const PyCompiled& self) { return self.c->program->launches(); })
+      // Device bytes the program's frames hold now (the compile-time report predates any frame).
+      .def("allocated_bytes", [](const PyCompiled& self) { return self.c->program->allocated_bytes(); })
       .def("step_seconds", [](const PyCompiled& self, std::vector<PyTensor> inputs, size_t repeats) {
         auto in = tensors(inputs);
         std::vector<double> secs(self.c->plan.steps.size(), 0.0);
