@@ -965,6 +965,14 @@ class CpuDevice : public Device {
   std::shared_ptr<Program> compile(const Plan& plan) override { return std::make_shared<CpuProgram>(plan); }
 };
 
+// Plans built as for the CUDA device (its fusion configuration and graph rewrites), executed by
+// this interpreter: lets CPU tests check the plans the device runs.
+class CudaPlanDevice : public CpuDevice {
+ public:
+  std::string name() const override { return "cuda-plan"; }
+  Fuse fuse() const override { return Fuse::CUDA(); }
+};
+
 }  // namespace
 
 void set_threads(int n) { pool().resize(n); }
@@ -993,6 +1001,11 @@ void exec_plan(const Plan& plan, std::vector<Buf>& slots) {
 
 std::shared_ptr<Device> cpu_device() {
   static auto d = std::make_shared<CpuDevice>();
+  return d;
+}
+
+std::shared_ptr<Device> cuda_plan_device() {
+  static auto d = std::make_shared<CudaPlanDevice>();
   return d;
 }
 

@@ -26,5 +26,8 @@ std::vector<Buf> frame(const Plan& plan);
 
 // The CPU device: plans run in this interpreter.
 std::shared_ptr<Device> cpu_device();
+// Plans built with the CUDA device's fusion configuration and rewrites, run in this interpreter
+// (device name "cuda-plan"; offered by `compile` but not listed as available).
+std::shared_ptr<Device> cuda_plan_device();
 
 }  // namespace rg::oracle

@@ -19,6 +19,7 @@ std::vector<std::string> module_available_devices() { return {"cpu"}; }
 
 std::shared_ptr<Device> module_device(const std::string& name) {
   if (name == "cpu") return oracle::cpu_device();
+  if (name == "cuda-plan") return oracle::cuda_plan_device();
   return nullptr;
 }
 

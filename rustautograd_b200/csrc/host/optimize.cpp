@@ -147,6 +147,55 @@ std::pair<Graph, std::vector<uint32_t>> rematerialize(const Graph& g, const std:
   return {std::move(h), std::move(out)};
 }
 
+// The device's own rewrite (no counterpart in rg): a sum of zero-padded blocks that tile one axis
+// of their common shape, as the gradient of slices taken along that axis comes out of autodiff
+// (the q, k, v split of an attention layer: pad each gradient to the full tensor, then add), is
+// the concatenation of the blocks. The sum writes every padded tensor in full and reads them all
+// again; the concatenation reads each block once. Every element equals the sum's (x + 0 = x),
+// except that a block's -0 stays -0 where the sum gives +0.
+// Collects the blocks of the sum rooted at `id`: (start on the padded axis, block id).
+bool pad_blocks(const Graph& g, uint32_t id, const std::vector<size_t>& shape, DType dt, int* axis,
+                std::vector<std::pair<size_t, uint32_t>>* blocks, int depth) {
+  const Node& n = g.nodes[id];
+  if (n.shape != shape || n.dtype != dt || depth > 64) return false;
+  if (n.op.kind == OpKind::Add)
+    return n.inputs.size() == 2 && pad_blocks(g, n.inputs[0], shape, dt, axis, blocks, depth + 1) &&
+           pad_blocks(g, n.inputs[1], shape, dt, axis, blocks, depth + 1);
+  if (n.op.kind != OpKind::Pad || n.inputs.size() != 1) return false;
+  const auto& xs = g.shape(n.inputs[0]);
+  if (xs.size() != shape.size() || n.op.starts.size() != shape.size()) return false;
+  int a = -1;
+  for (size_t d = 0; d < shape.size(); ++d) {
+    if (xs[d] == shape[d] && n.op.starts[d] == 0) continue;
+    if (a >= 0) return false;  // padded along two axes
+    a = (int)d;
+  }
+  if (a < 0 || (*axis >= 0 && *axis != a)) return false;
+  *axis = a;
+  blocks->emplace_back(n.op.starts[a], n.inputs[0]);
+  return true;
+}
+
+// The concatenation equal to the sum `a + b`, when the blocks tile the padded axis exactly.
+std::optional<std::pair<Op, std::vector<uint32_t>>> padded_sum_as_concat(const Graph& g, uint32_t a, uint32_t b, const std::vector<size_t>& shape,
+                                                                         DType dt) {
+  int axis = -1;
+  std::vector<std::pair<size_t, uint32_t>> blocks;
+  if (!pad_blocks(g, a, shape, dt, &axis, &blocks, 0) || !pad_blocks(g, b, shape, dt, &axis, &blocks, 0)) return std::nullopt;
+  std::sort(blocks.begin(), blocks.end());
+  size_t pos = 0;
+  std::vector<uint32_t> ins;
+  for (auto& [start, id] : blocks) {
+    if (start != pos) return std::nullopt;  // a gap or an overlap
+    pos += g.shape(id)[(size_t)axis];
+    ins.push_back(id);
+  }
+  if (pos != shape[(size_t)axis]) return std::nullopt;
+  Op op = Op::make(OpKind::Concat);
+  op.index = (size_t)axis;
+  return std::make_pair(op, ins);
+}
+
 struct Simplified {
   Graph g;
   std::vector<uint32_t> out;
@@ -155,7 +204,8 @@ struct Simplified {
 };
 
 // optimize.rs:286-403. Single forward rewrite: SSA order lets folds and identities cascade.
-Simplified simplify(const Graph& g, const std::vector<uint32_t>& outputs, bool flip_transposes) {
+// `concat_pads` adds the device's padded-sum rewrite (above).
+Simplified simplify(const Graph& g, const std::vector<uint32_t>& outputs, bool flip_transposes, bool concat_pads = false) {
   auto keep = g.reachable(outputs);
   Simplified r;
   r.st.nodes_before = (size_t)std::count(keep.begin(), keep.end(), true);
@@ -184,6 +234,13 @@ Simplified simplify(const Graph& g, const std::vector<uint32_t>& outputs, bool f
       continue;
     }
     Op op = node.op;
+    if (concat_pads && op.kind == OpKind::Add && ins.size() == 2) {
+      if (auto c = padded_sum_as_concat(ng, ins[0], ins[1], node.shape, node.dtype)) {
+        op = c->first;
+        ins = c->second;
+        r.st.simplified += 1;
+      }
+    }
     if (op.kind == OpKind::Pow) {
       auto s = splat(ng, ins[1]);
       if (s && *s == 2.0 && ng.shape(ins[0]) == node.shape) {
@@ -326,10 +383,10 @@ OptResult optimize_mode(const Graph& g, const std::vector<uint32_t>& outputs, Op
     return OptResult{g, outputs, st};
   }
   if (mode == OptMode::Standard) {
-    Simplified s = simplify(g, outputs, true);
+    Simplified s = simplify(g, outputs, true, gpu);
     return finish(s.g, s.out, s.backward, s.st);
   }
-  Simplified baseline = simplify(g, outputs, true);
+  Simplified baseline = simplify(g, outputs, true, gpu);
   Simplified first = simplify(g, outputs, false);
   size_t before = count_kept(g, outputs);
   if (mode == OptMode::SearchLinear && !has_matrix_structure(first.g, first.out)) {
@@ -340,7 +397,7 @@ OptResult optimize_mode(const Graph& g, const std::vector<uint32_t>& outputs, Op
   std::optional<Simplified> candidate;
   const CostModel& model = gpu ? CostModel::CUDA : CostModel::CPU;
   const int set = mode == OptMode::Search ? 2 : mode == OptMode::SearchLinear ? 1 : 0;
-  if (auto found = search(first.g, first.out, model, set, SEARCH_ITERATIONS, SEARCH_NODES, &ss)) candidate = simplify(found->first, found->second, true);
+  if (auto found = search(first.g, first.out, model, set, SEARCH_ITERATIONS, SEARCH_NODES, &ss)) candidate = simplify(found->first, found->second, true, gpu);
   // Compare final forms: both sides have folded constants and flagged transposes.
   ss.cost_before = model.graph_cost(baseline.g, baseline.out);
   ss.cost_after = candidate ? model.graph_cost(candidate->g, candidate->out) : ss.cost_before;

@@ -1,0 +1,105 @@
+"""Plans as the CUDA device builds them (its fusion configuration and graph rewrites), run on the
+CPU oracle through its "cuda-plan" device, against rg's own CPU plan of the same graph.
+
+The device's one rewrite of its own turns a sum of zero-padded blocks that tile an axis (the
+gradient of slices along that axis) into a concatenation; every element is the sum's, except
+that a -0 block element stays -0 where the sum gives +0, so results are compared with zeros of
+either sign equal.
+"""
+import json
+
+import numpy as np
+import pytest
+
+from rustautograd_b200 import frontend as F
+
+
+@pytest.fixture(autouse=True)
+def _frontend(oracle):
+    F.use(oracle, "cpu")
+    yield
+
+
+def plan_ops(c):
+    return [p.get("op") for p in json.loads(c._n.plan_summary()) if "op" in p]
+
+
+def run_both(fn, args):
+    out = {}
+    for dev in ("cpu", "cuda-plan"):
+        c = F.compile(fn, args, validate="none", device=dev)
+        leaves = [F.tensor(x) for x in F.flatten(args)[0]]
+        out[dev] = ([F.Tensor(g).numpy() for g in c._n.call([t._t for t in leaves])], c)
+    return out
+
+
+def assert_same(a, b):
+    assert len(a) == len(b)
+    for k, (x, y) in enumerate(zip(a, b)):
+        assert x.shape == y.shape and x.dtype == y.dtype, k
+        assert np.array_equal(x, y, equal_nan=True), f"output {k} differs"
+
+
+def slice_grad(bounds, axis=0, shape=(6, 5, 4)):
+    """Value and gradient of a sum over slices [a, b) of x along `axis`, each with its own weight:
+    the gradient is the sum of the slices' padded gradients."""
+    x = F.tensor(np.random.default_rng(3).normal(size=shape).astype("float32"))
+
+    def loss(x):
+        total = None
+        for i, (a, b) in enumerate(bounds):
+            idx = [slice(None)] * len(shape)
+            idx[axis] = slice(a, b)
+            xs = x[tuple(idx)]
+            part = (xs * xs).sum() * float(i + 2)
+            total = part if total is None else total + part
+        return total
+    return F.value_and_grad(loss), (x,)
+
+
+@pytest.mark.parametrize("bounds,axis", [
+    ([(0, 2), (2, 4), (4, 6)], 0),        # tiles axis 0, in order
+    ([(3, 6), (0, 3)], 0),                # tiles axis 0, blocks in the other order
+    ([(0, 1), (1, 5)], 1),                # tiles axis 1
+])
+def test_padded_gradient_sums_become_concatenations(bounds, axis):
+    fn, args = slice_grad(bounds, axis)
+    out = run_both(fn, args)
+    assert_same(out["cpu"][0], out["cuda-plan"][0])
+    assert "concat" in plan_ops(out["cuda-plan"][1])
+    assert "pad" not in plan_ops(out["cuda-plan"][1])
+    assert "pad" in plan_ops(out["cpu"][1]), "rg's own plan keeps the padded sum"
+
+
+@pytest.mark.parametrize("bounds,axis", [
+    ([(0, 2), (3, 6)], 0),                # a gap: the zeros between the blocks must stay
+    ([(0, 4), (2, 6)], 0),                # overlapping blocks add
+])
+def test_padded_sums_that_do_not_tile_stay_sums(bounds, axis):
+    fn, args = slice_grad(bounds, axis)
+    out = run_both(fn, args)
+    assert_same(out["cpu"][0], out["cuda-plan"][0])
+    assert "concat" not in plan_ops(out["cuda-plan"][1])
+
+
+def test_blocks_padded_along_two_axes_stay_sums():
+    x = F.tensor(np.random.default_rng(4).normal(size=(4, 4)).astype("float32"))
+    sq = lambda t: (t * t).sum()
+    fn = F.value_and_grad(lambda x: sq(x[0:2, 0:2]) * 3.0 + sq(x[2:4, 2:4]) * 5.0 + sq(x[0:2, 2:4]) + sq(x[2:4, 0:2]) * 7.0)
+    out = run_both(fn, (x,))
+    assert_same(out["cpu"][0], out["cuda-plan"][0])
+    assert "concat" not in plan_ops(out["cuda-plan"][1])
+
+
+def test_gpt_step_plan_concatenates_the_qkv_gradients():
+    """The attention layer's q, k, v split: rg's plan pads each gradient to the full (3, B, H, T,
+    hd) tensor and adds; the device's plan concatenates them, with every output unchanged."""
+    model = F.gpt.GPT(vocab=32, block=16, d=32, heads=4, layers=2)
+    params = model.init(F.random.key(0))
+    opt = F.optim.adamw(1e-3, weight_decay=0.01)
+    state = {"params": params, "opt": opt.init(params), "key": F.random.key(1)}
+    tokens = F.tensor(np.random.default_rng(0).integers(0, 32, size=2000, dtype="int32"))
+    out = run_both(F.gpt.make_train_step(model, opt, 8), (state, tokens))
+    assert_same(out["cpu"][0], out["cuda-plan"][0])
+    assert plan_ops(out["cuda-plan"][1]).count("concat") == 2  # one per layer
+    assert "pad" not in plan_ops(out["cuda-plan"][1])
