@@ -103,3 +103,62 @@ def test_gpt_step_plan_concatenates_the_qkv_gradients():
     assert_same(out["cpu"][0], out["cuda-plan"][0])
     assert plan_ops(out["cuda-plan"][1]).count("concat") == 2  # one per layer
     assert "pad" not in plan_ops(out["cuda-plan"][1])
+
+
+def run_steps(fn, state, data, steps, dev):
+    c = F.compile(fn, (state, data), validate="none", device=dev)
+    return F.run(c, state, data, steps=steps)
+
+
+def test_linear_regression_history_matches_rgs_plan():
+    """500 steps on the device's plan and on rg's, history bit for bit."""
+    x = np.random.default_rng(0).normal(size=(256, 8)).astype("float32")
+    y = x @ np.arange(8, dtype="float32")
+
+    def step(w, batch):
+        value, g = F.value_and_grad(lambda w, b: (((b[0] @ w) - b[1]) ** 2).mean())(w, batch)
+        return w - 0.05 * g, value
+    data = (F.tensor(x), F.tensor(y))
+    a = run_steps(step, F.zeros(8), data, 500, "cpu")
+    b = run_steps(step, F.zeros(8), data, 500, "cuda-plan")
+    assert list(a.history["aux"]) == list(b.history["aux"])
+    assert np.array_equal(a.state.numpy(), b.state.numpy())
+
+
+def test_adamw_update_matches_rgs_plan():
+    """BASELINE config 2 at a reduced size: the fused AdamW update (hoisted step-count chain,
+    dependency-level schedule) against rg's unfused plan, three steps, bit for bit."""
+    rng = np.random.default_rng(5)
+    shapes = [(64, 64), (64,), (16, 64), (64, 16)]
+    mk = lambda s: F.tensor((rng.normal(size=s) * 0.02).astype("float32"))
+    params = [mk(s) for s in shapes]
+    grads = [mk(s) for s in shapes]
+    opt = F.optim.adamw(1e-3, 0.9, 0.999, 1e-8, 0.01)
+    state = {"params": params, "opt": opt.init(params)}
+
+    def step(state, g):
+        p, o = opt.update(g, state["opt"], state["params"])
+        return {"params": p, "opt": o}, o["count"]
+    a = run_steps(step, state, grads, 3, "cpu")
+    b = run_steps(step, state, grads, 3, "cuda-plan")
+    la, lb = F.flatten(a.state)[0], F.flatten(b.state)[0]
+    assert len(la) == len(lb)
+    for k, (u, v) in enumerate(zip(la, lb)):
+        assert np.array_equal(u.numpy(), v.numpy()), f"state leaf {k} differs"
+
+
+def test_matrix_chain_plan_matches_rgs_plan():
+    """BASELINE config 3 at a small size with optimize="search-linear": the device's cost model
+    may pick another multiplication order, so values agree to rounding (1e-4, max-norm)."""
+    rng = np.random.default_rng(6)
+    n = 256
+    mk = lambda *s: F.tensor(rng.normal(size=s).astype("float32"))
+    args = (mk(n, 16), mk(16, n), mk(n, 16), mk(16, n))
+    fn = F.value_and_grad(lambda a, b, c, d: (a @ b @ c @ d).sum(), argnums=(0, 1, 2, 3))
+    out = {}
+    for dev in ("cpu", "cuda-plan"):
+        c = F.compile(fn, args, validate="none", device=dev, optimize="search-linear")
+        out[dev] = [F.Tensor(g).numpy() for g in c._n.call([t._t for t in args])]
+    for k, (u, v) in enumerate(zip(out["cpu"], out["cuda-plan"])):
+        scale = max(float(np.abs(u).max()), 1e-30)
+        assert float(np.abs(u.astype(np.float64) - v).max()) / scale <= 1e-4, f"output {k}"
