@@ -18,6 +18,12 @@ constexpr double SEARCH_MIN_GAIN = 0.9;
 // egraph.rs:363: iteration and e-node limits of the search (never a time limit).
 constexpr size_t SEARCH_ITERATIONS = 6, SEARCH_NODES = 20000;
 constexpr size_t COSTLY_REMAT_ABOVE_BYTES = size_t(2) << 30;
+// The device's own memory policy (no counterpart in rg): rg rematerialises elementwise values in
+// the backward pass to bound the memory of a unified-memory GPU, at the price of recomputing
+// them (8 % more algorithmic bytes in a GPT training step). An HBM device keeps the activations
+// when the plan without rematerialisation peaks at no more than this; recomputation gives the
+// same values, so results do not change.
+constexpr size_t DEVICE_KEEP_ACTIVATIONS_BYTES = size_t(48) << 30;
 
 // The value of a constant whose elements are all equal (optimize.rs:45-53).
 std::optional<double> splat(const Graph& g, uint32_t id) {
@@ -326,7 +332,13 @@ Simplified simplify(const Graph& g, const std::vector<uint32_t>& outputs, bool f
   return r;
 }
 
-OptResult finish(const Graph& ng, const std::vector<uint32_t>& out, const std::vector<bool>& backward, OptStats st) {
+// `gpu`: planning for the device, whose plans keep every activation (no rematerialisation) while
+// that plan's peak live bytes stay within DEVICE_KEEP_ACTIVATIONS_BYTES; above it, rg's policy.
+OptResult finish(const Graph& ng, const std::vector<uint32_t>& out, const std::vector<bool>& backward, OptStats st, bool gpu = false) {
+  if (gpu && Plan::build(ng, out, true).peak_live_bytes <= DEVICE_KEEP_ACTIVATIONS_BYTES) {
+    st.nodes_after = count_kept(ng, out);
+    return OptResult{ng, out, st};
+  }
   auto hr = rematerialize(ng, out, backward, REMAT_MIN, false, st);
   if (Plan::build(hr.first, hr.second, true).peak_live_bytes > COSTLY_REMAT_ABOVE_BYTES) {
     st.rematerialized = 0;
@@ -384,14 +396,14 @@ OptResult optimize_mode(const Graph& g, const std::vector<uint32_t>& outputs, Op
   }
   if (mode == OptMode::Standard) {
     Simplified s = simplify(g, outputs, true, gpu);
-    return finish(s.g, s.out, s.backward, s.st);
+    return finish(s.g, s.out, s.backward, s.st, gpu);
   }
   Simplified baseline = simplify(g, outputs, true, gpu);
   Simplified first = simplify(g, outputs, false);
   size_t before = count_kept(g, outputs);
   if (mode == OptMode::SearchLinear && !has_matrix_structure(first.g, first.out)) {
     baseline.st.nodes_before = before;
-    return finish(baseline.g, baseline.out, baseline.backward, baseline.st);
+    return finish(baseline.g, baseline.out, baseline.backward, baseline.st, gpu);
   }
   SearchStats ss;
   std::optional<Simplified> candidate;
@@ -405,7 +417,7 @@ OptResult optimize_mode(const Graph& g, const std::vector<uint32_t>& outputs, Op
   Simplified& chosen = ss.accepted ? *candidate : baseline;
   chosen.st.nodes_before = before;
   chosen.st.search = ss;
-  return finish(chosen.g, chosen.out, chosen.backward, chosen.st);
+  return finish(chosen.g, chosen.out, chosen.backward, chosen.st, gpu);
 }
 
 // optimize.rs:260-277

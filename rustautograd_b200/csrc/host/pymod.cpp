@@ -528,7 +528,14 @@ PYBIND11_MODULE(RG_MODULE_NAME, m) {
             for (auto& m : st.group.ops) ops += (ops.empty() ? "" : ",") + std::string(m.op.name());
             j["fused"] = ops;
             j["n"] = st.group.n;
+            std::vector<size_t> ins, outs;
+            for (auto& in : st.group.inputs) ins.push_back(in.slot);
+            for (auto& o : st.group.outputs) outs.push_back(o.second);
+            j["in"] = Json(ins);
+            j["out"] = Json(outs);
           } else {
+            j["in"] = Json(st.instr.args);
+            j["out"] = Json(std::vector<size_t>{st.instr.dst});
             j["op"] = st.instr.op.name();
             j["shape"] = Json(st.instr.shape);
             Json args = Json::array();
