@@ -178,7 +178,7 @@ std::string expr(DType d, const rg::Op& op, const std::vector<std::string>& a) {
 
 std::string ElemSpec::source_key() const {
   std::string k = "d" + std::to_string((int)dtype) + "|";
-  for (auto& in : inputs) k += std::to_string((int)in.kind) + (in.col ? "c," : ",");
+  for (auto& in : inputs) k += std::to_string((int)in.kind) + (in.via ? "v" : "") + (in.col ? "c," : ",");
   k += "|";
   for (auto& m : ops) {
     k += std::to_string((int)m.op.kind) + ":" + std::to_string(m.reg) + "(";
@@ -191,7 +191,7 @@ std::string ElemSpec::source_key() const {
 }
 
 // The column length when a broadcast input has the output's shape with a last extent of 1.
-static size_t column_of(const std::vector<size_t>& in, const std::vector<size_t>& out) {
+size_t column_of(const std::vector<size_t>& in, const std::vector<size_t>& out) {
   if (in.size() != out.size() || out.empty() || in.back() != 1 || out.back() <= 1) return 0;
   for (size_t d = 0; d + 1 < out.size(); ++d)
     if (in[d] != out[d]) return 0;
@@ -305,7 +305,16 @@ static std::string kernel_source(const ElemSpec& s, const std::string& name) {
   const int G = 2 * VW;
   for (size_t k = 0; k < s.inputs.size(); ++k) {
     const auto& in = s.inputs[k];
-    if (in.kind == ArgKind::Full) {
+    if (in.kind == ArgKind::Full && in.via) {
+      o << "      " << T << " i" << k << "[" << G << "];\n";
+      if (in.col) {
+        o << "      rg_col_fill<" << T << ", " << VW << ">(i" << k << ", " << in_ptr(k) << ", ea, a.row[" << k << "]);\n";
+        o << "      rg_col_fill<" << T << ", " << VW << ">(i" << k << " + " << VW << ", " << in_ptr(k) << ", eb, a.row[" << k << "]);\n";
+      } else {
+        o << "      rg_bc_fill<" << T << ", " << VW << ">(i" << k << ", " << in_ptr(k) << ", a.bc[" << in.bc << "], ea);\n";
+        o << "      rg_bc_fill<" << T << ", " << VW << ">(i" << k << " + " << VW << ", " << in_ptr(k) << ", a.bc[" << in.bc << "], eb);\n";
+      }
+    } else if (in.kind == ArgKind::Full) {
       o << "      " << T << " i" << k << "[" << G << "];\n";
       o << "      { const " << VT << " va = ((const " << VT << "*)a.in[" << k << "])[q], vb = ((const " << VT << "*)a.in[" << k
         << "])[h1 ? q1 : q];";
@@ -343,7 +352,10 @@ static std::string kernel_source(const ElemSpec& s, const std::string& name) {
   o << "     for (unsigned e = tid; e < n; e += stride) {\n";
   for (size_t k = 0; k < s.inputs.size(); ++k) {
     const auto& in = s.inputs[k];
-    if (in.kind == ArgKind::Full) {
+    if (in.kind == ArgKind::Full && in.via) {
+      if (in.col) o << "      " << T << " i" << k << "[1] = {" << in_ptr(k) << "[rg_fdiv(e, a.row[" << k << "])]};\n";
+      else o << "      unsigned c" << k << "; " << T << " i" << k << "[1] = {" << in_ptr(k) << "[rg_bc_off(a.bc[" << in.bc << "], e, &c" << k << ")]};\n";
+    } else if (in.kind == ArgKind::Full) {
       o << "      " << T << " i" << k << "[1] = {" << in_ptr(k) << "[e]};\n";
     } else {
       long r = in_reg[k];
@@ -365,7 +377,9 @@ static std::string kernel_source(const ElemSpec& s, const std::string& name) {
   o << "    for (long long e = tid; e < n; e += stride) {\n";
   for (size_t k = 0; k < s.inputs.size(); ++k) {
     const auto& in = s.inputs[k];
-    if (in.kind == ArgKind::Full) {
+    if (in.kind == ArgKind::Full && in.via) {
+      o << "      " << T << " i" << k << "[1] = {" << in_ptr(k) << "[bc_off(a.bc64[" << in.bc << "], e)]};\n";
+    } else if (in.kind == ArgKind::Full) {
       o << "      " << T << " i" << k << "[1] = {" << in_ptr(k) << "[e]};\n";
     } else {
       long r = in_reg[k];
@@ -415,7 +429,7 @@ void Jit::build() {
   }
   const char* opts[] = {"--gpu-architecture=sm_100a", "--fmad=false", "--prec-div=true", "--prec-sqrt=true", "--ftz=false", "-default-device",
                         "--std=c++17"};
-  std::string path = cache_dir() + "/" + std::to_string(fnv1a(src + "v5")) + ".cubin";
+  std::string path = cache_dir() + "/" + std::to_string(fnv1a(src + "v6")) + ".cubin";
   std::vector<char> cubin;
   {
     std::ifstream f(path, std::ios::binary);

@@ -45,6 +45,9 @@ struct ElemSpec {
     // A broadcast input of the output's shape with a last extent of 1 (a softmax or LayerNorm
     // statistic): element e reads value e / col, with col the output's last extent.
     size_t col = 0;
+    // A full input whose slot holds a materialised broadcast of a constant or input: the kernel
+    // reads the broadcast's source (`shape`) through broadcast indexing instead (same values).
+    bool via = false;
     std::vector<size_t> shape;
   };
   std::vector<In> inputs;
@@ -54,6 +57,9 @@ struct ElemSpec {
   size_t n = 0;
   std::string source_key() const;
 };
+
+// The output's last extent when `in` is the output's shape with a last extent of 1, else 0.
+size_t column_of(const std::vector<size_t>& in, const std::vector<size_t>& out);
 
 // Builds an ElemSpec from a fused group or from a single elementwise instruction.
 ElemSpec spec_from_group(const rg::Fused& f);

@@ -362,8 +362,10 @@ struct Builder {
     }
     size_t bc0 = bcs.size();
     bool small = spec.n < (1ull << 31);
+    // Descriptors in the order of the inputs' `bc` indices (broadcast inputs and full inputs read
+    // through their broadcast's source, in input order).
     for (auto& in : spec.inputs)
-      if (in.kind == rg::ArgKind::Broadcast) {
+      if (in.kind == rg::ArgKind::Broadcast || in.via) {
         Dims d = dims_of(spec.shape, rg::bstrides(in.shape, spec.shape.size()));
         bool ok = false;
         bcs.push_back(fast_dims(d, &ok));
@@ -949,6 +951,45 @@ std::unique_ptr<Program> make_program(const Plan& plan, int device) {
   }
   p->arena_bytes = off;
   Builder b{p.get()};
+  // The plan step that last wrote each slot, as steps are lowered in order. A full input of an
+  // elementwise step whose slot holds a BroadcastTo of a constant or an input (pinned slots, never
+  // rewritten during a step) is read from the broadcast's source through broadcast indexing: the
+  // same values without reading the full-size copy (an attention layer's causal mask and fill
+  // constants, read again by every layer). The BroadcastTo steps themselves still run, so every
+  // slot holds what the plan says it holds.
+  std::vector<long> last_writer(plan.slots.size(), -1);
+  auto note_writes = [&](size_t k) {
+    const auto& st = plan.steps[k];
+    if (st.fused) {
+      for (auto& o : st.group.outputs) last_writer[o.second] = (long)k;
+      return;
+    }
+    if (st.instr.dst < last_writer.size()) last_writer[st.instr.dst] = (long)k;
+    for (auto& [index, slot] : st.instr.outs) {
+      (void)index;
+      if (slot < last_writer.size()) last_writer[slot] = (long)k;
+    }
+  };
+  auto read_broadcast_sources = [&](ElemSpec& spec, std::vector<size_t>& ins) {
+    bool any = false;
+    for (size_t j = 0; j < spec.inputs.size() && j < ins.size(); ++j) {
+      auto& in = spec.inputs[j];
+      if (in.kind != rg::ArgKind::Full || last_writer[ins[j]] < 0) continue;
+      const rg::Step& w = plan.steps[(size_t)last_writer[ins[j]]];
+      if (w.fused || w.instr.op.kind != OpKind::BroadcastTo || w.instr.args.size() != 1) continue;
+      const size_t src = w.instr.args[0];
+      if (src >= plan.pinned.size() || !plan.pinned[src] || plan.slots[src].first != spec.dtype || w.instr.shape != spec.shape) continue;
+      in.via = true;
+      in.shape = w.instr.arg_shapes[0];
+      in.col = column_of(in.shape, spec.shape);
+      ins[j] = src;
+      any = true;
+    }
+    if (!any) return;
+    int nbc = 0;
+    for (auto& in : spec.inputs)
+      if (in.kind == rg::ArgKind::Broadcast || in.via) in.bc = nbc++;
+  };
   for (size_t k = 0; k < plan.steps.size(); ++k) {
     const auto& st = plan.steps[k];
     if (!st.fused && st.instr.op.kind == OpKind::AllReduce) {
@@ -957,6 +998,7 @@ std::unique_ptr<Program> make_program(const Plan& plan, int device) {
       while (k < plan.steps.size() && !plan.steps[k].fused && plan.steps[k].instr.op.kind == OpKind::AllReduce) {
         const Instr& i = plan.steps[k].instr;
         items.emplace_back(i.args[0], i.dst, i.n, i.dtype == DType::F64);
+        note_writes(k);
         ++k;
       }
       --k;
@@ -988,10 +1030,18 @@ std::unique_ptr<Program> make_program(const Plan& plan, int device) {
       std::vector<size_t> ins, outs;
       for (auto& in : st.group.inputs) ins.push_back(in.slot);
       for (auto& o : st.group.outputs) outs.push_back(o.second);
-      p->steps.push_back(b.elementwise(spec_from_group(st.group), ins, outs));
+      ElemSpec spec = spec_from_group(st.group);
+      read_broadcast_sources(spec, ins);
+      p->steps.push_back(b.elementwise(spec, ins, outs));
+    } else if (st.instr.op.is_unary_elementwise() || st.instr.op.is_binary_elementwise() || st.instr.op.kind == OpKind::Where) {
+      std::vector<size_t> ins = st.instr.args;
+      ElemSpec spec = spec_from_instr(st.instr);
+      read_broadcast_sources(spec, ins);
+      p->steps.push_back(b.elementwise(spec, ins, {st.instr.dst}));
     } else {
       p->steps.push_back(b.lower(st.instr));
     }
+    note_writes(k);
   }
   {
     std::lock_guard<std::mutex> lk(jit_mu());

@@ -106,6 +106,19 @@ def test_causal_softmax_division_with_zero_numerators_is_bit_exact(oracle, dtype
     assert_parity(oracle, lambda a, b: a / b, (F.tensor(e), s), exact=True)
 
 
+def test_where_with_broadcast_masks_is_bit_exact(oracle):
+    """`where` materialises broadcasts of its smaller operands; the device reads the sources of
+    those of constants and inputs directly (a causal mask, fill constants, a column input) and
+    keeps the copy for computed ones."""
+    t = 32
+    x = rnd(4, 3, t, t, seed=51)
+    m = F.tril(t)
+    col = F.tensor((np.random.default_rng(52).random((4, 3, t, 1)) > 0.5).astype("float32"))
+    fn = lambda x, mi, c: (F.where(m, x, -1e9), F.where(m, x * 2.0, 0.0) + x, F.where(mi, x, -1.0) * x, F.where(c, x, 3.0),
+                           F.where((mi + 0.5) > 1.0, x, 0.0))
+    assert_parity(oracle, fn, (x, F.tril(t), col), exact=True)
+
+
 def test_fused_chain_matches_and_forms_groups(oracle):
     x, y = rnd(3, 4096, seed=4), rnd(4096, seed=5)
     fn = lambda a, b: F.tanh(a * 0.7978845608 * (a + 0.044715 * a * a * a)) * b + F.exp(-abs(a)) / (1.0 + b * b)
