@@ -24,6 +24,10 @@ constexpr size_t COSTLY_REMAT_ABOVE_BYTES = size_t(2) << 30;
 // when the plan without rematerialisation peaks at no more than this; recomputation gives the
 // same values, so results do not change.
 constexpr size_t DEVICE_KEEP_ACTIVATIONS_BYTES = size_t(48) << 30;
+// rg also recomputes transcendental values (exp, tanh...) once the plan would peak above 2 GB;
+// the device does so only above this (d512 at batch 512: 1193 instead of 1257 GB of algorithmic
+// traffic per step for a 65 instead of 55 GB peak).
+constexpr size_t DEVICE_COSTLY_REMAT_ABOVE_BYTES = size_t(96) << 30;
 
 // The value of a constant whose elements are all equal (optimize.rs:45-53).
 std::optional<double> splat(const Graph& g, uint32_t id) {
@@ -333,14 +337,15 @@ Simplified simplify(const Graph& g, const std::vector<uint32_t>& outputs, bool f
 }
 
 // `gpu`: planning for the device, whose plans keep every activation (no rematerialisation) while
-// that plan's peak live bytes stay within DEVICE_KEEP_ACTIVATIONS_BYTES; above it, rg's policy.
+// that plan's peak live bytes stay within DEVICE_KEEP_ACTIVATIONS_BYTES; above it rg's policy,
+// escalating to transcendental values only above DEVICE_COSTLY_REMAT_ABOVE_BYTES.
 OptResult finish(const Graph& ng, const std::vector<uint32_t>& out, const std::vector<bool>& backward, OptStats st, bool gpu = false) {
   if (gpu && Plan::build(ng, out, true).peak_live_bytes <= DEVICE_KEEP_ACTIVATIONS_BYTES) {
     st.nodes_after = count_kept(ng, out);
     return OptResult{ng, out, st};
   }
   auto hr = rematerialize(ng, out, backward, REMAT_MIN, false, st);
-  if (Plan::build(hr.first, hr.second, true).peak_live_bytes > COSTLY_REMAT_ABOVE_BYTES) {
+  if (Plan::build(hr.first, hr.second, true).peak_live_bytes > (gpu ? DEVICE_COSTLY_REMAT_ABOVE_BYTES : COSTLY_REMAT_ABOVE_BYTES)) {
     st.rematerialized = 0;
     hr = rematerialize(ng, out, backward, REMAT_MIN, true, st);
   }
