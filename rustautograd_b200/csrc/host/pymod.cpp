@@ -577,6 +577,31 @@ PYBIND11_MODULE(RG_MODULE_NAME, m) {
   }, py::arg("graph"), py::arg("outputs"), py::arg("examples"), py::arg("level"), py::arg("device"), py::arg("optimize"));
 
   m.def("available_devices", [] { return module_available_devices(); });
+  // Not in rg's module: the optimised graph plans are built from (`gpu` adds the device's own
+  // rewrites and memory policy), node by node with the output ids, for tests and plan analysis.
+  m.def("_optimized_describe", [](const PyGraph& graph, std::vector<uint32_t> outputs, const std::string& optimize, bool gpu) {
+    OptMode mode;
+    if (!parse_opt_mode(optimize, &mode)) throw py::value_error("unknown optimize mode " + optimize);
+    for (auto id : outputs) graph.check_id(id);
+    OptResult r = optimize_mode(graph.g, outputs, mode, gpu);
+    auto keep = r.graph.reachable(r.outputs);
+    Json nodes = Json::array();
+    for (size_t i = 0; i < r.graph.nodes.size(); ++i) {
+      const Node& n = r.graph.nodes[i];
+      Json j = Json::object();
+      j["id"] = i;
+      j["op"] = n.op.name();
+      j["key"] = n.op.key();
+      j["inputs"] = Json(std::vector<size_t>(n.inputs.begin(), n.inputs.end()));
+      j["shape"] = Json(n.shape);
+      j["live"] = (bool)keep[i];
+      nodes.push(j);
+    }
+    Json out = Json::object();
+    out["nodes"] = nodes;
+    out["outputs"] = Json(std::vector<size_t>(r.outputs.begin(), r.outputs.end()));
+    return out.dump();
+  });
   // Not in rg's module: the CPU interpreter validate's device check compares a GPU against
   // (validate.rs:674-705). rg links its own; this module has none and takes one from the
   // embedding process: fn(plan blob bytes, [(bytes, shape, dtype)]) -> [(bytes, shape, dtype)].
