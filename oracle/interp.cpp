@@ -8,6 +8,7 @@
 #include <atomic>
 #include <chrono>
 #include <cmath>
+#include <limits>
 #include <condition_variable>
 #include <cstring>
 #include <functional>
@@ -781,6 +782,99 @@ void key_split(const Instr& i, std::vector<Buf>& s) {
   }
 }
 
+// Fused attention (the device's own ops, no counterpart in rg): the CPU definition the device's
+// kernels are checked against. Per batch entry and query row i: Z_j = mask_ij ? (q_i . k_j) / c :
+// fill; m = max_j Z_j; E_j = exp(Z_j - m); s = sum_j E_j; P_j = E_j / s; O_i = sum_j P_j v_j.
+// Sums run in index order. The backward recomputes P from the saved (m, s) and gives
+// dS_j = mask_ij ? P_j (dP_j - sum_l P_l dP_l) / c : 0 with dP_j = dO_i . v_j, then
+// dq = dS k, dk = dS^T q, dv = P^T dO.
+struct AttnDims {
+  size_t batch, t, d, dv;
+};
+AttnDims attn_dims(const Instr& i) {
+  const auto& q = i.arg_shapes[0];
+  size_t r = q.size();
+  AttnDims a;
+  a.t = q[r - 2];
+  a.d = q[r - 1];
+  a.dv = i.arg_shapes[2][r - 1];
+  a.batch = product(q) / (a.t * a.d);
+  return a;
+}
+
+// Z_ij for query row i, key j; `mask_row` is row i of the (T, T) mask.
+template <typename T> T attn_score(const T* q, const T* k, const T* mask_row, size_t i, size_t j, size_t d, T c, T fill) {
+  T acc = (T)0;
+  for (size_t e = 0; e < d; ++e) acc = acc + q[i * d + e] * k[j * d + e];
+  return mask_row[j] != (T)0 ? acc / c : fill;
+}
+
+template <typename T> void attn_fwd(const Instr& i, std::vector<Buf>& s) {
+  const AttnDims a = attn_dims(i);
+  const T c = (T)i.op.value->data.get(0), fill = (T)i.op.value->data.get(1);
+  const T *Q = S<T>(s[i.args[0]]), *K = S<T>(s[i.args[1]]), *V = S<T>(s[i.args[2]]), *M = S<T>(s[i.args[3]]);
+  T* out = S<T>(s[i.dst]);
+  const size_t w = a.dv + 2;
+  std::vector<T> z(a.t);
+  for (size_t b = 0; b < a.batch; ++b) {
+    const T *q = Q + b * a.t * a.d, *k = K + b * a.t * a.d, *v = V + b * a.t * a.dv;
+    for (size_t r = 0; r < a.t; ++r) {
+      T m = -std::numeric_limits<T>::infinity();
+      for (size_t j = 0; j < a.t; ++j) {
+        z[j] = attn_score(q, k, M + r * a.t, r, j, a.d, c, fill);
+        m = z[j] > m || std::isnan(z[j]) ? z[j] : m;
+      }
+      T sum = (T)0;
+      for (size_t j = 0; j < a.t; ++j) {
+        z[j] = std::exp(z[j] - m);
+        sum = sum + z[j];
+      }
+      T* o = out + (b * a.t + r) * w;
+      for (size_t e = 0; e < a.dv; ++e) o[e] = (T)0;
+      for (size_t j = 0; j < a.t; ++j) {
+        const T p = z[j] / sum;
+        for (size_t e = 0; e < a.dv; ++e) o[e] = o[e] + p * v[j * a.dv + e];
+      }
+      o[a.dv] = m;
+      o[a.dv + 1] = sum;
+    }
+  }
+}
+
+template <typename T> void attn_bwd(const Instr& i, std::vector<Buf>& s) {
+  const AttnDims a = attn_dims(i);
+  const T c = (T)i.op.value->data.get(0), fill = (T)i.op.value->data.get(1);
+  const T *Q = S<T>(s[i.args[0]]), *K = S<T>(s[i.args[1]]), *V = S<T>(s[i.args[2]]), *M = S<T>(s[i.args[3]]);
+  const T *ST = S<T>(s[i.args[4]]), *DO = S<T>(s[i.args[5]]);
+  T* out = S<T>(s[i.dst]);
+  const size_t w = 2 * a.d + a.dv;
+  std::fill(out, out + a.batch * a.t * w, (T)0);
+  std::vector<T> p(a.t), dp(a.t);
+  for (size_t b = 0; b < a.batch; ++b) {
+    const T *q = Q + b * a.t * a.d, *k = K + b * a.t * a.d, *v = V + b * a.t * a.dv, *dout = DO + b * a.t * a.dv;
+    T* g = out + b * a.t * w;
+    for (size_t r = 0; r < a.t; ++r) {
+      const T m = ST[(b * a.t + r) * 2], sum = ST[(b * a.t + r) * 2 + 1];
+      T dsum = (T)0;
+      for (size_t j = 0; j < a.t; ++j) {
+        p[j] = std::exp(attn_score(q, k, M + r * a.t, r, j, a.d, c, fill) - m) / sum;
+        T acc = (T)0;
+        for (size_t e = 0; e < a.dv; ++e) acc = acc + dout[r * a.dv + e] * v[j * a.dv + e];
+        dp[j] = acc;
+        dsum = dsum + p[j] * dp[j];
+      }
+      for (size_t j = 0; j < a.t; ++j) {
+        const T ds = M[r * a.t + j] != (T)0 ? p[j] * (dp[j] - dsum) / c : (T)0;
+        for (size_t e = 0; e < a.d; ++e) {
+          g[r * w + e] = g[r * w + e] + ds * k[j * a.d + e];                 // dq
+          g[j * w + a.d + e] = g[j * w + a.d + e] + ds * q[r * a.d + e];     // dk
+        }
+        for (size_t e = 0; e < a.dv; ++e) g[j * w + 2 * a.d + e] = g[j * w + 2 * a.d + e] + p[j] * dout[r * a.dv + e];  // dv
+      }
+    }
+  }
+}
+
 void copy_prefix(Buf& d, const Buf& s, size_t n) { std::memcpy(d.data(), s.data(), n * dtype_size(s.dtype)); }
 void copy_range(Buf& d, size_t at, const Buf& s, size_t from, size_t n) {
   size_t es = dtype_size(s.dtype);
@@ -822,6 +916,12 @@ void exec_instr(const Instr& i, std::vector<Buf>& s) {
       return arg_top_k<double>(i, s);
     case OpKind::KeySplit: return key_split(i, s);
     case OpKind::AllReduce: return all_reduce(i, s);
+    case OpKind::AttnFwd:
+      if (i.dtype == DType::F32) return attn_fwd<float>(i, s);
+      return attn_fwd<double>(i, s);
+    case OpKind::AttnBwd:
+      if (i.dtype == DType::F32) return attn_bwd<float>(i, s);
+      return attn_bwd<double>(i, s);
     case OpKind::Argmax:
       if (s[i.args[0]].dtype == DType::F32) return argmax<float>(i, s);
       return argmax<double>(i, s);

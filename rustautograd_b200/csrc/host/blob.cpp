@@ -183,7 +183,7 @@ struct Reader {
   Op op() {
     Op o;
     uint8_t k = u8();
-    if (k > (uint8_t)OpKind::AllReduce) throw std::runtime_error("plan blob has an unknown op");
+    if (k > (uint8_t)OpKind::AttnBwd) throw std::runtime_error("plan blob has an unknown op");
     o.kind = (OpKind)k;
     o.index = u64();
     o.shape = vec();

@@ -64,6 +64,8 @@ const char* Op::name() const {
     case OpKind::Placeholder: return "placeholder";
     case OpKind::Custom: return "custom_vjp";
     case OpKind::AllReduce: return "all_reduce";
+    case OpKind::AttnFwd: return "attention";
+    case OpKind::AttnBwd: return "attention_grad";
   }
   return "?";
 }
@@ -278,6 +280,8 @@ uint32_t Graph::add(Op op, const std::vector<uint32_t>& inputs) {
     case OpKind::MatMul: case OpKind::MatMulT: case OpKind::Take: case OpKind::TakeAlong:
     case OpKind::TakeGrad: case OpKind::TakeAlongGrad: arity = 2; break;
     case OpKind::Concat: arity = std::max<size_t>(inputs.size(), 1); break;
+    case OpKind::AttnFwd: arity = 4; break;
+    case OpKind::AttnBwd: arity = 6; break;
     default:
       if (op.is_control_flow()) arity = inputs.size();
       else if (op.is_binary_elementwise()) arity = 2;
@@ -501,6 +505,29 @@ std::vector<size_t> Graph::infer(const Op& op, const std::vector<std::vector<siz
     case OpKind::RandUniform: case OpKind::RandNormal: return op.shape;
     case OpKind::KeySplit: return {op.index, 2};
     case OpKind::Custom: case OpKind::AllReduce: return s[0];
+    case OpKind::AttnFwd: case OpKind::AttnBwd: {
+      // q (..., T, d), k (..., T, d), v (..., T, dv) with the same leading extents, mask (T, T);
+      // AttnBwd also stats (..., T, 2) and dO (..., T, dv).
+      const auto &q = s[0], &k = s[1], &v = s[2], &m = s[3];
+      size_t r = q.size();
+      bool ok = r >= 2 && k.size() == r && v.size() == r && m.size() == 2;
+      for (size_t i = 0; ok && i + 2 < r; ++i) ok = k[i] == q[i] && v[i] == q[i];
+      size_t t = ok ? q[r - 2] : 0, d = ok ? q[r - 1] : 0, dv = ok ? v[r - 1] : 0;
+      ok = ok && k[r - 2] == t && v[r - 2] == t && k[r - 1] == d && m[0] == t && m[1] == t;
+      if (ok && op.kind == OpKind::AttnBwd) {
+        std::vector<size_t> st = q, dout = v;
+        st[r - 1] = 2;
+        ok = s[4] == st && s[5] == dout;
+      }
+      if (!ok || !op.value || op.value->n() != 2) {
+        Json o = Json::object();
+        o["input_shapes"] = shapes_json(s);
+        static_err("SHAPE_MISMATCH", op, o, "attention_operands_do_not_fit");
+      }
+      std::vector<size_t> out = q;
+      out[r - 1] = op.kind == OpKind::AttnFwd ? dv + 2 : 2 * d + dv;
+      return out;
+    }
     case OpKind::Reduce: {
       size_t r = s[0].size();
       std::vector<bool> seen(r, false);

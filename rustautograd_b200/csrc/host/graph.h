@@ -33,6 +33,13 @@ enum class OpKind : uint8_t {
   Placeholder, Custom,
   // Data parallelism (no counterpart in rg): the sum of a value over all ranks.
   AllReduce,
+  // Fused attention (no counterpart in rg; produced only by the device's graph rewrite).
+  // AttnFwd(q, k, v, mask) with value = [c, fill]: per batch entry, Z = where(mask, q k^T / c,
+  // fill), softmax along the last axis (max-subtracted), O = P v; the result packs O with each
+  // row's max and exp-sum: (..., T, dv + 2). AttnBwd(q, k, v, mask, stats, dO): the gradients
+  // of O with respect to q, k and v for the cotangent dO, packed as (..., T, 2 d + dv).
+  AttnFwd,
+  AttnBwd,
 };
 
 struct Op {

@@ -2,6 +2,8 @@
 #include "optimize.h"
 
 #include <algorithm>
+#include <cstdlib>
+#include <functional>
 #include <map>
 #include <unordered_map>
 
@@ -206,6 +208,186 @@ std::optional<std::pair<Op, std::vector<uint32_t>>> padded_sum_as_concat(const G
   return std::make_pair(op, ins);
 }
 
+
+// ---- fused attention (the device's own rewrite, no counterpart in rg) ----
+//
+// rg's attention layer and its autodiff leave this pattern in the optimised graph (per layer):
+//   S = matmul_t(q, k; tb)  S1 = S / c  Z = where(mask, S1, fill)  m = max(Z, -1, keepdims)
+//   E = exp(Z - m)  s = sum(E, -1, keepdims)  P = E / s  O = P @ v
+//   dv = matmul_t(P, dO; ta)  dP = matmul_t(dO, v; tb)
+//   dE = dP / s + sum(((-dP) * E) / (s * s), -1, keepdims)  dS = where(mask, dE * E, 0) / c
+//   dq = matmul_t(dS, transpose(k); tb)  dk = transpose(matmul_t(q, dS; ta))
+// It becomes AttnFwd / AttnBwd (q, k, v, the (T, T) mask; O and dq, dk, dv as slices of their
+// packed results), so the (..., T, T) tensors between them are never materialised. Values agree
+// with the pattern's to rounding: softmax sums and products run in another order. Only with
+// RGC_FUSED_ATTENTION=1 while the device kernels await validation on a GPU.
+bool fused_attention_enabled() {
+  const char* e = getenv("RGC_FUSED_ATTENTION");
+  return e && std::string(e) == "1";
+}
+
+struct AttnMatch {
+  uint32_t q, k, v, O, dO, dv, dq, dk;
+  uint32_t mask_src = UINT32_MAX;  // a (T, T) node (the source of a broadcast), else:
+  TensorP mask_const;              // a (T, T) constant cut from a folded full-size mask
+  double c = 1, fill = 0;
+};
+
+std::optional<AttnMatch> match_attention(const Graph& g, uint32_t o_id, const std::vector<std::vector<uint32_t>>& users,
+                                         const std::vector<bool>& live) {
+  auto node = [&](uint32_t id) -> const Node& { return g.nodes[id]; };
+  auto is = [&](uint32_t id, OpKind k) { return node(id).op.kind == k; };
+  auto reduce_last = [&](uint32_t id, ReduceKind r) {
+    const Node& n = node(id);
+    return n.op.kind == OpKind::Reduce && n.op.reduce == r && n.op.flag_a && !n.shape.empty() && n.op.shape.size() == 1 &&
+           n.op.shape[0] + 1 == n.shape.size();
+  };
+  auto splat_of = [&](uint32_t id) -> std::optional<double> {
+    if (auto v = splat(g, id)) return v;
+    if (is(id, OpKind::BroadcastTo)) return splat(g, node(id).inputs[0]);
+    return std::nullopt;
+  };
+  auto user = [&](uint32_t id, const std::function<bool(uint32_t)>& pred) -> std::optional<uint32_t> {
+    std::optional<uint32_t> found;
+    for (uint32_t u : users[id])
+      if (live[u] && pred(u)) {
+        if (found) return std::nullopt;  // ambiguous
+        found = u;
+      }
+    return found;
+  };
+  const Node& on = node(o_id);
+  if (!is(o_id, OpKind::MatMul) || on.dtype != DType::F32 || on.inputs.size() != 2) return std::nullopt;
+  AttnMatch a;
+  a.O = o_id;
+  const uint32_t P = on.inputs[0];
+  a.v = on.inputs[1];
+  if (!is(P, OpKind::Div)) return std::nullopt;
+  const uint32_t E = node(P).inputs[0], s = node(P).inputs[1];
+  if (!reduce_last(s, ReduceKind::Sum) || node(s).inputs[0] != E || !is(E, OpKind::Exp)) return std::nullopt;
+  const uint32_t Zm = node(E).inputs[0];
+  if (!is(Zm, OpKind::Sub)) return std::nullopt;
+  const uint32_t Z = node(Zm).inputs[0], m = node(Zm).inputs[1];
+  if (!reduce_last(m, ReduceKind::Max) || node(m).inputs[0] != Z || !is(Z, OpKind::Where)) return std::nullopt;
+  const uint32_t cond = node(Z).inputs[0], S1 = node(Z).inputs[1], fill = node(Z).inputs[2];
+  if (!is(S1, OpKind::Div)) return std::nullopt;
+  const uint32_t S = node(S1).inputs[0], cn = node(S1).inputs[1];
+  const Node& sn = node(S);
+  if (sn.op.kind != OpKind::MatMulT || sn.op.flag_a || !sn.op.flag_b) return std::nullopt;
+  a.q = sn.inputs[0];
+  a.k = sn.inputs[1];
+  auto c = splat_of(cn);
+  auto f = splat_of(fill);
+  if (!c || !f) return std::nullopt;
+  a.c = *c;
+  a.fill = *f;
+  // Shapes: q, k (..., T, d), v (..., T, dv), S (..., T, T), same leading extents.
+  const auto &qs = g.shape(a.q), &ks = g.shape(a.k), &vs = g.shape(a.v), &Ss = sn.shape;
+  const size_t r = qs.size();
+  if (r < 2 || ks != qs || vs.size() != r || Ss.size() != r || g.dtype(a.q) != DType::F32) return std::nullopt;
+  const size_t T = qs[r - 2];
+  for (size_t i = 0; i + 1 < r; ++i)
+    if (vs[i] != qs[i]) return std::nullopt;
+  if (Ss[r - 1] != T || Ss[r - 2] != T) return std::nullopt;
+  // The mask: one (T, T) pattern for every batch entry.
+  const std::vector<size_t> tt{T, T};
+  if (is(cond, OpKind::BroadcastTo) && g.shape(node(cond).inputs[0]) == tt) {
+    a.mask_src = node(cond).inputs[0];
+  } else if (is(cond, OpKind::Const) && g.shape(cond) == Ss) {
+    const Tensor& full = *node(cond).op.value;
+    Buf b(full.dtype(), T * T);
+    for (size_t i = 0; i < T * T; ++i) b.f32()[i] = (float)full.data.get(i);
+    for (size_t i = T * T; i < full.n(); ++i)
+      if (!(full.data.get(i) == full.data.get(i % (T * T)))) return std::nullopt;
+    a.mask_const = std::make_shared<const Tensor>(tt, std::move(b));
+  } else {
+    return std::nullopt;
+  }
+  if (g.dtype(cond) != DType::F32) return std::nullopt;
+  // Backward: dv = P^T dO, dP = dO v^T, then the softmax gradient chain down to dS.
+  auto dvn = user(P, [&](uint32_t u) { const Node& n = node(u); return n.op.kind == OpKind::MatMulT && n.op.flag_a && !n.op.flag_b && n.inputs[0] == P; });
+  if (!dvn) return std::nullopt;
+  a.dv = *dvn;
+  a.dO = node(a.dv).inputs[1];
+  if (g.shape(a.dO) != vs) return std::nullopt;
+  auto dPn = user(a.dO, [&](uint32_t u) { const Node& n = node(u); return n.op.kind == OpKind::MatMulT && !n.op.flag_a && n.op.flag_b && n.inputs[0] == a.dO && n.inputs[1] == a.v; });
+  if (!dPn) return std::nullopt;
+  const uint32_t dP = *dPn;
+  auto t1 = user(dP, [&](uint32_t u) { return is(u, OpKind::Div) && node(u).inputs[0] == dP && node(u).inputs[1] == s; });
+  auto t2 = user(dP, [&](uint32_t u) { return is(u, OpKind::Neg); });
+  if (!t1 || !t2) return std::nullopt;
+  auto t3 = user(*t2, [&](uint32_t u) { const Node& n = node(u); return n.op.kind == OpKind::Mul && (n.inputs[0] == E || n.inputs[1] == E); });
+  if (!t3) return std::nullopt;
+  auto t4 = user(*t3, [&](uint32_t u) {
+    const Node& n = node(u);
+    if (n.op.kind != OpKind::Div || n.inputs[0] != *t3) return false;
+    const Node& d = node(n.inputs[1]);
+    return d.op.kind == OpKind::Mul && d.inputs[0] == s && d.inputs[1] == s;
+  });
+  if (!t4) return std::nullopt;
+  auto t5 = user(*t4, [&](uint32_t u) { return reduce_last(u, ReduceKind::Sum); });
+  if (!t5) return std::nullopt;
+  auto dE = user(*t5, [&](uint32_t u) {
+    const Node& n = node(u);
+    return n.op.kind == OpKind::Add && ((n.inputs[0] == *t1 && n.inputs[1] == *t5) || (n.inputs[0] == *t5 && n.inputs[1] == *t1));
+  });
+  if (!dE) return std::nullopt;
+  auto dZm = user(*dE, [&](uint32_t u) { const Node& n = node(u); return n.op.kind == OpKind::Mul && (n.inputs[0] == E || n.inputs[1] == E); });
+  if (!dZm) return std::nullopt;
+  // dS = where(mask, dZm, 0) / c, possibly computed more than once (full-size zero constants
+  // are not merged by common-subexpression elimination): every copy counts.
+  std::vector<uint32_t> dS;
+  for (uint32_t w : users[*dZm]) {
+    const Node& n = node(w);
+    if (!live[w] || n.op.kind != OpKind::Where || n.inputs[1] != *dZm || n.inputs[0] != cond) continue;
+    auto z = splat_of(n.inputs[2]);
+    if (!z || *z != 0.0) continue;
+    for (uint32_t u : users[w]) {
+      const Node& dn = node(u);
+      auto cc = dn.inputs.size() == 2 ? splat_of(dn.inputs[1]) : std::nullopt;
+      if (live[u] && dn.op.kind == OpKind::Div && dn.inputs[0] == w && cc && *cc == a.c) dS.push_back(u);
+    }
+  }
+  if (dS.empty()) return std::nullopt;
+  auto any_user = [&](const std::function<bool(uint32_t, uint32_t)>& pred) -> std::optional<uint32_t> {
+    std::optional<uint32_t> found;
+    for (uint32_t d : dS)
+      for (uint32_t u : users[d])
+        if (live[u] && pred(u, d)) {
+          if (found && *found != u) return std::nullopt;  // ambiguous
+          found = u;
+        }
+    return found;
+  };
+  auto swaps_last2 = [&](uint32_t id) {
+    const Node& n = node(id);
+    if (n.op.kind != OpKind::Transpose || n.op.shape.size() != r) return false;
+    for (size_t i = 0; i < r; ++i)
+      if (n.op.shape[i] != (i + 2 < r ? i : (i + 2 == r ? r - 1 : r - 2))) return false;
+    return true;
+  };
+  auto dqn = any_user([&](uint32_t u, uint32_t d) {
+    const Node& n = node(u);
+    if (n.inputs.size() != 2 || n.inputs[0] != d) return false;
+    if (n.op.kind == OpKind::MatMul) return n.inputs[1] == a.k;
+    return n.op.kind == OpKind::MatMulT && !n.op.flag_a && n.op.flag_b && swaps_last2(n.inputs[1]) && node(n.inputs[1]).inputs[0] == a.k;
+  });
+  if (!dqn) return std::nullopt;
+  a.dq = *dqn;
+  auto dkT = any_user([&](uint32_t u, uint32_t d) {
+    const Node& n = node(u);
+    return n.op.kind == OpKind::MatMulT && n.op.flag_a && !n.op.flag_b && n.inputs.size() == 2 && n.inputs[0] == a.q && n.inputs[1] == d;
+  });
+  if (!dkT) return std::nullopt;
+  auto dkn = user(*dkT, [&](uint32_t u) { return swaps_last2(u); });
+  if (!dkn) return std::nullopt;
+  a.dk = *dkn;
+  return a;
+}
+
+struct Simplified;
+Simplified fuse_attention(const Simplified& s);
+
 struct Simplified {
   Graph g;
   std::vector<uint32_t> out;
@@ -339,6 +521,109 @@ Simplified simplify(const Graph& g, const std::vector<uint32_t>& outputs, bool f
 // `gpu`: planning for the device, whose plans keep every activation (no rematerialisation) while
 // that plan's peak live bytes stay within DEVICE_KEEP_ACTIVATIONS_BYTES; above it rg's policy,
 // escalating to transcendental values only above DEVICE_COSTLY_REMAT_ABOVE_BYTES.
+
+// Rebuilds the graph with every matched attention replaced (see match_attention).
+Simplified fuse_attention(const Simplified& in) {
+  const Graph& g = in.g;
+  const size_t N = g.nodes.size();
+  auto live = g.reachable(in.out);
+  std::vector<std::vector<uint32_t>> users(N);
+  for (size_t i = 0; i < N; ++i)
+    if (live[i])
+      for (auto x : g.nodes[i].inputs) users[x].push_back((uint32_t)i);
+  std::vector<AttnMatch> matches;
+  std::vector<long> match_of(N, -1);  // O, dv, dq, dk node -> match index
+  for (size_t i = 0; i < N; ++i) {
+    if (!live[i] || match_of[i] >= 0) continue;
+    auto m = match_attention(g, (uint32_t)i, users, live);
+    if (!m || match_of[m->dv] >= 0 || match_of[m->dq] >= 0 || match_of[m->dk] >= 0) continue;
+    for (uint32_t id : {m->O, m->dv, m->dq, m->dk}) match_of[id] = (long)matches.size();
+    matches.push_back(*m);
+  }
+  if (matches.empty()) return in;
+  Simplified r;
+  r.st = in.st;
+  Graph& ng = r.g;
+  std::vector<uint32_t> map(N, UINT32_MAX);
+  std::vector<uint32_t> stats(matches.size(), UINT32_MAX), mask(matches.size(), UINT32_MAX);
+  std::vector<bool> grads_done(matches.size(), false);
+  std::vector<bool>& backward = r.backward;
+  auto slice_last = [&](uint32_t src, size_t from, size_t to) {
+    const auto& sh = ng.shape(src);
+    Op sl = Op::make(OpKind::Slice);
+    sl.starts.assign(sh.size(), 0);
+    sl.stops = sh;
+    sl.starts.back() = from;
+    sl.stops.back() = to;
+    return ng.add(sl, {src});
+  };
+  auto values = [&](const AttnMatch& m) {
+    Buf b(DType::F64, 2);
+    b.f64()[0] = m.c;
+    b.f64()[1] = m.fill;
+    return std::make_shared<const Tensor>(std::vector<size_t>{2}, std::move(b));
+  };
+  auto mark = [&](bool bw) { backward.resize(ng.nodes.size(), bw); };
+  for (size_t i = 0; i < N; ++i) {
+    const Node& node = g.nodes[i];
+    ng.cur_source = node.source;
+    ng.cur_origin.reset();
+    if (node.op.kind == OpKind::Input) {
+      map[i] = ng.input(node.shape, node.dtype);
+      ng.nodes[map[i]].op = node.op;
+      mark(false);
+      continue;
+    }
+    const long mi = match_of[i];
+    if (mi >= 0 && matches[mi].O == i) {
+      const AttnMatch& m = matches[mi];
+      if (m.mask_src != UINT32_MAX) mask[mi] = map[m.mask_src];
+      else mask[mi] = ng.constant(m.mask_const);
+      mark(false);
+      Op f = Op::make(OpKind::AttnFwd);
+      f.value = values(m);
+      uint32_t a = ng.add(f, {map[m.q], map[m.k], map[m.v], mask[mi]});
+      const size_t dv = g.shape(m.v).back();
+      map[i] = slice_last(a, 0, dv);
+      stats[mi] = slice_last(a, dv, dv + 2);
+      mark(false);
+      r.st.simplified += 1;
+      continue;
+    }
+    if (mi >= 0) {
+      const AttnMatch& m = matches[mi];
+      if (!grads_done[mi]) {
+        Op b = Op::make(OpKind::AttnBwd);
+        b.value = values(m);
+        uint32_t gid = ng.add(b, {map[m.q], map[m.k], map[m.v], mask[mi], stats[mi], map[m.dO]});
+        const size_t d = g.shape(m.q).back(), dv = g.shape(m.v).back();
+        uint32_t dq = slice_last(gid, 0, d), dk = slice_last(gid, d, 2 * d), dvv = slice_last(gid, 2 * d, 2 * d + dv);
+        mark(true);
+        map[m.dq] = dq;
+        map[m.dk] = dk;
+        map[m.dv] = dvv;
+        grads_done[mi] = true;
+      }
+      continue;
+    }
+    std::vector<uint32_t> ins;
+    bool ok = true;
+    for (auto x : node.inputs) {
+      ok = ok && map[x] != UINT32_MAX;
+      ins.push_back(map[x]);
+    }
+    if (!ok) continue;  // depends on a node that was replaced before its inputs existed (never live)
+    uint32_t id = node.op.kind == OpKind::Const ? ng.constant(node.op.value) : ng.add(node.op, ins);
+    ng.nodes[id].origin = node.origin;
+    mark(i < in.backward.size() && in.backward[i]);
+    backward[id] = i < in.backward.size() && in.backward[i];
+    map[i] = id;
+  }
+  for (auto o : in.out) r.out.push_back(map[o]);
+  backward.resize(ng.nodes.size(), false);
+  return r;
+}
+
 OptResult finish(const Graph& ng, const std::vector<uint32_t>& out, const std::vector<bool>& backward, OptStats st, bool gpu = false) {
   if (gpu && Plan::build(ng, out, true).peak_live_bytes <= DEVICE_KEEP_ACTIVATIONS_BYTES) {
     st.nodes_after = count_kept(ng, out);
@@ -401,6 +686,7 @@ OptResult optimize_mode(const Graph& g, const std::vector<uint32_t>& outputs, Op
   }
   if (mode == OptMode::Standard) {
     Simplified s = simplify(g, outputs, true, gpu);
+    if (gpu && fused_attention_enabled()) s = fuse_attention(s);
     return finish(s.g, s.out, s.backward, s.st, gpu);
   }
   Simplified baseline = simplify(g, outputs, true, gpu);
@@ -408,6 +694,7 @@ OptResult optimize_mode(const Graph& g, const std::vector<uint32_t>& outputs, Op
   size_t before = count_kept(g, outputs);
   if (mode == OptMode::SearchLinear && !has_matrix_structure(first.g, first.out)) {
     baseline.st.nodes_before = before;
+    if (gpu && fused_attention_enabled()) baseline = fuse_attention(baseline);
     return finish(baseline.g, baseline.out, baseline.backward, baseline.st, gpu);
   }
   SearchStats ss;
@@ -422,6 +709,7 @@ OptResult optimize_mode(const Graph& g, const std::vector<uint32_t>& outputs, Op
   Simplified& chosen = ss.accepted ? *candidate : baseline;
   chosen.st.nodes_before = before;
   chosen.st.search = ss;
+  if (gpu && fused_attention_enabled()) chosen = fuse_attention(chosen);
   return finish(chosen.g, chosen.out, chosen.backward, chosen.st, gpu);
 }
 

@@ -107,6 +107,15 @@ std::vector<StepCost> step_costs(const Plan& p) {
       (void)sb;
       c.flops = 2.0 * (double)i.n * k;
       c.bytes = in_bytes + (double)i.n * es;
+    } else if (i.op.kind == OpKind::AttnFwd || i.op.kind == OpKind::AttnBwd) {
+      // Products per batch entry: q k^T and P v forward; the backward recomputes q k^T and forms
+      // dO v^T, P^T dO, dS k and dS^T q.
+      const auto& q = i.arg_shapes[0];
+      const double t = (double)q[q.size() - 2], d = (double)q.back(), dv = (double)i.arg_shapes[2].back();
+      const double batch = (double)product(q) / (t * d);
+      c.kind = "attention";
+      c.flops = 2.0 * batch * t * t * (i.op.kind == OpKind::AttnFwd ? d + dv : 3.0 * d + 2.0 * dv);
+      c.bytes = in_bytes + (double)i.n * es;
     } else if (i.op.kind == OpKind::Reduce) {
       c.flops = in_bytes / es;
       c.bytes = in_bytes + (double)i.n * es;

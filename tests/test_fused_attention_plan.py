@@ -1,0 +1,102 @@
+"""The device's fused-attention rewrite (enabled with RGC_FUSED_ATTENTION=1), on the CPU: plans
+built for the CUDA device through the oracle's "cuda-plan" device, whose interpreter runs the fused
+ops' CPU definition, against rg's own plan of the same graph.
+
+The fused ops sum the softmax and its gradient in another order than rg's chain of ops, so values
+agree to rounding (1e-4, max-norm), not bit for bit. A gradient that is zero in exact arithmetic
+(the key bias of an attention layer) is rounding noise on both sides and is not compared.
+"""
+import json
+import math
+
+import numpy as np
+import pytest
+
+from rustautograd_b200 import frontend as F
+from rustautograd_b200.frontend import nn
+
+
+@pytest.fixture(autouse=True)
+def _frontend(oracle, monkeypatch):
+    F.use(oracle, "cpu")
+    monkeypatch.setenv("RGC_FUSED_ATTENTION", "1")
+    yield
+
+
+def ops_of(c):
+    return [p.get("op") for p in json.loads(c._n.plan_summary()) if "op" in p]
+
+
+def both(fn, args):
+    out = {}
+    for dev in ("cpu", "cuda-plan"):
+        c = F.compile(fn, args, validate="none", device=dev)
+        leaves = [F.tensor(x) for x in F.flatten(args)[0]]
+        out[dev] = ([F.Tensor(g).numpy() for g in c._n.call([t._t for t in leaves])], c)
+    return out
+
+
+def rel(a, b):
+    a = a.astype(np.float64)
+    return float(np.abs(a - b).max()) / max(float(np.abs(a).max()), 1e-30)
+
+
+def attention(q, k, v, mask):
+    scores = q @ F.swapaxes(k, -1, -2) / math.sqrt(q.shape[-1])
+    scores = F.where(mask, scores, -1e9)
+    return nn.softmax(scores) @ v
+
+
+@pytest.mark.parametrize("shape", [(2, 3, 16, 8), (1, 4, 33, 5), (3, 7, 4)])
+def test_attention_values_and_gradients_match_rgs_plan(shape):
+    rng = np.random.default_rng(7)
+    q, k, v, w = (F.tensor(rng.normal(size=shape).astype("float32")) for _ in range(4))
+    mask = F.tril(shape[-2])
+
+    def fn(q, k, v, w):
+        return F.value_and_grad(lambda q, k, v: (attention(q, k, v, mask) * w).sum(), argnums=(0, 1, 2))(q, k, v)
+    out = both(fn, (q, k, v, w))
+    assert ops_of(out["cuda-plan"][1]).count("attention") == 1
+    assert ops_of(out["cuda-plan"][1]).count("attention_grad") == 1
+    assert "attention" not in ops_of(out["cpu"][1])
+    for k_, (a, b) in enumerate(zip(out["cpu"][0], out["cuda-plan"][0])):
+        assert rel(a, b) <= 1e-4, f"output {k_}"
+
+
+def test_forward_only_attention_is_left_alone():
+    """Without the backward pattern (no gradient) nothing is rewritten."""
+    rng = np.random.default_rng(8)
+    q, k, v = (F.tensor(rng.normal(size=(2, 8, 4)).astype("float32")) for _ in range(3))
+    out = both(lambda q, k, v: attention(q, k, v, F.tril(8)), (q, k, v))
+    assert "attention" not in ops_of(out["cuda-plan"][1])
+    assert rel(out["cpu"][0][0], out["cuda-plan"][0][0]) == 0.0
+
+
+def test_gpt_step_with_fused_attention_matches_rgs_plan():
+    model = F.gpt.GPT(vocab=32, block=16, d=32, heads=4, layers=2)
+    params = model.init(F.random.key(0))
+    opt = F.optim.adamw(1e-3, weight_decay=0.01)
+    state = {"params": params, "opt": opt.init(params), "key": F.random.key(1)}
+    tokens = F.tensor(np.random.default_rng(0).integers(0, 32, size=2000, dtype="int32"))
+    out = both(F.gpt.make_train_step(model, opt, 8), (state, tokens))
+    ops = ops_of(out["cuda-plan"][1])
+    assert ops.count("attention") == 2 and ops.count("attention_grad") == 2  # one pair per layer
+    d = 32
+    for k_, (a, b) in enumerate(zip(out["cpu"][0], out["cuda-plan"][0])):
+        if a.dtype.kind != "f":
+            assert np.array_equal(a, b), f"output {k_}"
+        elif a.shape == (3 * d,):
+            # The fused q/k/v bias and its optimizer state: the key third is rounding noise.
+            keep = np.r_[0:d, 2 * d:3 * d]
+            assert rel(a[keep], b[keep]) <= 1e-4, f"output {k_}"
+        else:
+            assert rel(a, b) <= 1e-4, f"output {k_}"
+
+
+def test_default_plans_have_no_fused_attention(monkeypatch):
+    monkeypatch.delenv("RGC_FUSED_ATTENTION", raising=False)
+    rng = np.random.default_rng(9)
+    q, k, v, w = (F.tensor(rng.normal(size=(2, 8, 4)).astype("float32")) for _ in range(4))
+    fn = lambda q, k, v, w: F.value_and_grad(lambda q, k, v: (attention(q, k, v, F.tril(8)) * w).sum(), argnums=(0, 1, 2))(q, k, v)
+    c = F.compile(fn, (q, k, v, w), validate="none", device="cuda-plan")
+    assert "attention" not in ops_of(c)
