@@ -362,6 +362,8 @@ def minimum(a, b): return op("minimum", a, b)
 def exp(x): return op("exp", x)
 def log(x): return op("log", x)
 def sqrt(x): return op("sqrt", x)
+def sin(x): return op("sin", x)
+def cos(x): return op("cos", x)
 def tanh(x): return op("tanh", x)
 def floor(x): return op("floor", x)
 

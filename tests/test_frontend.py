@@ -120,14 +120,16 @@ def test_gpt_loss_and_every_gradient_match_pytorch_f64(fe):
         np.testing.assert_allclose(g.numpy(), t.grad.numpy(), rtol=1e-8, atol=1e-10)
 
 
-def test_gpt_memorises_a_pattern(fe):
-    """rg's test_framework.py:378-400 bar: loss below 0.05 within 300 steps."""
+def test_gpt_memorises_a_pattern(fe, tmp_path):
+    """rg's test_framework.py:378-400: loss below 0.05 within 300 steps with the gradient clipped
+    at norm 1, then the parameters survive a checkpoint and the sampler continues the pattern."""
     text = "abcdefgh" * 200
     chars = sorted(set(text))
     tokens = F.tensor(np.array([chars.index(c) for c in text], dtype="int32"))
-    model = F.gpt.GPT(vocab=len(chars), block=8, d=32, heads=2, layers=2)
+    cfg = dict(vocab=len(chars), block=8, d=32, heads=2, layers=2)
+    model = F.gpt.GPT(**cfg)
     params = model.init(F.random.key(0))
-    opt = F.optim.adamw(3e-3, weight_decay=0.0)
+    opt = F.optim.adamw(3e-3, weight_decay=0.0, max_grad_norm=1.0)
     state = {"params": params, "opt": opt.init(params), "key": F.random.key(1)}
     step = F.compile(F.gpt.make_train_step(model, opt, 16), (state, tokens), validate="standard", device="cpu")
     assert step.report["status"] == "ok", step.report
@@ -135,3 +137,37 @@ def test_gpt_memorises_a_pattern(fe):
     assert r.status == "completed"
     assert abs(r.history["aux"][0] - np.log(len(chars))) < 0.3
     assert r.history["aux"][-1] < 0.05
+    path = str(tmp_path / "gpt.safetensors")
+    F.checkpoint.save(path, r.state["params"], metadata={"config": json.dumps(cfg)})
+    loaded, meta = F.checkpoint.load(path, with_metadata=True)
+    sampler = F.gpt.compile_sampler(F.gpt.GPT(**json.loads(meta["config"])), loaded, temperature=0.5, device="cpu")
+    out = F.gpt.generate(sampler, 8, [chars.index(c) for c in "abc"], 16)
+    assert "".join(chars[t] for t in out) == "defghabcdefghabc"
+
+
+@pytest.mark.reference
+def test_optimiser_options_build_rgs_graphs(fe, oracle, rg_reference):
+    """Gradient clipping, a cosine schedule with warmup, SGD with momentum and RMSprop emit the
+    same graphs as rg's optim.py."""
+    rg = rg_reference
+    shapes = [(4, 3), (3,)]
+    rng = np.random.default_rng(3)
+    arrays = [rng.normal(size=s).astype("float32") for s in shapes]
+    cases = [
+        (lambda o: o.adamw(o.cosine_decay(1e-2, 100, warmup_steps=10), max_grad_norm=1.0)),
+        (lambda o: o.sgd(0.1, momentum=0.9, max_grad_norm=0.5)),
+        (lambda o: o.rmsprop(o.cosine_decay(1e-3, 50))),
+        (lambda o: o.adam(1e-3)),
+    ]
+    for make in cases:
+        graphs = []
+        for lib, tensor in ((rg, rg.tensor), (F, F.tensor)):
+            opt = make(lib.optim)
+            params = [tensor(a) for a in arrays]
+            grads = [tensor(a * 0.5) for a in arrays]
+            state = opt.init(params)
+
+            def step(state, p, g, opt=opt):
+                return opt.update(g, state, p)
+            graphs.append(capture_graph(oracle, lambda: lib.compile(step, (state, params, grads), validate="basic"))[1])
+        assert graphs[0] == graphs[1]
