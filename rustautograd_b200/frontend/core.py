@@ -290,6 +290,12 @@ def arange(n, dtype="int32"):
     return Tensor(native().Tensor(array.array(_TYPECODES[dtype], range(n)).tobytes(), [n], dtype))
 
 
+def eye(n, dtype="float32"):
+    """The n x n identity."""
+    vals = array.array(_TYPECODES[dtype], [1 if j == i else 0 for i in range(n) for j in range(n)])
+    return Tensor(native().Tensor(vals.tobytes(), [n, n], dtype))
+
+
 def tril(n, dtype="float32"):
     """Lower-triangular ones: the causal mask."""
     vals = array.array(_TYPECODES[dtype], [1 if j <= i else 0 for i in range(n) for j in range(n)])
@@ -358,6 +364,8 @@ def where(c, a, b):
 
 
 def maximum(a, b): return op("maximum", a, b)
+def equal(a, b): return op("ge", a, b) * op("ge", b, a)
+def not_equal(a, b): return 1 - equal(a, b)
 def minimum(a, b): return op("minimum", a, b)
 def exp(x): return op("exp", x)
 def log(x): return op("log", x)

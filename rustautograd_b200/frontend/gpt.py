@@ -11,11 +11,11 @@ from .core import all_reduce, arange, compile, concatenate, run, take, tensor, t
 
 
 class GPT:
-    def __init__(self, vocab, block, d=128, heads=4, layers=4):
+    def __init__(self, vocab, block, d=128, heads=4, layers=4, dropout_rate=0.0):
         self.block = block
         self.tok = nn.Embedding(vocab, d)
         self.pos = nn.Embedding(block, d)
-        self.blocks = [nn.TransformerBlock(d, heads) for _ in range(layers)]
+        self.blocks = [nn.TransformerBlock(d, heads, dropout_rate=dropout_rate) for _ in range(layers)]
         self.norm = nn.LayerNorm(d)
         self.head = nn.Linear(d, vocab, bias=False)
         self.mask = tril(block)

@@ -171,3 +171,55 @@ def test_optimiser_options_build_rgs_graphs(fe, oracle, rg_reference):
                 return opt.update(g, state, p)
             graphs.append(capture_graph(oracle, lambda: lib.compile(step, (state, params, grads), validate="basic"))[1])
         assert graphs[0] == graphs[1]
+
+
+@pytest.mark.reference
+def test_gpt_with_dropout_builds_rgs_graph(fe, oracle, rg_reference):
+    """examples/gpt.py with dropout_rate 0.1: attention-weight, attention-output and MLP dropout."""
+    import sys
+    sys.path.insert(0, "/root/reference/examples")
+    import gpt as ref_gpt
+    rg = rg_reference
+    cfg = dict(vocab=40, block=8, d=16, heads=2, layers=2, dropout_rate=0.1)
+    toks = np.random.default_rng(1).integers(0, 40, size=500, dtype="int32")
+    graphs = []
+    for lib, mod in ((rg, ref_gpt), (F, F.gpt)):
+        m = mod.GPT(**cfg)
+        p = m.init(lib.random.key(0))
+        o = lib.optim.adamw(1e-3)
+        st = {"params": p, "opt": o.init(p), "key": lib.random.key(1)}
+        graphs.append(capture_graph(oracle, lambda: lib.compile(mod.make_train_step(m, o, 4), (st, lib.tensor(toks)), validate="basic"))[1])
+    assert graphs[0] == graphs[1]
+
+
+@pytest.mark.reference
+def test_nn_layers_losses_and_activations_build_rgs_graphs(fe, oracle, rg_reference):
+    rg = rg_reference
+    rng = np.random.default_rng(4)
+    x_np = rng.normal(size=(3, 5)).astype("float32")
+    y_np = (rng.random((3, 5)) > 0.5).astype("float32")
+    lab_np = np.array([1, 0, 4], dtype="int32")
+    graphs, inits = [], []
+    for lib in (rg, F):
+        nn = lib.nn
+        gru = nn.GRUCell(5, 4)
+        seq = nn.Sequential(nn.Linear(5, 6), nn.relu, nn.Linear(6, 5))
+        params = {"gru": gru.init(lib.random.key(2)), "seq": seq.init(lib.random.key(3))}
+        inits.append([np.asarray(nn.xavier_uniform(lib.random.key(5), (4, 6)).numpy()),
+                      np.asarray(nn.kaiming_uniform(lib.random.key(6), (4, 6)).numpy())])
+
+        def loss(p, x, y, lab, nn=nn, gru=gru, seq=seq, lib=lib):
+            h = lib.zeros((3, 4))
+            for _ in range(3):
+                h = gru(p["gru"], x, h)
+            z = seq(p["seq"], x)
+            return (nn.binary_cross_entropy_with_logits(z, y) + nn.l1_loss(nn.sigmoid(z), y) + nn.softplus(z).mean() + nn.silu(z).mean()
+                    + (h * h).mean() + (nn.one_hot(lab, 5) * z).sum() + nn.accuracy(z, lab))
+
+        def step(p, x, y, lab, loss=loss, lib=lib):
+            return lib.value_and_grad(loss)(p, x, y, lab)
+        args = (params, lib.tensor(x_np), lib.tensor(y_np), lib.tensor(lab_np))
+        graphs.append(capture_graph(oracle, lambda: lib.compile(step, args, validate="basic"))[1])
+    assert graphs[0] == graphs[1]
+    for a, b in zip(inits[0], inits[1]):
+        np.testing.assert_array_equal(a, b)
