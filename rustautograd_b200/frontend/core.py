@@ -134,16 +134,29 @@ class _Math:
     def exp(self): return op("exp", self)
     def log(self): return op("log", self)
     def sqrt(self): return op("sqrt", self)
+    def sin(self): return op("sin", self)
+    def cos(self): return op("cos", self)
     def tanh(self): return op("tanh", self)
     def floor(self): return op("floor", self)
-
+    def take(self, idx, axis=0): return take(self, idx, axis)
+    def argmax(self, axis=-1): return argmax(self, axis)
+    def swapaxes(self, a, b): return swapaxes(self, a, b)
     def squeeze(self, axis=None): return squeeze(self, axis)
 
+    def var(self, axis=None, keepdims=False):
+        """Mean squared deviation from the mean (population variance)."""
+        d = self - self.mean(axis=axis, keepdims=True)
+        return (d * d).mean(axis=axis, keepdims=keepdims)
+
+    def std(self, axis=None, keepdims=False): return self.var(axis=axis, keepdims=keepdims).sqrt()
+
     def __iter__(self):
+        if self.ndim == 0:
+            raise _error("INVALID_SLICE", {"shape": self.shape}, "cannot_iterate_a_scalar")
         return (self[i] for i in range(self.shape[0]))
 
     def __getitem__(self, key):
-        if isinstance(key, (Tensor, Tracer, list)):
+        if isinstance(key, (Tensor, Tracer, list)) or (hasattr(key, "tobytes") and hasattr(key, "dtype")):
             return take(self, tensor(key, "int32") if isinstance(key, list) else key, 0)
         key = key if isinstance(key, tuple) else (key,)
         if any(k is Ellipsis for k in key):
@@ -157,6 +170,8 @@ class _Math:
         for k in key:
             if isinstance(k, slice) and k.step not in (None, 1):
                 idx = list(range(*k.indices(self.shape[position])))
+                if not idx:
+                    raise _error("INVALID_SLICE", {"shape": self.shape, "axis": position, "slice": repr(k)}, "stepped_slice_selects_nothing")
                 stepped = take(stepped, tensor(idx, "int32"), position)
                 k = slice(None)
             plain.append(k)
@@ -174,12 +189,14 @@ class _Math:
                 starts.append(start)
                 stops.append(max(start, stop))
                 keep.append(max(0, stop - start))
-            else:
+            elif isinstance(k, int):
                 i = k + dim if k < 0 else k
                 if not 0 <= i < dim:
                     raise _error("INVALID_SLICE", {"shape": self.shape, "axis": axis, "index": k}, "index_out_of_bounds")
                 starts.append(i)
                 stops.append(i + 1)
+            else:
+                raise _error("INVALID_SLICE", {"shape": self.shape, "index_type": type(k).__name__}, "unsupported_index_type")
             axis += 1
         out = op("slice", self, starts=starts, stops=stops)
         return out.reshape(keep) if tuple(keep) != out.shape else out
@@ -284,10 +301,18 @@ def zeros(shape, dtype="float32"): return _filled(shape, 0, dtype)
 def ones(shape, dtype="float32"): return _filled(shape, 1, dtype)
 def full(shape, value, dtype="float32"): return _filled(shape, value, dtype)
 def zeros_like(x): return _filled(x.shape, 0, x.dtype)
+def ones_like(x): return _filled(x.shape, 1, x.dtype)
 
 
 def arange(n, dtype="int32"):
     return Tensor(native().Tensor(array.array(_TYPECODES[dtype], range(n)).tobytes(), [n], dtype))
+
+
+def linspace(start, stop, num, dtype="float32"):
+    """`num` evenly spaced values from `start` to `stop`, both included (start + i * step)."""
+    step = (stop - start) / (num - 1) if num > 1 else 0.0
+    vals = array.array(_TYPECODES[dtype], [start + i * step for i in range(num)])
+    return Tensor(native().Tensor(vals.tobytes(), [num], dtype))
 
 
 def eye(n, dtype="float32"):
@@ -374,6 +399,30 @@ def sin(x): return op("sin", x)
 def cos(x): return op("cos", x)
 def tanh(x): return op("tanh", x)
 def floor(x): return op("floor", x)
+def abs(x): return op("abs", x)
+def sign(x): return op("sign", x)
+def square(x): return x * x
+def clip(x, low, high): return minimum(maximum(x, low), high)
+def broadcast_to(x, shape): return op("broadcast_to", x, shape=list(shape))
+def matmul(a, b): return op("matmul", a, b)
+def reshape(x, *shape): return x.reshape(*shape)
+def transpose(x, *perm): return x.transpose(*perm)
+
+
+def flip(x, axis=-1):
+    """Reverses `x` along `axis` (a take of the positions in reverse order)."""
+    axis = _axis(x, axis)
+    return take(x, tensor(list(range(x.shape[axis] - 1, -1, -1)), "int32"), axis)
+
+
+def expand_dims(x, axis):
+    axis = axis + x.ndim + 1 if axis < 0 else axis
+    return x.reshape(tuple(x.shape[:axis]) + (1,) + tuple(x.shape[axis:]))
+
+
+def stack(xs, axis=0):
+    """Joins equal-shaped tensors along a new axis: a concatenation of their expanded forms."""
+    return concatenate([expand_dims(x, axis) for x in xs], axis)
 
 
 def all_reduce(x):
@@ -642,8 +691,10 @@ def tree_leaves(t): return flatten(t)[0]
 
 # ---- transformations ----
 
-def value_and_grad(f, argnums=0):
-    """`(*args) -> (value, grads of args[argnums])`, recorded as gradient nodes on the trace."""
+def value_and_grad(f, argnums=0, has_aux=False):
+    """`(*args) -> (value, grads of args[argnums])`, recorded as gradient nodes on the trace.
+    With `has_aux=True`, `f` returns `(scalar, aux)` and the result is `((value, aux), grads)`;
+    a tuple `argnums` gives a tuple of gradients (python/rg/_core.py value_and_grad)."""
     many = isinstance(argnums, tuple)
     nums = argnums if many else (argnums,)
 
@@ -660,15 +711,104 @@ def value_and_grad(f, argnums=0):
             lifted = [Tracer(g, _as_node(g, l, dtype or "float32")) for l in leaves]
             call_args[n] = unflatten(tdef, lifted)
             groups.append((lifted, tdef))
-        y = f(*call_args)
+        out = f(*call_args)
+        y, aux = out if has_aux else (out, None)
+        if not isinstance(y, (Tensor, Tracer, int, float)):
+            raise _error("GRAD_NON_SCALAR", {"returned_type": type(y).__name__}, "function_must_return_a_scalar_tensor")
         yid = _as_node(g, y, _first_dtype([t for lifted, _ in groups for t in lifted]) or "float32")
         grads = []
         for lifted, tdef in groups:
             ids = g.grad(yid, [t._id for t in lifted], src)
             grads.append(unflatten(tdef, [Tracer(g, i) for i in ids]))
-        return Tracer(g, yid), (tuple(grads) if many else grads[0])
+        value = Tracer(g, yid)
+        return ((value, aux) if has_aux else value), (tuple(grads) if many else grads[0])
 
     return transformed
+
+
+def grad(f, argnums=0, has_aux=False):
+    """The gradients of `value_and_grad` alone (then `aux`, with `has_aux=True`)."""
+    vg = value_and_grad(f, argnums, has_aux)
+
+    def transformed(*args):
+        value, grads = vg(*args)
+        return (grads, value[1]) if has_aux else grads
+    return transformed
+
+
+def _traced(fn):
+    """`fn` on the current trace, or compiled and run once on concrete inputs outside one."""
+    def wrapped(*args):
+        return fn(*args) if _trace_stack else compile(fn, args, validate="none")(*args)
+    return wrapped
+
+
+def jvp(f, primals, tangents):
+    """Forward-mode `(f(*primals), J @ tangents)` from two reverse passes: the gradient of
+    <f(p), u> with respect to p is J^T u; its inner product with the tangents is linear in u,
+    and differentiating that with respect to u gives J t."""
+
+    def body(primals, tangents):
+        g = _trace_stack[-1]
+        ys = f(*primals)
+        u = Tracer(g, _as_node(g, zeros_like(ys), ys.dtype))
+        jt_u = grad(lambda ps: (f(*ps) * u).sum())(tuple(primals))
+        dot = sum((a * b).sum() for a, b in zip(flatten(jt_u)[0], flatten(tuple(tangents))[0]))
+        return ys, Tracer(g, g.grad(dot._id, [u._id], _where_from())[0])
+    return _traced(body)(tuple(primals), tuple(tangents))
+
+
+def hessian(f):
+    """Dense Hessian of a scalar function of one tensor, one reverse pass per row of the
+    flattened gradient; its size is the square of the input's."""
+
+    def body(x):
+        n = grad(f)(x).reshape(-1).shape[0]
+        rows = [grad(lambda v, i=i: grad(f)(v).reshape(-1)[i])(x).reshape(-1) for i in range(n)]
+        return stack(rows).reshape(tuple(x.shape) + tuple(x.shape))
+    return _traced(body)
+
+
+def custom_vjp(f, bwd):
+    """`f` with a hand-written gradient: `bwd(args, y, cotangent)` returns one gradient per
+    argument, each of its argument's shape and dtype. The graph records `f`'s output with the
+    rule in place of differentiating through `f`."""
+
+    def wrapped(*args):
+        if not _trace_stack:
+            return _traced(wrapped)(*args)
+        g = _trace_stack[-1]
+        src = _where_from()
+        dtype = _first_dtype(args)
+        lifted = [Tracer(g, _as_node(g, a, dtype or "float32")) for a in args]
+        y = f(*lifted)
+        ct = Tracer(g, g.placeholder(list(y.shape), y.dtype))
+        grads = bwd(tuple(lifted), y, ct)
+        if len(grads) != len(lifted):
+            raise _error("CUSTOM_VJP_MISMATCH", {"inputs": len(lifted), "gradients": len(grads)}, "rule_must_return_one_gradient_per_input")
+        rules = []
+        for a, c in zip(lifted, grads):
+            c = c if isinstance(c, Tracer) else Tracer(g, _as_node(g, c, a.dtype))
+            if c.shape != a.shape or c.dtype != a.dtype:
+                raise _error("CUSTOM_VJP_MISMATCH", {"input_shape": a.shape, "gradient_shape": c.shape, "input_dtype": a.dtype,
+                                                     "gradient_dtype": c.dtype}, "gradient_must_match_its_input")
+            rules.append((a._id, c._id))
+        return Tracer(g, g.custom(y._id, ct._id, rules, src))
+    return wrapped
+
+
+def devices():
+    """Device names `compile(device=...)` accepts on the selected engine module."""
+    return native().available_devices()
+
+
+class Report(dict):
+    """A compile, check or run report: plain JSON data that prints as indented JSON."""
+
+    def __str__(self): return json.dumps(self, indent=2, ensure_ascii=False)
+
+    @property
+    def ok(self): return self.get("status") != "validation_failed"
 
 
 class Compiled:
@@ -681,7 +821,7 @@ class Compiled:
         self._out_def = out_def
         self._n_out = n_out
         self._extras = list(extras)  # names of the observe=True instrument outputs after the outputs
-        self.report = json.loads(handle.report_json)
+        self.report = Report(json.loads(handle.report_json))
 
     def _inputs(self, args):
         leaves, tdef = flatten(args)
@@ -693,6 +833,14 @@ class Compiled:
     def __call__(self, *args):
         out = self._n.call(self._inputs(args))
         return unflatten(self._out_def, [Tensor(t) for t in out[:self._n_out]])
+
+    def check(self, *args):
+        """Runs the instrumented reference graph on these inputs and returns its diagnostics."""
+        return Report(json.loads(self._n.check(self._inputs(args))))
+
+    def profile(self, *args, repeats=5):
+        """Per-operation timing of the optimized plan on these inputs, slowest first."""
+        return Report(json.loads(self._n.profile(self._inputs(args), repeats)))
 
     def plan_blob(self):
         return self._n.plan_blob()
@@ -761,22 +909,81 @@ def compile(fn, example_inputs, validate="standard", device=None, optimize="sear
 
 
 class RunResult:
+    """Outcome of `run`: `state`, the last `aux`, `history` (each scalar aux per step), `status`,
+    `steps` run of `requested_steps`, `nonfinite_step`, `elapsed` device seconds."""
+
     def __init__(self, **kw):
         self.__dict__.update(kw)
 
+    def __repr__(self):
+        return f"RunResult(status={self.status!r}, steps={self.steps}, elapsed={self.elapsed:.4f}s)"
 
-def run(compiled, state, data=None, steps=1):
-    """Iterates `state = step(state[, data])` in the engine: one native call, no Python per step."""
+
+def _mismatch(k, want, got):
+    return _error("INPUT_SIGNATURE_MISMATCH", {"input_index": k, "expected": repr(want), "actual": repr(got), "recompile_required": True},
+                  "input_signature_changed")
+
+
+def _batch(compiled, batch, n_state):
+    ts = [tensor(l) for l in flatten(batch)[0]]
+    for k, t in enumerate(ts):
+        want = compiled._in_sig[n_state + k]
+        if (t.shape, t.dtype) != want:
+            raise _mismatch(n_state + k, want, (t.shape, t.dtype))
+    return [t._t for t in ts]
+
+
+def _run_contract(compiled, state, data):
+    """Checks `state` and `data` against the compiled step (python/rg/_core.py _setup): the step
+    takes `state` or `(state, data)` and returns `state` or `(state, aux)`; `data` is one batch,
+    a list of batches, or an iterator of batches."""
     arity = len(compiled._in_def[1])
+    if arity not in (1, 2):
+        raise _error("STATE_CONTRACT_VIOLATION", {"arity": arity}, "step_must_take_state_or_state_and_data")
     leaves, state_def = flatten(state)
     leaves = [tensor(l) for l in leaves]
+    if state_def != compiled._in_def[1][0]:
+        raise _error("INPUT_SIGNATURE_MISMATCH", {"expected_structure": repr(compiled._in_def[1][0]), "actual_structure": repr(state_def),
+                                                  "recompile_required": True}, "state_structure_changed")
+    for k, t in enumerate(leaves):
+        if (t.shape, t.dtype) != compiled._in_sig[k]:
+            raise _mismatch(k, compiled._in_sig[k], (t.shape, t.dtype))
     d = compiled._out_def
-    has_aux = not (d == state_def)
-    aux_def = d[1][1] if has_aux else None
-    n_state = len(leaves)
-    batches = []
+    if d == state_def:
+        aux_def, has_aux = None, False
+    elif d is not None and d[0] == "tuple" and len(d[1]) == 2 and d[1][0] == state_def:
+        aux_def, has_aux = d[1][1], True
+    else:
+        raise _error("STATE_CONTRACT_VIOLATION", {"state_structure": repr(state_def), "output_structure": repr(d)},
+                     "step_must_return_new_state_or_new_state_and_aux")
+    iterator, batches = None, []
     if arity == 2:
-        batches = [[tensor(l)._t for l in flatten(data)[0]]]
+        data_def = compiled._in_def[1][1]
+        if hasattr(data, "__next__"):
+            iterator = data
+        elif flatten(data)[1] == data_def:
+            batches = [_batch(compiled, data, len(leaves))]
+        elif isinstance(data, (list, tuple)) and data and all(flatten(b)[1] == data_def for b in data):
+            batches = [_batch(compiled, b, len(leaves)) for b in data]
+        else:
+            raise _error("INPUT_SIGNATURE_MISMATCH", {"expected_batch_structure": repr(data_def), "actual_structure": repr(flatten(data)[1]),
+                                                      "recompile_required": True}, "data_structure_changed")
+    return leaves, state_def, has_aux, aux_def, iterator, batches
+
+
+def run(compiled, state, data=None, steps=1, callback=None, every=None):
+    """Iterates `state = step(state[, data])` in the engine, with no Python between steps.
+
+    Batches in a list are cycled. With `every`, or an iterator (pulled 256 batches at a time by
+    default), the run goes in chunks of that many steps, and `callback(result)` after each chunk
+    may return False to stop. A non-finite step ends the run (status "stopped_nonfinite")."""
+    if not compiled.report.ok:
+        d = next(x for x in compiled.report["diagnostics"] if x["severity"] == "error")
+        e = DiagnosticError(json.dumps(d))
+        e.diagnostic = d
+        raise e
+    leaves, state_def, has_aux, aux_def, iterator, batches = _run_contract(compiled, state, data)
+    n_state = len(leaves)
     aux_names = _paths(aux_def, "aux") if has_aux else []
     shapes = compiled._n.output_shapes
     scalar = [k for k in range(n_state, n_state + len(aux_names)) if all(x == 1 for x in shapes[k])]
@@ -786,9 +993,94 @@ def run(compiled, state, data=None, steps=1):
         names[compiled._n_out + j] = name
     state_map = [(k, k) for k in range(n_state)]
     data_inputs = list(range(n_state, len(compiled._in_sig)))
-    new_state, outputs, hist, ran, bad, seconds = compiled._n.run(state_map, data_inputs, scalar, [t._t for t in leaves], batches, steps)
-    history = {names[k]: h for k, h in zip(scalar, hist)}
-    aux = unflatten(aux_def, [Tensor(t) for t in outputs[n_state:compiled._n_out]]) if has_aux and outputs else None
-    return RunResult(status="stopped_nonfinite" if bad is not None else "completed",
-                     state=unflatten(state_def, [Tensor(t) for t in new_state]), aux=aux, history=history, steps=ran,
-                     nonfinite_step=bad, elapsed=seconds)
+    chunk = every if every else (256 if iterator is not None else steps)
+    chunk = max(1, min(chunk, steps)) if steps else 1
+
+    current = [t._t for t in leaves]
+    history = {names[k]: [] for k in scalar}
+    done, elapsed, bad_step, aux, stopped = 0, 0.0, None, None, False
+    last = (current, batches[:1], 0, 0)  # the latest chunk's start state, batches, steps and offset
+    result = None
+    while done < steps and bad_step is None and not stopped:
+        n = min(chunk, steps - done)
+        if iterator is not None:
+            part = []
+            for _ in range(n):
+                try:
+                    part.append(_batch(compiled, next(iterator), n_state))
+                except StopIteration:
+                    break
+            if not part:
+                break
+            n = len(part)
+        else:
+            at = done % len(batches) if batches else 0
+            part = batches[at:] + batches[:at]
+        new_state, outputs, hist, ran, bad, seconds = compiled._n.run(state_map, data_inputs, scalar, current, part, n)
+        last = (current, part, ran, done)
+        for k, h in zip(scalar, hist):
+            history[names[k]].extend(h)
+        done += ran
+        elapsed += seconds
+        bad_step = None if bad is None else done - ran + bad
+        if bad_step is None and not all(t.is_finite() for t in new_state):
+            bad_step = done - 1
+        current = new_state
+        if has_aux and outputs:
+            aux = unflatten(aux_def, [Tensor(t) for t in outputs[n_state:compiled._n_out]])
+        result = RunResult(status="stopped_nonfinite" if bad_step is not None else "running", state=unflatten(state_def, [Tensor(t) for t in current]),
+                           aux=aux, history=history, steps=done, requested_steps=steps, nonfinite_step=bad_step, elapsed=elapsed,
+                           compiled=compiled, _replay=(state_map, data_inputs, scalar, state_def) + last)
+        if callback is not None and bad_step is None and callback(result) is False:
+            stopped = True
+    if result is None:
+        return RunResult(status="completed", state=unflatten(state_def, [Tensor(t) for t in current]), aux=None, history=history, steps=0,
+                         requested_steps=steps, nonfinite_step=None, elapsed=0.0, compiled=compiled,
+                         _replay=(state_map, data_inputs, scalar, state_def) + last)
+    if bad_step is None:
+        result.status = "stopped_by_callback" if stopped else "completed"
+    return result
+
+
+def _json_num(x):
+    if x != x:
+        return "nan"
+    if x in (float("inf"), float("-inf")):
+        return "inf" if x > 0 else "-inf"
+    return x
+
+
+def inspect(target):
+    """Explains a Compiled (its report) or a RunResult. A run that stopped on a non-finite value
+    is replayed from the start of its last chunk (every chunk ends with a finiteness check, so it
+    holds the failure) to the first bad step, whose inputs are checked node by node."""
+    if isinstance(target, Compiled):
+        return target.report
+    state_map, data_inputs, scalar, state_def, start, part, ran, offset = target._replay
+    c = target.compiled
+    out = Report(status=target.status, run={"steps": target.steps, "requested_steps": target.requested_steps, "elapsed_seconds": target.elapsed},
+                 history={k: {"first": _json_num(h[0]), "last": _json_num(h[-1]), "min": _json_num(min(h)), "max": _json_num(max(h))}
+                          for k, h in target.history.items() if h},
+                 diagnostics=[])
+    if target.status != "stopped_nonfinite":
+        batch = part[(ran - 1) % len(part)] if part and ran else (part[0] if part else [])
+        checked = json.loads(c._n.check([t._t for t in flatten(target.state)[0]] + batch))
+        out["gradients"] = checked["gradients"]
+        out["diagnostics"] = checked["diagnostics"]
+        return out
+    found = c._n.replay(state_map, data_inputs, scalar, start, part, ran)
+    if found is None:
+        out["status"] = "not_reproduced"
+        out["diagnostics"] = [{"code": "REPLAY_DID_NOT_REPRODUCE", "severity": "warning", "diagnosis": {"cause": "unknown", "certainty": "unknown"}}]
+        return out
+    step, batch_index, before = found
+    checked = json.loads(c._n.check(before + (part[batch_index] if part else [])))
+    out["status"] = "nonfinite_detected"
+    out["diagnostics"] = checked["diagnostics"]
+    if not any(d.get("severity") == "error" for d in out["diagnostics"]):
+        # The unoptimized reference graph can round differently from the plan near overflow.
+        out["diagnostics"].append({"code": "NONFINITE_NOT_LOCALIZED", "severity": "warning",
+                                   "diagnosis": {"cause": "reference_run_stayed_finite", "certainty": "unknown"}})
+    out["repro"] = {"step": offset + step, "batch_index": batch_index if part else None, "validate": c.report["repro"]["level"],
+                    "seed": c.report["repro"]["seed"]}
+    return out

@@ -223,3 +223,68 @@ def test_nn_layers_losses_and_activations_build_rgs_graphs(fe, oracle, rg_refere
     assert graphs[0] == graphs[1]
     for a, b in zip(inits[0], inits[1]):
         np.testing.assert_array_equal(a, b)
+
+
+@pytest.mark.reference
+def test_core_functions_and_transformations_build_rgs_graphs(fe, oracle, rg_reference):
+    """abs, sign, square, clip, flip, broadcast_to, matmul, reshape, transpose, expand_dims,
+    stack, ones_like, linspace, var/std, grad with aux, jvp, hessian and custom_vjp emit rg's ops."""
+    rg = rg_reference
+    rng = np.random.default_rng(7)
+    a_np = rng.normal(size=(3, 4)).astype("float32")
+    b_np = rng.normal(size=(4, 2)).astype("float32")
+    graphs = []
+    for lib in (rg, F):
+        def softsign(x, lib=lib):
+            return x / (1.0 + lib.abs(x))
+        softsign = lib.custom_vjp(softsign, lambda args, y, ct, lib=lib: (ct / lib.square(1.0 + lib.abs(args[0])),))
+
+        def f(a, b, lib=lib, softsign=softsign):
+            z = lib.matmul(lib.clip(a, -0.5, 0.5), b) + lib.sign(a).sum() * lib.ones_like(lib.transpose(b))[0, 0]
+            w = lib.stack([lib.flip(a, 0), lib.reshape(a, 3, 4)], axis=1)
+            e = lib.expand_dims(lib.broadcast_to(lib.linspace(0.0, 1.0, 4), (3, 4)), -1)
+            return (z * z).mean() + (w * e[:, None, :, 0]).std() + softsign(a).var() + a.sin().sum() + b.cos().sum()
+
+        def step(a, b, lib=lib, f=f):
+            (value, aux), g = lib.value_and_grad(lambda a, b: (f(a, b), a.sum()), argnums=(0, 1), has_aux=True)(a, b)
+            ga = lib.grad(lambda a: f(a, b))(a)
+            y, t = lib.jvp(lambda a: f(a, b), (a,), (lib.ones_like(a),))
+            h = lib.hessian(lambda v: (v * v * v).sum())(b[:, 0])
+            return value, aux, g, ga, y, t, h
+        args = (lib.tensor(a_np), lib.tensor(b_np))
+        graphs.append(capture_graph(oracle, lambda: lib.compile(step, args, validate="basic"))[1])
+    assert graphs[0] == graphs[1]
+
+
+@pytest.mark.reference
+def test_run_chunks_callbacks_and_inspect_match_rgs_front_end(fe, oracle, rg_reference):
+    """Cycled batch lists, an iterator in chunks with a stopping callback, and `inspect` of a run
+    that went non-finite: status, steps, history and the replayed diagnosis equal rg's."""
+    rg = rg_reference
+    rng = np.random.default_rng(8)
+    xs = [rng.normal(size=(16, 4)).astype("float32") for _ in range(3)]
+    ys = [x @ np.arange(4, dtype="float32") for x in xs]
+    results = []
+    for lib in (rg, F):
+        def step(w, batch, lib=lib):
+            value, g = lib.value_and_grad(lambda w: (((batch[0] @ w) - batch[1]) ** 2).mean())(w)
+            return w - 0.05 * g, value
+
+        def blow_up(w, lr, lib=lib):
+            return w * lr, (w * w).sum()
+        batches = [(lib.tensor(x), lib.tensor(y)) for x, y in zip(xs, ys)]
+        c = lib.compile(step, (lib.zeros(4), batches[0]), validate="none")
+        cycled = lib.run(c, lib.zeros(4), batches, steps=10)
+        calls = []
+        stopped = lib.run(c, lib.zeros(4), iter(batches * 5), steps=12, every=4, callback=lambda r: calls.append(r.steps) or r.steps < 8)
+        bad = lib.compile(blow_up, (lib.ones(2), lib.tensor(1e20)), validate="standard")
+        grew = lib.run(bad, lib.ones(2), lib.tensor(1e20), steps=5)
+        report = lib.inspect(grew)
+        results.append(dict(cycled=(cycled.status, cycled.steps, cycled.history, cycled.state.numpy().tolist()),
+                            stopped=(stopped.status, stopped.steps, calls, stopped.history),
+                            grew=(grew.status, grew.nonfinite_step, grew.steps),
+                            report=(report["status"], report.get("repro"), [d["code"] for d in report["diagnostics"]]),
+                            compiled_report=lib.inspect(c)["graph"]))
+    assert results[0] == results[1]
+    assert results[1]["stopped"][0] == "stopped_by_callback"
+    assert results[1]["grew"][0] == "stopped_nonfinite"
