@@ -21,15 +21,13 @@ constexpr double SEARCH_MIN_GAIN = 0.9;
 constexpr size_t SEARCH_ITERATIONS = 6, SEARCH_NODES = 20000;
 constexpr size_t COSTLY_REMAT_ABOVE_BYTES = size_t(2) << 30;
 // The device's own memory policy (no counterpart in rg): rg rematerialises elementwise values in
-// the backward pass to bound the memory of a unified-memory GPU, at the price of recomputing
-// them (8 % more algorithmic bytes in a GPT training step). An HBM device keeps the activations
-// when the plan without rematerialisation peaks at no more than this; recomputation gives the
-// same values, so results do not change.
-constexpr size_t DEVICE_KEEP_ACTIVATIONS_BYTES = size_t(48) << 30;
-// rg also recomputes transcendental values (exp, tanh...) once the plan would peak above 2 GB;
-// the device does so only above this (d512 at batch 512: 1193 instead of 1257 GB of algorithmic
-// traffic per step for a 65 instead of 55 GB peak).
-constexpr size_t DEVICE_COSTLY_REMAT_ABOVE_BYTES = size_t(96) << 30;
+// the backward pass to bound the memory of a unified-memory GPU, choosing them by memory. The
+// device instead recomputes what saves traffic (recompute_in_consumers below) and keeps every
+// other activation while the plan peaks at no more than this share of its 180 GB of HBM (the
+// rest holds the state snapshot, GEMM scratch and control-flow body frames). Above it rg's
+// rematerialisation bounds memory, transcendental values included. Recomputation gives the same
+// values, so results do not change.
+constexpr size_t DEVICE_ACTIVATIONS_BYTES = size_t(120) << 30;
 
 // The value of a constant whose elements are all equal (optimize.rs:45-53).
 std::optional<double> splat(const Graph& g, uint32_t id) {
@@ -130,6 +128,107 @@ std::pair<Graph, std::vector<uint32_t>> rematerialize(const Graph& g, const std:
   std::vector<int64_t> clone(N, -1);
   std::function<uint32_t(uint32_t)> value = [&](uint32_t i) -> uint32_t {
     if (!remat[i]) return map[i];
+    if (clone[i] >= 0) return (uint32_t)clone[i];
+    const Node& n = g.nodes[i];
+    std::vector<uint32_t> ins;
+    for (auto x : n.inputs) ins.push_back(value(x));
+    h.cur_source = n.source;
+    uint32_t id = h.add(n.op, ins);
+    clone[i] = id;
+    st.rematerialized += 1;
+    return id;
+  };
+  for (size_t i = 0; i < N; ++i) {
+    const Node& n = g.nodes[i];
+    if (n.op.kind == OpKind::Input) {
+      h.cur_source = n.source;
+      map[i] = h.input(n.shape, n.dtype);
+      h.nodes[map[i]].op = n.op;
+      continue;
+    }
+    if (!keep[i]) continue;
+    std::vector<uint32_t> ins;
+    for (auto x : n.inputs) ins.push_back(backward[i] ? value(x) : map[x]);
+    h.cur_source = n.source;
+    map[i] = n.op.kind == OpKind::Const ? h.constant(n.op.value) : h.add(n.op, ins);
+  }
+  std::vector<uint32_t> out;
+  for (auto o : outputs) out.push_back(map[o]);
+  return {std::move(h), std::move(out)};
+}
+
+// The device's own rematerialisation (no counterpart in rg): an elementwise forward value that
+// only elementwise consumers of its shape read is recomputed by its backward consumers when the
+// values it derives from include at most one full-size tensor that is stored anyway (a product's
+// output, a reduction's input, a value another kind of step reads). The clones run inside the
+// backward group that reads them (adjacent to it in graph order, or moved to its level by
+// Fuse::sink), so the forward group no longer writes the value and the backward group reads the
+// stored source instead: the GELU of an MLP block then writes only its output, and its backward
+// reads the product h = x W + b instead of six intermediates. Clones are the same operations
+// on the same inputs, so every value is unchanged. rg's own rematerialisation (above) chooses
+// what to recompute to bound memory and recomputes values that are stored anyway.
+std::pair<Graph, std::vector<uint32_t>> recompute_in_consumers(const Graph& g, const std::vector<uint32_t>& outputs,
+                                                               const std::vector<bool>& backward, OptStats& st) {
+  const size_t N = g.nodes.size();
+  auto keep = g.reachable(outputs);
+  auto elementwise = [&](size_t i) {
+    const Node& n = g.nodes[i];
+    return keep[i] && !is_leaf(n) && n.dtype != DType::I32 &&
+           (n.op.is_unary_elementwise() || n.op.is_binary_elementwise() || n.op.kind == OpKind::Where);
+  };
+  std::vector<std::vector<size_t>> users(N);
+  for (size_t i = 0; i < N; ++i)
+    if (keep[i] && !is_leaf(g.nodes[i]))
+      for (auto x : g.nodes[i].inputs) users[x].push_back(i);
+  std::vector<bool> output(N, false);
+  for (auto o : outputs) output[o] = true;
+  // Stored anyway: anything but an elementwise node, an output, or a value some step other than an
+  // elementwise node of its shape and dtype reads.
+  std::vector<bool> stored(N, false);
+  for (size_t i = 0; i < N; ++i) {
+    if (!keep[i]) continue;
+    bool s = !elementwise(i) || output[i];
+    for (size_t u : users[i])
+      s = s || !elementwise(u) || g.nodes[u].shape != g.nodes[i].shape || g.nodes[u].dtype != g.nodes[i].dtype;
+    stored[i] = s;
+  }
+  auto full = [&](size_t x, size_t like) { return g.nodes[x].shape == g.nodes[like].shape && g.nodes[x].n() >= REMAT_MIN; };
+  // The forward values a recomputation of `i` goes through (`i` and its unstored elementwise
+  // ancestors of its shape) and the full-size stored values it starts from.
+  constexpr size_t MAX_CHAIN = 48;
+  std::vector<bool> recompute(N, false);
+  for (size_t i = 0; i < N; ++i) {
+    if (!keep[i] || backward[i] || stored[i] || !elementwise(i) || !full(i, i)) continue;
+    bool read_by_backward = false;
+    for (size_t u : users[i]) read_by_backward = read_by_backward || backward[u];
+    if (!read_by_backward) continue;
+    std::vector<size_t> chain, todo{i}, sources;
+    std::vector<bool> seen_here;
+    bool ok = true;
+    while (!todo.empty() && ok) {
+      size_t v = todo.back();
+      todo.pop_back();
+      if (std::find(chain.begin(), chain.end(), v) != chain.end()) continue;
+      chain.push_back(v);
+      ok = chain.size() <= MAX_CHAIN;
+      for (auto x : g.nodes[v].inputs) {
+        bool through = !backward[x] && !stored[x] && elementwise(x) && full(x, i);
+        if (through) todo.push_back(x);
+        else if (full(x, i) && std::find(sources.begin(), sources.end(), (size_t)x) == sources.end()) sources.push_back(x);
+      }
+    }
+    recompute[i] = ok && sources.size() <= 1;
+  }
+  // Every forward value a recomputed one goes through is recomputed with it.
+  for (size_t i = N; i-- > 0;)
+    if (recompute[i])
+      for (auto x : g.nodes[i].inputs)
+        if (!backward[x] && !stored[x] && elementwise(x) && full(x, i)) recompute[x] = true;
+  Graph h;
+  std::vector<uint32_t> map(N, UINT32_MAX);
+  std::vector<int64_t> clone(N, -1);
+  std::function<uint32_t(uint32_t)> value = [&](uint32_t i) -> uint32_t {
+    if (!recompute[i]) return map[i];
     if (clone[i] >= 0) return (uint32_t)clone[i];
     const Node& n = g.nodes[i];
     std::vector<uint32_t> ins;
@@ -518,9 +617,10 @@ Simplified simplify(const Graph& g, const std::vector<uint32_t>& outputs, bool f
   return r;
 }
 
-// `gpu`: planning for the device, whose plans keep every activation (no rematerialisation) while
-// that plan's peak live bytes stay within DEVICE_KEEP_ACTIVATIONS_BYTES; above it rg's policy,
-// escalating to transcendental values only above DEVICE_COSTLY_REMAT_ABOVE_BYTES.
+// `gpu`: planning for the device, which recomputes forward values inside the backward groups
+// that read them (recompute_in_consumers) and keeps every other activation while the peak live
+// bytes stay within DEVICE_ACTIVATIONS_BYTES; above it rg's policy, escalating to transcendental
+// values when that plan still peaks above the same bound.
 
 // Rebuilds the graph with every matched attention replaced (see match_attention).
 Simplified fuse_attention(const Simplified& in) {
@@ -625,12 +725,16 @@ Simplified fuse_attention(const Simplified& in) {
 }
 
 OptResult finish(const Graph& ng, const std::vector<uint32_t>& out, const std::vector<bool>& backward, OptStats st, bool gpu = false) {
-  if (gpu && Plan::build(ng, out, true).peak_live_bytes <= DEVICE_KEEP_ACTIVATIONS_BYTES) {
-    st.nodes_after = count_kept(ng, out);
-    return OptResult{ng, out, st};
+  if (gpu) {
+    OptStats rs = st;
+    auto rc = recompute_in_consumers(ng, out, backward, rs);
+    if (Plan::build(rc.first, rc.second, true).peak_live_bytes <= DEVICE_ACTIVATIONS_BYTES) {
+      rs.nodes_after = count_kept(rc.first, rc.second);
+      return OptResult{std::move(rc.first), std::move(rc.second), rs};
+    }
   }
   auto hr = rematerialize(ng, out, backward, REMAT_MIN, false, st);
-  if (Plan::build(hr.first, hr.second, true).peak_live_bytes > (gpu ? DEVICE_COSTLY_REMAT_ABOVE_BYTES : COSTLY_REMAT_ABOVE_BYTES)) {
+  if (Plan::build(hr.first, hr.second, true).peak_live_bytes > (gpu ? DEVICE_ACTIVATIONS_BYTES : COSTLY_REMAT_ABOVE_BYTES)) {
     st.rematerialized = 0;
     hr = rematerialize(ng, out, backward, REMAT_MIN, true, st);
   }

@@ -268,6 +268,29 @@ std::vector<Item> schedule_levels(const Graph& g, const std::vector<bool>& keep,
       }
     }
     level[i] = (is_alias(g, i) || joins) ? deepest : deepest + 1;
+  }
+  if (cfg.sink) {
+    // Consumers first (reverse graph order), so that a chain of such nodes follows its last link.
+    // The new level is above every input's, so the node's inputs are still computed before it.
+    std::vector<std::vector<size_t>> users(g.nodes.size());
+    for (size_t i = 0; i < g.nodes.size(); ++i)
+      if (keep[i] && !up[i] && !is_leaf(g.nodes[i]))
+        for (auto x : g.nodes[i].inputs) users[x].push_back(i);
+    for (size_t i = g.nodes.size(); i-- > 0;) {
+      const Node& n = g.nodes[i];
+      if (!keep[i] || up[i] || is_leaf(n) || is_alias(g, i) || !gpu_fusable(i) || users[i].empty()) continue;
+      size_t first = SIZE_MAX;
+      bool all = true;
+      for (size_t u : users[i]) {
+        const Node& c = g.nodes[u];
+        all = all && !is_alias(g, u) && gpu_fusable(u) && c.shape == n.shape && c.dtype == n.dtype;
+        first = std::min(first, level[u]);
+      }
+      if (all && first > level[i]) level[i] = first;
+    }
+  }
+  for (size_t i = 0; i < g.nodes.size(); ++i) {
+    if (!keep[i] || up[i] || is_leaf(g.nodes[i])) continue;
     if (by_level.size() <= level[i]) by_level.resize(level[i] + 1);
     by_level[level[i]].push_back(i);
   }

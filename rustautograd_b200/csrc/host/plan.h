@@ -26,15 +26,20 @@ struct Fuse {
   // that a scalar chain (an optimizer's step count and bias corrections) does not push the
   // tensor ops that read it into a later dependency level and split their fusion group.
   bool hoist_small = false;
+  // Level order only: an elementwise node whose every consumer is an elementwise node of its
+  // shape and dtype moves up to the level of its first consumer, so that it runs inside that
+  // consumer's group. A value recomputed for the backward pass (a rematerialisation clone) then
+  // fuses into the backward group that reads it instead of being written by the forward group.
+  bool sink = false;
 
-  static Fuse DEFAULT() { return Fuse{200000.0, false, false, false, 28, false}; }
-  static Fuse METAL() { return Fuse{0.0, true, true, true, 28, false}; }
+  static Fuse DEFAULT() { return Fuse{200000.0, false, false, false, 28, false, false}; }
+  static Fuse METAL() { return Fuse{0.0, true, true, true, 28, false, false}; }
   // The CUDA device's configuration: groups of any cost, in dependency-level order when that
   // is cheaper, with up to 64 bindings per kernel (kernel parameters, not a binding table).
-  static Fuse CUDA() { return Fuse{0.0, true, true, false, 64, true}; }
+  static Fuse CUDA() { return Fuse{0.0, true, true, false, 64, true, true}; }
   std::string key() const {
     return std::to_string(parallel_ns) + (gpu ? "g" : "c") + (levels ? "l" : "n") + (hoist ? "h" : "x") + std::to_string(max_bindings) +
-           (hoist_small ? "s" : "");
+           (hoist_small ? "s" : "") + (sink ? "k" : "");
   }
 };
 

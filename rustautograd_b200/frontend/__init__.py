@@ -1,5 +1,5 @@
 """Python front end tracing rg programs onto an engine module with rg's `_rg` interface."""
-from . import checkpoint, gpt, nn, optim, random
+from . import checkpoint, gpt, nn, optim, random, tree
 from .core import (Compiled, DiagnosticError, Report, RunResult, Tensor, Tracer, abs, all_reduce, arange, argmax, argsort, broadcast_to, clip,
                    compile, concatenate, cond, cos, cumsum, custom_vjp, devices, equal, exp, expand_dims, eye, flatten, flip, floor, full,
                    grad, hessian, inspect, jvp, linspace, log, matmul, maximum, minimum, native, not_equal, ones, ones_like, op, reshape, run,

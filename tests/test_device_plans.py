@@ -164,16 +164,40 @@ def test_matrix_chain_plan_matches_rgs_plan():
         assert float(np.abs(u.astype(np.float64) - v).max()) / scale <= 1e-4, f"output {k}"
 
 
-def test_device_plans_keep_activations_within_the_memory_budget():
-    """rg rematerialises elementwise values for the backward pass (here 20 of them); the device's
-    plan of the same step keeps them (its peak is far below the 48 GB budget) with outputs
-    unchanged bit for bit."""
+def test_device_plans_recompute_forward_values_inside_their_backward_consumers():
+    """rg rematerialises values to bound memory; the device recomputes a forward elementwise value
+    inside the backward group that reads it when that needs at most one stored full-size source.
+    The GELU of the MLP block then writes only its output (one output, where the plan that keeps
+    activations writes seven) and its backward group reads the product h and the incoming gradient
+    instead of the intermediates. Every output is unchanged bit for bit."""
     model = F.gpt.GPT(vocab=32, block=32, d=64, heads=4, layers=1)
     params = model.init(F.random.key(0))
     opt = F.optim.adamw(1e-3, weight_decay=0.01)
     state = {"params": params, "opt": opt.init(params), "key": F.random.key(1)}
     tokens = F.tensor(np.random.default_rng(0).integers(0, 32, size=2000, dtype="int32"))
     out = run_both(F.gpt.make_train_step(model, opt, 16), (state, tokens))
-    assert out["cpu"][1].report["graph"]["optimization"]["rematerialized"] > 0
-    assert out["cuda-plan"][1].report["graph"]["optimization"]["rematerialized"] == 0
+    assert_same(out["cpu"][0], out["cuda-plan"][0])
+    assert out["cuda-plan"][1].report["graph"]["optimization"]["rematerialized"] > 0
+    hidden = 16 * 32 * 4 * 64
+    gelu = [p for p in json.loads(out["cuda-plan"][1]._n.plan_summary()) if "tanh" in p.get("fused", "") and p.get("n") == hidden]
+    assert len(gelu) == 2, "one forward and one backward group"
+    forward, backward = gelu
+    assert len(forward["out"]) == 1, "the forward group writes only the activation"
+    assert len(backward["out"]) == 1
+    assert len(backward["fused"].split(",")) > len(forward["fused"].split(",")), "the backward group recomputes the forward chain"
+    produced = set(forward["out"])
+    assert not produced & set(backward["in"]), "the backward group does not read the forward group's output"
+
+
+def test_recomputation_reads_stored_values_only():
+    """A forward value with two full-size stored sources stays stored (recomputing it would read
+    two tensors to save one), and values read by other kinds of steps are never recomputed."""
+    rng = np.random.default_rng(9)
+    a, b = (F.tensor(rng.normal(size=(64, 64)).astype("float32")) for _ in range(2))
+
+    def loss(a, b):
+        u = (a @ b).tanh()          # one stored source: recomputable
+        v = (a @ b.T) * (b @ a)     # two stored sources: stays stored
+        return (u * u).sum() + (v * v).sum()
+    out = run_both(F.value_and_grad(loss, argnums=(0, 1)), (a, b))
     assert_same(out["cpu"][0], out["cuda-plan"][0])
