@@ -2,6 +2,7 @@
 // checker and the timed CPU baseline. Each kernel cites the arm of src/plan.rs it follows.
 // Built with -ffp-contract=off: rg (Rust) never fuses a multiply and an add, so neither may we.
 #include "interp.h"
+#include "../rustautograd_b200/csrc/host/rowchain.h"
 
 #include <algorithm>
 #include <array>
@@ -9,6 +10,7 @@
 #include <chrono>
 #include <cmath>
 #include <limits>
+#include <map>
 #include <condition_variable>
 #include <cstring>
 #include <functional>
@@ -1087,15 +1089,61 @@ std::vector<Buf> frame(const Plan& plan) {
   return slots;
 }
 
+namespace {
+
+void exec_step(const Step& st, std::vector<Buf>& slots) {
+  if (st.fused) {
+    if (st.group.dtype == DType::F32) run_fused<float>(st.group, slots);
+    else if (st.group.dtype == DType::F64) run_fused<double>(st.group, slots);
+    else throw std::logic_error("integer ops are never fused");
+  } else {
+    exec_instr(st.instr, slots);
+  }
+}
+
+// A row chain as the CUDA device runs it (rowchain.h): the steps moved before it, then its
+// members with the broadcasts moved after it in plan order, which computes what the chain
+// computes. The device writes only the values the chain stores; every other slot the chain
+// writes keeps whatever it held, which no later step may read. This interpreter fills those
+// slots with NaN instead, so that a chain whose stored values were chosen wrongly changes the
+// results of the tests that run its plans here.
+void exec_chain(const Plan& plan, const RowChain& c, std::vector<Buf>& slots) {
+  for (size_t p : c.before) exec_step(plan.steps[p], slots);
+  std::vector<size_t> order = c.members;
+  order.insert(order.end(), c.after.begin(), c.after.end());
+  std::sort(order.begin(), order.end());
+  for (size_t p : order) exec_step(plan.steps[p], slots);
+  std::map<size_t, bool> keep;  // slot -> its final write in the range is kept
+  for (size_t p : order) {
+    auto m = std::find(c.members.begin(), c.members.end(), p);
+    auto writes = step_writes(plan.steps[p]);
+    for (size_t q = 0; q < writes.size(); ++q)
+      keep[writes[q]] = m == c.members.end() || c.store[(size_t)(m - c.members.begin())][q];
+  }
+  for (auto& [slot, kept] : keep) {
+    if (kept) continue;
+    Buf& b = slots[slot];
+    if (b.dtype == DType::F32) std::fill(b.f32(), b.f32() + b.n, std::numeric_limits<float>::quiet_NaN());
+    else if (b.dtype == DType::F64) std::fill(b.f64(), b.f64() + b.n, std::numeric_limits<double>::quiet_NaN());
+  }
+}
+
+}  // namespace
+
 void exec_plan(const Plan& plan, std::vector<Buf>& slots) {
-  for (const Step& st : plan.steps) {
-    if (st.fused) {
-      if (st.group.dtype == DType::F32) run_fused<float>(st.group, slots);
-      else if (st.group.dtype == DType::F64) run_fused<double>(st.group, slots);
-      else throw std::logic_error("integer ops are never fused");
-    } else {
-      exec_instr(st.instr, slots);
+  // Plans built with the CUDA device's fusion configuration run their row chains as the device
+  // does.
+  std::vector<RowChain> chains = find_row_chains(plan);
+  size_t next = 0;
+  for (size_t k = 0; k < plan.steps.size();) {
+    if (next < chains.size() && chains[next].first == k) {
+      exec_chain(plan, chains[next], slots);
+      k = chains[next].last + 1;
+      ++next;
+      continue;
     }
+    exec_step(plan.steps[k], slots);
+    ++k;
   }
 }
 

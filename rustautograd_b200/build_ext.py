@@ -23,7 +23,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-HOST_SOURCES = ["graph.cpp", "plan.cpp", "optimize.cpp", "egraph.cpp", "autodiff.cpp", "run.cpp", "validate.cpp", "blob.cpp"]
+HOST_SOURCES = ["graph.cpp", "plan.cpp", "optimize.cpp", "egraph.cpp", "autodiff.cpp", "run.cpp", "validate.cpp", "blob.cpp", "rowchain.cpp"]
 
 
 def _ext_suffix():

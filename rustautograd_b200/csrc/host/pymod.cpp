@@ -8,6 +8,7 @@
 
 #include "autodiff.h"
 #include "blob.h"
+#include "rowchain.h"
 #include "validate.h"
 
 namespace py = pybind11;
@@ -518,6 +519,34 @@ PYBIND11_MODULE(RG_MODULE_NAME, m) {
         std::vector<std::tuple<std::string, double, double>> out;
         for (auto& c : step_costs(self.c->plan)) out.emplace_back(c.kind, c.flops, c.bytes);
         return out;
+      })
+      // Not in rg's module: the row chains the CUDA device forms for this plan (RGC_ROW_CHAINS=1).
+      .def("row_chains", [](const PyCompiled& self) {
+        Json a = Json::array();
+        for (auto& c : find_row_chains(self.c->plan)) {
+          Json j = Json::object();
+          auto list = [](const std::vector<size_t>& v) {
+            Json x = Json::array();
+            for (size_t e : v) x.push(Json((double)e));
+            return x;
+          };
+          j["first"] = Json((double)c.first);
+          j["last"] = Json((double)c.last);
+          j["members"] = list(c.members);
+          j["before"] = list(c.before);
+          j["after"] = list(c.after);
+          j["rows"] = Json((double)c.rows);
+          j["cols"] = Json((double)c.cols);
+          Json st = Json::array();
+          for (auto& f : c.store) {
+            Json x = Json::array();
+            for (bool b : f) x.push(Json(b));
+            st.push(x);
+          }
+          j["store"] = st;
+          a.push(j);
+        }
+        return a.dump();
       })
       .def("plan_summary", [](const PyCompiled& self) {
         Json a = Json::array();
