@@ -1130,6 +1130,10 @@ void exec_chain(const Plan& plan, const RowChain& c, std::vector<Buf>& slots) {
 
 }  // namespace
 
+void exec_steps(const Plan& plan, const std::vector<size_t>& steps, std::vector<Buf>& slots) {
+  for (size_t k : steps) exec_step(plan.steps.at(k), slots);
+}
+
 void exec_plan(const Plan& plan, std::vector<Buf>& slots) {
   // Plans built with the CUDA device's fusion configuration run their row chains as the device
   // does.

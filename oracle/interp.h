@@ -23,6 +23,8 @@ int threads();
 void exec_plan(const Plan& plan, std::vector<Buf>& slots);
 // Fresh frame with constants loaded (plan.rs:641-647).
 std::vector<Buf> frame(const Plan& plan);
+// The given plan steps, in the given order, each as the interpreter runs it alone.
+void exec_steps(const Plan& plan, const std::vector<size_t>& steps, std::vector<Buf>& slots);
 
 // The CPU device: plans run in this interpreter.
 std::shared_ptr<Device> cpu_device();

@@ -78,6 +78,29 @@ void module_extra(py::module_& m) {
     for (auto& t : out) res.append(py::make_tuple(py::bytes((const char*)t.data.data(), t.data.bytes()), t.shape, std::string(dtype_name(t.dtype()))));
     return res;
   });
+  // Every slot of a plan blob's frame after loading `inputs` and running the plan steps listed in
+  // `steps`, in that order: (bytes, dtype) per slot. Tests run a device kernel that stands for
+  // some steps from the slots before them and compare with the slots after them.
+  m.def("plan_blob_slots", [](py::bytes blob, std::vector<std::tuple<py::bytes, std::vector<size_t>, std::string>> inputs,
+                              std::vector<size_t> steps) {
+    std::string_view b = blob;
+    Plan p = decode_plan((const uint8_t*)b.data(), b.size());
+    if (inputs.size() != p.input_slots.size()) throw py::value_error("wrong number of inputs for this plan");
+    auto slots = oracle::frame(p);
+    for (size_t k = 0; k < inputs.size(); ++k) {
+      std::string_view v = std::get<0>(inputs[k]);
+      Buf& dst = slots[p.input_slots[k]];
+      if (v.size() > dst.bytes()) throw py::value_error("input larger than its slot");
+      std::memcpy(dst.data(), v.data(), v.size());
+    }
+    {
+      py::gil_scoped_release nogil;
+      oracle::exec_steps(p, steps, slots);
+    }
+    py::list res;
+    for (auto& s : slots) res.append(py::make_tuple(py::bytes((const char*)s.data(), s.bytes()), std::string(dtype_name(s.dtype))));
+    return res;
+  });
   // Multi-step run of a plan blob on the CPU with rg's run-loop semantics, for history parity.
   m.def("run_plan_blob_steps", [](py::bytes blob, std::vector<std::pair<size_t, size_t>> state_map, std::vector<size_t> data_inputs,
                                   std::vector<size_t> history, std::vector<std::tuple<py::bytes, std::vector<size_t>, std::string>> inputs, size_t steps) {

@@ -35,6 +35,7 @@ const Driver& Driver::get() {
     load("cuLaunchKernel", (void**)&x.LaunchKernel);
     load("cuOccupancyMaxActiveBlocksPerMultiprocessor", (void**)&x.OccupancyMaxActiveBlocksPerMultiprocessor);
     load("cuLaunchKernelEx", (void**)&x.LaunchKernelEx);
+    load("cuFuncSetAttribute", (void**)&x.FuncSetAttribute);
     return x;
   }();
   return d;
@@ -175,6 +176,9 @@ std::string expr(DType d, const rg::Op& op, const std::vector<std::string>& a) {
 }
 
 }  // namespace
+
+std::string elem_expr(DType d, const rg::Op& op, const std::vector<std::string>& args) { return expr(d, op, args); }
+std::string elem_ctype(DType d) { return ctype(d); }
 
 std::string ElemSpec::source_key() const {
   std::string k = "d" + std::to_string((int)dtype) + "|";
@@ -408,8 +412,40 @@ std::string Jit::add(const ElemSpec& s) {
   std::string key = s.source_key();
   char name[64];
   snprintf(name, sizeof name, "rg_elem_%016llx", (unsigned long long)fnv1a(key));
-  if (!built_.count(name) && !pending_.count(name)) pending_[name] = kernel_source(s, name);
+  if (!built_.count(name) && !pending_.count(name)) {
+    pending_[name] = kernel_source(s, name);
+    functions_[name] = {name, std::string(name) + "_w"};
+  }
   return name;
+}
+
+void Jit::add_source(const std::string& name, const std::string& source) {
+  if (built_.count(name) || pending_.count(name)) return;
+  pending_[name] = source;
+  functions_[name] = {name};
+}
+
+static const char* const NVRTC_OPTS[] = {"--gpu-architecture=sm_100a", "--fmad=false", "--prec-div=true", "--prec-sqrt=true", "--ftz=false",
+                                         "-default-device", "--std=c++17"};
+
+std::string Jit::prelude() { return PRELUDE; }
+
+std::string Jit::compile_check(const std::vector<std::string>& sources) {
+  std::string src = PRELUDE;
+  for (auto& s : sources) src += s;
+  nvrtcProgram prog;
+  if (nvrtcCreateProgram(&prog, src.c_str(), "rg_check.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS) return "nvrtcCreateProgram failed";
+  nvrtcResult r = nvrtcCompileProgram(prog, (int)(sizeof NVRTC_OPTS / sizeof NVRTC_OPTS[0]), NVRTC_OPTS);
+  std::string log;
+  if (r != NVRTC_SUCCESS) {
+    size_t n = 0;
+    nvrtcGetProgramLogSize(prog, &n);
+    log.assign(n, '\0');
+    nvrtcGetProgramLog(prog, log.data());
+    if (log.empty()) log = "NVRTC compilation failed";
+  }
+  nvrtcDestroyProgram(&prog);
+  return log;
 }
 
 static std::string cache_dir() {
@@ -427,8 +463,7 @@ void Jit::build() {
     src += s;
     names.push_back(name);
   }
-  const char* opts[] = {"--gpu-architecture=sm_100a", "--fmad=false", "--prec-div=true", "--prec-sqrt=true", "--ftz=false", "-default-device",
-                        "--std=c++17"};
+  const char* const* opts = NVRTC_OPTS;
   std::string path = cache_dir() + "/" + std::to_string(fnv1a(src + "v6")) + ".cubin";
   std::vector<char> cubin;
   {
@@ -438,7 +473,7 @@ void Jit::build() {
   if (cubin.empty()) {
     nvrtcProgram prog;
     if (nvrtcCreateProgram(&prog, src.c_str(), "rg_fused.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS) throw std::runtime_error("nvrtcCreateProgram failed");
-    nvrtcResult r = nvrtcCompileProgram(prog, (int)(sizeof opts / sizeof opts[0]), opts);
+    nvrtcResult r = nvrtcCompileProgram(prog, (int)(sizeof NVRTC_OPTS / sizeof NVRTC_OPTS[0]), opts);
     if (r != NVRTC_SUCCESS) {
       size_t n = 0;
       nvrtcGetProgramLogSize(prog, &n);
@@ -464,12 +499,55 @@ void Jit::build() {
   if (lr != CUDA_SUCCESS) throw std::runtime_error("loading the fused-kernel module failed (CUresult " + std::to_string((int)lr) + ")");
   modules_.push_back(mod);
   for (auto& name : names)
-    for (const std::string& fname : {name, name + "_w"}) {
+    for (const std::string& fname : functions_[name]) {
       CUfunction fn;
       if (d.ModuleGetFunction(&fn, mod, fname.c_str()) != CUDA_SUCCESS) throw std::runtime_error("missing fused kernel " + fname);
       built_[fname] = fn;
     }
   pending_.clear();
+}
+
+void Jit::launch_rows(CUfunction f, const ElemArgs& a, long long blocks, size_t smem, cudaStream_t s) {
+  static int sms = [] {
+    int dev = 0, v = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    return v;
+  }();
+  static std::mutex mu;
+  static std::unordered_map<CUfunction, int> resident;
+  int per_sm = 0;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = resident.find(f);
+    if (it != resident.end()) {
+      per_sm = it->second;
+    } else {
+      const Driver& d = Driver::get();
+      if (d.FuncSetAttribute(f, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem) != CUDA_SUCCESS)
+        throw std::runtime_error("row-chain kernel: shared memory request refused");
+      if (d.OccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, f, 256, smem) != CUDA_SUCCESS || per_sm <= 0) per_sm = 1;
+      resident[f] = per_sm;
+    }
+  }
+  long long cap = (long long)sms * per_sm;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  void* params[] = {(void*)&a};
+  CUlaunchConfig cfg = {};
+  cfg.gridDimX = (unsigned)blocks;
+  cfg.gridDimY = cfg.gridDimZ = 1;
+  cfg.blockDimX = 256;
+  cfg.blockDimY = cfg.blockDimZ = 1;
+  cfg.sharedMemBytes = (unsigned)smem;
+  cfg.hStream = (CUstream)s;
+  CUlaunchAttribute attr[1];
+  attr[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+  attr[0].value.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  CUresult r = Driver::get().LaunchKernelEx(&cfg, f, params, nullptr);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("row-chain kernel launch failed (CUresult " + std::to_string((int)r) + ")");
 }
 
 CUfunction Jit::function(const std::string& name) const {

@@ -61,6 +61,11 @@ struct ElemSpec {
 // The output's last extent when `in` is the output's shape with a last extent of 1, else 0.
 size_t column_of(const std::vector<size_t>& in, const std::vector<size_t>& out);
 
+// One micro-op as a C expression over operand expressions, and the C type of a dtype: what every
+// generated kernel evaluates per element.
+std::string elem_expr(rg::DType d, const rg::Op& op, const std::vector<std::string>& args);
+std::string elem_ctype(rg::DType d);
+
 // Builds an ElemSpec from a fused group or from a single elementwise instruction.
 ElemSpec spec_from_group(const rg::Fused& f);
 ElemSpec spec_from_instr(const rg::Instr& i);
@@ -69,13 +74,24 @@ class Jit {
  public:
   // Registers a kernel; returns its name. Nothing compiles until `build`.
   std::string add(const ElemSpec& s);
+  // Registers a generated kernel given as source (one function `name`, ElemArgs parameter).
+  void add_source(const std::string& name, const std::string& source);
+  // Compiles `sources` with the prelude for sm_100a without loading them (no GPU needed): an
+  // empty string, or the compiler's log.
+  static std::string compile_check(const std::vector<std::string>& sources);
+  // The definitions every generated kernel is compiled with (types, index helpers, rg_div...).
+  static std::string prelude();
   // Compiles every registered kernel not yet built (one NVRTC program) and loads it.
   void build();
   CUfunction function(const std::string& name) const;
   static void launch(CUfunction f, const ElemArgs& a, long long n, int vec_width, cudaStream_t s);
+  // A row-chain kernel: `blocks` blocks of 256 threads at most (capped at one wave), `smem` bytes
+  // of dynamic shared memory each.
+  static void launch_rows(CUfunction f, const ElemArgs& a, long long blocks, size_t smem, cudaStream_t s);
 
  private:
   std::unordered_map<std::string, std::string> pending_;  // name -> source
+  std::unordered_map<std::string, std::vector<std::string>> functions_;  // name -> functions it defines
   std::unordered_map<std::string, CUfunction> built_;
   std::vector<CUmodule> modules_;
 };
@@ -88,6 +104,7 @@ struct Driver {
   CUresult (*LaunchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, CUstream, void**, void**) = nullptr;
   CUresult (*OccupancyMaxActiveBlocksPerMultiprocessor)(int*, CUfunction, int, size_t) = nullptr;
   CUresult (*LaunchKernelEx)(const CUlaunchConfig*, CUfunction, void**, void**) = nullptr;
+  CUresult (*FuncSetAttribute)(CUfunction, CUfunction_attribute, int) = nullptr;
   static const Driver& get();
 };
 

@@ -29,6 +29,7 @@
 #include "jit.h"
 #include "kernels.cuh"
 #include "rgc.h"
+#include "rowkernel.h"
 
 using rg::DType;
 using rg::Instr;
@@ -403,6 +404,45 @@ struct Builder {
     };
     if (in_slots.size() > (size_t)JIT_MAX_IN || out_slots.size() > (size_t)JIT_MAX_OUT)
       throw std::runtime_error("fused group has too many operands for one kernel");
+    return l;
+  }
+
+  // A row chain as one generated kernel (rowkernel.h).
+  Lowered rows(const RowKernel& rk) {
+    {
+      std::lock_guard<std::mutex> lk(jit_mu());
+      jit().add_source(rk.name, rk.source);
+    }
+    size_t bc0 = bcs.size();
+    for (auto& f : rk.bcs) {
+      bcs.push_back(f);
+      bcs64.push_back(Dims{});  // kept index-aligned with bcs; row kernels use the 32-bit form only
+    }
+    Program* prog = p;
+    auto fn = std::make_shared<CUfunction>(nullptr);
+    const std::string name = rk.name;
+    const auto ins = rk.in_slots, outs = rk.out_slots;
+    const auto divs = rk.in_div;
+    const long long rows = rk.rows, blocks = (rk.rows + rk.rows_per_block - 1) / rk.rows_per_block;
+    const size_t smem = rk.smem;
+    Lowered l;
+    l.run = [=](Ctx& c) {
+      if (!*fn) {
+        std::lock_guard<std::mutex> lk(jit_mu());
+        *fn = jit().function(name);
+      }
+      ElemArgs a;
+      std::memset(&a, 0, sizeof a);
+      a.n = rows;
+      for (size_t k = 0; k < ins.size(); ++k) {
+        a.in[k] = c.f->ptr[ins[k]];
+        a.row[k] = divs[k];
+      }
+      for (size_t q = 0; q < outs.size(); ++q) a.out[q] = c.f->ptr[outs[q]];
+      a.bc = prog->bc_dev + bc0;
+      a.bc64 = prog->bc64_dev + bc0;
+      if (rows > 0) Jit::launch_rows(*fn, a, blocks, smem, c.s);
+    };
     return l;
   }
 
@@ -990,8 +1030,74 @@ std::unique_ptr<Program> make_program(const Plan& plan, int device) {
     for (auto& in : spec.inputs)
       if (in.kind == rg::ArgKind::Broadcast || in.via) in.bc = nbc++;
   };
+  // One step that is neither an all-reduce nor part of a row chain.
+  auto lower_one = [&](size_t k) -> Lowered {
+    const auto& st = plan.steps[k];
+    if (st.fused) {
+      std::vector<size_t> ins, outs;
+      for (auto& in : st.group.inputs) ins.push_back(in.slot);
+      for (auto& o : st.group.outputs) outs.push_back(o.second);
+      ElemSpec spec = spec_from_group(st.group);
+      read_broadcast_sources(spec, ins);
+      return b.elementwise(spec, ins, outs);
+    }
+    if (st.instr.op.is_unary_elementwise() || st.instr.op.is_binary_elementwise() || st.instr.op.kind == OpKind::Where) {
+      std::vector<size_t> ins = st.instr.args;
+      ElemSpec spec = spec_from_instr(st.instr);
+      read_broadcast_sources(spec, ins);
+      return b.elementwise(spec, ins, {st.instr.dst});
+    }
+    return b.lower(st.instr);
+  };
+  const std::vector<rg::RowChain> chains = rg::find_row_chains(plan, true);
+  size_t next_chain = 0;
   for (size_t k = 0; k < plan.steps.size(); ++k) {
     const auto& st = plan.steps[k];
+    if (next_chain < chains.size() && chains[next_chain].first == k) {
+      const rg::RowChain& c = chains[next_chain++];
+      RowKernel rk;
+      std::string why;
+      if (make_row_kernel(plan, c, &rk, &why)) {
+        // The steps of the range in plan order (so that broadcast sources resolve as they would
+        // step by step): the ones that run before the chain, the chain, the ones that run after.
+        std::vector<Lowered> pre, post;
+        for (size_t q = c.first; q <= c.last; ++q) {
+          if (std::find(c.before.begin(), c.before.end(), q) != c.before.end()) pre.push_back(lower_one(q));
+          else if (std::find(c.after.begin(), c.after.end(), q) != c.after.end()) post.push_back(lower_one(q));
+          note_writes(q);
+        }
+        Lowered chain = b.rows(rk);
+        Lowered all;
+        all.kernels = chain.kernels;
+        all.capturable = true;
+        std::vector<std::function<void(Frame*, cudaStream_t)>> preps;
+        for (auto* part : {&pre, &post})
+          for (auto& l : *part) {
+            all.kernels += l.kernels;
+            all.capturable = all.capturable && l.capturable;
+            if (l.prepare) preps.push_back(l.prepare);
+          }
+        all.run = [pre, chain, post](Ctx& cx) {
+          for (auto& l : pre) l.run(cx);
+          chain.run(cx);
+          for (auto& l : post) l.run(cx);
+        };
+        if (!preps.empty())
+          all.prepare = [preps](Frame* f, cudaStream_t s) {
+            for (auto& pf : preps) pf(f, s);
+          };
+        p->steps.push_back(std::move(all));
+        // The chain stands for every step of its range: keep step indices aligned.
+        for (size_t q = c.first + 1; q <= c.last; ++q) {
+          Lowered empty;
+          empty.kernels = 0;
+          empty.run = [](Ctx&) {};
+          p->steps.push_back(std::move(empty));
+        }
+        k = c.last;
+        continue;
+      }
+    }
     if (!st.fused && st.instr.op.kind == OpKind::AllReduce) {
       // Consecutive all-reduces (a model's gradients) go to NCCL as one group.
       std::vector<std::tuple<size_t, size_t, size_t, bool>> items;  // (src, dst, count, f64)
@@ -1026,21 +1132,7 @@ std::unique_ptr<Program> make_program(const Plan& plan, int device) {
       }
       continue;
     }
-    if (st.fused) {
-      std::vector<size_t> ins, outs;
-      for (auto& in : st.group.inputs) ins.push_back(in.slot);
-      for (auto& o : st.group.outputs) outs.push_back(o.second);
-      ElemSpec spec = spec_from_group(st.group);
-      read_broadcast_sources(spec, ins);
-      p->steps.push_back(b.elementwise(spec, ins, outs));
-    } else if (st.instr.op.is_unary_elementwise() || st.instr.op.is_binary_elementwise() || st.instr.op.kind == OpKind::Where) {
-      std::vector<size_t> ins = st.instr.args;
-      ElemSpec spec = spec_from_instr(st.instr);
-      read_broadcast_sources(spec, ins);
-      p->steps.push_back(b.elementwise(spec, ins, {st.instr.dst}));
-    } else {
-      p->steps.push_back(b.lower(st.instr));
-    }
+    p->steps.push_back(lower_one(k));
     note_writes(k);
   }
   {
@@ -1958,3 +2050,109 @@ __attribute__((visibility("default"))) int rgc_exec_breakdown_json(rgc_exec* e, 
 }
 
 }  // extern "C"
+
+// Not part of include/rgc.h: test support. Builds the row-chain kernels the device would generate
+// for a plan blob and compiles them for sm_100a with NVRTC without loading them (no GPU or CUDA
+// context is needed). Returns the number of kernels, or -1 with the compiler's log in `log`;
+// chains that fall back to step-by-step lowering are listed in `log` either way.
+extern "C" __attribute__((visibility("default"))) int rgc_debug_row_kernels(const void* blob, size_t size, char* log, size_t cap) {
+  std::string msg;
+  int result = -1;
+  try {
+    rg::Plan plan = rg::decode_plan((const uint8_t*)blob, size);
+    std::vector<std::string> sources, names;
+    for (auto& c : rg::find_row_chains(plan, true)) {
+      rgc::RowKernel rk;
+      std::string why;
+      if (!rgc::make_row_kernel(plan, c, &rk, &why)) {
+        msg += "chain at step " + std::to_string(c.first) + " lowered step by step: " + why + "\n";
+        continue;
+      }
+      // Chains of the same structure (one per layer) share a kernel, as in the JIT.
+      if (std::find(names.begin(), names.end(), rk.name) == names.end()) {
+        names.push_back(rk.name);
+        sources.push_back(rk.source);
+      }
+    }
+    if (const char* dump = getenv("RGC_ROW_DUMP")) {
+      FILE* f = fopen(dump, "w");
+      if (f) {
+        for (auto& src : sources) fprintf(f, "%s\n", src.c_str());
+        fclose(f);
+      }
+    }
+    std::string err = sources.empty() ? std::string() : rgc::Jit::compile_check(sources);
+    if (err.empty()) {
+      result = (int)sources.size();
+    } else {
+      msg = err;
+    }
+  } catch (const std::exception& e) {
+    msg = e.what();
+  }
+  if (log && cap) {
+    size_t n = std::min(cap - 1, msg.size());
+    std::memcpy(log, msg.data(), n);
+    log[n] = '\0';
+  }
+  return result;
+}
+
+// Not part of include/rgc.h: test support. Describes the kernel of row chain `index` of a plan
+// blob as JSON (the chain's steps, the slots bound to its parameters, periods, broadcast
+// descriptors, rows, rows per block, shared memory) and writes the prelude and its source to
+// `source_path`, so that tests can compile it for the host and run it against the CPU
+// interpreter. Returns 0, 1 when the plan has no such chain or it falls back to step-by-step
+// lowering, or -1 with the reason in `json`.
+extern "C" __attribute__((visibility("default"))) int rgc_debug_row_kernel(const void* blob, size_t size, int index, char* json, size_t cap,
+                                                                           const char* source_path) {
+  std::string out;
+  int result = -1;
+  try {
+    rg::Plan plan = rg::decode_plan((const uint8_t*)blob, size);
+    auto chains = rg::find_row_chains(plan, true);
+    rgc::RowKernel rk;
+    std::string why;
+    if (index < 0 || (size_t)index >= chains.size() || !rgc::make_row_kernel(plan, chains[(size_t)index], &rk, &why)) {
+      out = why;
+      result = 1;
+    } else {
+      const rg::RowChain& c = chains[(size_t)index];
+      auto list = [](const std::vector<size_t>& v) {
+        std::string r = "[";
+        for (size_t i = 0; i < v.size(); ++i) r += (i ? "," : "") + std::to_string(v[i]);
+        return r + "]";
+      };
+      auto fdiv = [](const FDiv& f) { return "[" + std::to_string(f.d) + "," + std::to_string(f.m) + "," + std::to_string(f.s) + "]"; };
+      out = "{\"name\":\"" + rk.name + "\",\"first\":" + std::to_string(c.first) + ",\"last\":" + std::to_string(c.last) +
+            ",\"members\":" + list(c.members) + ",\"before\":" + list(c.before) + ",\"after\":" + list(c.after) +
+            ",\"in_slots\":" + list(rk.in_slots) + ",\"out_slots\":" + list(rk.out_slots) + ",\"rows\":" + std::to_string(rk.rows) +
+            ",\"rows_per_block\":" + std::to_string(rk.rows_per_block) + ",\"smem\":" + std::to_string(rk.smem) + ",\"in_div\":[";
+      for (size_t i = 0; i < rk.in_div.size(); ++i) out += (i ? "," : "") + fdiv(rk.in_div[i]);
+      out += "],\"bcs\":[";
+      for (size_t i = 0; i < rk.bcs.size(); ++i) {
+        const FDims& f = rk.bcs[i];
+        out += std::string(i ? "," : "") + "{\"rank\":" + std::to_string(f.rank) + ",\"d\":[";
+        for (int q = 0; q < MAXR; ++q) out += (q ? "," : "") + fdiv(f.d[q]);
+        out += "],\"st\":[";
+        for (int q = 0; q < MAXR; ++q) out += (q ? "," : "") + std::to_string(f.st[q]);
+        out += "]}";
+      }
+      out += "]}";
+      FILE* f = fopen(source_path, "w");
+      if (!f) throw std::runtime_error("cannot write the kernel source");
+      fprintf(f, "%s\n%s\n", rgc::Jit::prelude().c_str(), rk.source.c_str());
+      fclose(f);
+      result = 0;
+    }
+  } catch (const std::exception& e) {
+    out = e.what();
+    result = -1;
+  }
+  if (json && cap) {
+    size_t n = std::min(cap - 1, out.size());
+    std::memcpy(json, out.data(), n);
+    json[n] = '\0';
+  }
+  return result;
+}

@@ -413,10 +413,10 @@ std::vector<RowInput> row_inputs(const Plan& plan, const RowChain& c, size_t m) 
   return ins;
 }
 
-std::vector<RowChain> find_row_chains(const Plan& plan) {
+std::vector<RowChain> find_row_chains(const Plan& plan, bool device_plan) {
   std::vector<RowChain> out;
   // Only plans built with the CUDA device's fusion configuration (the one with `sink`).
-  if (!row_chains_enabled() || !plan.fuse.sink) return out;
+  if (!row_chains_enabled() || !(device_plan || plan.fuse.sink)) return out;
   size_t p = 0;
   while (p < plan.steps.size()) {
     RowChain c;

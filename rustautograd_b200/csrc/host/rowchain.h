@@ -32,9 +32,10 @@ struct RowChain {
 };
 
 // The chains the CUDA device forms for `plan`: with RGC_ROW_CHAINS=1, for plans built with its
-// fusion configuration (Fuse::CUDA); none otherwise.
+// fusion configuration (Fuse::CUDA); none otherwise. The device passes `device_plan`: the plans it
+// receives across the C ABI were built for it, and the plan blob does not carry the configuration.
 bool row_chains_enabled();
-std::vector<RowChain> find_row_chains(const Plan& plan);
+std::vector<RowChain> find_row_chains(const Plan& plan, bool device_plan = false);
 
 // Slots a plan step reads and writes.
 std::vector<size_t> step_reads(const Step& s);

@@ -10,7 +10,9 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def declared():
-    text = open(os.path.join(ROOT, "include", "rgc.h")).read()
+    """Entry points declared in include/: the device ABI (rgc.h) and test support (rgc_test.h)."""
+    inc = os.path.join(ROOT, "include")
+    text = "".join(open(os.path.join(inc, h)).read() for h in sorted(os.listdir(inc)) if h.endswith(".h"))
     return sorted(set(re.findall(r"\b(rgc_[a-z_]+)\s*\(", text)))
 
 
