@@ -114,6 +114,8 @@ struct Builder {
   std::vector<Role> roles;                                   // per member
   std::map<size_t, std::pair<size_t, size_t>> latest;        // slot -> (member, output) last written
   std::vector<size_t> member_writes, member_reads, after_writes, after_reads;
+  // Slots members read in place of a broadcast of them: no later step of the chain may write them.
+  std::vector<size_t> sources;
   std::map<size_t, bool> external_row_local;                 // slot read from outside: every read row-local
 
   // The plan step that last wrote `slot` before step `p`, or SIZE_MAX.
@@ -123,13 +125,18 @@ struct Builder {
     return SIZE_MAX;
   }
 
-  // A materialised broadcast of a pinned slot of the same dtype: its source slot, else SIZE_MAX.
-  size_t broadcast_source(size_t step) const {
+  // A materialised broadcast (step `step`) of a slot of the same dtype that still holds the
+  // broadcast's source when step `p` reads it: a pinned slot, or one no step in between writes.
+  // Its source slot, else SIZE_MAX.
+  size_t broadcast_source(size_t step, size_t p) const {
     if (step == SIZE_MAX) return SIZE_MAX;
     const Step& w = plan.steps[step];
     if (w.fused || w.instr.op.kind != OpKind::BroadcastTo || w.instr.args.size() != 1) return SIZE_MAX;
     size_t src = w.instr.args[0];
-    if (src >= plan.pinned.size() || !plan.pinned[src] || plan.slots[src].first != w.instr.dtype) return SIZE_MAX;
+    if (src >= plan.pinned.size() || plan.slots[src].first != w.instr.dtype) return SIZE_MAX;
+    if (!plan.pinned[src])
+      for (size_t q = step + 1; q < p; ++q)
+        if (contains(step_writes(plan.steps[q]), src)) return SIZE_MAX;
     return src;
   }
 
@@ -159,7 +166,7 @@ struct Builder {
         in.kind = RowInput::Full;
       } else if (as == shape) {
         in.kind = RowInput::Full;
-        size_t src = broadcast_source(last_writer(slot, p));
+        size_t src = broadcast_source(last_writer(slot, p), p);
         if (src != SIZE_MAX) {
           in.kind = RowInput::Source;
           in.through = slot;
@@ -196,7 +203,7 @@ struct Builder {
     if (!classify(p, r, &ins)) return false;
     auto writes = step_writes(st);
     for (size_t x : writes) {
-      if (plan.slots[x].first != dt) return false;
+      if (plan.slots[x].first != dt || contains(sources, x)) return false;
       // Other row blocks may still read a slot that is read as a whole (not row by row).
       auto e = external_row_local.find(x);
       if (e != external_row_local.end() && !e->second) return false;
@@ -219,6 +226,8 @@ struct Builder {
     // Every slot the step names, including broadcasts read through their source: the CPU
     // interpreter that checks chain plans reads them in plan order.
     for (size_t x : step_reads(st)) member_reads.push_back(x);
+    for (auto& in : ins)
+      if (in.through != SIZE_MAX) sources.push_back(in.slot);
     for (size_t q = 0; q < writes.size(); ++q) {
       latest[writes[q]] = {m, q};
       member_writes.push_back(writes[q]);
@@ -236,14 +245,15 @@ struct Builder {
     for (size_t x : step_reads(st))
       if (contains(member_writes, x) || contains(after_writes, x)) return false;
     for (size_t x : step_writes(st))
-      if (contains(member_writes, x) || contains(member_reads, x) || contains(after_writes, x) || contains(after_reads, x)) return false;
+      if (contains(member_writes, x) || contains(member_reads, x) || contains(after_writes, x) || contains(after_reads, x) || contains(sources, x))
+        return false;
     c.before.push_back(p);
     return true;
   }
 
   bool try_after(size_t p) {
     const Step& st = plan.steps[p];
-    if (broadcast_source(p) == SIZE_MAX) return false;
+    if (broadcast_source(p, p) == SIZE_MAX) return false;
     for (size_t x : step_reads(st))
       if (contains(member_writes, x)) return false;
     for (size_t x : step_writes(st)) {
