@@ -467,7 +467,7 @@ def main():
         if not args.no_cpu_baseline:
             secs_cpu, sample, threads = cpu_baseline(w)
             cpu = {"value": 1.0 / secs_cpu, "unit": "steps/s", "cores": threads, "kind": "port", "sample": sample}
-        cfg = dict(w.config(world), frame_bytes=compiled._n.allocated_bytes())
+        cfg = dict(w.config(world), frame_bytes=compiled._n.allocated_bytes(), row_chains=os.environ.get("RGC_ROW_CHAINS") == "1")
         out = {
             "metric": w.metric, "value": value, "unit": "steps/s", "n_gpus": world, "steps": done, "warmup": args.warmup,
             "ms_per_step": device_s / done * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
