@@ -137,3 +137,23 @@ def test_chains_are_off_by_default(monkeypatch):
     c = F.compile(fn, args, validate="none", device="cuda-plan")
     assert not chains(c)
     assert "sum" in plan_ops(c)
+
+
+def test_chains_inside_a_scan_body():
+    """A softmax-and-normalise recurrence under `scan`: the body plan, built with the device's
+    configuration, forms its own chains; value and gradients equal rg's plan bit for bit."""
+    rng = np.random.default_rng(6)
+    xs = F.tensor(rng.normal(size=(5, 12, 16)).astype("float32"))
+    w = F.tensor((rng.normal(size=(16, 16)) * 0.3).astype("float32"))
+
+    def loss(w, xs):
+        def body(h, x):
+            z = h @ w + x
+            p = F.nn.softmax(z)
+            mu = p.mean(axis=-1, keepdims=True)
+            h = (p - mu) / (((p - mu) ** 2).mean(axis=-1, keepdims=True) + 1e-5).sqrt()
+            return h, h.sum()
+        h, ys = F.scan(body, F.zeros((12, 16)), xs)
+        return (h * h).sum() + ys.sum()
+    out = run_both(F.value_and_grad(loss), (w, xs))
+    assert_same(out["cpu"][0], out["cuda-plan"][0])
