@@ -201,3 +201,31 @@ def test_recomputation_reads_stored_values_only():
         return (u * u).sum() + (v * v).sum()
     out = run_both(F.value_and_grad(loss, argnums=(0, 1)), (a, b))
     assert_same(out["cpu"][0], out["cuda-plan"][0])
+
+
+def test_custom_rules_and_control_flow_through_the_device_plan():
+    """Every device plan is rebuilt by the device's recomputation rule: a custom gradient rule,
+    scan and cond bodies (differentiated) and a while loop (forward only) give rg's results bit
+    for bit."""
+    rng = np.random.default_rng(0)
+    x = F.tensor(rng.normal(size=(64, 32)).astype("float32"))
+    w = F.tensor(rng.normal(size=(32, 32)).astype("float32"))
+    soft = F.custom_vjp(lambda v: v / (1.0 + F.abs(v)), lambda a, y, ct: (ct / F.square(1.0 + F.abs(a[0])),))
+
+    def with_rule(w, x):
+        h = F.nn.gelu(x @ w)
+        return (soft(h) * h).sum()
+
+    def with_bodies(w, x):
+        def body(c, r):
+            c = F.tanh(c @ w + r)
+            return c, (c * c).sum()
+        c, ys = F.scan(body, F.zeros((32,)), x)
+        return ys.sum() + F.cond(c.sum() > 0.0, lambda a: (a * a).sum(), lambda a: a.sum(), c)
+
+    def with_loop(w, x):
+        h = F.nn.softmax(x @ w)
+        return F.while_loop(lambda s: s[0] < 5.0, lambda s: (s[0] + 1.0, s[1] * 0.5 + h), (F.tensor(0.0), h))[1]
+    for fn in (F.value_and_grad(with_rule, argnums=(0, 1)), F.value_and_grad(with_bodies, argnums=(0, 1)), with_loop):
+        out = run_both(fn, (w, x))
+        assert_same(out["cpu"][0], out["cuda-plan"][0])
