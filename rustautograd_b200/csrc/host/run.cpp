@@ -1,10 +1,12 @@
 // The generic multi-step loop and one-off execution over the Exec contract.
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <stdexcept>
 #include <tuple>
 
 #include "exec.h"
+#include "rowchain.h"
 
 namespace rg {
 
@@ -124,6 +126,39 @@ std::vector<StepCost> step_costs(const Plan& p) {
       c.flops = 0;
     }
     out.push_back(c);
+  }
+  // A row chain (RGC_ROW_CHAINS=1) runs as one kernel at its first step: it reads each slot it
+  // reads from outside once and writes only the values it stores. Its members' own costs give
+  // way to that, so that time and bytes per step stay paired.
+  for (auto& ch : find_row_chains(p)) {
+    const double es = (double)dtype_size(ch.dtype), full = (double)ch.rows * (double)ch.cols, rows = (double)ch.rows;
+    double bytes = 0, flops = 0;
+    std::vector<std::pair<size_t, int>> seen;
+    for (size_t m = 0; m < ch.members.size(); ++m) {
+      const Step& st = p.steps[ch.members[m]];
+      // Per-row members read and write (..., 1) values; full ones and reductions read rows.
+      const bool per_row = !(st.fused ? st.group.shape == ch.shape : (st.instr.shape == ch.shape || st.instr.op.kind == OpKind::Reduce));
+      const bool full_out = st.fused ? st.group.shape == ch.shape : st.instr.shape == ch.shape;
+      flops += out[ch.members[m]].flops;
+      for (auto& in : row_inputs(p, ch, m)) {
+        if (in.kind == RowInput::Value) continue;
+        std::pair<size_t, int> key{in.slot, (int)in.kind};
+        if (std::find(seen.begin(), seen.end(), key) != seen.end()) continue;
+        seen.push_back(key);
+        switch (in.kind) {
+          case RowInput::Full: bytes += (per_row ? rows : full) * es; break;
+          case RowInput::Column: bytes += rows * es; break;
+          case RowInput::Periodic: bytes += (double)in.period * es; break;
+          case RowInput::Splat: bytes += es; break;
+          default: bytes += (double)product(in.shape) * es; break;
+        }
+      }
+      auto writes = step_writes(st);
+      for (size_t q = 0; q < writes.size(); ++q)
+        if (ch.store[m][q]) bytes += (full_out ? full : rows) * es;
+      out[ch.members[m]] = StepCost{"row_chain", 0.0, 0.0};
+    }
+    out[ch.first] = StepCost{"row_chain", flops, bytes};
   }
   return out;
 }
