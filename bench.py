@@ -342,6 +342,8 @@ def roofline(w, compiled, secs, pk):
     costs = compiled._n.step_costs()
     by_kind = {}
     for (kind, fl, by), s in zip(costs, secs):
+        if kind == "row_chain" and fl == 0 and by == 0:
+            continue  # the other steps of a row chain, which runs as one kernel at its first step
         e = by_kind.setdefault(kind, [0.0, 0.0, 0.0, 0])
         e[0] += s
         e[1] += fl
@@ -355,12 +357,15 @@ def roofline(w, compiled, secs, pk):
     else:
         achieved, peak, unit, bound = by / t_s / 1e9, pk["hbm_gbs"], "GB/s", "hbm"
     fused = by_kind.get("fused", [1e-30, 0, 0, 0])
+    chains = by_kind.get("row_chain")
     traffic, traffic_of = traffic_for(w.name, top)
     return {"bound": bound, "kernel": top, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
             "peak_source": pk["source"], "traffic": traffic, "traffic_of": traffic_of, "launches_per_step": n, "share_of_step": t_s / total,
             "algorithmic_per_launch": (fl if top == "matmul" else by) / max(n, 1),
             "fused_elementwise": {"achieved_gbs": fused[2] / fused[0] / 1e9, "frac_of_hbm": fused[2] / fused[0] / 1e9 / pk["hbm_gbs"],
-                                  "share_of_step": fused[0] / total}}
+                                  "share_of_step": fused[0] / total},
+            "row_chains": None if chains is None else {"achieved_gbs": chains[2] / chains[0] / 1e9, "frac_of_hbm": chains[2] / chains[0] / 1e9 / pk["hbm_gbs"],
+                                                       "share_of_step": chains[0] / total, "launches_per_step": chains[3]}}
 
 
 def main():
