@@ -157,3 +157,23 @@ def test_chains_inside_a_scan_body():
         return (h * h).sum() + ys.sum()
     out = run_both(F.value_and_grad(loss), (w, xs))
     assert_same(out["cpu"][0], out["cuda-plan"][0])
+
+
+def test_step_costs_count_a_chain_once(monkeypatch):
+    """With chains, a chain's first step carries its bytes (each outside slot read once, the
+    stored values written) and its other steps none, so per-step times and bytes stay paired;
+    the step moves fewer algorithmic bytes than without chains."""
+    fn, args = gpt_step(layers=1)
+    c = F.compile(fn, args, validate="none", device="cuda-plan")
+    with_chains = c._n.step_costs()
+    found = chains(c)
+    assert found
+    for ch in found:
+        first = int(ch["first"])
+        assert with_chains[first][0] == "row_chain" and with_chains[first][2] > 0
+        for m in ch["members"][1:]:
+            assert with_chains[int(m)] == ("row_chain", 0.0, 0.0)
+    monkeypatch.delenv("RGC_ROW_CHAINS", raising=False)
+    without = F.compile(fn, args, validate="none", device="cuda-plan")._n.step_costs()
+    assert sum(b for _, _, b in with_chains) < 0.9 * sum(b for _, _, b in without)
+    assert sum(f for _, f, _ in with_chains) == sum(f for _, f, _ in without)
