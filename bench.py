@@ -79,16 +79,29 @@ class Gpt:
                 "heads": self.heads, "vocab": self.vocab, "parallelism": f"dp{world}",
                 "l2": "state (params + AdamW moments) larger than L2 is streamed every step"}
 
-    def cpu_sample(self, F, oracle, budget=15.0):
-        """Batch-1 steps of the same model, scaled by the batch (every op of the step but the
-        optimizer update scales linearly in the batch)."""
-        step, state, data = self.build(F, batch=1)
-        c = F.compile(step, (state, data[0]), validate="none", device="cpu")
-        t, n = 0.0, 0
-        while n < 3 and t < budget:
-            t += F.run(c, state, data[0], steps=1).elapsed
-            n += 1
-        return t / n * self.batch, f"{n} steps of batch 1 (T={self.block}), scaled x{self.batch} to the global batch"
+    def cpu_sample(self, F, oracle, full=False):
+        """One step of the same model at batch 1 and, with `full`, one at batch 4. A full
+        global-batch step is far beyond a bounded sample (hours at d512), so its time is
+        extrapolated: with `full`, by the line through the two measured steps (the optimizer
+        update and the other batch-independent work are its intercept); otherwise linearly from
+        batch 1, which overstates the CPU step time (the interpreter goes parallel on more of a
+        step's operations as the batch grows)."""
+        batches = (1, 4) if full else (1,)
+        secs = []
+        for b in batches:
+            step, state, data = self.build(F, batch=b)
+            c = F.compile(step, (state, data[0]), validate="none", device="cpu")
+            secs.append(F.run(c, state, data[0], steps=1).elapsed)
+        if full:
+            slope = (secs[1] - secs[0]) / (batches[1] - batches[0])
+            est = secs[0] + slope * (self.batch - batches[0])
+            method = f"line through the measured steps at batch {batches[0]} and {batches[1]}, evaluated at the global batch {self.batch}"
+        else:
+            est = secs[0] * self.batch
+            method = f"the batch-1 step scaled x{self.batch} (linear from batch 1: an upper bound on the CPU step time)"
+        return {"seconds_per_step": est, "sample_steps": len(batches), "sample_batches": list(batches), "sample_seconds": secs,
+                "extrapolated": True, "method": method,
+                "sample": f"{len(batches)} step(s) of T={self.block} windows at batch {', '.join(map(str, batches))}; {method}"}
 
 
 class AdamW:
@@ -129,14 +142,12 @@ class AdamW:
         return {"workload": f"{self.name} 4 tensors {self.n} elements", "elements": self.n, "parallelism": "replicas",
                 "l2": "704 MB of state and gradients streamed every step (larger than L2)"}
 
-    def cpu_sample(self, F, oracle, budget=15.0):
+    def cpu_sample(self, F, oracle, full=False):
         step, state, grads = self.build(F)
         c = F.compile(step, (state, grads), validate="none", device="cpu")
-        t, n = 0.0, 0
-        while n < 5 and t < budget:
-            t += F.run(c, state, grads, steps=1).elapsed
-            n += 1
-        return t / n, f"{n} full steps"
+        n = 10 if full else 5
+        t = F.run(c, state, grads, steps=n).elapsed
+        return {"seconds_per_step": t / n, "sample_steps": n, "sample_seconds": [t], "extrapolated": False, "sample": f"{n} full steps in one run"}
 
 
 class LinReg:
@@ -163,11 +174,12 @@ class LinReg:
     def config(self, world):
         return {"workload": f"{self.name} x (256, 8) f32, lr 0.05", "parallelism": "replicas", "l2": "8 KB of data, L2-resident by design"}
 
-    def cpu_sample(self, F, oracle, budget=15.0):
+    def cpu_sample(self, F, oracle, full=False):
         step, state, data = self.build(F)
         c = F.compile(step, (state, list(data)), validate="none", device="cpu")
         r = F.run(c, state, list(data), steps=500)
-        return r.elapsed / 500, "500 steps in one run"
+        return {"seconds_per_step": r.elapsed / 500, "sample_steps": 500, "sample_seconds": [r.elapsed], "extrapolated": False,
+                "sample": "500 steps in one run"}
 
 
 class Gemm:
@@ -193,12 +205,13 @@ class Gemm:
         return {"workload": f"{self.name} {self.m}x{self.k} @ {self.k}x{self.n} f32", "parallelism": "replicas",
                 "l2": "operands and result (1.3 GB) larger than L2"}
 
-    def cpu_sample(self, F, oracle, budget=15.0):
+    def cpu_sample(self, F, oracle, full=False):
         m = 1024
         step, state, data = self.build(F, m=m)
         c = F.compile(step, (state, list(data)), validate="none", device="cpu")
         t = F.run(c, state, list(data), steps=1).elapsed
-        return t * self.m / m, f"one product with {m} of {self.m} rows, scaled x{self.m // m}"
+        return {"seconds_per_step": t * self.m / m, "sample_steps": 1, "sample_seconds": [t], "extrapolated": True,
+                "sample": f"one product with {m} of {self.m} rows, scaled x{self.m // m} (the product is linear in its rows)"}
 
 
 class Chain:
@@ -245,11 +258,12 @@ class Chain:
         return {"workload": f"{self.name} A(4096,16)@B@C@D and x(1024,4096)@(U@V)@x^T, values and gradients, search-linear",
                 "parallelism": "replicas", "l2": "operands and products larger than L2 (the 4096x4096 output of the first chain)"}
 
-    def cpu_sample(self, F, oracle, budget=15.0):
+    def cpu_sample(self, F, oracle, full=False):
         step, state, data = self.build(F, scale=4)
         c = F.compile(step, (state, data), validate="none", device="cpu", optimize="search-linear")
         t = F.run(c, state, data, steps=1).elapsed
-        return t * 16, "one step at a quarter of every large dimension (16x fewer multiplications), scaled x16"
+        return {"seconds_per_step": t * 16, "sample_steps": 1, "sample_seconds": [t], "extrapolated": True,
+                "sample": "one step at a quarter of every large dimension (16x fewer multiplications), scaled x16"}
 
 
 WORKLOADS = {
@@ -325,16 +339,18 @@ def traffic_for(workload, kernel):
         return None, None
 
 
-def cpu_baseline(w):
-    """The CPU oracle (restated rg interpreter) on all host threads, on a bounded sample."""
+def cpu_baseline(w, full=False):
+    """The CPU oracle (restated rg interpreter) on all host threads, on a bounded sample.
+    Returns the sample's record (cpu_sample) with the thread count."""
     sys.path.insert(0, os.path.join(ROOT, "oracle", "_build"))
     from rustautograd_b200 import build_ext
     build_ext.build_oracle()
     import _rg_oracle
     from rustautograd_b200 import frontend as F
     F.use(_rg_oracle, "cpu")
-    secs, sample = w.cpu_sample(F, _rg_oracle)
-    return secs, sample, _rg_oracle.threads()
+    rec = w.cpu_sample(F, _rg_oracle, full=full)
+    rec["cores"] = _rg_oracle.threads()
+    return rec
 
 
 def roofline(w, compiled, secs, pk):
@@ -383,15 +399,23 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
 
     if args.impl == "reference":
+        # rg's CPU interpreter (the restatement under oracle/; rg itself cannot be built here) on
+        # every host thread. It runs a bounded sample, not --steps global-batch steps: "steps" and
+        # "ms_per_step" describe the sample steps that actually ran, and "value" is the
+        # workload's steps/s derived from them as "extrapolation" states.
         if rank != 0:
             return
-        secs, sample, threads = cpu_baseline(w)
-        value = 1.0 / secs
+        rec = cpu_baseline(w, full=True)
+        value = 1.0 / rec["seconds_per_step"]
+        ran = sum(rec["sample_seconds"])
         print(json.dumps({
-            "impl": "reference", "metric": w.metric, "value": value, "unit": "steps/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": secs * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic", "config": w.config(args.gpus),
-            "cpu_baseline": {"value": value, "unit": "steps/s", "cores": threads, "kind": "port", "sample": sample},
+            "impl": "reference", "metric": w.metric, "value": value, "unit": "steps/s", "n_gpus": args.gpus,
+            "steps": rec["sample_steps"], "warmup": 0, "ms_per_step": ran / rec["sample_steps"] * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": w.config(args.gpus),
+            "extrapolation": {"extrapolated": rec["extrapolated"], "sample_batches": rec.get("sample_batches"),
+                              "sample_seconds": rec["sample_seconds"], "seconds_per_workload_step": rec["seconds_per_step"],
+                              "method": rec.get("method", rec["sample"])},
+            "cpu_baseline": {"value": value, "unit": "steps/s", "cores": rec["cores"], "kind": "port", "sample": rec["sample"]},
             "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }))
         return
@@ -470,9 +494,10 @@ def main():
                        "algorithmic_per_launch": w.algorithmic_bytes() / max(rf["launches_per_step"], 1)})
         cpu = None
         if not args.no_cpu_baseline:
-            secs_cpu, sample, threads = cpu_baseline(w)
-            cpu = {"value": 1.0 / secs_cpu, "unit": "steps/s", "cores": threads, "kind": "port", "sample": sample}
-        cfg = dict(w.config(world), frame_bytes=compiled._n.allocated_bytes(), row_chains=os.environ.get("RGC_ROW_CHAINS") == "1")
+            rec = cpu_baseline(w)
+            cpu = {"value": 1.0 / rec["seconds_per_step"], "unit": "steps/s", "cores": rec["cores"], "kind": "port", "sample": rec["sample"],
+                   "sample_steps": rec["sample_steps"], "sample_seconds": rec["sample_seconds"], "extrapolated": rec["extrapolated"]}
+        cfg = dict(w.config(world), frame_bytes=compiled._n.allocated_bytes(), row_chains=os.environ.get("RGC_ROW_CHAINS") != "0")
         out = {
             "metric": w.metric, "value": value, "unit": "steps/s", "n_gpus": world, "steps": done, "warmup": args.warmup,
             "ms_per_step": device_s / done * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,

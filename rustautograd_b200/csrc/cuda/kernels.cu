@@ -75,7 +75,7 @@ __device__ __forceinline__ void pdl_wait() {
 }
 
 template <typename... P, typename... A>
-void launch_with(bool pdl, void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A&&... args) {
+cudaError_t launch_with(bool pdl, void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -86,10 +86,10 @@ void launch_with(bool pdl, void (*kernel)(P...), dim3 grid, dim3 block, size_t s
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
-  cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
 }
-template <typename... P, typename... A> void launch(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A&&... args) {
-  launch_with(true, kernel, grid, block, smem, s, std::forward<A>(args)...);
+template <typename... P, typename... A> cudaError_t launch(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A&&... args) {
+  return launch_with(true, kernel, grid, block, smem, s, std::forward<A>(args)...);
 }
 
 // A grid-stride launch of `kernel` over n work items, covering the GPU in exactly one wave: as
@@ -1290,20 +1290,21 @@ size_t full_sum_scratch_bytes(long long n, EType t) {
   return (size_t)((n + SUM_CHUNK - 1) / SUM_CHUNK) * esize(t);
 }
 
-void reduce_full_sum(void* dst, const void* src, EType t, long long n, void* scratch, cudaStream_t s) {
+cudaError_t reduce_full_sum(void* dst, const void* src, EType t, long long n, void* scratch, cudaStream_t s) {
   if (n <= EXACT_SUM_MAX) {
-    if (t == EType::F64) launch(k_sum_exact<double>, 1, 32, 0, s, (double*)dst, (const double*)src, n);
-    else launch(k_sum_exact<float>, 1, 32, 0, s, (float*)dst, (const float*)src, n);
-    return;
+    if (t == EType::F64) return launch(k_sum_exact<double>, 1, 32, 0, s, (double*)dst, (const double*)src, n);
+    return launch(k_sum_exact<float>, 1, 32, 0, s, (float*)dst, (const float*)src, n);
   }
   long long parts = (n + SUM_CHUNK - 1) / SUM_CHUNK;
+  cudaError_t e;
   if (t == EType::F64) {
-    launch(k_sum_chunks<double>, (unsigned)parts, 256, 0, s, (double*)scratch, (const double*)src, n, SUM_CHUNK);
-    launch(k_sum_final<double>, 1, 1024, 0, s, (double*)dst, (const double*)scratch, parts);
-  } else {
-    launch(k_sum_chunks<float>, (unsigned)parts, 256, 0, s, (float*)scratch, (const float*)src, n, SUM_CHUNK);
-    launch(k_sum_final<float>, 1, 1024, 0, s, (float*)dst, (const float*)scratch, parts);
+    e = launch(k_sum_chunks<double>, (unsigned)parts, 256, 0, s, (double*)scratch, (const double*)src, n, SUM_CHUNK);
+    if (e != cudaSuccess) return e;
+    return launch(k_sum_final<double>, 1, 1024, 0, s, (double*)dst, (const double*)scratch, parts);
   }
+  e = launch(k_sum_chunks<float>, (unsigned)parts, 256, 0, s, (float*)scratch, (const float*)src, n, SUM_CHUNK);
+  if (e != cudaSuccess) return e;
+  return launch(k_sum_final<float>, 1, 1024, 0, s, (float*)dst, (const float*)scratch, parts);
 }
 
 template <typename T> static void rows_t(void* dst, const void* src, Red op, long long rows, long long len, cudaStream_t s) {

@@ -77,7 +77,8 @@ enum class Red : int { Sum = 0, Max = 1, Min = 2 };
 // Full sum in rg's eight-lane order (bit-exact) for small n; a fixed-order tree otherwise.
 // `scratch` needs full_sum_scratch_bytes(n) bytes.
 size_t full_sum_scratch_bytes(long long n, EType t);
-void reduce_full_sum(void* dst, const void* src, EType t, long long n, void* scratch, cudaStream_t s);
+// Returns the first launch error (the launches' own status, not cudaGetLastError).
+cudaError_t reduce_full_sum(void* dst, const void* src, EType t, long long n, void* scratch, cudaStream_t s);
 // Rows of length `len` reduced to one value each.
 void reduce_rows(void* dst, const void* src, EType t, Red op, long long rows, long long len, cudaStream_t s);
 // [rows, cols] reduced over rows in rg's order: sequentially, or, when `chunked` (rg's own

@@ -17,9 +17,13 @@
 //  - Every call on a device shares the one array. Two calls that may run at the same time on
 //    the GPU (different streams without ordering between them) race on it and can return wrong
 //    sums; order them on one stream, or with events.
-//  - The first call on each device does set-up: it looks up the array's device address
-//    (cudaGetSymbolAddress, with that device current) and its launches load the two kernels.
-//    Make that first call before any stream capture is begun.
+//  - The first call on each device (more exactly, in each CUDA context that is current when
+//    it is called) does set-up: it looks up the array's device address (cudaGetSymbolAddress,
+//    with that device current) and its launches load the two kernels. Make that first call
+//    before any stream capture is begun. The address is remembered together with the context it
+//    was looked up in, so a reset device or primary context is looked up afresh.
+//  - Errors are the launches' own return codes; an error that earlier CUDA work of the caller
+//    left pending is neither reported nor cleared by this call.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -45,23 +49,53 @@ constexpr int MAX_DEVICES = 64;
 static __device__ __align__(256) unsigned char g_sum_scratch[NOALLOC_SCRATCH_BYTES];
 
 std::mutex g_mu;
-void* g_scratch_of[MAX_DEVICES] = {};
+struct ScratchOf {
+  void* context = nullptr;  // the CUDA context the address was looked up in
+  void* address = nullptr;
+};
+ScratchOf g_scratch_of[MAX_DEVICES];
 
-// The array's device address on the current device, looked up once per device.
+// cuCtxGetCurrent through the runtime's driver entry points (no link against libcuda).
+using CtxGetCurrentFn = int (*)(void**);
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+#pragma GCC diagnostic push
+#pragma GCC diagnostic ignored "-Wdeprecated-declarations"
+    cudaError_t e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q);
+#pragma GCC diagnostic pop
+    return (e == cudaSuccess && q == cudaDriverEntryPointSuccess) ? (CtxGetCurrentFn)f : nullptr;
+  }();
+  return fn;
+}
+
+// The array's device address in the current device's current context, looked up once per
+// (device, context) pair.
 int scratch_address(void** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_last_error(RGC_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
   if (dev < 0 || dev >= MAX_DEVICES) return set_last_error(RGC_ERR_INVALID, "device ordinal out of range");
+  CtxGetCurrentFn get = ctx_get_current();
+  if (!get) return set_last_error(RGC_ERR_CUDA, "cuCtxGetCurrent is not available from the CUDA runtime");
+  void* ctx = nullptr;
+  if (get(&ctx) != 0) return set_last_error(RGC_ERR_CUDA, "cuCtxGetCurrent failed");
   std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_scratch_of[dev]) {
+  ScratchOf& slot = g_scratch_of[dev];
+  if (!ctx || !slot.address || slot.context != ctx) {
+    // cudaGetSymbolAddress also makes the device's primary context current when no context is
+    // yet; the context is read again after it, so the address is filed under the context the
+    // launches will use.
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_sum_scratch);
     if (e != cudaSuccess || !p)
       return set_last_error(RGC_ERR_CUDA, std::string("cudaGetSymbolAddress of the fixed sum scratch: ") + cudaGetErrorString(e));
-    g_scratch_of[dev] = p;
+    if (get(&ctx) != 0 || !ctx) return set_last_error(RGC_ERR_CUDA, "cuCtxGetCurrent: no current CUDA context");
+    slot.context = ctx;
+    slot.address = p;
   }
-  *out = g_scratch_of[dev];
+  *out = slot.address;
   return RGC_OK;
 }
 
@@ -85,8 +119,7 @@ extern "C" __attribute__((visibility("default"))) int rgc_sum_noalloc(const void
     if (rc != RGC_OK) return rc;
   }
   cudaStream_t s = (cudaStream_t)stream;
-  reduce_full_sum(dst, src, t, (long long)n, scratch, s);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = reduce_full_sum(dst, src, t, (long long)n, scratch, s);
   if (e != cudaSuccess) return set_last_error(RGC_ERR_CUDA, std::string("rgc_sum_noalloc launch: ") + cudaGetErrorString(e));
   return RGC_OK;
 }

@@ -520,7 +520,7 @@ PYBIND11_MODULE(RG_MODULE_NAME, m) {
         for (auto& c : step_costs(self.c->plan)) out.emplace_back(c.kind, c.flops, c.bytes);
         return out;
       })
-      // Not in rg's module: the row chains the CUDA device forms for this plan (RGC_ROW_CHAINS=1).
+      // Not in rg's module: the row chains the CUDA device forms for this plan (none with RGC_ROW_CHAINS=0).
       .def("row_chains", [](const PyCompiled& self) {
         Json a = Json::array();
         for (auto& c : find_row_chains(self.c->plan)) {

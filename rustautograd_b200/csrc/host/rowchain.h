@@ -31,7 +31,7 @@ struct RowChain {
   std::vector<std::vector<bool>> store;
 };
 
-// The chains the CUDA device forms for `plan`: with RGC_ROW_CHAINS=1, for plans built with its
+// The chains the CUDA device forms for `plan`: unless RGC_ROW_CHAINS=0, for plans built with its
 // fusion configuration (Fuse::CUDA); none otherwise. The device passes `device_plan`: the plans it
 // receives across the C ABI were built for it, and the plan blob does not carry the configuration.
 bool row_chains_enabled();

@@ -127,7 +127,7 @@ std::vector<StepCost> step_costs(const Plan& p) {
     }
     out.push_back(c);
   }
-  // A row chain (RGC_ROW_CHAINS=1) runs as one kernel at its first step: it reads each slot it
+  // A row chain (on unless RGC_ROW_CHAINS=0) runs as one kernel at its first step: it reads each slot it
   // reads from outside once and writes only the values it stores. Its members' own costs give
   // way to that, so that time and bytes per step stay paired.
   for (auto& ch : find_row_chains(p)) {

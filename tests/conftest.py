@@ -7,7 +7,11 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-REFERENCE_PY = "/root/reference/python"
+# rg's own checkout (its python/ and examples/ folders), when one is present on this machine: set
+# RG_REFERENCE_ROOT to it. Tests that drive rg's Python front end skip when it is unset.
+REFERENCE_ROOT = os.environ.get("RG_REFERENCE_ROOT", "")
+REFERENCE_PY = os.path.join(REFERENCE_ROOT, "python") if REFERENCE_ROOT else ""
+REFERENCE_EXAMPLES = os.path.join(REFERENCE_ROOT, "examples") if REFERENCE_ROOT else ""
 
 
 def pytest_configure(config):
@@ -51,8 +55,8 @@ def cuda(product):
 @pytest.fixture(scope="session")
 def rg_reference(oracle):
     """rg's own Python front end, driven over the oracle module (build container only)."""
-    if not os.path.isdir(REFERENCE_PY):
-        pytest.skip("rg's Python front end is not present on this machine")
+    if not REFERENCE_PY or not os.path.isdir(REFERENCE_PY):
+        pytest.skip("rg's Python front end is not present (set RG_REFERENCE_ROOT to rg's checkout)")
     sys.modules["rg._rg"] = oracle
     if REFERENCE_PY not in sys.path:
         sys.path.insert(0, REFERENCE_PY)

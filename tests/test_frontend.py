@@ -9,6 +9,7 @@ import numpy as np
 import pytest
 
 from rustautograd_b200 import frontend as F
+from conftest import REFERENCE_EXAMPLES
 
 
 @pytest.fixture
@@ -35,7 +36,7 @@ def capture_graph(m, compile_fn):
 @pytest.mark.reference
 def test_gpt_training_step_graph_is_identical_to_rgs_front_end(fe, oracle, rg_reference):
     import sys
-    sys.path.insert(0, "/root/reference/examples")
+    sys.path.insert(0, REFERENCE_EXAMPLES)
     import gpt as ref_gpt
     rg = rg_reference
     cfg = dict(vocab=96, block=16, d=32, heads=4, layers=2)
@@ -177,7 +178,7 @@ def test_optimiser_options_build_rgs_graphs(fe, oracle, rg_reference):
 def test_gpt_with_dropout_builds_rgs_graph(fe, oracle, rg_reference):
     """examples/gpt.py with dropout_rate 0.1: attention-weight, attention-output and MLP dropout."""
     import sys
-    sys.path.insert(0, "/root/reference/examples")
+    sys.path.insert(0, REFERENCE_EXAMPLES)
     import gpt as ref_gpt
     rg = rg_reference
     cfg = dict(vocab=40, block=8, d=16, heads=2, layers=2, dropout_rate=0.1)

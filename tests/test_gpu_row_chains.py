@@ -1,28 +1,20 @@
-"""Row chains on the CUDA device (RGC_ROW_CHAINS=1): the same plans with and without chains give
-bit-identical results, since a chain evaluates the same operations in the same order as the
-plan's own kernels; rows without transcendental functions also equal the CPU interpreter's.
-
-Chains are off by default until these tests have run on a B200; they skip unless RGC_ROW_CHAINS=1
-is set for the test process. (The generated kernels are checked on the CPU, thread by thread
+"""Row chains on the CUDA device (on by default; RGC_ROW_CHAINS=0 turns them off): the same plans
+with and without chains give bit-identical results, since a chain evaluates the same operations
+in the same order as the plan's own kernels; rows without transcendental functions also equal
+the CPU interpreter's. (The generated kernels are also checked on the CPU, thread by thread
 against the interpreter, by test_row_kernels_emulated.py.)
 """
-import os
-
 import numpy as np
 import pytest
 
 from rustautograd_b200 import frontend as F
 from helpers import assert_bits_equal, compile_and_compare
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("RGC_ROW_CHAINS") != "1", reason="row chains run only with RGC_ROW_CHAINS=1")]
+pytestmark = pytest.mark.gpu
 
 
 def outputs(fn, args, chains, monkeypatch):
-    if chains:
-        monkeypatch.setenv("RGC_ROW_CHAINS", "1")
-    else:
-        monkeypatch.delenv("RGC_ROW_CHAINS", raising=False)
+    monkeypatch.setenv("RGC_ROW_CHAINS", "1" if chains else "0")
     c = F.compile(fn, args, validate="none", device="cuda")
     leaves = [F.tensor(x) for x in F.flatten(args)[0]]
     return [F.Tensor(t).numpy() for t in c._n.call([t._t for t in leaves])], c

@@ -1,4 +1,4 @@
-"""Row chains (RGC_ROW_CHAINS=1) on the CPU: the plan steps the CUDA device computes as one row
+"""Row chains (on by default, RGC_ROW_CHAINS=0 turns them off) on the CPU: the plan steps the CUDA device computes as one row
 kernel, chosen by the same host code the device uses, run by the oracle's "cuda-plan" device the
 way the device runs them. Values a chain does not store are filled with NaN there, so a chain
 that fails to store a value some later step reads changes the results. Every result is compared
@@ -131,9 +131,11 @@ def test_reductions_over_other_axes_and_wide_rows_are_left_alone():
     assert not chains(cols), "column reductions are not row chains"
 
 
-def test_chains_are_off_by_default(monkeypatch):
+def test_chains_are_on_by_default_and_off_with_the_switch(monkeypatch):
     monkeypatch.delenv("RGC_ROW_CHAINS", raising=False)
     fn, args = gpt_step(layers=1)
+    assert chains(F.compile(fn, args, validate="none", device="cuda-plan"))
+    monkeypatch.setenv("RGC_ROW_CHAINS", "0")
     c = F.compile(fn, args, validate="none", device="cuda-plan")
     assert not chains(c)
     assert "sum" in plan_ops(c)
@@ -173,7 +175,7 @@ def test_step_costs_count_a_chain_once(monkeypatch):
         assert with_chains[first][0] == "row_chain" and with_chains[first][2] > 0
         for m in ch["members"][1:]:
             assert with_chains[int(m)] == ("row_chain", 0.0, 0.0)
-    monkeypatch.delenv("RGC_ROW_CHAINS", raising=False)
+    monkeypatch.setenv("RGC_ROW_CHAINS", "0")
     without = F.compile(fn, args, validate="none", device="cuda-plan")._n.step_costs()
     assert sum(b for _, _, b in with_chains) < 0.9 * sum(b for _, _, b in without)
     assert sum(f for _, f, _ in with_chains) == sum(f for _, f, _ in without)
