@@ -1,16 +1,21 @@
-"""Python front end tracing rg programs onto an engine module with rg's `_rg` interface."""
-from . import checkpoint, gpt, nn, optim, random, tree
-from .core import (Compiled, DiagnosticError, Report, RunResult, Tensor, Tracer, abs, all_reduce, arange, argmax, argsort, broadcast_to, clip,
-                   compile, concatenate, cond, cos, cumsum, custom_vjp, devices, equal, exp, expand_dims, eye, flatten, flip, floor, full,
-                   grad, hessian, inspect, jvp, linspace, log, matmul, maximum, minimum, native, not_equal, ones, ones_like, op, reshape, run,
-                   scan, sign, sin, sort, sqrt, square, squeeze, stack, stop_gradient, swapaxes, take, take_along_axis, tanh, tensor, top_k,
-                   transpose, tree_leaves, tree_map, tril, unflatten, use, value_and_grad, where, while_loop, zeros, zeros_like)
+"""A small front end that records the workloads of BASELINE's configs as rg graphs and drives the
+engine's compile / run over them: the linear regression (config 1), AdamW (config 2), matrix
+chains (config 3), the character GPT training step and sampler (configs 4 and 5), and control
+flow, gradient rules, observe statistics and checkpoints for the tests.
+
+rg's own Python package (`python/rg/`) runs unchanged over this package's `_rg` module; this
+front end exists for machines where rg's package is not installed (the GPU boxes), and records
+the same graphs for the same programs (tests/golden holds graphs recorded by rg's front end).
+"""
+from . import checkpoint, gpt, nn, optim, random
 from .checkpoint import Session
+from .program import Compiled, Report, RunResult, compile, cond, custom_vjp, grad, run, scan, value_and_grad, while_loop
+from .tracing import (DiagnosticError, Tensor, Traced, abs, all_reduce, arange, argmax, argsort, broadcast_to, concatenate, cumsum, exp, floor,
+                      full, log, matmul, maximum, minimum, native, ones, ones_like, op, sort, sqrt, square, stop_gradient, swapaxes, take,
+                      take_along_axis, tanh, tensor, top_k, tril, use, where, zeros, zeros_like)
+from .trees import flatten, tree_leaves, tree_map, unflatten
 
 
-def sum(x, axis=None, keepdims=False): return x.sum(axis, keepdims)
-def mean(x, axis=None, keepdims=False): return x.mean(axis, keepdims)
-def max(x, axis=None, keepdims=False): return x.max(axis, keepdims)
-def min(x, axis=None, keepdims=False): return x.min(axis, keepdims)
-def var(x, axis=None, keepdims=False): return x.var(axis, keepdims)
-def std(x, axis=None, keepdims=False): return x.std(axis, keepdims)
+def devices():
+    """Device names the selected engine module compiles for."""
+    return native().available_devices()

@@ -1,22 +1,31 @@
-"""Keyed random numbers (the op compositions of python/rg/random.py): every function is pure
-in its key, so a compiled step that carries its key in its state replays exactly."""
-from .core import argmax, floor, log, maximum, op, tensor
+"""Keyed random numbers. A key is a pair of int32 words; every draw is a pure function of its key
+(the engine's SplitMix64 streams), so a step that carries its key in its state replays exactly.
+
+`key(seed)` derives the pair as rg does (the seed times the 64-bit golden-ratio constant, high
+word first, each word as a signed int32), so seeds give the same streams in both front ends.
+"""
+from .tracing import argmax, floor, log, maximum, op, tensor
+
+_GOLDEN = 0x9E3779B97F4A7C15
+
+
+def _i32(word):
+    return word - (1 << 32) if word >= (1 << 31) else word
 
 
 def key(seed):
-    """A key from an integer seed: the seed times the 64-bit golden ratio, as two int32 halves."""
-    mixed = seed * 0x9E3779B97F4A7C15 % (1 << 64)
-    signed = lambda v: v - (1 << 32) if v >= (1 << 31) else v
-    return tensor([signed(mixed >> 32), signed(mixed & 0xFFFFFFFF)], "int32")
+    mixed = (seed * _GOLDEN) & ((1 << 64) - 1)
+    return tensor([_i32(mixed >> 32), _i32(mixed & 0xFFFFFFFF)], "int32")
 
 
 def split(k, n=2):
+    """`n` independent keys, shape (n, 2)."""
     return op("key_split", k, n=n)
 
 
 def uniform(k, shape=(), dtype="float32", low=0.0, high=1.0):
     u = op("random_uniform", k, shape=list(shape), dtype=dtype)
-    return u if low == 0.0 and high == 1.0 else low + (high - low) * u
+    return u if (low, high) == (0.0, 1.0) else low + (high - low) * u
 
 
 def normal(k, shape=(), dtype="float32"):
@@ -24,22 +33,14 @@ def normal(k, shape=(), dtype="float32"):
 
 
 def randint(k, shape, low, high):
-    """Uniform int32 in [low, high), drawn in float64 so every integer of the range is reachable."""
+    """int32 uniform over [low, high): drawn in float64 so every integer of a large range is
+    reachable, then floored."""
     u = op("random_uniform", k, shape=list(shape), dtype="float64")
     return floor(low + (high - low) * u).cast("int32")
 
 
-def bernoulli(k, p=0.5, shape=(), dtype="float32"):
-    """1 with probability `p`, else 0, as floats."""
-    return op("gt", tensor(float(p), dtype), op("random_uniform", k, shape=list(shape), dtype=dtype))
-
-
-def gumbel(k, shape=(), dtype="float32"):
-    u = op("random_uniform", k, shape=list(shape), dtype=dtype)
-    eps = 1e-7 if dtype == "float32" else 1e-15
-    return -log(-log(maximum(u, eps)))
-
-
 def categorical(k, logits, axis=-1):
-    """Indices drawn from unnormalised log-probabilities with the Gumbel-max trick."""
-    return argmax(logits + gumbel(k, logits.shape, logits.dtype), axis)
+    """Indices drawn from unnormalised log-probabilities by the Gumbel-max trick."""
+    u = op("random_uniform", k, shape=list(logits.shape), dtype=logits.dtype)
+    tiny = 1e-7 if logits.dtype == "float32" else 1e-15
+    return argmax(logits + -log(-log(maximum(u, tiny))), axis)

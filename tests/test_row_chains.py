@@ -84,12 +84,11 @@ def test_layernorm_and_cross_entropy_chains():
     rng = np.random.default_rng(3)
     x = F.tensor(rng.normal(size=(64, 48)).astype("float32"))
     labels = F.tensor(rng.integers(0, 10, size=(64,), dtype="int32"))
-    norm = F.nn.LayerNorm(48)
-    head = F.nn.Linear(48, 10)
-    params = {"norm": norm.init(F.random.key(0)), "head": head.init(F.random.key(1))}
+    params = {"norm": {"scale": F.ones(48), "shift": F.zeros(48)},
+              "head": {"w": F.random.normal(F.random.key(1), (48, 10)) * 0.02, "b": F.zeros(10)}}
 
     def loss(p, x, y):
-        return F.nn.cross_entropy(head(p["head"], norm(p["norm"], x)), y)
+        return F.nn.cross_entropy(F.gpt.linear(p["head"], F.gpt.layer_norm(p["norm"], x)), y)
     out = run_both(F.value_and_grad(loss), (params, x, labels))
     assert_same(out["cpu"][0], out["cuda-plan"][0])
     widths = sorted({int(ch["cols"]) for ch in chains(out["cuda-plan"][1])})
@@ -102,10 +101,14 @@ def test_training_run_history_with_row_chains():
     rng = np.random.default_rng(4)
     x = F.tensor(rng.normal(size=(128, 16)).astype("float32"))
     y = F.tensor(rng.integers(0, 5, size=(128,), dtype="int32"))
-    model = F.nn.Sequential(F.nn.Linear(16, 32), F.nn.gelu, F.nn.LayerNorm(32), F.nn.Linear(32, 5))
-    params = model.init(F.random.key(2))
-    opt = F.optim.adam(1e-2)
+    k1, k2 = F.random.split(F.random.key(2))
+    params = {"fc1": {"w": F.random.normal(k1, (16, 32)) * 0.02, "b": F.zeros(32)}, "norm": {"scale": F.ones(32), "shift": F.zeros(32)},
+              "fc2": {"w": F.random.normal(k2, (32, 5)) * 0.02, "b": F.zeros(5)}}
+    opt = F.optim.adamw(1e-2, weight_decay=0.0)
     state = {"params": params, "opt": opt.init(params)}
+
+    def model(p, x):
+        return F.gpt.linear(p["fc2"], F.gpt.layer_norm(p["norm"], F.nn.gelu(F.gpt.linear(p["fc1"], x))))
 
     def step(state, batch):
         value, g = F.value_and_grad(lambda p: F.nn.cross_entropy(model(p, batch[0]), batch[1]))(state["params"])
