@@ -16,10 +16,13 @@ using rg::RowInput;
 
 namespace {
 
-// Shared memory a block may use: two blocks per SM. Rows per block are capped so that a block's
-// stages still give every thread several elements.
-constexpr size_t SMEM_TARGET = 100 * 1024, SMEM_MAX = 200 * 1024;
-constexpr int MAX_ROWS_PER_BLOCK = 64;
+// Shared memory a block may use. The kernels are bound by memory latency as much as by
+// bandwidth: a stage issues its loads, and the block then waits at a barrier before its
+// reductions, so the SM needs several blocks in flight to keep HBM busy. About 44 KB per block
+// lets five blocks (40 warps) share an SM; rows per block are capped so that each block still
+// turns over often enough to overlap with the others.
+constexpr size_t SMEM_TARGET = 44 * 1024, SMEM_MAX = 200 * 1024;
+constexpr int MAX_ROWS_PER_BLOCK = 32;
 
 enum class Role { Full, Col, Reduce };
 
@@ -317,6 +320,9 @@ bool make_row_kernel(const rg::Plan& plan, const rg::RowChain& c, RowKernel* k, 
           if (b >= 0 && std::find(used.begin(), used.end(), b) == used.end()) used.push_back(b);
     o << "    // stage " << s << "\n";
     if (role == Role::Full) {
+      // Unrolled, so that the loads of several iterations can be in flight together where the
+      // compiler can order them ahead of the earlier iterations' stores.
+      o << "    #pragma unroll 4\n";
       o << "    for (int v = threadIdx.x; v < nr * " << CV << "; v += " << ROW_THREADS << ") {\n";
       o << "      const int rl = v / " << CV << ", j = (v - rl * " << CV << ") * " << G << ";\n";
       o << "      const unsigned e = (unsigned)((r0 + rl) * " << L(C) << " + j);\n";

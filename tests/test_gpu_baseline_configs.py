@@ -12,13 +12,22 @@ at a reduced batch, since the oracle needs about 30 s per window of 256 tokens a
   benchmarked step all run.
 
 The bound is rg's device-check metric (validate.rs:690-697): max |gpu - cpu| over max |cpu|, per
-tensor, at most 1e-4. One tensor per attention block is treated apart, by name: the key third of
-the fused q/k/v bias (`blocks.<i>.attn.qkv.b`, elements d..2d). Adding a constant vector to every
-key adds the same amount to every score of a row, which softmax cancels, so the exact gradient of
-that third is zero and both implementations compute rounding noise there. Its gradient is held to
-a noise bound (1e-2 of the tensor's max-norm) and its updated parameters to the 2 * lr that Adam's
-g / (|g| + eps) can move a parameter whose gradient is noise; the q and v thirds of the same
-tensor keep the 1e-4 bound.
+tensor, at most 1e-4, for losses, gradients and moments everywhere. Two exceptions, both named:
+
+* The key third of each attention block's fused q/k/v bias (`blocks.<i>.attn.qkv.b`, elements
+  d..2d). Adding a constant vector to every key adds the same amount to every score of a row,
+  which softmax cancels, so the exact gradient of that third is zero and both implementations
+  compute rounding noise there: its gradient is held to a noise bound (1e-2 of the tensor's
+  max-norm), its q and v thirds to 1e-4.
+* Updated parameters where Adam's first step is ill-conditioned. From zero moments the step is
+  lr * g / (|g| + eps) with eps = 1e-8, whose derivative eps / (|g| + eps)^2 is large where |g| is
+  within a few orders of eps: an element whose gradient is 1e-7 moves by lr times a factor that a
+  1e-9 change of g shifts by about 1e-3, while a gradient that meets the 1e-4 bound may differ by
+  1e-4 of the tensor's largest gradient. So every updated parameter is first held (to 1e-6 of
+  the tensor's max-norm) to the AdamW update of the device's own moments, computed here in
+  float64: the device applies the update right. Against the oracle, elements whose oracle
+  gradient is at least 1e-4 of the tensor's largest are held to 1e-4, and the rest (and the key
+  third above) to the 2 * lr that the step can move a parameter at most.
 """
 import numpy as np
 import pytest
@@ -61,17 +70,33 @@ def check_gradient(path, g, w):
     assert d[k].max() / scale <= 1e-2, f"{path} (key third, rounding noise): {d[k].max() / scale}"
 
 
-def check_parameter(path, g, w):
-    k = key_third(path, g.size)
-    if k is None:
-        assert max_rel(g, w) <= TOL, f"{path}: {max_rel(g, w)}"
-        return
+def adamw_step(p, m, v, t=1, lr=LR, b1=0.9, b2=0.999, eps=1e-8, wd=0.01):
+    """AdamW's update (rg's optim.py:86-113) in float64 from the new moments m, v at step t. The
+    hyper-parameters are the float32 constants the recorded graph holds (1 - 0.999 differs from
+    1 - float32(0.999) by 1.3e-5 relative, which would show in every update)."""
+    lr, b1, b2, eps, wd = (float(np.float32(x)) for x in (lr, b1, b2, eps, wd))
+    p, m, v = (np.asarray(x, np.float64) for x in (p, m, v))
+    d = (m / (1.0 - b1 ** t)) / (np.sqrt(v / (1.0 - b2 ** t)) + eps)
+    if p.ndim >= 2:
+        d = d + wd * p
+    return p - lr * d
+
+
+def check_parameter(path, old, g, w, m_gpu, v_gpu, grad_cpu):
+    """Updated parameter `g` (device) against `w` (oracle); `old` the parameter before the step,
+    `m_gpu`/`v_gpu` the device's new moments, `grad_cpu` the oracle's gradient (mu / (1 - b1))."""
     scale = max(float(np.abs(w).max()), 1e-30)
-    qv = np.ones(g.size, bool)
-    qv[k] = False
+    mine = adamw_step(old, m_gpu, v_gpu)
+    assert np.abs(g - mine).max() / scale <= 1e-6, f"{path}: the update differs from AdamW of the device's own moments"
+    big = np.abs(grad_cpu) >= 1e-4 * max(float(np.abs(grad_cpu).max()), 1e-30)
+    k = key_third(path, g.size)
+    if k is not None:
+        big = big.copy()
+        big.reshape(-1)[k] = False
     d = np.abs(g.astype(np.float64) - w)
-    assert d[qv].max() / scale <= TOL, f"{path} (q and v thirds): {d[qv].max() / scale}"
-    assert d[k].max() <= 2 * LR + 1e-7, f"{path} (key third): {d[k].max()}"
+    if big.any():
+        assert d[big].max() / scale <= TOL, f"{path} (well-conditioned elements): {d[big].max() / scale}"
+    assert d.max() <= 2 * LR + 1e-7, f"{path}: {d.max()}"
 
 
 # ---------------------------------------------------------------------------------------------
@@ -145,10 +170,11 @@ def check_train_step(oracle, model, opt, state, tokens, batch):
     assert len(gpu) == 3 + 3 * n
     assert_bits_equal(gpu[0], cpu[0], "key")
     assert_bits_equal(gpu[1], cpu[1], "step count")
+    before = [t.numpy() for t in F.tree_leaves(state["params"])]
     for k in range(n):
         check_gradient("mu " + names[k], gpu[2 + k], cpu[2 + k])
         check_gradient("nu " + names[k], gpu[2 + n + k], cpu[2 + n + k])
-        check_parameter(names[k], gpu[2 + 2 * n + k], cpu[2 + 2 * n + k])
+        check_parameter(names[k], before[k], gpu[2 + 2 * n + k], cpu[2 + 2 * n + k], gpu[2 + k], gpu[2 + n + k], cpu[2 + k] / 0.1)
     assert max_rel(gpu[-1], cpu[-1]) <= TOL, f"loss: {gpu[-1]} vs {cpu[-1]}"
     return gpu, cpu
 
