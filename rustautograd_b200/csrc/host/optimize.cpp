@@ -1,6 +1,8 @@
 // Restates src/optimize.rs (line references below are to that file).
 #include "optimize.h"
 
+#include <cstring>
+
 #include <algorithm>
 #include <cstdlib>
 #include <functional>
@@ -320,6 +322,36 @@ std::optional<std::pair<Op, std::vector<uint32_t>>> padded_sum_as_concat(const G
 // packed results), so the (..., T, T) tensors between them are never materialised. Values agree
 // with the pattern's to rounding: softmax sums and products run in another order. Only with
 // RGC_FUSED_ATTENTION=1 while the device kernels await validation on a GPU.
+// GPU planning: a slice of a constant is a constant, made at plan time. The causal mask of a
+// GPT is `tril[:t, :t]`: as a plan step its output slot is free for reuse once the mask's
+// broadcast has run, and the allocator hands it to a later step, so row chains must read the
+// materialised (B, H, T, T) broadcast. As a constant it is pinned, and the chains read the
+// (T, T) source through the broadcast, once per row period. The values are the slice's own.
+// Only slices of at most 2^22 elements fold, so constants stay small.
+std::optional<Tensor> slice_of_constant(const Graph& g, uint32_t src, const Op& op, const std::vector<size_t>& shape) {
+  const Node& n = g.nodes[src];
+  if (n.op.kind != OpKind::Const || !n.op.value || shape.empty() || product(shape) > (size_t(1) << 22)) return std::nullopt;
+  const Tensor& t = *n.op.value;
+  const size_t rank = t.shape.size(), es = dtype_size(t.dtype());
+  if (op.starts.size() != rank || shape.size() != rank) return std::nullopt;
+  std::vector<size_t> stride(rank, 1);
+  for (size_t k = rank; k-- > 1;) stride[k - 1] = stride[k] * t.shape[k];
+  Buf out(t.dtype(), product(shape));
+  std::vector<size_t> at(rank, 0);
+  const char* from = (const char*)t.data.data();
+  char* to = (char*)out.data();
+  for (size_t e = 0; e < out.n; ++e) {
+    size_t off = 0;
+    for (size_t k = 0; k < rank; ++k) off += (op.starts[k] + at[k]) * stride[k];
+    std::memcpy(to + e * es, from + off * es, es);
+    for (size_t k = rank; k-- > 0;) {
+      if (++at[k] < shape[k]) break;
+      at[k] = 0;
+    }
+  }
+  return Tensor(shape, std::move(out));
+}
+
 bool fused_attention_enabled() {
   const char* e = getenv("RGC_FUSED_ATTENTION");
   return e && std::string(e) == "1";
@@ -525,6 +557,14 @@ Simplified simplify(const Graph& g, const std::vector<uint32_t>& outputs, bool f
       continue;
     }
     Op op = node.op;
+    if (concat_pads && op.kind == OpKind::Slice && ins.size() == 1) {
+      if (auto folded = slice_of_constant(ng, ins[0], op, node.shape)) {
+        op = Op::make(OpKind::Const);
+        op.value = std::make_shared<const Tensor>(std::move(*folded));
+        ins.clear();
+        r.st.folded += 1;
+      }
+    }
     if (concat_pads && op.kind == OpKind::Add && ins.size() == 2) {
       if (auto c = padded_sum_as_concat(ng, ins[0], ins[1], node.shape, node.dtype)) {
         op = c->first;

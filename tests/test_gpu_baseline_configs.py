@@ -22,12 +22,14 @@ tensor, at most 1e-4, for losses, gradients and moments everywhere. Two exceptio
 * Updated parameters where Adam's first step is ill-conditioned. From zero moments the step is
   lr * g / (|g| + eps) with eps = 1e-8, whose derivative eps / (|g| + eps)^2 is large where |g| is
   within a few orders of eps: an element whose gradient is 1e-7 moves by lr times a factor that a
-  1e-9 change of g shifts by about 1e-3, while a gradient that meets the 1e-4 bound may differ by
-  1e-4 of the tensor's largest gradient. So every updated parameter is first held (to 1e-6 of
-  the tensor's max-norm) to the AdamW update of the device's own moments, computed here in
-  float64: the device applies the update right. Against the oracle, elements whose oracle
-  gradient is at least 1e-4 of the tensor's largest are held to 1e-4, and the rest (and the key
-  third above) to the 2 * lr that the step can move a parameter at most.
+  1e-9 change of g shifts by about 1e-3. So every updated parameter is first held (to 1e-6 of the
+  tensor's max-norm) to the AdamW update of the device's own moments, computed here in float64:
+  the device applies the update right. Against the oracle, a gradient error of up to 1e-4 of the
+  tensor's largest gradient G (what the gradient check allows) moves the step of an element
+  with gradient g by at most lr * eps * 1e-4 G / g^2; that stays within 1e-4 of the parameter
+  tensor's max-norm P wherever g^2 >= lr * eps * G / P. Elements above three times that bound
+  are held to 1e-4, the rest (and the key third above) to the 2 * lr that one step can move a
+  parameter at most.
 """
 import numpy as np
 import pytest
@@ -88,7 +90,8 @@ def check_parameter(path, old, g, w, m_gpu, v_gpu, grad_cpu):
     scale = max(float(np.abs(w).max()), 1e-30)
     mine = adamw_step(old, m_gpu, v_gpu)
     assert np.abs(g - mine).max() / scale <= 1e-6, f"{path}: the update differs from AdamW of the device's own moments"
-    big = np.abs(grad_cpu) >= 1e-4 * max(float(np.abs(grad_cpu).max()), 1e-30)
+    G = max(float(np.abs(grad_cpu).max()), 1e-30)
+    big = np.abs(grad_cpu) >= 3.0 * np.sqrt(LR * 1e-8 * G / scale)
     k = key_third(path, g.size)
     if k is not None:
         big = big.copy()
