@@ -3,7 +3,6 @@
 
 #include <algorithm>
 #include <cstdio>
-#include <cstdlib>
 #include <functional>
 #include <map>
 #include <sstream>
@@ -191,224 +190,6 @@ bool make_row_kernel(const rg::Plan& plan, const rg::RowChain& c, RowKernel* k, 
   if (binds.size() > (size_t)JIT_MAX_IN || k->out_slots.size() > (size_t)JIT_MAX_OUT) {
     *why = "too many operands";
     return false;
-  }
-
-  // Register form: for rows of at most 256 float32 (128 float64) elements whose kept full values
-  // fit in registers, eight lanes own a row (lane k holds elements k, k + 8, ...: exactly the
-  // classes of rg's eight running sums), four rows per warp, and every value stays in registers:
-  // no shared memory and no block barriers, reductions by warp shuffles. The arithmetic and its
-  // order are the shared-memory form's. RGC_ROW_REGS=0 keeps the shared-memory form.
-  {
-    const long long NI = (C + 7) / 8, C8 = C / 8 * 8;
-    const char* env_regs = getenv("RGC_ROW_REGS");
-    const bool regs_on = !(env_regs && std::string(env_regs) == "0");
-    const long long budget = dt == DType::F64 ? 32 : 64;
-    if (regs_on && C <= (dt == DType::F64 ? 128 : 256) && (long long)nbuf * NI <= budget) {
-      std::ostringstream o;
-      auto in_ptr = [&](int b) { return "((const " + T + "*)a.in[" + I(b) + "])"; };
-      auto out_ptr = [&](int q) { return "((" + T + "*)a.out[" + I(q) + "])"; };
-      auto kept = [&](int buf) { return "kb" + I(buf); };
-      auto cvar = [&](int col) { return "c" + I(col); };
-      std::vector<int> loaded(binds.size(), -1);
-      o << "(const ElemArgs a) {\n";
-      o << "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n";
-      o << "  asm volatile(\"griddepcontrol.launch_dependents;\" ::: \"memory\");\n";
-      o << "  const int lane = threadIdx.x & 31, k8 = lane & 7, sub = lane >> 3;\n";
-      o << "  const int wrow = (threadIdx.x >> 5) * 4 + sub;\n";
-      o << "  (void)k8;\n";
-      for (size_t b = 0; b < binds.size(); ++b)
-        if (binds[b].in.kind == RowInput::Splat) o << "  const " << T << " sp" << b << " = " << in_ptr((int)b) << "[0];\n";
-      o << "  const long long R = a.n;\n";
-      o << "  for (long long r0 = (long long)blockIdx.x * 32LL; r0 < R; r0 += (long long)gridDim.x * 32LL) {\n";
-      // Lanes of rows past the end still take part in the shuffles, on the last row, and store nothing.
-      o << "    const bool ok = r0 + wrow < R;\n";
-      o << "    const long long rr = ok ? r0 + wrow : R - 1;\n";
-      for (int b = 0; b < nbuf; ++b) o << "    " << T << " " << kept(b) << "[" << NI << "];\n";
-      for (int c = 0; c < ncol; ++c) o << "    " << T << " " << cvar(c) << " = (" << T << ")0;\n";
-
-      // Loads binding b for the element at e (full space) or for the row (per-row space).
-      auto load = [&](int b, int s, bool full_space, const std::string& e) -> std::string {
-        Bind& bd = binds[b];
-        const std::string x = "x" + I(b);
-        std::ostringstream l;
-        switch (bd.in.kind) {
-          case RowInput::Full:
-            if (full_space && bd.buf >= 0 && loaded[b] >= 0 && loaded[b] < s) {
-              l << "        const " << T << " " << x << " = " << kept(bd.buf) << "[i];\n";
-            } else if (full_space) {
-              l << "        const " << T << " " << x << " = " << in_ptr(b) << "[" << e << "];\n";
-              if (bd.buf >= 0) {
-                l << "        " << kept(bd.buf) << "[i] = " << x << ";\n";
-                loaded[b] = s;
-              }
-            } else {
-              l << "        const " << T << " " << x << " = " << in_ptr(b) << "[rr];\n";
-            }
-            break;
-          case RowInput::Column:
-            l << "        const " << T << " " << x << " = " << in_ptr(b) << "[rr];\n";
-            break;
-          case RowInput::Splat:
-            l << "        const " << T << " " << x << " = sp" << b << ";\n";
-            break;
-          case RowInput::Periodic:
-            l << "        " << T << " " << x << ";\n        rg_row_fill<" << T << ", 1>(&" << x << ", " << in_ptr(b) << ", " << e << ", a.row[" << b << "]);\n";
-            break;
-          default:
-            l << "        " << T << " " << x << ";\n        rg_bc_fill<" << T << ", 1>(&" << x << ", " << in_ptr(b) << ", a.bc[" << bd.bc << "], " << e << ");\n";
-            break;
-        }
-        return l.str();
-      };
-      // The members of stage s, one element (or the row) at a time.
-      bool ok_members = true;
-      auto members = [&](int s, bool full_space, std::ostringstream& l) {
-        for (size_t m = 0; m < ms.size(); ++m) {
-          if (ms[m].stage != s) continue;
-          const Member& mb = ms[m];
-          const std::string P0 = "m" + I((long long)m) + "_";
-          for (size_t q = 0; q < mb.ins.size(); ++q) {
-            const RowInput& in = mb.ins[q];
-            std::string dst = mb.in_reg[q] < 0 ? P0 + "i" + I((long long)q) : P0 + "r" + I(mb.in_reg[q]);
-            std::string src;
-            if (in.kind != RowInput::Value) {
-              src = "x" + I(member_bind[m][q]);
-            } else {
-              const Member& pm = ms[in.producer];
-              const Val& v = vals[{in.producer, in.output}];
-              // (A reduction's output has no register of a member program: it is read as a
-              // per-row value, always in a later stage.)
-              auto preg = [&] { return "m" + I((long long)in.producer) + "_r" + I((long long)pm.spec.out_regs[in.output]); };
-              if (pm.role != Role::Full) {
-                src = pm.stage == s ? preg() : cvar(v.col);
-              } else if (!full_space) {
-                ok_members = false;  // a per-row member reading a full value: not a chain shape
-              } else {
-                src = pm.stage == s ? preg() : kept(v.buf) + "[i]";
-              }
-            }
-            l << "        const " << T << " " << dst << " = " << src << ";\n";
-          }
-          for (auto& op : mb.spec.ops) {
-            std::vector<std::string> args;
-            for (auto& x : op.args) args.push_back(P0 + (x.reg ? "r" : "i") + I((long long)x.idx));
-            l << "        const " << T << " " << P0 << "r" << op.reg << " = " << elem_expr(dt, op.op, args) << ";\n";
-          }
-        }
-      };
-
-      for (int s = 0; s < stages; ++s) {
-        Role role = Role::Full;
-        for (auto& mb : ms)
-          if (mb.stage == s) role = mb.role;
-        std::vector<int> used;
-        for (size_t m = 0; m < ms.size(); ++m)
-          if (ms[m].stage == s)
-            for (int b : member_bind[m])
-              if (b >= 0 && std::find(used.begin(), used.end(), b) == used.end()) used.push_back(b);
-        o << "    // stage " << s << "\n";
-        if (s > 0) o << "    __syncwarp();\n";
-        if (role == Role::Full) {
-          std::ostringstream l;
-          for (int b : used) l << load(b, s, true, "e");
-          members(s, true, l);
-          for (size_t m = 0; m < ms.size(); ++m) {
-            if (ms[m].stage != s) continue;
-            for (size_t q = 0; q < ms[m].writes.size(); ++q) {
-              const Val& v = vals[{m, q}];
-              const std::string r = "m" + I((long long)m) + "_r" + I((long long)ms[m].spec.out_regs[q]);
-              if (v.buf >= 0) l << "        " << kept(v.buf) << "[i] = " << r << ";\n";
-              if (v.out >= 0) l << "        if (ok) " << out_ptr(v.out) << "[e] = " << r << ";\n";
-            }
-          }
-          o << "    #pragma unroll\n    for (int i = 0; i < " << NI << "; ++i) {\n";
-          o << "      const int j = k8 + 8 * i;\n      if (j < " << C << ") {\n";
-          o << "        const unsigned e = (unsigned)(rr * " << L(C) << " + j);\n";
-          o << l.str();
-          o << "      }\n    }\n";
-        } else if (role == Role::Col) {
-          std::ostringstream l;
-          for (int b : used) l << load(b, s, false, "(unsigned)rr");
-          members(s, false, l);
-          for (size_t m = 0; m < ms.size(); ++m) {
-            if (ms[m].stage != s) continue;
-            for (size_t q = 0; q < ms[m].writes.size(); ++q) {
-              const Val& v = vals[{m, q}];
-              const std::string r = "m" + I((long long)m) + "_r" + I((long long)ms[m].spec.out_regs[q]);
-              l << "        " << cvar(v.col) << " = " << r << ";\n";
-              if (v.out >= 0) l << "        if (ok && k8 == 0) " << out_ptr(v.out) << "[rr] = " << r << ";\n";
-            }
-          }
-          o << "    {\n" << l.str() << "    }\n";
-        } else {
-          size_t m = 0;
-          while (ms[m].stage != s) ++m;
-          const Member& mb = ms[m];
-          const RowInput& in = mb.ins[0];
-          std::string arr;
-          if (in.kind == RowInput::Value) {
-            arr = kept(vals[{in.producer, in.output}].buf);
-          } else {
-            const int b = member_bind[m][0];
-            Bind& bd = binds[b];
-            if (bd.buf < 0) {
-              *why = "a reduction input without a register array";
-              return false;
-            }
-            if (loaded[b] < 0) {
-              o << "    #pragma unroll\n    for (int i = 0; i < " << NI << "; ++i) {\n      const int j = k8 + 8 * i;\n";
-              o << "      if (j < " << C << ") " << kept(bd.buf) << "[i] = " << in_ptr(b) << "[(unsigned)(rr * " << L(C) << " + j)];\n    }\n";
-              loaded[b] = s;
-            }
-            arr = kept(bd.buf);
-          }
-          const Val& v = vals[{m, 0}];
-          o << "    {\n";
-          if (mb.red == rg::ReduceKind::Sum) {
-            o << "      " << T << " acc = (" << T << ")0;\n";
-            o << "      #pragma unroll\n      for (int i = 0; i < " << C8 / 8 << "; ++i) acc = acc + " << arr << "[i];\n";
-            o << "      " << T << " out = (" << T << ")0;\n";
-            o << "      #pragma unroll\n      for (int q = 0; q < 8; ++q) out = out + __shfl_sync(0xffffffffu, acc, (sub << 3) + q);\n";
-            if (C8 < C) {
-              o << "      const " << T << " tail = k8 < " << (C - C8) << " ? " << arr << "[" << C8 / 8 << "] : (" << T << ")0;\n";
-              o << "      #pragma unroll\n      for (int q = 0; q < " << (C - C8) << "; ++q) out = out + __shfl_sync(0xffffffffu, tail, (sub << 3) + q);\n";
-            }
-          } else {
-            const bool mx = mb.red == rg::ReduceKind::Max;
-            const std::string gt = mx ? ">" : "<", ge = mx ? ">=" : "<=";
-            const std::string inf = dt == DType::F64 ? "__longlong_as_double(0x7ff0000000000000LL)" : "__int_as_float(0x7f800000)";
-            o << "      " << T << " acc = " << (mx ? "-" : "") << inf << ";\n      int idx = -1;\n";
-            o << "      #pragma unroll\n      for (int i = 0; i < " << NI << "; ++i) {\n        const int j = k8 + 8 * i;\n";
-            o << "        if (j < " << C << ") {\n          const " << T << " x = " << arr << "[i];\n";
-            o << "          if (!(acc " << gt << " x) && x " << ge << " acc) idx = j;\n";
-            o << "          acc = " << (mx ? "rg_max" : "rg_min") << "<" << T << ">(acc, x);\n        }\n      }\n";
-            o << "      bool nan = false;\n      " << T << " out = acc;\n      int at = idx;\n";
-            o << "      #pragma unroll\n      for (int q = 0; q < 8; ++q) {\n";
-            o << "        const " << T << " y = __shfl_sync(0xffffffffu, acc, (sub << 3) + q);\n";
-            o << "        const int yi = __shfl_sync(0xffffffffu, idx, (sub << 3) + q);\n";
-            o << "        nan = nan || y != y;\n";
-            o << "        if (yi >= 0 && (at < 0 || y " << gt << " out || (y == out && yi > at))) { out = y; at = yi; }\n";
-            o << "      }\n";
-            o << "      if (nan) out = rg_nan(out);\n";
-          }
-          o << "      " << cvar(v.col) << " = out;\n";
-          if (v.out >= 0) o << "      if (ok && k8 == 0) " << out_ptr(v.out) << "[rr] = out;\n";
-          o << "    }\n";
-        }
-      }
-      o << "  }\n}\n";
-      if (ok_members) {
-        std::string body = o.str();
-        char nm[64];
-        snprintf(nm, sizeof nm, "rg_rowr_%016llx", (unsigned long long)std::hash<std::string>{}(body));
-        k->name = nm;
-        k->source = "extern \"C\" __global__ void __launch_bounds__(" + I(ROW_THREADS) + ") " + k->name + body;
-        k->rows = R;
-        k->rows_per_block = 32;
-        k->smem = 0;
-        return true;
-      }
-    }
   }
 
   // Geometry: a row pitch of 8 (mod 32) 4-byte words, so that the eight lanes summing each of

@@ -94,7 +94,6 @@ struct RgBlock {
 inline RgBlock* rg_block = nullptr;
 
 inline void __syncthreads() { rg_block->block.wait(); }
-inline void __syncwarp(unsigned = 0xffffffffu) { rg_block->warps[(int)threadIdx.x / 32]->wait(); }
 
 template <typename T> T __shfl_sync(unsigned, T v, int src) {
   const int warp = (int)threadIdx.x / 32, lane = (int)threadIdx.x % 32;

@@ -13,11 +13,8 @@ from helpers import assert_bits_equal, compile_and_compare
 pytestmark = pytest.mark.gpu
 
 
-def outputs(fn, args, chains, monkeypatch, form="registers"):
-    """Outputs with chains off, or on in the register form (the default where rows fit) or the
-    shared-memory form (RGC_ROW_REGS=0)."""
+def outputs(fn, args, chains, monkeypatch):
     monkeypatch.setenv("RGC_ROW_CHAINS", "1" if chains else "0")
-    monkeypatch.setenv("RGC_ROW_REGS", "0" if form == "shared" else "1")
     c = F.compile(fn, args, validate="none", device="cuda")
     leaves = [F.tensor(x) for x in F.flatten(args)[0]]
     return [F.Tensor(t).numpy() for t in c._n.call([t._t for t in leaves])], c
@@ -36,11 +33,10 @@ def gpt(d=64, heads=4, layers=2, block=32, batch=16):
 def test_gpt_step_identical_with_and_without_row_chains(cuda, monkeypatch, cfg):
     F.use(cuda, "cuda")
     fn, args = gpt(**cfg)
+    on, _ = outputs(fn, args, True, monkeypatch)
     off, _ = outputs(fn, args, False, monkeypatch)
-    for form in ("registers", "shared"):
-        on, _ = outputs(fn, args, True, monkeypatch, form)
-        for k, (a, b) in enumerate(zip(on, off)):
-            assert_bits_equal(a, b, f"output {k} ({form} form)")
+    for k, (a, b) in enumerate(zip(on, off)):
+        assert_bits_equal(a, b, f"output {k}")
 
 
 @pytest.mark.parametrize("dtype,cols", [("float32", 256), ("float32", 10), ("float64", 96), ("float64", 7)])
@@ -57,11 +53,10 @@ def test_softmax_layernorm_identical_with_and_without_row_chains(cuda, monkeypat
         y = (x - mu) / (((x - mu) ** 2).mean(axis=-1, keepdims=True) + 1e-5).sqrt() * g
         return (p * y).sum() + F.nn.log_softmax(y).min()
     fn = F.value_and_grad(f, argnums=(0, 1))
+    on, _ = outputs(fn, (x, g, mask), True, monkeypatch)
     off, _ = outputs(fn, (x, g, mask), False, monkeypatch)
-    for form in ("registers", "shared"):
-        on, _ = outputs(fn, (x, g, mask), True, monkeypatch, form)
-        for k, (a, b) in enumerate(zip(on, off)):
-            assert_bits_equal(a, b, f"output {k} ({form} form)")
+    for k, (a, b) in enumerate(zip(on, off)):
+        assert_bits_equal(a, b, f"output {k}")
 
 
 def test_row_extrema_equal_the_interpreter(cuda, oracle, monkeypatch):

@@ -57,12 +57,9 @@ extern "C" void rg_emulate(const ElemArgs* a, int grid) {
 """
 
 
-@pytest.fixture(autouse=True, params=["registers", "shared"])
-def _chains(oracle, monkeypatch, request):
-    """Both kernel forms: rows held in registers (the default where they fit) and rows staged
-    in shared memory (RGC_ROW_REGS=0, and every row too long for registers)."""
+@pytest.fixture(autouse=True)
+def _chains(oracle, monkeypatch):
     monkeypatch.setenv("RGC_ROW_CHAINS", "1")
-    monkeypatch.setenv("RGC_ROW_REGS", "1" if request.param == "registers" else "0")
     F.use(oracle, "cpu")
     yield
 
