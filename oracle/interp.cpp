@@ -847,23 +847,26 @@ template <typename T> void attn_bwd(const Instr& i, std::vector<Buf>& s) {
   const AttnDims a = attn_dims(i);
   const T c = (T)i.op.value->data.get(0), fill = (T)i.op.value->data.get(1);
   const T *Q = S<T>(s[i.args[0]]), *K = S<T>(s[i.args[1]]), *V = S<T>(s[i.args[2]]), *M = S<T>(s[i.args[3]]);
-  const T *ST = S<T>(s[i.args[4]]), *DO = S<T>(s[i.args[5]]);
+  // args[4]: the forward's packed output, (..., T, dv + 2) = O, row max, row exp-sum.
+  const T *FW = S<T>(s[i.args[4]]), *DO = S<T>(s[i.args[5]]);
   T* out = S<T>(s[i.dst]);
-  const size_t w = 2 * a.d + a.dv;
+  const size_t w = 2 * a.d + a.dv, fw = a.dv + 2;
   std::fill(out, out + a.batch * a.t * w, (T)0);
   std::vector<T> p(a.t), dp(a.t);
   for (size_t b = 0; b < a.batch; ++b) {
     const T *q = Q + b * a.t * a.d, *k = K + b * a.t * a.d, *v = V + b * a.t * a.dv, *dout = DO + b * a.t * a.dv;
     T* g = out + b * a.t * w;
     for (size_t r = 0; r < a.t; ++r) {
-      const T m = ST[(b * a.t + r) * 2], sum = ST[(b * a.t + r) * 2 + 1];
+      const T* o = FW + (b * a.t + r) * fw;
+      const T m = o[a.dv], sum = o[a.dv + 1];
+      // D = sum_j P_rj dP_rj = dO_r . O_r (O_r = sum_j P_rj v_j).
       T dsum = (T)0;
+      for (size_t e = 0; e < a.dv; ++e) dsum = dsum + dout[r * a.dv + e] * o[e];
       for (size_t j = 0; j < a.t; ++j) {
         p[j] = std::exp(attn_score(q, k, M + r * a.t, r, j, a.d, c, fill) - m) / sum;
         T acc = (T)0;
         for (size_t e = 0; e < a.dv; ++e) acc = acc + dout[r * a.dv + e] * v[j * a.dv + e];
         dp[j] = acc;
-        dsum = dsum + p[j] * dp[j];
       }
       for (size_t j = 0; j < a.t; ++j) {
         const T ds = M[r * a.t + j] != (T)0 ? p[j] * (dp[j] - dsum) / c : (T)0;

@@ -177,11 +177,13 @@ __device__ __forceinline__ long long fd_off(const FDims& s, unsigned e) {
 
 template <typename T> __global__ void k_gather32(T* __restrict__ dst, const T* __restrict__ src, FDims s, long long base, unsigned n) {
   pdl_wait();
+#pragma unroll 4
   for (unsigned e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) dst[e] = src[base + fd_off(s, e)];
 }
 
 template <typename T> __global__ void k_scatter32(T* __restrict__ dst, const T* __restrict__ src, FDims s, long long base, unsigned n) {
   pdl_wait();
+#pragma unroll 4
   for (unsigned e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) dst[base + fd_off(s, e)] = src[e];
 }
 
@@ -190,6 +192,9 @@ template <typename T> __global__ void k_scatter32(T* __restrict__ dst, const T* 
 template <typename VT, int V>
 __global__ void k_gather_vec(VT* __restrict__ dst, const VT* __restrict__ src, FDims s, long long base, unsigned nv) {
   pdl_wait();
+  // Unrolled: with one wave of blocks each thread copies many vectors, and the loads of several
+  // iterations are issued before their stores (the pointers do not alias).
+#pragma unroll 4
   for (unsigned q = blockIdx.x * blockDim.x + threadIdx.x; q < nv; q += gridDim.x * blockDim.x)
     dst[q] = src[(base + fd_off(s, q * V)) / V];
 }
@@ -197,6 +202,7 @@ __global__ void k_gather_vec(VT* __restrict__ dst, const VT* __restrict__ src, F
 template <typename VT, int V>
 __global__ void k_scatter_vec(VT* __restrict__ dst, const VT* __restrict__ src, FDims s, long long base, unsigned nv) {
   pdl_wait();
+#pragma unroll 4
   for (unsigned q = blockIdx.x * blockDim.x + threadIdx.x; q < nv; q += gridDim.x * blockDim.x)
     dst[(base + fd_off(s, q * V)) / V] = src[q];
 }

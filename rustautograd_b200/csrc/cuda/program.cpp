@@ -23,6 +23,7 @@
 #include <unordered_map>
 #include <vector>
 
+#include "attention.cuh"
 #include "blob.h"
 #include "dist.h"
 #include "gemm_tc.cuh"
@@ -593,6 +594,9 @@ struct Builder {
       case OpKind::KeySplit:
         l.run = [=](Ctx& c) { key_split((int32_t*)c.f->ptr[dst], (const int32_t*)c.f->ptr[a[0]], n / 2, c.s); };
         return l;
+      case OpKind::AttnFwd:
+      case OpKind::AttnBwd:
+        return attention(i);
       case OpKind::Scan:
       case OpKind::While:
       case OpKind::Cond:
@@ -600,6 +604,38 @@ struct Builder {
       default:
         throw std::runtime_error(std::string("the CUDA device has no kernel for ") + i.op.name());
     }
+  }
+
+  // The device's fused attention (graph.h AttnFwd / AttnBwd; attention.cuh).
+  Lowered attention(const Instr& i) {
+    Lowered l;
+    const auto& qs = i.arg_shapes[0];
+    const size_t r = qs.size();
+    AttnShape as;
+    as.t = (int)qs[r - 2];
+    as.d = (int)qs[r - 1];
+    as.dv = (int)i.arg_shapes[2][r - 1];
+    as.batch = (long long)(rg::product(qs) / (qs[r - 2] * qs[r - 1]));
+    as.c = (float)i.op.value->data.get(0);
+    as.fill = (float)i.op.value->data.get(1);
+    if (i.dtype != DType::F32 || (!attention_tc_supported(as) && as.t > 1024))
+      throw std::runtime_error(std::string("the CUDA device has no kernel for ") + i.op.name() + " of this dtype or length");
+    attention_init();
+    const auto a = i.args;
+    const size_t dst = i.dst;
+    if (i.op.kind == OpKind::AttnFwd) {
+      l.run = [=](Ctx& c) {
+        attention_fwd((float*)c.f->ptr[dst], (const float*)c.f->ptr[a[0]], (const float*)c.f->ptr[a[1]], (const float*)c.f->ptr[a[2]],
+                      (const float*)c.f->ptr[a[3]], as, c.f->prog->tc_error, c.s);
+      };
+    } else {
+      l.kernels = 2;
+      l.run = [=](Ctx& c) {
+        attention_bwd((float*)c.f->ptr[dst], (const float*)c.f->ptr[a[0]], (const float*)c.f->ptr[a[1]], (const float*)c.f->ptr[a[2]],
+                      (const float*)c.f->ptr[a[3]], (const float*)c.f->ptr[a[4]], (const float*)c.f->ptr[a[5]], as, c.f->prog->tc_error, c.s);
+      };
+    }
+    return l;
   }
 
   // plan.rs:1453-1493
@@ -1219,7 +1255,7 @@ void launch_plan(rgc_exec* e) {
 void check_tc_error(rgc_exec* e) {
   int code = 0;
   if (cudaMemcpy(&code, e->owner->p->tc_error, sizeof code, cudaMemcpyDeviceToHost) == cudaSuccess && code)
-    mark_failed(e, "tensor-core GEMM pipeline wait timed out (stage " + std::to_string(code) + ")");
+    mark_failed(e, "tensor-core kernel pipeline wait timed out (stage " + std::to_string(code) + ")");
 }
 
 void check_async(rgc_exec* e) {

@@ -507,7 +507,7 @@ std::vector<size_t> Graph::infer(const Op& op, const std::vector<std::vector<siz
     case OpKind::Custom: case OpKind::AllReduce: return s[0];
     case OpKind::AttnFwd: case OpKind::AttnBwd: {
       // q (..., T, d), k (..., T, d), v (..., T, dv) with the same leading extents, mask (T, T);
-      // AttnBwd also stats (..., T, 2) and dO (..., T, dv).
+      // AttnBwd also the forward's packed output (..., T, dv + 2) and dO (..., T, dv).
       const auto &q = s[0], &k = s[1], &v = s[2], &m = s[3];
       size_t r = q.size();
       bool ok = r >= 2 && k.size() == r && v.size() == r && m.size() == 2;
@@ -516,7 +516,7 @@ std::vector<size_t> Graph::infer(const Op& op, const std::vector<std::vector<siz
       ok = ok && k[r - 2] == t && v[r - 2] == t && k[r - 1] == d && m[0] == t && m[1] == t;
       if (ok && op.kind == OpKind::AttnBwd) {
         std::vector<size_t> st = q, dout = v;
-        st[r - 1] = 2;
+        st[r - 1] = dv + 2;
         ok = s[4] == st && s[5] == dout;
       }
       if (!ok || !op.value || op.value->n() != 2) {

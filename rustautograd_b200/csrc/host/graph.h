@@ -36,8 +36,11 @@ enum class OpKind : uint8_t {
   // Fused attention (no counterpart in rg; produced only by the device's graph rewrite).
   // AttnFwd(q, k, v, mask) with value = [c, fill]: per batch entry, Z = where(mask, q k^T / c,
   // fill), softmax along the last axis (max-subtracted), O = P v; the result packs O with each
-  // row's max and exp-sum: (..., T, dv + 2). AttnBwd(q, k, v, mask, stats, dO): the gradients
-  // of O with respect to q, k and v for the cotangent dO, packed as (..., T, 2 d + dv).
+  // row's max and exp-sum: (..., T, dv + 2). AttnBwd(q, k, v, mask, fwd, dO), with `fwd` that
+  // packed forward output: the gradients of O with respect to q, k and v for the cotangent dO,
+  // packed as (..., T, 2 d + dv). With P the softmax rebuilt from the row statistics and
+  // D = rowsum(dO * O): dS = P (dO v^T - D) / c where the mask is nonzero (0 elsewhere),
+  // dq = dS k, dk = dS^T q, dv = P^T dO.
   AttnFwd,
   AttnBwd,
 };

@@ -310,18 +310,6 @@ std::optional<std::pair<Op, std::vector<uint32_t>>> padded_sum_as_concat(const G
 }
 
 
-// ---- fused attention (the device's own rewrite, no counterpart in rg) ----
-//
-// rg's attention layer and its autodiff leave this pattern in the optimised graph (per layer):
-//   S = matmul_t(q, k; tb)  S1 = S / c  Z = where(mask, S1, fill)  m = max(Z, -1, keepdims)
-//   E = exp(Z - m)  s = sum(E, -1, keepdims)  P = E / s  O = P @ v
-//   dv = matmul_t(P, dO; ta)  dP = matmul_t(dO, v; tb)
-//   dE = dP / s + sum(((-dP) * E) / (s * s), -1, keepdims)  dS = where(mask, dE * E, 0) / c
-//   dq = matmul_t(dS, transpose(k); tb)  dk = transpose(matmul_t(q, dS; ta))
-// It becomes AttnFwd / AttnBwd (q, k, v, the (T, T) mask; O and dq, dk, dv as slices of their
-// packed results), so the (..., T, T) tensors between them are never materialised. Values agree
-// with the pattern's to rounding: softmax sums and products run in another order. Only with
-// RGC_FUSED_ATTENTION=1 while the device kernels await validation on a GPU.
 // GPU planning: a slice of a constant is a constant, made at plan time. The causal mask of a
 // GPT is `tril[:t, :t]`: as a plan step its output slot is free for reuse once the mask's
 // broadcast has run, and the allocator hands it to a later step, so row chains must read the
@@ -352,6 +340,18 @@ std::optional<Tensor> slice_of_constant(const Graph& g, uint32_t src, const Op& 
   return Tensor(shape, std::move(out));
 }
 
+// ---- fused attention (the device's own rewrite, no counterpart in rg) ----
+//
+// rg's attention layer and its autodiff leave this pattern in the optimised graph (per layer):
+//   S = matmul_t(q, k; tb)  S1 = S / c  Z = where(mask, S1, fill)  m = max(Z, -1, keepdims)
+//   E = exp(Z - m)  s = sum(E, -1, keepdims)  P = E / s  O = P @ v
+//   dv = matmul_t(P, dO; ta)  dP = matmul_t(dO, v; tb)
+//   dE = dP / s + sum(((-dP) * E) / (s * s), -1, keepdims)  dS = where(mask, dE * E, 0) / c
+//   dq = matmul_t(dS, transpose(k); tb)  dk = transpose(matmul_t(q, dS; ta))
+// It becomes AttnFwd / AttnBwd (q, k, v, the (T, T) mask; O and dq, dk, dv as slices of their
+// packed results), so the (..., T, T) tensors between them are never materialised. Values agree
+// with the pattern's to rounding: softmax sums and products run in another order. Only with
+// RGC_FUSED_ATTENTION=1 while the device kernels await validation on a GPU.
 bool fused_attention_enabled() {
   const char* e = getenv("RGC_FUSED_ATTENTION");
   return e && std::string(e) == "1";
@@ -725,7 +725,7 @@ Simplified fuse_attention(const Simplified& in) {
       uint32_t a = ng.add(f, {map[m.q], map[m.k], map[m.v], mask[mi]});
       const size_t dv = g.shape(m.v).back();
       map[i] = slice_last(a, 0, dv);
-      stats[mi] = slice_last(a, dv, dv + 2);
+      stats[mi] = a;  // the backward reads O and the row statistics from the packed output
       mark(false);
       r.st.simplified += 1;
       continue;
