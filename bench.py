@@ -12,7 +12,8 @@ all-reduce when N > 1, and the AdamW update.
 Other workloads (--config): gpt-d256-l6 (the 1-GPU companion of config 5), gpt-d128-l4
 (config 4), adamw-c2 (config 2: the AdamW update of four large tensors, HBM-bound),
 linreg-c1 (config 1), chain-c3 (config 3: matrix chains reordered by the e-graph search),
-gemm-mlp (one 131072 x 512 x 2048 product of config 5, for profiling).
+gemm-mlp (one 131072 x 512 x 2048 product of config 5, for profiling), gpt-d512-l1 (one layer of
+the d512 model at batch 64, for profiling).
 
 `value` is device time (CUDA events inside the run loop, state already in HBM); `e2e` is the
 same run through the C-ABI run call from host buffers (state and data copied in, state and the
@@ -270,6 +271,9 @@ WORKLOADS = {
     "gpt-d512-l12": Gpt("gpt-d512-l12", vocab=96, block=256, d=512, heads=8, layers=12, batch=512, tokens="zipf"),
     "gpt-d256-l6": Gpt("gpt-d256-l6", vocab=96, block=256, d=256, heads=8, layers=6, batch=64, tokens="zipf"),
     "gpt-d128-l4": Gpt("gpt-d128-l4", vocab=96, block=128, d=128, heads=4, layers=4, batch=64, tokens="uniform"),
+    # One d512 layer at batch 64, for ncu captures of the kernels of the benchmarked step on a case
+    # that holds a few GB (each (B, H, T, T) tensor is 134 MB, above L2).
+    "gpt-d512-l1": Gpt("gpt-d512-l1", vocab=96, block=256, d=512, heads=8, layers=1, batch=64, tokens="zipf"),
     "adamw-c2": AdamW("adamw-c2"),
     "linreg-c1": LinReg("linreg-c1"),
     "gemm-mlp": Gemm("gemm-mlp", m=131072, k=512, n=2048),

@@ -173,8 +173,6 @@ __global__ void k_attn_dkdv_simt(float* __restrict__ out, const float* __restric
 // Tensor-core building blocks
 // ---------------------------------------------------------------------------------------------
 
-constexpr int TC_THREADS = 128;
-
 // Byte offset of element (row, k) in a K-major tile of R rows whose K extent is cut into 32-wide
 // blocks (R x 128 bytes each): 8-row groups of 1024 bytes, 128 bytes per row, and the row's
 // 16-byte chunk (k % 32) / 4 stored at chunk position ((k % 32) / 4) ^ (row % 8) — the 128-byte
@@ -189,7 +187,7 @@ __device__ __forceinline__ float tf32_lo(float x) { return x - tf32_trunc(x); }
 // aligned rows) into K-major hi / lo tiles.
 __device__ __forceinline__ void stage(uint8_t* hi, uint8_t* lo, const float* src, int R, int K, long long ld) {
   const int k4 = K >> 2;
-  for (int i = threadIdx.x; i < R * k4; i += TC_THREADS) {
+  for (int i = threadIdx.x; i < R * k4; i += blockDim.x) {
     const int row = i / k4, col = (i - row * k4) << 2;
     const float4 x = *(const float4*)(src + row * ld + col);
     const uint32_t off = kmaj(R, row, col);
@@ -202,7 +200,7 @@ __device__ __forceinline__ void stage(uint8_t* hi, uint8_t* lo, const float* src
 // source columns [0, Cs) its rows (a K-major tile of Cs rows over K = Rs).
 __device__ __forceinline__ void stage_t(uint8_t* hi, uint8_t* lo, const float* src, int Rs, int Cs, long long ld) {
   const int c4 = Cs >> 2;
-  for (int i = threadIdx.x; i < Rs * c4; i += TC_THREADS) {
+  for (int i = threadIdx.x; i < Rs * c4; i += blockDim.x) {
     const int j = i / c4, col = (i - j * c4) << 2;
     const float4 x = *(const float4*)(src + j * ld + col);
     const float xs[4] = {x.x, x.y, x.z, x.w};
@@ -236,14 +234,6 @@ __device__ __forceinline__ void mma3(uint32_t d, uint32_t ah, uint32_t al, uint3
 
 __device__ __forceinline__ void proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-template <int T, int D> struct FwdLayout {
-  static constexpr int QB = 128 * D * 4, KB = T * D * 4, VB = D * T * 4, PB = 128 * 32 * 4;
-  static constexpr int PHASE1 = 2 * QB + 2 * KB, PHASE2 = 2 * VB + 4 * PB;
-  static constexpr int REGION = PHASE1 > PHASE2 ? PHASE1 : PHASE2;
-  static constexpr int SMEM = 1024 + REGION + 128;
-  static constexpr uint32_t TCOLS = T + D <= 256 ? 256 : 512;
-};
-
 // Waits for `phase` of `bar`, bounded; every thread of the CTA calls it, and the outcome is
 // made uniform across the CTA (a barrier, then the shared abort flag), so that the threads
 // leave their loops together.
@@ -253,31 +243,50 @@ __device__ __forceinline__ bool cta_wait(uint64_t* bar, uint32_t phase, volatile
   return *abort == 0;
 }
 
-// Forward, one CTA per (batch entry, 128 query rows).
+constexpr int FWD_THREADS = 512;
+
+template <int T, int D> struct FwdLayout {
+  static constexpr int QB = 128 * D * 4, KB = T * D * 4;
+  static constexpr int VB = D * 128 * 4;   // v^T of one half of the keys: D rows over 128 keys
+  static constexpr int EB = 128 * 32 * 4;  // one 32-key chunk of E
+  static constexpr int PHASE1 = 2 * QB + 2 * KB, PHASE2 = 2 * VB + 8 * EB;
+  static constexpr int REGION = PHASE1 > PHASE2 ? PHASE1 : PHASE2;
+  static constexpr int SMEM = 1024 + REGION + 2 * 4 * 128 * 4 + 128;
+  static constexpr uint32_t TCOLS = T + D <= 256 ? 256 : 512;
+};
+
+// Forward, one CTA of 16 warps per (batch entry, 128 query rows). Warp w reads TMEM lanes
+// 32 (w % 4) .. +31 (query rows) and, as group g = w / 4, the key chunk g of every half of
+// 128 keys, so the four warps of a row share its 32-column chunks. Pass 1 gives each row's
+// maximum (partial maxima combined through shared memory); then per half of the keys
+// E = exp(Z - m) goes to shared memory as four 32-key chunks (hi and lo) beside v^T of the
+// half, and O += E v accumulates in TMEM. O is divided by the row's exp-sum at the end.
 template <int T, int D>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_attn_fwd_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
-                                                             const float* __restrict__ v, const float* __restrict__ mask, float c, float fill,
-                                                             int* err) {
+__global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
+                                                              const float* __restrict__ v, const float* __restrict__ mask, float inv_c, float fill,
+                                                              int* err) {
   using L = FwdLayout<T, D>;
-  constexpr int NQB = T / 128, NCH = T / 32;
+  constexpr int NQB = T / 128, NH = T / 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *Qh = sm, *Ql = Qh + L::QB, *Kh = Ql + L::QB, *Kl = Kh + L::KB;  // phase 1
-  uint8_t *Vh = sm, *Vl = Vh + L::VB, *P0 = Vl + L::VB;                     // phase 2: P buffers b: hi P0 + 2b PB, lo + PB
-  uint64_t* bars = (uint64_t*)(sm + L::REGION);
-  uint64_t *bar_s = bars, *bar_p = bars + 1, *bar_o = bars + 3, *bar_done = bars + 4;
-  uint32_t* tslot = (uint32_t*)(bars + 5);
+  uint8_t *Vh = sm, *Vl = Vh + L::VB, *E0 = Vl + L::VB;                     // phase 2: chunk g at E0 + 2 g EB (hi), + EB (lo)
+  float* part = (float*)(sm + L::REGION);                                   // [2][4][128]: partial max, partial sum
+  uint64_t* bars = (uint64_t*)(part + 2 * 4 * 128);
+  uint64_t *bar_s = bars, *bar_o = bars + 1, *bar_done = bars + 2;
+  uint32_t* tslot = (uint32_t*)(bars + 3);
   volatile int* abort = (volatile int*)(tslot + 1);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, lq = warp & 3, g = warp >> 2;
+  const int row = lq * 32 + lane;  // this thread's query row within the block
   const long long z = blockIdx.x / NQB;
-  const int r0 = (int)(blockIdx.x - z * NQB) * 128, r = r0 + tid;
+  const int r0 = (int)(blockIdx.x - z * NQB) * 128, r = r0 + row;
   q += (z * T + r0) * D;
   k += z * T * D;
   v += z * T * D;
 
   if (tid == 0) {
-    for (int b = 0; b < 5; ++b) mbar_init(&bars[b], 1);
+    for (int b = 0; b < 3; ++b) mbar_init(&bars[b], 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -289,7 +298,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attn_fwd_tc(float* __restrict
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t lanes = (uint32_t)(warp * 32) << 16;  // this warp's TMEM lane quarter
+  const uint32_t lanes = (uint32_t)(lq * 32) << 16;
   const uint32_t S_t = tmem, O_t = tmem + T;
 
   // S = q k^T.
@@ -305,91 +314,87 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attn_fwd_tc(float* __restrict
   bool ok = cta_wait(bar_s, 0, abort, err, 21);
   fence_after();
 
-  // Row statistics: the mask row as bits, the max, then the exp-sum in key order.
-  uint32_t bits[NCH];
-  float m = -INFINITY, sum = 0.0f;
+  // Pass 1: the mask bits of this thread's chunks and the row maximum.
+  const float* mrow = mask + (long long)r * T;
+  uint32_t bits[NH];
+  float m = -INFINITY;
   if (ok) {
-    const float* mrow = mask + (long long)r * T;
-#pragma unroll 1
-    for (int ch = 0; ch < NCH; ++ch) {
+#pragma unroll
+    for (int h = 0; h < NH; ++h) {
+      const int c0 = h * 128 + g * 32;
       uint32_t x[32];
-      tmem_ld32(S_t + lanes + ch * 32, x);
+      tmem_ld32(S_t + lanes + c0, x);
       uint32_t b = 0;
 #pragma unroll
       for (int j = 0; j < 32; j += 4) {
-        const float4 mk = *(const float4*)(mrow + ch * 32 + j);
+        const float4 mk = *(const float4*)(mrow + c0 + j);
         b |= (mk.x != 0.0f ? 1u : 0u) << j | (mk.y != 0.0f ? 1u : 0u) << (j + 1) | (mk.z != 0.0f ? 1u : 0u) << (j + 2) |
              (mk.w != 0.0f ? 1u : 0u) << (j + 3);
       }
-      bits[ch] = b;
+      bits[h] = b;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) m = nan_max(m, ((b >> j) & 1u) ? __uint_as_float(x[j]) / c : fill);
+      for (int j = 0; j < 32; ++j) m = nan_max(m, ((b >> j) & 1u) ? __uint_as_float(x[j]) * inv_c : fill);
     }
-#pragma unroll 1
-    for (int ch = 0; ch < NCH; ++ch) {
-      uint32_t x[32];
-      tmem_ld32(S_t + lanes + ch * 32, x);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) sum = sum + expf((((bits[ch] >> j) & 1u) ? __uint_as_float(x[j]) / c : fill) - m);
-    }
-  }
-  fence_before();
-  __syncthreads();
-
-  // v^T into the freed operand space (the S products are complete).
-  if (ok) {
-    stage_t(Vh, Vl, v, T, D, D);
-    proxy_fence();
+    part[g * 128 + row] = m;
   }
   __syncthreads();
+  if (ok) m = nan_max(nan_max(part[row], part[128 + row]), nan_max(part[256 + row], part[384 + row]));
 
-  // O = P v, 32 keys at a time; P double-buffered in shared memory.
+  // Per half of the keys: v^T of the half and the half's E chunks in shared memory, then
+  // O += E v (the S products are complete, so their operand space is free).
+  float sum = 0.0f;
 #pragma unroll 1
-  for (int ch = 0; ch < NCH && ok; ++ch) {
-    const int b = ch & 1;
-    if (ch >= 2 && !cta_wait(&bar_p[b], (uint32_t)(((ch >> 1) - 1) & 1), abort, err, 22)) {
-      ok = false;
-      break;
-    }
-    fence_after();
-    uint8_t* ph = P0 + 2 * b * L::PB;
-    uint8_t* pl = ph + L::PB;
+  for (int h = 0; h < NH && ok; ++h) {
+    if (h > 0 && !(ok = cta_wait(bar_o, (uint32_t)((h - 1) & 1), abort, err, 22))) break;
+    stage_t(Vh, Vl, v + (long long)h * 128 * D, 128, D, D);
+    const int c0 = h * 128 + g * 32;
     uint32_t x[32];
-    tmem_ld32(S_t + lanes + ch * 32, x);
+    tmem_ld32(S_t + lanes + c0, x);
+    uint8_t* eh = E0 + 2 * g * L::EB;
+    uint8_t* el = eh + L::EB;
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
-      float p[4];
+      float e[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) p[u] = expf((((bits[ch] >> (j + u)) & 1u) ? __uint_as_float(x[j + u]) / c : fill) - m) / sum;
-      const uint32_t off = kmaj(128, tid, j);
-      *(float4*)(ph + off) = make_float4(p[0], p[1], p[2], p[3]);
-      *(float4*)(pl + off) = make_float4(tf32_lo(p[0]), tf32_lo(p[1]), tf32_lo(p[2]), tf32_lo(p[3]));
+      for (int u = 0; u < 4; ++u) {
+        e[u] = __expf((((bits[h] >> (j + u)) & 1u) ? __uint_as_float(x[j + u]) * inv_c : fill) - m);
+        sum = sum + e[u];
+      }
+      const uint32_t off = kmaj(128, row, j);
+      *(float4*)(eh + off) = make_float4(e[0], e[1], e[2], e[3]);
+      *(float4*)(el + off) = make_float4(tf32_lo(e[0]), tf32_lo(e[1]), tf32_lo(e[2]), tf32_lo(e[3]));
     }
     proxy_fence();
     fence_before();
     __syncthreads();
     if (tid == 0) {
       fence_after();
-      const uint32_t vo = (uint32_t)(ch * D * 128);
-      mma3(O_t, saddr(ph), saddr(pl), saddr(Vh) + vo, saddr(Vl) + vo, D, 32, idesc_tf32(128, D), ch > 0);
-      mma_commit(&bar_p[b]);
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        uint8_t* ch = E0 + 2 * cc * L::EB;
+        const uint32_t vo = (uint32_t)(cc * D * 128);
+        mma3(O_t, saddr(ch), saddr(ch + L::EB), saddr(Vh) + vo, saddr(Vl) + vo, D, 32, idesc_tf32(128, D), h > 0 || cc > 0);
+      }
+      mma_commit(bar_o);
     }
   }
-  if (tid == 0) mma_commit(bar_o);
-  if (ok) ok = cta_wait(bar_o, 0, abort, err, 23);
+  if (ok) ok = cta_wait(bar_o, (uint32_t)((NH - 1) & 1), abort, err, 23);
   fence_after();
+  if (ok) part[512 + g * 128 + row] = sum;
+  __syncthreads();
 
-  // O, m and s of row r.
+  // O / s, m and s of row r: group g writes O columns [32 g, 32 g + 32).
   if (ok) {
+    const float s4 = (part[512 + row] + part[640 + row]) + (part[768 + row] + part[896 + row]);
     float* orow = out + ((z * T) + r) * (D + 2);
-#pragma unroll 1
-    for (int e0 = 0; e0 < D; e0 += 32) {
+    if (g * 32 < D) {
       uint32_t x[32];
-      tmem_ld32(O_t + lanes + e0, x);
+      tmem_ld32(O_t + lanes + g * 32, x);
 #pragma unroll
-      for (int j = 0; j < 32; j += 2) *(float2*)(orow + e0 + j) = make_float2(__uint_as_float(x[j]), __uint_as_float(x[j + 1]));
+      for (int j = 0; j < 32; j += 2)
+        *(float2*)(orow + g * 32 + j) = make_float2(__uint_as_float(x[j]) / s4, __uint_as_float(x[j + 1]) / s4);
     }
-    *(float2*)(orow + D) = make_float2(m, sum);
+    if (g == 0) *(float2*)(orow + D) = make_float2(m, s4);
   }
 
   // Teardown: every product issued has completed before the TMEM goes.
@@ -408,16 +413,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attn_fwd_tc(float* __restrict
   }
 }
 
-// Shared-memory plan of the backward kernels: phases a and b stage two 128-row operands each
-// (hi and lo); phase c holds two transposed 128-column operands (dkdv) or one (dq) and the
-// chunk tiles the epilogue writes (32 columns, hi and lo).
+// Shared-memory plan of the backward kernels: phases a and b stage two 128-row operands (hi and
+// lo); phase c holds one transposed operand (128 columns) and the four 32-column chunk tiles
+// the four warp groups write.
 template <int D> struct BwdLayout {
   static constexpr int TB = 128 * D * 4;  // a 128 x D tile, or its transpose
   static constexpr int CB = 128 * 32 * 4; // a 128 x 32 chunk tile
-  static constexpr int AB = 4 * TB;       // phases a, b
-  static constexpr int DQ_C = 2 * TB + 4 * CB, KV_C = 4 * TB + 4 * CB;
-  static constexpr int DQ_REGION = AB > DQ_C ? AB : DQ_C, KV_REGION = AB > KV_C ? AB : KV_C;
-  static constexpr int DQ_SMEM = 1024 + DQ_REGION + 128, KV_SMEM = 1024 + KV_REGION + 3 * 128 * 4 + 128;
+  static constexpr int AB = 4 * TB, CPH = 2 * TB + 8 * CB;
+  static constexpr int REGION = AB > CPH ? AB : CPH;
+  static constexpr int SMEM = 1024 + REGION + 3 * 128 * 4 + 128;
 };
 
 // Bounded wait on `bar` for its next phase; `count` tracks the phases already consumed.
@@ -427,34 +431,72 @@ __device__ __forceinline__ bool cta_next(uint64_t* bar, int& count, volatile int
   return ok;
 }
 
-// dq, one CTA per (batch entry, 128 query rows), one thread per query row. Per half of the keys
-// (128 keys): S = q k^T and dP = dO v^T into TMEM, then per 32-key chunk dS = P (dP - D) / c to
-// shared memory and dq += dS k (k transposed, K-major over the keys).
+// The mask bits of 32 consecutive elements of a row.
+__device__ __forceinline__ uint32_t mask_bits(const float* m) {
+  uint32_t b = 0;
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    const float4 mk = *(const float4*)(m + j);
+    b |= (mk.x != 0.0f ? 1u : 0u) << j | (mk.y != 0.0f ? 1u : 0u) << (j + 1) | (mk.z != 0.0f ? 1u : 0u) << (j + 2) | (mk.w != 0.0f ? 1u : 0u) << (j + 3);
+  }
+  return b;
+}
+
+__device__ __forceinline__ void put_chunk(uint8_t* hi, uint8_t* lo, int row, const float (&x)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    const uint32_t off = kmaj(128, row, j);
+    *(float4*)(hi + off) = make_float4(x[j], x[j + 1], x[j + 2], x[j + 3]);
+    *(float4*)(lo + off) = make_float4(tf32_lo(x[j]), tf32_lo(x[j + 1]), tf32_lo(x[j + 2]), tf32_lo(x[j + 3]));
+  }
+}
+
+__device__ __forceinline__ void tc_teardown(uint64_t* bar_done, uint32_t tmem, uint32_t cols) {
+  fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mma_commit(bar_done);
+    unsigned long long t0 = now_ns();
+    while (!mbar_try(bar_done, 0) && now_ns() - t0 < WAIT_LIMIT_NS) {
+    }
+  }
+  __syncthreads();
+  if ((threadIdx.x >> 5) == 0) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(cols) : "memory");
+  }
+}
+
+// dq, one CTA of 16 warps per (batch entry, 128 query rows); warp w reads TMEM lanes 32 (w % 4)
+// (query rows) and, as group g = w / 4, key chunk g of each half. Per half of the keys (128):
+// S = q k^T and dP = dO v^T into TMEM, then k^T of the half and the four dS chunks in shared
+// memory, and dq += dS k.
 template <int T, int D>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_attn_dq_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
-                                                            const float* __restrict__ v, const float* __restrict__ mask, const float* __restrict__ fwd,
-                                                            const float* __restrict__ dout, float c, float fill, int* err) {
+__global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
+                                                             const float* __restrict__ v, const float* __restrict__ mask, const float* __restrict__ fwd,
+                                                             const float* __restrict__ dout, float inv_c, float fill, int* err) {
   using L = BwdLayout<D>;
   constexpr int NQB = T / 128, NH = T / 128, W = 3 * D;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *Ah = sm, *Al = Ah + L::TB, *Bh = Al + L::TB, *Bl = Bh + L::TB;  // phases a, b
-  uint8_t *Kth = sm, *Ktl = Kth + L::TB, *C0 = Ktl + L::TB;              // phase c: k^T, dS chunks (buffer b: hi C0 + 2b CB)
-  uint64_t* bars = (uint64_t*)(sm + L::DQ_REGION);
-  uint64_t *bar_a = bars, *bar_b = bars + 1, *bar_c = bars + 2, *bar_done = bars + 4;  // bar_c: two buffers
-  uint32_t* tslot = (uint32_t*)(bars + 5);
+  uint8_t *Th = sm, *Tl = Th + L::TB, *C0 = Tl + L::TB;                  // phase c: k^T, chunk g at C0 + 2 g CB
+  uint64_t* bars = (uint64_t*)(sm + L::REGION + 3 * 128 * 4);
+  uint64_t *bar_a = bars, *bar_b = bars + 1, *bar_c = bars + 2, *bar_done = bars + 3;
+  uint32_t* tslot = (uint32_t*)(bars + 4);
   volatile int* abort = (volatile int*)(tslot + 1);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, lq = warp & 3, g = warp >> 2;
+  const int row = lq * 32 + lane;
   const long long z = blockIdx.x / NQB;
-  const int r0 = (int)(blockIdx.x - z * NQB) * 128, r = r0 + tid;
+  const int r0 = (int)(blockIdx.x - z * NQB) * 128, r = r0 + row;
   const float* qb = q + (z * T + r0) * D;
   const float* db = dout + (z * T + r0) * D;
   k += z * T * D;
   v += z * T * D;
 
   if (tid == 0) {
-    for (int b = 0; b < 5; ++b) mbar_init(&bars[b], 1);
+    for (int b = 0; b < 4; ++b) mbar_init(&bars[b], 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -465,30 +507,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attn_dq_tc(float* __restrict_
   fence_before();
   __syncthreads();
   fence_after();
-  const uint32_t tmem = *tslot, lanes = (uint32_t)(warp * 32) << 16;
+  const uint32_t tmem = *tslot, lanes = (uint32_t)(lq * 32) << 16;
   const uint32_t S_t = tmem, P_t = tmem + 128, Q_t = tmem + 256;
 
   // Row r's statistics and D = dO . O.
   const float* fr = fwd + (z * T + r) * (D + 2);
-  const float m = fr[D], sum = fr[D + 1];
+  const float m = fr[D], inv_sum = 1.0f / fr[D + 1];
   float Dr = 0.0f;
   {
-    const float* dr = db + (long long)tid * D;
+    const float* dr = db + (long long)row * D;
     for (int e = 0; e < D; e += 4) {
-      const float4 a = *(const float4*)(dr + e);
+      const float4 a4 = *(const float4*)(dr + e);
       const float2 o0 = *(const float2*)(fr + e), o1 = *(const float2*)(fr + e + 2);
-      Dr = Dr + a.x * o0.x;
-      Dr = Dr + a.y * o0.y;
-      Dr = Dr + a.z * o1.x;
-      Dr = Dr + a.w * o1.y;
+      Dr = Dr + a4.x * o0.x;
+      Dr = Dr + a4.y * o0.y;
+      Dr = Dr + a4.z * o1.x;
+      Dr = Dr + a4.w * o1.y;
     }
   }
   const float* mrow = mask + (long long)r * T;
   bool ok = true;
-  int na = 0, nb = 0, nc[2] = {0, 0};
+  int na = 0, nb = 0, nc = 0;
 #pragma unroll 1
   for (int h = 0; h < NH && ok; ++h) {
-    // a: S = q k_h^T.
+    // a: S = q k_h^T (the previous half's products are complete).
     stage(Ah, Al, qb, 128, D, D);
     stage(Bh, Bl, k + (long long)h * 128 * D, 128, D, D);
     proxy_fence();
@@ -511,104 +553,75 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attn_dq_tc(float* __restrict_
     }
     if (!(ok = cta_next(bar_b, nb, abort, err, 32))) break;
     fence_after();
-    // c: k_h^T over the freed space, then dS chunk by chunk into dq.
-    stage_t(Kth, Ktl, k + (long long)h * 128 * D, 128, D, D);
-    proxy_fence();
-    __syncthreads();
-#pragma unroll 1
-    for (int ch = 0; ch < 4; ++ch) {
-      const int b = ch & 1;
-      if (ch >= 2 && !(ok = cta_next(&bar_c[b], nc[b], abort, err, 33))) break;
-      fence_after();
-      uint8_t* dh = C0 + 2 * b * L::CB;
-      uint8_t* dl = dh + L::CB;
+    // c: k_h^T, and this group's dS chunk.
+    stage_t(Th, Tl, k + (long long)h * 128 * D, 128, D, D);
+    {
       uint32_t xs[32], xp[32];
-      tmem_ld32(S_t + lanes + ch * 32, xs);
-      tmem_ld32(P_t + lanes + ch * 32, xp);
-      const int j0 = h * 128 + ch * 32;
+      tmem_ld32(S_t + lanes + g * 32, xs);
+      tmem_ld32(P_t + lanes + g * 32, xp);
+      const uint32_t bits = mask_bits(mrow + h * 128 + g * 32);
+      float ds[32];
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        const float4 mk = *(const float4*)(mrow + j0 + j);
-        const float mv[4] = {mk.x, mk.y, mk.z, mk.w};
-        float ds[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const bool on = mv[u] != 0.0f;
-          const float p = expf((on ? __uint_as_float(xs[j + u]) / c : fill) - m) / sum;
-          ds[u] = on ? p * (__uint_as_float(xp[j + u]) - Dr) / c : 0.0f;
-        }
-        const uint32_t off = kmaj(128, tid, j);
-        *(float4*)(dh + off) = make_float4(ds[0], ds[1], ds[2], ds[3]);
-        *(float4*)(dl + off) = make_float4(tf32_lo(ds[0]), tf32_lo(ds[1]), tf32_lo(ds[2]), tf32_lo(ds[3]));
+      for (int j = 0; j < 32; ++j) {
+        const bool on = (bits >> j) & 1u;
+        const float p = __expf((on ? __uint_as_float(xs[j]) * inv_c : fill) - m) * inv_sum;
+        ds[j] = on ? p * (__uint_as_float(xp[j]) - Dr) * inv_c : 0.0f;
       }
-      proxy_fence();
-      fence_before();
-      __syncthreads();
-      if (tid == 0) {
-        fence_after();
-        const uint32_t ko = (uint32_t)(ch * D * 128);
-        mma3(Q_t, saddr(dh), saddr(dl), saddr(Kth) + ko, saddr(Ktl) + ko, D, 32, idesc_tf32(128, D), h > 0 || ch > 0);
-        mma_commit(&bar_c[b]);
-      }
+      put_chunk(C0 + 2 * g * L::CB, C0 + (2 * g + 1) * L::CB, row, ds);
     }
-    // The chunk products read k^T and dS from shared memory: they finish before the next half
-    // stages over them (and before the next S overwrites the TMEM columns read above).
-    for (int b = 0; b < 2 && ok; ++b)
-      if (!(ok = cta_next(&bar_c[b], nc[b], abort, err, 34))) break;
-    fence_after();
-  }
-  fence_after();
-  if (ok) {
-    float* g = out + (z * T + r) * W;
+    proxy_fence();
+    fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      fence_after();
 #pragma unroll 1
-    for (int e0 = 0; e0 < D; e0 += 32) {
-      uint32_t x[32];
-      tmem_ld32(Q_t + lanes + e0, x);
-#pragma unroll
-      for (int j = 0; j < 32; j += 4)
-        *(float4*)(g + e0 + j) = make_float4(__uint_as_float(x[j]), __uint_as_float(x[j + 1]), __uint_as_float(x[j + 2]), __uint_as_float(x[j + 3]));
+      for (int cc = 0; cc < 4; ++cc) {
+        const uint32_t ko = (uint32_t)(cc * D * 128);
+        uint8_t* ch = C0 + 2 * cc * L::CB;
+        mma3(Q_t, saddr(ch), saddr(ch + L::CB), saddr(Th) + ko, saddr(Tl) + ko, D, 32, idesc_tf32(128, D), h > 0 || cc > 0);
+      }
+      mma_commit(bar_c);
     }
-  }
-  fence_before();
-  __syncthreads();
-  if (tid == 0) {
-    mma_commit(bar_done);
-    unsigned long long t0 = now_ns();
-    while (!mbar_try(bar_done, 0) && now_ns() - t0 < WAIT_LIMIT_NS) {
-    }
-  }
-  __syncthreads();
-  if (warp == 0) {
+    if (!(ok = cta_next(bar_c, nc, abort, err, 33))) break;
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512u) : "memory");
   }
+  if (ok && g * 32 < D) {
+    float* gq = out + (z * T + r) * W + g * 32;
+    uint32_t x[32];
+    tmem_ld32(Q_t + lanes + g * 32, x);
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+      *(float4*)(gq + j) = make_float4(__uint_as_float(x[j]), __uint_as_float(x[j + 1]), __uint_as_float(x[j + 2]), __uint_as_float(x[j + 3]));
+  }
+  tc_teardown(bar_done, tmem, 512u);
 }
 
-// dk and dv, one CTA per (batch entry, 128 keys), one thread per key row. Per half of the
-// queries (128 queries): S^T = k q^T and dP^T = v dO^T into TMEM, then per 32-query chunk P^T and
-// dS^T to shared memory, dv += P^T dO and dk += dS^T q (dO and q transposed, K-major over the
-// queries). The queries' statistics (max, exp-sum, D = dO . O) sit in shared memory.
+// dk and dv, one CTA of 16 warps per (batch entry, 128 keys); warp w reads TMEM lanes 32 (w % 4)
+// (key rows) and, as group g = w / 4, query chunk g of each half. Per half of the queries
+// (128): S^T = k q^T and dP^T = v dO^T into TMEM; then dO^T of the half and the four P^T chunks
+// in shared memory, dv += P^T dO; then q^T and the four dS^T chunks (kept in registers
+// meanwhile), dk += dS^T q. The half's query statistics (max, 1 / exp-sum, D) sit in shared memory.
 template <int T, int D>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_attn_dkdv_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
-                                                              const float* __restrict__ v, const float* __restrict__ mask,
-                                                              const float* __restrict__ fwd, const float* __restrict__ dout, float c, float fill,
-                                                              int* err) {
+__global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
+                                                               const float* __restrict__ v, const float* __restrict__ mask,
+                                                               const float* __restrict__ fwd, const float* __restrict__ dout, float inv_c, float fill,
+                                                               int* err) {
   using L = BwdLayout<D>;
   constexpr int NKB = T / 128, NH = T / 128, W = 3 * D;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *Ah = sm, *Al = Ah + L::TB, *Bh = Al + L::TB, *Bl = Bh + L::TB;  // phases a, b
-  uint8_t *Qth = sm, *Qtl = Qth + L::TB, *Oth = Qtl + L::TB, *Otl = Oth + L::TB;  // phase c: q^T, dO^T
-  uint8_t *Ph = Otl + L::TB, *Pl = Ph + L::CB, *Dh = Pl + L::CB, *Dl = Dh + L::CB;  // P^T and dS^T chunks
-  float* stats = (float*)(sm + L::KV_REGION);  // [3][128]: max, exp-sum, D of the half's queries
+  uint8_t *Th = sm, *Tl = Th + L::TB, *C0 = Tl + L::TB;                  // phase c
+  float* stats = (float*)(sm + L::REGION);  // [3][128]
   uint64_t* bars = (uint64_t*)(stats + 3 * 128);
   uint64_t *bar_a = bars, *bar_b = bars + 1, *bar_c = bars + 2, *bar_done = bars + 3;
   uint32_t* tslot = (uint32_t*)(bars + 4);
   volatile int* abort = (volatile int*)(tslot + 1);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, lq = warp & 3, g = warp >> 2;
+  const int row = lq * 32 + lane;  // key row within the block
   const long long z = blockIdx.x / NKB;
-  const int j0 = (int)(blockIdx.x - z * NKB) * 128, j = j0 + tid;
+  const int j0 = (int)(blockIdx.x - z * NKB) * 128, j = j0 + row;
   const float* kb = k + (z * T + j0) * D;
   const float* vb = v + (z * T + j0) * D;
   q += z * T * D;
@@ -627,7 +640,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attn_dkdv_tc(float* __restric
   fence_before();
   __syncthreads();
   fence_after();
-  const uint32_t tmem = *tslot, lanes = (uint32_t)(warp * 32) << 16;
+  const uint32_t tmem = *tslot, lanes = (uint32_t)(lq * 32) << 16;
   const uint32_t S_t = tmem, P_t = tmem + 128, V_t = tmem + 256, K_t = tmem + 256 + D;
 
   bool ok = true;
@@ -635,21 +648,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attn_dkdv_tc(float* __restric
 #pragma unroll 1
   for (int h = 0; h < NH && ok; ++h) {
     const int q0 = h * 128;
-    // The half's query statistics: thread i takes query q0 + i.
-    {
+    // The half's query statistics (the previous half's readers finished at its last wait).
+    if (tid < 128) {
       const float* fr = fwd + (long long)(q0 + tid) * (D + 2);
       const float* dr = dout + (long long)(q0 + tid) * D;
       float Dq = 0.0f;
       for (int e = 0; e < D; e += 4) {
-        const float4 a = *(const float4*)(dr + e);
+        const float4 a4 = *(const float4*)(dr + e);
         const float2 o0 = *(const float2*)(fr + e), o1 = *(const float2*)(fr + e + 2);
-        Dq = Dq + a.x * o0.x;
-        Dq = Dq + a.y * o0.y;
-        Dq = Dq + a.z * o1.x;
-        Dq = Dq + a.w * o1.y;
+        Dq = Dq + a4.x * o0.x;
+        Dq = Dq + a4.y * o0.y;
+        Dq = Dq + a4.z * o1.x;
+        Dq = Dq + a4.w * o1.y;
       }
       stats[tid] = fr[D];
-      stats[128 + tid] = fr[D + 1];
+      stats[128 + tid] = 1.0f / fr[D + 1];
       stats[256 + tid] = Dq;
     }
     // a: S^T = k q_h^T.
@@ -675,80 +688,68 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attn_dkdv_tc(float* __restric
     }
     if (!(ok = cta_next(bar_b, nb, abort, err, 42))) break;
     fence_after();
-    // c: q_h^T and dO_h^T over the freed space, then P^T and dS^T chunk by chunk.
-    stage_t(Qth, Qtl, q + (long long)q0 * D, 128, D, D);
-    stage_t(Oth, Otl, dout + (long long)q0 * D, 128, D, D);
-    proxy_fence();
-    __syncthreads();
-#pragma unroll 1
-    for (int ch = 0; ch < 4; ++ch) {
-      if (ch > 0 && !(ok = cta_next(bar_c, nc, abort, err, 43))) break;
-      fence_after();
+    // c1: dO_h^T and this group's P^T chunk (query columns q0 + 32 g ..); dS^T stays in registers.
+    stage_t(Th, Tl, dout + (long long)q0 * D, 128, D, D);
+    float pv[32], dsv[32];
+    {
       uint32_t xs[32], xp[32];
-      tmem_ld32(S_t + lanes + ch * 32, xs);
-      tmem_ld32(P_t + lanes + ch * 32, xp);
+      tmem_ld32(S_t + lanes + g * 32, xs);
+      tmem_ld32(P_t + lanes + g * 32, xp);
 #pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        float pv[4], dv[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int rl = ch * 32 + i + u, rq = q0 + rl;
-          const bool on = mask[(long long)rq * T + j] != 0.0f;
-          const float p = expf((on ? __uint_as_float(xs[i + u]) / c : fill) - stats[rl]) / stats[128 + rl];
-          pv[u] = p;
-          dv[u] = on ? p * (__uint_as_float(xp[i + u]) - stats[256 + rl]) / c : 0.0f;
-        }
-        const uint32_t off = kmaj(128, tid, i);
-        *(float4*)(Ph + off) = make_float4(pv[0], pv[1], pv[2], pv[3]);
-        *(float4*)(Pl + off) = make_float4(tf32_lo(pv[0]), tf32_lo(pv[1]), tf32_lo(pv[2]), tf32_lo(pv[3]));
-        *(float4*)(Dh + off) = make_float4(dv[0], dv[1], dv[2], dv[3]);
-        *(float4*)(Dl + off) = make_float4(tf32_lo(dv[0]), tf32_lo(dv[1]), tf32_lo(dv[2]), tf32_lo(dv[3]));
-      }
-      proxy_fence();
-      fence_before();
-      __syncthreads();
-      if (tid == 0) {
-        fence_after();
-        const uint32_t qo = (uint32_t)(ch * D * 128);
-        const bool acc = h > 0 || ch > 0;
-        mma3(V_t, saddr(Ph), saddr(Pl), saddr(Oth) + qo, saddr(Otl) + qo, D, 32, idesc_tf32(128, D), acc);
-        mma3(K_t, saddr(Dh), saddr(Dl), saddr(Qth) + qo, saddr(Qtl) + qo, D, 32, idesc_tf32(128, D), acc);
-        mma_commit(bar_c);
+      for (int i = 0; i < 32; ++i) {
+        const int rl = g * 32 + i;
+        const bool on = mask[(long long)(q0 + rl) * T + j] != 0.0f;
+        const float p = __expf((on ? __uint_as_float(xs[i]) * inv_c : fill) - stats[rl]) * stats[128 + rl];
+        pv[i] = p;
+        dsv[i] = on ? p * (__uint_as_float(xp[i]) - stats[256 + rl]) * inv_c : 0.0f;
       }
     }
-    // The last chunk's products finish before the stats, tiles and TMEM columns are reused.
-    if (ok) ok = cta_next(bar_c, nc, abort, err, 44);
-    fence_after();
-  }
-  fence_after();
-  if (ok) {
-    float* g = out + (z * T + j) * W;
+    put_chunk(C0 + 2 * g * L::CB, C0 + (2 * g + 1) * L::CB, row, pv);
+    proxy_fence();
+    fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      fence_after();
 #pragma unroll 1
-    for (int e0 = 0; e0 < D; e0 += 32) {
-      uint32_t x[32], y[32];
-      tmem_ld32(K_t + lanes + e0, x);
-      tmem_ld32(V_t + lanes + e0, y);
-#pragma unroll
-      for (int u = 0; u < 32; u += 4) {
-        *(float4*)(g + D + e0 + u) = make_float4(__uint_as_float(x[u]), __uint_as_float(x[u + 1]), __uint_as_float(x[u + 2]), __uint_as_float(x[u + 3]));
-        *(float4*)(g + 2 * D + e0 + u) =
-            make_float4(__uint_as_float(y[u]), __uint_as_float(y[u + 1]), __uint_as_float(y[u + 2]), __uint_as_float(y[u + 3]));
+      for (int cc = 0; cc < 4; ++cc) {
+        const uint32_t qo = (uint32_t)(cc * D * 128);
+        uint8_t* ch = C0 + 2 * cc * L::CB;
+        mma3(V_t, saddr(ch), saddr(ch + L::CB), saddr(Th) + qo, saddr(Tl) + qo, D, 32, idesc_tf32(128, D), h > 0 || cc > 0);
       }
+      mma_commit(bar_c);
     }
-  }
-  fence_before();
-  __syncthreads();
-  if (tid == 0) {
-    mma_commit(bar_done);
-    unsigned long long t0 = now_ns();
-    while (!mbar_try(bar_done, 0) && now_ns() - t0 < WAIT_LIMIT_NS) {
+    if (!(ok = cta_next(bar_c, nc, abort, err, 43))) break;
+    // c2: q_h^T and the dS^T chunks.
+    stage_t(Th, Tl, q + (long long)q0 * D, 128, D, D);
+    put_chunk(C0 + 2 * g * L::CB, C0 + (2 * g + 1) * L::CB, row, dsv);
+    proxy_fence();
+    fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      fence_after();
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        const uint32_t qo = (uint32_t)(cc * D * 128);
+        uint8_t* ch = C0 + 2 * cc * L::CB;
+        mma3(K_t, saddr(ch), saddr(ch + L::CB), saddr(Th) + qo, saddr(Tl) + qo, D, 32, idesc_tf32(128, D), h > 0 || cc > 0);
+      }
+      mma_commit(bar_c);
     }
-  }
-  __syncthreads();
-  if (warp == 0) {
+    if (!(ok = cta_next(bar_c, nc, abort, err, 44))) break;
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512u) : "memory");
   }
+  if (ok && g * 32 < D) {
+    float* gk = out + (z * T + j) * W;
+    uint32_t x[32], y[32];
+    tmem_ld32(K_t + lanes + g * 32, x);
+    tmem_ld32(V_t + lanes + g * 32, y);
+#pragma unroll
+    for (int u = 0; u < 32; u += 4) {
+      *(float4*)(gk + D + g * 32 + u) = make_float4(__uint_as_float(x[u]), __uint_as_float(x[u + 1]), __uint_as_float(x[u + 2]), __uint_as_float(x[u + 3]));
+      *(float4*)(gk + 2 * D + g * 32 + u) = make_float4(__uint_as_float(y[u]), __uint_as_float(y[u + 1]), __uint_as_float(y[u + 2]), __uint_as_float(y[u + 3]));
+    }
+  }
+  tc_teardown(bar_done, tmem, 512u);
 }
 
 template <int T, int D> void set_smem(void (*kern)(float*, const float*, const float*, const float*, const float*, float, float, int*)) {
@@ -758,19 +759,19 @@ template <int T, int D> void set_smem(void (*kern)(float*, const float*, const f
 template <int T, int D> void launch_fwd_tc(float* out, const float* q, const float* k, const float* v, const float* mask, const AttnShape& a, int* err,
                                            cudaStream_t s) {
   const long long blocks = a.batch * (T / 128);
-  k_attn_fwd_tc<T, D><<<(unsigned)blocks, TC_THREADS, FwdLayout<T, D>::SMEM, s>>>(out, q, k, v, mask, a.c, a.fill, err);
+  k_attn_fwd_tc<T, D><<<(unsigned)blocks, FWD_THREADS, FwdLayout<T, D>::SMEM, s>>>(out, q, k, v, mask, 1.0f / a.c, a.fill, err);
 }
 
 template <int T, int D> void set_smem_bwd() {
-  cudaFuncSetAttribute(k_attn_dq_tc<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdLayout<D>::DQ_SMEM);
-  cudaFuncSetAttribute(k_attn_dkdv_tc<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdLayout<D>::KV_SMEM);
+  cudaFuncSetAttribute(k_attn_dq_tc<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdLayout<D>::SMEM);
+  cudaFuncSetAttribute(k_attn_dkdv_tc<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdLayout<D>::SMEM);
 }
 
 template <int T, int D> void launch_bwd_tc(float* out, const float* q, const float* k, const float* v, const float* mask, const float* fwd,
                                            const float* dout, const AttnShape& a, int* err, cudaStream_t s) {
   const unsigned blocks = (unsigned)(a.batch * (T / 128));
-  k_attn_dq_tc<T, D><<<blocks, TC_THREADS, BwdLayout<D>::DQ_SMEM, s>>>(out, q, k, v, mask, fwd, dout, a.c, a.fill, err);
-  k_attn_dkdv_tc<T, D><<<blocks, TC_THREADS, BwdLayout<D>::KV_SMEM, s>>>(out, q, k, v, mask, fwd, dout, a.c, a.fill, err);
+  k_attn_dq_tc<T, D><<<blocks, FWD_THREADS, BwdLayout<D>::SMEM, s>>>(out, q, k, v, mask, fwd, dout, 1.0f / a.c, a.fill, err);
+  k_attn_dkdv_tc<T, D><<<blocks, FWD_THREADS, BwdLayout<D>::SMEM, s>>>(out, q, k, v, mask, fwd, dout, 1.0f / a.c, a.fill, err);
 }
 
 }  // namespace

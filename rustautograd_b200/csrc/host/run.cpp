@@ -1,5 +1,6 @@
 // The generic multi-step loop and one-off execution over the Exec contract.
 #include <algorithm>
+#include <map>
 #include <chrono>
 #include <cmath>
 #include <stdexcept>
@@ -133,7 +134,9 @@ std::vector<StepCost> step_costs(const Plan& p) {
   for (auto& ch : find_row_chains(p)) {
     const double es = (double)dtype_size(ch.dtype), full = (double)ch.rows * (double)ch.cols, rows = (double)ch.rows;
     double bytes = 0, flops = 0;
-    std::vector<std::pair<size_t, int>> seen;
+    // Each slot read from outside counts once, at the largest extent any member reads it (one
+    // member may read a slot in full where another reads one value per row of it).
+    std::map<size_t, double> reads;
     for (size_t m = 0; m < ch.members.size(); ++m) {
       const Step& st = p.steps[ch.members[m]];
       // Per-row members read and write (..., 1) values; full ones and reductions read rows.
@@ -142,22 +145,23 @@ std::vector<StepCost> step_costs(const Plan& p) {
       flops += out[ch.members[m]].flops;
       for (auto& in : row_inputs(p, ch, m)) {
         if (in.kind == RowInput::Value) continue;
-        std::pair<size_t, int> key{in.slot, (int)in.kind};
-        if (std::find(seen.begin(), seen.end(), key) != seen.end()) continue;
-        seen.push_back(key);
+        double b = 0;
         switch (in.kind) {
-          case RowInput::Full: bytes += (per_row ? rows : full) * es; break;
-          case RowInput::Column: bytes += rows * es; break;
-          case RowInput::Periodic: bytes += (double)in.period * es; break;
-          case RowInput::Splat: bytes += es; break;
-          default: bytes += (double)product(in.shape) * es; break;
+          case RowInput::Full: b = (per_row ? rows : full) * es; break;
+          case RowInput::Column: b = rows * es; break;
+          case RowInput::Periodic: b = (double)in.period * es; break;
+          case RowInput::Splat: b = es; break;
+          default: b = (double)product(in.shape) * es; break;
         }
+        double& r = reads[in.slot];
+        r = std::max(r, b);
       }
       auto writes = step_writes(st);
       for (size_t q = 0; q < writes.size(); ++q)
         if (ch.store[m][q]) bytes += (full_out ? full : rows) * es;
       out[ch.members[m]] = StepCost{"row_chain", 0.0, 0.0};
     }
+    for (auto& [slot, b] : reads) bytes += b;
     out[ch.first] = StepCost{"row_chain", flops, bytes};
   }
   return out;
