@@ -372,12 +372,16 @@ def roofline(w, compiled, secs, pk):
     total = sum(v[0] for v in by_kind.values()) or 1e-30
     top = max(by_kind, key=lambda k: by_kind[k][0])
     t_s, fl, by, n = by_kind[top]
-    if top == "matmul":
+    if top in ("matmul", "attention"):
+        # Tensor-core classes: the products' FLOPs (2 m n k; for the fused attention its q k^T,
+        # P v and backward products) per second against the measured bf16 peak.
         achieved, peak, unit, bound = fl / t_s / 1e12, pk["bf16_tflops_sustained"], "TFLOP/s", "tensor"
     else:
         achieved, peak, unit, bound = by / t_s / 1e9, pk["hbm_gbs"], "GB/s", "hbm"
     fused = by_kind.get("fused", [1e-30, 0, 0, 0])
     chains = by_kind.get("row_chain")
+    attn = by_kind.get("attention")
+    gemm = by_kind.get("matmul")
     traffic, traffic_of = traffic_for(w.name, top)
     return {"bound": bound, "kernel": top, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
             "peak_source": pk["source"], "traffic": traffic, "traffic_of": traffic_of, "launches_per_step": n, "share_of_step": t_s / total,
@@ -385,7 +389,11 @@ def roofline(w, compiled, secs, pk):
             "fused_elementwise": {"achieved_gbs": fused[2] / fused[0] / 1e9, "frac_of_hbm": fused[2] / fused[0] / 1e9 / pk["hbm_gbs"],
                                   "share_of_step": fused[0] / total},
             "row_chains": None if chains is None else {"achieved_gbs": chains[2] / chains[0] / 1e9, "frac_of_hbm": chains[2] / chains[0] / 1e9 / pk["hbm_gbs"],
-                                                       "share_of_step": chains[0] / total, "launches_per_step": chains[3]}}
+                                                       "share_of_step": chains[0] / total, "launches_per_step": chains[3]},
+            "gemm": None if gemm is None else {"achieved_tflops": gemm[1] / gemm[0] / 1e12, "frac_of_bf16_sustained": gemm[1] / gemm[0] / 1e12 / pk["bf16_tflops_sustained"],
+                                               "share_of_step": gemm[0] / total, "launches_per_step": gemm[3]},
+            "attention": None if attn is None else {"achieved_tflops": attn[1] / attn[0] / 1e12, "share_of_step": attn[0] / total,
+                                                    "ops_per_step": attn[3]}}
 
 
 def main():

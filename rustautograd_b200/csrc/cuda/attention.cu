@@ -184,31 +184,51 @@ __device__ __forceinline__ uint32_t kmaj(int R, int row, int k) {
 __device__ __forceinline__ float tf32_lo(float x) { return x - tf32_trunc(x); }
 
 // Rows [0, R) x columns [0, K) of a row-major global block (row stride `ld` floats, 16-byte
-// aligned rows) into K-major hi / lo tiles.
-__device__ __forceinline__ void stage(uint8_t* hi, uint8_t* lo, const float* src, int R, int K, long long ld) {
-  const int k4 = K >> 2;
-  for (int i = threadIdx.x; i < R * k4; i += blockDim.x) {
-    const int row = i / k4, col = (i - row * k4) << 2;
-    const float4 x = *(const float4*)(src + row * ld + col);
-    const uint32_t off = kmaj(R, row, col);
-    *(float4*)(hi + off) = x;
-    *(float4*)(lo + off) = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
+// aligned rows) into K-major hi / lo tiles. Each thread moves four 16-byte vectors at a time,
+// all four loads issued before the first store.
+__device__ __forceinline__ void stage(uint8_t* hi, uint8_t* lo, const float* __restrict__ src, int R, int K, long long ld) {
+  const int k4 = K >> 2, n = R * k4, step = blockDim.x;
+  for (int i0 = threadIdx.x; i0 < n; i0 += 4 * step) {
+    float4 x[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * step;
+      if (i < n) {
+        const int row = i / k4, col = (i - row * k4) << 2;
+        x[u] = *(const float4*)(src + row * ld + col);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * step;
+      if (i < n) {
+        const int row = i / k4, col = (i - row * k4) << 2;
+        const uint32_t off = kmaj(R, row, col);
+        *(float4*)(hi + off) = x[u];
+        *(float4*)(lo + off) = make_float4(tf32_lo(x[u].x), tf32_lo(x[u].y), tf32_lo(x[u].z), tf32_lo(x[u].w));
+      }
+    }
   }
 }
 
 // The transpose of a row-major global block: source rows [0, Rs) become the tile's K index and
-// source columns [0, Cs) its rows (a K-major tile of Cs rows over K = Rs).
-__device__ __forceinline__ void stage_t(uint8_t* hi, uint8_t* lo, const float* src, int Rs, int Cs, long long ld) {
-  const int c4 = Cs >> 2;
-  for (int i = threadIdx.x; i < Rs * c4; i += blockDim.x) {
-    const int j = i / c4, col = (i - j * c4) << 2;
-    const float4 x = *(const float4*)(src + j * ld + col);
-    const float xs[4] = {x.x, x.y, x.z, x.w};
+// source columns [0, Cs) its rows (a K-major tile of Cs rows over K = Rs). Each thread takes a
+// 4 x 4 block (source rows j..j+3, columns e..e+3), transposes it in registers and writes four
+// 16-byte vectors (tile rows e..e+3, K = j..j+3). Rs and Cs are multiples of 4.
+__device__ __forceinline__ void stage_t(uint8_t* hi, uint8_t* lo, const float* __restrict__ src, int Rs, int Cs, long long ld) {
+  const int c4 = Cs >> 2, n = (Rs >> 2) * c4;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int jb = i / c4, e = (i - jb * c4) << 2, j = jb << 2;
+    float4 x[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t off = kmaj(Cs, col + q, j);
-      *(float*)(hi + off) = xs[q];
-      *(float*)(lo + off) = tf32_lo(xs[q]);
+    for (int u = 0; u < 4; ++u) x[u] = *(const float4*)(src + (long long)(j + u) * ld + e);
+    const float4 t[4] = {make_float4(x[0].x, x[1].x, x[2].x, x[3].x), make_float4(x[0].y, x[1].y, x[2].y, x[3].y),
+                         make_float4(x[0].z, x[1].z, x[2].z, x[3].z), make_float4(x[0].w, x[1].w, x[2].w, x[3].w)};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t off = kmaj(Cs, e + u, j);
+      *(float4*)(hi + off) = t[u];
+      *(float4*)(lo + off) = make_float4(tf32_lo(t[u].x), tf32_lo(t[u].y), tf32_lo(t[u].z), tf32_lo(t[u].w));
     }
   }
 }
@@ -688,23 +708,22 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
     }
     if (!(ok = cta_next(bar_b, nb, abort, err, 42))) break;
     fence_after();
-    // c1: dO_h^T and this group's P^T chunk (query columns q0 + 32 g ..); dS^T stays in registers.
+    // c1: dO_h^T and this group's P^T chunk (query columns q0 + 32 g ..).
     stage_t(Th, Tl, dout + (long long)q0 * D, 128, D, D);
-    float pv[32], dsv[32];
+    uint32_t qbits = 0;  // the mask bits of this key column over the chunk's queries
+#pragma unroll 8
+    for (int i = 0; i < 32; ++i) qbits |= (mask[(long long)(q0 + g * 32 + i) * T + j] != 0.0f ? 1u : 0u) << i;
     {
-      uint32_t xs[32], xp[32];
+      uint32_t xs[32];
       tmem_ld32(S_t + lanes + g * 32, xs);
-      tmem_ld32(P_t + lanes + g * 32, xp);
+      float pv[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const int rl = g * 32 + i;
-        const bool on = mask[(long long)(q0 + rl) * T + j] != 0.0f;
-        const float p = __expf((on ? __uint_as_float(xs[i]) * inv_c : fill) - stats[rl]) * stats[128 + rl];
-        pv[i] = p;
-        dsv[i] = on ? p * (__uint_as_float(xp[i]) - stats[256 + rl]) * inv_c : 0.0f;
+        pv[i] = __expf((((qbits >> i) & 1u) ? __uint_as_float(xs[i]) * inv_c : fill) - stats[rl]) * stats[128 + rl];
       }
+      put_chunk(C0 + 2 * g * L::CB, C0 + (2 * g + 1) * L::CB, row, pv);
     }
-    put_chunk(C0 + 2 * g * L::CB, C0 + (2 * g + 1) * L::CB, row, pv);
     proxy_fence();
     fence_before();
     __syncthreads();
@@ -719,9 +738,22 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
       mma_commit(bar_c);
     }
     if (!(ok = cta_next(bar_c, nc, abort, err, 43))) break;
-    // c2: q_h^T and the dS^T chunks.
+    // c2: q_h^T and the dS^T chunks (P^T recomputed from the scores still in TMEM).
     stage_t(Th, Tl, q + (long long)q0 * D, 128, D, D);
-    put_chunk(C0 + 2 * g * L::CB, C0 + (2 * g + 1) * L::CB, row, dsv);
+    {
+      uint32_t xs[32], xp[32];
+      tmem_ld32(S_t + lanes + g * 32, xs);
+      tmem_ld32(P_t + lanes + g * 32, xp);
+      float dsv[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int rl = g * 32 + i;
+        const bool on = (qbits >> i) & 1u;
+        const float p = __expf((on ? __uint_as_float(xs[i]) * inv_c : fill) - stats[rl]) * stats[128 + rl];
+        dsv[i] = on ? p * (__uint_as_float(xp[i]) - stats[256 + rl]) * inv_c : 0.0f;
+      }
+      put_chunk(C0 + 2 * g * L::CB, C0 + (2 * g + 1) * L::CB, row, dsv);
+    }
     proxy_fence();
     fence_before();
     __syncthreads();
