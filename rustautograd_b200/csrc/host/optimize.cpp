@@ -350,12 +350,23 @@ std::optional<Tensor> slice_of_constant(const Graph& g, uint32_t src, const Op& 
 //   dq = matmul_t(dS, transpose(k); tb)  dk = transpose(matmul_t(q, dS; ta))
 // It becomes AttnFwd / AttnBwd (q, k, v, the (T, T) mask; O and dq, dk, dv as slices of their
 // packed results), so the (..., T, T) tensors between them are never materialised. Values agree
-// with the pattern's to rounding: softmax sums and products run in another order. Only with
-// RGC_FUSED_ATTENTION=1 while the device kernels await validation on a GPU.
-bool fused_attention_enabled() {
+// with the pattern's to rounding: softmax sums and products run in another order.
+//
+// Which attentions are fused: RGC_FUSED_ATTENTION=1 fuses every match and =0 none. By default
+// the device fuses the shapes its tensor-core kernels take (attention.cu) where they measured
+// faster than the unfused plan on a B200: sequence length 128 or 256 with head size 32 (a d256
+// step of 8 heads: 9.77 against 10.32 ms). With head size 64 the kernels run one CTA per SM and
+// the unfused plan (row chains and the GEMM) is faster (a d512 step: 287 against 280 ms), so
+// those stay unfused.
+enum class AttnFuse { None, Default, All };
+AttnFuse fused_attention_mode() {
   const char* e = getenv("RGC_FUSED_ATTENTION");
-  return e && std::string(e) == "1";
+  if (e && std::string(e) == "1") return AttnFuse::All;
+  if (e && std::string(e) == "0") return AttnFuse::None;
+  return AttnFuse::Default;
 }
+bool fused_attention_enabled() { return fused_attention_mode() != AttnFuse::None; }
+bool fuse_by_default(size_t t, size_t d, size_t dv) { return (t == 128 || t == 256) && d == 32 && dv == 32; }
 
 struct AttnMatch {
   uint32_t q, k, v, O, dO, dv, dq, dk;
@@ -677,6 +688,10 @@ Simplified fuse_attention(const Simplified& in) {
     if (!live[i] || match_of[i] >= 0) continue;
     auto m = match_attention(g, (uint32_t)i, users, live);
     if (!m || match_of[m->dv] >= 0 || match_of[m->dq] >= 0 || match_of[m->dk] >= 0) continue;
+    if (fused_attention_mode() == AttnFuse::Default) {
+      const auto& qs = g.shape(m->q);
+      if (!fuse_by_default(qs[qs.size() - 2], qs.back(), g.shape(m->v).back())) continue;
+    }
     for (uint32_t id : {m->O, m->dv, m->dq, m->dk}) match_of[id] = (long)matches.size();
     matches.push_back(*m);
   }

@@ -1,4 +1,5 @@
-"""The device's fused-attention rewrite (enabled with RGC_FUSED_ATTENTION=1), on the CPU: plans
+"""The device's fused-attention rewrite (every match with RGC_FUSED_ATTENTION=1; by default only
+the shapes where the device's fused kernels are faster), on the CPU: plans
 built for the CUDA device through the oracle's "cuda-plan" device, whose interpreter runs the fused
 ops' CPU definition, against rg's own plan of the same graph.
 
@@ -93,10 +94,21 @@ def test_gpt_step_with_fused_attention_matches_rgs_plan():
             assert rel(a, b) <= 1e-4, f"output {k_}"
 
 
-def test_default_plans_have_no_fused_attention(monkeypatch):
+def test_default_fuses_only_head_size_32_at_tensor_core_lengths(monkeypatch):
+    """By default the device fuses attention of length 128 or 256 with head size 32 (measured
+    faster on a B200) and leaves other shapes (head size 64 among them) to the unfused plan;
+    RGC_FUSED_ATTENTION=0 turns fusion off for every shape."""
     monkeypatch.delenv("RGC_FUSED_ATTENTION", raising=False)
     rng = np.random.default_rng(9)
-    q, k, v, w = (F.tensor(rng.normal(size=(2, 8, 4)).astype("float32")) for _ in range(4))
-    fn = lambda q, k, v, w: F.value_and_grad(lambda q, k, v: (attention(q, k, v, F.tril(8)) * w).sum(), argnums=(0, 1, 2))(q, k, v)
-    c = F.compile(fn, (q, k, v, w), validate="none", device="cuda-plan")
-    assert "attention" not in ops_of(c)
+
+    def plan(shape):
+        q, k, v, w = (F.tensor(rng.normal(size=shape).astype("float32")) for _ in range(4))
+        mask = F.tril(shape[-2])
+        fn = lambda q, k, v, w: F.value_and_grad(lambda q, k, v: (attention(q, k, v, mask) * w).sum(), argnums=(0, 1, 2))(q, k, v)
+        return ops_of(F.compile(fn, (q, k, v, w), validate="none", device="cuda-plan"))
+    assert "attention" not in plan((2, 8, 4))
+    assert "attention" not in plan((1, 2, 128, 64))
+    assert "attention" in plan((1, 2, 128, 32))
+    assert "attention" in plan((1, 1, 256, 32))
+    monkeypatch.setenv("RGC_FUSED_ATTENTION", "0")
+    assert "attention" not in plan((1, 2, 128, 32))
