@@ -404,6 +404,8 @@ def main():
     ap.add_argument("--config", default="gpt-d512-l12", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--full-cpu-baseline", action="store_true",
+                    help="GPT workloads: fit the CPU step time through batches 1 and 4 (as --impl reference does) instead of scaling batch 1")
     args = ap.parse_args()
     w = WORKLOADS[args.config]
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -506,7 +508,7 @@ def main():
                        "algorithmic_per_launch": w.algorithmic_bytes() / max(rf["launches_per_step"], 1)})
         cpu = None
         if not args.no_cpu_baseline:
-            rec = cpu_baseline(w)
+            rec = cpu_baseline(w, full=args.full_cpu_baseline)
             cpu = {"value": 1.0 / rec["seconds_per_step"], "unit": "steps/s", "cores": rec["cores"], "kind": "port", "sample": rec["sample"],
                    "sample_steps": rec["sample_steps"], "sample_seconds": rec["sample_seconds"], "extrapolated": rec["extrapolated"]}
         cfg = dict(w.config(world), frame_bytes=compiled._n.allocated_bytes(), row_chains=os.environ.get("RGC_ROW_CHAINS") != "0")
