@@ -434,6 +434,11 @@ def main():
         }))
         return
 
+    # Libraries write banners to stdout (NCCL prints its version at communicator set-up); they go
+    # to stderr, so that rank 0's stdout is the one JSON line.
+    json_out = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
     import torch
     torch.cuda.set_device(local)
     dist = None
@@ -531,7 +536,7 @@ def main():
         _rg.dist_finalize()
         dist.destroy_process_group()
     if out is not None:
-        print(json.dumps(out))
+        print(json.dumps(out), file=json_out, flush=True)
 
 
 if __name__ == "__main__":
