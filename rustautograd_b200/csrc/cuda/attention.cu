@@ -5,15 +5,17 @@
 // TF32; lo = x - trunc_tf32(x); A B = A_hi B_hi + A_hi B_lo + A_lo B_hi). Operand tiles are staged
 // in shared memory by the CTA's own threads, which write hi and lo in the K-major 128-byte-swizzle
 // layout the MMA descriptors read (a transposed operand is written transposed, so every operand is
-// K-major). One CTA of four warps takes 128 query rows of one batch entry; thread i owns row i
-// (TMEM lane i), so row statistics need no exchange:
-//   forward   S = q k^T into TMEM (T columns); two passes over S give each row's max and exp-sum
-//             (the sum in key order); then per 32-key chunk P = exp(Z - m) / s goes to shared
-//             memory (hi and lo, double-buffered) and O += P v accumulates in TMEM.
-//   backward  two kernels, each recomputing the scores: k_attn_dq_tc (one thread per query row)
-//             forms dS chunk by chunk and accumulates dq = dS k; k_attn_dkdv_tc (one thread per
-//             key row) works on the transposes, forming P^T and dS^T and accumulating
-//             dv = P^T dO and dk = dS^T q. D = rowsum(dO * O) comes from the forward's O.
+// K-major). One CTA of 16 warps takes 128 rows (queries, or keys for dk / dv) of one batch entry:
+// warp w reads TMEM lanes 32 (w % 4) .. + 31 and, as group w / 4, one 32-column chunk of every
+// 128 columns, so a row's four warps share its chunks.
+//   forward   S = q k^T into TMEM (T columns); pass 1 gives each row's max; then per half of the
+//             keys E = exp(Z - m) goes to shared memory (hi and lo) beside v^T and O += E v
+//             accumulates in TMEM; O / s, m and s leave as the block's contiguous packed rows.
+//   backward  two kernels, each recomputing the scores: k_attn_dq_tc (query rows) forms dS per
+//             half of the keys and accumulates dq = dS k; k_attn_dkdv_tc (key rows) works on the
+//             transposes, forming P^T and dS^T and accumulating dv = P^T dO and dk = dS^T q.
+//             D = rowsum(dO * O) comes from the forward's O.
+// A causal mask is computed from the indices; any other mask is packed into bits once per CTA.
 //
 // CUDA-core path (any other T up to 1024 and any d): one warp per row, for the small shapes of
 // tests and models outside the tensor-core tiles.
@@ -183,6 +185,8 @@ __device__ __forceinline__ uint32_t kmaj(int R, int row, int k) {
 
 __device__ __forceinline__ float tf32_lo(float x) { return x - tf32_trunc(x); }
 
+__device__ __forceinline__ float4 lo4(const float4& x) { return make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w)); }
+
 // Rows [0, R) x columns [0, K) of a row-major global block (row stride `ld` floats, 16-byte
 // aligned rows) into K-major hi / lo tiles. Each thread moves four 16-byte vectors at a time,
 // all four loads issued before the first store.
@@ -205,31 +209,43 @@ __device__ __forceinline__ void stage(uint8_t* hi, uint8_t* lo, const float* __r
         const int row = i / k4, col = (i - row * k4) << 2;
         const uint32_t off = kmaj(R, row, col);
         *(float4*)(hi + off) = x[u];
-        *(float4*)(lo + off) = make_float4(tf32_lo(x[u].x), tf32_lo(x[u].y), tf32_lo(x[u].z), tf32_lo(x[u].w));
+        *(float4*)(lo + off) = lo4(x[u]);
       }
     }
   }
 }
 
-// The transpose of a row-major global block: source rows [0, Rs) become the tile's K index and
-// source columns [0, Cs) its rows (a K-major tile of Cs rows over K = Rs). Each thread takes a
-// 4 x 4 block (source rows j..j+3, columns e..e+3), transposes it in registers and writes four
-// 16-byte vectors (tile rows e..e+3, K = j..j+3). Rs and Cs are multiples of 4.
-__device__ __forceinline__ void stage_t(uint8_t* hi, uint8_t* lo, const float* __restrict__ src, int Rs, int Cs, long long ld) {
-  const int c4 = Cs >> 2, n = (Rs >> 2) * c4;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int jb = i / c4, e = (i - jb * c4) << 2, j = jb << 2;
-    float4 x[4];
+// The transpose of a 128-row global block of C columns (C = 32 or 64): source rows become the
+// tile's K index and source columns its rows (a K-major tile of C rows over K = 128). Thread i
+// takes the 4 x 4 block i (source rows j..j+3, columns e..e+3); blockDim.x >= 8 C, so one block
+// per thread. Split into the loads (issued early, before a wait) and the transposed stores.
+struct TBlock {
+  float4 x[4];
+  int e, j;
+  bool on;
+};
+__device__ __forceinline__ TBlock load_t(const float* __restrict__ src, int C, long long ld) {
+  TBlock b;
+  const int c4 = C >> 2, i = threadIdx.x;
+  b.on = i < 32 * c4;
+  const int jb = i / c4;
+  b.e = (i - jb * c4) << 2;
+  b.j = jb << 2;
+  if (b.on) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) x[u] = *(const float4*)(src + (long long)(j + u) * ld + e);
-    const float4 t[4] = {make_float4(x[0].x, x[1].x, x[2].x, x[3].x), make_float4(x[0].y, x[1].y, x[2].y, x[3].y),
-                         make_float4(x[0].z, x[1].z, x[2].z, x[3].z), make_float4(x[0].w, x[1].w, x[2].w, x[3].w)};
+    for (int u = 0; u < 4; ++u) b.x[u] = *(const float4*)(src + (long long)(b.j + u) * ld + b.e);
+  }
+  return b;
+}
+__device__ __forceinline__ void store_t(uint8_t* hi, uint8_t* lo, const TBlock& b, int C) {
+  if (!b.on) return;
+  const float4 t[4] = {make_float4(b.x[0].x, b.x[1].x, b.x[2].x, b.x[3].x), make_float4(b.x[0].y, b.x[1].y, b.x[2].y, b.x[3].y),
+                       make_float4(b.x[0].z, b.x[1].z, b.x[2].z, b.x[3].z), make_float4(b.x[0].w, b.x[1].w, b.x[2].w, b.x[3].w)};
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const uint32_t off = kmaj(Cs, e + u, j);
-      *(float4*)(hi + off) = t[u];
-      *(float4*)(lo + off) = make_float4(tf32_lo(t[u].x), tf32_lo(t[u].y), tf32_lo(t[u].z), tf32_lo(t[u].w));
-    }
+  for (int u = 0; u < 4; ++u) {
+    const uint32_t off = kmaj(C, b.e + u, b.j);
+    *(float4*)(hi + off) = t[u];
+    *(float4*)(lo + off) = lo4(t[u]);
   }
 }
 
@@ -263,6 +279,128 @@ __device__ __forceinline__ bool cta_wait(uint64_t* bar, uint32_t phase, volatile
   return *abort == 0;
 }
 
+// Bounded wait on `bar` for its next phase; `count` tracks the phases already consumed.
+__device__ __forceinline__ bool cta_next(uint64_t* bar, int& count, volatile int* abort, int* err, int code) {
+  const bool ok = cta_wait(bar, (uint32_t)(count & 1), abort, err, code);
+  ++count;
+  return ok;
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]),
+        "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Writes 16 values of one row (K positions j0 .. j0 + 15, j0 a multiple of 16) of a 128-row
+// K-major chunk tile, hi and lo.
+__device__ __forceinline__ void put16(uint8_t* hi, uint8_t* lo, int row, int j0, const float (&x)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; j += 4) {
+    const uint32_t off = kmaj(128, row, j0 + j);
+    const float4 v = make_float4(x[j], x[j + 1], x[j + 2], x[j + 3]);
+    *(float4*)(hi + off) = v;
+    *(float4*)(lo + off) = lo4(v);
+  }
+}
+
+__device__ __forceinline__ void tc_teardown(uint64_t* bar_done, uint32_t tmem, uint32_t cols) {
+  fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mma_commit(bar_done);
+    unsigned long long t0 = now_ns();
+    while (!mbar_try(bar_done, 0) && now_ns() - t0 < WAIT_LIMIT_NS) {
+    }
+  }
+  __syncthreads();
+  if ((threadIdx.x >> 5) == 0) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(cols) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Mask bits
+// ---------------------------------------------------------------------------------------------
+// A causal mask (mask[i][j] != 0 exactly where j <= i: a constant lower triangle, recognised by
+// the planner) is computed from the indices and never read. Any other mask is packed once per
+// CTA into words in shared memory, bit (j - j0) % 32 of words[(i - i0) * (C / 32) + (j - j0) / 32]
+// set where mask[i][j] != 0, for rows [i0, i0 + R) and columns [j0, j0 + C) (C a multiple of
+// 32): one coalesced 128-byte load and one ballot per word, eight loads in flight per warp.
+
+// Keys j0 .. j0 + 31 of query i under the causal mask.
+__device__ __forceinline__ uint32_t causal_keys(int i, int j0) {
+  const int n = i - j0 + 1;
+  return n <= 0 ? 0u : n >= 32 ? 0xffffffffu : ((1u << n) - 1u);
+}
+// Queries i0 .. i0 + 31 of key j under the causal mask.
+__device__ __forceinline__ uint32_t causal_queries(int j, int i0) {
+  const int n = j - i0;
+  return n <= 0 ? 0xffffffffu : n >= 32 ? 0u : (0xffffffffu << n);
+}
+
+__device__ void pack_mask(uint32_t* words, const float* __restrict__ mask, int T, int i0, int R, int j0, int C) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int wpr = C >> 5, n = R * wpr;
+  for (int b = warp; b < n; b += 8 * nw) {
+    float x[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int it = b + u * nw;
+      x[u] = 0.0f;
+      if (it < n) {
+        const int row = it / wpr, w = it - row * wpr;
+        x[u] = mask[(long long)(i0 + row) * T + j0 + 32 * w + lane];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int it = b + u * nw;
+      const uint32_t bits = __ballot_sync(FULL, x[u] != 0.0f);
+      if (lane == 0 && it < n) words[it] = bits;
+    }
+  }
+}
+
+// Per query row of a 128-row block (global rows row0 ..): the forward's row maximum m and
+// 1 / exp-sum, and D = rowsum(dO * O) with O read from the forward's packed output. Warp w
+// takes rows 8 w .. 8 w + 7, lanes over the row's columns; st[0..127] = m, st[128..255] = 1 / s,
+// st[256..383] = D.
+template <int D>
+__device__ __forceinline__ void query_stats(float* st, const float* __restrict__ fwd, const float* __restrict__ dout, long long row0) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int PER = D / 32;
+  float a[8][PER], o[8][PER];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const long long r = row0 + warp * 8 + u;
+#pragma unroll
+    for (int p = 0; p < PER; ++p) {
+      a[u][p] = dout[r * D + p * 32 + lane];
+      o[u][p] = fwd[r * (D + 2) + p * 32 + lane];
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    float s = a[u][0] * o[u][0];
+#pragma unroll
+    for (int p = 1; p < PER; ++p) s = s + a[u][p] * o[u][p];
+#pragma unroll
+    for (int off = 16; off; off >>= 1) s = s + __shfl_xor_sync(FULL, s, off);
+    const int rl = warp * 8 + u;
+    if (lane == 0) {
+      const float* f = fwd + (row0 + rl) * (D + 2) + D;
+      st[rl] = f[0];
+      st[128 + rl] = 1.0f / f[1];
+      st[256 + rl] = s;
+    }
+  }
+}
+
 constexpr int FWD_THREADS = 512;
 
 template <int T, int D> struct FwdLayout {
@@ -271,8 +409,10 @@ template <int T, int D> struct FwdLayout {
   static constexpr int EB = 128 * 32 * 4;  // one 32-key chunk of E
   static constexpr int PHASE1 = 2 * QB + 2 * KB, PHASE2 = 2 * VB + 8 * EB;
   static constexpr int REGION = PHASE1 > PHASE2 ? PHASE1 : PHASE2;
-  static constexpr int SMEM = 1024 + REGION + 2 * 4 * 128 * 4 + 128;
+  static constexpr int WORDS = 128 * (T / 32) * 4;  // the mask bits of the block's rows
+  static constexpr int SMEM = 1024 + REGION + WORDS + 2 * 4 * 128 * 4 + 128;
   static constexpr uint32_t TCOLS = T + D <= 256 ? 256 : 512;
+  static_assert(128 * (D + 2) * 4 <= REGION, "output staging fits the operand region");
 };
 
 // Forward, one CTA of 16 warps per (batch entry, 128 query rows). Warp w reads TMEM lanes
@@ -280,18 +420,22 @@ template <int T, int D> struct FwdLayout {
 // 128 keys, so the four warps of a row share its 32-column chunks. Pass 1 gives each row's
 // maximum (partial maxima combined through shared memory); then per half of the keys
 // E = exp(Z - m) goes to shared memory as four 32-key chunks (hi and lo) beside v^T of the
-// half, and O += E v accumulates in TMEM. O is divided by the row's exp-sum at the end.
+// half, and O += E v accumulates in TMEM; each half's v is loaded into registers before the
+// wait that frees its tiles. O is divided by the row's exp-sum and the block's packed rows
+// (O, m, s) leave through shared memory as one contiguous, coalesced store.
 template <int T, int D>
 __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
-                                                              const float* __restrict__ v, const float* __restrict__ mask, float inv_c, float fill,
-                                                              int* err) {
+                                                              const float* __restrict__ v, const float* __restrict__ mask, int causal, float inv_c,
+                                                              float fill, int* err) {
   using L = FwdLayout<T, D>;
-  constexpr int NQB = T / 128, NH = T / 128;
+  constexpr int NQB = T / 128, NH = T / 128, NW = T / 32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *Qh = sm, *Ql = Qh + L::QB, *Kh = Ql + L::QB, *Kl = Kh + L::KB;  // phase 1
   uint8_t *Vh = sm, *Vl = Vh + L::VB, *E0 = Vl + L::VB;                     // phase 2: chunk g at E0 + 2 g EB (hi), + EB (lo)
-  float* part = (float*)(sm + L::REGION);                                   // [2][4][128]: partial max, partial sum
+  float* ost = (float*)sm;                                                  // epilogue: the block's packed rows
+  uint32_t* words = (uint32_t*)(sm + L::REGION);                            // [128][NW]
+  float* part = (float*)(sm + L::REGION + L::WORDS);                        // [2][4][128]: partial max, partial sum
   uint64_t* bars = (uint64_t*)(part + 2 * 4 * 128);
   uint64_t *bar_s = bars, *bar_o = bars + 1, *bar_done = bars + 2;
   uint32_t* tslot = (uint32_t*)(bars + 3);
@@ -314,6 +458,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tslot)), "r"(L::TCOLS) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  if (!causal) pack_mask(words, mask, T, r0, 128, 0, T);
   fence_before();
   __syncthreads();
   fence_after();
@@ -331,11 +476,11 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
     mma3(S_t, saddr(Qh), saddr(Ql), saddr(Kh), saddr(Kl), T, D, idesc_tf32(128, T), false);
     mma_commit(bar_s);
   }
+  TBlock vb = load_t(v, D, D);  // v^T of the first half, in flight across the wait
   bool ok = cta_wait(bar_s, 0, abort, err, 21);
   fence_after();
 
   // Pass 1: the mask bits of this thread's chunks and the row maximum.
-  const float* mrow = mask + (long long)r * T;
   uint32_t bits[NH];
   float m = -INFINITY;
   if (ok) {
@@ -344,13 +489,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
       const int c0 = h * 128 + g * 32;
       uint32_t x[32];
       tmem_ld32(S_t + lanes + c0, x);
-      uint32_t b = 0;
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        const float4 mk = *(const float4*)(mrow + c0 + j);
-        b |= (mk.x != 0.0f ? 1u : 0u) << j | (mk.y != 0.0f ? 1u : 0u) << (j + 1) | (mk.z != 0.0f ? 1u : 0u) << (j + 2) |
-             (mk.w != 0.0f ? 1u : 0u) << (j + 3);
-      }
+      const uint32_t b = causal ? causal_keys(r, c0) : words[row * NW + (c0 >> 5)];
       bits[h] = b;
 #pragma unroll
       for (int j = 0; j < 32; ++j) m = nan_max(m, ((b >> j) & 1u) ? __uint_as_float(x[j]) * inv_c : fill);
@@ -365,8 +504,11 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
   float sum = 0.0f;
 #pragma unroll 1
   for (int h = 0; h < NH && ok; ++h) {
-    if (h > 0 && !(ok = cta_wait(bar_o, (uint32_t)((h - 1) & 1), abort, err, 22))) break;
-    stage_t(Vh, Vl, v + (long long)h * 128 * D, 128, D, D);
+    if (h > 0) {
+      vb = load_t(v + (long long)h * 128 * D, D, D);
+      if (!(ok = cta_wait(bar_o, (uint32_t)((h - 1) & 1), abort, err, 22))) break;
+    }
+    store_t(Vh, Vl, vb, D);
     const int c0 = h * 128 + g * 32;
     uint32_t x[32];
     tmem_ld32(S_t + lanes + c0, x);
@@ -381,8 +523,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
         sum = sum + e[u];
       }
       const uint32_t off = kmaj(128, row, j);
-      *(float4*)(eh + off) = make_float4(e[0], e[1], e[2], e[3]);
-      *(float4*)(el + off) = make_float4(tf32_lo(e[0]), tf32_lo(e[1]), tf32_lo(e[2]), tf32_lo(e[3]));
+      const float4 ev = make_float4(e[0], e[1], e[2], e[3]);
+      *(float4*)(eh + off) = ev;
+      *(float4*)(el + off) = lo4(ev);
     }
     proxy_fence();
     fence_before();
@@ -403,10 +546,11 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
   if (ok) part[512 + g * 128 + row] = sum;
   __syncthreads();
 
-  // O / s, m and s of row r: group g writes O columns [32 g, 32 g + 32).
+  // O / s, m and s of row `row` into the staging rows (group g: O columns [32 g, 32 g + 32)),
+  // then the block's 128 (D + 2)-float rows, contiguous in `out`, in 16-byte stores.
   if (ok) {
     const float s4 = (part[512 + row] + part[640 + row]) + (part[768 + row] + part[896 + row]);
-    float* orow = out + ((z * T) + r) * (D + 2);
+    float* orow = ost + row * (D + 2);
     if (g * 32 < D) {
       uint32_t x[32];
       tmem_ld32(O_t + lanes + g * 32, x);
@@ -416,92 +560,46 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
     }
     if (g == 0) *(float2*)(orow + D) = make_float2(m, s4);
   }
-
-  // Teardown: every product issued has completed before the TMEM goes.
-  fence_before();
   __syncthreads();
-  if (tid == 0) {
-    mma_commit(bar_done);
-    unsigned long long t0 = now_ns();
-    while (!mbar_try(bar_done, 0) && now_ns() - t0 < WAIT_LIMIT_NS) {
-    }
+  if (ok) {
+    float4* dst = (float4*)(out + (z * T + r0) * (D + 2));
+    const float4* srcv = (const float4*)ost;
+    for (int i = tid; i < 32 * (D + 2); i += FWD_THREADS) dst[i] = srcv[i];
   }
-  __syncthreads();
-  if (warp == 0) {
-    fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::TCOLS) : "memory");
-  }
+  tc_teardown(bar_done, tmem, L::TCOLS);
 }
 
 // Shared-memory plan of the backward kernels: phases a and b stage two 128-row operands (hi and
 // lo); phase c holds one transposed operand (128 columns) and the four 32-column chunk tiles
-// the four warp groups write.
-template <int D> struct BwdLayout {
+// the four warp groups write; then the query statistics and the mask words.
+template <int T, int D> struct BwdLayout {
   static constexpr int TB = 128 * D * 4;  // a 128 x D tile, or its transpose
   static constexpr int CB = 128 * 32 * 4; // a 128 x 32 chunk tile
   static constexpr int AB = 4 * TB, CPH = 2 * TB + 8 * CB;
   static constexpr int REGION = AB > CPH ? AB : CPH;
-  static constexpr int SMEM = 1024 + REGION + 3 * 128 * 4 + 128;
+  static constexpr int WORDS = 128 * (T / 32) * 4;
+  static constexpr int SMEM = 1024 + REGION + 3 * 128 * 4 + WORDS + 128;
+  static_assert(128 * (2 * D + 4) * 4 <= REGION, "output staging fits the operand region");
 };
-
-// Bounded wait on `bar` for its next phase; `count` tracks the phases already consumed.
-__device__ __forceinline__ bool cta_next(uint64_t* bar, int& count, volatile int* abort, int* err, int code) {
-  const bool ok = cta_wait(bar, (uint32_t)(count & 1), abort, err, code);
-  ++count;
-  return ok;
-}
-
-// The mask bits of 32 consecutive elements of a row.
-__device__ __forceinline__ uint32_t mask_bits(const float* m) {
-  uint32_t b = 0;
-#pragma unroll
-  for (int j = 0; j < 32; j += 4) {
-    const float4 mk = *(const float4*)(m + j);
-    b |= (mk.x != 0.0f ? 1u : 0u) << j | (mk.y != 0.0f ? 1u : 0u) << (j + 1) | (mk.z != 0.0f ? 1u : 0u) << (j + 2) | (mk.w != 0.0f ? 1u : 0u) << (j + 3);
-  }
-  return b;
-}
-
-__device__ __forceinline__ void put_chunk(uint8_t* hi, uint8_t* lo, int row, const float (&x)[32]) {
-#pragma unroll
-  for (int j = 0; j < 32; j += 4) {
-    const uint32_t off = kmaj(128, row, j);
-    *(float4*)(hi + off) = make_float4(x[j], x[j + 1], x[j + 2], x[j + 3]);
-    *(float4*)(lo + off) = make_float4(tf32_lo(x[j]), tf32_lo(x[j + 1]), tf32_lo(x[j + 2]), tf32_lo(x[j + 3]));
-  }
-}
-
-__device__ __forceinline__ void tc_teardown(uint64_t* bar_done, uint32_t tmem, uint32_t cols) {
-  fence_before();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    mma_commit(bar_done);
-    unsigned long long t0 = now_ns();
-    while (!mbar_try(bar_done, 0) && now_ns() - t0 < WAIT_LIMIT_NS) {
-    }
-  }
-  __syncthreads();
-  if ((threadIdx.x >> 5) == 0) {
-    fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(cols) : "memory");
-  }
-}
 
 // dq, one CTA of 16 warps per (batch entry, 128 query rows); warp w reads TMEM lanes 32 (w % 4)
 // (query rows) and, as group g = w / 4, key chunk g of each half. Per half of the keys (128):
-// S = q k^T and dP = dO v^T into TMEM, then k^T of the half and the four dS chunks in shared
-// memory, and dq += dS k.
+// S = q k^T and dP = dO v^T into TMEM, then k^T of the half (loaded before the dP wait) and the
+// four dS chunks in shared memory, and dq += dS k. dq leaves through shared memory in
+// row-contiguous stores.
 template <int T, int D>
 __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
                                                              const float* __restrict__ v, const float* __restrict__ mask, const float* __restrict__ fwd,
-                                                             const float* __restrict__ dout, float inv_c, float fill, int* err) {
-  using L = BwdLayout<D>;
-  constexpr int NQB = T / 128, NH = T / 128, W = 3 * D;
+                                                             const float* __restrict__ dout, int causal, float inv_c, float fill, int* err) {
+  using L = BwdLayout<T, D>;
+  constexpr int NQB = T / 128, NH = T / 128, W = 3 * D, NW = T / 32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *Ah = sm, *Al = Ah + L::TB, *Bh = Al + L::TB, *Bl = Bh + L::TB;  // phases a, b
   uint8_t *Th = sm, *Tl = Th + L::TB, *C0 = Tl + L::TB;                  // phase c: k^T, chunk g at C0 + 2 g CB
-  uint64_t* bars = (uint64_t*)(sm + L::REGION + 3 * 128 * 4);
+  float* stats = (float*)(sm + L::REGION);                                // [3][128]
+  uint32_t* words = (uint32_t*)(stats + 3 * 128);                         // [128][NW]
+  uint64_t* bars = (uint64_t*)(sm + L::REGION + 3 * 128 * 4 + L::WORDS);
   uint64_t *bar_a = bars, *bar_b = bars + 1, *bar_c = bars + 2, *bar_done = bars + 3;
   uint32_t* tslot = (uint32_t*)(bars + 4);
   volatile int* abort = (volatile int*)(tslot + 1);
@@ -524,28 +622,15 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tslot)), "r"(512u) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  query_stats<D>(stats, fwd, dout, z * T + r0);
+  if (!causal) pack_mask(words, mask, T, r0, 128, 0, T);
   fence_before();
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tslot, lanes = (uint32_t)(lq * 32) << 16;
   const uint32_t S_t = tmem, P_t = tmem + 128, Q_t = tmem + 256;
+  const float m = stats[row], inv_sum = stats[128 + row], Dr = stats[256 + row];
 
-  // Row r's statistics and D = dO . O.
-  const float* fr = fwd + (z * T + r) * (D + 2);
-  const float m = fr[D], inv_sum = 1.0f / fr[D + 1];
-  float Dr = 0.0f;
-  {
-    const float* dr = db + (long long)row * D;
-    for (int e = 0; e < D; e += 4) {
-      const float4 a4 = *(const float4*)(dr + e);
-      const float2 o0 = *(const float2*)(fr + e), o1 = *(const float2*)(fr + e + 2);
-      Dr = Dr + a4.x * o0.x;
-      Dr = Dr + a4.y * o0.y;
-      Dr = Dr + a4.z * o1.x;
-      Dr = Dr + a4.w * o1.y;
-    }
-  }
-  const float* mrow = mask + (long long)r * T;
   bool ok = true;
   int na = 0, nb = 0, nc = 0;
 #pragma unroll 1
@@ -571,23 +656,29 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
       mma3(P_t, saddr(Ah), saddr(Al), saddr(Bh), saddr(Bl), 128, D, idesc_tf32(128, 128), false);
       mma_commit(bar_b);
     }
+    const TBlock kt = load_t(k + (long long)h * 128 * D, D, D);
     if (!(ok = cta_next(bar_b, nb, abort, err, 32))) break;
     fence_after();
-    // c: k_h^T, and this group's dS chunk.
-    stage_t(Th, Tl, k + (long long)h * 128 * D, 128, D, D);
+    // c: k_h^T, and this group's dS chunk, in two 16-column pieces.
+    store_t(Th, Tl, kt, D);
     {
-      uint32_t xs[32], xp[32];
-      tmem_ld32(S_t + lanes + g * 32, xs);
-      tmem_ld32(P_t + lanes + g * 32, xp);
-      const uint32_t bits = mask_bits(mrow + h * 128 + g * 32);
-      float ds[32];
+      const int c0 = h * 128 + g * 32;
+      const uint32_t bits = causal ? causal_keys(r, c0) : words[row * NW + (c0 >> 5)];
+      uint8_t* ch = C0 + 2 * g * L::CB;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const bool on = (bits >> j) & 1u;
-        const float p = __expf((on ? __uint_as_float(xs[j]) * inv_c : fill) - m) * inv_sum;
-        ds[j] = on ? p * (__uint_as_float(xp[j]) - Dr) * inv_c : 0.0f;
+      for (int p = 0; p < 2; ++p) {
+        uint32_t xs[16], xp[16];
+        tmem_ld16(S_t + lanes + g * 32 + 16 * p, xs);
+        tmem_ld16(P_t + lanes + g * 32 + 16 * p, xp);
+        float ds[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const bool on = (bits >> (16 * p + j)) & 1u;
+          const float pr = __expf((on ? __uint_as_float(xs[j]) * inv_c : fill) - m) * inv_sum;
+          ds[j] = on ? pr * (__uint_as_float(xp[j]) - Dr) * inv_c : 0.0f;
+        }
+        put16(ch, ch + L::CB, row, 16 * p, ds);
       }
-      put_chunk(C0 + 2 * g * L::CB, C0 + (2 * g + 1) * L::CB, row, ds);
     }
     proxy_fence();
     fence_before();
@@ -605,13 +696,23 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
     if (!(ok = cta_next(bar_c, nc, abort, err, 33))) break;
     fence_after();
   }
+  // dq rows through shared memory (pitch D + 4 floats), then D-float row segments of `out`.
+  float* ost = (float*)sm;
   if (ok && g * 32 < D) {
-    float* gq = out + (z * T + r) * W + g * 32;
     uint32_t x[32];
     tmem_ld32(Q_t + lanes + g * 32, x);
 #pragma unroll
     for (int j = 0; j < 32; j += 4)
-      *(float4*)(gq + j) = make_float4(__uint_as_float(x[j]), __uint_as_float(x[j + 1]), __uint_as_float(x[j + 2]), __uint_as_float(x[j + 3]));
+      *(float4*)(ost + row * (D + 4) + g * 32 + j) =
+          make_float4(__uint_as_float(x[j]), __uint_as_float(x[j + 1]), __uint_as_float(x[j + 2]), __uint_as_float(x[j + 3]));
+  }
+  __syncthreads();
+  if (ok) {
+    constexpr int V4 = D / 4;  // 16-byte vectors per row
+    for (int i = tid; i < 128 * V4; i += FWD_THREADS) {
+      const int rr = i / V4, c = (i - rr * V4) * 4;
+      *(float4*)(out + (z * T + r0 + rr) * W + c) = *(const float4*)(ost + rr * (D + 4) + c);
+    }
   }
   tc_teardown(bar_done, tmem, 512u);
 }
@@ -619,21 +720,23 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
 // dk and dv, one CTA of 16 warps per (batch entry, 128 keys); warp w reads TMEM lanes 32 (w % 4)
 // (key rows) and, as group g = w / 4, query chunk g of each half. Per half of the queries
 // (128): S^T = k q^T and dP^T = v dO^T into TMEM; then dO^T of the half and the four P^T chunks
-// in shared memory, dv += P^T dO; then q^T and the four dS^T chunks (kept in registers
-// meanwhile), dk += dS^T q. The half's query statistics (max, 1 / exp-sum, D) sit in shared memory.
+// in shared memory, dv += P^T dO; then q^T and the four dS^T chunks, dk += dS^T q. The half's
+// query statistics (max, 1 / exp-sum, D) sit in shared memory; the transposed operands are
+// loaded before the waits that free their tiles. dk and dv leave through shared memory.
 template <int T, int D>
 __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
                                                                const float* __restrict__ v, const float* __restrict__ mask,
-                                                               const float* __restrict__ fwd, const float* __restrict__ dout, float inv_c, float fill,
-                                                               int* err) {
-  using L = BwdLayout<D>;
+                                                               const float* __restrict__ fwd, const float* __restrict__ dout, int causal, float inv_c,
+                                                               float fill, int* err) {
+  using L = BwdLayout<T, D>;
   constexpr int NKB = T / 128, NH = T / 128, W = 3 * D;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *Ah = sm, *Al = Ah + L::TB, *Bh = Al + L::TB, *Bl = Bh + L::TB;  // phases a, b
   uint8_t *Th = sm, *Tl = Th + L::TB, *C0 = Tl + L::TB;                  // phase c
-  float* stats = (float*)(sm + L::REGION);  // [3][128]
-  uint64_t* bars = (uint64_t*)(stats + 3 * 128);
+  float* stats = (float*)(sm + L::REGION);                                // [3][128]
+  uint32_t* words = (uint32_t*)(stats + 3 * 128);                         // [T][4]: queries x the block's 128 keys
+  uint64_t* bars = (uint64_t*)(sm + L::REGION + 3 * 128 * 4 + L::WORDS);
   uint64_t *bar_a = bars, *bar_b = bars + 1, *bar_c = bars + 2, *bar_done = bars + 3;
   uint32_t* tslot = (uint32_t*)(bars + 4);
   volatile int* abort = (volatile int*)(tslot + 1);
@@ -644,9 +747,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
   const int j0 = (int)(blockIdx.x - z * NKB) * 128, j = j0 + row;
   const float* kb = k + (z * T + j0) * D;
   const float* vb = v + (z * T + j0) * D;
-  q += z * T * D;
-  dout += z * T * D;
-  fwd += z * T * (D + 2);
+  const float* qz = q + z * T * D;
+  const float* dz = dout + z * T * D;
 
   if (tid == 0) {
     for (int b = 0; b < 4; ++b) mbar_init(&bars[b], 1);
@@ -657,6 +759,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tslot)), "r"(512u) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  if (!causal) pack_mask(words, mask, T, 0, T, j0, 128);
   fence_before();
   __syncthreads();
   fence_after();
@@ -669,25 +772,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
   for (int h = 0; h < NH && ok; ++h) {
     const int q0 = h * 128;
     // The half's query statistics (the previous half's readers finished at its last wait).
-    if (tid < 128) {
-      const float* fr = fwd + (long long)(q0 + tid) * (D + 2);
-      const float* dr = dout + (long long)(q0 + tid) * D;
-      float Dq = 0.0f;
-      for (int e = 0; e < D; e += 4) {
-        const float4 a4 = *(const float4*)(dr + e);
-        const float2 o0 = *(const float2*)(fr + e), o1 = *(const float2*)(fr + e + 2);
-        Dq = Dq + a4.x * o0.x;
-        Dq = Dq + a4.y * o0.y;
-        Dq = Dq + a4.z * o1.x;
-        Dq = Dq + a4.w * o1.y;
-      }
-      stats[tid] = fr[D];
-      stats[128 + tid] = 1.0f / fr[D + 1];
-      stats[256 + tid] = Dq;
-    }
+    query_stats<D>(stats, fwd, dout, z * T + q0);
     // a: S^T = k q_h^T.
     stage(Ah, Al, kb, 128, D, D);
-    stage(Bh, Bl, q + (long long)q0 * D, 128, D, D);
+    stage(Bh, Bl, qz + (long long)q0 * D, 128, D, D);
     proxy_fence();
     __syncthreads();
     if (tid == 0) {
@@ -698,7 +786,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
     if (!(ok = cta_next(bar_a, na, abort, err, 41))) break;
     // b: dP^T = v dO_h^T.
     stage(Ah, Al, vb, 128, D, D);
-    stage(Bh, Bl, dout + (long long)q0 * D, 128, D, D);
+    stage(Bh, Bl, dz + (long long)q0 * D, 128, D, D);
     proxy_fence();
     __syncthreads();
     if (tid == 0) {
@@ -706,23 +794,33 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
       mma3(P_t, saddr(Ah), saddr(Al), saddr(Bh), saddr(Bl), 128, D, idesc_tf32(128, 128), false);
       mma_commit(bar_b);
     }
+    const TBlock dt = load_t(dz + (long long)q0 * D, D, D);
+    // The mask bits of this key over the chunk's queries q0 + 32 g ...
+    uint32_t qbits = 0;
+    if (causal) {
+      qbits = causal_queries(j, q0 + g * 32);
+    } else {
+#pragma unroll 8
+      for (int i = 0; i < 32; ++i) qbits |= ((words[(q0 + g * 32 + i) * 4 + (row >> 5)] >> lane) & 1u) << i;
+    }
     if (!(ok = cta_next(bar_b, nb, abort, err, 42))) break;
     fence_after();
     // c1: dO_h^T and this group's P^T chunk (query columns q0 + 32 g ..).
-    stage_t(Th, Tl, dout + (long long)q0 * D, 128, D, D);
-    uint32_t qbits = 0;  // the mask bits of this key column over the chunk's queries
-#pragma unroll 8
-    for (int i = 0; i < 32; ++i) qbits |= (mask[(long long)(q0 + g * 32 + i) * T + j] != 0.0f ? 1u : 0u) << i;
+    store_t(Th, Tl, dt, D);
     {
-      uint32_t xs[32];
-      tmem_ld32(S_t + lanes + g * 32, xs);
-      float pv[32];
+      uint8_t* ch = C0 + 2 * g * L::CB;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int rl = g * 32 + i;
-        pv[i] = __expf((((qbits >> i) & 1u) ? __uint_as_float(xs[i]) * inv_c : fill) - stats[rl]) * stats[128 + rl];
+      for (int p = 0; p < 2; ++p) {
+        uint32_t xs[16];
+        tmem_ld16(S_t + lanes + g * 32 + 16 * p, xs);
+        float pv[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int rl = g * 32 + 16 * p + i;
+          pv[i] = __expf((((qbits >> (16 * p + i)) & 1u) ? __uint_as_float(xs[i]) * inv_c : fill) - stats[rl]) * stats[128 + rl];
+        }
+        put16(ch, ch + L::CB, row, 16 * p, pv);
       }
-      put_chunk(C0 + 2 * g * L::CB, C0 + (2 * g + 1) * L::CB, row, pv);
     }
     proxy_fence();
     fence_before();
@@ -737,22 +835,27 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
       }
       mma_commit(bar_c);
     }
+    const TBlock qt = load_t(qz + (long long)q0 * D, D, D);
     if (!(ok = cta_next(bar_c, nc, abort, err, 43))) break;
     // c2: q_h^T and the dS^T chunks (P^T recomputed from the scores still in TMEM).
-    stage_t(Th, Tl, q + (long long)q0 * D, 128, D, D);
+    store_t(Th, Tl, qt, D);
     {
-      uint32_t xs[32], xp[32];
-      tmem_ld32(S_t + lanes + g * 32, xs);
-      tmem_ld32(P_t + lanes + g * 32, xp);
-      float dsv[32];
+      uint8_t* ch = C0 + 2 * g * L::CB;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int rl = g * 32 + i;
-        const bool on = (qbits >> i) & 1u;
-        const float p = __expf((on ? __uint_as_float(xs[i]) * inv_c : fill) - stats[rl]) * stats[128 + rl];
-        dsv[i] = on ? p * (__uint_as_float(xp[i]) - stats[256 + rl]) * inv_c : 0.0f;
+      for (int p = 0; p < 2; ++p) {
+        uint32_t xs[16], xp[16];
+        tmem_ld16(S_t + lanes + g * 32 + 16 * p, xs);
+        tmem_ld16(P_t + lanes + g * 32 + 16 * p, xp);
+        float dsv[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int rl = g * 32 + 16 * p + i;
+          const bool on = (qbits >> (16 * p + i)) & 1u;
+          const float pr = __expf((on ? __uint_as_float(xs[i]) * inv_c : fill) - stats[rl]) * stats[128 + rl];
+          dsv[i] = on ? pr * (__uint_as_float(xp[i]) - stats[256 + rl]) * inv_c : 0.0f;
+        }
+        put16(ch, ch + L::CB, row, 16 * p, dsv);
       }
-      put_chunk(C0 + 2 * g * L::CB, C0 + (2 * g + 1) * L::CB, row, dsv);
     }
     proxy_fence();
     fence_before();
@@ -770,40 +873,53 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
     if (!(ok = cta_next(bar_c, nc, abort, err, 44))) break;
     fence_after();
   }
+  // dk and dv rows through shared memory (pitch 2 D + 4 floats), then 2 D-float row segments.
+  float* ost = (float*)sm;
   if (ok && g * 32 < D) {
-    float* gk = out + (z * T + j) * W;
-    uint32_t x[32], y[32];
+    uint32_t x[32];
     tmem_ld32(K_t + lanes + g * 32, x);
-    tmem_ld32(V_t + lanes + g * 32, y);
 #pragma unroll
-    for (int u = 0; u < 32; u += 4) {
-      *(float4*)(gk + D + g * 32 + u) = make_float4(__uint_as_float(x[u]), __uint_as_float(x[u + 1]), __uint_as_float(x[u + 2]), __uint_as_float(x[u + 3]));
-      *(float4*)(gk + 2 * D + g * 32 + u) = make_float4(__uint_as_float(y[u]), __uint_as_float(y[u + 1]), __uint_as_float(y[u + 2]), __uint_as_float(y[u + 3]));
+    for (int u = 0; u < 32; u += 4)
+      *(float4*)(ost + row * (2 * D + 4) + g * 32 + u) =
+          make_float4(__uint_as_float(x[u]), __uint_as_float(x[u + 1]), __uint_as_float(x[u + 2]), __uint_as_float(x[u + 3]));
+    tmem_ld32(V_t + lanes + g * 32, x);
+#pragma unroll
+    for (int u = 0; u < 32; u += 4)
+      *(float4*)(ost + row * (2 * D + 4) + D + g * 32 + u) =
+          make_float4(__uint_as_float(x[u]), __uint_as_float(x[u + 1]), __uint_as_float(x[u + 2]), __uint_as_float(x[u + 3]));
+  }
+  __syncthreads();
+  if (ok) {
+    constexpr int V4 = D / 2;  // 16-byte vectors per row (2 D floats)
+    for (int i = tid; i < 128 * V4; i += FWD_THREADS) {
+      const int rr = i / V4, c = (i - rr * V4) * 4;
+      *(float4*)(out + (z * T + j0 + rr) * W + D + c) = *(const float4*)(ost + rr * (2 * D + 4) + c);
     }
   }
   tc_teardown(bar_done, tmem, 512u);
 }
 
-template <int T, int D> void set_smem(void (*kern)(float*, const float*, const float*, const float*, const float*, float, float, int*)) {
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FwdLayout<T, D>::SMEM);
+template <int T, int D> void set_smem() {
+  cudaFuncSetAttribute(k_attn_fwd_tc<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, FwdLayout<T, D>::SMEM);
 }
 
 template <int T, int D> void launch_fwd_tc(float* out, const float* q, const float* k, const float* v, const float* mask, const AttnShape& a, int* err,
                                            cudaStream_t s) {
   const long long blocks = a.batch * (T / 128);
-  k_attn_fwd_tc<T, D><<<(unsigned)blocks, FWD_THREADS, FwdLayout<T, D>::SMEM, s>>>(out, q, k, v, mask, 1.0f / a.c, a.fill, err);
+  k_attn_fwd_tc<T, D><<<(unsigned)blocks, FWD_THREADS, FwdLayout<T, D>::SMEM, s>>>(out, q, k, v, mask, a.causal ? 1 : 0, 1.0f / a.c, a.fill, err);
 }
 
 template <int T, int D> void set_smem_bwd() {
-  cudaFuncSetAttribute(k_attn_dq_tc<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdLayout<D>::SMEM);
-  cudaFuncSetAttribute(k_attn_dkdv_tc<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdLayout<D>::SMEM);
+  cudaFuncSetAttribute(k_attn_dq_tc<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdLayout<T, D>::SMEM);
+  cudaFuncSetAttribute(k_attn_dkdv_tc<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdLayout<T, D>::SMEM);
 }
 
 template <int T, int D> void launch_bwd_tc(float* out, const float* q, const float* k, const float* v, const float* mask, const float* fwd,
                                            const float* dout, const AttnShape& a, int* err, cudaStream_t s) {
   const unsigned blocks = (unsigned)(a.batch * (T / 128));
-  k_attn_dq_tc<T, D><<<blocks, FWD_THREADS, BwdLayout<D>::SMEM, s>>>(out, q, k, v, mask, fwd, dout, 1.0f / a.c, a.fill, err);
-  k_attn_dkdv_tc<T, D><<<blocks, FWD_THREADS, BwdLayout<D>::SMEM, s>>>(out, q, k, v, mask, fwd, dout, 1.0f / a.c, a.fill, err);
+  const int causal = a.causal ? 1 : 0;
+  k_attn_dq_tc<T, D><<<blocks, FWD_THREADS, BwdLayout<T, D>::SMEM, s>>>(out, q, k, v, mask, fwd, dout, causal, 1.0f / a.c, a.fill, err);
+  k_attn_dkdv_tc<T, D><<<blocks, FWD_THREADS, BwdLayout<T, D>::SMEM, s>>>(out, q, k, v, mask, fwd, dout, causal, 1.0f / a.c, a.fill, err);
 }
 
 }  // namespace
@@ -811,10 +927,10 @@ template <int T, int D> void launch_bwd_tc(float* out, const float* q, const flo
 void attention_init() {
   static std::once_flag once;
   std::call_once(once, [] {
-    set_smem<128, 32>(k_attn_fwd_tc<128, 32>);
-    set_smem<128, 64>(k_attn_fwd_tc<128, 64>);
-    set_smem<256, 32>(k_attn_fwd_tc<256, 32>);
-    set_smem<256, 64>(k_attn_fwd_tc<256, 64>);
+    set_smem<128, 32>();
+    set_smem<128, 64>();
+    set_smem<256, 32>();
+    set_smem<256, 64>();
     set_smem_bwd<128, 32>();
     set_smem_bwd<128, 64>();
     set_smem_bwd<256, 32>();

@@ -17,6 +17,9 @@ struct AttnShape {
   long long batch = 0;  // Z
   int t = 0, d = 0, dv = 0;
   float c = 1.0f, fill = 0.0f;
+  // The mask is the causal pattern (mask[i][j] != 0 exactly where j <= i, a constant lower
+  // triangle): the tensor-core kernels then compute its bits from the indices.
+  bool causal = false;
 };
 
 // One-time setup (shared-memory limits of the tensor-core kernels); before any graph capture.

@@ -607,6 +607,20 @@ struct Builder {
   }
 
   // The device's fused attention (graph.h AttnFwd / AttnBwd; attention.cuh).
+  // Whether slot `s` holds a constant (T, T) matrix that is nonzero exactly where j <= i (the
+  // causal mask of an attention layer; constants are uploaded once and never rewritten).
+  bool causal_constant(size_t s, int T) const {
+    for (const auto& [slot, t] : p->plan.consts) {
+      if (slot != s) continue;
+      if (t->n() != (size_t)T * (size_t)T) return false;
+      for (int r = 0; r < T; ++r)
+        for (int c = 0; c < T; ++c)
+          if ((t->data.get((size_t)r * T + c) != 0.0) != (c <= r)) return false;
+      return true;
+    }
+    return false;
+  }
+
   Lowered attention(const Instr& i) {
     Lowered l;
     const auto& qs = i.arg_shapes[0];
@@ -622,6 +636,7 @@ struct Builder {
       throw std::runtime_error(std::string("the CUDA device has no kernel for ") + i.op.name() + " of this dtype or length");
     attention_init();
     const auto a = i.args;
+    as.causal = causal_constant(a[3], as.t);
     const size_t dst = i.dst;
     if (i.op.kind == OpKind::AttnFwd) {
       l.run = [=](Ctx& c) {

@@ -355,9 +355,8 @@ std::optional<Tensor> slice_of_constant(const Graph& g, uint32_t src, const Op& 
 // Which attentions are fused: RGC_FUSED_ATTENTION=1 fuses every match and =0 none. By default
 // the device fuses the shapes its tensor-core kernels take (attention.cu) where they measured
 // faster than the unfused plan on a B200: sequence length 128 or 256 with head size 32 (a d256
-// step of 8 heads: 9.77 against 10.32 ms). With head size 64 the kernels run one CTA per SM and
-// the unfused plan (row chains and the GEMM) is faster (a d512 step: 287 against 280 ms), so
-// those stay unfused.
+// step of 8 heads: 9.23 against 10.32 ms) and length 256 with head size 64 (a d512 step: 273.7
+// against 280.2 ms). Length 128 with head size 64 has not been measured and stays unfused.
 enum class AttnFuse { None, Default, All };
 AttnFuse fused_attention_mode() {
   const char* e = getenv("RGC_FUSED_ATTENTION");
@@ -366,7 +365,7 @@ AttnFuse fused_attention_mode() {
   return AttnFuse::Default;
 }
 bool fused_attention_enabled() { return fused_attention_mode() != AttnFuse::None; }
-bool fuse_by_default(size_t t, size_t d, size_t dv) { return (t == 128 || t == 256) && d == 32 && dv == 32; }
+bool fuse_by_default(size_t t, size_t d, size_t dv) { return dv == d && (((t == 128 || t == 256) && d == 32) || (t == 256 && d == 64)); }
 
 struct AttnMatch {
   uint32_t q, k, v, O, dO, dv, dq, dk;

@@ -94,10 +94,11 @@ def test_gpt_step_with_fused_attention_matches_rgs_plan():
             assert rel(a, b) <= 1e-4, f"output {k_}"
 
 
-def test_default_fuses_only_head_size_32_at_tensor_core_lengths(monkeypatch):
-    """By default the device fuses attention of length 128 or 256 with head size 32 (measured
-    faster on a B200) and leaves other shapes (head size 64 among them) to the unfused plan;
-    RGC_FUSED_ATTENTION=0 turns fusion off for every shape."""
+def test_default_fuses_the_shapes_measured_faster(monkeypatch):
+    """By default the device fuses attention of length 128 or 256 with head size 32, and of
+    length 256 with head size 64 (measured faster on a B200), and leaves other shapes (length
+    128 with head size 64 among them) to the unfused plan; RGC_FUSED_ATTENTION=0 turns fusion off
+    for every shape."""
     monkeypatch.delenv("RGC_FUSED_ATTENTION", raising=False)
     rng = np.random.default_rng(9)
 
@@ -110,5 +111,6 @@ def test_default_fuses_only_head_size_32_at_tensor_core_lengths(monkeypatch):
     assert "attention" not in plan((1, 2, 128, 64))
     assert "attention" in plan((1, 2, 128, 32))
     assert "attention" in plan((1, 1, 256, 32))
+    assert "attention" in plan((1, 1, 256, 64))
     monkeypatch.setenv("RGC_FUSED_ATTENTION", "0")
     assert "attention" not in plan((1, 2, 128, 32))
