@@ -9,12 +9,14 @@
 // warp w reads TMEM lanes 32 (w % 4) .. + 31 and, as group w / 4, one 32-column chunk of every
 // 128 columns, so a row's four warps share its chunks.
 //   forward   S = q k^T into TMEM (T columns); pass 1 gives each row's max; then per half of the
-//             keys E = exp(Z - m) goes to shared memory (hi and lo) beside v^T and O += E v
-//             accumulates in TMEM; O / s, m and s leave as the block's contiguous packed rows.
+//             keys E = exp(Z - m) replaces S in TMEM (hi; lo in a TMEM buffer) and O += E v
+//             takes E from TMEM as the product's A operand; O / s, m and s leave as the block's
+//             contiguous packed rows.
 //   backward  two kernels, each recomputing the scores: k_attn_dq_tc (query rows) forms dS per
 //             half of the keys and accumulates dq = dS k; k_attn_dkdv_tc (key rows) works on the
 //             transposes, forming P^T and dS^T and accumulating dv = P^T dO and dk = dS^T q.
-//             D = rowsum(dO * O) comes from the forward's O.
+//             dS, P^T and dS^T, like E, are A operands in TMEM. D = rowsum(dO * O) comes from
+//             the forward's O.
 // A causal mask is computed from the indices; any other mask is packed into bits once per CTA.
 //
 // CUDA-core path (any other T up to 1024 and any d): one warp per row, for the small shapes of
@@ -187,34 +189,6 @@ __device__ __forceinline__ float tf32_lo(float x) { return x - tf32_trunc(x); }
 
 __device__ __forceinline__ float4 lo4(const float4& x) { return make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w)); }
 
-// Rows [0, R) x columns [0, K) of a row-major global block (row stride `ld` floats, 16-byte
-// aligned rows) into K-major hi / lo tiles. Each thread moves four 16-byte vectors at a time,
-// all four loads issued before the first store.
-__device__ __forceinline__ void stage(uint8_t* hi, uint8_t* lo, const float* __restrict__ src, int R, int K, long long ld) {
-  const int k4 = K >> 2, n = R * k4, step = blockDim.x;
-  for (int i0 = threadIdx.x; i0 < n; i0 += 4 * step) {
-    float4 x[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = i0 + u * step;
-      if (i < n) {
-        const int row = i / k4, col = (i - row * k4) << 2;
-        x[u] = *(const float4*)(src + row * ld + col);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = i0 + u * step;
-      if (i < n) {
-        const int row = i / k4, col = (i - row * k4) << 2;
-        const uint32_t off = kmaj(R, row, col);
-        *(float4*)(hi + off) = x[u];
-        *(float4*)(lo + off) = lo4(x[u]);
-      }
-    }
-  }
-}
-
 // The transpose of a 128-row global block of C columns (C = 32 or 64): source rows become the
 // tile's K index and source columns its rows (a K-major tile of C rows over K = 128). Thread i
 // takes the 4 x 4 block i (source rows j..j+3, columns e..e+3); blockDim.x >= 8 C, so one block
@@ -268,6 +242,81 @@ __device__ __forceinline__ void mma3(uint32_t d, uint32_t ah, uint32_t al, uint3
   }
 }
 
+// Two row-major blocks into K-major hi / lo tiles, each thread's loads (up to eight 16-byte
+// vectors) issued before its stores: A with RA rows and B with RB rows, K columns each (row
+// stride `ld` floats, 16-byte aligned rows).
+__device__ __forceinline__ void stage2(uint8_t* ah, uint8_t* al, const float* __restrict__ a, int RA, uint8_t* bh, uint8_t* bl,
+                                       const float* __restrict__ b, int RB, int K, long long ld) {
+  const int k4 = K >> 2, na = RA * k4, n = na + RB * k4, step = blockDim.x;
+  for (int i0 = threadIdx.x; i0 < n; i0 += 8 * step) {
+    float4 x[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * step;
+      if (i < n) {
+        const bool in_a = i < na;
+        const int e = in_a ? i : i - na, row = e / k4, col = (e - row * k4) << 2;
+        x[u] = *(const float4*)((in_a ? a : b) + row * ld + col);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * step;
+      if (i < n) {
+        const bool in_a = i < na;
+        const int e = in_a ? i : i - na, row = e / k4, col = (e - row * k4) << 2;
+        const uint32_t off = kmaj(in_a ? RA : RB, row, col);
+        *(float4*)((in_a ? ah : bh) + off) = x[u];
+        *(float4*)((in_a ? al : bl) + off) = lo4(x[u]);
+      }
+    }
+  }
+}
+
+// TMEM stores of 16 or 32 consecutive columns of the warp's 32 lanes; tmem_st_wait makes them
+// complete before the fence and barrier that hand them to a product.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr), "r"(v[0]), "r"(v[1]),
+      "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]),
+      "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,"
+      "%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]),
+      "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+      "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// One TF32 product with A (128 rows = TMEM lanes, 8 K columns from column address `a`) in TMEM
+// and B from shared memory.
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  const uint32_t no_mask = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\ttcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(no_mask)
+      : "memory");
+}
+
+// D (128 x N) (+)= A (128 x K) B (N x K)^T in 3xTF32 with A in TMEM: hi in columns ah .. ah + K - 1,
+// lo in al .. al + K - 1 (row = lane); B a K-major hi / lo tile pair in shared memory (N rows).
+__device__ __forceinline__ void mma3_ts(uint32_t d, uint32_t ah, uint32_t al, uint32_t bh, uint32_t bl, int N, int K, uint32_t idesc, bool accumulate) {
+  for (int kb = 0; kb < K / 32; ++kb) {
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const uint32_t ao = (uint32_t)(kb * 32 + kk * 8), bo = (uint32_t)(kb * N * 128 + kk * 32);
+      mma_tf32_ts(d, ah + ao, desc_k(bh + bo), idesc, (accumulate || kb || kk) ? 1u : 0u);
+      mma_tf32_ts(d, ah + ao, desc_k(bl + bo), idesc, 1u);
+      mma_tf32_ts(d, al + ao, desc_k(bh + bo), idesc, 1u);
+    }
+  }
+}
+
 __device__ __forceinline__ void proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Waits for `phase` of `bar`, bounded; every thread of the CTA calls it, and the outcome is
@@ -293,18 +342,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
         "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// Writes 16 values of one row (K positions j0 .. j0 + 15, j0 a multiple of 16) of a 128-row
-// K-major chunk tile, hi and lo.
-__device__ __forceinline__ void put16(uint8_t* hi, uint8_t* lo, int row, int j0, const float (&x)[16]) {
-#pragma unroll
-  for (int j = 0; j < 16; j += 4) {
-    const uint32_t off = kmaj(128, row, j0 + j);
-    const float4 v = make_float4(x[j], x[j + 1], x[j + 2], x[j + 3]);
-    *(float4*)(hi + off) = v;
-    *(float4*)(lo + off) = lo4(v);
-  }
 }
 
 __device__ __forceinline__ void tc_teardown(uint64_t* bar_done, uint32_t tmem, uint32_t cols) {
@@ -374,7 +411,7 @@ template <int D>
 __device__ __forceinline__ void query_stats(float* st, const float* __restrict__ fwd, const float* __restrict__ dout, long long row0) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int PER = D / 32;
-  float a[8][PER], o[8][PER];
+  float a[8][PER], o[8][PER], ms[8];
 #pragma unroll
   for (int u = 0; u < 8; ++u) {
     const long long r = row0 + warp * 8 + u;
@@ -383,6 +420,7 @@ __device__ __forceinline__ void query_stats(float* st, const float* __restrict__
       a[u][p] = dout[r * D + p * 32 + lane];
       o[u][p] = fwd[r * (D + 2) + p * 32 + lane];
     }
+    ms[u] = lane < 2 ? fwd[r * (D + 2) + D + lane] : 0.0f;  // lane 0: m, lane 1: s
   }
 #pragma unroll
   for (int u = 0; u < 8; ++u) {
@@ -391,11 +429,11 @@ __device__ __forceinline__ void query_stats(float* st, const float* __restrict__
     for (int p = 1; p < PER; ++p) s = s + a[u][p] * o[u][p];
 #pragma unroll
     for (int off = 16; off; off >>= 1) s = s + __shfl_xor_sync(FULL, s, off);
+    const float mu = __shfl_sync(FULL, ms[u], 0), su = __shfl_sync(FULL, ms[u], 1);
     const int rl = warp * 8 + u;
     if (lane == 0) {
-      const float* f = fwd + (row0 + rl) * (D + 2) + D;
-      st[rl] = f[0];
-      st[128 + rl] = 1.0f / f[1];
+      st[rl] = mu;
+      st[128 + rl] = 1.0f / su;
       st[256 + rl] = s;
     }
   }
@@ -405,24 +443,25 @@ constexpr int FWD_THREADS = 512;
 
 template <int T, int D> struct FwdLayout {
   static constexpr int QB = 128 * D * 4, KB = T * D * 4;
-  static constexpr int VB = D * 128 * 4;   // v^T of one half of the keys: D rows over 128 keys
-  static constexpr int EB = 128 * 32 * 4;  // one 32-key chunk of E
-  static constexpr int PHASE1 = 2 * QB + 2 * KB, PHASE2 = 2 * VB + 8 * EB;
+  static constexpr int VB = D * 128 * 4;  // v^T of one half of the keys: D rows over 128 keys
+  static constexpr int PHASE1 = 2 * QB + 2 * KB, PHASE2 = 2 * VB * (T / 128);
   static constexpr int REGION = PHASE1 > PHASE2 ? PHASE1 : PHASE2;
   static constexpr int WORDS = 128 * (T / 32) * 4;  // the mask bits of the block's rows
   static constexpr int SMEM = 1024 + REGION + WORDS + 2 * 4 * 128 * 4 + 128;
-  static constexpr uint32_t TCOLS = T + D <= 256 ? 256 : 512;
+  static constexpr uint32_t LO = T + D;  // TMEM: S (and E) [0, T), O [T, T + D), E lo [LO, LO + 128)
+  static_assert(LO + 128 <= 512, "TMEM columns");
   static_assert(128 * (D + 2) * 4 <= REGION, "output staging fits the operand region");
 };
 
 // Forward, one CTA of 16 warps per (batch entry, 128 query rows). Warp w reads TMEM lanes
 // 32 (w % 4) .. +31 (query rows) and, as group g = w / 4, the key chunk g of every half of
-// 128 keys, so the four warps of a row share its 32-column chunks. Pass 1 gives each row's
-// maximum (partial maxima combined through shared memory); then per half of the keys
-// E = exp(Z - m) goes to shared memory as four 32-key chunks (hi and lo) beside v^T of the
-// half, and O += E v accumulates in TMEM; each half's v is loaded into registers before the
-// wait that frees its tiles. O is divided by the row's exp-sum and the block's packed rows
-// (O, m, s) leave through shared memory as one contiguous, coalesced store.
+// 128 keys, so the four warps of a row share its 32-column chunks. S = q k^T lands in TMEM;
+// v^T of both halves is staged once the product is done (the loads in flight across its
+// wait). Pass 1 gives each row's maximum (partial maxima combined through shared memory).
+// Per half of the keys, E = exp(Z - m) replaces the half's S columns in TMEM (the hi part) and
+// its lo part goes to a TMEM buffer; O += E v takes E from TMEM. O is divided by the row's
+// exp-sum and the block's packed rows (O, m, s) leave through shared memory as one
+// contiguous, coalesced store.
 template <int T, int D>
 __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
                                                               const float* __restrict__ v, const float* __restrict__ mask, int causal, float inv_c,
@@ -432,7 +471,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *Qh = sm, *Ql = Qh + L::QB, *Kh = Ql + L::QB, *Kl = Kh + L::KB;  // phase 1
-  uint8_t *Vh = sm, *Vl = Vh + L::VB, *E0 = Vl + L::VB;                     // phase 2: chunk g at E0 + 2 g EB (hi), + EB (lo)
+  uint8_t* V0 = sm;                                                         // phase 2: half h at V0 + 2 h VB (hi), + VB (lo)
   float* ost = (float*)sm;                                                  // epilogue: the block's packed rows
   uint32_t* words = (uint32_t*)(sm + L::REGION);                            // [128][NW]
   float* part = (float*)(sm + L::REGION + L::WORDS);                        // [2][4][128]: partial max, partial sum
@@ -455,7 +494,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tslot)), "r"(L::TCOLS) : "memory");
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tslot)), "r"(512u) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (!causal) pack_mask(words, mask, T, r0, 128, 0, T);
@@ -464,11 +503,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
   fence_after();
   const uint32_t tmem = *tslot;
   const uint32_t lanes = (uint32_t)(lq * 32) << 16;
-  const uint32_t S_t = tmem, O_t = tmem + T;
+  const uint32_t S_t = tmem, O_t = tmem + T, LO_t = tmem + L::LO;
 
   // S = q k^T.
-  stage(Qh, Ql, q, 128, D, D);
-  stage(Kh, Kl, k, T, D, D);
+  stage2(Qh, Ql, q, 128, Kh, Kl, k, T, D, D);
   proxy_fence();
   __syncthreads();
   if (tid == 0) {
@@ -479,6 +517,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
   TBlock vb = load_t(v, D, D);  // v^T of the first half, in flight across the wait
   bool ok = cta_wait(bar_s, 0, abort, err, 21);
   fence_after();
+  store_t(V0, V0 + L::VB, vb, D);
+  if (NH > 1) vb = load_t(v + 128 * D, D, D);
 
   // Pass 1: the mask bits of this thread's chunks and the row maximum.
   uint32_t bits[NH];
@@ -496,48 +536,37 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
     }
     part[g * 128 + row] = m;
   }
+  if (NH > 1) store_t(V0 + 2 * L::VB, V0 + 3 * L::VB, vb, D);
   __syncthreads();
   if (ok) m = nan_max(nan_max(part[row], part[128 + row]), nan_max(part[256 + row], part[384 + row]));
 
-  // Per half of the keys: v^T of the half and the half's E chunks in shared memory, then
-  // O += E v (the S products are complete, so their operand space is free).
+  // Per half of the keys: E over the half's S columns (hi) and into the lo buffer, then O += E v.
   float sum = 0.0f;
 #pragma unroll 1
   for (int h = 0; h < NH && ok; ++h) {
-    if (h > 0) {
-      vb = load_t(v + (long long)h * 128 * D, D, D);
-      if (!(ok = cta_wait(bar_o, (uint32_t)((h - 1) & 1), abort, err, 22))) break;
-    }
-    store_t(Vh, Vl, vb, D);
     const int c0 = h * 128 + g * 32;
     uint32_t x[32];
     tmem_ld32(S_t + lanes + c0, x);
-    uint8_t* eh = E0 + 2 * g * L::EB;
-    uint8_t* el = eh + L::EB;
 #pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-      float e[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        e[u] = __expf((((bits[h] >> (j + u)) & 1u) ? __uint_as_float(x[j + u]) * inv_c : fill) - m);
-        sum = sum + e[u];
-      }
-      const uint32_t off = kmaj(128, row, j);
-      const float4 ev = make_float4(e[0], e[1], e[2], e[3]);
-      *(float4*)(eh + off) = ev;
-      *(float4*)(el + off) = lo4(ev);
+    for (int j = 0; j < 32; ++j) {
+      const float e = __expf((((bits[h] >> j) & 1u) ? __uint_as_float(x[j]) * inv_c : fill) - m);
+      sum = sum + e;
+      x[j] = __float_as_uint(e);
     }
+    tmem_st32(S_t + lanes + c0, x);
+    // The lo buffer is free once the previous half's products are done.
+    if (h > 0 && !(ok = cta_wait(bar_o, (uint32_t)((h - 1) & 1), abort, err, 22))) break;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = __float_as_uint(tf32_lo(__uint_as_float(x[j])));
+    tmem_st32(LO_t + lanes + g * 32, x);
+    tmem_st_wait();
     proxy_fence();
     fence_before();
     __syncthreads();
     if (tid == 0) {
       fence_after();
-#pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
-        uint8_t* ch = E0 + 2 * cc * L::EB;
-        const uint32_t vo = (uint32_t)(cc * D * 128);
-        mma3(O_t, saddr(ch), saddr(ch + L::EB), saddr(Vh) + vo, saddr(Vl) + vo, D, 32, idesc_tf32(128, D), h > 0 || cc > 0);
-      }
+      uint8_t* vh = V0 + 2 * h * L::VB;
+      mma3_ts(O_t, S_t + h * 128, LO_t, saddr(vh), saddr(vh + L::VB), D, 128, idesc_tf32(128, D), h > 0);
       mma_commit(bar_o);
     }
   }
@@ -566,27 +595,28 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
     const float4* srcv = (const float4*)ost;
     for (int i = tid; i < 32 * (D + 2); i += FWD_THREADS) dst[i] = srcv[i];
   }
-  tc_teardown(bar_done, tmem, L::TCOLS);
+  tc_teardown(bar_done, tmem, 512u);
 }
 
-// Shared-memory plan of the backward kernels: phases a and b stage two 128-row operands (hi and
-// lo); phase c holds one transposed operand (128 columns) and the four 32-column chunk tiles
-// the four warp groups write; then the query statistics and the mask words.
+// Shared-memory plan of the backward kernels: region 0 stages two 128-row operands (hi and lo)
+// for the score products; region 1 one transposed operand (D rows over 128 columns, hi and lo);
+// then the query statistics and the mask words. TMEM: the scores (then P or its transpose, hi)
+// [0, 128), dP (then dS, hi) [128, 256), a lo buffer of 128 columns and the accumulators.
 template <int T, int D> struct BwdLayout {
   static constexpr int TB = 128 * D * 4;  // a 128 x D tile, or its transpose
-  static constexpr int CB = 128 * 32 * 4; // a 128 x 32 chunk tile
-  static constexpr int AB = 4 * TB, CPH = 2 * TB + 8 * CB;
-  static constexpr int REGION = AB > CPH ? AB : CPH;
+  static constexpr int R0 = 4 * TB, R1 = 2 * TB;
+  static constexpr int REGION = R0 + R1;
   static constexpr int WORDS = 128 * (T / 32) * 4;
   static constexpr int SMEM = 1024 + REGION + 3 * 128 * 4 + WORDS + 128;
   static_assert(128 * (2 * D + 4) * 4 <= REGION, "output staging fits the operand region");
+  static_assert(384 + 2 * D <= 512, "TMEM columns");
 };
 
 // dq, one CTA of 16 warps per (batch entry, 128 query rows); warp w reads TMEM lanes 32 (w % 4)
 // (query rows) and, as group g = w / 4, key chunk g of each half. Per half of the keys (128):
-// S = q k^T and dP = dO v^T into TMEM, then k^T of the half (loaded before the dP wait) and the
-// four dS chunks in shared memory, and dq += dS k. dq leaves through shared memory in
-// row-contiguous stores.
+// S = q k^T, then dP = dO v^T with k^T of the half staged beside it; dS replaces S in TMEM (hi)
+// with its lo part in the lo buffer, and dq += dS k takes dS from TMEM. dq leaves through
+// shared memory in row-contiguous stores.
 template <int T, int D>
 __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
                                                              const float* __restrict__ v, const float* __restrict__ mask, const float* __restrict__ fwd,
@@ -595,8 +625,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
   constexpr int NQB = T / 128, NH = T / 128, W = 3 * D, NW = T / 32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t *Ah = sm, *Al = Ah + L::TB, *Bh = Al + L::TB, *Bl = Bh + L::TB;  // phases a, b
-  uint8_t *Th = sm, *Tl = Th + L::TB, *C0 = Tl + L::TB;                  // phase c: k^T, chunk g at C0 + 2 g CB
+  uint8_t *Ah = sm, *Al = Ah + L::TB, *Bh = Al + L::TB, *Bl = Bh + L::TB;  // region 0
+  uint8_t *Xh = sm + L::R0, *Xl = Xh + L::TB;                            // region 1: k^T of the half
   float* stats = (float*)(sm + L::REGION);                                // [3][128]
   uint32_t* words = (uint32_t*)(stats + 3 * 128);                         // [128][NW]
   uint64_t* bars = (uint64_t*)(sm + L::REGION + 3 * 128 * 4 + L::WORDS);
@@ -628,7 +658,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tslot, lanes = (uint32_t)(lq * 32) << 16;
-  const uint32_t S_t = tmem, P_t = tmem + 128, Q_t = tmem + 256;
+  const uint32_t S_t = tmem, P_t = tmem + 128, Q_t = tmem + 256, LO_t = tmem + 256 + D;
   const float m = stats[row], inv_sum = stats[128 + row], Dr = stats[256 + row];
 
   bool ok = true;
@@ -636,8 +666,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
 #pragma unroll 1
   for (int h = 0; h < NH && ok; ++h) {
     // a: S = q k_h^T (the previous half's products are complete).
-    stage(Ah, Al, qb, 128, D, D);
-    stage(Bh, Bl, k + (long long)h * 128 * D, 128, D, D);
+    stage2(Ah, Al, qb, 128, Bh, Bl, k + (long long)h * 128 * D, 128, D, D);
     proxy_fence();
     __syncthreads();
     if (tid == 0) {
@@ -645,10 +674,11 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
       mma3(S_t, saddr(Ah), saddr(Al), saddr(Bh), saddr(Bl), 128, D, idesc_tf32(128, 128), false);
       mma_commit(bar_a);
     }
+    const TBlock kt = load_t(k + (long long)h * 128 * D, D, D);
     if (!(ok = cta_next(bar_a, na, abort, err, 31))) break;
-    // b: dP = dO v_h^T.
-    stage(Ah, Al, db, 128, D, D);
-    stage(Bh, Bl, v + (long long)h * 128 * D, 128, D, D);
+    // b: dP = dO v_h^T, and k_h^T in region 1.
+    stage2(Ah, Al, db, 128, Bh, Bl, v + (long long)h * 128 * D, 128, D, D);
+    store_t(Xh, Xl, kt, D);
     proxy_fence();
     __syncthreads();
     if (tid == 0) {
@@ -656,41 +686,35 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
       mma3(P_t, saddr(Ah), saddr(Al), saddr(Bh), saddr(Bl), 128, D, idesc_tf32(128, 128), false);
       mma_commit(bar_b);
     }
-    const TBlock kt = load_t(k + (long long)h * 128 * D, D, D);
     if (!(ok = cta_next(bar_b, nb, abort, err, 32))) break;
     fence_after();
-    // c: k_h^T, and this group's dS chunk, in two 16-column pieces.
-    store_t(Th, Tl, kt, D);
+    // c: this group's dS chunk in two 16-column pieces, hi over S and lo into the buffer.
     {
       const int c0 = h * 128 + g * 32;
       const uint32_t bits = causal ? causal_keys(r, c0) : words[row * NW + (c0 >> 5)];
-      uint8_t* ch = C0 + 2 * g * L::CB;
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
         uint32_t xs[16], xp[16];
         tmem_ld16(S_t + lanes + g * 32 + 16 * p, xs);
         tmem_ld16(P_t + lanes + g * 32 + 16 * p, xp);
-        float ds[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const bool on = (bits >> (16 * p + j)) & 1u;
           const float pr = __expf((on ? __uint_as_float(xs[j]) * inv_c : fill) - m) * inv_sum;
-          ds[j] = on ? pr * (__uint_as_float(xp[j]) - Dr) * inv_c : 0.0f;
+          const float ds = on ? pr * (__uint_as_float(xp[j]) - Dr) * inv_c : 0.0f;
+          xs[j] = __float_as_uint(ds);
+          xp[j] = __float_as_uint(tf32_lo(ds));
         }
-        put16(ch, ch + L::CB, row, 16 * p, ds);
+        tmem_st16(S_t + lanes + g * 32 + 16 * p, xs);
+        tmem_st16(LO_t + lanes + g * 32 + 16 * p, xp);
       }
     }
-    proxy_fence();
+    tmem_st_wait();
     fence_before();
     __syncthreads();
     if (tid == 0) {
       fence_after();
-#pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
-        const uint32_t ko = (uint32_t)(cc * D * 128);
-        uint8_t* ch = C0 + 2 * cc * L::CB;
-        mma3(Q_t, saddr(ch), saddr(ch + L::CB), saddr(Th) + ko, saddr(Tl) + ko, D, 32, idesc_tf32(128, D), h > 0 || cc > 0);
-      }
+      mma3_ts(Q_t, S_t, LO_t, saddr(Xh), saddr(Xl), D, 128, idesc_tf32(128, D), h > 0);
       mma_commit(bar_c);
     }
     if (!(ok = cta_next(bar_c, nc, abort, err, 33))) break;
@@ -719,10 +743,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
 
 // dk and dv, one CTA of 16 warps per (batch entry, 128 keys); warp w reads TMEM lanes 32 (w % 4)
 // (key rows) and, as group g = w / 4, query chunk g of each half. Per half of the queries
-// (128): S^T = k q^T and dP^T = v dO^T into TMEM; then dO^T of the half and the four P^T chunks
-// in shared memory, dv += P^T dO; then q^T and the four dS^T chunks, dk += dS^T q. The half's
-// query statistics (max, 1 / exp-sum, D) sit in shared memory; the transposed operands are
-// loaded before the waits that free their tiles. dk and dv leave through shared memory.
+// (128): S^T = k q^T; dP^T = v dO^T with dO^T of the half staged beside it; P^T replaces S^T in
+// TMEM (hi, lo in the buffer) and dv += P^T dO; then, with q^T staged over the score operands,
+// dS^T replaces dP^T (hi, lo in the buffer) and dk += dS^T q. The half's query statistics (max,
+// 1 / exp-sum, D) sit in shared memory. dk and dv leave through shared memory.
 template <int T, int D>
 __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
                                                                const float* __restrict__ v, const float* __restrict__ mask,
@@ -732,13 +756,13 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
   constexpr int NKB = T / 128, NH = T / 128, W = 3 * D;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t *Ah = sm, *Al = Ah + L::TB, *Bh = Al + L::TB, *Bl = Bh + L::TB;  // phases a, b
-  uint8_t *Th = sm, *Tl = Th + L::TB, *C0 = Tl + L::TB;                  // phase c
+  uint8_t *Ah = sm, *Al = Ah + L::TB, *Bh = Al + L::TB, *Bl = Bh + L::TB;  // region 0; q^T of the half at Ah / Al after dP^T
+  uint8_t *Xh = sm + L::R0, *Xl = Xh + L::TB;                            // region 1: dO^T of the half
   float* stats = (float*)(sm + L::REGION);                                // [3][128]
   uint32_t* words = (uint32_t*)(stats + 3 * 128);                         // [T][4]: queries x the block's 128 keys
   uint64_t* bars = (uint64_t*)(sm + L::REGION + 3 * 128 * 4 + L::WORDS);
-  uint64_t *bar_a = bars, *bar_b = bars + 1, *bar_c = bars + 2, *bar_done = bars + 3;
-  uint32_t* tslot = (uint32_t*)(bars + 4);
+  uint64_t *bar_a = bars, *bar_b = bars + 1, *bar_c = bars + 2, *bar_d = bars + 3, *bar_done = bars + 4;
+  uint32_t* tslot = (uint32_t*)(bars + 5);
   volatile int* abort = (volatile int*)(tslot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, lq = warp & 3, g = warp >> 2;
@@ -751,7 +775,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
   const float* dz = dout + z * T * D;
 
   if (tid == 0) {
-    for (int b = 0; b < 4; ++b) mbar_init(&bars[b], 1);
+    for (int b = 0; b < 5; ++b) mbar_init(&bars[b], 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -764,35 +788,23 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tslot, lanes = (uint32_t)(lq * 32) << 16;
-  const uint32_t S_t = tmem, P_t = tmem + 128, V_t = tmem + 256, K_t = tmem + 256 + D;
+  const uint32_t S_t = tmem, P_t = tmem + 128, LO_t = tmem + 256, V_t = tmem + 384, K_t = tmem + 384 + D;
 
   bool ok = true;
-  int na = 0, nb = 0, nc = 0;
+  int na = 0, nb = 0, nc = 0, nd = 0;
 #pragma unroll 1
   for (int h = 0; h < NH && ok; ++h) {
     const int q0 = h * 128;
     // The half's query statistics (the previous half's readers finished at its last wait).
     query_stats<D>(stats, fwd, dout, z * T + q0);
     // a: S^T = k q_h^T.
-    stage(Ah, Al, kb, 128, D, D);
-    stage(Bh, Bl, qz + (long long)q0 * D, 128, D, D);
+    stage2(Ah, Al, kb, 128, Bh, Bl, qz + (long long)q0 * D, 128, D, D);
     proxy_fence();
     __syncthreads();
     if (tid == 0) {
       fence_after();
       mma3(S_t, saddr(Ah), saddr(Al), saddr(Bh), saddr(Bl), 128, D, idesc_tf32(128, 128), false);
       mma_commit(bar_a);
-    }
-    if (!(ok = cta_next(bar_a, na, abort, err, 41))) break;
-    // b: dP^T = v dO_h^T.
-    stage(Ah, Al, vb, 128, D, D);
-    stage(Bh, Bl, dz + (long long)q0 * D, 128, D, D);
-    proxy_fence();
-    __syncthreads();
-    if (tid == 0) {
-      fence_after();
-      mma3(P_t, saddr(Ah), saddr(Al), saddr(Bh), saddr(Bl), 128, D, idesc_tf32(128, 128), false);
-      mma_commit(bar_b);
     }
     const TBlock dt = load_t(dz + (long long)q0 * D, D, D);
     // The mask bits of this key over the chunk's queries q0 + 32 g ...
@@ -803,74 +815,74 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
 #pragma unroll 8
       for (int i = 0; i < 32; ++i) qbits |= ((words[(q0 + g * 32 + i) * 4 + (row >> 5)] >> lane) & 1u) << i;
     }
-    if (!(ok = cta_next(bar_b, nb, abort, err, 42))) break;
-    fence_after();
-    // c1: dO_h^T and this group's P^T chunk (query columns q0 + 32 g ..).
-    store_t(Th, Tl, dt, D);
-    {
-      uint8_t* ch = C0 + 2 * g * L::CB;
-#pragma unroll
-      for (int p = 0; p < 2; ++p) {
-        uint32_t xs[16];
-        tmem_ld16(S_t + lanes + g * 32 + 16 * p, xs);
-        float pv[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int rl = g * 32 + 16 * p + i;
-          pv[i] = __expf((((qbits >> (16 * p + i)) & 1u) ? __uint_as_float(xs[i]) * inv_c : fill) - stats[rl]) * stats[128 + rl];
-        }
-        put16(ch, ch + L::CB, row, 16 * p, pv);
-      }
-    }
+    if (!(ok = cta_next(bar_a, na, abort, err, 41))) break;
+    // b: dP^T = v dO_h^T, and dO_h^T in region 1.
+    stage2(Ah, Al, vb, 128, Bh, Bl, dz + (long long)q0 * D, 128, D, D);
+    store_t(Xh, Xl, dt, D);
     proxy_fence();
+    __syncthreads();
+    if (tid == 0) {
+      fence_after();
+      mma3(P_t, saddr(Ah), saddr(Al), saddr(Bh), saddr(Bl), 128, D, idesc_tf32(128, 128), false);
+      mma_commit(bar_b);
+    }
+    fence_after();
+    // c1: this group's P^T chunk (query columns q0 + 32 g ..) over S^T (hi) and into the buffer.
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      uint32_t xs[16], xl[16];
+      tmem_ld16(S_t + lanes + g * 32 + 16 * p, xs);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int rl = g * 32 + 16 * p + i;
+        const float pv = __expf((((qbits >> (16 * p + i)) & 1u) ? __uint_as_float(xs[i]) * inv_c : fill) - stats[rl]) * stats[128 + rl];
+        xs[i] = __float_as_uint(pv);
+        xl[i] = __float_as_uint(tf32_lo(pv));
+      }
+      tmem_st16(S_t + lanes + g * 32 + 16 * p, xs);
+      tmem_st16(LO_t + lanes + g * 32 + 16 * p, xl);
+    }
+    tmem_st_wait();
     fence_before();
     __syncthreads();
     if (tid == 0) {
       fence_after();
-#pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
-        const uint32_t qo = (uint32_t)(cc * D * 128);
-        uint8_t* ch = C0 + 2 * cc * L::CB;
-        mma3(V_t, saddr(ch), saddr(ch + L::CB), saddr(Th) + qo, saddr(Tl) + qo, D, 32, idesc_tf32(128, D), h > 0 || cc > 0);
-      }
+      mma3_ts(V_t, S_t, LO_t, saddr(Xh), saddr(Xl), D, 128, idesc_tf32(128, D), h > 0);
       mma_commit(bar_c);
     }
     const TBlock qt = load_t(qz + (long long)q0 * D, D, D);
+    // dP^T done: region 0 takes q_h^T. dv done: the lo buffer is free.
+    if (!(ok = cta_next(bar_b, nb, abort, err, 42))) break;
+    store_t(Ah, Al, qt, D);
     if (!(ok = cta_next(bar_c, nc, abort, err, 43))) break;
-    // c2: q_h^T and the dS^T chunks (P^T recomputed from the scores still in TMEM).
-    store_t(Th, Tl, qt, D);
-    {
-      uint8_t* ch = C0 + 2 * g * L::CB;
+    fence_after();
+    // c2: the dS^T chunk from P^T and dP^T in TMEM, over dP^T (hi) and into the buffer.
 #pragma unroll
-      for (int p = 0; p < 2; ++p) {
-        uint32_t xs[16], xp[16];
-        tmem_ld16(S_t + lanes + g * 32 + 16 * p, xs);
-        tmem_ld16(P_t + lanes + g * 32 + 16 * p, xp);
-        float dsv[16];
+    for (int p = 0; p < 2; ++p) {
+      uint32_t xs[16], xp[16];
+      tmem_ld16(S_t + lanes + g * 32 + 16 * p, xs);
+      tmem_ld16(P_t + lanes + g * 32 + 16 * p, xp);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int rl = g * 32 + 16 * p + i;
-          const bool on = (qbits >> (16 * p + i)) & 1u;
-          const float pr = __expf((on ? __uint_as_float(xs[i]) * inv_c : fill) - stats[rl]) * stats[128 + rl];
-          dsv[i] = on ? pr * (__uint_as_float(xp[i]) - stats[256 + rl]) * inv_c : 0.0f;
-        }
-        put16(ch, ch + L::CB, row, 16 * p, dsv);
+      for (int i = 0; i < 16; ++i) {
+        const int rl = g * 32 + 16 * p + i;
+        const bool on = (qbits >> (16 * p + i)) & 1u;
+        const float ds = on ? __uint_as_float(xs[i]) * (__uint_as_float(xp[i]) - stats[256 + rl]) * inv_c : 0.0f;
+        xp[i] = __float_as_uint(ds);
+        xs[i] = __float_as_uint(tf32_lo(ds));
       }
+      tmem_st16(P_t + lanes + g * 32 + 16 * p, xp);
+      tmem_st16(LO_t + lanes + g * 32 + 16 * p, xs);
     }
+    tmem_st_wait();
     proxy_fence();
     fence_before();
     __syncthreads();
     if (tid == 0) {
       fence_after();
-#pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
-        const uint32_t qo = (uint32_t)(cc * D * 128);
-        uint8_t* ch = C0 + 2 * cc * L::CB;
-        mma3(K_t, saddr(ch), saddr(ch + L::CB), saddr(Th) + qo, saddr(Tl) + qo, D, 32, idesc_tf32(128, D), h > 0 || cc > 0);
-      }
-      mma_commit(bar_c);
+      mma3_ts(K_t, P_t, LO_t, saddr(Ah), saddr(Al), D, 128, idesc_tf32(128, D), h > 0);
+      mma_commit(bar_d);
     }
-    if (!(ok = cta_next(bar_c, nc, abort, err, 44))) break;
+    if (!(ok = cta_next(bar_d, nd, abort, err, 44))) break;
     fence_after();
   }
   // dk and dv rows through shared memory (pitch 2 D + 4 floats), then 2 D-float row segments.

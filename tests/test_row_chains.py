@@ -65,10 +65,12 @@ def test_softmax_chain_stores_what_later_steps_read():
     assert all(flag for flags in ch["store"][2:] for flag in flags), "exponentials, sums and probabilities are stored"
 
 
-def test_backward_softmax_chain_defers_the_fill_broadcast():
-    """In the greedy-order plan of a d512 layer (compiled, not run), the softmax backward reads a
-    broadcast zero through its source; the broadcast step, which writes the slot the chain's first
-    member reads dP from, runs after the chain."""
+def test_backward_softmax_chain_defers_the_fill_broadcast(monkeypatch):
+    """In the greedy-order plan of a d512 layer (compiled, not run; attention unfused, as the
+    device fuses this shape by default), the softmax backward reads a broadcast zero through its
+    source; the broadcast step, which writes the slot the chain's first member reads dP from,
+    runs after the chain."""
+    monkeypatch.setenv("RGC_FUSED_ATTENTION", "0")
     fn, args = gpt_step(d=512, heads=8, layers=1, block=256, batch=512)
     c = F.compile(fn, args, validate="none", device="cuda-plan")
     ps = summary(c)
