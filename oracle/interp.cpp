@@ -790,18 +790,35 @@ void key_split(const Instr& i, std::vector<Buf>& s) {
 // Sums run in index order. The backward recomputes P from the saved (m, s) and gives
 // dS_j = mask_ij ? P_j (dP_j - sum_l P_l dP_l) / c : 0 with dP_j = dO_i . v_j, then
 // dq = dS k, dk = dS^T q, dv = P^T dO.
+// With a third attribute H (value = [c, fill, H]) q, k and v come packed as one (B, T, 3, H, d)
+// tensor (the projection's output before the head split), batch entry b * H + h; dO comes as
+// (B, T, H, d) and the backward's result is the gradient of that packed (B, T, 3, H, d) tensor.
 struct AttnDims {
   size_t batch, t, d, dv;
+  size_t heads = 0;  // > 0: the packed (B, T, 3, H, d) layout
 };
 AttnDims attn_dims(const Instr& i) {
   const auto& q = i.arg_shapes[0];
   size_t r = q.size();
   AttnDims a;
+  if (i.op.value->n() == 3) {
+    a.heads = (size_t)i.op.value->data.get(2);
+    a.t = q[1];
+    a.d = a.dv = q[4];
+    a.batch = q[0] * a.heads;
+    return a;
+  }
   a.t = q[r - 2];
   a.d = q[r - 1];
   a.dv = i.arg_shapes[2][r - 1];
   a.batch = product(q) / (a.t * a.d);
   return a;
+}
+
+// Element (batch entry z, row t, column e) of part `which` (0 q, 1 k, 2 v) of the packed layout.
+inline size_t packed_at(const AttnDims& a, size_t which, size_t z, size_t t, size_t e) {
+  const size_t b = z / a.heads, h = z - b * a.heads;
+  return ((b * a.t + t) * 3 + which) * a.heads * a.d + h * a.d + e;
 }
 
 // Z_ij for query row i, key j; `mask_row` is row i of the (T, T) mask.
@@ -811,15 +828,43 @@ template <typename T> T attn_score(const T* q, const T* k, const T* mask_row, si
   return mask_row[j] != (T)0 ? acc / c : fill;
 }
 
+// Batch entry z's q, k, v (and dO), contiguous (T, d) rows, from either layout.
+template <typename T> struct AttnEntry {
+  std::vector<T> q, k, v, dout;
+  void load(const AttnDims& a, const Instr& i, std::vector<Buf>& s, size_t z, bool with_dout) {
+    const T *Q = S<T>(s[i.args[0]]), *K = a.heads ? Q : S<T>(s[i.args[1]]), *V = a.heads ? Q : S<T>(s[i.args[2]]);
+    q.resize(a.t * a.d);
+    k.resize(a.t * a.d);
+    v.resize(a.t * a.dv);
+    for (size_t t = 0; t < a.t; ++t) {
+      for (size_t e = 0; e < a.d; ++e) {
+        q[t * a.d + e] = a.heads ? Q[packed_at(a, 0, z, t, e)] : Q[(z * a.t + t) * a.d + e];
+        k[t * a.d + e] = a.heads ? K[packed_at(a, 1, z, t, e)] : K[(z * a.t + t) * a.d + e];
+      }
+      for (size_t e = 0; e < a.dv; ++e) v[t * a.dv + e] = a.heads ? V[packed_at(a, 2, z, t, e)] : V[(z * a.t + t) * a.dv + e];
+    }
+    if (!with_dout) return;
+    const T* DO = S<T>(s[i.args[a.heads ? 3 : 5]]);
+    dout.resize(a.t * a.dv);
+    for (size_t t = 0; t < a.t; ++t)
+      for (size_t e = 0; e < a.dv; ++e) {
+        const size_t b = a.heads ? z / a.heads : 0, h = a.heads ? z - b * a.heads : 0;
+        dout[t * a.dv + e] = a.heads ? DO[((b * a.t + t) * a.heads + h) * a.dv + e] : DO[(z * a.t + t) * a.dv + e];
+      }
+  }
+};
+
 template <typename T> void attn_fwd(const Instr& i, std::vector<Buf>& s) {
   const AttnDims a = attn_dims(i);
   const T c = (T)i.op.value->data.get(0), fill = (T)i.op.value->data.get(1);
-  const T *Q = S<T>(s[i.args[0]]), *K = S<T>(s[i.args[1]]), *V = S<T>(s[i.args[2]]), *M = S<T>(s[i.args[3]]);
+  const T* M = S<T>(s[i.args[a.heads ? 1 : 3]]);
   T* out = S<T>(s[i.dst]);
   const size_t w = a.dv + 2;
   std::vector<T> z(a.t);
+  AttnEntry<T> en;
   for (size_t b = 0; b < a.batch; ++b) {
-    const T *q = Q + b * a.t * a.d, *k = K + b * a.t * a.d, *v = V + b * a.t * a.dv;
+    en.load(a, i, s, b, false);
+    const T *q = en.q.data(), *k = en.k.data(), *v = en.v.data();
     for (size_t r = 0; r < a.t; ++r) {
       T m = -std::numeric_limits<T>::infinity();
       for (size_t j = 0; j < a.t; ++j) {
@@ -846,16 +891,18 @@ template <typename T> void attn_fwd(const Instr& i, std::vector<Buf>& s) {
 template <typename T> void attn_bwd(const Instr& i, std::vector<Buf>& s) {
   const AttnDims a = attn_dims(i);
   const T c = (T)i.op.value->data.get(0), fill = (T)i.op.value->data.get(1);
-  const T *Q = S<T>(s[i.args[0]]), *K = S<T>(s[i.args[1]]), *V = S<T>(s[i.args[2]]), *M = S<T>(s[i.args[3]]);
-  // args[4]: the forward's packed output, (..., T, dv + 2) = O, row max, row exp-sum.
-  const T *FW = S<T>(s[i.args[4]]), *DO = S<T>(s[i.args[5]]);
+  const T* M = S<T>(s[i.args[a.heads ? 1 : 3]]);
+  // The forward's packed output, (..., T, dv + 2) = O, row max, row exp-sum.
+  const T* FW = S<T>(s[i.args[a.heads ? 2 : 4]]);
   T* out = S<T>(s[i.dst]);
   const size_t w = 2 * a.d + a.dv, fw = a.dv + 2;
-  std::fill(out, out + a.batch * a.t * w, (T)0);
-  std::vector<T> p(a.t), dp(a.t);
+  std::vector<T> p(a.t), dp(a.t), g(a.t * w);
+  AttnEntry<T> en;
+  if (!a.heads) std::fill(out, out + a.batch * a.t * w, (T)0);
   for (size_t b = 0; b < a.batch; ++b) {
-    const T *q = Q + b * a.t * a.d, *k = K + b * a.t * a.d, *v = V + b * a.t * a.dv, *dout = DO + b * a.t * a.dv;
-    T* g = out + b * a.t * w;
+    en.load(a, i, s, b, true);
+    const T *q = en.q.data(), *k = en.k.data(), *v = en.v.data(), *dout = en.dout.data();
+    std::fill(g.begin(), g.end(), (T)0);
     for (size_t r = 0; r < a.t; ++r) {
       const T* o = FW + (b * a.t + r) * fw;
       const T m = o[a.dv], sum = o[a.dv + 1];
@@ -875,6 +922,17 @@ template <typename T> void attn_bwd(const Instr& i, std::vector<Buf>& s) {
           g[j * w + a.d + e] = g[j * w + a.d + e] + ds * q[r * a.d + e];     // dk
         }
         for (size_t e = 0; e < a.dv; ++e) g[j * w + 2 * a.d + e] = g[j * w + 2 * a.d + e] + p[j] * dout[r * a.dv + e];  // dv
+      }
+    }
+    for (size_t t = 0; t < a.t; ++t) {
+      if (!a.heads) {
+        std::copy(g.begin() + t * w, g.begin() + (t + 1) * w, out + (b * a.t + t) * w);
+        continue;
+      }
+      for (size_t e = 0; e < a.d; ++e) {
+        out[packed_at(a, 0, b, t, e)] = g[t * w + e];
+        out[packed_at(a, 1, b, t, e)] = g[t * w + a.d + e];
+        out[packed_at(a, 2, b, t, e)] = g[t * w + 2 * a.d + e];
       }
     }
   }

@@ -243,10 +243,10 @@ __device__ __forceinline__ void mma3(uint32_t d, uint32_t ah, uint32_t al, uint3
 }
 
 // Two row-major blocks into K-major hi / lo tiles, each thread's loads (up to eight 16-byte
-// vectors) issued before its stores: A with RA rows and B with RB rows, K columns each (row
-// stride `ld` floats, 16-byte aligned rows).
-__device__ __forceinline__ void stage2(uint8_t* ah, uint8_t* al, const float* __restrict__ a, int RA, uint8_t* bh, uint8_t* bl,
-                                       const float* __restrict__ b, int RB, int K, long long ld) {
+// vectors) issued before its stores: A with RA rows (row stride lda floats) and B with RB rows
+// (row stride ldb), K columns each, 16-byte aligned rows.
+__device__ __forceinline__ void stage2(uint8_t* ah, uint8_t* al, const float* __restrict__ a, int RA, long long lda, uint8_t* bh, uint8_t* bl,
+                                       const float* __restrict__ b, int RB, long long ldb, int K) {
   const int k4 = K >> 2, na = RA * k4, n = na + RB * k4, step = blockDim.x;
   for (int i0 = threadIdx.x; i0 < n; i0 += 8 * step) {
     float4 x[8];
@@ -256,7 +256,7 @@ __device__ __forceinline__ void stage2(uint8_t* ah, uint8_t* al, const float* __
       if (i < n) {
         const bool in_a = i < na;
         const int e = in_a ? i : i - na, row = e / k4, col = (e - row * k4) << 2;
-        x[u] = *(const float4*)((in_a ? a : b) + row * ld + col);
+        x[u] = *(const float4*)(in_a ? a + row * lda + col : b + row * ldb + col);
       }
     }
 #pragma unroll
@@ -408,16 +408,16 @@ __device__ void pack_mask(uint32_t* words, const float* __restrict__ mask, int T
 // takes rows 8 w .. 8 w + 7, lanes over the row's columns; st[0..127] = m, st[128..255] = 1 / s,
 // st[256..383] = D.
 template <int D>
-__device__ __forceinline__ void query_stats(float* st, const float* __restrict__ fwd, const float* __restrict__ dout, long long row0) {
+__device__ __forceinline__ void query_stats(float* st, const float* __restrict__ fwd, const float* __restrict__ dout, long long ldo) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int PER = D / 32;
   float a[8][PER], o[8][PER], ms[8];
 #pragma unroll
   for (int u = 0; u < 8; ++u) {
-    const long long r = row0 + warp * 8 + u;
+    const long long r = warp * 8 + u;
 #pragma unroll
     for (int p = 0; p < PER; ++p) {
-      a[u][p] = dout[r * D + p * 32 + lane];
+      a[u][p] = dout[r * ldo + p * 32 + lane];
       o[u][p] = fwd[r * (D + 2) + p * 32 + lane];
     }
     ms[u] = lane < 2 ? fwd[r * (D + 2) + D + lane] : 0.0f;  // lane 0: m, lane 1: s
@@ -440,6 +440,30 @@ __device__ __forceinline__ void query_stats(float* st, const float* __restrict__
 }
 
 constexpr int FWD_THREADS = 512;
+
+// Where batch entry z's rows live (AttnShape::heads): with heads = 0, q, k, v and dO are (Z, T, d)
+// row blocks and the backward writes (Z, T, 3 d) rows; with heads = H > 0, entry z = b H + h of
+// q, k, v is part 0, 1, 2 of the packed (B, T, 3, H, d) tensor (row stride 3 H d), dO is
+// (B, T, H, d) (row stride H d) and the backward writes the packed tensor's gradient.
+template <int T, int D> struct Rows {
+  long long xo, ld, dO, ldo;  // q / k / v offset of row 0 and row stride; the same for dO
+  int heads;
+  long long z;
+  __device__ Rows(long long z_, int heads_) : heads(heads_), z(z_) {
+    if (heads) {
+      const long long b = z / heads, h = z - b * heads;
+      xo = (b * T * 3 * heads + h) * D;
+      ld = 3LL * heads * D;
+      dO = (b * T * heads + h) * D;
+      ldo = (long long)heads * D;
+    } else {
+      xo = dO = z * T * D;
+      ld = ldo = D;
+    }
+  }
+  // Offset of part w (0 dq, 1 dk, 2 dv) of row t in the backward's result.
+  __device__ long long grad(int t, int w) const { return heads ? xo + t * ld + (long long)w * heads * D : (z * T + t) * 3 * D + (long long)w * D; }
+};
 
 template <int T, int D> struct FwdLayout {
   static constexpr int QB = 128 * D * 4, KB = T * D * 4;
@@ -464,8 +488,8 @@ template <int T, int D> struct FwdLayout {
 // contiguous, coalesced store.
 template <int T, int D>
 __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
-                                                              const float* __restrict__ v, const float* __restrict__ mask, int causal, float inv_c,
-                                                              float fill, int* err) {
+                                                              const float* __restrict__ v, const float* __restrict__ mask, int causal, int heads,
+                                                              float inv_c, float fill, int* err) {
   using L = FwdLayout<T, D>;
   constexpr int NQB = T / 128, NH = T / 128, NW = T / 32;
   extern __shared__ uint8_t smem_raw[];
@@ -484,9 +508,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
   const int row = lq * 32 + lane;  // this thread's query row within the block
   const long long z = blockIdx.x / NQB;
   const int r0 = (int)(blockIdx.x - z * NQB) * 128, r = r0 + row;
-  q += (z * T + r0) * D;
-  k += z * T * D;
-  v += z * T * D;
+  const Rows<T, D> rows(z, heads);
+  q += rows.xo + r0 * rows.ld;
+  k += rows.xo;
+  v += rows.xo;
 
   if (tid == 0) {
     for (int b = 0; b < 3; ++b) mbar_init(&bars[b], 1);
@@ -506,7 +531,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
   const uint32_t S_t = tmem, O_t = tmem + T, LO_t = tmem + L::LO;
 
   // S = q k^T.
-  stage2(Qh, Ql, q, 128, Kh, Kl, k, T, D, D);
+  stage2(Qh, Ql, q, 128, rows.ld, Kh, Kl, k, T, rows.ld, D);
   proxy_fence();
   __syncthreads();
   if (tid == 0) {
@@ -514,11 +539,11 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
     mma3(S_t, saddr(Qh), saddr(Ql), saddr(Kh), saddr(Kl), T, D, idesc_tf32(128, T), false);
     mma_commit(bar_s);
   }
-  TBlock vb = load_t(v, D, D);  // v^T of the first half, in flight across the wait
+  TBlock vb = load_t(v, D, rows.ld);  // v^T of the first half, in flight across the wait
   bool ok = cta_wait(bar_s, 0, abort, err, 21);
   fence_after();
   store_t(V0, V0 + L::VB, vb, D);
-  if (NH > 1) vb = load_t(v + 128 * D, D, D);
+  if (NH > 1) vb = load_t(v + 128 * rows.ld, D, rows.ld);
 
   // Pass 1: the mask bits of this thread's chunks and the row maximum.
   uint32_t bits[NH];
@@ -620,9 +645,9 @@ template <int T, int D> struct BwdLayout {
 template <int T, int D>
 __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
                                                              const float* __restrict__ v, const float* __restrict__ mask, const float* __restrict__ fwd,
-                                                             const float* __restrict__ dout, int causal, float inv_c, float fill, int* err) {
+                                                             const float* __restrict__ dout, int causal, int heads, float inv_c, float fill, int* err) {
   using L = BwdLayout<T, D>;
-  constexpr int NQB = T / 128, NH = T / 128, W = 3 * D, NW = T / 32;
+  constexpr int NQB = T / 128, NH = T / 128, NW = T / 32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *Ah = sm, *Al = Ah + L::TB, *Bh = Al + L::TB, *Bl = Bh + L::TB;  // region 0
@@ -638,10 +663,12 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
   const int row = lq * 32 + lane;
   const long long z = blockIdx.x / NQB;
   const int r0 = (int)(blockIdx.x - z * NQB) * 128, r = r0 + row;
-  const float* qb = q + (z * T + r0) * D;
-  const float* db = dout + (z * T + r0) * D;
-  k += z * T * D;
-  v += z * T * D;
+  const Rows<T, D> rows(z, heads);
+  const long long ld = rows.ld, ldo = rows.ldo;
+  const float* qb = q + rows.xo + r0 * ld;
+  const float* db = dout + rows.dO + r0 * ldo;
+  k += rows.xo;
+  v += rows.xo;
 
   if (tid == 0) {
     for (int b = 0; b < 4; ++b) mbar_init(&bars[b], 1);
@@ -652,7 +679,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tslot)), "r"(512u) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  query_stats<D>(stats, fwd, dout, z * T + r0);
+  query_stats<D>(stats, fwd + (z * T + r0) * (D + 2), db, ldo);
   if (!causal) pack_mask(words, mask, T, r0, 128, 0, T);
   fence_before();
   __syncthreads();
@@ -666,7 +693,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
 #pragma unroll 1
   for (int h = 0; h < NH && ok; ++h) {
     // a: S = q k_h^T (the previous half's products are complete).
-    stage2(Ah, Al, qb, 128, Bh, Bl, k + (long long)h * 128 * D, 128, D, D);
+    stage2(Ah, Al, qb, 128, ld, Bh, Bl, k + h * 128 * ld, 128, ld, D);
     proxy_fence();
     __syncthreads();
     if (tid == 0) {
@@ -674,10 +701,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
       mma3(S_t, saddr(Ah), saddr(Al), saddr(Bh), saddr(Bl), 128, D, idesc_tf32(128, 128), false);
       mma_commit(bar_a);
     }
-    const TBlock kt = load_t(k + (long long)h * 128 * D, D, D);
+    const TBlock kt = load_t(k + h * 128 * ld, D, ld);
     if (!(ok = cta_next(bar_a, na, abort, err, 31))) break;
     // b: dP = dO v_h^T, and k_h^T in region 1.
-    stage2(Ah, Al, db, 128, Bh, Bl, v + (long long)h * 128 * D, 128, D, D);
+    stage2(Ah, Al, db, 128, ldo, Bh, Bl, v + h * 128 * ld, 128, ld, D);
     store_t(Xh, Xl, kt, D);
     proxy_fence();
     __syncthreads();
@@ -735,7 +762,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
     constexpr int V4 = D / 4;  // 16-byte vectors per row
     for (int i = tid; i < 128 * V4; i += FWD_THREADS) {
       const int rr = i / V4, c = (i - rr * V4) * 4;
-      *(float4*)(out + (z * T + r0 + rr) * W + c) = *(const float4*)(ost + rr * (D + 4) + c);
+      *(float4*)(out + rows.grad(r0 + rr, 0) + c) = *(const float4*)(ost + rr * (D + 4) + c);
     }
   }
   tc_teardown(bar_done, tmem, 512u);
@@ -750,10 +777,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
 template <int T, int D>
 __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
                                                                const float* __restrict__ v, const float* __restrict__ mask,
-                                                               const float* __restrict__ fwd, const float* __restrict__ dout, int causal, float inv_c,
-                                                               float fill, int* err) {
+                                                               const float* __restrict__ fwd, const float* __restrict__ dout, int causal, int heads,
+                                                               float inv_c, float fill, int* err) {
   using L = BwdLayout<T, D>;
-  constexpr int NKB = T / 128, NH = T / 128, W = 3 * D;
+  constexpr int NKB = T / 128, NH = T / 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *Ah = sm, *Al = Ah + L::TB, *Bh = Al + L::TB, *Bl = Bh + L::TB;  // region 0; q^T of the half at Ah / Al after dP^T
@@ -769,10 +796,12 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
   const int row = lq * 32 + lane;  // key row within the block
   const long long z = blockIdx.x / NKB;
   const int j0 = (int)(blockIdx.x - z * NKB) * 128, j = j0 + row;
-  const float* kb = k + (z * T + j0) * D;
-  const float* vb = v + (z * T + j0) * D;
-  const float* qz = q + z * T * D;
-  const float* dz = dout + z * T * D;
+  const Rows<T, D> rows(z, heads);
+  const long long ld = rows.ld, ldo = rows.ldo;
+  const float* kb = k + rows.xo + j0 * ld;
+  const float* vb = v + rows.xo + j0 * ld;
+  const float* qz = q + rows.xo;
+  const float* dz = dout + rows.dO;
 
   if (tid == 0) {
     for (int b = 0; b < 5; ++b) mbar_init(&bars[b], 1);
@@ -796,9 +825,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
   for (int h = 0; h < NH && ok; ++h) {
     const int q0 = h * 128;
     // The half's query statistics (the previous half's readers finished at its last wait).
-    query_stats<D>(stats, fwd, dout, z * T + q0);
+    query_stats<D>(stats, fwd + (z * T + q0) * (D + 2), dz + q0 * ldo, ldo);
     // a: S^T = k q_h^T.
-    stage2(Ah, Al, kb, 128, Bh, Bl, qz + (long long)q0 * D, 128, D, D);
+    stage2(Ah, Al, kb, 128, ld, Bh, Bl, qz + q0 * ld, 128, ld, D);
     proxy_fence();
     __syncthreads();
     if (tid == 0) {
@@ -806,7 +835,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
       mma3(S_t, saddr(Ah), saddr(Al), saddr(Bh), saddr(Bl), 128, D, idesc_tf32(128, 128), false);
       mma_commit(bar_a);
     }
-    const TBlock dt = load_t(dz + (long long)q0 * D, D, D);
+    const TBlock dt = load_t(dz + q0 * ldo, D, ldo);
     // The mask bits of this key over the chunk's queries q0 + 32 g ...
     uint32_t qbits = 0;
     if (causal) {
@@ -817,7 +846,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
     }
     if (!(ok = cta_next(bar_a, na, abort, err, 41))) break;
     // b: dP^T = v dO_h^T, and dO_h^T in region 1.
-    stage2(Ah, Al, vb, 128, Bh, Bl, dz + (long long)q0 * D, 128, D, D);
+    stage2(Ah, Al, vb, 128, ld, Bh, Bl, dz + q0 * ldo, 128, ldo, D);
     store_t(Xh, Xl, dt, D);
     proxy_fence();
     __syncthreads();
@@ -850,7 +879,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
       mma3_ts(V_t, S_t, LO_t, saddr(Xh), saddr(Xl), D, 128, idesc_tf32(128, D), h > 0);
       mma_commit(bar_c);
     }
-    const TBlock qt = load_t(qz + (long long)q0 * D, D, D);
+    const TBlock qt = load_t(qz + q0 * ld, D, ld);
     // dP^T done: region 0 takes q_h^T. dv done: the lo buffer is free.
     if (!(ok = cta_next(bar_b, nb, abort, err, 42))) break;
     store_t(Ah, Al, qt, D);
@@ -902,10 +931,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
   }
   __syncthreads();
   if (ok) {
-    constexpr int V4 = D / 2;  // 16-byte vectors per row (2 D floats)
-    for (int i = tid; i < 128 * V4; i += FWD_THREADS) {
-      const int rr = i / V4, c = (i - rr * V4) * 4;
-      *(float4*)(out + (z * T + j0 + rr) * W + D + c) = *(const float4*)(ost + rr * (2 * D + 4) + c);
+    constexpr int V4 = D / 4;  // 16-byte vectors per row and part
+    for (int i = tid; i < 128 * 2 * V4; i += FWD_THREADS) {
+      const int rr = i / (2 * V4), rem = i - rr * 2 * V4, w = rem / V4, c = (rem - w * V4) * 4;
+      *(float4*)(out + rows.grad(j0 + rr, 1 + w) + c) = *(const float4*)(ost + rr * (2 * D + 4) + w * D + c);
     }
   }
   tc_teardown(bar_done, tmem, 512u);
@@ -918,7 +947,8 @@ template <int T, int D> void set_smem() {
 template <int T, int D> void launch_fwd_tc(float* out, const float* q, const float* k, const float* v, const float* mask, const AttnShape& a, int* err,
                                            cudaStream_t s) {
   const long long blocks = a.batch * (T / 128);
-  k_attn_fwd_tc<T, D><<<(unsigned)blocks, FWD_THREADS, FwdLayout<T, D>::SMEM, s>>>(out, q, k, v, mask, a.causal ? 1 : 0, 1.0f / a.c, a.fill, err);
+  k_attn_fwd_tc<T, D><<<(unsigned)blocks, FWD_THREADS, FwdLayout<T, D>::SMEM, s>>>(out, q, k, v, mask, a.causal ? 1 : 0, a.heads, 1.0f / a.c, a.fill,
+                                                                                  err);
 }
 
 template <int T, int D> void set_smem_bwd() {
@@ -930,8 +960,8 @@ template <int T, int D> void launch_bwd_tc(float* out, const float* q, const flo
                                            const float* dout, const AttnShape& a, int* err, cudaStream_t s) {
   const unsigned blocks = (unsigned)(a.batch * (T / 128));
   const int causal = a.causal ? 1 : 0;
-  k_attn_dq_tc<T, D><<<blocks, FWD_THREADS, BwdLayout<T, D>::SMEM, s>>>(out, q, k, v, mask, fwd, dout, causal, 1.0f / a.c, a.fill, err);
-  k_attn_dkdv_tc<T, D><<<blocks, FWD_THREADS, BwdLayout<T, D>::SMEM, s>>>(out, q, k, v, mask, fwd, dout, causal, 1.0f / a.c, a.fill, err);
+  k_attn_dq_tc<T, D><<<blocks, FWD_THREADS, BwdLayout<T, D>::SMEM, s>>>(out, q, k, v, mask, fwd, dout, causal, a.heads, 1.0f / a.c, a.fill, err);
+  k_attn_dkdv_tc<T, D><<<blocks, FWD_THREADS, BwdLayout<T, D>::SMEM, s>>>(out, q, k, v, mask, fwd, dout, causal, a.heads, 1.0f / a.c, a.fill, err);
 }
 
 }  // namespace
@@ -962,6 +992,7 @@ void attention_fwd(float* out, const float* q, const float* k, const float* v, c
     if (a.d == 32) return launch_fwd_tc<256, 32>(out, q, k, v, mask, a, error, s);
     return launch_fwd_tc<256, 64>(out, q, k, v, mask, a, error, s);
   }
+  if (a.heads) throw std::runtime_error("attention: the packed layout runs on the tensor-core kernels only");
   const long long rows = a.batch * a.t;
   k_attn_fwd_simt<<<(unsigned)((rows + 3) / 4), 128, 4 * a.t * sizeof(float), s>>>(out, q, k, v, mask, rows, a.t, a.d, a.dv, a.c, a.fill);
 }
@@ -975,6 +1006,7 @@ void attention_bwd(float* out, const float* q, const float* k, const float* v, c
     if (a.d == 32) return launch_bwd_tc<256, 32>(out, q, k, v, mask, fwd, dout, a, error, s);
     return launch_bwd_tc<256, 64>(out, q, k, v, mask, fwd, dout, a, error, s);
   }
+  if (a.heads) throw std::runtime_error("attention: the packed layout runs on the tensor-core kernels only");
   const long long rows = a.batch * a.t;
   const unsigned blocks = (unsigned)((rows + 3) / 4);
   k_attn_dq_simt<<<blocks, 128, 4 * a.t * sizeof(float), s>>>(out, q, k, v, mask, fwd, dout, rows, a.t, a.d, a.dv, a.c, a.fill);

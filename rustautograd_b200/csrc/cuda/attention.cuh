@@ -20,6 +20,11 @@ struct AttnShape {
   // The mask is the causal pattern (mask[i][j] != 0 exactly where j <= i, a constant lower
   // triangle): the tensor-core kernels then compute its bits from the indices.
   bool causal = false;
+  // Packed layout (tensor-core shapes only): heads > 0 means q, k and v are the parts of one
+  // (B, T, 3, heads, d) tensor (q, k, v point at parts 0, 1, 2; batch entry b * heads + h; row
+  // stride 3 heads d), dO is (B, T, heads, d), and the backward writes the gradient of the
+  // (B, T, 3, heads, d) tensor instead of the packed (..., T, 3 d) rows.
+  int heads = 0;
 };
 
 // One-time setup (shared-memory limits of the tensor-core kernels); before any graph capture.

@@ -625,29 +625,46 @@ struct Builder {
     Lowered l;
     const auto& qs = i.arg_shapes[0];
     const size_t r = qs.size();
+    const bool packed = i.op.value->n() == 3;  // q, k, v as one (B, T, 3, H, d) tensor (graph.h)
     AttnShape as;
-    as.t = (int)qs[r - 2];
-    as.d = (int)qs[r - 1];
-    as.dv = (int)i.arg_shapes[2][r - 1];
-    as.batch = (long long)(rg::product(qs) / (qs[r - 2] * qs[r - 1]));
+    if (packed) {
+      as.heads = (int)i.op.value->data.get(2);
+      as.t = (int)qs[1];
+      as.d = as.dv = (int)qs[4];
+      as.batch = (long long)(qs[0] * qs[3]);
+    } else {
+      as.t = (int)qs[r - 2];
+      as.d = (int)qs[r - 1];
+      as.dv = (int)i.arg_shapes[2][r - 1];
+      as.batch = (long long)(rg::product(qs) / (qs[r - 2] * qs[r - 1]));
+    }
     as.c = (float)i.op.value->data.get(0);
     as.fill = (float)i.op.value->data.get(1);
-    if (i.dtype != DType::F32 || (!attention_tc_supported(as) && as.t > 1024))
-      throw std::runtime_error(std::string("the CUDA device has no kernel for ") + i.op.name() + " of this dtype or length");
+    if (i.dtype != DType::F32 || (!attention_tc_supported(as) && (as.t > 1024 || packed)))
+      throw std::runtime_error(std::string("the CUDA device has no kernel for ") + i.op.name() + " of this dtype, length or layout");
     attention_init();
     const auto a = i.args;
-    as.causal = causal_constant(a[3], as.t);
+    // Argument slots: q, k, v, mask, fwd, dO; packed: the one qkv slot three times (each part at
+    // its offset), then mask, fwd, dO.
+    const size_t part = packed ? (size_t)as.heads * as.d : 0;
+    const std::vector<size_t> slot = packed ? std::vector<size_t>{a[0], a[0], a[0], a[1], i.op.kind == OpKind::AttnBwd ? a[2] : 0,
+                                                                  i.op.kind == OpKind::AttnBwd ? a[3] : 0}
+                                            : std::vector<size_t>(a.begin(), a.end());
+    as.causal = causal_constant(slot[3], as.t);
     const size_t dst = i.dst;
     if (i.op.kind == OpKind::AttnFwd) {
       l.run = [=](Ctx& c) {
-        attention_fwd((float*)c.f->ptr[dst], (const float*)c.f->ptr[a[0]], (const float*)c.f->ptr[a[1]], (const float*)c.f->ptr[a[2]],
-                      (const float*)c.f->ptr[a[3]], as, c.f->prog->tc_error, c.s);
+        const float* q = (const float*)c.f->ptr[slot[0]];
+        attention_fwd((float*)c.f->ptr[dst], q, (const float*)c.f->ptr[slot[1]] + part, (const float*)c.f->ptr[slot[2]] + 2 * part,
+                      (const float*)c.f->ptr[slot[3]], as, c.f->prog->tc_error, c.s);
       };
     } else {
       l.kernels = 2;
       l.run = [=](Ctx& c) {
-        attention_bwd((float*)c.f->ptr[dst], (const float*)c.f->ptr[a[0]], (const float*)c.f->ptr[a[1]], (const float*)c.f->ptr[a[2]],
-                      (const float*)c.f->ptr[a[3]], (const float*)c.f->ptr[a[4]], (const float*)c.f->ptr[a[5]], as, c.f->prog->tc_error, c.s);
+        const float* q = (const float*)c.f->ptr[slot[0]];
+        attention_bwd((float*)c.f->ptr[dst], q, (const float*)c.f->ptr[slot[1]] + part, (const float*)c.f->ptr[slot[2]] + 2 * part,
+                      (const float*)c.f->ptr[slot[3]], (const float*)c.f->ptr[slot[4]], (const float*)c.f->ptr[slot[5]], as, c.f->prog->tc_error,
+                      c.s);
       };
     }
     return l;

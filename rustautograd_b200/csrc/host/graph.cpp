@@ -280,8 +280,10 @@ uint32_t Graph::add(Op op, const std::vector<uint32_t>& inputs) {
     case OpKind::MatMul: case OpKind::MatMulT: case OpKind::Take: case OpKind::TakeAlong:
     case OpKind::TakeGrad: case OpKind::TakeAlongGrad: arity = 2; break;
     case OpKind::Concat: arity = std::max<size_t>(inputs.size(), 1); break;
-    case OpKind::AttnFwd: arity = 4; break;
-    case OpKind::AttnBwd: arity = 6; break;
+    // With a third attribute (heads) q, k, v come as one packed tensor: (qkv, mask) and
+    // (qkv, mask, fwd, dO).
+    case OpKind::AttnFwd: arity = op.value && op.value->n() == 3 ? 2 : 4; break;
+    case OpKind::AttnBwd: arity = op.value && op.value->n() == 3 ? 4 : 6; break;
     default:
       if (op.is_control_flow()) arity = inputs.size();
       else if (op.is_binary_elementwise()) arity = 2;
@@ -506,6 +508,23 @@ std::vector<size_t> Graph::infer(const Op& op, const std::vector<std::vector<siz
     case OpKind::KeySplit: return {op.index, 2};
     case OpKind::Custom: case OpKind::AllReduce: return s[0];
     case OpKind::AttnFwd: case OpKind::AttnBwd: {
+      if (op.value && op.value->n() == 3) {
+        // Packed: qkv (B, T, 3, H, d) with H the third attribute, mask (T, T); AttnBwd also the
+        // forward's packed output (B, H, T, d + 2) and dO (B, T, H, d). AttnFwd gives
+        // (B, H, T, d + 2), AttnBwd the gradient of qkv, (B, T, 3, H, d).
+        const auto& x = s[0];
+        const size_t heads = (size_t)op.value->data.get(2);
+        bool ok = x.size() == 5 && x[2] == 3 && x[3] == heads && heads > 0 && s[1] == std::vector<size_t>{x[1], x[1]};
+        if (ok && op.kind == OpKind::AttnBwd)
+          ok = s[2] == std::vector<size_t>{x[0], heads, x[1], x[4] + 2} && s[3] == std::vector<size_t>{x[0], x[1], heads, x[4]};
+        if (!ok) {
+          Json o = Json::object();
+          o["input_shapes"] = shapes_json(s);
+          static_err("SHAPE_MISMATCH", op, o, "attention_operands_do_not_fit");
+        }
+        if (op.kind == OpKind::AttnBwd) return x;
+        return {x[0], heads, x[1], x[4] + 2};
+      }
       // q (..., T, d), k (..., T, d), v (..., T, dv) with the same leading extents, mask (T, T);
       // AttnBwd also the forward's packed output (..., T, dv + 2) and dO (..., T, dv).
       const auto &q = s[0], &k = s[1], &v = s[2], &m = s[3];

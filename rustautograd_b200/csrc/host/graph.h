@@ -41,6 +41,10 @@ enum class OpKind : uint8_t {
   // packed as (..., T, 2 d + dv). With P the softmax rebuilt from the row statistics and
   // D = rowsum(dO * O): dS = P (dO v^T - D) / c where the mask is nonzero (0 elsewhere),
   // dq = dS k, dk = dS^T q, dv = P^T dO.
+  // Packed form, value = [c, fill, H]: AttnFwd(qkv, mask) and AttnBwd(qkv, mask, fwd, dO) with
+  // qkv the (B, T, 3, H, d) projection output before the head split (batch entry b * H + h) and
+  // dO (B, T, H, d) before the head merge is undone; AttnFwd still gives (B, H, T, d + 2) and
+  // AttnBwd gives the gradient of qkv, (B, T, 3, H, d). No head-split copies are needed.
   AttnFwd,
   AttnBwd,
 };

@@ -667,6 +667,87 @@ Simplified simplify(const Graph& g, const std::vector<uint32_t>& outputs, bool f
   return r;
 }
 
+// The packed form of a matched attention (graph.h): q, k and v are the three parts of one
+// (B, T, 3, H, d) tensor, split by transpose (2, 0, 3, 1, 4) and a slice each (through reshapes);
+// dO is a (B, T, H, d) tensor under transpose (0, 2, 1, 3); and dq, dk, dv are used only to be
+// joined back: reshaped, concatenated on axis 0 and transposed by (1, 3, 0, 2, 4). The fused ops
+// then read and write the packed tensors, and the head-split and head-join copies go away. Only
+// for the shapes of the tensor-core kernels (length 128 or 256, head size 32 or 64).
+struct AttnPacked {
+  uint32_t qkv = 0, dO = 0, grad = 0;  // grad: the transpose whose value is the gradient of qkv
+  size_t heads = 0;
+};
+
+std::optional<AttnPacked> packed_attention(const Graph& g, const AttnMatch& m, const std::vector<std::vector<uint32_t>>& users,
+                                           const std::vector<bool>& live) {
+  auto strip = [&](uint32_t id) {
+    while (g.nodes[id].op.kind == OpKind::Reshape) id = g.nodes[id].inputs[0];
+    return id;
+  };
+  auto transpose_of = [&](uint32_t id, const std::vector<size_t>& perm) {
+    const Node& n = g.nodes[id];
+    return n.op.kind == OpKind::Transpose && n.op.shape == perm && n.inputs.size() == 1;
+  };
+  // The single live user of `id`, or none.
+  auto only_user = [&](uint32_t id) -> std::optional<uint32_t> {
+    std::optional<uint32_t> found;
+    for (uint32_t u : users[id])
+      if (live[u]) {
+        if (found) return std::nullopt;
+        found = u;
+      }
+    return found;
+  };
+  const auto& qs = g.shape(m.q);
+  if (qs.size() != 4 || g.shape(m.k) != qs || g.shape(m.v) != qs) return std::nullopt;
+  const size_t B = qs[0], H = qs[1], T = qs[2], d = qs[3];
+  if (!((T == 128 || T == 256) && (d == 32 || d == 64))) return std::nullopt;
+  AttnPacked p;
+  p.heads = H;
+  uint32_t split = UINT32_MAX;
+  const uint32_t parts[3] = {m.q, m.k, m.v};
+  for (size_t w = 0; w < 3; ++w) {
+    const uint32_t sl = strip(parts[w]);
+    const Node& n = g.nodes[sl];
+    if (n.op.kind != OpKind::Slice || n.inputs.size() != 1 || !transpose_of(n.inputs[0], {2, 0, 3, 1, 4})) return std::nullopt;
+    const std::vector<size_t> ts = {3, B, H, T, d};
+    if (g.shape(n.inputs[0]) != ts) return std::nullopt;
+    std::vector<size_t> starts(5, 0), stops = ts;
+    starts[0] = w;
+    stops[0] = w + 1;
+    if (n.op.starts != starts || n.op.stops != stops) return std::nullopt;
+    if (split != UINT32_MAX && split != n.inputs[0]) return std::nullopt;
+    split = n.inputs[0];
+  }
+  p.qkv = g.nodes[split].inputs[0];
+  const std::vector<size_t> packed = {B, T, 3, H, d};
+  if (g.shape(p.qkv) != packed || g.nodes[p.qkv].dtype != DType::F32) return std::nullopt;
+  const uint32_t dt = strip(m.dO);
+  if (!transpose_of(dt, {0, 2, 1, 3})) return std::nullopt;
+  p.dO = g.nodes[dt].inputs[0];
+  if (g.shape(p.dO) != std::vector<size_t>{B, T, H, d}) return std::nullopt;
+  // dq, dk, dv: each used once, through reshapes, by one concat on axis 0 in that order.
+  std::optional<uint32_t> cat;
+  const uint32_t grads[3] = {m.dq, m.dk, m.dv};
+  for (size_t w = 0; w < 3; ++w) {
+    uint32_t id = grads[w];
+    std::optional<uint32_t> u = only_user(id);
+    while (u && g.nodes[*u].op.kind == OpKind::Reshape) {
+      id = *u;
+      u = only_user(id);
+    }
+    if (!u || g.nodes[*u].op.kind != OpKind::Concat || g.nodes[*u].op.index != 0) return std::nullopt;
+    const Node& c = g.nodes[*u];
+    if (c.inputs.size() != 3 || c.inputs[w] != id || strip(c.inputs[w]) != grads[w]) return std::nullopt;
+    if (cat && *cat != *u) return std::nullopt;
+    cat = *u;
+  }
+  auto t = only_user(*cat);
+  if (!t || !transpose_of(*t, {1, 3, 0, 2, 4}) || g.shape(*t) != packed) return std::nullopt;
+  p.grad = *t;
+  return p;
+}
+
 // `gpu`: planning for the device, which recomputes forward values inside the backward groups
 // that read them (recompute_in_consumers) and keeps every other activation while the peak live
 // bytes stay within DEVICE_ACTIVATIONS_BYTES; above it rg's policy, escalating to transcendental
@@ -682,6 +763,7 @@ Simplified fuse_attention(const Simplified& in) {
     if (live[i])
       for (auto x : g.nodes[i].inputs) users[x].push_back((uint32_t)i);
   std::vector<AttnMatch> matches;
+  std::vector<std::optional<AttnPacked>> packs;
   std::vector<long> match_of(N, -1);  // O, dv, dq, dk node -> match index
   for (size_t i = 0; i < N; ++i) {
     if (!live[i] || match_of[i] >= 0) continue;
@@ -693,6 +775,7 @@ Simplified fuse_attention(const Simplified& in) {
     }
     for (uint32_t id : {m->O, m->dv, m->dq, m->dk}) match_of[id] = (long)matches.size();
     matches.push_back(*m);
+    packs.push_back(packed_attention(g, *m, users, live));
   }
   if (matches.empty()) return in;
   Simplified r;
@@ -711,11 +794,13 @@ Simplified fuse_attention(const Simplified& in) {
     sl.stops.back() = to;
     return ng.add(sl, {src});
   };
-  auto values = [&](const AttnMatch& m) {
-    Buf b(DType::F64, 2);
+  auto values = [&](const AttnMatch& m, size_t heads) {
+    const size_t n = heads ? 3 : 2;
+    Buf b(DType::F64, n);
     b.f64()[0] = m.c;
     b.f64()[1] = m.fill;
-    return std::make_shared<const Tensor>(std::vector<size_t>{2}, std::move(b));
+    if (heads) b.f64()[2] = (double)heads;
+    return std::make_shared<const Tensor>(std::vector<size_t>{n}, std::move(b));
   };
   auto mark = [&](bool bw) { backward.resize(ng.nodes.size(), bw); };
   for (size_t i = 0; i < N; ++i) {
@@ -735,8 +820,9 @@ Simplified fuse_attention(const Simplified& in) {
       else mask[mi] = ng.constant(m.mask_const);
       mark(false);
       Op f = Op::make(OpKind::AttnFwd);
-      f.value = values(m);
-      uint32_t a = ng.add(f, {map[m.q], map[m.k], map[m.v], mask[mi]});
+      const auto& pk = packs[mi];
+      f.value = values(m, pk ? pk->heads : 0);
+      uint32_t a = pk ? ng.add(f, {map[pk->qkv], mask[mi]}) : ng.add(f, {map[m.q], map[m.k], map[m.v], mask[mi]});
       const size_t dv = g.shape(m.v).back();
       map[i] = slice_last(a, 0, dv);
       stats[mi] = a;  // the backward reads O and the row statistics from the packed output
@@ -746,9 +832,18 @@ Simplified fuse_attention(const Simplified& in) {
     }
     if (mi >= 0) {
       const AttnMatch& m = matches[mi];
+      if (!grads_done[mi] && packs[mi]) {
+        // Packed: the gradient of qkv directly; dq, dk, dv and their join are not rebuilt.
+        const auto& pk = *packs[mi];
+        Op b = Op::make(OpKind::AttnBwd);
+        b.value = values(m, pk.heads);
+        map[pk.grad] = ng.add(b, {map[pk.qkv], mask[mi], stats[mi], map[pk.dO]});
+        mark(true);
+        grads_done[mi] = true;
+      }
       if (!grads_done[mi]) {
         Op b = Op::make(OpKind::AttnBwd);
-        b.value = values(m);
+        b.value = values(m, 0);
         uint32_t gid = ng.add(b, {map[m.q], map[m.k], map[m.v], mask[mi], stats[mi], map[m.dO]});
         const size_t d = g.shape(m.q).back(), dv = g.shape(m.v).back();
         uint32_t dq = slice_last(gid, 0, d), dk = slice_last(gid, d, 2 * d), dvv = slice_last(gid, 2 * d, 2 * d + dv);
@@ -760,6 +855,7 @@ Simplified fuse_attention(const Simplified& in) {
       }
       continue;
     }
+    if (map[i] != UINT32_MAX) continue;  // the gradient of a packed attention's qkv, already built
     std::vector<uint32_t> ins;
     bool ok = true;
     for (auto x : node.inputs) {

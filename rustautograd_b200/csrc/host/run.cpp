@@ -114,8 +114,10 @@ std::vector<StepCost> step_costs(const Plan& p) {
       // Products per batch entry: q k^T and P v forward; the backward recomputes q k^T and forms
       // dO v^T, P^T dO, dS k and dS^T q.
       const auto& q = i.arg_shapes[0];
-      const double t = (double)q[q.size() - 2], d = (double)q.back(), dv = (double)i.arg_shapes[2].back();
-      const double batch = (double)product(q) / (t * d);
+      const bool packed = i.op.value && i.op.value->n() == 3;  // q, k, v as one (B, T, 3, H, d) tensor
+      const double t = packed ? (double)q[1] : (double)q[q.size() - 2], d = (double)q.back();
+      const double dv = packed ? d : (double)i.arg_shapes[2].back();
+      const double batch = packed ? (double)(q[0] * q[3]) : (double)product(q) / (t * d);
       c.kind = "attention";
       c.flops = 2.0 * batch * t * t * (i.op.kind == OpKind::AttnFwd ? d + dv : 3.0 * d + 2.0 * dv);
       c.bytes = in_bytes + (double)i.n * es;

@@ -114,3 +114,30 @@ def test_default_fuses_the_shapes_measured_faster(monkeypatch):
     assert "attention" in plan((1, 1, 256, 64))
     monkeypatch.setenv("RGC_FUSED_ATTENTION", "0")
     assert "attention" not in plan((1, 2, 128, 32))
+
+
+def test_gpt_step_at_tensor_core_shapes_uses_the_packed_form():
+    """At length 128 with head size 32 the fused ops read q, k, v straight from the (B, T, 3, H, d)
+    projection output and give the gradient of that tensor: no head-split transpose, no
+    q / k / v slices, no concat or transpose of the gradients. Values against rg's plan as above."""
+    model = F.gpt.GPT(vocab=32, block=128, d=64, heads=2, layers=1)
+    params = model.init(F.random.key(0))
+    opt = F.optim.adamw(1e-3, weight_decay=0.01)
+    state = {"params": params, "opt": opt.init(params), "key": F.random.key(1)}
+    tokens = F.tensor(np.random.default_rng(0).integers(0, 32, size=2000, dtype="int32"))
+    out = both(F.gpt.make_train_step(model, opt, 2), (state, tokens))
+    steps = [p for p in json.loads(out["cuda-plan"][1]._n.plan_summary()) if "op" in p]
+    fwd = [p for p in steps if p["op"] == "attention"]
+    bwd = [p for p in steps if p["op"] == "attention_grad"]
+    assert len(fwd) == 1 and len(bwd) == 1
+    assert fwd[0]["args"][0] == [2, 128, 3, 2, 32] and bwd[0]["shape"] == [2, 128, 3, 2, 32]
+    assert not [p for p in steps if p["op"] in ("transpose", "concat") and 3 in p["shape"][:1]]
+    d = 64
+    for k_, (a, b) in enumerate(zip(out["cpu"][0], out["cuda-plan"][0])):
+        if a.dtype.kind != "f":
+            assert np.array_equal(a, b), f"output {k_}"
+        elif a.shape == (3 * d,):
+            keep = np.r_[0:d, 2 * d:3 * d]
+            assert rel(a[keep], b[keep]) <= 1e-4, f"output {k_}"
+        else:
+            assert rel(a, b) <= 1e-4, f"output {k_}"
