@@ -1045,6 +1045,32 @@ struct Builder {
   }
 };
 
+// Whether the value in `slot` is dead after plan step k: no later step reads the slot before
+// one writes it, and it is neither pinned (an input or constant) nor a plan output. Control
+// flow counts as reading every slot.
+bool dead_after(const Plan& plan, size_t k, size_t slot) {
+  if (slot < plan.pinned.size() && plan.pinned[slot]) return false;
+  for (size_t j = k + 1; j < plan.steps.size(); ++j) {
+    const rg::Step& st = plan.steps[j];
+    if (st.fused) {
+      for (const auto& in : st.group.inputs)
+        if (in.slot == slot) return false;
+      for (const auto& o : st.group.outputs)
+        if (o.second == slot) return true;
+      continue;
+    }
+    if (st.instr.op.is_control_flow()) return false;
+    for (size_t a : st.instr.args)
+      if (a == slot) return false;
+    if (st.instr.dst == slot) return true;
+    for (const auto& o : st.instr.outs)
+      if (o.second == slot) return true;
+  }
+  for (const auto& o : plan.outputs)
+    if (o.slot == slot) return false;
+  return true;
+}
+
 std::unique_ptr<Program> make_program(const Plan& plan, int device) {
   auto p = std::make_unique<Program>();
   p->device = device;
@@ -1167,37 +1193,56 @@ std::unique_ptr<Program> make_program(const Plan& plan, int device) {
       }
     }
     if (!st.fused && st.instr.op.kind == OpKind::AllReduce) {
-      // Consecutive all-reduces (a model's gradients) go to NCCL as one group.
-      std::vector<std::tuple<size_t, size_t, size_t, bool>> items;  // (src, dst, count, f64)
+      // Consecutive all-reduces (a model's gradients) go to NCCL as one group. The operations of
+      // a group may run concurrently, while the plan assigns slots assuming them in order (a
+      // later all-reduce may write the slot an earlier one read, once that value is dead). So an
+      // item whose source is dead after it reduces in place, and its destination receives a copy
+      // after the group, in plan order: in place, the items of a group touch disjoint slots. An
+      // item whose source is still read later runs alone, as before.
+      std::vector<std::tuple<size_t, size_t, size_t, bool>> group;  // (src, dst, count, f64), in place
+      auto flush = [&](std::vector<std::tuple<size_t, size_t, size_t, bool>> items, bool in_place) {
+        if (items.empty()) return;
+        Lowered l;
+        l.kernels = (int)items.size();
+        l.collective = true;
+        l.run = [items, in_place](Ctx& c) {
+          if (dist_aborted()) throw std::runtime_error("the data-parallel communicator was aborted after a stalled collective");
+          if (!dist_active()) {
+            for (auto& [src, dst, n, f64] : items)
+              ck(cudaMemcpyAsync(c.f->ptr[dst], c.f->ptr[src], n * (f64 ? 8 : 4), cudaMemcpyDeviceToDevice, c.s), "all_reduce copy");
+            return;
+          }
+          dist_group_start();
+          for (auto& [src, dst, n, f64] : items) dist_all_reduce_into(c.f->ptr[in_place ? src : dst], c.f->ptr[src], n, f64, c.s);
+          dist_group_end();
+          if (in_place)
+            for (auto& [src, dst, n, f64] : items)
+              if (dst != src) ck(cudaMemcpyAsync(c.f->ptr[dst], c.f->ptr[src], n * (f64 ? 8 : 4), cudaMemcpyDeviceToDevice, c.s), "all_reduce copy");
+        };
+        p->steps.push_back(std::move(l));
+        // The grouped step stands for several plan steps: keep step indices aligned.
+        for (size_t q = 1; q < items.size(); ++q) {
+          Lowered empty;
+          empty.kernels = 0;
+          empty.run = [](Ctx&) {};
+          p->steps.push_back(std::move(empty));
+        }
+      };
       while (k < plan.steps.size() && !plan.steps[k].fused && plan.steps[k].instr.op.kind == OpKind::AllReduce) {
         const Instr& i = plan.steps[k].instr;
-        items.emplace_back(i.args[0], i.dst, i.n, i.dtype == DType::F64);
+        auto item = std::make_tuple(i.args[0], i.dst, i.n, i.dtype == DType::F64);
         note_writes(k);
+        if (dead_after(plan, k, i.args[0])) {
+          group.push_back(item);
+        } else {
+          flush(std::move(group), true);
+          group.clear();
+          flush({item}, false);
+        }
         ++k;
       }
+      flush(std::move(group), true);
       --k;
-      Lowered l;
-      l.kernels = (int)items.size();
-      l.collective = true;
-      l.run = [items](Ctx& c) {
-        if (dist_aborted()) throw std::runtime_error("the data-parallel communicator was aborted after a stalled collective");
-        if (!dist_active()) {
-          for (auto& [src, dst, n, f64] : items)
-            ck(cudaMemcpyAsync(c.f->ptr[dst], c.f->ptr[src], n * (f64 ? 8 : 4), cudaMemcpyDeviceToDevice, c.s), "all_reduce copy");
-          return;
-        }
-        dist_group_start();
-        for (auto& [src, dst, n, f64] : items) dist_all_reduce_into(c.f->ptr[dst], c.f->ptr[src], n, f64, c.s);
-        dist_group_end();
-      };
-      p->steps.push_back(std::move(l));
-      // The grouped step stands for several plan steps: keep step indices aligned.
-      for (size_t q = 1; q < items.size(); ++q) {
-        Lowered empty;
-        empty.kernels = 0;
-        empty.run = [](Ctx&) {};
-        p->steps.push_back(std::move(empty));
-      }
       continue;
     }
     p->steps.push_back(lower_one(k));

@@ -206,6 +206,23 @@ void emit_hoisted(const Graph& g, const std::vector<bool>& up, const Fuse& cfg, 
   close();
 }
 
+// Device plans with data parallelism (no counterpart in rg): the all-reduces and every node that
+// depends on one (the optimizer update, the reported loss) come after all other nodes, so the
+// all-reduces are consecutive plan steps that run as one NCCL group after the backward pass,
+// instead of one group per gradient between pieces of it (each group a synchronisation point).
+std::vector<bool> after_collectives(const Graph& g, const std::vector<bool>& keep, const Fuse& cfg) {
+  std::vector<bool> late(g.nodes.size(), false);
+  if (!cfg.gpu) return late;
+  for (size_t i = 0; i < g.nodes.size(); ++i) {
+    if (!keep[i]) continue;
+    const Node& n = g.nodes[i];
+    bool dep = n.op.kind == OpKind::AllReduce;
+    for (auto x : n.inputs) dep = dep || late[x];
+    late[i] = dep;
+  }
+  return late;
+}
+
 // plan.rs:297-350
 std::vector<Item> schedule(const Graph& g, const std::vector<bool>& keep, const Fuse& cfg) {
   if (cfg.gpu && cfg.levels) return schedule_levels(g, keep, cfg);
@@ -226,22 +243,28 @@ std::vector<Item> schedule(const Graph& g, const std::vector<bool>& keep, const 
   };
   std::vector<bool> up = hoisted_for(g, keep, cfg);
   emit_hoisted(g, up, cfg, items);
-  for (size_t i = 0; i < g.nodes.size(); ++i) {
-    const Node& n = g.nodes[i];
-    if (!keep[i] || up[i] || is_leaf(n)) continue;
-    if (fusable(g, i, cfg.gpu) && !(cfg.hoist && n.dtype == DType::F64)) {
-      bool same = open.empty() || (g.nodes[open[0]].shape == n.shape && g.nodes[open[0]].dtype == n.dtype);
-      size_t inputs = external_inputs(g, open, n);
-      if (!same || (cfg.gpu && inputs + open.size() + 1 > cfg.max_bindings)) close();
-      open.push_back(i);
-    } else {
-      bool reads_open = false;
-      for (auto x : n.inputs) reads_open = reads_open || contains(open, x);
-      if (reads_open) close();
-      items.push_back(Item{false, i, {}});
+  const std::vector<bool> late = after_collectives(g, keep, cfg);
+  // Passes: the nodes before any all-reduce, the all-reduces, what depends on them.
+  for (int pass = 0; pass < 3; ++pass) {
+    for (size_t i = 0; i < g.nodes.size(); ++i) {
+      const Node& n = g.nodes[i];
+      if (!keep[i] || up[i] || is_leaf(n)) continue;
+      const int want = !late[i] ? 0 : n.op.kind == OpKind::AllReduce ? 1 : 2;
+      if (want != pass) continue;
+      if (fusable(g, i, cfg.gpu) && !(cfg.hoist && n.dtype == DType::F64)) {
+        bool same = open.empty() || (g.nodes[open[0]].shape == n.shape && g.nodes[open[0]].dtype == n.dtype);
+        size_t inputs = external_inputs(g, open, n);
+        if (!same || (cfg.gpu && inputs + open.size() + 1 > cfg.max_bindings)) close();
+        open.push_back(i);
+      } else {
+        bool reads_open = false;
+        for (auto x : n.inputs) reads_open = reads_open || contains(open, x);
+        if (reads_open) close();
+        items.push_back(Item{false, i, {}});
+      }
     }
+    close();
   }
-  close();
   return items;
 }
 
@@ -253,9 +276,18 @@ std::vector<Item> schedule_levels(const Graph& g, const std::vector<bool>& keep,
   auto gpu_fusable = [&](size_t i) { return fusable(g, i, true) && !(cfg.hoist && g.nodes[i].dtype == DType::F64); };
   std::vector<size_t> level(g.nodes.size(), 0);
   std::vector<std::vector<size_t>> by_level;
+  // The all-reduces and what depends on them go above every other node, the all-reduces on one
+  // level (after_collectives).
+  const std::vector<bool> late = after_collectives(g, keep, cfg);
+  size_t top = 0;
+  for (int pass = 0; pass < 2; ++pass)
   for (size_t i = 0; i < g.nodes.size(); ++i) {
     const Node& n = g.nodes[i];
-    if (!keep[i] || up[i] || is_leaf(n)) continue;
+    if (!keep[i] || up[i] || is_leaf(n) || late[i] != (pass == 1)) continue;
+    if (n.op.kind == OpKind::AllReduce) {
+      level[i] = top + 1;
+      continue;
+    }
     size_t deepest = 0;
     for (auto x : n.inputs) deepest = std::max(deepest, level[x]);
     bool joins = gpu_fusable(i) && deepest > 0;
@@ -268,6 +300,7 @@ std::vector<Item> schedule_levels(const Graph& g, const std::vector<bool>& keep,
       }
     }
     level[i] = (is_alias(g, i) || joins) ? deepest : deepest + 1;
+    if (pass == 0) top = std::max(top, level[i]);
   }
   if (cfg.sink) {
     // Consumers first (reverse graph order), so that a chain of such nodes follows its last link.
