@@ -1107,6 +1107,31 @@ size_t esize(EType t) { return t == EType::F64 ? 8 : 4; }
 
 void fill_zero(void* dst, size_t bytes, cudaStream_t s) { cudaMemsetAsync(dst, 0, bytes, s); }
 
+// One segment per blockIdx.y; 16-byte vectors when both ends are 16-byte aligned.
+__global__ void k_copy_segments(const Segments segs) {
+  pdl_wait();
+  const int g = blockIdx.y;
+  const long long n = segs.count[g];
+  const float* src = segs.src[g];
+  float* dst = segs.dst[g];
+  const long long stride = (long long)gridDim.x * blockDim.x, t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  long long done = 0;
+  if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+    const long long n4 = n >> 2;
+    for (long long i = t; i < n4; i += stride) reinterpret_cast<float4*>(dst)[i] = reinterpret_cast<const float4*>(src)[i];
+    done = n4 << 2;
+  }
+  for (long long i = done + t; i < n; i += stride) dst[i] = src[i];
+}
+
+cudaError_t copy_segments(const Segments& segs, cudaStream_t s) {
+  if (segs.n <= 0) return cudaSuccess;
+  long long longest = 0;
+  for (int i = 0; i < segs.n; ++i) longest = std::max(longest, segs.count[i]);
+  const long long blocks = std::min<long long>((longest / 4 + 255) / 256, 256);
+  return launch(k_copy_segments, dim3((unsigned)std::max<long long>(blocks, 1), (unsigned)segs.n), dim3(256), 0, s, segs);
+}
+
 #define DISPATCH(t, F, ...)                 \
   switch (t) {                              \
     case EType::F32: F<float>(__VA_ARGS__); break;  \

@@ -128,4 +128,15 @@ void write_count(int32_t* dst, const long long* count, cudaStream_t s);
 // Any index outside [0, dim) -> *flag = 1.
 void index_outside(const int32_t* idx, long long n, long long dim, int* flag, cudaStream_t s);
 
+// Up to SEGMENTS_MAX float segments copied in one launch (the gradients of a data-parallel
+// step gathered into one contiguous buffer for a single all-reduce, and scattered back).
+constexpr int SEGMENTS_MAX = 64;
+struct Segments {
+  int n = 0;
+  const float* src[SEGMENTS_MAX];
+  float* dst[SEGMENTS_MAX];
+  long long count[SEGMENTS_MAX];
+};
+cudaError_t copy_segments(const Segments& segs, cudaStream_t s);
+
 }  // namespace rgc

@@ -1045,32 +1045,6 @@ struct Builder {
   }
 };
 
-// Whether the value in `slot` is dead after plan step k: no later step reads the slot before
-// one writes it, and it is neither pinned (an input or constant) nor a plan output. Control
-// flow counts as reading every slot.
-bool dead_after(const Plan& plan, size_t k, size_t slot) {
-  if (slot < plan.pinned.size() && plan.pinned[slot]) return false;
-  for (size_t j = k + 1; j < plan.steps.size(); ++j) {
-    const rg::Step& st = plan.steps[j];
-    if (st.fused) {
-      for (const auto& in : st.group.inputs)
-        if (in.slot == slot) return false;
-      for (const auto& o : st.group.outputs)
-        if (o.second == slot) return true;
-      continue;
-    }
-    if (st.instr.op.is_control_flow()) return false;
-    for (size_t a : st.instr.args)
-      if (a == slot) return false;
-    if (st.instr.dst == slot) return true;
-    for (const auto& o : st.instr.outs)
-      if (o.second == slot) return true;
-  }
-  for (const auto& o : plan.outputs)
-    if (o.slot == slot) return false;
-  return true;
-}
-
 std::unique_ptr<Program> make_program(const Plan& plan, int device) {
   auto p = std::make_unique<Program>();
   p->device = device;
@@ -1193,31 +1167,63 @@ std::unique_ptr<Program> make_program(const Plan& plan, int device) {
       }
     }
     if (!st.fused && st.instr.op.kind == OpKind::AllReduce) {
-      // Consecutive all-reduces (a model's gradients) go to NCCL as one group. The operations of
-      // a group may run concurrently, while the plan assigns slots assuming them in order (a
-      // later all-reduce may write the slot an earlier one read, once that value is dead). So an
-      // item whose source is dead after it reduces in place, and its destination receives a copy
-      // after the group, in plan order: in place, the items of a group touch disjoint slots. An
-      // item whose source is still read later runs alone, as before.
-      std::vector<std::tuple<size_t, size_t, size_t, bool>> group;  // (src, dst, count, f64), in place
-      auto flush = [&](std::vector<std::tuple<size_t, size_t, size_t, bool>> items, bool in_place) {
+      // Consecutive all-reduces (a model's gradients): the f32 ones are gathered into one
+      // contiguous buffer (the frame's scratch, 256-byte aligned segments), all-reduced as one
+      // NCCL operation and scattered to their destinations; one operation of 150 MB runs at
+      // link bandwidth, while a group of 150 small ones pays a latency per operation. Sources
+      // are all read before any destination is written, so slots the plan reuses between the
+      // steps (a later destination in an earlier source's slot) are safe; a run is cut before
+      // a destination that meets an earlier destination of the run. f64 items reduce alone.
+      struct Item {
+        size_t src, dst, n;
+        bool f64;
+      };
+      std::vector<Item> all;
+      while (k < plan.steps.size() && !plan.steps[k].fused && plan.steps[k].instr.op.kind == OpKind::AllReduce) {
+        const Instr& i = plan.steps[k].instr;
+        all.push_back(Item{i.args[0], i.dst, i.n, i.dtype == DType::F64});
+        note_writes(k);
+        ++k;
+      }
+      --k;
+      auto emit = [&](std::vector<Item> items, bool staged) {
         if (items.empty()) return;
+        std::vector<size_t> offsets;  // staged: each item's place in the contiguous buffer (floats)
+        size_t total = 0;
+        for (auto& it : items) {
+          offsets.push_back(total);
+          total += (it.n + 63) / 64 * 64;
+        }
+        if (staged) b.scratch = std::max(b.scratch, total * sizeof(float));
         Lowered l;
         l.kernels = (int)items.size();
         l.collective = true;
-        l.run = [items, in_place](Ctx& c) {
+        l.run = [items, offsets, total, staged](Ctx& c) {
           if (dist_aborted()) throw std::runtime_error("the data-parallel communicator was aborted after a stalled collective");
           if (!dist_active()) {
-            for (auto& [src, dst, n, f64] : items)
-              ck(cudaMemcpyAsync(c.f->ptr[dst], c.f->ptr[src], n * (f64 ? 8 : 4), cudaMemcpyDeviceToDevice, c.s), "all_reduce copy");
+            for (auto& it : items)
+              ck(cudaMemcpyAsync(c.f->ptr[it.dst], c.f->ptr[it.src], it.n * (it.f64 ? 8 : 4), cudaMemcpyDeviceToDevice, c.s), "all_reduce copy");
             return;
           }
-          dist_group_start();
-          for (auto& [src, dst, n, f64] : items) dist_all_reduce_into(c.f->ptr[in_place ? src : dst], c.f->ptr[src], n, f64, c.s);
-          dist_group_end();
-          if (in_place)
-            for (auto& [src, dst, n, f64] : items)
-              if (dst != src) ck(cudaMemcpyAsync(c.f->ptr[dst], c.f->ptr[src], n * (f64 ? 8 : 4), cudaMemcpyDeviceToDevice, c.s), "all_reduce copy");
+          if (!staged) {
+            for (auto& it : items) dist_all_reduce_into(c.f->ptr[it.dst], c.f->ptr[it.src], it.n, it.f64, c.s);
+            return;
+          }
+          float* stage = (float*)c.f->scratch;
+          for (int pass = 0; pass < 2; ++pass) {  // gather, then (after the all-reduce) scatter
+            if (pass == 1) dist_all_reduce(stage, total, false, c.s);
+            for (size_t q = 0; q < items.size(); q += SEGMENTS_MAX) {
+              Segments g;
+              g.n = (int)std::min<size_t>(SEGMENTS_MAX, items.size() - q);
+              for (int j = 0; j < g.n; ++j) {
+                float* dev = (float*)c.f->ptr[pass ? items[q + j].dst : items[q + j].src];
+                g.src[j] = pass ? stage + offsets[q + j] : dev;
+                g.dst[j] = pass ? dev : stage + offsets[q + j];
+                g.count[j] = (long long)items[q + j].n;
+              }
+              ck(copy_segments(g, c.s), pass ? "all_reduce scatter" : "all_reduce gather");
+            }
+          }
         };
         p->steps.push_back(std::move(l));
         // The grouped step stands for several plan steps: keep step indices aligned.
@@ -1228,21 +1234,25 @@ std::unique_ptr<Program> make_program(const Plan& plan, int device) {
           p->steps.push_back(std::move(empty));
         }
       };
-      while (k < plan.steps.size() && !plan.steps[k].fused && plan.steps[k].instr.op.kind == OpKind::AllReduce) {
-        const Instr& i = plan.steps[k].instr;
-        auto item = std::make_tuple(i.args[0], i.dst, i.n, i.dtype == DType::F64);
-        note_writes(k);
-        if (dead_after(plan, k, i.args[0])) {
-          group.push_back(item);
-        } else {
-          flush(std::move(group), true);
-          group.clear();
-          flush({item}, false);
+      std::vector<Item> run;
+      std::vector<size_t> dsts;
+      for (auto& it : all) {
+        if (it.f64) {
+          emit(std::move(run), true);
+          run.clear();
+          dsts.clear();
+          emit({it}, false);
+          continue;
         }
-        ++k;
+        if (std::find(dsts.begin(), dsts.end(), it.dst) != dsts.end()) {
+          emit(std::move(run), true);
+          run.clear();
+          dsts.clear();
+        }
+        run.push_back(it);
+        dsts.push_back(it.dst);
       }
-      flush(std::move(group), true);
-      --k;
+      emit(std::move(run), true);
       continue;
     }
     p->steps.push_back(lower_one(k));
