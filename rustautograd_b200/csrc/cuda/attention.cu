@@ -229,15 +229,19 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
 }
 
 // D (128 x N) (+)= A (128 x K) B (N x K)^T in 3xTF32, A and B K-major hi/lo tiles (shared-memory
-// addresses; B's tile has N rows). Issued by one thread.
-__device__ __forceinline__ void mma3(uint32_t d, uint32_t ah, uint32_t al, uint32_t bh, uint32_t bl, int N, int K, uint32_t idesc, bool accumulate) {
+// addresses; B's tile has N rows). Issued by one thread, fully unrolled: the descriptors are
+// formed once and stepped by constant offsets (the address field is address / 16).
+template <int N, int K>
+__device__ __forceinline__ void mma3(uint32_t d, uint32_t ah, uint32_t al, uint32_t bh, uint32_t bl, uint32_t idesc, bool accumulate) {
+  const uint64_t dah = desc_k(ah), dal = desc_k(al), dbh = desc_k(bh), dbl = desc_k(bl);
+#pragma unroll
   for (int kb = 0; kb < K / 32; ++kb) {
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
-      const uint32_t ao = (uint32_t)(kb * 128 * 128 + kk * 32), bo = (uint32_t)(kb * N * 128 + kk * 32);
-      mma_tf32(d, desc_k(ah + ao), desc_k(bh + bo), idesc, (accumulate || kb || kk) ? 1u : 0u);
-      mma_tf32(d, desc_k(ah + ao), desc_k(bl + bo), idesc, 1u);
-      mma_tf32(d, desc_k(al + ao), desc_k(bh + bo), idesc, 1u);
+      const uint64_t ao = (uint64_t)((kb * 128 * 128 + kk * 32) >> 4), bo = (uint64_t)((kb * N * 128 + kk * 32) >> 4);
+      mma_tf32(d, dah + ao, dbh + bo, idesc, (accumulate || kb || kk) ? 1u : 0u);
+      mma_tf32(d, dah + ao, dbl + bo, idesc, 1u);
+      mma_tf32(d, dal + ao, dbh + bo, idesc, 1u);
     }
   }
 }
@@ -305,14 +309,19 @@ __device__ __forceinline__ void mma_tf32_ts(uint32_t d, uint32_t a, uint64_t b, 
 
 // D (128 x N) (+)= A (128 x K) B (N x K)^T in 3xTF32 with A in TMEM: hi in columns ah .. ah + K - 1,
 // lo in al .. al + K - 1 (row = lane); B a K-major hi / lo tile pair in shared memory (N rows).
-__device__ __forceinline__ void mma3_ts(uint32_t d, uint32_t ah, uint32_t al, uint32_t bh, uint32_t bl, int N, int K, uint32_t idesc, bool accumulate) {
+// Fully unrolled, descriptors stepped by constant offsets as in mma3.
+template <int N, int K>
+__device__ __forceinline__ void mma3_ts(uint32_t d, uint32_t ah, uint32_t al, uint32_t bh, uint32_t bl, uint32_t idesc, bool accumulate) {
+  const uint64_t dbh = desc_k(bh), dbl = desc_k(bl);
+#pragma unroll
   for (int kb = 0; kb < K / 32; ++kb) {
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
-      const uint32_t ao = (uint32_t)(kb * 32 + kk * 8), bo = (uint32_t)(kb * N * 128 + kk * 32);
-      mma_tf32_ts(d, ah + ao, desc_k(bh + bo), idesc, (accumulate || kb || kk) ? 1u : 0u);
-      mma_tf32_ts(d, ah + ao, desc_k(bl + bo), idesc, 1u);
-      mma_tf32_ts(d, al + ao, desc_k(bh + bo), idesc, 1u);
+      const uint32_t ao = (uint32_t)(kb * 32 + kk * 8);
+      const uint64_t bo = (uint64_t)((kb * N * 128 + kk * 32) >> 4);
+      mma_tf32_ts(d, ah + ao, dbh + bo, idesc, (accumulate || kb || kk) ? 1u : 0u);
+      mma_tf32_ts(d, ah + ao, dbl + bo, idesc, 1u);
+      mma_tf32_ts(d, al + ao, dbh + bo, idesc, 1u);
     }
   }
 }
@@ -536,7 +545,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
   __syncthreads();
   if (tid == 0) {
     fence_after();
-    mma3(S_t, saddr(Qh), saddr(Ql), saddr(Kh), saddr(Kl), T, D, idesc_tf32(128, T), false);
+    mma3<T, D>(S_t, saddr(Qh), saddr(Ql), saddr(Kh), saddr(Kl), idesc_tf32(128, T), false);
     mma_commit(bar_s);
   }
   TBlock vb = load_t(v, D, rows.ld);  // v^T of the first half, in flight across the wait
@@ -591,7 +600,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
     if (tid == 0) {
       fence_after();
       uint8_t* vh = V0 + 2 * h * L::VB;
-      mma3_ts(O_t, S_t + h * 128, LO_t, saddr(vh), saddr(vh + L::VB), D, 128, idesc_tf32(128, D), h > 0);
+      mma3_ts<D, 128>(O_t, S_t + h * 128, LO_t, saddr(vh), saddr(vh + L::VB), idesc_tf32(128, D), h > 0);
       mma_commit(bar_o);
     }
   }
@@ -698,7 +707,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
     __syncthreads();
     if (tid == 0) {
       fence_after();
-      mma3(S_t, saddr(Ah), saddr(Al), saddr(Bh), saddr(Bl), 128, D, idesc_tf32(128, 128), false);
+      mma3<128, D>(S_t, saddr(Ah), saddr(Al), saddr(Bh), saddr(Bl), idesc_tf32(128, 128), false);
       mma_commit(bar_a);
     }
     const TBlock kt = load_t(k + h * 128 * ld, D, ld);
@@ -710,7 +719,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
     __syncthreads();
     if (tid == 0) {
       fence_after();
-      mma3(P_t, saddr(Ah), saddr(Al), saddr(Bh), saddr(Bl), 128, D, idesc_tf32(128, 128), false);
+      mma3<128, D>(P_t, saddr(Ah), saddr(Al), saddr(Bh), saddr(Bl), idesc_tf32(128, 128), false);
       mma_commit(bar_b);
     }
     if (!(ok = cta_next(bar_b, nb, abort, err, 32))) break;
@@ -741,7 +750,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
     __syncthreads();
     if (tid == 0) {
       fence_after();
-      mma3_ts(Q_t, S_t, LO_t, saddr(Xh), saddr(Xl), D, 128, idesc_tf32(128, D), h > 0);
+      mma3_ts<D, 128>(Q_t, S_t, LO_t, saddr(Xh), saddr(Xl), idesc_tf32(128, D), h > 0);
       mma_commit(bar_c);
     }
     if (!(ok = cta_next(bar_c, nc, abort, err, 33))) break;
@@ -832,7 +841,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
     __syncthreads();
     if (tid == 0) {
       fence_after();
-      mma3(S_t, saddr(Ah), saddr(Al), saddr(Bh), saddr(Bl), 128, D, idesc_tf32(128, 128), false);
+      mma3<128, D>(S_t, saddr(Ah), saddr(Al), saddr(Bh), saddr(Bl), idesc_tf32(128, 128), false);
       mma_commit(bar_a);
     }
     const TBlock dt = load_t(dz + q0 * ldo, D, ldo);
@@ -852,7 +861,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
     __syncthreads();
     if (tid == 0) {
       fence_after();
-      mma3(P_t, saddr(Ah), saddr(Al), saddr(Bh), saddr(Bl), 128, D, idesc_tf32(128, 128), false);
+      mma3<128, D>(P_t, saddr(Ah), saddr(Al), saddr(Bh), saddr(Bl), idesc_tf32(128, 128), false);
       mma_commit(bar_b);
     }
     fence_after();
@@ -876,7 +885,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
     __syncthreads();
     if (tid == 0) {
       fence_after();
-      mma3_ts(V_t, S_t, LO_t, saddr(Xh), saddr(Xl), D, 128, idesc_tf32(128, D), h > 0);
+      mma3_ts<D, 128>(V_t, S_t, LO_t, saddr(Xh), saddr(Xl), idesc_tf32(128, D), h > 0);
       mma_commit(bar_c);
     }
     const TBlock qt = load_t(qz + q0 * ld, D, ld);
@@ -908,7 +917,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
     __syncthreads();
     if (tid == 0) {
       fence_after();
-      mma3_ts(K_t, P_t, LO_t, saddr(Ah), saddr(Al), D, 128, idesc_tf32(128, D), h > 0);
+      mma3_ts<D, 128>(K_t, P_t, LO_t, saddr(Ah), saddr(Al), idesc_tf32(128, D), h > 0);
       mma_commit(bar_d);
     }
     if (!(ok = cta_next(bar_d, nd, abort, err, 44))) break;
