@@ -391,8 +391,12 @@ def roofline(w, compiled, secs, pk):
             "row_chains": None if chains is None else {"achieved_gbs": chains[2] / chains[0] / 1e9, "frac_of_hbm": chains[2] / chains[0] / 1e9 / pk["hbm_gbs"],
                                                        "share_of_step": chains[0] / total, "launches_per_step": chains[3]},
             "gemm": None if gemm is None else {"achieved_tflops": gemm[1] / gemm[0] / 1e12, "frac_of_bf16_sustained": gemm[1] / gemm[0] / 1e12 / pk["bf16_tflops_sustained"],
+                                               # fp32-accurate products run as three TF32 products at half the bf16 rate:
+                                               # their ceiling is 1/6 of the bf16 peak.
+                                               "frac_of_3xtf32_ceiling": gemm[1] / gemm[0] / 1e12 / (pk["bf16_tflops_sustained"] / 6),
                                                "share_of_step": gemm[0] / total, "launches_per_step": gemm[3]},
             "attention": None if attn is None else {"achieved_tflops": attn[1] / attn[0] / 1e12, "share_of_step": attn[0] / total,
+                                                    "frac_of_3xtf32_ceiling": attn[1] / attn[0] / 1e12 / (pk["bf16_tflops_sustained"] / 6),
                                                     "ops_per_step": attn[3]}}
 
 
