@@ -277,6 +277,42 @@ __device__ __forceinline__ void stage2(uint8_t* ah, uint8_t* al, const float* __
   }
 }
 
+// stage2 split in two, with all of a thread's vectors (U of them; U blockDim.x >= the block's
+// vector count) loaded at once, so that the loads can be issued before other work and the
+// stores made later.
+template <int U> struct Staged {
+  float4 x[U];
+};
+template <int U>
+__device__ __forceinline__ void load2(Staged<U>& st, const float* __restrict__ a, int RA, long long lda, const float* __restrict__ b, int RB,
+                                      long long ldb, int K) {
+  const int k4 = K >> 2, na = RA * k4, n = na + RB * k4;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int i = threadIdx.x + u * blockDim.x;
+    if (i < n) {
+      const bool in_a = i < na;
+      const int e = in_a ? i : i - na, row = e / k4, col = (e - row * k4) << 2;
+      st.x[u] = *(const float4*)(in_a ? a + row * lda + col : b + row * ldb + col);
+    }
+  }
+}
+template <int U>
+__device__ __forceinline__ void store2(const Staged<U>& st, uint8_t* ah, uint8_t* al, int RA, uint8_t* bh, uint8_t* bl, int RB, int K) {
+  const int k4 = K >> 2, na = RA * k4, n = na + RB * k4;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int i = threadIdx.x + u * blockDim.x;
+    if (i < n) {
+      const bool in_a = i < na;
+      const int e = in_a ? i : i - na, row = e / k4, col = (e - row * k4) << 2;
+      const uint32_t off = kmaj(in_a ? RA : RB, row, col);
+      *(float4*)((in_a ? ah : bh) + off) = st.x[u];
+      *(float4*)((in_a ? al : bl) + off) = lo4(st.x[u]);
+    }
+  }
+}
+
 // TMEM stores of 16 or 32 consecutive columns of the warp's 32 lanes; tmem_st_wait makes them
 // complete before the fence and barrier that hand them to a product.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
@@ -521,6 +557,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
   q += rows.xo + r0 * rows.ld;
   k += rows.xo;
   v += rows.xo;
+  // q and k in flight across the set-up (all of a thread's vectors at once).
+  constexpr int UQK = ((128 + T) * D / 4 + FWD_THREADS - 1) / FWD_THREADS;
+  Staged<UQK> qk;
+  load2(qk, q, 128, rows.ld, k, T, rows.ld, D);
 
   if (tid == 0) {
     for (int b = 0; b < 3; ++b) mbar_init(&bars[b], 1);
@@ -540,7 +580,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_fwd_tc(float* __restric
   const uint32_t S_t = tmem, O_t = tmem + T, LO_t = tmem + L::LO;
 
   // S = q k^T.
-  stage2(Qh, Ql, q, 128, rows.ld, Kh, Kl, k, T, rows.ld, D);
+  store2(qk, Qh, Ql, 128, Kh, Kl, T, D);
   proxy_fence();
   __syncthreads();
   if (tid == 0) {
