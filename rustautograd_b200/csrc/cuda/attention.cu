@@ -694,7 +694,8 @@ template <int T, int D> struct BwdLayout {
 template <int T, int D>
 __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
                                                              const float* __restrict__ v, const float* __restrict__ mask, const float* __restrict__ fwd,
-                                                             const float* __restrict__ dout, int causal, int heads, float inv_c, float fill, int* err) {
+                                                             const float* __restrict__ dout, float* __restrict__ qstats, int causal, int heads,
+                                                             float inv_c, float fill, int* err) {
   using L = BwdLayout<T, D>;
   constexpr int NQB = T / 128, NH = T / 128, NW = T / 32;
   extern __shared__ uint8_t smem_raw[];
@@ -736,6 +737,13 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
   const uint32_t tmem = *tslot, lanes = (uint32_t)(lq * 32) << 16;
   const uint32_t S_t = tmem, P_t = tmem + 128, Q_t = tmem + 256, LO_t = tmem + 256 + D;
   const float m = stats[row], inv_sum = stats[128 + row], Dr = stats[256 + row];
+  // The block's query statistics for the dk / dv kernel: m, 1 / s and D, each a (Z, T) array.
+  if (tid < 128) {
+    const long long zt = (long long)(gridDim.x / NQB) * T, at = z * T + r0 + tid;
+    qstats[at] = stats[tid];
+    qstats[zt + at] = stats[128 + tid];
+    qstats[2 * zt + at] = stats[256 + tid];
+  }
 
   bool ok = true;
   int na = 0, nb = 0, nc = 0;
@@ -826,8 +834,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
 template <int T, int D>
 __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
                                                                const float* __restrict__ v, const float* __restrict__ mask,
-                                                               const float* __restrict__ fwd, const float* __restrict__ dout, int causal, int heads,
-                                                               float inv_c, float fill, int* err) {
+                                                               const float* __restrict__ fwd, const float* __restrict__ dout,
+                                                               const float* __restrict__ qstats, int causal, int heads, float inv_c, float fill, int* err) {
   using L = BwdLayout<T, D>;
   constexpr int NKB = T / 128, NH = T / 128;
   extern __shared__ uint8_t smem_raw[];
@@ -873,8 +881,14 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restri
 #pragma unroll 1
   for (int h = 0; h < NH && ok; ++h) {
     const int q0 = h * 128;
-    // The half's query statistics (the previous half's readers finished at its last wait).
-    query_stats<D>(stats, fwd + (z * T + q0) * (D + 2), dz + q0 * ldo, ldo);
+    // The half's query statistics, from the dq kernel (the previous half's readers finished at
+    // its last wait).
+    if (tid < 128) {
+      const long long zt = (long long)(gridDim.x / NKB) * T, at = z * T + q0 + tid;
+      stats[tid] = qstats[at];
+      stats[128 + tid] = qstats[zt + at];
+      stats[256 + tid] = qstats[2 * zt + at];
+    }
     // a: S^T = k q_h^T.
     stage2(Ah, Al, kb, 128, ld, Bh, Bl, qz + q0 * ld, 128, ld, D);
     proxy_fence();
@@ -1006,11 +1020,13 @@ template <int T, int D> void set_smem_bwd() {
 }
 
 template <int T, int D> void launch_bwd_tc(float* out, const float* q, const float* k, const float* v, const float* mask, const float* fwd,
-                                           const float* dout, const AttnShape& a, int* err, cudaStream_t s) {
+                                           const float* dout, const AttnShape& a, float* qstats, int* err, cudaStream_t s) {
   const unsigned blocks = (unsigned)(a.batch * (T / 128));
   const int causal = a.causal ? 1 : 0;
-  k_attn_dq_tc<T, D><<<blocks, FWD_THREADS, BwdLayout<T, D>::SMEM, s>>>(out, q, k, v, mask, fwd, dout, causal, a.heads, 1.0f / a.c, a.fill, err);
-  k_attn_dkdv_tc<T, D><<<blocks, FWD_THREADS, BwdLayout<T, D>::SMEM, s>>>(out, q, k, v, mask, fwd, dout, causal, a.heads, 1.0f / a.c, a.fill, err);
+  k_attn_dq_tc<T, D><<<blocks, FWD_THREADS, BwdLayout<T, D>::SMEM, s>>>(out, q, k, v, mask, fwd, dout, qstats, causal, a.heads, 1.0f / a.c, a.fill,
+                                                                        err);
+  k_attn_dkdv_tc<T, D><<<blocks, FWD_THREADS, BwdLayout<T, D>::SMEM, s>>>(out, q, k, v, mask, fwd, dout, qstats, causal, a.heads, 1.0f / a.c,
+                                                                          a.fill, err);
 }
 
 }  // namespace
@@ -1046,14 +1062,17 @@ void attention_fwd(float* out, const float* q, const float* k, const float* v, c
   k_attn_fwd_simt<<<(unsigned)((rows + 3) / 4), 128, 4 * a.t * sizeof(float), s>>>(out, q, k, v, mask, rows, a.t, a.d, a.dv, a.c, a.fill);
 }
 
+size_t attention_bwd_scratch_bytes(const AttnShape& a) { return attention_tc_supported(a) ? 3 * (size_t)a.batch * a.t * sizeof(float) : 0; }
+
 void attention_bwd(float* out, const float* q, const float* k, const float* v, const float* mask, const float* fwd, const float* dout,
-                   const AttnShape& a, int* error, cudaStream_t s) {
+                   const AttnShape& a, void* scratch, int* error, cudaStream_t s) {
   if (a.batch == 0) return;
   if (attention_tc_supported(a)) {
-    if (a.t == 128 && a.d == 32) return launch_bwd_tc<128, 32>(out, q, k, v, mask, fwd, dout, a, error, s);
-    if (a.t == 128) return launch_bwd_tc<128, 64>(out, q, k, v, mask, fwd, dout, a, error, s);
-    if (a.d == 32) return launch_bwd_tc<256, 32>(out, q, k, v, mask, fwd, dout, a, error, s);
-    return launch_bwd_tc<256, 64>(out, q, k, v, mask, fwd, dout, a, error, s);
+    float* st = (float*)scratch;
+    if (a.t == 128 && a.d == 32) return launch_bwd_tc<128, 32>(out, q, k, v, mask, fwd, dout, a, st, error, s);
+    if (a.t == 128) return launch_bwd_tc<128, 64>(out, q, k, v, mask, fwd, dout, a, st, error, s);
+    if (a.d == 32) return launch_bwd_tc<256, 32>(out, q, k, v, mask, fwd, dout, a, st, error, s);
+    return launch_bwd_tc<256, 64>(out, q, k, v, mask, fwd, dout, a, st, error, s);
   }
   if (a.heads) throw std::runtime_error("attention: the packed layout runs on the tensor-core kernels only");
   const long long rows = a.batch * a.t;

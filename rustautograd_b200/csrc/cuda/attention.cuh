@@ -34,7 +34,10 @@ void attention_init();
 bool attention_tc_supported(const AttnShape& a);
 void attention_fwd(float* out, const float* q, const float* k, const float* v, const float* mask, const AttnShape& a, int* error,
                    cudaStream_t s);
+// `scratch`: attention_bwd_scratch_bytes(a) bytes of device memory the two backward kernels pass
+// the query statistics through (the dq kernel computes them, the dk / dv kernel reads them).
+size_t attention_bwd_scratch_bytes(const AttnShape& a);
 void attention_bwd(float* out, const float* q, const float* k, const float* v, const float* mask, const float* fwd, const float* dout,
-                   const AttnShape& a, int* error, cudaStream_t s);
+                   const AttnShape& a, void* scratch, int* error, cudaStream_t s);
 
 }  // namespace rgc

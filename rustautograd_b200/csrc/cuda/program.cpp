@@ -660,11 +660,12 @@ struct Builder {
       };
     } else {
       l.kernels = 2;
+      scratch = std::max(scratch, attention_bwd_scratch_bytes(as));
       l.run = [=](Ctx& c) {
         const float* q = (const float*)c.f->ptr[slot[0]];
         attention_bwd((float*)c.f->ptr[dst], q, (const float*)c.f->ptr[slot[1]] + part, (const float*)c.f->ptr[slot[2]] + 2 * part,
-                      (const float*)c.f->ptr[slot[3]], (const float*)c.f->ptr[slot[4]], (const float*)c.f->ptr[slot[5]], as, c.f->prog->tc_error,
-                      c.s);
+                      (const float*)c.f->ptr[slot[3]], (const float*)c.f->ptr[slot[4]], (const float*)c.f->ptr[slot[5]], as, c.f->scratch,
+                      c.f->prog->tc_error, c.s);
       };
     }
     return l;
