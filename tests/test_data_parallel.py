@@ -74,3 +74,24 @@ def test_two_rank_step_equals_full_batch_step(oracle, tmp_path):
     # Both ranks hold bit-identical replicated state after the all-reduced update.
     for k in range(len(full)):
         np.testing.assert_array_equal(ranks[0][f"arr_{k}"], ranks[1][f"arr_{k}"])
+
+
+def test_device_plan_runs_the_all_reduces_after_the_backward(oracle):
+    """For the device, the planner emits the all-reduces and what depends on them (the AdamW
+    update, the reported loss) after every other step, so the all-reduces are consecutive steps
+    (one staged NCCL operation on the GPU) instead of one between every pair of backward
+    pieces. Plan order only: rg's CPU plan keeps its own order."""
+    import json
+    from rustautograd_b200 import frontend as F
+    F.use(oracle, "cpu")
+    model = F.gpt.GPT(vocab=13, block=8, d=16, heads=2, layers=2)
+    params = model.init(F.random.key(3))
+    opt = F.optim.adamw(1e-2, weight_decay=0.01)
+    state = {"params": params, "opt": opt.init(params), "key": F.random.key(4)}
+    tokens = F.tensor(np.random.default_rng(2).integers(0, 13, size=500, dtype="int32"))
+    step = F.gpt.make_train_step(model, opt, 4, 2, 0)
+    c = F.compile(step, (state, tokens), validate="none", device="cuda-plan")
+    ops = [p.get("op") for p in json.loads(c._n.plan_summary()) if "op" in p or "fused" in p]
+    at = [i for i, op in enumerate(ops) if op == "all_reduce"]
+    assert len(at) == len(F.tree_leaves(params)) + 1  # every gradient and the loss
+    assert at == list(range(at[0], at[0] + len(at))), "the all-reduces are consecutive steps"
