@@ -830,7 +830,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dq_tc(float* __restrict
 // (128): S^T = k q^T; dP^T = v dO^T with dO^T of the half staged beside it; P^T replaces S^T in
 // TMEM (hi, lo in the buffer) and dv += P^T dO; then, with q^T staged over the score operands,
 // dS^T replaces dP^T (hi, lo in the buffer) and dk += dS^T q. The half's query statistics (max,
-// 1 / exp-sum, D) sit in shared memory. dk and dv leave through shared memory.
+// 1 / exp-sum, D), which the dq kernel leaves in `qstats`, sit in shared memory. dk and dv leave
+// through shared memory.
 template <int T, int D>
 __global__ void __launch_bounds__(FWD_THREADS, 1) k_attn_dkdv_tc(float* __restrict__ out, const float* __restrict__ q, const float* __restrict__ k,
                                                                const float* __restrict__ v, const float* __restrict__ mask,
