@@ -141,3 +141,40 @@ def test_gpt_step_at_tensor_core_shapes_uses_the_packed_form():
             assert rel(a[keep], b[keep]) <= 1e-4, f"output {k_}"
         else:
             assert rel(a, b) <= 1e-4, f"output {k_}"
+
+
+def _packed_layer_with_mask(mask_np):
+    """A GPT attention layer (projection, head split, attention, head merge, projection) over a
+    given (T, T) mask, its value and gradients for inputs and weights."""
+    rng = np.random.default_rng(11)
+    b, t, d, heads = 2, mask_np.shape[0], 64, 2
+    mk = lambda *s: F.tensor((rng.normal(size=s) * 0.3).astype("float32"))
+    p = {"qkv": {"w": mk(d, 3 * d), "b": mk(3 * d)}, "out": {"w": mk(d, d), "b": mk(d)}}
+    x, w = mk(b, t, d), mk(b, t, d)
+    mask = F.tensor(mask_np)
+
+    def fn(p, x, w):
+        return F.value_and_grad(lambda p, x: (F.gpt.attention(p, x, heads, mask) * w).sum(), argnums=(0, 1))(p, x)
+    return fn, (p, x, w)
+
+
+def general_mask(t=128, seed=5):
+    m = (np.random.default_rng(seed).random((t, t)) < 0.6).astype("float32")
+    np.fill_diagonal(m, 1.0)
+    m[3] = 0.0  # a row with every key masked
+    return m
+
+
+def test_packed_form_with_a_general_mask_matches_rgs_plan():
+    """The packed form with a mask that is not causal (packed into bits by the kernels, and a
+    fully masked row) against rg's plan; the key bias's gradient is left out as above."""
+    fn, args = _packed_layer_with_mask(general_mask())
+    out = both(fn, args)
+    steps = [p for p in json.loads(out["cuda-plan"][1]._n.plan_summary()) if "op" in p]
+    assert [p["args"][0] for p in steps if p["op"] == "attention"] == [[2, 128, 3, 2, 32]]
+    for k_, (a, b) in enumerate(zip(out["cpu"][0], out["cuda-plan"][0])):
+        if a.shape == (3 * 64,):
+            keep = np.r_[0:64, 128:192]
+            assert rel(a[keep], b[keep]) <= 1e-4, f"output {k_}"
+        else:
+            assert rel(a, b) <= 1e-4, f"output {k_}"

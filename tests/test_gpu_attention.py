@@ -102,3 +102,33 @@ def test_gpt_training_step_with_fused_attention(cuda, oracle, monkeypatch):
             else:
                 assert max_rel(g, o) <= 1e-4, f"output {i}: {max_rel(g, o)}"
     assert max_rel(fused[-1], cpu[-1]) <= 1e-4
+
+
+def test_packed_form_with_a_general_mask(cuda, oracle, monkeypatch):
+    """A GPT attention layer over a mask that is not causal (the kernels pack it into bits; one
+    row has every key masked), in the packed form: values and gradients against the oracle; the
+    key third of the q/k/v bias gradient is rounding noise and is left out."""
+    F.use(cuda, "cuda")
+    rng = np.random.default_rng(11)
+    b, t, d, heads = 2, 128, 64, 2
+    mk = lambda *s: F.tensor((rng.normal(size=s) * 0.3).astype("float32"))
+    p = {"qkv": {"w": mk(d, 3 * d), "b": mk(3 * d)}, "out": {"w": mk(d, d), "b": mk(d)}}
+    x, w = mk(b, t, d), mk(b, t, d)
+    m = (np.random.default_rng(5).random((t, t)) < 0.6).astype("float32")
+    np.fill_diagonal(m, 1.0)
+    m[3] = 0.0
+    mask = F.tensor(m)
+
+    def fn(p, x, w):
+        return F.value_and_grad(lambda p, x: (F.gpt.attention(p, x, heads, mask) * w).sum(), argnums=(0, 1))(p, x)
+    got, c, leaves = run(fn, (p, x, w), True, monkeypatch)
+    steps = [q for q in json.loads(c._n.plan_summary()) if "op" in q]
+    assert [q["args"][0] for q in steps if q["op"] == "attention"] == [[b, t, 3, heads, d // heads]]
+    cpu = [np_of(y) for y in oracle.run_plan_blob(c.plan_blob(), [triple(l) for l in leaves])]
+    for i, (g, o) in enumerate(zip(got, cpu)):
+        assert np.isfinite(g).all()
+        if g.shape == (3 * d,):
+            keep = np.r_[0:d, 2 * d:3 * d]
+            assert max_rel(g[keep], o[keep]) <= 1e-4, f"output {i}"
+        else:
+            assert max_rel(g, o) <= 1e-4, f"output {i}: {max_rel(g, o)}"
